@@ -1,0 +1,184 @@
+/*
+ * wcb.h — C ABI of the B200 (sm_100a) transformer token loop.
+ *
+ * Drop-in boundary for wasm-chord's `wasm-chord-runtime` Model / generate /
+ * GenerationConfig path (crates/wasm-chord-runtime/src/transformer/model.rs).
+ * Conventions copied from the reference C ABI:
+ *   - every call returns a uint32 error code (ErrorCode, wasm-chord-runtime/src/lib.rs:80-89);
+ *   - the message of the last failure on the calling thread is read with
+ *     wcb_last_error (wasmchord_last_error, abi.rs:209-222);
+ *   - model handles are uint32 > 0, 0 is never a valid handle (abi.rs:57-92).
+ * All buffers in these signatures are HOST memory owned by the caller, except
+ * where a parameter is documented as a device pointer. The library owns the
+ * device weights, KV cache and CUDA graphs of each handle; wcb_model_free
+ * releases them. One handle is one model replica on one GPU and is not
+ * re-entrant (the reference's `&mut self`); distinct handles may be driven from
+ * distinct threads.
+ */
+#ifndef WCB_H
+#define WCB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ErrorCode — wasm-chord-runtime/src/lib.rs:80-89 */
+enum {
+  WCB_OK = 0,
+  WCB_ERR_GENERIC = 1,
+  WCB_ERR_OOM = 2,
+  WCB_ERR_INVALID_ARGUMENT = 3,
+  WCB_ERR_MODEL_PARSE = 4,
+  WCB_ERR_BACKEND_UNSUPPORTED = 5,
+  WCB_ERR_SHADER_COMPILE = 6, /* unused; kept so codes line up with the reference */
+  WCB_ERR_IO = 7
+};
+
+/* GGUF tensor types accepted for 2-D weights */
+enum { WCB_DTYPE_F32 = 0, WCB_DTYPE_Q4_K = 12, WCB_DTYPE_Q6_K = 14 };
+
+/* KV cache element type */
+enum { WCB_KV_F32 = 0, WCB_KV_F16 = 1 };
+
+/* Load options (no counterpart in the reference, whose Model::new takes only a
+ * TransformerConfig: model.rs:188). Zero-initialised options are valid. */
+typedef struct wcb_load_opts {
+  int32_t device;     /* CUDA device ordinal */
+  uint32_t max_seq;   /* KV capacity in tokens; 0 = GGUF context_length (kv_cache.rs:48-53) */
+  uint32_t kv_dtype;  /* WCB_KV_F32 (reference numerics) or WCB_KV_F16 */
+  uint32_t max_batch; /* sequences per wcb_generate_batch call; 0 = 1 */
+  uint32_t flags;     /* bit 0: do not use CUDA graphs for decode steps */
+} wcb_load_opts;
+
+/* TransformerConfig — transformer/config.rs:6-41 (plus head_dim) */
+typedef struct wcb_model_config {
+  uint32_t vocab_size, hidden_size, num_layers, num_heads, num_kv_heads;
+  uint32_t intermediate_size, max_seq_len, head_dim;
+  float rms_norm_eps, rope_theta;
+} wcb_model_config;
+
+/* GenerationConfig — transformer/config.rs:60-78, plus the sampler seed that
+ * generate() hard-codes to 42 (model.rs:1336) and the EOS id that generate()
+ * reads from the tokenizer (model.rs:1400). eos_id = UINT32_MAX disables EOS. */
+typedef struct wcb_gen_config {
+  uint32_t max_tokens;
+  float temperature;
+  float top_p;
+  uint32_t top_k;
+  float repetition_penalty;
+  uint64_t seed;
+  uint32_t eos_id;
+} wcb_gen_config;
+
+/* Fills the reference defaults: max_tokens 100, temperature 0.7, top_p 0.9,
+ * top_k 40, repetition_penalty 1.1 (config.rs:74-78), seed 42, eos_id 2. */
+void wcb_gen_config_default(wcb_gen_config* cfg);
+
+/* Model::new + Model::load_from_gguf (model.rs:188, :364) from a GGUF file:
+ * parses the header and config (gguf.rs:111-276), uploads raw Q4_K / Q6_K
+ * blocks to HBM unchanged (Q6_K blocks padded from 210 to 224 bytes for 16-byte
+ * alignment), allocates the device KV cache. */
+uint32_t wcb_model_load(const char* gguf_path, const wcb_load_opts* opts, uint32_t* out_handle);
+
+/* Releases a handle (wasmchord_free_model, abi.rs:95-108). */
+uint32_t wcb_model_free(uint32_t handle);
+
+/* TransformerConfig of a loaded model. */
+uint32_t wcb_model_config_get(uint32_t handle, wcb_model_config* out);
+
+/* Model::forward (model.rs:832-1192): runs n tokens at `position`, appends their
+ * K/V at the current KV length, writes the vocab_size logits of the LAST token
+ * to logits_out (host). Errors: n == 0, or KV overflow (kv_cache.rs:48-53,
+ * WCB_ERR_MODEL_PARSE as in the reference). */
+uint32_t wcb_forward(uint32_t handle, const uint32_t* ids, size_t n, size_t position, float* logits_out);
+
+/* Model::clear_kv_cache (model.rs:1547) and the KV length (KVCache::current_seq_len). */
+uint32_t wcb_clear_kv(uint32_t handle);
+uint32_t wcb_kv_len(uint32_t handle, size_t* out_len);
+
+/* Model::generate (model.rs:1322-1415) on token ids: clears the KV cache,
+ * prefills the prompt, samples the first token without an EOS check, then
+ * decodes until cfg->max_tokens tokens or EOS (checked before the push).
+ * Writes the generated ids (prompt excluded) to out[0 .. min(*n_out, cap)). */
+uint32_t wcb_generate_tokens(uint32_t handle, const uint32_t* prompt, size_t n, const wcb_gen_config* cfg,
+                             uint32_t* out, size_t cap, size_t* n_out);
+
+/* Data-parallel serving: n_seq independent generate() runs batched through one
+ * replica (each sequence has its own KV cache and sampler). prompts holds the
+ * n_seq prompts back to back with lengths lens[]; out is n_seq x cap;
+ * n_out receives n_seq counts. n_seq <= wcb_load_opts.max_batch. */
+uint32_t wcb_generate_batch(uint32_t handle, const uint32_t* prompts, const size_t* lens, size_t n_seq,
+                            const wcb_gen_config* cfg, uint32_t* out, size_t cap, size_t* n_out);
+
+/* Streaming generation, the token-id form of the reference's wasmchord_infer /
+ * wasmchord_next_token / wasmchord_close_stream (abi.rs:119-200, placeholders
+ * there). wcb_infer starts generate()'s loop on a model (clears its KV cache,
+ * prefills, samples the first token) and returns a stream handle > 0; starting
+ * another generation on the same model invalidates earlier streams. */
+uint32_t wcb_infer(uint32_t handle, const uint32_t* prompt, size_t n, const wcb_gen_config* cfg,
+                   uint32_t* out_stream);
+
+/* Writes up to max_tokens next generated ids to out (host), running decode
+ * steps on the device as needed (greedy decoding runs them back to back without
+ * a host round trip); *finished = 1 once EOS or max_tokens has ended the
+ * sequence and every token was returned. A KV overflow is reported (code 4) on
+ * the call after the last token produced before it. */
+uint32_t wcb_next_tokens(uint32_t stream, size_t max_tokens, uint32_t* out, size_t* n_out, uint32_t* finished);
+
+/* One token: returns 1 with *out_token set, -1 at the end, -2 on error
+ * (wasmchord_next_token's convention, abi.rs:155-190). */
+int32_t wcb_next_token(uint32_t stream, uint32_t* out_token);
+
+uint32_t wcb_close_stream(uint32_t stream);
+
+/* Kernels one greedy decode step launches (for launch accounting). */
+uint32_t wcb_model_launches_per_step(uint32_t handle, uint32_t* out);
+
+/* LogitsProcessor (sampling.rs:29-264) over host logits: with_params(seed, T,
+ * top_p, top_k, repetition_penalty) -> sampler handle; sample() mutates
+ * logits in place (repetition penalty) and records the token. */
+uint32_t wcb_sampler_new(const wcb_gen_config* cfg, uint32_t* out_sampler);
+uint32_t wcb_sampler_sample(uint32_t sampler, float* logits, size_t n, uint32_t* out_token);
+uint32_t wcb_sampler_free(uint32_t sampler);
+
+/* Last error message of the calling thread (wasmchord_last_error, abi.rs:209-222):
+ * NUL-terminated, returns bytes copied excluding the NUL. */
+size_t wcb_last_error(char* buf, size_t len);
+
+/* Library version string (wasmchord_version, abi.rs:225-228). */
+const char* wcb_version(void);
+
+/* ---- kernel-level entry points (device pointers, caller's stream) ----------
+ * No counterpart in the reference's public API: they expose the hot kernels
+ * (the reference's quant.rs dequantisers and gemm.rs matmul_transposed) for
+ * parity tests and microbenchmarks. `stream` is a cudaStream_t (NULL = legacy
+ * default stream). All return after enqueueing; errors are launch errors. */
+
+/* dequantize_q4_k / dequantize_q6_k (quant.rs:58-115, :206-261) over nblocks raw
+ * blocks (144 / 210 bytes each, packed) into nblocks*256 floats. Bit-exact. */
+uint32_t wcb_dequant_dev(const void* blocks, uint32_t dtype, size_t nblocks, float* out, void* stream);
+
+/* Q6_K blocks are 210 bytes, so they cannot be read with 16-byte loads in
+ * place; the device layout pads each block to 224 bytes (bytes 210..223 zero,
+ * the first 210 unchanged). Repacks nblocks packed blocks into that layout. */
+uint32_t wcb_repack_q6k_dev(const void* packed, size_t nblocks, void* padded, void* stream);
+
+/* y[m][n] = sum_k x[m][k] * W[n][k] (matmul_transposed, gemm.rs:83-143) with W
+ * an [n, k] tensor in device layout: raw Q4_K blocks (dtype WCB_DTYPE_Q4_K) or
+ * padded Q6_K blocks (WCB_DTYPE_Q6_K, see wcb_repack_q6k_dev). x is [m][k] and
+ * y is [m][n], f32, row-major. k % 256 == 0, n % 4 == 0, 1 <= m <= 64. */
+uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const float* x, size_t m, float* y,
+                      void* stream);
+
+/* Device stream a model handle launches on (a cudaStream_t), for callers that
+ * time or order work against it. */
+uint32_t wcb_model_stream(uint32_t handle, void** out_stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WCB_H */

@@ -1,0 +1,120 @@
+"""CPU checks of the synthetic-model generator and of the C ABI library that
+need no GPU: symbol exports, error codes and the host sampler."""
+import ctypes as C
+import os
+import re
+import struct
+
+import numpy as np
+import pytest
+
+import wcb
+from wcb import synth
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_fast_quantizers_match_numpy():
+    x = synth.normal(7, 3, 256 * 200, 0.0, 0.02)
+    assert np.array_equal(synth.quantize_q4_k_fast(x), synth.quantize_q4_k(x))
+    assert np.array_equal(synth.quantize_q6_k_fast(x), synth.quantize_q6_k(x))
+
+
+def test_normal_generator_is_deterministic_and_normal():
+    a = synth.normal(0, 5, 100001, 0.0, 1.0)
+    b = synth.normal(0, 5, 100001, 0.0, 1.0)
+    assert np.array_equal(a, b)
+    assert abs(a.mean()) < 0.02 and abs(a.std() - 1.0) < 0.02
+    assert not np.array_equal(a[:1000], synth.normal(0, 6, 1000, 0.0, 1.0))
+
+
+def test_gguf_file_reads_back_with_gguf_py(tiny_mix_gguf):
+    from gguf import GGUFReader
+    r = GGUFReader(tiny_mix_gguf)
+    names = {t.name: t for t in r.tensors}
+    cfg = synth.PRESETS["tiny_mix"]
+    plan = synth.tensor_plan(cfg)
+    assert [p[0] for p in plan] == [t.name for t in r.tensors]
+    for name, ne, ty in plan:
+        t = names[name]
+        assert int(t.tensor_type) == ty
+        assert tuple(int(d) for d in t.shape) == tuple(ne)
+    assert int(names["blk.0.attn_v.weight"].tensor_type) == synth.GGML_Q6_K
+    assert int(names["blk.1.attn_v.weight"].tensor_type) == synth.GGML_Q4_K
+    f = r.fields["llama.context_length"]
+    assert int(f.parts[f.data[0]][0]) == cfg.context_length
+
+
+def _declared_symbols():
+    hdr = open(os.path.join(REPO, "include", "wcb.h")).read()
+    return sorted(set(re.findall(r"\b(wcb_[a-z0-9_]+)\s*\(", hdr)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = wcb.lib()
+    declared = _declared_symbols()
+    assert len(declared) >= 18
+    for name in declared:
+        assert hasattr(L, name), name
+    assert set(declared) == set(wcb.EXPORTED)
+
+
+def test_version_and_defaults():
+    assert wcb.version().startswith("wcb-")
+    c = wcb._GenConfig()
+    wcb.lib().wcb_gen_config_default(C.byref(c))
+    assert (c.max_tokens, c.top_k, c.seed, c.eos_id) == (100, 40, 42, 2)
+    assert abs(c.temperature - 0.7) < 1e-7 and abs(c.top_p - 0.9) < 1e-7
+    assert abs(c.repetition_penalty - 1.1) < 1e-7
+
+
+def test_load_errors_without_touching_the_gpu(tmp_path):
+    with pytest.raises(wcb.WcbError) as e:
+        wcb.Model.load_from_gguf(str(tmp_path / "missing.gguf"))
+    assert e.value.code == 7  # IoError
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGUX" + b"\0" * 64)
+    with pytest.raises(wcb.WcbError) as e:
+        wcb.Model.load_from_gguf(str(bad))
+    assert e.value.code == 4 and "magic" in e.value.message
+    v9 = tmp_path / "v9.gguf"
+    v9.write_bytes(b"GGUF" + struct.pack("<IQQ", 9, 0, 0))
+    with pytest.raises(wcb.WcbError) as e:
+        wcb.Model.load_from_gguf(str(v9))
+    assert e.value.code == 4 and "version" in e.value.message
+
+
+def test_last_error_is_taken_once():
+    L = wcb.lib()
+    h = C.c_uint32(0)
+    assert L.wcb_model_load(b"/nonexistent/x.gguf", None, C.byref(h)) == 7
+    assert h.value == 0
+    assert "cannot open" in wcb.last_error()
+    assert wcb.last_error() == "No error"
+
+
+def test_invalid_handles():
+    L = wcb.lib()
+    assert L.wcb_model_free(12345) == 3
+    n = C.c_size_t(0)
+    assert L.wcb_kv_len(12345, C.byref(n)) == 3
+
+
+def test_host_sampler_matches_oracle_argmax_and_penalty():
+    import oracle
+    rng = np.random.default_rng(11)
+    s_w = wcb.LogitsProcessor(42, 0.0, 0.9, 40, 1.3)
+    s_o = oracle.Sampler(42, 0.0, 0.9, 40, 1.3)
+    for _ in range(30):
+        l = rng.standard_normal(300).astype(np.float32)
+        l[rng.integers(0, 300)] = l.max()  # a tie
+        a, b = l.copy(), l.copy()
+        assert s_w.sample(a) == s_o.sample(b)
+        assert np.array_equal(a, b)
+
+
+def test_host_sampler_nan_is_generic_failure():
+    s = wcb.LogitsProcessor(42, 0.0, 0.9, 40, 1.0)
+    with pytest.raises(wcb.WcbError) as e:
+        s.sample(np.array([0.0, np.nan], np.float32))
+    assert e.value.code == 1

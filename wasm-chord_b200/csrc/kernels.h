@@ -1,0 +1,134 @@
+// Device kernels of the token loop and their host launchers.
+//
+// HBM layout (one model replica):
+//   weights   raw GGUF blocks, row-major [rows][K/256 blocks]: Q4_K 144 B/block,
+//             Q6_K padded to 224 B/block (first 210 bytes unchanged)
+//   embedding f32 [vocab][hidden] (token_embd as stored in the GGUF)
+//   KV cache  per layer: K and V, [n_kv_heads][max_seq][head_dim], f32 or f16
+//   RoPE      cos/sin tables [max_seq][head_dim/2] computed on the host with the
+//             reference formula (attention.rs:230-248), so rotations are bit-exact
+//   StepState one small struct the kernels read position / KV length from, so a
+//             decode step can be captured once in a CUDA graph and replayed
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace wcb {
+
+constexpr int QK_K = 256;
+constexpr int Q4K_BYTES = 144;
+constexpr int Q6K_BYTES = 210;
+constexpr int Q6K_DEV_BYTES = 224;
+constexpr int DT_Q4K = 12;
+constexpr int DT_Q6K = 14;
+
+#ifdef __CUDACC__
+#define WCB_HD __host__ __device__
+#else
+#define WCB_HD
+#endif
+WCB_HD inline size_t dev_block_bytes(int dtype) { return dtype == DT_Q4K ? Q4K_BYTES : Q6K_DEV_BYTES; }
+
+// State shared by the kernels of one forward / decode step (device memory).
+struct StepState {
+  int position;  // RoPE position / causal-mask base of token 0 of this forward
+  int kv_len;    // KV length before this forward (slot of token 0)
+  int n_tokens;  // tokens in this forward
+  int done;      // decode loop finished: kernels of later steps return at once
+  int gen;       // tokens generated so far (generate loop)
+  int max_gen;   // generate's max_tokens
+  int nhist;     // sampler history length (LogitsProcessor::previous_tokens)
+  int err;       // device error word: 1 = NaN logit (sampler), 2 = KV overflow
+  int eos;       // EOS id (-1: none)
+  int max_seq;   // KV capacity
+  int pad[6];
+};
+
+// ---------------------------------------------------------------- GEMV ----
+enum GemvPro { PRO_NONE = 0, PRO_RMSNORM = 1 };
+enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+
+struct GemvSeg {
+  const uint8_t* w;
+  int dtype;
+  int rows;
+};
+
+struct GemvArgs {
+  GemvSeg seg[3];
+  int nseg;
+  int K;
+  int M;              // activation rows (tokens) in this launch
+  int ngroups;        // row groups of 4
+  int ksplit;         // warps sharing one row group (split over K)
+  const float* x;     // [M][ldx] input (PRO_NONE) or residual stream h (PRO_RMSNORM)
+  int ldx;
+  const float* norm_w;  // PRO_RMSNORM weight
+  float eps;
+  float* y;           // EPI_STORE / EPI_RESID / EPI_SWIGLU output [M][ldy]
+  int ldy;
+  const float* resid;  // EPI_RESID residual [M][ldr]
+  int ldr;
+  // EPI_QKV
+  float* q;           // [M][ldq]
+  int ldq;
+  void* kc;           // this layer's K cache [n_kv][max_seq][hd]
+  void* vc;
+  int kv_half;        // KV element type: 0 f32, 1 f16
+  int hidden;
+  int kv_dim;
+  int head_dim;
+  int max_seq;
+  const float* rope_cos;  // [max_seq][head_dim/2]
+  const float* rope_sin;
+  const StepState* st;
+  int token_offset;   // first token of this launch within the forward (column groups)
+};
+
+size_t gemv_smem_bytes(int M, int K);
+int gemv_max_cols(int K);  // widest column group whose activation planes fit in shared memory
+cudaError_t launch_gemv(const GemvArgs& a, int pro, int epi, cudaStream_t s);
+
+// ----------------------------------------------------------- attention ----
+struct AttnArgs {
+  const float* q;     // [T][n_heads][hd] (post-RoPE)
+  const void* kc;     // [n_kv][max_seq][hd]
+  const void* vc;
+  int kv_half;
+  float* out;         // [T][n_heads][hd]
+  float* part;        // scratch: [T][n_heads][max_splits][hd + 2]
+  int* ticket;        // scratch: [T][n_kv], zero between launches
+  int n_heads, n_kv, head_dim, max_seq;
+  int T;
+  int chunk;          // keys per split
+  int max_splits;
+  float scale;        // 1 / sqrt(head_dim)
+  const StepState* st;
+};
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// ------------------------------------------------------------ elementwise --
+cudaError_t launch_embed(const float* emb, int vocab, int hidden, const uint32_t* ids, int T, float* x,
+                         const StepState* st, cudaStream_t s);
+// decode-step embedding: id = hist[nhist - 1]
+cudaError_t launch_embed_last(const float* emb, int vocab, int hidden, const uint32_t* hist, float* x,
+                              const StepState* st, cudaStream_t s);
+
+// Repetition penalty + argmax (sampling.rs:86-125) over logits[V] with the
+// history hist[0..st->nhist). mode 0: write *tok only; mode 1 (generate):
+// also apply generate()'s EOS / push / counters and advance the KV position.
+cudaError_t launch_sample_argmax(const float* logits, int V, float* work, uint32_t* hist, float rep,
+                                 uint32_t* tok, StepState* st, int mode, int first, cudaStream_t s);
+
+// StepState writers (single-thread kernels, so they order with the stream and
+// can sit inside a captured graph)
+cudaError_t launch_set_state(StepState* st, int position, int kv_len, int n_tokens, cudaStream_t s);
+cudaError_t launch_init_gen(StepState* st, int max_gen, int eos, int max_seq, cudaStream_t s);
+// sets the shared-memory limits of every GEMV instantiation (before any capture)
+cudaError_t gemv_configure_all();
+
+cudaError_t launch_dequant(const void* blocks, int dtype, size_t nblocks, float* out, cudaStream_t s);
+cudaError_t launch_repack_q6k(const void* packed, size_t nblocks, void* padded, cudaStream_t s);
+
+}  // namespace wcb

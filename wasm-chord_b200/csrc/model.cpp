@@ -1,0 +1,594 @@
+#include "model.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+namespace wcb {
+
+namespace {
+
+constexpr int T_MAX = 256;        // tokens per forward launch (longer prompts are split, same results)
+constexpr int DECODE_CHUNK = 32;  // keys per attention split in decode steps
+
+float f16_to_f32_host(uint16_t h) {
+  const uint32_t sign = uint32_t(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1F, mant = h & 0x3FF, out;
+  if (exp == 0) {
+    if (mant == 0) {
+      out = sign;
+    } else {
+      int e = -1;
+      do { e++; mant <<= 1; } while (!(mant & 0x400));
+      out = sign | (uint32_t(127 - 15 - e) << 23) | ((mant & 0x3FF) << 13);
+    }
+  } else if (exp == 31) {
+    out = sign | 0x7F800000u | (mant << 13);
+  } else {
+    out = sign | ((exp + 112) << 23) | (mant << 13);
+  }
+  float f;
+  std::memcpy(&f, &out, 4);
+  return f;
+}
+
+uint32_t cuda_code(cudaError_t e) { return e == cudaErrorMemoryAllocation ? E_OOM : E_BACKEND; }
+
+}  // namespace
+
+void Model::check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess)
+    throw WcbError(cuda_code(e), std::string("Backend error: ") + what + ": " + cudaGetErrorString(e));
+}
+
+void* Model::dalloc(size_t bytes) {
+  void* p = nullptr;
+  check(cudaMalloc(&p, std::max<size_t>(bytes, 16)), "cudaMalloc");
+  allocs_.push_back(p);
+  return p;
+}
+
+Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), device_(opt.device) {
+  GgufFile f(path);
+  cfg_ = f.config();
+  const ModelConfig& c = cfg_;
+  if (c.heads == 0 || c.kv_heads == 0 || c.hidden % c.heads || c.heads % c.kv_heads)
+    throw WcbError(E_INVALID, "Invalid tensor shape: heads / kv_heads / hidden are inconsistent");
+  const uint32_t hd = c.head_dim();
+  if (hd != 64 && hd != 128) throw WcbError(E_BACKEND, "Backend error: head_dim must be 64 or 128");
+  if (c.hidden % 256 || c.ffn % 256)
+    throw WcbError(E_BACKEND, "Backend error: hidden and intermediate sizes must be multiples of 256");
+  if (c.heads / c.kv_heads > 16) throw WcbError(E_BACKEND, "Backend error: more than 16 query heads per KV head");
+  if (c.vocab % 4) throw WcbError(E_BACKEND, "Backend error: vocab size must be a multiple of 4");
+  max_seq_ = opt.max_seq ? opt.max_seq : c.max_seq;
+  if (max_seq_ == 0) throw WcbError(E_INVALID, "Invalid tensor shape: context length 0");
+
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  check(gemv_configure_all(), "configure GEMV kernels");
+  try {
+    // token embeddings (model.rs:432-446): first name that loads
+    bool have_emb = false;
+    for (const char* n : {"token_embd.weight", "model.embed_tokens.weight", "embed_tokens.weight"}) {
+      const GgufTensor* t = f.find(n);
+      if (!t) continue;
+      if (t->numel != uint64_t(c.vocab) * c.hidden)
+        throw WcbError(E_GENERIC, std::string("tensor ") + n + " has the wrong number of elements");
+      std::vector<uint8_t> raw(t->nbytes);
+      f.read(*t, raw.data());
+      emb_ = static_cast<float*>(dalloc(sizeof(float) * t->numel));
+      if (t->dtype == 0) {
+        check(cudaMemcpy(emb_, raw.data(), t->nbytes, cudaMemcpyHostToDevice), "upload embeddings");
+      } else if (t->dtype == 1) {
+        std::vector<float> v(t->numel);
+        for (uint64_t i = 0; i < t->numel; ++i) {
+          uint16_t hbits;
+          std::memcpy(&hbits, &raw[2 * i], 2);
+          v[i] = f16_to_f32_host(hbits);
+        }
+        check(cudaMemcpy(emb_, v.data(), sizeof(float) * v.size(), cudaMemcpyHostToDevice), "upload embeddings");
+      } else if (t->dtype == DT_Q4K || t->dtype == DT_Q6K) {
+        void* tmp = nullptr;
+        check(cudaMalloc(&tmp, t->nbytes), "cudaMalloc");
+        check(cudaMemcpy(tmp, raw.data(), t->nbytes, cudaMemcpyHostToDevice), "upload embeddings");
+        check(launch_dequant(tmp, int(t->dtype), t->numel / QK_K, emb_, stream_), "dequantise embeddings");
+        check(cudaStreamSynchronize(stream_), "dequantise embeddings");
+        cudaFree(tmp);
+      } else {
+        continue;
+      }
+      have_emb = true;
+      break;
+    }
+    if (!have_emb) throw WcbError(E_PARSE, "Parse error: Missing token embeddings");
+    upload_vector(f, "output_norm.weight", c.hidden, 1.0f, out_norm_);
+
+    // LM head (model.rs:482-606)
+    bool have_head = false;
+    for (const char* n : {"output.weight", "lm_head.weight", "model.lm_head.weight"}) {
+      const GgufTensor* t = f.find(n);
+      if (!t || (t->dtype != DT_Q4K && t->dtype != DT_Q6K)) continue;
+      upload_weight(f, n, c.vocab, c.hidden, lm_head_, false);
+      have_head = true;
+      break;
+    }
+    if (!have_head)
+      throw WcbError(E_BACKEND,
+                     "Backend error: the LM head must be a Q4_K or Q6_K tensor (tied embeddings are not supported)");
+
+    const uint32_t kvd = c.kv_heads * hd;
+    layers_.resize(c.layers);
+    for (uint32_t l = 0; l < c.layers; ++l) {
+      DevLayer& L = layers_[l];
+      const std::string p = "blk." + std::to_string(l) + ".";
+      auto attn = [&](const char* base, uint32_t rows, DevWeight& w) {
+        std::string n = p + base + ".weight";
+        if (!f.find(n)) n = p + base;
+        upload_weight(f, n, rows, c.hidden, w, true);
+      };
+      attn("attn_q", c.hidden, L.q);
+      attn("attn_k", kvd, L.k);
+      attn("attn_v", kvd, L.v);
+      attn("attn_output", c.hidden, L.o);
+      upload_weight(f, p + "ffn_gate.weight", c.ffn, c.hidden, L.gate, true);
+      upload_weight(f, p + "ffn_up.weight", c.ffn, c.hidden, L.up, true);
+      upload_weight(f, p + "ffn_down.weight", c.hidden, c.ffn, L.down, true);
+      upload_vector(f, p + "attn_norm.weight", c.hidden, 1.0f, L.attn_norm);
+      upload_vector(f, p + "ffn_norm.weight", c.hidden, 1.0f, L.ffn_norm);
+      if (L.gate.dtype != L.up.dtype)
+        throw WcbError(E_BACKEND, "Backend error: ffn_gate and ffn_up must share a quantisation type");
+    }
+
+    // KV cache (kv_cache.rs:6-34), [L][n_kv][max_seq][hd]
+    kv_layer_elems_ = size_t(c.kv_heads) * max_seq_ * hd;
+    const size_t kv_bytes = kv_layer_elems_ * c.layers * (opt.kv_half ? 2 : 4);
+    kcache_ = dalloc(kv_bytes);
+    vcache_ = dalloc(kv_bytes);
+    check(cudaMemset(kcache_, 0, kv_bytes), "clear KV");
+    check(cudaMemset(vcache_, 0, kv_bytes), "clear KV");
+
+    build_rope(max_seq_);
+    attn_scale_ = 1.0f / std::sqrt(float(hd));  // attention.rs:363
+
+    t_max_ = T_MAX;
+    st_ = static_cast<StepState*>(dalloc(sizeof(StepState)));
+    check(cudaMemset(st_, 0, sizeof(StepState)), "clear state");
+    ids_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * std::max<size_t>(max_seq_, 1)));
+    hist_cap_ = max_seq_ + 2;
+    hist_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * hist_cap_));
+    tok_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t)));
+    x_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
+    h_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
+    q_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
+    att_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
+    act_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.ffn));
+    logits_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
+    work_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
+    // attention partials: enough for T_MAX tokens at 256-key splits and for one
+    // token at DECODE_CHUNK-key splits
+    max_splits_ = int((max_seq_ + DECODE_CHUNK - 1) / DECODE_CHUNK);
+    const size_t part_prefill = size_t(t_max_) * c.heads * ((max_seq_ + 255) / 256) * (hd + 2);
+    const size_t part_decode = size_t(c.heads) * max_splits_ * (hd + 2);
+    part_ = static_cast<float*>(dalloc(sizeof(float) * std::max(part_prefill, part_decode)));
+    ticket_ = static_cast<int*>(dalloc(sizeof(int) * size_t(t_max_) * c.kv_heads));
+    check(cudaMemset(ticket_, 0, sizeof(int) * size_t(t_max_) * c.kv_heads), "clear tickets");
+    check(cudaMallocHost(&host_ids_, sizeof(uint32_t) * std::max<size_t>(max_seq_, 1)), "cudaMallocHost");
+    check(cudaDeviceSynchronize(), "load");
+  } catch (...) {
+    for (void* p : allocs_) cudaFree(p);
+    allocs_.clear();
+    if (host_ids_) cudaFreeHost(host_ids_);
+    host_ids_ = nullptr;
+    cudaStreamDestroy(stream_);
+    stream_ = nullptr;
+    throw;
+  }
+}
+
+Model::~Model() {
+  cudaSetDevice(device_);
+  if (stream_) cudaStreamSynchronize(stream_);
+  if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
+  if (decode_graph_) cudaGraphDestroy(decode_graph_);
+  for (void* p : allocs_) cudaFree(p);
+  if (host_ids_) cudaFreeHost(host_ids_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+// Uploads a 2-D weight [rows][cols] as raw blocks (Q6_K padded to 224 bytes).
+// A missing tensor leaves zeros, as the reference's `if let Ok(..)` loads do
+// (model.rs:618-760): an all-zero Q4_K block dequantises to 0.
+void Model::upload_weight(const GgufFile& f, const std::string& name, uint32_t rows, uint32_t cols, DevWeight& w,
+                          bool missing_is_zero) {
+  w.rows = rows;
+  w.cols = cols;
+  const size_t nb = size_t(cols) / QK_K;
+  const GgufTensor* t = f.find(name);
+  if (!t) {
+    if (!missing_is_zero) throw WcbError(E_GENERIC, "Tensor not found: " + name);
+    w.dtype = DT_Q4K;
+    const size_t bytes = size_t(rows) * nb * Q4K_BYTES;
+    w.ptr = static_cast<uint8_t*>(dalloc(bytes));
+    check(cudaMemset(w.ptr, 0, bytes), "zero weight");
+    return;
+  }
+  if (t->numel != uint64_t(rows) * cols)
+    throw WcbError(E_GENERIC, "tensor " + name + " has " + std::to_string(t->numel) + " elements, expected " +
+                                  std::to_string(uint64_t(rows) * cols));
+  if (t->dtype != DT_Q4K && t->dtype != DT_Q6K)
+    throw WcbError(E_BACKEND, "Backend error: tensor " + name + " must be Q4_K or Q6_K (GGUF type " +
+                                  std::to_string(t->dtype) + ")");
+  w.dtype = int(t->dtype);
+  std::vector<uint8_t> raw(t->nbytes);
+  f.read(*t, raw.data());
+  if (w.dtype == DT_Q4K) {
+    w.ptr = static_cast<uint8_t*>(dalloc(raw.size()));
+    check(cudaMemcpy(w.ptr, raw.data(), raw.size(), cudaMemcpyHostToDevice), "upload weight");
+  } else {
+    const size_t nblk = raw.size() / Q6K_BYTES;
+    std::vector<uint8_t> pad(nblk * Q6K_DEV_BYTES, 0);
+    for (size_t b = 0; b < nblk; ++b) std::memcpy(&pad[b * Q6K_DEV_BYTES], &raw[b * Q6K_BYTES], Q6K_BYTES);
+    w.ptr = static_cast<uint8_t*>(dalloc(pad.size()));
+    check(cudaMemcpy(w.ptr, pad.data(), pad.size(), cudaMemcpyHostToDevice), "upload weight");
+  }
+}
+
+void Model::upload_vector(const GgufFile& f, const std::string& name, uint32_t n, float fill, float*& dst) {
+  std::vector<float> v(n, fill);
+  const GgufTensor* t = f.find(name);
+  if (t && (t->dtype == 0 || t->dtype == 1)) {
+    if (t->numel != n)
+      throw WcbError(E_GENERIC, "tensor " + name + " has " + std::to_string(t->numel) + " elements, expected " +
+                                    std::to_string(n));
+    std::vector<uint8_t> raw(t->nbytes);
+    f.read(*t, raw.data());
+    for (uint32_t i = 0; i < n; ++i) {
+      if (t->dtype == 0) {
+        std::memcpy(&v[i], &raw[4 * size_t(i)], 4);
+      } else {
+        uint16_t hb;
+        std::memcpy(&hb, &raw[2 * size_t(i)], 2);
+        v[i] = f16_to_f32_host(hb);
+      }
+    }
+  }
+  dst = static_cast<float*>(dalloc(sizeof(float) * n));
+  check(cudaMemcpy(dst, v.data(), sizeof(float) * n, cudaMemcpyHostToDevice), "upload vector");
+}
+
+// cos / sin of the RoPE angles exactly as apply_rope computes them
+// (attention.rs:230-248): freq = 1 / theta^(i/hd) and angle = pos * freq in f32.
+void Model::build_rope(uint32_t len) {
+  const uint32_t hd = cfg_.head_dim(), half = hd / 2;
+  std::vector<float> cs(size_t(len) * half), sn(size_t(len) * half);
+  for (uint32_t i = 0; i < hd; i += 2) {
+    const float freq = 1.0f / std::pow(cfg_.theta, float(i) / float(hd));
+    for (uint32_t p = 0; p < len; ++p) {
+      const float angle = float(p) * freq;
+      cs[size_t(p) * half + i / 2] = std::cos(angle);
+      sn[size_t(p) * half + i / 2] = std::sin(angle);
+    }
+  }
+  float* c = static_cast<float*>(dalloc(sizeof(float) * cs.size()));
+  float* s = static_cast<float*>(dalloc(sizeof(float) * sn.size()));
+  check(cudaMemcpy(c, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice), "upload rope");
+  check(cudaMemcpy(s, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice), "upload rope");
+  rope_cos_ = c;
+  rope_sin_ = s;
+  rope_len_ = len;
+  if (decode_exec_) {  // captured graphs hold the old table pointers
+    cudaGraphExecDestroy(decode_exec_);
+    cudaGraphDestroy(decode_graph_);
+    decode_exec_ = nullptr;
+    decode_graph_ = nullptr;
+  }
+}
+
+void Model::set_state(int position, int kv_len, int n_tokens) {
+  check(launch_set_state(st_, position, kv_len, n_tokens, stream_), "set state");
+}
+
+void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, int ldx, const float* norm_w,
+                 float eps, int pro, int epi, float* y, int ldy, const float* resid, int ldr, float* q, int ldq,
+                 int layer, int token_offset) {
+  GemvArgs a{};
+  int rows = 0;
+  for (int i = 0; i < nseg; ++i) {
+    a.seg[i].w = segs[i].ptr;
+    a.seg[i].dtype = segs[i].dtype;
+    a.seg[i].rows = int(segs[i].rows);
+    rows += int(segs[i].rows);
+  }
+  a.nseg = nseg;
+  a.K = K;
+  a.ngroups = epi == EPI_SWIGLU ? int(segs[0].rows) / 2 : rows / 4;
+  // split K over warps while the row groups alone leave the GPU under-filled,
+  // keeping at least 16 chunks of work per warp
+  const int chunks = (K / QK_K) * (segs[0].dtype == DT_Q4K ? 8 : 4);
+  int ks = 1;
+  while (ks < 8 && a.ngroups * ks < 148 * 16 && chunks / (ks * 2) >= 16) ks *= 2;
+  a.ksplit = ks;
+  a.norm_w = norm_w;
+  a.eps = eps;
+  a.ldx = ldx;
+  a.ldy = ldy;
+  a.ldr = ldr;
+  a.ldq = ldq;
+  a.hidden = int(cfg_.hidden);
+  a.kv_dim = int(cfg_.kv_heads * cfg_.head_dim());
+  a.head_dim = int(cfg_.head_dim());
+  a.max_seq = int(max_seq_);
+  a.kv_half = int(opt_.kv_half);
+  if (layer >= 0) {
+    const size_t esz = opt_.kv_half ? 2 : 4;
+    a.kc = static_cast<uint8_t*>(kcache_) + size_t(layer) * kv_layer_elems_ * esz;
+    a.vc = static_cast<uint8_t*>(vcache_) + size_t(layer) * kv_layer_elems_ * esz;
+  }
+  a.rope_cos = rope_cos_;
+  a.rope_sin = rope_sin_;
+  a.st = st_;
+  const int mmax = gemv_max_cols(K);
+  for (int c0 = 0; c0 < M; c0 += mmax) {
+    GemvArgs b = a;
+    b.M = std::min(mmax, M - c0);
+    b.x = x + size_t(c0) * ldx;
+    b.y = y ? y + size_t(c0) * ldy : nullptr;
+    b.resid = resid ? resid + size_t(c0) * ldr : nullptr;
+    b.q = q ? q + size_t(c0) * ldq : nullptr;
+    b.token_offset = token_offset + c0;
+    check(launch_gemv(b, pro, epi, stream_), "gemv");
+  }
+}
+
+void Model::enqueue_layers(int T) {
+  const ModelConfig& c = cfg_;
+  const int H = int(c.hidden), F = int(c.ffn), hd = int(c.head_dim());
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    const DevLayer& L = layers_[l];
+    // RMSNorm(eps 1e-6, layer.rs:51-57) -> Q/K/V projections (attention.rs:80-129)
+    // -> RoPE (:140-143) -> KV append (:162)
+    const DevWeight qkv[3] = {L.q, L.k, L.v};
+    gemv(qkv, 3, H, T, x_, H, L.attn_norm, 1e-6f, PRO_RMSNORM, EPI_QKV, nullptr, 0, nullptr, 0, q_, H, int(l), 0);
+    // attention over the cache (attention.rs:173, :332-435)
+    AttnArgs a{};
+    a.q = q_;
+    const size_t esz = opt_.kv_half ? 2 : 4;
+    a.kc = static_cast<uint8_t*>(kcache_) + size_t(l) * kv_layer_elems_ * esz;
+    a.vc = static_cast<uint8_t*>(vcache_) + size_t(l) * kv_layer_elems_ * esz;
+    a.kv_half = int(opt_.kv_half);
+    a.out = att_;
+    a.part = part_;
+    a.ticket = ticket_;
+    a.n_heads = int(c.heads);
+    a.n_kv = int(c.kv_heads);
+    a.head_dim = hd;
+    a.max_seq = int(max_seq_);
+    a.T = T;
+    if (T == 1) {
+      a.chunk = DECODE_CHUNK;
+      a.max_splits = max_splits_;
+    } else {
+      a.chunk = 256;
+      a.max_splits = int((max_seq_ + 255) / 256);
+    }
+    a.scale = attn_scale_;
+    a.st = st_;
+    check(launch_attention(a, stream_), "attention");
+    // output projection + residual (attention.rs:182-191, layer.rs:68)
+    const DevWeight o[1] = {L.o};
+    gemv(o, 1, H, T, att_, H, nullptr, 0.0f, PRO_NONE, EPI_RESID, h_, H, x_, H, nullptr, 0, -1, 0);
+    // RMSNorm(eps 1e-6, layer.rs:71-77) -> gate/up -> SwiGLU (ffn.rs:60-94)
+    const DevWeight gu[2] = {L.gate, L.up};
+    gemv(gu, 2, H, T, h_, H, L.ffn_norm, 1e-6f, PRO_RMSNORM, EPI_SWIGLU, act_, F, nullptr, 0, nullptr, 0, -1, 0);
+    // down projection + residual (ffn.rs:97-106, layer.rs:86)
+    const DevWeight dn[1] = {L.down};
+    gemv(dn, 1, F, T, act_, F, nullptr, 0.0f, PRO_NONE, EPI_RESID, x_, H, h_, H, nullptr, 0, -1, 0);
+  }
+}
+
+// final RMSNorm with the config eps (model.rs:937-943) + LM head on the last
+// token (model.rs:975-1037)
+void Model::enqueue_lm_head(int T) {
+  const int H = int(cfg_.hidden);
+  const DevWeight head[1] = {lm_head_};
+  gemv(head, 1, H, 1, x_ + size_t(T - 1) * H, H, out_norm_, cfg_.eps, PRO_RMSNORM, EPI_STORE, logits_,
+       int(cfg_.vocab), nullptr, 0, nullptr, 0, -1, 0);
+}
+
+void Model::enqueue_forward(const uint32_t* dev_ids, int T, bool from_hist) {
+  if (from_hist) check(launch_embed_last(emb_, int(cfg_.vocab), int(cfg_.hidden), hist_, x_, st_, stream_), "embed");
+  else check(launch_embed(emb_, int(cfg_.vocab), int(cfg_.hidden), dev_ids, T, x_, st_, stream_), "embed");
+  enqueue_layers(T);
+}
+
+void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logits_out) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (n == 0) throw WcbError(E_INVALID, "Invalid tensor shape: empty token sequence");
+  if (kv_len_ + n > max_seq_)
+    throw WcbError(E_PARSE, "Parse error: KV cache overflow: " + std::to_string(kv_len_) + " + " + std::to_string(n) +
+                                " > " + std::to_string(max_seq_));
+  if (position + n > rope_len_) build_rope(uint32_t(std::max<size_t>(position + n, size_t(rope_len_) * 2)));
+  std::memcpy(host_ids_, ids, n * sizeof(uint32_t));
+  check(cudaMemcpyAsync(ids_, host_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "upload ids");
+  for (size_t c0 = 0; c0 < n; c0 += size_t(t_max_)) {
+    const int T = int(std::min(n - c0, size_t(t_max_)));
+    set_state(int(position + c0), int(kv_len_ + c0), T);
+    enqueue_forward(ids_ + c0, T, false);
+  }
+  const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
+  enqueue_lm_head(last_T);
+  if (logits_out)
+    check(cudaMemcpyAsync(logits_out, logits_, sizeof(float) * cfg_.vocab, cudaMemcpyDeviceToHost, stream_),
+          "download logits");
+  check(cudaStreamSynchronize(stream_), "forward");
+  kv_len_ += n;
+}
+
+void Model::decode_steps(int steps) {
+  for (int i = 0; i < steps; ++i) {
+    if (decode_exec_) {
+      check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
+    } else {
+      enqueue_forward(nullptr, 1, true);
+      enqueue_lm_head(1);
+      check(launch_sample_argmax(logits_, int(cfg_.vocab), work_, hist_, graph_rep_, tok_, st_, 1, 0, stream_),
+            "sample");
+    }
+  }
+}
+
+void Model::capture_decode_graph() {
+  cudaGraph_t g = nullptr;
+  check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+  try {
+    enqueue_forward(nullptr, 1, true);
+    enqueue_lm_head(1);
+    check(launch_sample_argmax(logits_, int(cfg_.vocab), work_, hist_, graph_rep_, tok_, st_, 1, 0, stream_),
+          "sample");
+  } catch (...) {
+    cudaStreamEndCapture(stream_, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  check(cudaStreamEndCapture(stream_, &g), "end capture");
+  cudaGraphExec_t e = nullptr;
+  const cudaError_t r = cudaGraphInstantiate(&e, g, 0);
+  if (r != cudaSuccess) {
+    cudaGraphDestroy(g);
+    check(r, "graph instantiate");
+  }
+  decode_graph_ = g;
+  decode_exec_ = e;
+}
+
+void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  ++session_;
+  sess_active_ = false;
+  clear_kv();  // model.rs:1344
+  if (n == 0) throw WcbError(E_PARSE, "Parse error: Empty token sequence");
+  sess_params_ = g;
+  sess_sampler_ = std::make_unique<Sampler>(g.seed, g.temperature, g.top_p, g.top_k, g.repetition_penalty);
+  sess_greedy_ = sess_sampler_->greedy();
+  sess_delivered_ = 0;
+  sess_tokens_.clear();
+  sess_done_ = false;
+  sess_steps_left_ = g.max_tokens > 1 ? size_t(g.max_tokens) - 1 : 0;
+  if (!sess_greedy_) {
+    // host-sampled path: Model::generate's loop with the LogitsProcessor on the host
+    std::vector<float> logits(cfg_.vocab);
+    for (size_t cs = 0; cs < n; cs += size_t(t_max_)) {
+      const size_t ce = std::min(cs + size_t(t_max_), n);
+      forward(prompt + cs, ce - cs, cs, ce == n ? logits.data() : nullptr);
+    }
+    sess_last_ = sess_sampler_->sample(logits.data(), logits.size());  // no EOS check (model.rs:1380)
+    sess_tokens_.push_back(sess_last_);
+    sess_done_ = sess_steps_left_ == 0;
+    sess_active_ = true;
+    return;
+  }
+  // greedy: the decode loop runs on the device (argmax + repetition penalty +
+  // EOS / max_tokens bookkeeping in the sampler kernel), no host round trip per token
+  if (n > max_seq_)
+    throw WcbError(E_PARSE, "Parse error: KV cache overflow: 0 + " + std::to_string(n) + " > " +
+                                std::to_string(max_seq_));
+  std::memcpy(host_ids_, prompt, n * sizeof(uint32_t));
+  check(cudaMemcpyAsync(ids_, host_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "upload ids");
+  for (size_t c0 = 0; c0 < n; c0 += size_t(t_max_)) {
+    const int T = int(std::min(n - c0, size_t(t_max_)));
+    set_state(int(c0), int(c0), T);
+    enqueue_forward(ids_ + c0, T, false);
+  }
+  const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
+  enqueue_lm_head(last_T);
+  const int eos = g.eos == 0xFFFFFFFFu ? -1 : int(g.eos);
+  check(launch_init_gen(st_, int(std::max<uint32_t>(g.max_tokens, 1)), eos, int(max_seq_), stream_), "init");
+  const float rep = g.repetition_penalty;
+  check(launch_sample_argmax(logits_, int(cfg_.vocab), work_, hist_, rep, tok_, st_, 1, 1, stream_), "sample");
+  if (!(opt_.flags & 1) && (!decode_exec_ || graph_rep_ != rep)) {
+    if (decode_exec_) {
+      cudaGraphExecDestroy(decode_exec_);
+      cudaGraphDestroy(decode_graph_);
+      decode_exec_ = nullptr;
+      decode_graph_ = nullptr;
+    }
+    graph_rep_ = rep;
+    capture_decode_graph();
+  }
+  graph_rep_ = rep;
+  sync_session_state();
+  sess_active_ = true;
+}
+
+void Model::sync_session_state() {
+  check(cudaMemcpyAsync(&sess_state_, st_, sizeof(StepState), cudaMemcpyDeviceToHost, stream_), "read state");
+  check(cudaStreamSynchronize(stream_), "generate");
+  kv_len_ = size_t(sess_state_.kv_len);
+  if (sess_state_.err == 1) {
+    sess_done_ = true;
+    throw WcbError(E_GENERIC, "Runtime error: NaN logit");
+  }
+  if (sess_state_.done) sess_done_ = true;
+}
+
+std::vector<uint32_t> Model::next(size_t max_tokens, bool* finished) {
+  if (!sess_active_) throw WcbError(E_INVALID, "Invalid argument: no active generation on this model");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  std::vector<uint32_t> out;
+  if (!sess_greedy_) {
+    std::vector<float> logits(cfg_.vocab);
+    while (sess_tokens_.size() - sess_delivered_ < max_tokens && !sess_done_) {
+      if (sess_steps_left_ == 0) { sess_done_ = true; break; }
+      forward(&sess_last_, 1, kv_len_, logits.data());
+      const uint32_t nx = sess_sampler_->sample(logits.data(), logits.size());
+      --sess_steps_left_;
+      if (nx == sess_params_.eos) { sess_done_ = true; break; }
+      sess_tokens_.push_back(nx);
+      sess_last_ = nx;
+      if (sess_steps_left_ == 0) sess_done_ = true;
+    }
+    const size_t take = std::min(max_tokens, sess_tokens_.size() - sess_delivered_);
+    out.assign(sess_tokens_.begin() + long(sess_delivered_), sess_tokens_.begin() + long(sess_delivered_ + take));
+    sess_delivered_ += take;
+    if (finished) *finished = sess_done_ && sess_delivered_ == sess_tokens_.size();
+    return out;
+  }
+  const size_t have = size_t(sess_state_.nhist) - sess_delivered_;
+  if (have < max_tokens && !sess_done_) {
+    const size_t steps = std::min(max_tokens - have, sess_steps_left_);
+    if (steps) {
+      decode_steps(int(steps));
+      sess_steps_left_ -= steps;
+    }
+    sync_session_state();
+    if (sess_steps_left_ == 0) sess_done_ = true;
+  }
+  const size_t avail = size_t(sess_state_.nhist) - sess_delivered_;
+  const size_t take = std::min(max_tokens, avail);
+  out.resize(take);
+  if (take)
+    check(cudaMemcpy(out.data(), hist_ + sess_delivered_, sizeof(uint32_t) * take, cudaMemcpyDeviceToHost),
+          "read tokens");
+  sess_delivered_ += take;
+  // a KV overflow ends the loop with an error (kv_cache.rs:48-53), reported once
+  // every token produced before it has been handed out
+  if (take == 0 && sess_state_.err == 2)
+    throw WcbError(E_PARSE, "Parse error: KV cache overflow: " + std::to_string(sess_state_.kv_len) + " + 1 > " +
+                                std::to_string(max_seq_));
+  if (finished) *finished = sess_done_ && sess_state_.err == 0 && sess_delivered_ == size_t(sess_state_.nhist);
+  return out;
+}
+
+std::vector<uint32_t> Model::generate(const uint32_t* prompt, size_t n, const GenParams& g) {
+  start(prompt, n, g);
+  std::vector<uint32_t> all;
+  bool fin = false;
+  while (!fin) {
+    std::vector<uint32_t> part = next(size_t(g.max_tokens) + 1, &fin);
+    all.insert(all.end(), part.begin(), part.end());
+    if (part.empty() && !fin) break;
+  }
+  return all;
+}
+
+}  // namespace wcb

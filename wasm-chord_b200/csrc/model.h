@@ -1,0 +1,149 @@
+// One model replica on one GPU: the device-resident counterpart of the
+// reference's Model (crates/wasm-chord-runtime/src/transformer/model.rs:19-44).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.h"
+#include "kernels.h"
+#include "sampler.h"
+
+namespace wcb {
+
+struct DevWeight {
+  uint8_t* ptr = nullptr;
+  int dtype = DT_Q4K;
+  uint32_t rows = 0, cols = 0;
+};
+
+struct DevLayer {
+  DevWeight q, k, v, o, gate, up, down;
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+};
+
+struct LoadOptions {
+  int device = 0;
+  uint32_t max_seq = 0;
+  uint32_t kv_half = 0;
+  uint32_t max_batch = 1;
+  uint32_t flags = 0;
+};
+
+struct GenParams {
+  uint32_t max_tokens = 100;
+  float temperature = 0.7f, top_p = 0.9f;
+  uint32_t top_k = 40;
+  float repetition_penalty = 1.1f;
+  uint64_t seed = 42;
+  uint32_t eos = 2;
+};
+
+class Model {
+ public:
+  Model(const std::string& path, const LoadOptions& opt);
+  ~Model();
+  Model(const Model&) = delete;
+  Model& operator=(const Model&) = delete;
+
+  const ModelConfig& config() const { return cfg_; }
+  cudaStream_t stream() const { return stream_; }
+  size_t kv_len() const { return kv_len_; }
+
+  // Model::forward (model.rs:832-1192); logits_out (host) may be null
+  void forward(const uint32_t* ids, size_t n, size_t position, float* logits_out);
+  void clear_kv() { kv_len_ = 0; }
+  // Model::generate (model.rs:1322-1415) on token ids
+  std::vector<uint32_t> generate(const uint32_t* prompt, size_t n, const GenParams& g);
+  // The same loop as a session (the reference's wasmchord_infer / next_token,
+  // abi.rs:119-200): start() clears the KV cache, prefills and samples the first
+  // token; next() returns up to max_tokens further tokens of the sequence,
+  // running decode steps as needed; *finished is set once EOS or max_tokens ends it.
+  void start(const uint32_t* prompt, size_t n, const GenParams& g);
+  std::vector<uint32_t> next(size_t max_tokens, bool* finished);
+  uint64_t session_id() const { return session_; }
+  // kernels launched by one greedy decode step
+  int launches_per_decode_step() const { return 3 + 5 * int(cfg_.layers); }
+
+ private:
+  void upload_weight(const GgufFile& f, const std::string& name, uint32_t rows, uint32_t cols, DevWeight& w,
+                     bool required_shape_only);
+  void upload_vector(const GgufFile& f, const std::string& name, uint32_t n, float fill, float*& dst);
+  void build_rope(uint32_t len);
+  void* dalloc(size_t bytes);
+  void set_state(int position, int kv_len, int n_tokens);
+  void enqueue_forward(const uint32_t* dev_ids, int T, bool from_hist);
+  void enqueue_layers(int T);
+  void enqueue_lm_head(int T);
+  void gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, int ldx, const float* norm_w, float eps,
+            int pro, int epi, float* y, int ldy, const float* resid, int ldr, float* q, int ldq, int layer,
+            int token_offset);
+  void check(cudaError_t e, const char* what);
+  void decode_steps(int steps);
+  void capture_decode_graph();
+
+  ModelConfig cfg_;
+  LoadOptions opt_;
+  int device_ = 0;
+  cudaStream_t stream_ = nullptr;
+  std::vector<void*> allocs_;
+
+  float* emb_ = nullptr;
+  float* out_norm_ = nullptr;
+  DevWeight lm_head_;
+  std::vector<DevLayer> layers_;
+
+  void* kcache_ = nullptr;  // [L][n_kv][max_seq][hd]
+  void* vcache_ = nullptr;
+  size_t kv_layer_elems_ = 0;
+  uint32_t max_seq_ = 0;
+  size_t kv_len_ = 0;
+
+  float* rope_cos_ = nullptr;
+  float* rope_sin_ = nullptr;
+  uint32_t rope_len_ = 0;
+  float attn_scale_ = 0.0f;
+
+  int t_max_ = 0;  // tokens per forward launch
+  StepState* st_ = nullptr;
+  uint32_t* ids_ = nullptr;
+  uint32_t* hist_ = nullptr;
+  uint32_t hist_cap_ = 0;
+  uint32_t* tok_ = nullptr;
+  float* x_ = nullptr;
+  float* h_ = nullptr;
+  float* q_ = nullptr;
+  float* att_ = nullptr;
+  float* act_ = nullptr;
+  float* logits_ = nullptr;
+  float* work_ = nullptr;
+  float* part_ = nullptr;
+  int* ticket_ = nullptr;
+  int max_splits_ = 0;
+  uint32_t* host_ids_ = nullptr;  // pinned staging
+
+  void sync_session_state();
+
+  // session
+  uint64_t session_ = 0;
+  bool sess_active_ = false;
+  bool sess_greedy_ = true;
+  bool sess_done_ = true;
+  size_t sess_delivered_ = 0;
+  size_t sess_steps_left_ = 0;
+  GenParams sess_params_;
+  std::unique_ptr<Sampler> sess_sampler_;
+  std::vector<uint32_t> sess_tokens_;  // host-sampled path: generated ids
+  uint32_t sess_last_ = 0;
+  StepState sess_state_{};
+
+  cudaGraphExec_t decode_exec_ = nullptr;
+  cudaGraph_t decode_graph_ = nullptr;
+  float graph_rep_ = -1.0f;
+};
+
+}  // namespace wcb

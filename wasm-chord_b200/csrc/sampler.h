@@ -1,0 +1,42 @@
+// Host LogitsProcessor: crates/wasm-chord-runtime/src/sampling.rs:29-264.
+// with_params chooses ArgMax when temperature < 1e-7, else top-k-then-top-p,
+// top-k, top-p or all (:57-78); sample() applies the repetition penalty once per
+// previously sampled occurrence (:86-103), then argmax (the LAST maximum wins,
+// :118-125; a NaN logit is an error where the reference panics) or temperature
+// softmax + top-k / top-p + a weighted draw (:106-229). The weighted draw uses a
+// splitmix64 stream seeded with `seed`; the reference's rand 0.9 StdRng stream
+// is not reproduced, so sampled (temperature > 0) sequences differ from it.
+#pragma once
+#include <cstdint>
+#include <vector>
+
+namespace wcb {
+
+class Sampler {
+ public:
+  enum Kind { ARGMAX, ALL, TOPK, TOPP, TOPK_TOPP };
+  Sampler(uint64_t seed, double temperature, double top_p, uint32_t top_k, float repetition_penalty);
+  uint32_t sample(float* logits, size_t n);  // throws WcbError on NaN / invalid weights
+  void penalize(float* logits, size_t n) const;
+  static uint32_t argmax(const float* logits, size_t n);
+  Kind kind() const { return kind_; }
+  bool greedy() const { return kind_ == ARGMAX; }
+  float repetition_penalty() const { return rep_; }
+  std::vector<uint32_t>& history() { return prev_; }
+
+ private:
+  float uniform();
+  uint32_t multinomial(const std::vector<float>& p);
+  uint32_t top_p(std::vector<float>& p, float tp);
+  static void keep_top_k(std::vector<float>& p, size_t k);
+  static void renormalize(std::vector<float>& p);
+
+  uint64_t state_;
+  Kind kind_;
+  double temperature_, top_p_;
+  size_t top_k_;
+  float rep_;
+  std::vector<uint32_t> prev_;
+};
+
+}  // namespace wcb

@@ -1,0 +1,334 @@
+"""Python binding of the wcb C ABI (include/wcb.h), shaped like wasm-chord's
+``wasm-chord-runtime`` API: ``Model.load_from_gguf`` / ``forward`` /
+``generate`` / ``clear_kv_cache`` and ``GenerationConfig`` with the reference
+defaults (crates/wasm-chord-runtime/src/transformer/config.rs:60-78).
+
+The binding only marshals arguments; all compute runs in ``libwcb.so`` on the
+GPU. There is no CPU fallback: loading a model without a CUDA device raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+import os
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libwcb.so")
+
+WCB_OK = 0
+ERROR_NAMES = {
+    0: "Ok", 1: "GenericFailure", 2: "OutOfMemory", 3: "InvalidArgument", 4: "ModelParseError",
+    5: "BackendUnsupported", 6: "ShaderCompileError", 7: "IoError",
+}
+DTYPE_Q4_K = 12
+DTYPE_Q6_K = 14
+KV_F32 = 0
+KV_F16 = 1
+
+EXPORTED = [
+    "wcb_gen_config_default", "wcb_model_load", "wcb_model_free", "wcb_model_config_get", "wcb_forward",
+    "wcb_clear_kv", "wcb_kv_len", "wcb_generate_tokens", "wcb_generate_batch", "wcb_sampler_new",
+    "wcb_sampler_sample", "wcb_sampler_free", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
+    "wcb_repack_q6k_dev", "wcb_gemv_dev", "wcb_model_stream", "wcb_infer", "wcb_next_tokens",
+    "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step",
+]
+
+
+class WcbError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{ERROR_NAMES.get(code, code)}: {message}")
+        self.code = code
+        self.message = message
+
+
+class _LoadOpts(C.Structure):
+    _fields_ = [("device", C.c_int32), ("max_seq", C.c_uint32), ("kv_dtype", C.c_uint32),
+                ("max_batch", C.c_uint32), ("flags", C.c_uint32)]
+
+
+class _ModelConfig(C.Structure):
+    _fields_ = [("vocab_size", C.c_uint32), ("hidden_size", C.c_uint32), ("num_layers", C.c_uint32),
+                ("num_heads", C.c_uint32), ("num_kv_heads", C.c_uint32), ("intermediate_size", C.c_uint32),
+                ("max_seq_len", C.c_uint32), ("head_dim", C.c_uint32), ("rms_norm_eps", C.c_float),
+                ("rope_theta", C.c_float)]
+
+
+class _GenConfig(C.Structure):
+    _fields_ = [("max_tokens", C.c_uint32), ("temperature", C.c_float), ("top_p", C.c_float),
+                ("top_k", C.c_uint32), ("repetition_penalty", C.c_float), ("seed", C.c_uint64),
+                ("eos_id", C.c_uint32)]
+
+
+_LIB = None
+
+
+def lib() -> C.CDLL:
+    """Loads libwcb.so (building it first if it is missing)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(LIB_PATH):
+        from . import build
+        build.build_lib()
+    L = C.CDLL(LIB_PATH)
+    u32, sz, vp = C.c_uint32, C.c_size_t, C.c_void_p
+    L.wcb_gen_config_default.argtypes = [C.POINTER(_GenConfig)]
+    L.wcb_gen_config_default.restype = None
+    L.wcb_model_load.argtypes = [C.c_char_p, C.POINTER(_LoadOpts), C.POINTER(u32)]
+    L.wcb_model_free.argtypes = [u32]
+    L.wcb_model_config_get.argtypes = [u32, C.POINTER(_ModelConfig)]
+    L.wcb_forward.argtypes = [u32, vp, sz, sz, vp]
+    L.wcb_clear_kv.argtypes = [u32]
+    L.wcb_kv_len.argtypes = [u32, C.POINTER(sz)]
+    L.wcb_generate_tokens.argtypes = [u32, vp, sz, C.POINTER(_GenConfig), vp, sz, C.POINTER(sz)]
+    L.wcb_generate_batch.argtypes = [u32, vp, vp, sz, C.POINTER(_GenConfig), vp, sz, vp]
+    L.wcb_sampler_new.argtypes = [C.POINTER(_GenConfig), C.POINTER(u32)]
+    L.wcb_sampler_sample.argtypes = [u32, vp, sz, C.POINTER(u32)]
+    L.wcb_sampler_free.argtypes = [u32]
+    L.wcb_last_error.argtypes = [C.c_char_p, sz]
+    L.wcb_last_error.restype = sz
+    L.wcb_version.restype = C.c_char_p
+    L.wcb_dequant_dev.argtypes = [vp, u32, sz, vp, vp]
+    L.wcb_repack_q6k_dev.argtypes = [vp, sz, vp, vp]
+    L.wcb_gemv_dev.argtypes = [vp, u32, sz, sz, vp, sz, vp, vp]
+    L.wcb_model_stream.argtypes = [u32, C.POINTER(vp)]
+    L.wcb_infer.argtypes = [u32, vp, sz, C.POINTER(_GenConfig), C.POINTER(u32)]
+    L.wcb_next_tokens.argtypes = [u32, sz, vp, C.POINTER(sz), C.POINTER(u32)]
+    L.wcb_next_token.argtypes = [u32, C.POINTER(u32)]
+    L.wcb_next_token.restype = C.c_int32
+    L.wcb_close_stream.argtypes = [u32]
+    L.wcb_model_launches_per_step.argtypes = [u32, C.POINTER(u32)]
+    for name in EXPORTED:
+        f = getattr(L, name)
+        if f.restype is C.c_int:  # ctypes default
+            f.restype = u32
+    _LIB = L
+    return L
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(4096)
+    lib().wcb_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def _check(code: int) -> None:
+    if code != WCB_OK:
+        raise WcbError(code, last_error())
+
+
+def version() -> str:
+    return lib().wcb_version().decode()
+
+
+@dataclasses.dataclass
+class TransformerConfig:
+    """transformer/config.rs:6-41"""
+    vocab_size: int
+    hidden_size: int
+    num_layers: int
+    num_heads: int
+    num_kv_heads: int
+    intermediate_size: int
+    max_seq_len: int
+    rms_norm_eps: float
+    rope_theta: float
+    head_dim: int
+
+
+@dataclasses.dataclass
+class GenerationConfig:
+    """GenerationConfig (config.rs:60-78) with its defaults, plus the sampler
+    seed generate() fixes at 42 (model.rs:1336) and the tokenizer's EOS id."""
+    max_tokens: int = 100
+    temperature: float = 0.7
+    top_p: float = 0.9
+    top_k: int = 40
+    repetition_penalty: float = 1.1
+    seed: int = 42
+    eos_id: Optional[int] = 2
+
+    def _c(self) -> _GenConfig:
+        c = _GenConfig()
+        c.max_tokens = int(self.max_tokens)
+        c.temperature = float(self.temperature)
+        c.top_p = float(self.top_p)
+        c.top_k = int(self.top_k)
+        c.repetition_penalty = float(self.repetition_penalty)
+        c.seed = int(self.seed)
+        c.eos_id = 0xFFFFFFFF if self.eos_id is None else int(self.eos_id)
+        return c
+
+
+def _u32(ids: Sequence[int]) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(ids, dtype=np.uint32))
+
+
+class Model:
+    """One model replica on one GPU (the reference's ``Model``)."""
+
+    def __init__(self, handle: int):
+        self._h = handle
+        cfg = _ModelConfig()
+        _check(lib().wcb_model_config_get(handle, C.byref(cfg)))
+        self.config = TransformerConfig(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
+                                        cfg.num_kv_heads, cfg.intermediate_size, cfg.max_seq_len,
+                                        cfg.rms_norm_eps, cfg.rope_theta, cfg.head_dim)
+
+    @classmethod
+    def load_from_gguf(cls, path: str, device: int = 0, max_seq: int = 0, kv_dtype: int = KV_F32,
+                       max_batch: int = 1, use_graphs: bool = True) -> "Model":
+        o = _LoadOpts(device, max_seq, kv_dtype, max_batch, 0 if use_graphs else 1)
+        h = C.c_uint32(0)
+        _check(lib().wcb_model_load(os.fsencode(path), C.byref(o), C.byref(h)))
+        return cls(h.value)
+
+    def close(self) -> None:
+        if self._h:
+            lib().wcb_model_free(self._h)
+            self._h = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def handle(self) -> int:
+        return self._h
+
+    def forward(self, token_ids: Sequence[int], position: int) -> np.ndarray:
+        """Model::forward (model.rs:832): logits of the last token, float32[vocab]."""
+        ids = _u32(token_ids)
+        out = np.empty(self.config.vocab_size, dtype=np.float32)
+        _check(lib().wcb_forward(self._h, ids.ctypes.data, ids.size, int(position), out.ctypes.data))
+        return out
+
+    def clear_kv_cache(self) -> None:
+        _check(lib().wcb_clear_kv(self._h))
+
+    def kv_len(self) -> int:
+        n = C.c_size_t(0)
+        _check(lib().wcb_kv_len(self._h, C.byref(n)))
+        return n.value
+
+    def generate_tokens(self, prompt_ids: Sequence[int], config: GenerationConfig) -> List[int]:
+        """Model::generate (model.rs:1322-1415) on token ids; returns the generated ids."""
+        ids = _u32(prompt_ids)
+        cap = max(1, int(config.max_tokens))
+        out = np.zeros(cap, dtype=np.uint32)
+        n = C.c_size_t(0)
+        c = config._c()
+        _check(lib().wcb_generate_tokens(self._h, ids.ctypes.data, ids.size, C.byref(c), out.ctypes.data, cap,
+                                         C.byref(n)))
+        return out[: min(n.value, cap)].tolist()
+
+    def generate_batch(self, prompts: Sequence[Sequence[int]], config: GenerationConfig) -> List[List[int]]:
+        flat = _u32([t for p in prompts for t in p])
+        lens = np.asarray([len(p) for p in prompts], dtype=np.uintp)
+        cap = max(1, int(config.max_tokens))
+        out = np.zeros((len(prompts), cap), dtype=np.uint32)
+        n_out = np.zeros(len(prompts), dtype=np.uintp)
+        c = config._c()
+        _check(lib().wcb_generate_batch(self._h, flat.ctypes.data, lens.ctypes.data, len(prompts), C.byref(c),
+                                        out.ctypes.data, cap, n_out.ctypes.data))
+        return [out[i, : min(int(n_out[i]), cap)].tolist() for i in range(len(prompts))]
+
+    def infer(self, prompt_ids: Sequence[int], config: GenerationConfig) -> "TokenStream":
+        """Starts generate()'s loop as a stream (wasmchord_infer, abi.rs:119-150)."""
+        ids = _u32(prompt_ids)
+        c = config._c()
+        s = C.c_uint32(0)
+        _check(lib().wcb_infer(self._h, ids.ctypes.data, ids.size, C.byref(c), C.byref(s)))
+        return TokenStream(s.value)
+
+    def launches_per_step(self) -> int:
+        n = C.c_uint32(0)
+        _check(lib().wcb_model_launches_per_step(self._h, C.byref(n)))
+        return n.value
+
+    def stream(self) -> int:
+        s = C.c_void_p(0)
+        _check(lib().wcb_model_stream(self._h, C.byref(s)))
+        return s.value or 0
+
+
+class TokenStream:
+    """A generation stream (wasmchord_next_token / close_stream, abi.rs:155-200)."""
+
+    def __init__(self, handle: int):
+        self._h = handle
+        self.finished = False
+
+    def next_tokens(self, max_tokens: int) -> List[int]:
+        out = np.zeros(max(1, max_tokens), dtype=np.uint32)
+        n = C.c_size_t(0)
+        fin = C.c_uint32(0)
+        _check(lib().wcb_next_tokens(self._h, max_tokens, out.ctypes.data, C.byref(n), C.byref(fin)))
+        self.finished = bool(fin.value)
+        return out[: n.value].tolist()
+
+    def next_token(self) -> Optional[int]:
+        t = C.c_uint32(0)
+        r = lib().wcb_next_token(self._h, C.byref(t))
+        if r == -2:
+            raise WcbError(1, last_error())
+        return None if r == -1 else t.value
+
+    def close(self) -> None:
+        if self._h:
+            lib().wcb_close_stream(self._h)
+            self._h = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class LogitsProcessor:
+    """sampling.rs:29-264 through the C ABI (host sampler)."""
+
+    def __init__(self, seed: int, temperature: float, top_p: float, top_k: int, repetition_penalty: float):
+        c = GenerationConfig(temperature=temperature, top_p=top_p, top_k=top_k,
+                             repetition_penalty=repetition_penalty, seed=seed)._c()
+        h = C.c_uint32(0)
+        _check(lib().wcb_sampler_new(C.byref(c), C.byref(h)))
+        self._h = h.value
+
+    def sample(self, logits: np.ndarray) -> int:
+        if logits.dtype != np.float32 or not logits.flags.c_contiguous:
+            raise TypeError("logits must be a contiguous float32 array (it is modified in place)")
+        t = C.c_uint32(0)
+        _check(lib().wcb_sampler_sample(self._h, logits.ctypes.data, logits.size, C.byref(t)))
+        return t.value
+
+    def __del__(self):
+        try:
+            lib().wcb_sampler_free(self._h)
+        except Exception:
+            pass
+
+
+# ---- kernel-level entry points on device pointers ---------------------------
+def dequant_dev(blocks_ptr: int, dtype: int, nblocks: int, out_ptr: int, stream: int = 0) -> None:
+    _check(lib().wcb_dequant_dev(blocks_ptr, dtype, nblocks, out_ptr, stream or None))
+
+
+def repack_q6k_dev(packed_ptr: int, nblocks: int, padded_ptr: int, stream: int = 0) -> None:
+    _check(lib().wcb_repack_q6k_dev(packed_ptr, nblocks, padded_ptr, stream or None))
+
+
+def gemv_dev(w_ptr: int, dtype: int, n: int, k: int, x_ptr: int, m: int, y_ptr: int, stream: int = 0) -> None:
+    _check(lib().wcb_gemv_dev(w_ptr, dtype, n, k, x_ptr, m, y_ptr, stream or None))
