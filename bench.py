@@ -118,7 +118,7 @@ def ensure_model(rank, world, dist):
     return path
 
 
-def gemv_roofline(torch, wcb, stream_ptr, cfg, peak):
+def gemv_roofline(torch, wcb, stream_ptr, cfg, peak, reps_per_copy=8):
     """Times the dominant kernel of the decode step — the fused Q4_K dequant-GEMV
     at the FFN gate+up shape [2*F, H], M = 1 — on the stream it is launched on,
     rotating over enough weight copies that each launch reads from HBM."""
@@ -132,9 +132,9 @@ def gemv_roofline(torch, wcb, stream_ptr, cfg, peak):
     x = torch.from_numpy(synth.normal(98, 1, k, 0.0, 1.0)).cuda()
     y = torch.empty(n, dtype=torch.float32, device="cuda")
     s = torch.cuda.ExternalStream(stream_ptr)
-    reps = 8 * copies
+    reps = reps_per_copy * copies
     with torch.cuda.stream(s):
-        for i in range(2 * copies):
+        for i in range(min(2, reps_per_copy) * copies):
             wcb.gemv_dev(ws[i % copies].data_ptr(), wcb.DTYPE_Q4_K, n, k, x.data_ptr(), 1, y.data_ptr(), stream_ptr)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
@@ -242,10 +242,12 @@ def run_ours(args, rank, world, dist):
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
         e0.record(s)
         toks = stream.next_tokens(K)
         e1.record(s)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     if world > 1:
         dist.barrier()
     assert len(toks) == K, (len(toks), K)
@@ -320,7 +322,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemv-only", type=int, default=0, metavar="REPS",
+                    help="only time the dominant GEMV (REPS launches per weight copy) and print its line")
     args = ap.parse_args()
+    if args.gemv_only:
+        import torch
+        import wcb
+        from wcb import synth
+        cfg = synth.PRESETS["tinyllama"]
+        stream_ptr = torch.cuda.current_stream().cuda_stream
+        r = gemv_roofline(torch, wcb, stream_ptr, cfg, peaks()[0], reps_per_copy=args.gemv_only)
+        print(json.dumps(r), flush=True)
+        return
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))

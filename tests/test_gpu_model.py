@@ -195,3 +195,38 @@ def test_tinyllama_64_greedy_tokens_identical(model_dir, gpu):
     assert got == ref, f"first mismatch at {next(i for i, (a, b) in enumerate(zip(got, ref)) if a != b)}; " \
                        f"smallest top-1/top-2 gap {min(gaps):.3g}"
     m.close()
+
+
+def test_stream_api_matches_generate(tiny_pair):
+    m, o = tiny_pair
+    prompt = synth.random_prompt(18, 512, seed=30).tolist()
+    cfg = wcb.GenerationConfig(max_tokens=25, temperature=0.0, repetition_penalty=1.1, eos_id=None)
+    ref = o.generate(prompt, 25, repetition_penalty=1.1, eos_id=None)
+    s = m.infer(prompt, cfg)
+    got = []
+    for chunk in (1, 3, 7, 100):
+        got += s.next_tokens(chunk)
+    assert got == ref and s.finished
+    assert s.next_tokens(4) == []
+    s2 = m.infer(prompt, cfg)
+    one = []
+    while True:
+        t = s2.next_token()
+        if t is None:
+            break
+        one.append(t)
+    assert one == ref
+    with pytest.raises(wcb.WcbError):  # a newer generation on the model invalidates the old stream
+        s.next_tokens(1)
+    s.close()
+    s2.close()
+
+
+def test_stream_api_stops_at_eos(tiny_pair):
+    m, o = tiny_pair
+    prompt = synth.random_prompt(11, 512, seed=31).tolist()
+    base = o.generate(prompt, 20, eos_id=None)
+    cfg = wcb.GenerationConfig(max_tokens=20, temperature=0.0, repetition_penalty=1.0, eos_id=base[5])
+    s = m.infer(prompt, cfg)
+    got = s.next_tokens(50)
+    assert got == o.generate(prompt, 20, eos_id=base[5]) and s.finished

@@ -332,8 +332,8 @@ uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const f
   if (dtype != WCB_DTYPE_Q4_K && dtype != WCB_DTYPE_Q6_K)
     return fail(WCB_ERR_INVALID_ARGUMENT, "Unsupported data type: gemv supports Q4_K and Q6_K");
   if (!w || !x || !y) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
-  if (k == 0 || k % 256 || n == 0 || n % 4 || m == 0 || m > 64 || k > (1u << 20) || n > (1u << 28))
-    return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid tensor shape: need k % 256 == 0, n % 4 == 0, 1 <= m <= 64");
+  if (k == 0 || k % 256 || n == 0 || n % 4 || m == 0 || m > 4096 || k > (1u << 20) || n > (1u << 28))
+    return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid tensor shape: need k % 256 == 0, n % 4 == 0, 1 <= m <= 4096");
   static bool configured = false;
   if (!configured) {
     const cudaError_t e = wcb::gemv_configure_all();

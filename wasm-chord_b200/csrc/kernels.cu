@@ -83,57 +83,140 @@ __device__ __forceinline__ XPlanes carve(uint8_t* smem, int M, int K) {
   return p;
 }
 
+// Quantises 8 consecutive activations held by one thread into the planes.
+// Four consecutive threads cover one 32-value group (max reduced over them),
+// two cover a 16-value half (sum of X).
+__device__ __forceinline__ void quant8(const float (&v)[8], size_t off, int kglob, const XPlanes& p, int K, int t) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+  bool bad = false;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) bad |= !(fabsf(v[e]) <= FLT_MAX);  // NaN / inf
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  bad = __shfl_xor_sync(0xffffffffu, int(bad), 1) | bad;
+  bad = __shfl_xor_sync(0xffffffffu, int(bad), 2) | bad;
+  int X[8];
+  float s;
+  if (!bad && amax > 0.0f) {
+    const float inv = XQ_MAX / amax;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) X[e] = max(-8388607, min(8388607, __float2int_rn(v[e] * inv)));
+    s = amax / XQ_MAX;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) X[e] = 0;
+    s = bad ? __int_as_float(0x7fc00000) : 0.0f;  // inf / NaN input -> NaN output
+  }
+  uint32_t w0[2], w1[2], w2[2];
+  int sx = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int x = X[4 * h + e];
+      b0 |= uint32_t(x & 0xFF) << (8 * e);
+      b1 |= uint32_t((x >> 8) & 0xFF) << (8 * e);
+      b2 |= uint32_t((x >> 16) & 0xFF) << (8 * e);
+      sx += x;
+    }
+    w0[h] = b0;
+    w1[h] = b1;
+    w2[h] = b2;
+  }
+  *reinterpret_cast<uint2*>(p.l0 + off) = make_uint2(w0[0], w0[1]);
+  *reinterpret_cast<uint2*>(p.l1 + off) = make_uint2(w1[0], w1[1]);
+  *reinterpret_cast<uint2*>(p.l2 + off) = make_uint2(w2[0], w2[1]);
+  sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+  const int lane = threadIdx.x & 31;
+  if ((lane & 1) == 0) p.sum16[size_t(t) * (K / 16) + kglob / 16] = s * float(sx);
+  if ((lane & 3) == 0) p.scale[size_t(t) * (K / 32) + kglob / 32] = s;
+}
+
 // Builds the activation planes. PRO_RMSNORM normalises row h first exactly as
 // CandleTensorBackend::rms_norm does (candle_tensor_backend.rs:30-57):
 // m = sqrt(sum(h^2)/K + eps), x = h / m * w (IEEE divide and sqrt).
+// Every thread owns 8 consecutive values of each 2048-value round; the loads of
+// up to four rounds are issued together so the prologue costs one or two DRAM
+// round trips, not one per group.
 template <int M, int PRO>
 __device__ void build_planes(const GemvArgs& a, const XPlanes& p) {
   const int K = a.K;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x;
+  constexpr int ROUND = GEMV_THREADS * 8;
+  constexpr int BATCH = 4;
+  const int rounds = (K + ROUND - 1) / ROUND;
   __shared__ float s_part[GEMV_WARPS];
   __shared__ float s_m[4];
-  if (PRO == PRO_RMSNORM) {
-    for (int t = 0; t < M; ++t) {
-      const float* h = a.x + size_t(t) * a.ldx;
+  for (int t = 0; t < M; ++t) {
+    const float* x = a.x + size_t(t) * a.ldx;
+    if (PRO == PRO_RMSNORM) {
       float ss = 0.0f;
-      for (int k = threadIdx.x; k < K; k += GEMV_THREADS) ss = __fadd_rn(ss, __fmul_rn(h[k], h[k]));
+      for (int r0 = 0; r0 < rounds; r0 += BATCH) {
+        float4 v[BATCH][2];
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          const int k = (r0 + b) * ROUND + tid * 8;
+          if (r0 + b < rounds && k < K) {
+            v[b][0] = __ldg(reinterpret_cast<const float4*>(x + k));
+            v[b][1] = __ldg(reinterpret_cast<const float4*>(x + k + 4));
+          } else {
+            v[b][0] = v[b][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            ss = __fadd_rn(ss, __fmul_rn(v[b][h].x, v[b][h].x));
+            ss = __fadd_rn(ss, __fmul_rn(v[b][h].y, v[b][h].y));
+            ss = __fadd_rn(ss, __fmul_rn(v[b][h].z, v[b][h].z));
+            ss = __fadd_rn(ss, __fmul_rn(v[b][h].w, v[b][h].w));
+          }
+      }
       ss = warp_sum(ss);
       if (lane == 0) s_part[warp] = ss;
       __syncthreads();
-      if (threadIdx.x == 0) {
+      if (tid == 0) {
         float tot = 0.0f;
         for (int w = 0; w < GEMV_WARPS; ++w) tot = __fadd_rn(tot, s_part[w]);
         s_m[t] = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(K)), a.eps));
       }
       __syncthreads();
     }
-  }
-  const int groups = M * (K / 32);
-  for (int gi = warp; gi < groups; gi += GEMV_WARPS) {
-    const int t = gi / (K / 32);
-    const int k0 = (gi % (K / 32)) * 32;
-    float v = a.x[size_t(t) * a.ldx + k0 + lane];
-    if (PRO == PRO_RMSNORM) v = __fmul_rn(__fdiv_rn(v, s_m[t]), a.norm_w[k0 + lane]);
-    const float amax = warp_max(fabsf(v));
-    int X = 0;
-    float s;
-    if (amax > 0.0f && amax <= FLT_MAX) {
-      const float inv = XQ_MAX / amax;
-      X = __float2int_rn(v * inv);
-      X = max(-8388607, min(8388607, X));
-      s = amax / XQ_MAX;
-    } else {
-      s = (amax == 0.0f) ? 0.0f : __int_as_float(0x7fc00000);  // inf / NaN input -> NaN output
-    }
-    const size_t off = size_t(t) * K + k0 + lane;
-    p.l0[off] = uint8_t(X & 0xFF);
-    p.l1[off] = uint8_t((X >> 8) & 0xFF);
-    p.l2[off] = uint8_t((X >> 16) & 0xFF);
-    int sx = X;
+    for (int r0 = 0; r0 < rounds; r0 += BATCH) {
+      float4 v[BATCH][2], w[BATCH][2];
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);  // sums of 16-lane halves
-    if (lane == 0) p.scale[size_t(t) * (K / 32) + k0 / 32] = s;
-    if ((lane & 15) == 0) p.sum16[size_t(t) * (K / 16) + (k0 + lane) / 16] = s * float(sx);
+      for (int b = 0; b < BATCH; ++b) {
+        const int k = (r0 + b) * ROUND + tid * 8;
+        if (r0 + b < rounds && k < K) {
+          v[b][0] = __ldg(reinterpret_cast<const float4*>(x + k));
+          v[b][1] = __ldg(reinterpret_cast<const float4*>(x + k + 4));
+          if (PRO == PRO_RMSNORM) {
+            w[b][0] = __ldg(reinterpret_cast<const float4*>(a.norm_w + k));
+            w[b][1] = __ldg(reinterpret_cast<const float4*>(a.norm_w + k + 4));
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < BATCH; ++b) {
+        const int k = (r0 + b) * ROUND + tid * 8;
+        // whole warps are in or out of range (K is a multiple of 256)
+        if (r0 + b < rounds && k < K) {
+          float e[8] = {v[b][0].x, v[b][0].y, v[b][0].z, v[b][0].w, v[b][1].x, v[b][1].y, v[b][1].z, v[b][1].w};
+          if (PRO == PRO_RMSNORM) {
+            const float g[8] = {w[b][0].x, w[b][0].y, w[b][0].z, w[b][0].w,
+                                w[b][1].x, w[b][1].y, w[b][1].z, w[b][1].w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) e[i] = __fmul_rn(__fdiv_rn(e[i], s_m[t]), g[i]);
+          }
+          quant8(e, size_t(t) * K + k, k, p, K, t);
+        }
+      }
+    }
   }
   __syncthreads();
 }
@@ -236,212 +319,337 @@ __device__ __forceinline__ void q6k_chunk(const uint4& ql0, const uint4& ql1, co
   }
 }
 
-__device__ __forceinline__ void resolve_row(const GemvArgs& a, int vrow, const uint8_t*& w, int& dtype, int& local) {
-  int r = vrow;
-  for (int s = 0; s < a.nseg; ++s) {
-    if (r < a.seg[s].rows || s == a.nseg - 1) {
-      w = a.seg[s].w;
-      dtype = a.seg[s].dtype;
-      local = r;
-      return;
-    }
-    r -= a.seg[s].rows;
+// Programmatic dependent launch: a kernel launched with the PDL attribute may
+// start while its predecessor drains; griddepcontrol.wait blocks until the
+// predecessor has completed and its writes are visible (a no-op otherwise).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// order-preserving u32 image of a float (+0 and -0 compare equal, as in max_by)
+__device__ __forceinline__ uint32_t order_key(float v) {
+  if (v == 0.0f) v = 0.0f;
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int DT>
+struct WRegs;
+template <>
+struct WRegs<DT_Q4K> {
+  uint4 q[ROWS], h[ROWS];
+};
+template <>
+struct WRegs<DT_Q6K> {
+  uint4 l0[ROWS], l1[ROWS], qh[ROWS], sc[ROWS];
+  uint32_t d[ROWS];
+};
+
+__device__ __forceinline__ void load_chunk(WRegs<DT_Q4K>& r, const uint8_t* const (&rw)[ROWS], int c) {
+  const int b = c >> 3, j = c & 7;
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) {
+    const uint8_t* blk = rw[i] + size_t(b) * Q4K_BYTES;
+    r.h[i] = __ldg(reinterpret_cast<const uint4*>(blk));
+    r.q[i] = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * j));
   }
 }
 
-template <int M, int PRO, int EPI>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvArgs a) {
+__device__ __forceinline__ void load_chunk(WRegs<DT_Q6K>& r, const uint8_t* const (&rw)[ROWS], int c) {
+  const int b = c >> 2, hh = (c >> 1) & 1, aa = c & 1;
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) {
+    const uint8_t* blk = rw[i] + size_t(b) * Q6K_DEV_BYTES;
+    r.l0[i] = __ldg(reinterpret_cast<const uint4*>(blk + 64 * hh + 16 * aa));
+    r.l1[i] = __ldg(reinterpret_cast<const uint4*>(blk + 64 * hh + 32 + 16 * aa));
+    r.qh[i] = __ldg(reinterpret_cast<const uint4*>(blk + 128 + 32 * hh + 16 * aa));
+    r.sc[i] = __ldg(reinterpret_cast<const uint4*>(blk + 192));
+    r.d[i] = __ldg(reinterpret_cast<const unsigned short*>(blk + 208));
+  }
+}
+
+template <int M>
+__device__ __forceinline__ void compute_chunk(const WRegs<DT_Q4K>& r, int c, int K, const XPlanes& p,
+                                              float (&acc)[ROWS][M]) {
+  const int b = c >> 3, j = c & 7;
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) q4k_chunk<M>(r.q[i], r.h[i], j, b * QK_K, K, p, acc[i]);
+}
+
+template <int M>
+__device__ __forceinline__ void compute_chunk(const WRegs<DT_Q6K>& r, int c, int K, const XPlanes& p,
+                                              float (&acc)[ROWS][M]) {
+  const int b = c >> 2, hh = (c >> 1) & 1, aa = c & 1;
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) q6k_chunk<M>(r.l0[i], r.l1[i], r.qh[i], r.sc[i], r.d[i], hh, aa, b * QK_K, K, p, acc[i]);
+}
+
+// Sampler bookkeeping of generate() (model.rs:1380-1409) after the LM head:
+// the argmax token is pushed unless it is EOS (never for the first token), the
+// KV position advances, max_tokens / KV capacity end the loop.
+__device__ void finish_sample(const GemvArgs& a) {
+  StepState* st = a.st;
+  const unsigned long long best = atomicExch(&st->best, 0ull);
+  const int nan = atomicExch(&st->nan, 0);
+  st->ticket = 0;
+  if (nan) {  // partial_cmp().unwrap() panics on NaN in the reference
+    st->err = 1;
+    st->done = 1;
+    return;
+  }
+  const uint32_t tok = uint32_t(best & 0xFFFFFFFFull);
+  const bool first = st->gen == 0;
+  st->kv_len += st->n_tokens;
+  st->position = st->kv_len;
+  st->n_tokens = 1;
+  if (!first && st->eos >= 0 && tok == uint32_t(st->eos)) {
+    st->done = 1;
+    return;
+  }
+  a.hist[st->nhist] = tok;
+  st->nhist += 1;
+  a.pen_cnt_w[tok] += 1;
+  st->gen += 1;
+  if (st->gen >= st->max_gen) st->done = 1;
+  else if (st->kv_len + 1 > st->max_seq) {  // the next step's KV append would overflow (kv_cache.rs:48-53)
+    st->err = 2;
+    st->done = 1;
+  }
+}
+
+// One warp set (KS warps) per group of 4 rows; the grid covers all groups.
+// Weights are prefetched into registers before the activations are waited on,
+// and the chunk loop keeps the next chunk's loads in flight while it computes.
+template <int M, int PRO, int EPI, int DT>
+__global__ void __launch_bounds__(GEMV_THREADS, (M == 1 && DT == DT_Q4K) ? 2 : 1) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  if (a.st && a.st->done) return;
   const int K = a.K;
   const XPlanes p = carve(smem, M, K);
-  build_planes<M, PRO>(a, p);
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KS = a.ksplit;
-  const int gpc = GEMV_WARPS / KS;  // row groups per CTA iteration
+  const int gpc = GEMV_WARPS / KS;
   const int NB = K / QK_K;
+  const int g = blockIdx.x * gpc + warp / KS;
+  const int ks = warp % KS;
+  const bool active = g < a.ngroups;
+  constexpr int CPB = DT == DT_Q4K ? 8 : 4;
+  constexpr int BB = DT == DT_Q4K ? Q4K_BYTES : Q6K_DEV_BYTES;
+  const int NC = NB * CPB;
+  const int c0 = ks * NC / KS, c1 = (ks + 1) * NC / KS;
+  const size_t row_bytes = size_t(NB) * BB;
 
-  for (int base = blockIdx.x * gpc; base < a.ngroups; base += gridDim.x * gpc) {
-    const int g = base + warp / KS;
-    const int ks = warp % KS;
-    float acc[ROWS][M];
+  const uint8_t* rw[ROWS];
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) rw[i] = nullptr;
+  if (active) {
+    if (EPI == EPI_SWIGLU) {
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) rw[i] = a.seg[i < 2 ? 0 : 1].w + size_t(2 * g + (i & 1)) * row_bytes;
+    } else {
+      int r = ROWS * g, sg = 0;
+      while (sg < a.nseg - 1 && r >= a.seg[sg].rows) r -= a.seg[sg++].rows;
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) rw[i] = a.seg[sg].w + size_t(r + i) * row_bytes;
+    }
+  }
+  WRegs<DT> cur;
+  int c = c0 + lane;
+  if (active && c < c1) load_chunk(cur, rw, c);
+
+  pdl_trigger();
+  pdl_wait();
+  if (a.st && a.st->done) return;
+  build_planes<M, PRO>(a, p);
+
+  float acc[ROWS][M];
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i)
+#pragma unroll
+    for (int t = 0; t < M; ++t) acc[i][t] = 0.0f;
+  if (active) {
+    for (; c < c1; c += 32) {
+      WRegs<DT> nxt;
+      const bool more = c + 32 < c1;
+      if (more) load_chunk(nxt, rw, c + 32);
+      compute_chunk<M>(cur, c, K, p, acc);
+      if (more) cur = nxt;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i)
+#pragma unroll
+    for (int t = 0; t < M; ++t) acc[i][t] = warp_sum(acc[i][t]);
+
+  // combine the KS warps of a row group, then run the epilogue on final values
+  float* red = p.red;
+  if (lane < ROWS * M) {
+    float v = 0.0f;
 #pragma unroll
     for (int i = 0; i < ROWS; ++i)
 #pragma unroll
-      for (int t = 0; t < M; ++t) acc[i][t] = 0.0f;
-
-    if (g < a.ngroups) {
-      const uint8_t* rw[ROWS];
-      int dtype = DT_Q4K;
-#pragma unroll
-      for (int i = 0; i < ROWS; ++i) {
-        int local, dt;
-        const uint8_t* w;
-        if (EPI == EPI_SWIGLU) {
-          const GemvSeg& sg = a.seg[i < 2 ? 0 : 1];
-          w = sg.w;
-          dt = sg.dtype;
-          local = 2 * g + (i & 1);
-        } else {
-          resolve_row(a, ROWS * g + i, w, dt, local);
-        }
-        dtype = dt;
-        rw[i] = w + size_t(local) * NB * dev_block_bytes(dt);
+      for (int t = 0; t < M; ++t)
+        if (lane == i * M + t) v = acc[i][t];
+    red[warp * 16 + lane] = v;
+  }
+  __syncthreads();
+  const bool lead = ks == 0 && active && lane < ROWS * M;
+  if (lead) {
+    float v = 0.0f;
+    for (int k = 0; k < KS; ++k) v += red[(warp + k) * 16 + lane];
+    red[warp * 16 + lane] = v;
+  }
+  __syncwarp();
+  unsigned long long best = 0ull;
+  int nan = 0;
+  if (lead) {
+    const int i = lane / M, t = lane % M;
+    const float v = red[warp * 16 + lane];
+    const int tok = t;  // column within this launch
+    if (EPI == EPI_STORE) {
+      a.y[size_t(tok) * a.ldy + ROWS * g + i] = v;
+    } else if (EPI == EPI_RESID) {
+      const size_t o = size_t(tok) * a.ldy + ROWS * g + i;
+      a.y[o] = __fadd_rn(a.resid[size_t(tok) * a.ldr + ROWS * g + i], v);
+    } else if (EPI == EPI_SWIGLU) {
+      if (i < 2) {
+        const float gv = v, uv = red[warp * 16 + (i + 2) * M + t];
+        // ffn.rs:90-94: sigmoid = 1/(1+exp(-g)); silu = g*sigmoid; g = silu*u
+        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+        a.y[size_t(tok) * a.ldy + 2 * g + i] = __fmul_rn(__fmul_rn(gv, sig), uv);
       }
-      if (dtype == DT_Q4K) {
-        const int NC = NB * 8;
-        const int c0 = ks * NC / KS, c1 = (ks + 1) * NC / KS;
-        for (int c = c0 + lane; c < c1; c += 32) {
-          const int b = c >> 3, j = c & 7;
-          uint4 qv[ROWS], hv[ROWS];
-#pragma unroll
-          for (int i = 0; i < ROWS; ++i) {
-            const uint8_t* blk = rw[i] + size_t(b) * Q4K_BYTES;
-            hv[i] = __ldg(reinterpret_cast<const uint4*>(blk));
-            qv[i] = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * j));
-          }
-#pragma unroll
-          for (int i = 0; i < ROWS; ++i) q4k_chunk<M>(qv[i], hv[i], j, b * QK_K, K, p, acc[i]);
+    } else if (EPI == EPI_LMHEAD) {
+      const int n = ROWS * g + i;
+      a.y[n] = v;
+      if (a.gen_mode) {
+        float pv = v;
+        if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
+          const uint32_t cnt = a.pen_cnt[n];
+          for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, a.rep) : __fmul_rn(pv, a.rep);
         }
-      } else {
-        const int NC = NB * 4;
-        const int c0 = ks * NC / KS, c1 = (ks + 1) * NC / KS;
-        for (int c = c0 + lane; c < c1; c += 32) {
-          const int b = c >> 2, hh = (c >> 1) & 1, aa = c & 1;
-          uint4 l0v[ROWS], l1v[ROWS], qhv[ROWS], scv[ROWS];
-          uint32_t dv[ROWS];
-#pragma unroll
-          for (int i = 0; i < ROWS; ++i) {
-            const uint8_t* blk = rw[i] + size_t(b) * Q6K_DEV_BYTES;
-            l0v[i] = __ldg(reinterpret_cast<const uint4*>(blk + 64 * hh + 16 * aa));
-            l1v[i] = __ldg(reinterpret_cast<const uint4*>(blk + 64 * hh + 32 + 16 * aa));
-            qhv[i] = __ldg(reinterpret_cast<const uint4*>(blk + 128 + 32 * hh + 16 * aa));
-            scv[i] = __ldg(reinterpret_cast<const uint4*>(blk + 192));
-            dv[i] = __ldg(reinterpret_cast<const unsigned short*>(blk + 208));
-          }
-#pragma unroll
-          for (int i = 0; i < ROWS; ++i)
-            q6k_chunk<M>(l0v[i], l1v[i], qhv[i], scv[i], dv[i], hh, aa, b * QK_K, K, p, acc[i]);
-        }
+        if (pv != pv) nan = 1;
+        else best = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
       }
-    }
-#pragma unroll
-    for (int i = 0; i < ROWS; ++i)
-#pragma unroll
-      for (int t = 0; t < M; ++t) acc[i][t] = warp_sum(acc[i][t]);
-
-    // combine the KS warps of a row group, then run the epilogue on final values
-    float* red = p.red;
-    if (lane < ROWS * M) {
-      float v = 0.0f;
-#pragma unroll
-      for (int i = 0; i < ROWS; ++i)
-#pragma unroll
-        for (int t = 0; t < M; ++t)
-          if (lane == i * M + t) v = acc[i][t];
-      red[warp * 16 + lane] = v;
-    }
-    __syncthreads();
-    if (ks == 0 && g < a.ngroups && lane < ROWS * M) {
-      float v = 0.0f;
-      for (int k = 0; k < KS; ++k) v += red[(warp + k) * 16 + lane];
-      red[warp * 16 + lane] = v;
-    }
-    __syncwarp();
-    if (ks == 0 && g < a.ngroups && lane < ROWS * M) {
-      const int i = lane / M, t = lane % M;
-      const float v = red[warp * 16 + lane];
-      const int tok = t;  // column within this launch
-      if (EPI == EPI_STORE) {
-        a.y[size_t(tok) * a.ldy + ROWS * g + i] = v;
-      } else if (EPI == EPI_RESID) {
-        const size_t o = size_t(tok) * a.ldy + ROWS * g + i;
-        a.y[o] = __fadd_rn(a.resid[size_t(tok) * a.ldr + ROWS * g + i], v);
-      } else if (EPI == EPI_SWIGLU) {
-        if (i < 2) {
-          const float gv = v, uv = red[warp * 16 + (i + 2) * M + t];
-          // ffn.rs:90-94: sigmoid = 1/(1+exp(-g)); silu = g*sigmoid; g = silu*u
-          const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
-          a.y[size_t(tok) * a.ldy + 2 * g + i] = __fmul_rn(__fmul_rn(gv, sig), uv);
-        }
-      } else {  // EPI_QKV
-        const int vr = ROWS * g + i;
-        const int gtok = a.token_offset + tok;
-        const int pos = a.st->position + gtok;
-        const int slot = a.st->kv_len + gtok;
-        const int hd = a.head_dim;
-        if (vr < a.hidden + a.kv_dim) {
-          // RoPE on (2i, 2i+1) pairs (attention.rs:230-262), cos/sin from the table
-          if ((i & 1) == 0) {
-            const float x0 = v, x1 = red[warp * 16 + (i + 1) * M + t];
-            const int col = vr < a.hidden ? vr : vr - a.hidden;
-            const int pi = (col % hd) >> 1;
-            const float c = a.rope_cos[size_t(pos) * (hd / 2) + pi];
-            const float sn = a.rope_sin[size_t(pos) * (hd / 2) + pi];
-            const float n0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-            const float n1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-            if (vr < a.hidden) {
-              a.q[size_t(tok) * a.ldq + vr] = n0;
-              a.q[size_t(tok) * a.ldq + vr + 1] = n1;
+    } else {  // EPI_QKV
+      const int vr = a.row_offset + ROWS * g + i;
+      const int gtok = a.token_offset + tok;
+      const int pos = a.st->position + gtok;
+      const int slot = a.st->kv_len + gtok;
+      const int hd = a.head_dim;
+      if (vr < a.hidden + a.kv_dim) {
+        // RoPE on (2i, 2i+1) pairs (attention.rs:230-262), cos/sin from the table
+        if ((i & 1) == 0) {
+          const float x0 = v, x1 = red[warp * 16 + (i + 1) * M + t];
+          const int col = vr < a.hidden ? vr : vr - a.hidden;
+          const int pi = (col % hd) >> 1;
+          const float cs = a.rope_cos[size_t(pos) * (hd / 2) + pi];
+          const float sn = a.rope_sin[size_t(pos) * (hd / 2) + pi];
+          const float n0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+          const float n1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+          if (vr < a.hidden) {
+            a.q[size_t(tok) * a.ldq + vr] = n0;
+            a.q[size_t(tok) * a.ldq + vr + 1] = n1;
+          } else {
+            const int kh = col / hd, dd = col % hd;
+            const size_t o = (size_t(kh) * a.max_seq + slot) * hd + dd;
+            if (a.kv_half) {
+              reinterpret_cast<__half*>(a.kc)[o] = __float2half_rn(n0);
+              reinterpret_cast<__half*>(a.kc)[o + 1] = __float2half_rn(n1);
             } else {
-              const int kh = col / hd, dd = col % hd;
-              const size_t o = (size_t(kh) * a.max_seq + slot) * hd + dd;
-              if (a.kv_half) {
-                reinterpret_cast<__half*>(a.kc)[o] = __float2half_rn(n0);
-                reinterpret_cast<__half*>(a.kc)[o + 1] = __float2half_rn(n1);
-              } else {
-                reinterpret_cast<float*>(a.kc)[o] = n0;
-                reinterpret_cast<float*>(a.kc)[o + 1] = n1;
-              }
+              reinterpret_cast<float*>(a.kc)[o] = n0;
+              reinterpret_cast<float*>(a.kc)[o + 1] = n1;
             }
           }
-        } else {
-          const int col = vr - a.hidden - a.kv_dim;
-          const int kh = col / hd, dd = col % hd;
-          const size_t o = (size_t(kh) * a.max_seq + slot) * hd + dd;
-          if (a.kv_half) reinterpret_cast<__half*>(a.vc)[o] = __float2half_rn(v);
-          else reinterpret_cast<float*>(a.vc)[o] = v;
         }
+      } else {
+        const int col = vr - a.hidden - a.kv_dim;
+        const int kh = col / hd, dd = col % hd;
+        const size_t o = (size_t(kh) * a.max_seq + slot) * hd + dd;
+        if (a.kv_half) reinterpret_cast<__half*>(a.vc)[o] = __float2half_rn(v);
+        else reinterpret_cast<float*>(a.vc)[o] = v;
       }
     }
+  }
+  if (EPI == EPI_LMHEAD && a.gen_mode) {
+    // CTA-wide max of the keys, one atomic per CTA; the last CTA to finish runs
+    // the sampler bookkeeping (no CTA ever waits for another)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+      best = ob > best ? ob : best;
+      nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+    }
+    __shared__ unsigned long long s_best[GEMV_WARPS];
+    __shared__ int s_nan[GEMV_WARPS];
+    if (lane == 0) {
+      s_best[warp] = best;
+      s_nan[warp] = nan;
+    }
     __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long b = 0ull;
+      int n = 0;
+      for (int w = 0; w < GEMV_WARPS; ++w) {
+        b = s_best[w] > b ? s_best[w] : b;
+        n |= s_nan[w];
+      }
+      if (b) atomicMax(&a.st->best, b);
+      if (n) atomicOr(&a.st->nan, 1);
+      __threadfence();
+      const int prev = atomicAdd(&a.st->ticket, 1);
+      if (prev == int(gridDim.x) - 1) {
+        __threadfence();
+        finish_sample(a);
+      }
+    }
   }
 }
 
 int g_sms = 0;
+bool g_pdl = true;
 
-template <int M, int PRO, int EPI>
-cudaError_t configure_gemv_t() {
-  return cudaFuncSetAttribute(gemv_kernel<M, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+template <typename Kern, typename... Args>
+cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (pdl && g_pdl) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-template <int M, int PRO, int EPI>
+template <int M, int PRO, int EPI, int DT>
+cudaError_t configure_gemv_t() {
+  return cudaFuncSetAttribute(gemv_kernel<M, PRO, EPI, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
+template <int M, int PRO, int EPI, int DT>
 cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t s) {
   const size_t smem = gemv_smem_bytes(M, a.K);
   const int gpc = GEMV_WARPS / a.ksplit;
-  int grid = (a.ngroups + gpc - 1) / gpc;
-  const int per_sm = smem > 100 * 1024 ? 1 : 2;
-  const int sms = g_sms > 0 ? g_sms : 148;
-  grid = grid < sms * per_sm ? grid : sms * per_sm;
-  gemv_kernel<M, PRO, EPI><<<grid, GEMV_THREADS, smem, s>>>(a);
-  return cudaGetLastError();
+  const int grid = (a.ngroups + gpc - 1) / gpc;
+  const cudaError_t e =
+      launch_ex(gemv_kernel<M, PRO, EPI, DT>, dim3(grid), dim3(GEMV_THREADS), smem, s, a.pdl != 0, a);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-#define WCB_GEMV_CASES(F)             \
-  F(PRO_NONE, EPI_STORE)              \
-  F(PRO_NONE, EPI_RESID)              \
-  F(PRO_NONE, EPI_SWIGLU)             \
-  F(PRO_NONE, EPI_QKV)                \
-  F(PRO_RMSNORM, EPI_STORE)           \
-  F(PRO_RMSNORM, EPI_RESID)           \
-  F(PRO_RMSNORM, EPI_SWIGLU)          \
-  F(PRO_RMSNORM, EPI_QKV)
+#define WCB_GEMV_CASES(F)   \
+  F(PRO_NONE, EPI_STORE)    \
+  F(PRO_NONE, EPI_RESID)    \
+  F(PRO_RMSNORM, EPI_QKV)   \
+  F(PRO_RMSNORM, EPI_SWIGLU) \
+  F(PRO_RMSNORM, EPI_STORE) \
+  F(PRO_RMSNORM, EPI_LMHEAD)
 
 template <int M>
 cudaError_t launch_gemv_m(const GemvArgs& a, int pro, int epi, cudaStream_t s) {
-#define WCB_GEMV_CASE(P, E) \
-  if (pro == P && epi == E) return launch_gemv_t<M, P, E>(a, s);
+  const int dt = a.seg[0].dtype;
+#define WCB_GEMV_CASE(P, E)                                                  \
+  if (pro == P && epi == E)                                                  \
+    return dt == DT_Q4K ? launch_gemv_t<M, P, E, DT_Q4K>(a, s) : launch_gemv_t<M, P, E, DT_Q6K>(a, s);
   WCB_GEMV_CASES(WCB_GEMV_CASE)
 #undef WCB_GEMV_CASE
   return cudaErrorInvalidValue;
@@ -450,8 +658,9 @@ cudaError_t launch_gemv_m(const GemvArgs& a, int pro, int epi, cudaStream_t s) {
 template <int M>
 cudaError_t configure_gemv_m() {
   cudaError_t e = cudaSuccess;
-#define WCB_GEMV_CFG(P, E) \
-  if (e == cudaSuccess) e = configure_gemv_t<M, P, E>();
+#define WCB_GEMV_CFG(P, E)                                      \
+  if (e == cudaSuccess) e = configure_gemv_t<M, P, E, DT_Q4K>(); \
+  if (e == cudaSuccess) e = configure_gemv_t<M, P, E, DT_Q6K>();
   WCB_GEMV_CASES(WCB_GEMV_CFG)
 #undef WCB_GEMV_CFG
   return e;
@@ -459,21 +668,31 @@ cudaError_t configure_gemv_m() {
 
 // ------------------------------------------------------------- attention --
 template <typename KT>
-__device__ __forceinline__ float ld_kv(const KT* p);
+__device__ __forceinline__ float4 ld_kv4(const KT* p);
 template <>
-__device__ __forceinline__ float ld_kv<float>(const float* p) { return *p; }
+__device__ __forceinline__ float4 ld_kv4<float>(const float* p) { return *reinterpret_cast<const float4*>(p); }
 template <>
-__device__ __forceinline__ float ld_kv<__half>(const __half* p) { return __half2float(*p); }
+__device__ __forceinline__ float4 ld_kv4<__half>(const __half* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
 
 constexpr int ATT_THREADS = 128;
+constexpr int ATT_WARPS = ATT_THREADS / 32;
 
-// One CTA = (kv head, query token, key split). Scores for the n_rep query heads
-// sharing the kv head (repeat_kv, attention.rs:297-322), masked j > position+t,
-// softmax with max subtraction, P.V (attention.rs:332-435); partial results of
-// the splits are merged by the last CTA of the (token, kv head) pair.
+// One CTA = (kv head, query token, key split). The n_rep query heads sharing
+// the kv head (repeat_kv, attention.rs:297-322) are processed together; keys
+// are staged ATT_TILE at a time in shared memory, scores s = (q.k)*scale with
+// the dot product in key order without contraction, causal limit j <= position+t,
+// softmax with a running max, P.V (attention.rs:332-435). With several splits
+// the last CTA of a (token, kv head) merges the partial results (ticket counter).
 template <int HD, typename KT>
 __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) float asmem[];
+  pdl_trigger();
+  pdl_wait();
   const StepState* st = a.st;
   if (st->done) return;
   const int kh = blockIdx.x, t = blockIdx.y, split = blockIdx.z;
@@ -483,81 +702,130 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
   const int nkeys = min(kv_total, limit + 1);
   const int nsplit = (nkeys + a.chunk - 1) / a.chunk;
   if (split >= nsplit) return;
-  const int j0 = split * a.chunk, j1 = min(j0 + a.chunk, nkeys), nj = j1 - j0;
+  const int j0 = split * a.chunk, j1 = min(j0 + a.chunk, nkeys);
+  constexpr int TS = ATT_TILE, KP = HD + 1;
   float* qs = asmem;               // [n_rep][HD]
-  float* S = qs + n_rep * HD;      // [n_rep][chunk]
-  float* ml = S + n_rep * a.chunk; // [n_rep][2]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* Ks = qs + n_rep * HD;     // [TS][HD+1]
+  float* Vs = Ks + TS * KP;        // [TS][HD]
+  float* S = Vs + TS * HD;         // [n_rep][TS]
+  float* ml = S + n_rep * TS;      // [n_rep][2] running (max, sum)
+  float* corr = ml + 2 * n_rep;    // [n_rep] rescale of the running sums for this tile
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float* qsrc = a.q + (size_t(t) * a.n_heads + size_t(kh) * n_rep) * HD;
-  for (int i = threadIdx.x; i < n_rep * HD; i += ATT_THREADS) qs[i] = qsrc[i];
-  __syncthreads();
+  for (int i = tid; i < n_rep * HD / 4; i += ATT_THREADS)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(qsrc)[i];
+  for (int r = tid; r < n_rep; r += ATT_THREADS) {
+    ml[2 * r] = -INFINITY;
+    ml[2 * r + 1] = 0.0f;
+  }
   const KT* Kp = reinterpret_cast<const KT*>(a.kc) + size_t(kh) * a.max_seq * HD;
   const KT* Vp = reinterpret_cast<const KT*>(a.vc) + size_t(kh) * a.max_seq * HD;
-  constexpr int PER = HD / 32;
-  for (int j = j0 + warp; j < j1; j += ATT_THREADS / 32) {
-    float kv[PER];
+  constexpr int MAXI = 16;  // (n_rep * HD) / ATT_THREADS <= 16
+  const int ni = (n_rep * HD + ATT_THREADS - 1) / ATT_THREADS;
+  float acc[MAXI];
 #pragma unroll
-    for (int e = 0; e < PER; ++e) kv[e] = ld_kv<KT>(Kp + size_t(j) * HD + lane * PER + e);
-    for (int r = 0; r < n_rep; ++r) {
-      float d = 0.0f;
+  for (int k = 0; k < MAXI; ++k) acc[k] = 0.0f;
+
+  for (int tile0 = j0; tile0 < j1; tile0 += TS) {
+    const int nt = min(TS, j1 - tile0);
+    __syncthreads();
+    {  // stage K and V rows [tile0, tile0 + nt): all loads issued before any store
+      constexpr int PER = TS * HD / 4 / ATT_THREADS;  // float4 per thread per matrix
+      float4 kv[PER], vv[PER];
 #pragma unroll
-      for (int e = 0; e < PER; ++e) d += qs[r * HD + lane * PER + e] * kv[e];
-      d = warp_sum(d);
-      if (lane == 0) S[r * a.chunk + (j - j0)] = d * a.scale;
+      for (int e = 0; e < PER; ++e) {
+        const int i = tid + e * ATT_THREADS;
+        const int row = (i * 4) / HD;
+        if (row < nt) {
+          kv[e] = ld_kv4<KT>(Kp + size_t(tile0) * HD + size_t(i) * 4);
+          vv[e] = ld_kv4<KT>(Vp + size_t(tile0) * HD + size_t(i) * 4);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        const int i = tid + e * ATT_THREADS;
+        const int row = (i * 4) / HD, col = (i * 4) % HD;
+        if (row < nt) {
+          float* kr = Ks + row * KP + col;
+          kr[0] = kv[e].x; kr[1] = kv[e].y; kr[2] = kv[e].z; kr[3] = kv[e].w;
+          *reinterpret_cast<float4*>(Vs + row * HD + col) = vv[e];
+        }
+      }
     }
-  }
-  __syncthreads();
-  for (int r = warp; r < n_rep; r += ATT_THREADS / 32) {
-    float mx = -INFINITY;
-    for (int jj = lane; jj < nj; jj += 32) mx = fmaxf(mx, S[r * a.chunk + jj]);
-    mx = warp_max(mx);
-    float l = 0.0f;
-    for (int jj = lane; jj < nj; jj += 32) {
-      const float e = expf(S[r * a.chunk + jj] - mx);
-      S[r * a.chunk + jj] = e;
-      l += e;
+    __syncthreads();
+    for (int r = warp; r < n_rep; r += ATT_WARPS) {
+      float sc = -INFINITY;
+      if (lane < nt) {
+        float d = 0.0f;
+        const float* qr = qs + r * HD;
+        const float* kr = Ks + lane * KP;
+#pragma unroll 16
+        for (int dd = 0; dd < HD; ++dd) d = __fadd_rn(d, __fmul_rn(qr[dd], kr[dd]));
+        sc = __fmul_rn(d, a.scale);
+      }
+      const float m_old = ml[2 * r];
+      const float m_new = fmaxf(m_old, warp_max(sc));
+      const float pr = lane < nt ? expf(sc - m_new) : 0.0f;
+      const float psum = warp_sum(pr);
+      S[r * TS + lane] = pr;
+      if (lane == 0) {
+        const float cf = expf(m_old - m_new);
+        ml[2 * r] = m_new;
+        ml[2 * r + 1] = ml[2 * r + 1] * cf + psum;
+        corr[r] = cf;
+      }
     }
-    l = warp_sum(l);
-    if (lane == 0) {
-      ml[2 * r] = mx;
-      ml[2 * r + 1] = l;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < MAXI; ++k) {
+      const int idx = tid + k * ATT_THREADS;
+      if (k < ni && idx < n_rep * HD) {
+        const int r = idx / HD, d = idx % HD;
+        float s2 = acc[k] * corr[r];
+        for (int jj = 0; jj < nt; ++jj) s2 += S[r * TS + jj] * Vs[jj * HD + d];
+        acc[k] = s2;
+      }
     }
   }
   __syncthreads();
   const size_t pstride = HD + 2;
   if (nsplit == 1) {
-    for (int i = threadIdx.x; i < n_rep * HD; i += ATT_THREADS) {
-      const int r = i / HD, d = i % HD;
-      float acc = 0.0f;
-      for (int jj = 0; jj < nj; ++jj) acc += S[r * a.chunk + jj] * ld_kv<KT>(Vp + size_t(j0 + jj) * HD + d);
-      const float l = ml[2 * r + 1];
-      a.out[(size_t(t) * a.n_heads + kh * n_rep + r) * HD + d] = l > 0.0f ? acc / l : 0.0f;
+#pragma unroll
+    for (int k = 0; k < MAXI; ++k) {
+      const int idx = tid + k * ATT_THREADS;
+      if (k < ni && idx < n_rep * HD) {
+        const int r = idx / HD, d = idx % HD;
+        const float l = ml[2 * r + 1];
+        a.out[(size_t(t) * a.n_heads + kh * n_rep + r) * HD + d] = l > 0.0f ? acc[k] / l : 0.0f;
+      }
     }
     return;
   }
-  for (int i = threadIdx.x; i < n_rep * HD; i += ATT_THREADS) {
-    const int r = i / HD, d = i % HD;
-    float acc = 0.0f;
-    for (int jj = 0; jj < nj; ++jj) acc += S[r * a.chunk + jj] * ld_kv<KT>(Vp + size_t(j0 + jj) * HD + d);
-    float* pp = a.part + ((size_t(t) * a.n_heads + kh * n_rep + r) * a.max_splits + split) * pstride;
-    pp[2 + d] = acc;
-    if (d == 0) {
-      pp[0] = ml[2 * r];
-      pp[1] = ml[2 * r + 1];
+#pragma unroll
+  for (int k = 0; k < MAXI; ++k) {
+    const int idx = tid + k * ATT_THREADS;
+    if (k < ni && idx < n_rep * HD) {
+      const int r = idx / HD, d = idx % HD;
+      float* pp = a.part + ((size_t(t) * a.n_heads + kh * n_rep + r) * a.max_splits + split) * pstride;
+      pp[2 + d] = acc[k];
+      if (d == 0) {
+        pp[0] = ml[2 * r];
+        pp[1] = ml[2 * r + 1];
+      }
     }
   }
   __syncthreads();
   __threadfence();
   __shared__ int s_last;
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     const int prev = atomicAdd(a.ticket + t * a.n_kv + kh, 1);
     s_last = (prev == nsplit - 1);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  if (threadIdx.x == 0) a.ticket[t * a.n_kv + kh] = 0;
-  for (int i = threadIdx.x; i < n_rep * HD; i += ATT_THREADS) {
+  if (tid == 0) a.ticket[t * a.n_kv + kh] = 0;
+  for (int i = tid; i < n_rep * HD; i += ATT_THREADS) {
     const int r = i / HD, d = i % HD;
     const float* pp = a.part + (size_t(t) * a.n_heads + kh * n_rep + r) * a.max_splits * pstride;
     float M = -INFINITY;
@@ -575,113 +843,28 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
 // ------------------------------------------------------------ small ops ---
 __global__ void embed_kernel(const float* emb, int vocab, int hidden, const uint32_t* ids, int T, float* x,
                              const StepState* st) {
+  pdl_trigger();
+  pdl_wait();
   if (st && st->done) return;
   const int t = blockIdx.y;
   const uint32_t id = ids[t];
-  for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < hidden; d += gridDim.x * blockDim.x)
-    x[size_t(t) * hidden + d] = id < uint32_t(vocab) ? emb[size_t(id) * hidden + d] : 0.0f;
+  for (int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4; d < hidden; d += gridDim.x * blockDim.x * 4) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (id < uint32_t(vocab)) v = *reinterpret_cast<const float4*>(emb + size_t(id) * hidden + d);
+    *reinterpret_cast<float4*>(x + size_t(t) * hidden + d) = v;
+  }
 }
 
 __global__ void embed_last_kernel(const float* emb, int vocab, int hidden, const uint32_t* hist, float* x,
                                   const StepState* st) {
+  pdl_trigger();
+  pdl_wait();
   if (st->done) return;
   const uint32_t id = hist[st->nhist - 1];
-  for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < hidden; d += gridDim.x * blockDim.x)
-    x[d] = id < uint32_t(vocab) ? emb[size_t(id) * hidden + d] : 0.0f;
-}
-
-constexpr int SAMPLE_THREADS = 1024;
-
-__global__ void __launch_bounds__(SAMPLE_THREADS)
-    sample_argmax_kernel(const float* logits, int V, float* work, uint32_t* hist, float rep, uint32_t* tok,
-                         StepState* st, int mode, int first) {
-  if (mode == 1 && st->done) return;
-  const int n = st->nhist;
-  for (int i = threadIdx.x; i < V; i += SAMPLE_THREADS) work[i] = logits[i];
-  __syncthreads();
-  if (rep != 1.0f) {
-    // apply_repetition_penalty (sampling.rs:86-103): once per occurrence, in order;
-    // the thread owning a token's first occurrence applies all of its repeats
-    for (int e = threadIdx.x; e < n; e += SAMPLE_THREADS) {
-      const uint32_t tk = hist[e];
-      bool owner = tk < uint32_t(V);
-      for (int f = 0; f < e && owner; ++f) owner = hist[f] != tk;
-      if (!owner) continue;
-      int cnt = 0;
-      for (int f = e; f < n; ++f) cnt += hist[f] == tk;
-      float v = work[tk];
-      for (int c = 0; c < cnt; ++c) v = v > 0.0f ? __fdiv_rn(v, rep) : __fmul_rn(v, rep);
-      work[tk] = v;
-    }
-    __syncthreads();
-  }
-  // sample_argmax (sampling.rs:118-125): Iterator::max_by keeps the last maximum
-  float best = -INFINITY;
-  int bi = -1;
-  int nan = 0;
-  for (int i = threadIdx.x; i < V; i += SAMPLE_THREADS) {
-    const float v = work[i];
-    if (v != v) nan = 1;
-    else if (bi < 0 || !(best > v)) {
-      best = v;
-      bi = i;
-    }
-  }
-  nan = __syncthreads_or(nan);
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) {
-      best = ov;
-      bi = oi;
-    }
-  }
-  __shared__ float s_v[SAMPLE_THREADS / 32];
-  __shared__ int s_i[SAMPLE_THREADS / 32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) {
-    s_v[warp] = best;
-    s_i[warp] = bi;
-  }
-  __syncthreads();
-  if (threadIdx.x != 0) return;
-  for (int w = 1; w < SAMPLE_THREADS / 32; ++w) {
-    const float ov = s_v[w];
-    const int oi = s_i[w];
-    if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) {
-      best = ov;
-      bi = oi;
-    }
-  }
-  if (bi < 0) bi = 0;
-  if (nan) {
-    st->err = 1;
-    if (mode == 1) st->done = 1;
-    *tok = 0;
-    return;
-  }
-  *tok = uint32_t(bi);
-  if (mode == 0) return;
-  // generate() bookkeeping (model.rs:1380-1409)
-  st->kv_len += st->n_tokens;
-  st->position = st->kv_len;
-  st->n_tokens = 1;
-  if (first) {
-    hist[st->nhist] = uint32_t(bi);
-    st->nhist += 1;
-    st->gen = 1;
-  } else if (st->eos >= 0 && uint32_t(bi) == uint32_t(st->eos)) {
-    st->done = 1;
-    return;
-  } else {
-    hist[st->nhist] = uint32_t(bi);
-    st->nhist += 1;
-    st->gen += 1;
-  }
-  if (st->gen >= st->max_gen) st->done = 1;
-  else if (st->kv_len + 1 > st->max_seq) {  // the next step's KV append would overflow (kv_cache.rs:48-53)
-    st->err = 2;
-    st->done = 1;
+  for (int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4; d < hidden; d += gridDim.x * blockDim.x * 4) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (id < uint32_t(vocab)) v = *reinterpret_cast<const float4*>(emb + size_t(id) * hidden + d);
+    *reinterpret_cast<float4*>(x + d) = v;
   }
 }
 
@@ -691,9 +874,15 @@ __global__ void set_state_kernel(StepState* st, int position, int kv_len, int n_
   st->n_tokens = n_tokens;
   st->done = 0;
   st->err = 0;
+  st->best = 0ull;
+  st->ticket = 0;
+  st->nan = 0;
 }
 
 __global__ void init_gen_kernel(StepState* st, int max_gen, int eos, int max_seq) {
+  st->best = 0ull;
+  st->ticket = 0;
+  st->nan = 0;
   st->gen = 0;
   st->nhist = 0;
   st->max_gen = max_gen;
@@ -778,38 +967,39 @@ cudaError_t launch_gemv(const GemvArgs& a, int pro, int epi, cudaStream_t s) {
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
   const int n_rep = a.n_heads / a.n_kv;
-  const size_t smem = sizeof(float) * (size_t(n_rep) * a.head_dim + size_t(n_rep) * a.chunk + 2 * n_rep);
-  dim3 grid(a.n_kv, a.T, a.max_splits);
-  if (a.head_dim == 64) {
-    if (a.kv_half) attn_kernel<64, __half><<<grid, ATT_THREADS, smem, s>>>(a);
-    else attn_kernel<64, float><<<grid, ATT_THREADS, smem, s>>>(a);
-  } else if (a.head_dim == 128) {
-    if (a.kv_half) attn_kernel<128, __half><<<grid, ATT_THREADS, smem, s>>>(a);
-    else attn_kernel<128, float><<<grid, ATT_THREADS, smem, s>>>(a);
+  const int hd = a.head_dim;
+  const size_t smem = sizeof(float) * (size_t(n_rep) * hd + size_t(ATT_TILE) * (hd + 1) + size_t(ATT_TILE) * hd +
+                                       size_t(n_rep) * ATT_TILE + 3 * size_t(n_rep));
+  if (n_rep * hd > ATT_THREADS * 16) return cudaErrorInvalidValue;
+  const dim3 grid(a.n_kv, a.T, a.max_splits);
+  cudaError_t e;
+  if (hd == 64) {
+    e = a.kv_half ? launch_ex(attn_kernel<64, __half>, grid, dim3(ATT_THREADS), smem, s, true, a)
+                  : launch_ex(attn_kernel<64, float>, grid, dim3(ATT_THREADS), smem, s, true, a);
+  } else if (hd == 128) {
+    e = a.kv_half ? launch_ex(attn_kernel<128, __half>, grid, dim3(ATT_THREADS), smem, s, true, a)
+                  : launch_ex(attn_kernel<128, float>, grid, dim3(ATT_THREADS), smem, s, true, a);
   } else {
     return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_embed(const float* emb, int vocab, int hidden, const uint32_t* ids, int T, float* x,
                          const StepState* st, cudaStream_t s) {
-  dim3 grid((hidden + 255) / 256, T);
-  embed_kernel<<<grid, 256, 0, s>>>(emb, vocab, hidden, ids, T, x, st);
-  return cudaGetLastError();
+  const dim3 grid((hidden / 4 + 255) / 256, T);
+  const cudaError_t e = launch_ex(embed_kernel, grid, dim3(256), 0, s, true, emb, vocab, hidden, ids, T, x, st);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_embed_last(const float* emb, int vocab, int hidden, const uint32_t* hist, float* x,
                               const StepState* st, cudaStream_t s) {
-  embed_last_kernel<<<(hidden + 255) / 256, 256, 0, s>>>(emb, vocab, hidden, hist, x, st);
-  return cudaGetLastError();
+  const cudaError_t e =
+      launch_ex(embed_last_kernel, dim3((hidden / 4 + 255) / 256), dim3(256), 0, s, true, emb, vocab, hidden, hist, x, st);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-cudaError_t launch_sample_argmax(const float* logits, int V, float* work, uint32_t* hist, float rep, uint32_t* tok,
-                                 StepState* st, int mode, int first, cudaStream_t s) {
-  sample_argmax_kernel<<<1, SAMPLE_THREADS, 0, s>>>(logits, V, work, hist, rep, tok, st, mode, first);
-  return cudaGetLastError();
-}
+void set_pdl(bool on) { g_pdl = on; }
 
 cudaError_t launch_set_state(StepState* st, int position, int kv_len, int n_tokens, cudaStream_t s) {
   set_state_kernel<<<1, 1, 0, s>>>(st, position, kv_len, n_tokens);

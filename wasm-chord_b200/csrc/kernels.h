@@ -32,6 +32,7 @@ WCB_HD inline size_t dev_block_bytes(int dtype) { return dtype == DT_Q4K ? Q4K_B
 
 // State shared by the kernels of one forward / decode step (device memory).
 struct StepState {
+  unsigned long long best;  // LM-head argmax key: (order-preserving logit bits << 32) | index
   int position;  // RoPE position / causal-mask base of token 0 of this forward
   int kv_len;    // KV length before this forward (slot of token 0)
   int n_tokens;  // tokens in this forward
@@ -42,12 +43,18 @@ struct StepState {
   int err;       // device error word: 1 = NaN logit (sampler), 2 = KV overflow
   int eos;       // EOS id (-1: none)
   int max_seq;   // KV capacity
-  int pad[6];
+  int ticket;    // LM-head CTAs finished (the last one runs the sampler bookkeeping)
+  int nan;       // a penalised logit was NaN
+  int pad[2];
 };
+static_assert(sizeof(StepState) == 64, "StepState layout");
 
 // ---------------------------------------------------------------- GEMV ----
 enum GemvPro { PRO_NONE = 0, PRO_RMSNORM = 1 };
-enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+// EPI_LMHEAD: store the logits and, in generate mode, fuse the repetition
+// penalty, the argmax and generate()'s bookkeeping (sampling.rs:86-125,
+// model.rs:1380-1409) into the LM-head launch.
+enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_LMHEAD = 4 };
 
 struct GemvSeg {
   const uint8_t* w;
@@ -82,8 +89,18 @@ struct GemvArgs {
   int max_seq;
   const float* rope_cos;  // [max_seq][head_dim/2]
   const float* rope_sin;
-  const StepState* st;
+  StepState* st;
   int token_offset;   // first token of this launch within the forward (column groups)
+  int row_offset;     // EPI_QKV: first q/k/v row of this launch
+  // EPI_LMHEAD
+  int gen_mode;            // 1: penalty + argmax + generate bookkeeping
+  const uint32_t* pen_cnt; // occurrences of each token in the sampler history
+  uint32_t* pen_cnt_w;     // same array, incremented when a token is pushed
+  float rep;               // repetition penalty
+  uint32_t* hist;          // sampler history
+  // 1: launch with programmatic dependent launch. Only for static weights: the
+  // kernel reads its weights before waiting on the previous kernel.
+  int pdl;
 };
 
 size_t gemv_smem_bytes(int M, int K);
@@ -106,6 +123,7 @@ struct AttnArgs {
   float scale;        // 1 / sqrt(head_dim)
   const StepState* st;
 };
+constexpr int ATT_TILE = 32;  // keys staged in shared memory per pass
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 
 // ------------------------------------------------------------ elementwise --
@@ -115,16 +133,13 @@ cudaError_t launch_embed(const float* emb, int vocab, int hidden, const uint32_t
 cudaError_t launch_embed_last(const float* emb, int vocab, int hidden, const uint32_t* hist, float* x,
                               const StepState* st, cudaStream_t s);
 
-// Repetition penalty + argmax (sampling.rs:86-125) over logits[V] with the
-// history hist[0..st->nhist). mode 0: write *tok only; mode 1 (generate):
-// also apply generate()'s EOS / push / counters and advance the KV position.
-cudaError_t launch_sample_argmax(const float* logits, int V, float* work, uint32_t* hist, float rep,
-                                 uint32_t* tok, StepState* st, int mode, int first, cudaStream_t s);
-
 // StepState writers (single-thread kernels, so they order with the stream and
 // can sit inside a captured graph)
 cudaError_t launch_set_state(StepState* st, int position, int kv_len, int n_tokens, cudaStream_t s);
 cudaError_t launch_init_gen(StepState* st, int max_gen, int eos, int max_seq, cudaStream_t s);
+// kernels launched with programmatic dependent launch (PDL): a kernel may start
+// while its predecessor drains, prefetching weights before it waits on it
+void set_pdl(bool on);
 // sets the shared-memory limits of every GEMV instantiation (before any capture)
 cudaError_t gemv_configure_all();
 

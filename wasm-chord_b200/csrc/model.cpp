@@ -66,6 +66,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
   check(cudaSetDevice(device_), "cudaSetDevice");
   check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   check(gemv_configure_all(), "configure GEMV kernels");
+  set_pdl(!(opt.flags & 2));
   try {
     // token embeddings (model.rs:432-446): first name that loads
     bool have_emb = false;
@@ -156,20 +157,17 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     ids_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * std::max<size_t>(max_seq_, 1)));
     hist_cap_ = max_seq_ + 2;
     hist_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * hist_cap_));
-    tok_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t)));
     x_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
     h_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
     q_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
     att_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
     act_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.ffn));
     logits_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
-    work_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
-    // attention partials: enough for T_MAX tokens at 256-key splits and for one
-    // token at DECODE_CHUNK-key splits
+    pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab));
+    check(cudaMemset(pen_cnt_, 0, sizeof(uint32_t) * c.vocab), "clear penalty counts");
+    // attention partials of one decode token split into DECODE_CHUNK-key pieces
     max_splits_ = int((max_seq_ + DECODE_CHUNK - 1) / DECODE_CHUNK);
-    const size_t part_prefill = size_t(t_max_) * c.heads * ((max_seq_ + 255) / 256) * (hd + 2);
-    const size_t part_decode = size_t(c.heads) * max_splits_ * (hd + 2);
-    part_ = static_cast<float*>(dalloc(sizeof(float) * std::max(part_prefill, part_decode)));
+    part_ = static_cast<float*>(dalloc(sizeof(float) * size_t(c.heads) * max_splits_ * (hd + 2)));
     ticket_ = static_cast<int*>(dalloc(sizeof(int) * size_t(t_max_) * c.kv_heads));
     check(cudaMemset(ticket_, 0, sizeof(int) * size_t(t_max_) * c.kv_heads), "clear tickets");
     check(cudaMallocHost(&host_ids_, sizeof(uint32_t) * std::max<size_t>(max_seq_, 1)), "cudaMallocHost");
@@ -291,52 +289,71 @@ void Model::set_state(int position, int kv_len, int n_tokens) {
 void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, int ldx, const float* norm_w,
                  float eps, int pro, int epi, float* y, int ldy, const float* resid, int ldr, float* q, int ldq,
                  int layer, int token_offset) {
-  GemvArgs a{};
-  int rows = 0;
-  for (int i = 0; i < nseg; ++i) {
-    a.seg[i].w = segs[i].ptr;
-    a.seg[i].dtype = segs[i].dtype;
-    a.seg[i].rows = int(segs[i].rows);
-    rows += int(segs[i].rows);
-  }
-  a.nseg = nseg;
-  a.K = K;
-  a.ngroups = epi == EPI_SWIGLU ? int(segs[0].rows) / 2 : rows / 4;
-  // split K over warps while the row groups alone leave the GPU under-filled,
-  // keeping at least 16 chunks of work per warp
-  const int chunks = (K / QK_K) * (segs[0].dtype == DT_Q4K ? 8 : 4);
-  int ks = 1;
-  while (ks < 8 && a.ngroups * ks < 148 * 16 && chunks / (ks * 2) >= 16) ks *= 2;
-  a.ksplit = ks;
-  a.norm_w = norm_w;
-  a.eps = eps;
-  a.ldx = ldx;
-  a.ldy = ldy;
-  a.ldr = ldr;
-  a.ldq = ldq;
-  a.hidden = int(cfg_.hidden);
-  a.kv_dim = int(cfg_.kv_heads * cfg_.head_dim());
-  a.head_dim = int(cfg_.head_dim());
-  a.max_seq = int(max_seq_);
-  a.kv_half = int(opt_.kv_half);
-  if (layer >= 0) {
-    const size_t esz = opt_.kv_half ? 2 : 4;
-    a.kc = static_cast<uint8_t*>(kcache_) + size_t(layer) * kv_layer_elems_ * esz;
-    a.vc = static_cast<uint8_t*>(vcache_) + size_t(layer) * kv_layer_elems_ * esz;
-  }
-  a.rope_cos = rope_cos_;
-  a.rope_sin = rope_sin_;
-  a.st = st_;
-  const int mmax = gemv_max_cols(K);
-  for (int c0 = 0; c0 < M; c0 += mmax) {
-    GemvArgs b = a;
-    b.M = std::min(mmax, M - c0);
-    b.x = x + size_t(c0) * ldx;
-    b.y = y ? y + size_t(c0) * ldy : nullptr;
-    b.resid = resid ? resid + size_t(c0) * ldr : nullptr;
-    b.q = q ? q + size_t(c0) * ldq : nullptr;
-    b.token_offset = token_offset + c0;
-    check(launch_gemv(b, pro, epi, stream_), "gemv");
+  // one launch per run of segments sharing a quantisation type (a Q4_K_M layer
+  // can mix Q4_K q/k with a Q6_K v)
+  int row_offset = 0;
+  for (int s0 = 0; s0 < nseg;) {
+    int s1 = s0 + 1;
+    if (epi == EPI_SWIGLU) s1 = nseg;
+    else
+      while (s1 < nseg && segs[s1].dtype == segs[s0].dtype) ++s1;
+    GemvArgs a{};
+    int rows = 0;
+    for (int i = s0; i < s1; ++i) {
+      a.seg[i - s0].w = segs[i].ptr;
+      a.seg[i - s0].dtype = segs[i].dtype;
+      a.seg[i - s0].rows = int(segs[i].rows);
+      rows += int(segs[i].rows);
+    }
+    a.nseg = s1 - s0;
+    a.K = K;
+    a.ngroups = epi == EPI_SWIGLU ? int(segs[0].rows) / 2 : rows / 4;
+    // split K over warps while the row groups alone leave the GPU under-filled,
+    // keeping at least 16 chunks of work per warp
+    const int chunks = (K / QK_K) * (segs[s0].dtype == DT_Q4K ? 8 : 4);
+    int ks = 1;
+    while (ks < 8 && a.ngroups * ks < 148 * 16 && chunks / (ks * 2) >= 16) ks *= 2;
+    a.ksplit = ks;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.ldx = ldx;
+    a.ldy = ldy;
+    a.ldr = ldr;
+    a.ldq = ldq;
+    a.hidden = int(cfg_.hidden);
+    a.kv_dim = int(cfg_.kv_heads * cfg_.head_dim());
+    a.head_dim = int(cfg_.head_dim());
+    a.max_seq = int(max_seq_);
+    a.kv_half = int(opt_.kv_half);
+    a.row_offset = row_offset;
+    if (layer >= 0) {
+      const size_t esz = opt_.kv_half ? 2 : 4;
+      a.kc = static_cast<uint8_t*>(kcache_) + size_t(layer) * kv_layer_elems_ * esz;
+      a.vc = static_cast<uint8_t*>(vcache_) + size_t(layer) * kv_layer_elems_ * esz;
+    }
+    a.rope_cos = rope_cos_;
+    a.rope_sin = rope_sin_;
+    a.st = st_;
+    a.gen_mode = gen_mode_;
+    a.pen_cnt = pen_cnt_;
+    a.pen_cnt_w = pen_cnt_;
+    a.rep = rep_;
+    a.hist = hist_;
+    a.pdl = 1;
+    const int mmax = epi == EPI_LMHEAD ? 1 : gemv_max_cols(K);
+    for (int c0 = 0; c0 < M; c0 += mmax) {
+      GemvArgs b = a;
+      b.M = std::min(mmax, M - c0);
+      b.x = x + size_t(c0) * ldx;
+      b.y = y ? y + size_t(c0) * ldy : nullptr;
+      b.resid = resid ? resid + size_t(c0) * ldr : nullptr;
+      b.q = q ? q + size_t(c0) * ldq : nullptr;
+      b.token_offset = token_offset + c0;
+      check(launch_gemv(b, pro, epi, stream_), "gemv");
+      ++launches_;
+    }
+    row_offset += rows;
+    s0 = s1;
   }
 }
 
@@ -364,16 +381,17 @@ void Model::enqueue_layers(int T) {
     a.head_dim = hd;
     a.max_seq = int(max_seq_);
     a.T = T;
-    if (T == 1) {
+    if (T == 1) {  // decode: split the keys for parallelism, merged by the last CTA
       a.chunk = DECODE_CHUNK;
       a.max_splits = max_splits_;
-    } else {
-      a.chunk = 256;
-      a.max_splits = int((max_seq_ + 255) / 256);
+    } else {  // prefill: the query tokens give the parallelism, one split per token
+      a.chunk = int(max_seq_);
+      a.max_splits = 1;
     }
     a.scale = attn_scale_;
     a.st = st_;
     check(launch_attention(a, stream_), "attention");
+    ++launches_;
     // output projection + residual (attention.rs:182-191, layer.rs:68)
     const DevWeight o[1] = {L.o};
     gemv(o, 1, H, T, att_, H, nullptr, 0.0f, PRO_NONE, EPI_RESID, h_, H, x_, H, nullptr, 0, -1, 0);
@@ -387,17 +405,21 @@ void Model::enqueue_layers(int T) {
 }
 
 // final RMSNorm with the config eps (model.rs:937-943) + LM head on the last
-// token (model.rs:975-1037)
-void Model::enqueue_lm_head(int T) {
+// token (model.rs:975-1037); in generate mode the same launch applies the
+// repetition penalty, takes the argmax and does generate()'s bookkeeping
+void Model::enqueue_lm_head(int T, bool gen) {
   const int H = int(cfg_.hidden);
   const DevWeight head[1] = {lm_head_};
-  gemv(head, 1, H, 1, x_ + size_t(T - 1) * H, H, out_norm_, cfg_.eps, PRO_RMSNORM, EPI_STORE, logits_,
+  gen_mode_ = gen ? 1 : 0;
+  gemv(head, 1, H, 1, x_ + size_t(T - 1) * H, H, out_norm_, cfg_.eps, PRO_RMSNORM, EPI_LMHEAD, logits_,
        int(cfg_.vocab), nullptr, 0, nullptr, 0, -1, 0);
+  gen_mode_ = 0;
 }
 
 void Model::enqueue_forward(const uint32_t* dev_ids, int T, bool from_hist) {
   if (from_hist) check(launch_embed_last(emb_, int(cfg_.vocab), int(cfg_.hidden), hist_, x_, st_, stream_), "embed");
   else check(launch_embed(emb_, int(cfg_.vocab), int(cfg_.hidden), dev_ids, T, x_, st_, stream_), "embed");
+  ++launches_;
   enqueue_layers(T);
 }
 
@@ -416,7 +438,7 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
     enqueue_forward(ids_ + c0, T, false);
   }
   const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
-  enqueue_lm_head(last_T);
+  enqueue_lm_head(last_T, false);
   if (logits_out)
     check(cudaMemcpyAsync(logits_out, logits_, sizeof(float) * cfg_.vocab, cudaMemcpyDeviceToHost, stream_),
           "download logits");
@@ -430,21 +452,18 @@ void Model::decode_steps(int steps) {
       check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
     } else {
       enqueue_forward(nullptr, 1, true);
-      enqueue_lm_head(1);
-      check(launch_sample_argmax(logits_, int(cfg_.vocab), work_, hist_, graph_rep_, tok_, st_, 1, 0, stream_),
-            "sample");
+      enqueue_lm_head(1, true);
     }
   }
 }
 
 void Model::capture_decode_graph() {
   cudaGraph_t g = nullptr;
+  launches_ = 0;
   check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
   try {
     enqueue_forward(nullptr, 1, true);
-    enqueue_lm_head(1);
-    check(launch_sample_argmax(logits_, int(cfg_.vocab), work_, hist_, graph_rep_, tok_, st_, 1, 0, stream_),
-          "sample");
+    enqueue_lm_head(1, true);
   } catch (...) {
     cudaStreamEndCapture(stream_, &g);
     if (g) cudaGraphDestroy(g);
@@ -459,6 +478,7 @@ void Model::capture_decode_graph() {
   }
   decode_graph_ = g;
   decode_exec_ = e;
+  launches_per_step_ = launches_;
 }
 
 void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
@@ -492,6 +512,11 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   if (n > max_seq_)
     throw WcbError(E_PARSE, "Parse error: KV cache overflow: 0 + " + std::to_string(n) + " > " +
                                 std::to_string(max_seq_));
+  const int eos = g.eos == 0xFFFFFFFFu ? -1 : int(g.eos);
+  check(launch_init_gen(st_, int(std::max<uint32_t>(g.max_tokens, 1)), eos, int(max_seq_), stream_), "init");
+  check(cudaMemsetAsync(pen_cnt_, 0, sizeof(uint32_t) * cfg_.vocab, stream_), "clear penalty counts");
+  const float rep = g.repetition_penalty;
+  rep_ = rep;
   std::memcpy(host_ids_, prompt, n * sizeof(uint32_t));
   check(cudaMemcpyAsync(ids_, host_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "upload ids");
   for (size_t c0 = 0; c0 < n; c0 += size_t(t_max_)) {
@@ -500,11 +525,7 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
     enqueue_forward(ids_ + c0, T, false);
   }
   const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
-  enqueue_lm_head(last_T);
-  const int eos = g.eos == 0xFFFFFFFFu ? -1 : int(g.eos);
-  check(launch_init_gen(st_, int(std::max<uint32_t>(g.max_tokens, 1)), eos, int(max_seq_), stream_), "init");
-  const float rep = g.repetition_penalty;
-  check(launch_sample_argmax(logits_, int(cfg_.vocab), work_, hist_, rep, tok_, st_, 1, 1, stream_), "sample");
+  enqueue_lm_head(last_T, true);  // samples the first token (no EOS check)
   if (!(opt_.flags & 1) && (!decode_exec_ || graph_rep_ != rep)) {
     if (decode_exec_) {
       cudaGraphExecDestroy(decode_exec_);

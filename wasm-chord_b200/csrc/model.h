@@ -67,7 +67,7 @@ class Model {
   std::vector<uint32_t> next(size_t max_tokens, bool* finished);
   uint64_t session_id() const { return session_; }
   // kernels launched by one greedy decode step
-  int launches_per_decode_step() const { return 3 + 5 * int(cfg_.layers); }
+  int launches_per_decode_step() const { return launches_per_step_; }
 
  private:
   void upload_weight(const GgufFile& f, const std::string& name, uint32_t rows, uint32_t cols, DevWeight& w,
@@ -78,7 +78,7 @@ class Model {
   void set_state(int position, int kv_len, int n_tokens);
   void enqueue_forward(const uint32_t* dev_ids, int T, bool from_hist);
   void enqueue_layers(int T);
-  void enqueue_lm_head(int T);
+  void enqueue_lm_head(int T, bool gen);
   void gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, int ldx, const float* norm_w, float eps,
             int pro, int epi, float* y, int ldy, const float* resid, int ldr, float* q, int ldq, int layer,
             int token_offset);
@@ -113,14 +113,17 @@ class Model {
   uint32_t* ids_ = nullptr;
   uint32_t* hist_ = nullptr;
   uint32_t hist_cap_ = 0;
-  uint32_t* tok_ = nullptr;
   float* x_ = nullptr;
   float* h_ = nullptr;
   float* q_ = nullptr;
   float* att_ = nullptr;
   float* act_ = nullptr;
   float* logits_ = nullptr;
-  float* work_ = nullptr;
+  uint32_t* pen_cnt_ = nullptr;  // occurrences of each token in the sampler history
+  int gen_mode_ = 0;
+  float rep_ = 1.0f;
+  int launches_ = 0;
+  int launches_per_step_ = 0;
   float* part_ = nullptr;
   int* ticket_ = nullptr;
   int max_splits_ = 0;
