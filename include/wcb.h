@@ -50,7 +50,8 @@ typedef struct wcb_load_opts {
   uint32_t max_seq;   /* KV capacity in tokens; 0 = GGUF context_length (kv_cache.rs:48-53) */
   uint32_t kv_dtype;  /* WCB_KV_F32 (reference numerics) or WCB_KV_F16 */
   uint32_t max_batch; /* sequences per wcb_generate_batch call; 0 = 1 */
-  uint32_t flags;     /* bit 0: do not use CUDA graphs for decode steps */
+  uint32_t flags;     /* bit 0: no CUDA graphs for decode steps; bit 1: no programmatic
+                         dependent launch; bit 2: no tensor-core GEMM for prefill (GEMV only) */
 } wcb_load_opts;
 
 /* TransformerConfig — transformer/config.rs:6-41 (plus head_dim) */
@@ -169,9 +170,23 @@ uint32_t wcb_repack_q6k_dev(const void* packed, size_t nblocks, void* padded, vo
 /* y[m][n] = sum_k x[m][k] * W[n][k] (matmul_transposed, gemm.rs:83-143) with W
  * an [n, k] tensor in device layout: raw Q4_K blocks (dtype WCB_DTYPE_Q4_K) or
  * padded Q6_K blocks (WCB_DTYPE_Q6_K, see wcb_repack_q6k_dev). x is [m][k] and
- * y is [m][n], f32, row-major. k % 256 == 0, n % 4 == 0, 1 <= m <= 4096. */
+ * y is [m][n], f32, row-major. k % 256 == 0, n % 4 == 0, 1 <= m <= 4096.
+ * m >= 16 runs the tcgen05 tensor-core GEMM, smaller m the dp4a GEMV. */
 uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const float* x, size_t m, float* y,
                       void* stream);
+
+/* compute_attention (attention.rs:332-435, with repeat_kv :297-322) for n_tokens
+ * query tokens on device buffers: q [n_tokens][n_heads][head_dim] (after RoPE),
+ * K / V caches [n_kv_heads][max_seq][head_dim] f32 holding kv_len keys, out
+ * [n_tokens][n_heads][head_dim]. Query t attends to keys j < kv_len with
+ * j <= position + t, scores (q.k) / sqrt(head_dim), softmax, weighted sum of V.
+ * head_dim 64 or 128, <= 16 query heads per kv head, n_tokens <= kv_len <= max_seq.
+ * A single-token call splits the keys over up to 64 CTAs whose partial results
+ * are merged in device scratch this library allocates once per device and
+ * reuses; calls that overlap on the GPU race on that scratch. */
+uint32_t wcb_attention_dev(const float* q, const float* k_cache, const float* v_cache, float* out, uint32_t n_tokens,
+                           uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t max_seq,
+                           uint32_t kv_len, uint32_t position, void* stream);
 
 /* Device stream a model handle launches on (a cudaStream_t), for callers that
  * time or order work against it. */

@@ -91,7 +91,7 @@ def test_gemv_q4k_ragged(gpu, n, k, m):
     assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max() * np.sqrt(k / 256)
 
 
-@pytest.mark.parametrize("n,k,m", [(4096, 4096, 1), (4096, 11008, 1), (32000, 4096, 1), (12, 256, 4), (256, 1024, 9)])
+@pytest.mark.parametrize("n,k,m", [(4096, 4096, 1), (4096, 11008, 1), (32000, 4096, 1), (12, 256, 4), (256, 1024, 9), (512, 4096, 40)])
 def test_gemv_q6k(gpu, n, k, m):
     got, ref = _gemv_case(n, k, m, wcb.DTYPE_Q6_K, seed=5)
     assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max() * np.sqrt(k / 256)

@@ -230,3 +230,18 @@ def test_stream_api_stops_at_eos(tiny_pair):
     s = m.infer(prompt, cfg)
     got = s.next_tokens(50)
     assert got == o.generate(prompt, 20, eos_id=base[5]) and s.finished
+
+
+def test_prefill_gemv_and_tensor_core_paths(tiny_gguf, tiny_pair):
+    """Prompts of >= 16 tokens run the tcgen05 GEMM; the GEMV-only model (and the
+    model without programmatic dependent launch) must agree with the oracle too."""
+    _, o = tiny_pair
+    prompt = synth.random_prompt(70, 512, seed=40).tolist()
+    o.clear_kv_cache()
+    ref = o.forward(prompt, 0)
+    for kw in ({}, {"use_tensor_cores": False}, {"use_pdl": False}):
+        m = wcb.Model.load_from_gguf(tiny_gguf, **kw)
+        assert_logits_close(m.forward(prompt, 0), ref)
+        cfg = wcb.GenerationConfig(max_tokens=12, temperature=0.0, repetition_penalty=1.1, eos_id=None)
+        assert m.generate_tokens(prompt, cfg) == o.generate(prompt, 12, repetition_penalty=1.1, eos_id=None)
+        m.close()

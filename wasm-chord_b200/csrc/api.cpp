@@ -4,6 +4,7 @@
 // read by wcb_last_error; no C++ exception crosses the boundary.
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -336,7 +337,8 @@ uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const f
     return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid tensor shape: need k % 256 == 0, n % 4 == 0, 1 <= m <= 4096");
   static bool configured = false;
   if (!configured) {
-    const cudaError_t e = wcb::gemv_configure_all();
+    cudaError_t e = wcb::gemv_configure_all();
+    if (e == cudaSuccess) e = wcb::gemm_tc_configure();
     if (e != cudaSuccess) return cuda_fail(e, "configure");
     configured = true;
   }
@@ -347,12 +349,15 @@ uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const f
   a.nseg = 1;
   a.K = int(k);
   a.ngroups = int(n / 4);
-  const int chunks = int(k / 256) * (dtype == WCB_DTYPE_Q4_K ? 8 : 4);
-  int ks = 1;
-  while (ks < 8 && a.ngroups * ks < 148 * 16 && chunks / (ks * 2) >= 16) ks *= 2;
-  a.ksplit = ks;
   a.ldx = int(k);
   a.ldy = int(n);
+  if (m >= size_t(wcb::TC_MIN_TOKENS)) {  // tensor-core GEMM (tcgen05)
+    a.M = int(m);
+    a.x = x;
+    a.y = y;
+    const cudaError_t e = wcb::launch_gemm_tc(a, wcb::PRO_NONE, wcb::EPI_STORE, nullptr, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WCB_OK : cuda_fail(e, "gemm");
+  }
   const int mmax = wcb::gemv_max_cols(int(k));
   for (size_t c0 = 0; c0 < m; c0 += size_t(mmax)) {
     wcb::GemvArgs b = a;
@@ -363,6 +368,117 @@ uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const f
     if (e != cudaSuccess) return cuda_fail(e, "gemv");
   }
   return WCB_OK;
+}
+
+}  // extern "C"
+
+namespace {
+// Scratch of wcb_attention_dev (StepState, split tickets, split partials),
+// allocated once per device with cudaMalloc and grown on demand.
+std::mutex g_attn_mu;
+std::map<int, std::pair<void*, size_t>> g_attn_scratch;
+
+// Key splits of a single-token call: at most 64 splits of a multiple of 32 keys.
+void attn_split(uint32_t kv_len, int* chunk, int* splits) {
+  int s = int((kv_len + 31) / 32);
+  s = s < 1 ? 1 : (s > 64 ? 64 : s);
+  int c = int((kv_len + uint32_t(s) - 1) / uint32_t(s));
+  c = (c + 31) / 32 * 32;
+  *chunk = c;
+  *splits = int((kv_len + uint32_t(c) - 1) / uint32_t(c));
+}
+
+uint32_t check_attn_args(const float* q, const float* k, const float* v, float* out, uint32_t T, uint32_t nh,
+                         uint32_t nkv, uint32_t hd, uint32_t max_seq, uint32_t kv_len) {
+  if (!q || !k || !v || !out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+  if ((hd != 64 && hd != 128) || nkv == 0 || nh % nkv || nh / nkv > 16 || T == 0 || T > 4096 || kv_len < T ||
+      kv_len > max_seq)
+    return fail(WCB_ERR_INVALID_ARGUMENT,
+                "Invalid tensor shape: need head_dim 64|128, n_heads % n_kv_heads == 0 (<= 16 per kv head), "
+                "1 <= n_tokens <= kv_len <= max_seq");
+  return WCB_OK;
+}
+
+wcb::AttnArgs attn_args(const float* q, const float* k, const float* v, float* out, uint32_t T, uint32_t nh,
+                        uint32_t nkv, uint32_t hd, uint32_t max_seq, uint32_t kv_len) {
+  wcb::AttnArgs a{};
+  a.q = q;
+  a.kc = k;
+  a.vc = v;
+  a.kv_half = 0;
+  a.out = out;
+  a.n_heads = int(nh);
+  a.n_kv = int(nkv);
+  a.head_dim = int(hd);
+  a.max_seq = int(max_seq);
+  a.T = int(T);
+  a.scale = 1.0f / std::sqrt(float(hd));
+  if (T == 1) {
+    attn_split(kv_len, &a.chunk, &a.max_splits);
+  } else {
+    a.chunk = int(max_seq);
+    a.max_splits = 1;
+  }
+  return a;
+}
+
+// StepState | tickets [T][n_kv] | partials [T==1: n_heads][splits][hd+2]
+size_t attn_scratch_bytes(const wcb::AttnArgs& a) {
+  const size_t tickets = (sizeof(int) * size_t(a.T) * a.n_kv + 255) / 256 * 256;
+  const size_t part = a.T == 1 ? sizeof(float) * size_t(a.n_heads) * a.max_splits * (a.head_dim + 2) : 0;
+  return 256 + tickets + part;
+}
+
+cudaError_t attn_run(wcb::AttnArgs a, uint8_t* scratch, uint32_t kv_len, uint32_t position, cudaStream_t s) {
+  wcb::StepState* st = reinterpret_cast<wcb::StepState*>(scratch);
+  a.ticket = reinterpret_cast<int*>(scratch + 256);
+  a.part = reinterpret_cast<float*>(scratch + 256 + (sizeof(int) * size_t(a.T) * a.n_kv + 255) / 256 * 256);
+  a.st = st;
+  cudaError_t e = wcb::launch_set_state(st, int(position), int(kv_len - uint32_t(a.T)), a.T, s);
+  if (e == cudaSuccess) e = wcb::launch_attention(a, s);
+  return e;
+}
+}  // namespace
+
+extern "C" {
+
+uint32_t wcb_attention_dev(const float* q, const float* k_cache, const float* v_cache, float* out, uint32_t n_tokens,
+                           uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t max_seq,
+                           uint32_t kv_len, uint32_t position, void* stream) {
+  const uint32_t rc = check_attn_args(q, k_cache, v_cache, out, n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
+                                      kv_len);
+  if (rc != WCB_OK) return rc;
+  const wcb::AttnArgs a = attn_args(q, k_cache, v_cache, out, n_tokens, n_heads, n_kv_heads, head_dim, max_seq, kv_len);
+  const size_t need = attn_scratch_bytes(a);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  uint8_t* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_attn_mu);
+    auto& slot = g_attn_scratch[dev];
+    if (slot.second < need) {
+      if (slot.first) {
+        cudaDeviceSynchronize();
+        cudaFree(slot.first);
+        slot.first = nullptr;
+        slot.second = 0;
+      }
+      e = cudaMalloc(&slot.first, need);
+      if (e == cudaSuccess) e = cudaMemset(slot.first, 0, need);
+      if (e != cudaSuccess) return cuda_fail(e, "attention scratch");
+      slot.second = need;
+    }
+    scratch = static_cast<uint8_t*>(slot.first);
+  }
+  static bool configured = false;
+  if (!configured) {
+    e = wcb::gemv_configure_all();
+    if (e != cudaSuccess) return cuda_fail(e, "configure");
+    configured = true;
+  }
+  e = attn_run(a, scratch, kv_len, position, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? WCB_OK : cuda_fail(e, "attention");
 }
 
 uint32_t wcb_model_stream(uint32_t h, void** out) {

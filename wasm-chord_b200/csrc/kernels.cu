@@ -12,6 +12,7 @@
 // summation order.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 
@@ -24,7 +25,8 @@ namespace {
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 constexpr int ROWS = 4;  // rows per warp group
-constexpr float XQ_MAX = 8388607.0f;  // 2^23 - 1
+constexpr float XQ_MAX = 4194303.0f;  // 2^22 - 1: a 32-value dot of 4-bit weights stays below 2^31
+constexpr int XQ_IMAX = 4194303;
 
 __device__ __forceinline__ float half_bits(uint32_t b) { return __half2float(__ushort_as_half((unsigned short)b)); }
 
@@ -68,7 +70,7 @@ struct XPlanes {
   uint8_t* l1;
   uint8_t* l2;
   float* scale;  // [M][K/32]
-  float* sum16;  // [M][K/16]  s_g * sum(X) over 16 values
+  float* sum32;  // [M][K/32]  s_g * sum(X) over the group
   float* red;    // [GEMV_WARPS][16]
 };
 
@@ -78,14 +80,14 @@ __device__ __forceinline__ XPlanes carve(uint8_t* smem, int M, int K) {
   p.l1 = smem + size_t(M) * K;
   p.l2 = smem + 2 * size_t(M) * K;
   p.scale = reinterpret_cast<float*>(smem + 3 * size_t(M) * K);
-  p.sum16 = p.scale + size_t(M) * (K / 32);
-  p.red = p.sum16 + size_t(M) * (K / 16);
+  p.sum32 = p.scale + size_t(M) * (K / 32);
+  p.red = p.sum32 + size_t(M) * (K / 32);
   return p;
 }
 
 // Quantises 8 consecutive activations held by one thread into the planes.
-// Four consecutive threads cover one 32-value group (max reduced over them),
-// two cover a 16-value half (sum of X).
+// Four consecutive threads cover one 32-value group (max and sum of X reduced
+// over them).
 __device__ __forceinline__ void quant8(const float (&v)[8], size_t off, int kglob, const XPlanes& p, int K, int t) {
   float amax = 0.0f;
 #pragma unroll
@@ -102,7 +104,7 @@ __device__ __forceinline__ void quant8(const float (&v)[8], size_t off, int kglo
   if (!bad && amax > 0.0f) {
     const float inv = XQ_MAX / amax;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) X[e] = max(-8388607, min(8388607, __float2int_rn(v[e] * inv)));
+    for (int e = 0; e < 8; ++e) X[e] = max(-XQ_IMAX, min(XQ_IMAX, __float2int_rn(v[e] * inv)));
     s = amax / XQ_MAX;
   } else {
 #pragma unroll
@@ -130,9 +132,12 @@ __device__ __forceinline__ void quant8(const float (&v)[8], size_t off, int kglo
   *reinterpret_cast<uint2*>(p.l1 + off) = make_uint2(w1[0], w1[1]);
   *reinterpret_cast<uint2*>(p.l2 + off) = make_uint2(w2[0], w2[1]);
   sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+  sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // |sum X| <= 32 * (2^22 - 1) < 2^31
   const int lane = threadIdx.x & 31;
-  if ((lane & 1) == 0) p.sum16[size_t(t) * (K / 16) + kglob / 16] = s * float(sx);
-  if ((lane & 3) == 0) p.scale[size_t(t) * (K / 32) + kglob / 32] = s;
+  if ((lane & 3) == 0) {
+    p.scale[size_t(t) * (K / 32) + kglob / 32] = s;
+    p.sum32[size_t(t) * (K / 32) + kglob / 32] = s * float(sx);
+  }
 }
 
 // Builds the activation planes. PRO_RMSNORM normalises row h first exactly as
@@ -232,47 +237,51 @@ __device__ __forceinline__ void scale_min(int s, uint32_t w0, uint32_t w1, uint3
   }
 }
 
-// One Q4_K chunk: 16 qs bytes (j-th of 8 in the block) = 16 values of
-// sub-block 2p (low nibbles) and 16 of sub-block 2p+1 (high nibbles).
+// One Q4_K chunk: the 32 qs bytes of sub-block pair pr = 32 values of
+// sub-block 2pr (low nibbles) and 32 of sub-block 2pr+1 (high nibbles).
 template <int M>
-__device__ __forceinline__ void q4k_chunk(const uint4& qs, const uint4& hd, int j, int vbase, int K, const XPlanes& p,
-                                          float (&acc)[M]) {
-  const int pr = j >> 1, hh = j & 1;
+__device__ __forceinline__ void q4k_chunk(const uint4& qa, const uint4& qb, const uint4& hd, int pr, int vbase, int K,
+                                          const XPlanes& p, float (&acc)[M]) {
   const float d = half_bits(hd.x & 0xFFFFu), dmin = half_bits(hd.x >> 16);
   uint32_t sc0, m0, sc1, m1;
   scale_min(2 * pr, hd.y, hd.z, hd.w, sc0, m0);
   scale_min(2 * pr + 1, hd.y, hd.z, hd.w, sc1, m1);
-  const uint32_t w[4] = {qs.x, qs.y, qs.z, qs.w};
-  uint32_t lo[4], hi[4];
+  const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  uint32_t lo[8], hi[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 8; ++i) {
     lo[i] = w[i] & 0x0F0F0F0Fu;
     hi[i] = (w[i] >> 4) & 0x0F0F0F0Fu;
   }
-  const int vlo = vbase + 64 * pr + 16 * hh, vhi = vlo + 32;
+  const int vlo = vbase + 64 * pr, vhi = vlo + 32;
 #pragma unroll
   for (int t = 0; t < M; ++t) {
     const size_t ct = size_t(t) * K;
-    const uint4 a0 = *reinterpret_cast<const uint4*>(p.l0 + ct + vlo);
-    const uint4 a1 = *reinterpret_cast<const uint4*>(p.l1 + ct + vlo);
-    const uint4 a2 = *reinterpret_cast<const uint4*>(p.l2 + ct + vlo);
-    const uint4 b0 = *reinterpret_cast<const uint4*>(p.l0 + ct + vhi);
-    const uint4 b1 = *reinterpret_cast<const uint4*>(p.l1 + ct + vhi);
-    const uint4 b2 = *reinterpret_cast<const uint4*>(p.l2 + ct + vhi);
     int u0 = 0, u1 = 0, u2 = 0, v0 = 0, v1 = 0, v2 = 0;
-    u0 = dp4a_uu(lo[0], a0.x, u0); u0 = dp4a_uu(lo[1], a0.y, u0); u0 = dp4a_uu(lo[2], a0.z, u0); u0 = dp4a_uu(lo[3], a0.w, u0);
-    u1 = dp4a_uu(lo[0], a1.x, u1); u1 = dp4a_uu(lo[1], a1.y, u1); u1 = dp4a_uu(lo[2], a1.z, u1); u1 = dp4a_uu(lo[3], a1.w, u1);
-    u2 = dp4a_us(lo[0], a2.x, u2); u2 = dp4a_us(lo[1], a2.y, u2); u2 = dp4a_us(lo[2], a2.z, u2); u2 = dp4a_us(lo[3], a2.w, u2);
-    v0 = dp4a_uu(hi[0], b0.x, v0); v0 = dp4a_uu(hi[1], b0.y, v0); v0 = dp4a_uu(hi[2], b0.z, v0); v0 = dp4a_uu(hi[3], b0.w, v0);
-    v1 = dp4a_uu(hi[0], b1.x, v1); v1 = dp4a_uu(hi[1], b1.y, v1); v1 = dp4a_uu(hi[2], b1.z, v1); v1 = dp4a_uu(hi[3], b1.w, v1);
-    v2 = dp4a_us(hi[0], b2.x, v2); v2 = dp4a_us(hi[1], b2.y, v2); v2 = dp4a_us(hi[2], b2.z, v2); v2 = dp4a_us(hi[3], b2.w, v2);
-    // |sum q*X| <= 16*15*(2^23-1) < 2^31: exact in int32
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 a0 = *reinterpret_cast<const uint4*>(p.l0 + ct + vlo + 16 * h);
+      const uint4 a1 = *reinterpret_cast<const uint4*>(p.l1 + ct + vlo + 16 * h);
+      const uint4 a2 = *reinterpret_cast<const uint4*>(p.l2 + ct + vlo + 16 * h);
+      const uint4 b0 = *reinterpret_cast<const uint4*>(p.l0 + ct + vhi + 16 * h);
+      const uint4 b1 = *reinterpret_cast<const uint4*>(p.l1 + ct + vhi + 16 * h);
+      const uint4 b2 = *reinterpret_cast<const uint4*>(p.l2 + ct + vhi + 16 * h);
+      const uint32_t* L = lo + 4 * h;
+      const uint32_t* H = hi + 4 * h;
+      u0 = dp4a_uu(L[0], a0.x, u0); u0 = dp4a_uu(L[1], a0.y, u0); u0 = dp4a_uu(L[2], a0.z, u0); u0 = dp4a_uu(L[3], a0.w, u0);
+      u1 = dp4a_uu(L[0], a1.x, u1); u1 = dp4a_uu(L[1], a1.y, u1); u1 = dp4a_uu(L[2], a1.z, u1); u1 = dp4a_uu(L[3], a1.w, u1);
+      u2 = dp4a_us(L[0], a2.x, u2); u2 = dp4a_us(L[1], a2.y, u2); u2 = dp4a_us(L[2], a2.z, u2); u2 = dp4a_us(L[3], a2.w, u2);
+      v0 = dp4a_uu(H[0], b0.x, v0); v0 = dp4a_uu(H[1], b0.y, v0); v0 = dp4a_uu(H[2], b0.z, v0); v0 = dp4a_uu(H[3], b0.w, v0);
+      v1 = dp4a_uu(H[0], b1.x, v1); v1 = dp4a_uu(H[1], b1.y, v1); v1 = dp4a_uu(H[2], b1.z, v1); v1 = dp4a_uu(H[3], b1.w, v1);
+      v2 = dp4a_us(H[0], b2.x, v2); v2 = dp4a_us(H[1], b2.y, v2); v2 = dp4a_us(H[2], b2.z, v2); v2 = dp4a_us(H[3], b2.w, v2);
+    }
+    // |sum q*X| <= 32*15*(2^22-1) < 2^31: exact in int32
     const int dlo = u2 * 65536 + u1 * 256 + u0;
     const int dhi = v2 * 65536 + v1 * 256 + v0;
     const float* sc = p.scale + size_t(t) * (K / 32);
-    const float* sm = p.sum16 + size_t(t) * (K / 16);
+    const float* sm = p.sum32 + size_t(t) * (K / 32);
     const float dot = float(sc0) * sc[vlo >> 5] * float(dlo) + float(sc1) * sc[vhi >> 5] * float(dhi);
-    const float mn = float(m0) * sm[vlo >> 4] + float(m1) * sm[vhi >> 4];
+    const float mn = float(m0) * sm[vlo >> 5] + float(m1) * sm[vhi >> 5];
     acc[t] += d * dot - dmin * mn;
   }
 }
@@ -332,55 +341,60 @@ __device__ __forceinline__ uint32_t order_key(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-template <int DT>
-struct WRegs;
-template <>
-struct WRegs<DT_Q4K> {
-  uint4 q[ROWS], h[ROWS];
-};
-template <>
-struct WRegs<DT_Q6K> {
-  uint4 l0[ROWS], l1[ROWS], qh[ROWS], sc[ROWS];
-  uint32_t d[ROWS];
-};
-
-__device__ __forceinline__ void load_chunk(WRegs<DT_Q4K>& r, const uint8_t* const (&rw)[ROWS], int c) {
-  const int b = c >> 3, j = c & 7;
-#pragma unroll
-  for (int i = 0; i < ROWS; ++i) {
-    const uint8_t* blk = rw[i] + size_t(b) * Q4K_BYTES;
-    r.h[i] = __ldg(reinterpret_cast<const uint4*>(blk));
-    r.q[i] = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * j));
+// ---- TMA bulk copies (cp.async.bulk, no multicast) and mbarriers --------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Bounded wait for one phase of an mbarrier; false after ~2^22 polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t it = 0; it < (1u << 22); ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
   }
+  return false;
 }
 
-__device__ __forceinline__ void load_chunk(WRegs<DT_Q6K>& r, const uint8_t* const (&rw)[ROWS], int c) {
+// Q6_K chunk (64 values) of a row held in shared memory
+template <int M>
+__device__ __forceinline__ void q6k_chunk_smem(const uint8_t* row, int c, int K, const XPlanes& p, float (&acc)[M]) {
   const int b = c >> 2, hh = (c >> 1) & 1, aa = c & 1;
-#pragma unroll
-  for (int i = 0; i < ROWS; ++i) {
-    const uint8_t* blk = rw[i] + size_t(b) * Q6K_DEV_BYTES;
-    r.l0[i] = __ldg(reinterpret_cast<const uint4*>(blk + 64 * hh + 16 * aa));
-    r.l1[i] = __ldg(reinterpret_cast<const uint4*>(blk + 64 * hh + 32 + 16 * aa));
-    r.qh[i] = __ldg(reinterpret_cast<const uint4*>(blk + 128 + 32 * hh + 16 * aa));
-    r.sc[i] = __ldg(reinterpret_cast<const uint4*>(blk + 192));
-    r.d[i] = __ldg(reinterpret_cast<const unsigned short*>(blk + 208));
-  }
+  const uint8_t* blk = row + size_t(b) * Q6K_DEV_BYTES;
+  const uint4 l0 = *reinterpret_cast<const uint4*>(blk + 64 * hh + 16 * aa);
+  const uint4 l1 = *reinterpret_cast<const uint4*>(blk + 64 * hh + 32 + 16 * aa);
+  const uint4 qh = *reinterpret_cast<const uint4*>(blk + 128 + 32 * hh + 16 * aa);
+  const uint4 sc = *reinterpret_cast<const uint4*>(blk + 192);
+  const uint32_t d = *reinterpret_cast<const unsigned short*>(blk + 208);
+  q6k_chunk<M>(l0, l1, qh, sc, d, hh, aa, b * QK_K, K, p, acc);
 }
 
 template <int M>
-__device__ __forceinline__ void compute_chunk(const WRegs<DT_Q4K>& r, int c, int K, const XPlanes& p,
-                                              float (&acc)[ROWS][M]) {
-  const int b = c >> 3, j = c & 7;
-#pragma unroll
-  for (int i = 0; i < ROWS; ++i) q4k_chunk<M>(r.q[i], r.h[i], j, b * QK_K, K, p, acc[i]);
-}
-
-template <int M>
-__device__ __forceinline__ void compute_chunk(const WRegs<DT_Q6K>& r, int c, int K, const XPlanes& p,
-                                              float (&acc)[ROWS][M]) {
-  const int b = c >> 2, hh = (c >> 1) & 1, aa = c & 1;
-#pragma unroll
-  for (int i = 0; i < ROWS; ++i) q6k_chunk<M>(r.l0[i], r.l1[i], r.qh[i], r.sc[i], r.d[i], hh, aa, b * QK_K, K, p, acc[i]);
+__device__ __forceinline__ void q4k_chunk_smem(const uint8_t* row, int c, int K, const XPlanes& p, float (&acc)[M]) {
+  const int b = c >> 2, pr = c & 3;
+  const uint8_t* blk = row + size_t(b) * Q4K_BYTES;
+  const uint4 hd = *reinterpret_cast<const uint4*>(blk);
+  const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * pr);
+  const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * pr);
+  q4k_chunk<M>(qa, qb, hd, pr, b * QK_K, K, p, acc);
 }
 
 // Sampler bookkeeping of generate() (model.rs:1380-1409) after the LM head:
@@ -416,156 +430,331 @@ __device__ void finish_sample(const GemvArgs& a) {
   }
 }
 
-// One warp set (KS warps) per group of 4 rows; the grid covers all groups.
-// Weights are prefetched into registers before the activations are waited on,
-// and the chunk loop keeps the next chunk's loads in flight while it computes.
-template <int M, int PRO, int EPI, int DT>
-__global__ void __launch_bounds__(GEMV_THREADS, (M == 1 && DT == DT_Q4K) ? 2 : 1) gemv_kernel(const GemvArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int K = a.K;
-  const XPlanes p = carve(smem, M, K);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KS = a.ksplit;
-  const int gpc = GEMV_WARPS / KS;
-  const int NB = K / QK_K;
-  const int g = blockIdx.x * gpc + warp / KS;
-  const int ks = warp % KS;
-  const bool active = g < a.ngroups;
-  constexpr int CPB = DT == DT_Q4K ? 8 : 4;
-  constexpr int BB = DT == DT_Q4K ? Q4K_BYTES : Q6K_DEV_BYTES;
-  const int NC = NB * CPB;
-  const int c0 = ks * NC / KS, c1 = (ks + 1) * NC / KS;
-  const size_t row_bytes = size_t(NB) * BB;
+__device__ __forceinline__ uint4 lds4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
 
-  const uint8_t* rw[ROWS];
+// shared-memory addresses of the activation planes
+struct XAddr {
+  uint32_t l[3], scale, sum32;
+};
+
+// One 64-value Q4_K chunk (sub-block pair pr of block b) of four rows held in
+// shared memory at row addresses ra[]: the activation limbs of the chunk are
+// loaded once and shared by the four rows.
+template <int M>
+__device__ __forceinline__ void q4k_chunk_rows(const uint32_t (&ra)[ROWS], int c, int K, const XAddr& xa,
+                                               float (&acc)[ROWS][M]) {
+  const int b = c >> 2, pr = c & 3;
+  const int vlo = b * QK_K + 64 * pr, vhi = vlo + 32;
+  const bool upper = pr >= 2;
+  const int sh = 16 * (pr & 1);
 #pragma unroll
-  for (int i = 0; i < ROWS; ++i) rw[i] = nullptr;
-  if (active) {
-    if (EPI == EPI_SWIGLU) {
+  for (int t = 0; t < M; ++t) {
+    const uint32_t xo = uint32_t(t * K);
+    uint4 xl[3][2], xh[3][2];
 #pragma unroll
-      for (int i = 0; i < ROWS; ++i) rw[i] = a.seg[i < 2 ? 0 : 1].w + size_t(2 * g + (i & 1)) * row_bytes;
-    } else {
-      int r = ROWS * g, sg = 0;
-      while (sg < a.nseg - 1 && r >= a.seg[sg].rows) r -= a.seg[sg++].rows;
+    for (int l = 0; l < 3; ++l) {
+      xl[l][0] = lds4(xa.l[l] + xo + vlo);
+      xl[l][1] = lds4(xa.l[l] + xo + vlo + 16);
+      xh[l][0] = lds4(xa.l[l] + xo + vhi);
+      xh[l][1] = lds4(xa.l[l] + xo + vhi + 16);
+    }
+    const uint32_t so = 4u * uint32_t(t * (K / 32));
+    const float s_lo = ldsf(xa.scale + so + 4 * (vlo >> 5)), s_hi = ldsf(xa.scale + so + 4 * (vhi >> 5));
+    const float m_lo = ldsf(xa.sum32 + so + 4 * (vlo >> 5)), m_hi = ldsf(xa.sum32 + so + 4 * (vhi >> 5));
 #pragma unroll
-      for (int i = 0; i < ROWS; ++i) rw[i] = a.seg[sg].w + size_t(r + i) * row_bytes;
+    for (int i = 0; i < ROWS; ++i) {
+      const uint32_t blk = ra[i] + uint32_t(b * Q4K_BYTES);
+      const uint4 hd = lds4(blk);
+      const uint4 qa = lds4(blk + 16 + 32 * pr);
+      const uint4 qb = lds4(blk + 32 + 32 * pr);
+      // get_scale_min_k4 (quant.rs:43-53) for sub-blocks 2pr and 2pr+1, branch-free
+      const uint32_t y = hd.y >> sh, z = hd.z >> sh, w = hd.w >> sh;
+      const uint32_t y0 = y & 0xFF, y1 = (y >> 8) & 0xFF, z0 = z & 0xFF, z1 = (z >> 8) & 0xFF;
+      const uint32_t w0 = w & 0xFF, w1 = (w >> 8) & 0xFF;
+      const uint32_t sc0 = upper ? ((w0 & 0xF) | ((y0 >> 6) << 4)) : (y0 & 63);
+      const uint32_t sc1 = upper ? ((w1 & 0xF) | ((y1 >> 6) << 4)) : (y1 & 63);
+      const uint32_t mn0 = upper ? ((w0 >> 4) | ((z0 >> 6) << 4)) : (z0 & 63);
+      const uint32_t mn1 = upper ? ((w1 >> 4) | ((z1 >> 6) << 4)) : (z1 & 63);
+      const float d = half_bits(hd.x & 0xFFFFu), dmin = half_bits(hd.x >> 16);
+      const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      int u0 = 0, u1 = 0, u2 = 0, v0 = 0, v1 = 0, v2 = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t* qq = q + 4 * h;
+        const uint32_t L0 = qq[0] & 0x0F0F0F0Fu, L1 = qq[1] & 0x0F0F0F0Fu, L2 = qq[2] & 0x0F0F0F0Fu,
+                       L3 = qq[3] & 0x0F0F0F0Fu;
+        const uint32_t H0 = (qq[0] >> 4) & 0x0F0F0F0Fu, H1 = (qq[1] >> 4) & 0x0F0F0F0Fu,
+                       H2 = (qq[2] >> 4) & 0x0F0F0F0Fu, H3 = (qq[3] >> 4) & 0x0F0F0F0Fu;
+        u0 = dp4a_uu(L0, xl[0][h].x, u0); u0 = dp4a_uu(L1, xl[0][h].y, u0); u0 = dp4a_uu(L2, xl[0][h].z, u0); u0 = dp4a_uu(L3, xl[0][h].w, u0);
+        u1 = dp4a_uu(L0, xl[1][h].x, u1); u1 = dp4a_uu(L1, xl[1][h].y, u1); u1 = dp4a_uu(L2, xl[1][h].z, u1); u1 = dp4a_uu(L3, xl[1][h].w, u1);
+        u2 = dp4a_us(L0, xl[2][h].x, u2); u2 = dp4a_us(L1, xl[2][h].y, u2); u2 = dp4a_us(L2, xl[2][h].z, u2); u2 = dp4a_us(L3, xl[2][h].w, u2);
+        v0 = dp4a_uu(H0, xh[0][h].x, v0); v0 = dp4a_uu(H1, xh[0][h].y, v0); v0 = dp4a_uu(H2, xh[0][h].z, v0); v0 = dp4a_uu(H3, xh[0][h].w, v0);
+        v1 = dp4a_uu(H0, xh[1][h].x, v1); v1 = dp4a_uu(H1, xh[1][h].y, v1); v1 = dp4a_uu(H2, xh[1][h].z, v1); v1 = dp4a_uu(H3, xh[1][h].w, v1);
+        v2 = dp4a_us(H0, xh[2][h].x, v2); v2 = dp4a_us(H1, xh[2][h].y, v2); v2 = dp4a_us(H2, xh[2][h].z, v2); v2 = dp4a_us(H3, xh[2][h].w, v2);
+      }
+      // |sum q*X| <= 32*15*(2^22-1) < 2^31: exact in int32
+      const int dlo = u2 * 65536 + u1 * 256 + u0;
+      const int dhi = v2 * 65536 + v1 * 256 + v0;
+      const float dot = float(sc0) * s_lo * float(dlo) + float(sc1) * s_hi * float(dhi);
+      const float mn = float(mn0) * m_lo + float(mn1) * m_hi;
+      acc[i][t] += d * dot - dmin * mn;
     }
   }
-  WRegs<DT> cur;
-  int c = c0 + lane;
-  if (active && c < c1) load_chunk(cur, rw, c);
+}
 
+// Shared-memory layout of one GEMV CTA (sizes from the host, GemvArgs):
+//   [slot 0][slot 1]   weight stages: stage_groups groups of 4 rows, raw blocks
+//   [planes]           activation limbs (XPlanes)
+//   [part]             per-unit partial sums  (stage_groups * ksplit * 16 floats)
+//   [fin]              per-group final sums   (stage_groups * 16 floats)
+//   [bar]              two mbarriers
+struct GemvSmem {
+  uint8_t* slot[2];
+  XPlanes p;
+  float* part;
+  float* fin;
+  uint64_t* bar;
+};
+
+__device__ __forceinline__ GemvSmem gemv_carve(uint8_t* smem, const GemvArgs& a, int M) {
+  GemvSmem g;
+  g.slot[0] = smem;
+  g.slot[1] = smem + a.slot_bytes;
+  uint8_t* q = smem + 2 * size_t(a.slot_bytes);
+  g.p = carve(q, M, a.K);
+  q += gemv_planes_bytes(M, a.K);
+  g.part = reinterpret_cast<float*>(q);
+  q += sizeof(float) * size_t(a.stage_groups) * a.ksplit * 16;
+  g.fin = reinterpret_cast<float*>(q);
+  q += sizeof(float) * size_t(a.stage_groups) * 16;
+  g.bar = reinterpret_cast<uint64_t*>(q);
+  return g;
+}
+
+// Issues the bulk copies of stage `stage` (groups [gs, ge) of this CTA) into
+// slot `slot`: one copy per contiguous row range (per segment, or the gate and
+// the up rows of SwiGLU pairs).
+template <int EPI>
+__device__ void issue_stage(const GemvArgs& a, const GemvSmem& sm, int slot, int gs, int ge, size_t row_bytes) {
+  uint64_t* bar = sm.bar + slot;
+  const int ng = ge - gs;
+  uint8_t* dst = sm.slot[slot];
+  if (EPI == EPI_SWIGLU) {
+    const uint32_t bytes = uint32_t(2 * ng * row_bytes);
+    mbar_expect_tx(bar, 2 * bytes);
+    bulk_g2s(dst, a.seg[0].w + size_t(2 * gs) * row_bytes, bytes, bar);
+    bulk_g2s(dst + bytes, a.seg[1].w + size_t(2 * gs) * row_bytes, bytes, bar);
+    return;
+  }
+  mbar_expect_tx(bar, uint32_t(4 * ng * row_bytes));
+  int r0 = ROWS * gs;
+  const int r1 = ROWS * ge;
+  int base = 0;
+  for (int sg = 0; sg < a.nseg && r0 < r1; ++sg) {
+    const int s0 = base, s1 = base + a.seg[sg].rows;
+    base = s1;
+    if (r0 >= s1) continue;
+    const int e = min(r1, s1);
+    const uint32_t bytes = uint32_t(size_t(e - r0) * row_bytes);
+    bulk_g2s(dst, a.seg[sg].w + size_t(r0 - s0) * row_bytes, bytes, bar);
+    dst += bytes;
+    r0 = e;
+  }
+}
+
+// Fused dequant-GEMV. The grid is at most one wave; CTA c owns row groups
+// [c*G/grid, (c+1)*G/grid). Its weights stream through two shared-memory
+// stages with TMA bulk copies; the first two stages are issued before the
+// kernel waits on its predecessor (programmatic dependent launch), so weight
+// traffic overlaps the previous kernel. Warps take (row group, K slice) units.
+template <int M, int PRO, int EPI, int DT>
+__global__ void __launch_bounds__(GEMV_THREADS, M == 1 ? 2 : 1) gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int K = a.K;
+  const GemvSmem sm = gemv_carve(smem, a, M);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KS = a.ksplit;
+  const int NB = K / QK_K;
+  constexpr int BB = DT == DT_Q4K ? Q4K_BYTES : Q6K_DEV_BYTES;
+  const size_t row_bytes = size_t(NB) * BB;
+  const int NC = NB * 4;  // 64-value chunks per row
+  const int g_begin = int((long long)blockIdx.x * a.ngroups / gridDim.x);
+  const int g_end = int((long long)(blockIdx.x + 1) * a.ngroups / gridDim.x);
+  const int SG = a.stage_groups;
+  const int nstages = (g_end - g_begin + SG - 1) / SG;
+
+  if (tid == 0) {
+    mbar_init(sm.bar + 0, 1);
+    mbar_init(sm.bar + 1, 1);
+    mbar_fence_init();
+    for (int st = 0; st < 2 && st < nstages; ++st)
+      issue_stage<EPI>(a, sm, st, g_begin + st * SG, min(g_end, g_begin + (st + 1) * SG), row_bytes);
+  }
   pdl_trigger();
   pdl_wait();
-  if (a.st && a.st->done) return;
-  build_planes<M, PRO>(a, p);
+  if (a.st && a.st->done) {
+    // wait (bounded) for the copies issued above before the CTA retires
+    if (tid == 0)
+      for (int st = 0; st < 2 && st < nstages; ++st) mbar_wait(sm.bar + st, 0);
+    return;
+  }
+  build_planes<M, PRO>(a, sm.p);  // ends with __syncthreads (the barrier init is visible too)
 
-  float acc[ROWS][M];
-#pragma unroll
-  for (int i = 0; i < ROWS; ++i)
-#pragma unroll
-    for (int t = 0; t < M; ++t) acc[i][t] = 0.0f;
-  if (active) {
-    for (; c < c1; c += 32) {
-      WRegs<DT> nxt;
-      const bool more = c + 32 < c1;
-      if (more) load_chunk(nxt, rw, c + 32);
-      compute_chunk<M>(cur, c, K, p, acc);
-      if (more) cur = nxt;
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < ROWS; ++i)
-#pragma unroll
-    for (int t = 0; t < M; ++t) acc[i][t] = warp_sum(acc[i][t]);
-
-  // combine the KS warps of a row group, then run the epilogue on final values
-  float* red = p.red;
-  if (lane < ROWS * M) {
-    float v = 0.0f;
-#pragma unroll
-    for (int i = 0; i < ROWS; ++i)
-#pragma unroll
-      for (int t = 0; t < M; ++t)
-        if (lane == i * M + t) v = acc[i][t];
-    red[warp * 16 + lane] = v;
-  }
-  __syncthreads();
-  const bool lead = ks == 0 && active && lane < ROWS * M;
-  if (lead) {
-    float v = 0.0f;
-    for (int k = 0; k < KS; ++k) v += red[(warp + k) * 16 + lane];
-    red[warp * 16 + lane] = v;
-  }
-  __syncwarp();
   unsigned long long best = 0ull;
   int nan = 0;
-  if (lead) {
-    const int i = lane / M, t = lane % M;
-    const float v = red[warp * 16 + lane];
-    const int tok = t;  // column within this launch
-    if (EPI == EPI_STORE) {
-      a.y[size_t(tok) * a.ldy + ROWS * g + i] = v;
-    } else if (EPI == EPI_RESID) {
-      const size_t o = size_t(tok) * a.ldy + ROWS * g + i;
-      a.y[o] = __fadd_rn(a.resid[size_t(tok) * a.ldr + ROWS * g + i], v);
-    } else if (EPI == EPI_SWIGLU) {
-      if (i < 2) {
-        const float gv = v, uv = red[warp * 16 + (i + 2) * M + t];
-        // ffn.rs:90-94: sigmoid = 1/(1+exp(-g)); silu = g*sigmoid; g = silu*u
-        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
-        a.y[size_t(tok) * a.ldy + 2 * g + i] = __fmul_rn(__fmul_rn(gv, sig), uv);
+  for (int st = 0; st < nstages; ++st) {
+    const int slot = st & 1;
+    const int gs = g_begin + st * SG, ge = min(g_end, gs + SG), ng = ge - gs;
+    const bool ok = mbar_wait(sm.bar + slot, uint32_t((st >> 1) & 1));
+    if (__syncthreads_or(!ok)) {  // a copy never landed: report, give the other slot a bounded wait, stop
+      if (tid == 0) {
+        if (a.st) atomicOr(&a.st->err, 4);
+        mbar_wait(sm.bar + (slot ^ 1), uint32_t((st >> 1) & 1));
       }
-    } else if (EPI == EPI_LMHEAD) {
-      const int n = ROWS * g + i;
-      a.y[n] = v;
-      if (a.gen_mode) {
-        float pv = v;
-        if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
-          const uint32_t cnt = a.pen_cnt[n];
-          for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, a.rep) : __fmul_rn(pv, a.rep);
+      return;
+    }
+    const uint8_t* sbase = sm.slot[slot];
+    const uint32_t sbase_a = smem_u32(sbase);
+    XAddr xad;
+    xad.l[0] = smem_u32(sm.p.l0);
+    xad.l[1] = smem_u32(sm.p.l1);
+    xad.l[2] = smem_u32(sm.p.l2);
+    xad.scale = smem_u32(sm.p.scale);
+    xad.sum32 = smem_u32(sm.p.sum32);
+    const int units = ng * KS;
+    for (int u = warp; u < units; u += GEMV_WARPS) {
+      const int gl = u / KS, ks = u % KS;
+      const uint8_t* rw[ROWS];
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) {
+        if (EPI == EPI_SWIGLU)
+          rw[i] = sbase + size_t((i < 2 ? 0 : 2 * ng) + 2 * gl + (i & 1)) * row_bytes;
+        else
+          rw[i] = sbase + size_t(ROWS * gl + i) * row_bytes;
+      }
+      float acc[ROWS][M];
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i)
+#pragma unroll
+        for (int t = 0; t < M; ++t) acc[i][t] = 0.0f;
+      const int c1 = (ks + 1) * NC / KS;
+      if (DT == DT_Q4K) {
+        uint32_t ra[ROWS];
+#pragma unroll
+        for (int i = 0; i < ROWS; ++i) ra[i] = sbase_a + uint32_t(rw[i] - sbase);
+        for (int c = ks * NC / KS + lane; c < c1; c += 32) q4k_chunk_rows<M>(ra, c, K, xad, acc);
+      } else {
+        for (int c = ks * NC / KS + lane; c < c1; c += 32) {
+#pragma unroll
+          for (int i = 0; i < ROWS; ++i) q6k_chunk_smem<M>(rw[i], c, K, sm.p, acc[i]);
         }
-        if (pv != pv) nan = 1;
-        else best = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
       }
-    } else {  // EPI_QKV
-      const int vr = a.row_offset + ROWS * g + i;
-      const int gtok = a.token_offset + tok;
-      const int pos = a.st->position + gtok;
-      const int slot = a.st->kv_len + gtok;
-      const int hd = a.head_dim;
-      if (vr < a.hidden + a.kv_dim) {
-        // RoPE on (2i, 2i+1) pairs (attention.rs:230-262), cos/sin from the table
-        if ((i & 1) == 0) {
-          const float x0 = v, x1 = red[warp * 16 + (i + 1) * M + t];
-          const int col = vr < a.hidden ? vr : vr - a.hidden;
-          const int pi = (col % hd) >> 1;
-          const float cs = a.rope_cos[size_t(pos) * (hd / 2) + pi];
-          const float sn = a.rope_sin[size_t(pos) * (hd / 2) + pi];
-          const float n0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-          const float n1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-          if (vr < a.hidden) {
-            a.q[size_t(tok) * a.ldq + vr] = n0;
-            a.q[size_t(tok) * a.ldq + vr + 1] = n1;
-          } else {
-            const int kh = col / hd, dd = col % hd;
-            const size_t o = (size_t(kh) * a.max_seq + slot) * hd + dd;
-            if (a.kv_half) {
-              reinterpret_cast<__half*>(a.kc)[o] = __float2half_rn(n0);
-              reinterpret_cast<__half*>(a.kc)[o + 1] = __float2half_rn(n1);
-            } else {
-              reinterpret_cast<float*>(a.kc)[o] = n0;
-              reinterpret_cast<float*>(a.kc)[o + 1] = n1;
-            }
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i)
+#pragma unroll
+        for (int t = 0; t < M; ++t) {
+          const float v = warp_sum(acc[i][t]);
+          if (lane == i * M + t) sm.part[u * 16 + lane] = v;
+        }
+    }
+    __syncthreads();
+    // fixed-order sum of the K slices of every (group, output)
+    for (int o = tid; o < ng * 16; o += GEMV_THREADS) {
+      const int gl = o >> 4, j = o & 15;
+      float v = 0.0f;
+      if (j < ROWS * M)
+        for (int k = 0; k < KS; ++k) v += sm.part[(gl * KS + k) * 16 + j];
+      sm.fin[o] = v;
+    }
+    __syncthreads();
+    for (int o = tid; o < ng * 16; o += GEMV_THREADS) {
+      const int gl = o >> 4, j = o & 15;
+      if (j >= ROWS * M) continue;
+      const int g = gs + gl;
+      const int i = j / M, t = j % M;
+      const float v = sm.fin[o];
+      const float* fin = sm.fin + gl * 16;
+      const int tok = t;  // column within this launch
+      if (EPI == EPI_STORE) {
+        a.y[size_t(tok) * a.ldy + ROWS * g + i] = v;
+      } else if (EPI == EPI_RESID) {
+        const size_t off = size_t(tok) * a.ldy + ROWS * g + i;
+        a.y[off] = __fadd_rn(a.resid[size_t(tok) * a.ldr + ROWS * g + i], v);
+      } else if (EPI == EPI_SWIGLU) {
+        if (i < 2) {
+          const float gv = v, uv = fin[(i + 2) * M + t];
+          // ffn.rs:90-94: sigmoid = 1/(1+exp(-g)); silu = g*sigmoid; g = silu*u
+          const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+          a.y[size_t(tok) * a.ldy + 2 * g + i] = __fmul_rn(__fmul_rn(gv, sig), uv);
+        }
+      } else if (EPI == EPI_LMHEAD) {
+        const int n = ROWS * g + i;
+        a.y[n] = v;
+        if (a.gen_mode) {
+          float pv = v;
+          if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
+            const uint32_t cnt = a.pen_cnt[n];
+            for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, a.rep) : __fmul_rn(pv, a.rep);
+          }
+          if (pv != pv) nan = 1;
+          else {
+            const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
+            best = key > best ? key : best;
           }
         }
-      } else {
-        const int col = vr - a.hidden - a.kv_dim;
-        const int kh = col / hd, dd = col % hd;
-        const size_t o = (size_t(kh) * a.max_seq + slot) * hd + dd;
-        if (a.kv_half) reinterpret_cast<__half*>(a.vc)[o] = __float2half_rn(v);
-        else reinterpret_cast<float*>(a.vc)[o] = v;
+      } else {  // EPI_QKV
+        const int vr = a.row_offset + ROWS * g + i;
+        const int gtok = a.token_offset + tok;
+        const int pos = a.st->position + gtok;
+        const int slot_kv = a.st->kv_len + gtok;
+        const int hd = a.head_dim;
+        if (vr < a.hidden + a.kv_dim) {
+          // RoPE on (2i, 2i+1) pairs (attention.rs:230-262), cos/sin from the table
+          if ((i & 1) == 0) {
+            const float x0 = v, x1 = fin[(i + 1) * M + t];
+            const int col = vr < a.hidden ? vr : vr - a.hidden;
+            const int pi = (col % hd) >> 1;
+            const float cs = a.rope_cos[size_t(pos) * (hd / 2) + pi];
+            const float sn = a.rope_sin[size_t(pos) * (hd / 2) + pi];
+            const float n0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+            const float n1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+            if (vr < a.hidden) {
+              a.q[size_t(tok) * a.ldq + vr] = n0;
+              a.q[size_t(tok) * a.ldq + vr + 1] = n1;
+            } else {
+              const int kh = col / hd, dd = col % hd;
+              const size_t off = (size_t(kh) * a.max_seq + slot_kv) * hd + dd;
+              if (a.kv_half) {
+                reinterpret_cast<__half*>(a.kc)[off] = __float2half_rn(n0);
+                reinterpret_cast<__half*>(a.kc)[off + 1] = __float2half_rn(n1);
+              } else {
+                reinterpret_cast<float*>(a.kc)[off] = n0;
+                reinterpret_cast<float*>(a.kc)[off + 1] = n1;
+              }
+            }
+          }
+        } else {
+          const int col = vr - a.hidden - a.kv_dim;
+          const int kh = col / hd, dd = col % hd;
+          const size_t off = (size_t(kh) * a.max_seq + slot_kv) * hd + dd;
+          if (a.kv_half) reinterpret_cast<__half*>(a.vc)[off] = __float2half_rn(v);
+          else reinterpret_cast<float*>(a.vc)[off] = v;
+        }
       }
+    }
+    __syncthreads();  // the slot, part and fin are free again
+    if (tid == 0 && st + 2 < nstages) {
+      fence_proxy_async();
+      issue_stage<EPI>(a, sm, slot, g_begin + (st + 2) * SG, min(g_end, g_begin + (st + 3) * SG), row_bytes);
     }
   }
   if (EPI == EPI_LMHEAD && a.gen_mode) {
@@ -584,7 +773,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, (M == 1 && DT == DT_Q4K) ? 2 : 1
       s_nan[warp] = nan;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       unsigned long long b = 0ull;
       int n = 0;
       for (int w = 0; w < GEMV_WARPS; ++w) {
@@ -621,16 +810,51 @@ cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// dynamic shared memory a GEMV CTA may use: the device's per-block opt-in
+// limit less 2 KB for the kernel's static shared memory
+size_t g_smem_max = 200 * 1024;
+
 template <int M, int PRO, int EPI, int DT>
 cudaError_t configure_gemv_t() {
-  return cudaFuncSetAttribute(gemv_kernel<M, PRO, EPI, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  return cudaFuncSetAttribute(gemv_kernel<M, PRO, EPI, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(g_smem_max));
+}
+
+// Grid, stage size and K split of one launch: a single wave of CTAs (two per
+// SM when two double-buffered stages fit in half of the shared memory).
+template <int DT>
+size_t plan_gemv(GemvArgs& a, int M, int* grid) {
+  const int NB = a.K / QK_K;
+  const size_t row_bytes = size_t(NB) * (DT == DT_Q4K ? Q4K_BYTES : Q6K_DEV_BYTES);
+  const size_t group_bytes = ROWS * row_bytes;
+  const size_t planes = gemv_planes_bytes(M, a.K);
+  const int sms = g_sms > 0 ? g_sms : 148;
+  const int NC = NB * 4;
+  for (int per_sm = 2; per_sm >= 1; --per_sm) {
+    const size_t budget = per_sm == 2 ? 108 * 1024 : g_smem_max;
+    const int G = std::min(a.ngroups, sms * per_sm);
+    const int gpc = (a.ngroups + G - 1) / G;
+    const size_t extra = sizeof(float) * 9 * 16 + 64;  // part + fin per group (KS <= 8) + barriers
+    if (planes + 2 * (group_bytes + extra) > budget && per_sm == 2) continue;
+    int SG = int((budget - planes) / (2 * group_bytes + extra));
+    SG = std::max(1, std::min(SG, gpc));
+    int ks = 1;
+    while (ks < 8 && SG * ks * 2 <= 8 && NC / (ks * 2) >= 16) ks *= 2;
+    a.ksplit = ks;
+    a.stage_groups = SG;
+    a.slot_bytes = int((SG * group_bytes + 127) / 128 * 128);
+    *grid = G;
+    return 2 * size_t(a.slot_bytes) + planes + sizeof(float) * size_t(SG) * ks * 16 + sizeof(float) * SG * 16 + 16;
+  }
+  return 0;
 }
 
 template <int M, int PRO, int EPI, int DT>
-cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t s) {
-  const size_t smem = gemv_smem_bytes(M, a.K);
-  const int gpc = GEMV_WARPS / a.ksplit;
-  const int grid = (a.ngroups + gpc - 1) / gpc;
+cudaError_t launch_gemv_t(const GemvArgs& a0, cudaStream_t s) {
+  GemvArgs a = a0;
+  int grid = 0;
+  const size_t smem = plan_gemv<DT>(a, M, &grid);
+  if (smem == 0 || smem > g_smem_max) return cudaErrorInvalidValue;
   const cudaError_t e =
       launch_ex(gemv_kernel<M, PRO, EPI, DT>, dim3(grid), dim3(GEMV_THREADS), smem, s, a.pdl != 0, a);
   return e != cudaSuccess ? e : cudaGetLastError();
@@ -710,6 +934,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
   float* S = Vs + TS * HD;         // [n_rep][TS]
   float* ml = S + n_rep * TS;      // [n_rep][2] running (max, sum)
   float* corr = ml + 2 * n_rep;    // [n_rep] rescale of the running sums for this tile
+  float* mm = corr + n_rep;        // [n_rep][max_splits] split maxima, then merge weights
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float* qsrc = a.q + (size_t(t) * a.n_heads + size_t(kh) * n_rep) * HD;
   for (int i = tid; i < n_rep * HD / 4; i += ATT_THREADS)
@@ -825,17 +1050,42 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
   if (!s_last) return;
   __threadfence();
   if (tid == 0) a.ticket[t * a.n_kv + kh] = 0;
+  // merge: running max / sum of every (head, split) staged in shared memory first,
+  // then each (head, dim) output reads its nsplit partial sums with independent loads
+  const size_t hstride = size_t(a.max_splits) * pstride;
+  const float* pbase = a.part + (size_t(t) * a.n_heads + size_t(kh) * n_rep) * hstride;
+  for (int i = tid; i < n_rep * nsplit; i += ATT_THREADS) {
+    const int r = i / nsplit, sp = i % nsplit;
+    mm[r * nsplit + sp] = __ldcg(pbase + r * hstride + sp * pstride);
+  }
+  __syncthreads();
+  for (int r = warp; r < n_rep; r += ATT_WARPS) {
+    float M = -INFINITY;
+    for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, mm[r * nsplit + sp]);
+    M = warp_max(M);
+    float L = 0.0f;
+    for (int sp = lane; sp < nsplit; sp += 32) {
+      const float f = expf(mm[r * nsplit + sp] - M);
+      L += __ldcg(pbase + r * hstride + sp * pstride + 1) * f;
+      mm[r * nsplit + sp] = f;
+    }
+    L = warp_sum(L);
+    if (lane == 0) ml[2 * r + 1] = L;
+  }
+  __syncthreads();
   for (int i = tid; i < n_rep * HD; i += ATT_THREADS) {
     const int r = i / HD, d = i % HD;
-    const float* pp = a.part + (size_t(t) * a.n_heads + kh * n_rep + r) * a.max_splits * pstride;
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(pp + sp * pstride));
-    float L = 0.0f, O = 0.0f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float f = expf(__ldcg(pp + sp * pstride) - M);
-      L += __ldcg(pp + sp * pstride + 1) * f;
-      O += __ldcg(pp + sp * pstride + 2 + d) * f;
+    const float* pp = pbase + r * hstride + 2 + d;
+    float O = 0.0f;
+    int sp = 0;
+    for (; sp + 4 <= nsplit; sp += 4) {
+      const float o0 = __ldcg(pp + (sp + 0) * pstride), o1 = __ldcg(pp + (sp + 1) * pstride);
+      const float o2 = __ldcg(pp + (sp + 2) * pstride), o3 = __ldcg(pp + (sp + 3) * pstride);
+      O += o0 * mm[r * nsplit + sp] + o1 * mm[r * nsplit + sp + 1] + o2 * mm[r * nsplit + sp + 2] +
+           o3 * mm[r * nsplit + sp + 3];
     }
+    for (; sp < nsplit; ++sp) O += __ldcg(pp + sp * pstride) * mm[r * nsplit + sp];
+    const float L = ml[2 * r + 1];
     a.out[(size_t(t) * a.n_heads + kh * n_rep + r) * HD + d] = L > 0.0f ? O / L : 0.0f;
   }
 }
@@ -944,14 +1194,10 @@ __global__ void repack_q6k_kernel(const uint8_t* src, size_t nblocks, uint8_t* d
 
 }  // namespace
 
-size_t gemv_smem_bytes(int M, int K) {
-  return size_t(3) * M * K + sizeof(float) * (size_t(M) * (K / 32) + size_t(M) * (K / 16)) +
-         sizeof(float) * GEMV_WARPS * 16;
-}
 
 int gemv_max_cols(int K) {
   for (int m = 4; m > 1; --m)
-    if (gemv_smem_bytes(m, K) <= 96 * 1024) return m;
+    if (gemv_planes_bytes(m, K) <= 64 * 1024) return m;
   return 1;
 }
 
@@ -969,7 +1215,9 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
   const int n_rep = a.n_heads / a.n_kv;
   const int hd = a.head_dim;
   const size_t smem = sizeof(float) * (size_t(n_rep) * hd + size_t(ATT_TILE) * (hd + 1) + size_t(ATT_TILE) * hd +
-                                       size_t(n_rep) * ATT_TILE + 3 * size_t(n_rep));
+                                       size_t(n_rep) * ATT_TILE + 3 * size_t(n_rep) +
+                                       (a.max_splits > 1 ? size_t(n_rep) * a.max_splits : 0));
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
   if (n_rep * hd > ATT_THREADS * 16) return cudaErrorInvalidValue;
   const dim3 grid(a.n_kv, a.T, a.max_splits);
   cudaError_t e;
@@ -1015,10 +1263,18 @@ cudaError_t gemv_configure_all() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+  int optin = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e == cudaSuccess) g_smem_max = size_t(optin) - 2048;
   if (e == cudaSuccess) e = configure_gemv_m<1>();
   if (e == cudaSuccess) e = configure_gemv_m<2>();
   if (e == cudaSuccess) e = configure_gemv_m<3>();
   if (e == cudaSuccess) e = configure_gemv_m<4>();
+  const int att_max = int(std::min<size_t>(g_smem_max, 200 * 1024));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_max);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_max);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<128, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_max);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<128, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_max);
   return e;
 }
 

@@ -68,7 +68,9 @@ struct GemvArgs {
   int K;
   int M;              // activation rows (tokens) in this launch
   int ngroups;        // row groups of 4
-  int ksplit;         // warps sharing one row group (split over K)
+  int ksplit;         // K slices per row group (set by launch_gemv)
+  int stage_groups;   // row groups per shared-memory stage (set by launch_gemv)
+  int slot_bytes;     // bytes of one stage slot (set by launch_gemv)
   const float* x;     // [M][ldx] input (PRO_NONE) or residual stream h (PRO_RMSNORM)
   int ldx;
   const float* norm_w;  // PRO_RMSNORM weight
@@ -103,9 +105,21 @@ struct GemvArgs {
   int pdl;
 };
 
-size_t gemv_smem_bytes(int M, int K);
+// shared memory of the activation planes of M columns of K values (+ a
+// 8 x 16 float reduction scratch)
+WCB_HD inline size_t gemv_planes_bytes(int M, int K) {
+  return size_t(3) * M * K + sizeof(float) * 2 * size_t(M) * (K / 32) + sizeof(float) * 8 * 16;
+}
 int gemv_max_cols(int K);  // widest column group whose activation planes fit in shared memory
 cudaError_t launch_gemv(const GemvArgs& a, int pro, int epi, cudaStream_t s);
+
+// Tensor-core (tcgen05) GEMM for prefill: same arguments and epilogues as the
+// GEMV (EPI_STORE, EPI_RESID, EPI_QKV, EPI_SWIGLU), a.M = tokens (any count),
+// row_m = per-token RMSNorm divisors from launch_row_rms when pro == PRO_RMSNORM.
+cudaError_t gemm_tc_configure();
+cudaError_t launch_gemm_tc(const GemvArgs& a, int pro, int epi, const float* row_m, cudaStream_t s);
+cudaError_t launch_row_rms(const float* x, int ldx, int T, int K, float eps, float* m, bool pdl, cudaStream_t s);
+constexpr int TC_MIN_TOKENS = 16;  // below this the GEMV (dp4a) path is used
 
 // ----------------------------------------------------------- attention ----
 struct AttnArgs {

@@ -66,6 +66,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
   check(cudaSetDevice(device_), "cudaSetDevice");
   check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
   check(gemv_configure_all(), "configure GEMV kernels");
+  check(gemm_tc_configure(), "configure GEMM kernels");
   set_pdl(!(opt.flags & 2));
   try {
     // token embeddings (model.rs:432-446): first name that loads
@@ -163,6 +164,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     att_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
     act_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.ffn));
     logits_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
+    row_m_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_)));
     pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab));
     check(cudaMemset(pen_cnt_, 0, sizeof(uint32_t) * c.vocab), "clear penalty counts");
     // attention partials of one decode token split into DECODE_CHUNK-key pieces
@@ -308,12 +310,6 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
     a.nseg = s1 - s0;
     a.K = K;
     a.ngroups = epi == EPI_SWIGLU ? int(segs[0].rows) / 2 : rows / 4;
-    // split K over warps while the row groups alone leave the GPU under-filled,
-    // keeping at least 16 chunks of work per warp
-    const int chunks = (K / QK_K) * (segs[s0].dtype == DT_Q4K ? 8 : 4);
-    int ks = 1;
-    while (ks < 8 && a.ngroups * ks < 148 * 16 && chunks / (ks * 2) >= 16) ks *= 2;
-    a.ksplit = ks;
     a.norm_w = norm_w;
     a.eps = eps;
     a.ldx = ldx;
@@ -340,6 +336,25 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
     a.rep = rep_;
     a.hist = hist_;
     a.pdl = 1;
+    if (M >= TC_MIN_TOKENS && epi != EPI_LMHEAD && !(opt_.flags & 4)) {
+      // prefill: one tensor-core GEMM over all M tokens
+      GemvArgs b = a;
+      b.M = M;
+      b.x = x;
+      b.y = y;
+      b.resid = resid;
+      b.q = q;
+      b.token_offset = token_offset;
+      if (pro == PRO_RMSNORM) {
+        check(launch_row_rms(x, ldx, M, K, eps, row_m_, true, stream_), "row rms");
+        ++launches_;
+      }
+      check(launch_gemm_tc(b, pro, epi, row_m_, stream_), "gemm");
+      ++launches_;
+      row_offset += rows;
+      s0 = s1;
+      continue;
+    }
     const int mmax = epi == EPI_LMHEAD ? 1 : gemv_max_cols(K);
     for (int c0 = 0; c0 < M; c0 += mmax) {
       GemvArgs b = a;

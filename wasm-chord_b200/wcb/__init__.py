@@ -33,7 +33,7 @@ EXPORTED = [
     "wcb_clear_kv", "wcb_kv_len", "wcb_generate_tokens", "wcb_generate_batch", "wcb_sampler_new",
     "wcb_sampler_sample", "wcb_sampler_free", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
     "wcb_repack_q6k_dev", "wcb_gemv_dev", "wcb_model_stream", "wcb_infer", "wcb_next_tokens",
-    "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step",
+    "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_attention_dev",
 ]
 
 
@@ -101,9 +101,10 @@ def lib() -> C.CDLL:
     L.wcb_next_token.restype = C.c_int32
     L.wcb_close_stream.argtypes = [u32]
     L.wcb_model_launches_per_step.argtypes = [u32, C.POINTER(u32)]
+    L.wcb_attention_dev.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     for name in EXPORTED:
         f = getattr(L, name)
-        if f.restype is C.c_int:  # ctypes default
+        if f.restype is C.c_int and name != "wcb_next_token":  # ctypes default
             f.restype = u32
     _LIB = L
     return L
@@ -180,8 +181,10 @@ class Model:
 
     @classmethod
     def load_from_gguf(cls, path: str, device: int = 0, max_seq: int = 0, kv_dtype: int = KV_F32,
-                       max_batch: int = 1, use_graphs: bool = True) -> "Model":
-        o = _LoadOpts(device, max_seq, kv_dtype, max_batch, 0 if use_graphs else 1)
+                       max_batch: int = 1, use_graphs: bool = True, use_pdl: bool = True,
+                       use_tensor_cores: bool = True) -> "Model":
+        flags = (0 if use_graphs else 1) | (0 if use_pdl else 2) | (0 if use_tensor_cores else 4)
+        o = _LoadOpts(device, max_seq, kv_dtype, max_batch, flags)
         h = C.c_uint32(0)
         _check(lib().wcb_model_load(os.fsencode(path), C.byref(o), C.byref(h)))
         return cls(h.value)
@@ -332,3 +335,9 @@ def repack_q6k_dev(packed_ptr: int, nblocks: int, padded_ptr: int, stream: int =
 
 def gemv_dev(w_ptr: int, dtype: int, n: int, k: int, x_ptr: int, m: int, y_ptr: int, stream: int = 0) -> None:
     _check(lib().wcb_gemv_dev(w_ptr, dtype, n, k, x_ptr, m, y_ptr, stream or None))
+
+
+def attention_dev(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, n_tokens: int, n_heads: int, n_kv_heads: int,
+                  head_dim: int, max_seq: int, kv_len: int, position: int, stream: int = 0) -> None:
+    _check(lib().wcb_attention_dev(q_ptr, k_ptr, v_ptr, out_ptr, n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
+                                   kv_len, position, stream or None))
