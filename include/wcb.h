@@ -188,6 +188,21 @@ uint32_t wcb_attention_dev(const float* q, const float* k_cache, const float* v_
                            uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t max_seq,
                            uint32_t kv_len, uint32_t position, void* stream);
 
+/* The same attention as wcb_attention_dev, for callers that cannot allocate
+ * GPU memory once they are running (a host whose device memory is already
+ * handed to its own pool, or a serving loop that must not stall its other
+ * streams on the device-wide synchronisation of cudaMalloc / cudaFree). No
+ * counterpart in the reference. Allocates nothing: the scratch is a fixed
+ * 4 MiB array inside the library, which every GPU that loads the library keeps
+ * until exit. A call needing more (n_heads * splits * (head_dim + 2) floats for
+ * one query token, splits <= 64, plus 4 bytes per query token and kv head)
+ * fails with WCB_ERR_INVALID_ARGUMENT. The first call on each device looks up
+ * the array's device address; make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race. */
+uint32_t wcb_attention_dev_noalloc(const float* q, const float* k_cache, const float* v_cache, float* out,
+                                   uint32_t n_tokens, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                                   uint32_t max_seq, uint32_t kv_len, uint32_t position, void* stream);
+
 /* Device stream a model handle launches on (a cudaStream_t), for callers that
  * time or order work against it. */
 uint32_t wcb_model_stream(uint32_t handle, void** out_stream);

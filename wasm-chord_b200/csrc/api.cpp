@@ -80,6 +80,11 @@ uint32_t cuda_fail(cudaError_t e, const char* what) {
 
 }  // namespace
 
+// lets the other translation units of the library report through wcb_last_error
+extern "C" __attribute__((visibility("hidden"))) void wcb_internal_set_last_error(const char* msg) {
+  g_last_error = msg ? msg : "";
+}
+
 extern "C" {
 
 void wcb_gen_config_default(wcb_gen_config* c) {

@@ -34,6 +34,7 @@ EXPORTED = [
     "wcb_sampler_sample", "wcb_sampler_free", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
     "wcb_repack_q6k_dev", "wcb_gemv_dev", "wcb_model_stream", "wcb_infer", "wcb_next_tokens",
     "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_attention_dev",
+    "wcb_attention_dev_noalloc",
 ]
 
 
@@ -102,6 +103,7 @@ def lib() -> C.CDLL:
     L.wcb_close_stream.argtypes = [u32]
     L.wcb_model_launches_per_step.argtypes = [u32, C.POINTER(u32)]
     L.wcb_attention_dev.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
+    L.wcb_attention_dev_noalloc.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     for name in EXPORTED:
         f = getattr(L, name)
         if f.restype is C.c_int and name != "wcb_next_token":  # ctypes default
@@ -341,3 +343,11 @@ def attention_dev(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, n_tokens: in
                   head_dim: int, max_seq: int, kv_len: int, position: int, stream: int = 0) -> None:
     _check(lib().wcb_attention_dev(q_ptr, k_ptr, v_ptr, out_ptr, n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
                                    kv_len, position, stream or None))
+
+
+def attention_dev_noalloc(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, n_tokens: int, n_heads: int,
+                          n_kv_heads: int, head_dim: int, max_seq: int, kv_len: int, position: int,
+                          stream: int = 0) -> None:
+    """wcb_attention_dev with the library's fixed scratch array (no GPU allocation)."""
+    _check(lib().wcb_attention_dev_noalloc(q_ptr, k_ptr, v_ptr, out_ptr, n_tokens, n_heads, n_kv_heads, head_dim,
+                                           max_seq, kv_len, position, stream or None))
