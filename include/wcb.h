@@ -51,7 +51,8 @@ typedef struct wcb_load_opts {
   uint32_t kv_dtype;  /* WCB_KV_F32 (reference numerics) or WCB_KV_F16 */
   uint32_t max_batch; /* sequences per wcb_generate_batch call; 0 = 1 */
   uint32_t flags;     /* bit 0: no CUDA graphs for decode steps; bit 1: no programmatic
-                         dependent launch; bit 2: no tensor-core GEMM for prefill (GEMV only) */
+                         dependent launch; bit 2: no tensor-core GEMM for prefill (GEMV only);
+                         bit 3: no persistent decode-step kernel (one launch per op instead) */
 } wcb_load_opts;
 
 /* TransformerConfig — transformer/config.rs:6-41 (plus head_dim) */

@@ -140,6 +140,80 @@ struct AttnArgs {
 constexpr int ATT_TILE = 32;  // keys staged in shared memory per pass
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 
+// ------------------------------------------------ persistent decode step --
+// One launch runs a whole greedy decode step (T = 1): every layer's QKV + RoPE
+// + KV append, attention, output projection + residual, gate/up + SwiGLU,
+// down + residual, then the final norm, LM head, penalty, argmax and
+// generate()'s bookkeeping. One CTA per SM (cooperative launch, so all CTAs
+// are resident). A producer warp streams this CTA's share of every weight
+// matrix, phase after phase, through a ring of shared-memory slots with bulk
+// copies, independent of the activations; consumer warps wait only for the
+// activations of each phase, on a per-phase counter that every CTA bumps when
+// its share of the phase is written.
+enum MkKind { MK_QKV = 0, MK_ATT = 1, MK_O = 2, MK_GU = 3, MK_D = 4, MK_LM = 5 };
+
+// One weight "part" of a phase: rows of one quantisation type, processed in
+// groups of 4 rows (MK_GU: 2 gate + 2 up rows, giving 2 outputs).
+struct MkPart {
+  const uint8_t* w[3];  // MK_QKV: segments of the virtual [q; k; v] matrix; MK_GU: gate, up; else w[0]
+  int rows[3];          // rows of each segment
+  int nseg;
+  int kind;             // MkKind
+  int layer;
+  int dtype;            // DT_Q4K / DT_Q6K (MK_ATT: unused)
+  int K;                // input length
+  int ngroups;
+  int row_offset;       // MK_QKV: row of the virtual matrix at this part's row 0
+  int gpt;              // groups per tile (whole-K tiles)
+  int kbt;              // k-blocks per tile (K/256 unless the tile holds one group's K range)
+  int first, last;      // first / last part of its phase
+  int phase;            // phase index (its counter)
+  int dep;              // phase whose counter this phase waits on (-1: none)
+  int dep_target;       // counter value that releases it
+  const float* norm;    // RMSNorm weight of the phase input (null: none)
+  float eps;
+};
+
+struct MkArgs {
+  const MkPart* parts;
+  int nparts;
+  int nphases;
+  int* cnt;  // [nphases][32] phase counters (128-byte stride), zero between launches
+  StepState* st;
+  const float* emb;
+  int vocab, hidden, ffn, n_heads, n_kv, head_dim, max_seq;
+  const float* rope_cos;
+  const float* rope_sin;
+  void* kcache;  // [layers][n_kv][max_seq][hd]
+  void* vcache;
+  size_t kv_layer_elems;
+  int kv_half;
+  float attn_scale;
+  float* xa;            // residual stream between layers
+  float* xb;            // residual stream after attention
+  float* q;             // post-RoPE queries [hidden]
+  float* att;           // attention output [hidden]
+  float* act;           // SwiGLU output [ffn]
+  float* logits;        // [vocab]
+  const float* zero;    // [hidden] zeros (embedding of an out-of-vocabulary id)
+  float* part;          // attention split partials [n_heads][max_splits][hd + 2]
+  int* ticket;          // [n_kv], zero between launches
+  int max_splits;
+  int gen_mode;         // 1: token = hist[nhist - 1], penalty + argmax + bookkeeping
+  const uint32_t* ids;  // gen_mode 0: token = ids[0]
+  uint32_t* hist;
+  uint32_t* pen_cnt;
+  float rep;
+  // shared-memory layout (from decode_step_plan)
+  int slot_bytes, nslots, region_bytes, part_units;
+};
+// Fills the tile sizes of the parts and the shared-memory layout; false when
+// the model does not fit the persistent kernel (then the per-op kernels run).
+bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* smem);
+int decode_step_grid();  // CTAs of one launch (one per SM)
+cudaError_t decode_step_configure();
+cudaError_t launch_decode_step(const MkArgs& a, size_t smem, cudaStream_t s);
+
 // ------------------------------------------------------------ elementwise --
 cudaError_t launch_embed(const float* emb, int vocab, int hidden, const uint32_t* ids, int T, float* x,
                          const StepState* st, cudaStream_t s);

@@ -173,6 +173,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     ticket_ = static_cast<int*>(dalloc(sizeof(int) * size_t(t_max_) * c.kv_heads));
     check(cudaMemset(ticket_, 0, sizeof(int) * size_t(t_max_) * c.kv_heads), "clear tickets");
     check(cudaMallocHost(&host_ids_, sizeof(uint32_t) * std::max<size_t>(max_seq_, 1)), "cudaMallocHost");
+    build_decode_step();
     check(cudaDeviceSynchronize(), "load");
   } catch (...) {
     for (void* p : allocs_) cudaFree(p);
@@ -447,23 +448,225 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
   if (position + n > rope_len_) build_rope(uint32_t(std::max<size_t>(position + n, size_t(rope_len_) * 2)));
   std::memcpy(host_ids_, ids, n * sizeof(uint32_t));
   check(cudaMemcpyAsync(ids_, host_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "upload ids");
-  for (size_t c0 = 0; c0 < n; c0 += size_t(t_max_)) {
-    const int T = int(std::min(n - c0, size_t(t_max_)));
-    set_state(int(position + c0), int(kv_len_ + c0), T);
-    enqueue_forward(ids_ + c0, T, false);
+  if (n == 1 && mk_ok_) {  // one token: the persistent decode step
+    set_state(int(position), int(kv_len_), 1);
+    launch_decode_step_kernel(false);
+  } else {
+    for (size_t c0 = 0; c0 < n; c0 += size_t(t_max_)) {
+      const int T = int(std::min(n - c0, size_t(t_max_)));
+      set_state(int(position + c0), int(kv_len_ + c0), T);
+      enqueue_forward(ids_ + c0, T, false);
+    }
+    const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
+    enqueue_lm_head(last_T, false);
   }
-  const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
-  enqueue_lm_head(last_T, false);
   if (logits_out)
     check(cudaMemcpyAsync(logits_out, logits_, sizeof(float) * cfg_.vocab, cudaMemcpyDeviceToHost, stream_),
           "download logits");
   check(cudaStreamSynchronize(stream_), "forward");
+  if (n == 1 && mk_ok_) {
+    int err = 0;
+    check(cudaMemcpy(&err, &st_->err, sizeof(int), cudaMemcpyDeviceToHost), "read state");
+    if (err)
+      throw WcbError(E_BACKEND, "Backend error: decode step kernel: a bounded wait expired (device error word " +
+                                    std::to_string(err) + ")");
+  }
   kv_len_ += n;
+}
+
+// Phase list of the persistent decode step: per layer [q;k;v] (one part per
+// run of equal quantisation types), attention, o, gate/up, down; then the LM
+// head. Each phase waits on the counter of the phase whose output it reads.
+void Model::build_decode_step() {
+  mk_ok_ = false;
+  if (opt_.flags & 8) return;
+  if (decode_step_configure() != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  const ModelConfig& c = cfg_;
+  const int H = int(c.hidden), F = int(c.ffn);
+  const int grid = decode_step_grid();
+  std::vector<MkPart> parts;
+  int phase = 0, prev_d = -1;
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    const DevLayer& L = layers_[l];
+    const int p_qkv = phase++;
+    const DevWeight* segs[3] = {&L.q, &L.k, &L.v};
+    const size_t first = parts.size();
+    int row_off = 0;
+    for (int s0 = 0; s0 < 3;) {
+      int s1 = s0 + 1;
+      while (s1 < 3 && segs[s1]->dtype == segs[s0]->dtype) ++s1;
+      MkPart P{};
+      P.kind = MK_QKV;
+      P.layer = int(l);
+      P.dtype = segs[s0]->dtype;
+      P.K = H;
+      int rows = 0;
+      for (int i = s0; i < s1; ++i) {
+        P.w[i - s0] = segs[i]->ptr;
+        P.rows[i - s0] = int(segs[i]->rows);
+        rows += int(segs[i]->rows);
+      }
+      P.nseg = s1 - s0;
+      P.ngroups = rows / 4;
+      P.row_offset = row_off;
+      row_off += rows;
+      P.phase = p_qkv;
+      P.dep = prev_d;
+      P.dep_target = grid;
+      P.norm = L.attn_norm;
+      P.eps = 1e-6f;
+      parts.push_back(P);
+      s0 = s1;
+    }
+    parts[first].first = 1;
+    parts.back().last = 1;
+    const int p_att = phase++;
+    {
+      MkPart P{};
+      P.kind = MK_ATT;
+      P.layer = int(l);
+      P.phase = p_att;
+      P.dep = p_qkv;
+      P.dep_target = grid;
+      P.first = P.last = 1;
+      parts.push_back(P);
+    }
+    const int p_o = phase++;
+    {
+      MkPart P{};
+      P.kind = MK_O;
+      P.layer = int(l);
+      P.dtype = L.o.dtype;
+      P.K = H;
+      P.w[0] = L.o.ptr;
+      P.rows[0] = int(L.o.rows);
+      P.nseg = 1;
+      P.ngroups = int(L.o.rows) / 4;
+      P.phase = p_o;
+      P.dep = p_att;
+      P.dep_target = int(c.kv_heads);  // one signal per merged KV head
+      P.first = P.last = 1;
+      parts.push_back(P);
+    }
+    if (L.gate.dtype != L.up.dtype) return;  // gate/up rows are paired inside one tile
+    const int p_gu = phase++;
+    {
+      MkPart P{};
+      P.kind = MK_GU;
+      P.layer = int(l);
+      P.dtype = L.gate.dtype;
+      P.K = H;
+      P.w[0] = L.gate.ptr;
+      P.w[1] = L.up.ptr;
+      P.rows[0] = int(L.gate.rows);
+      P.rows[1] = int(L.up.rows);
+      P.nseg = 2;
+      P.ngroups = int(L.gate.rows) / 2;
+      P.phase = p_gu;
+      P.dep = p_o;
+      P.dep_target = grid;
+      P.norm = L.ffn_norm;
+      P.eps = 1e-6f;
+      P.first = P.last = 1;
+      parts.push_back(P);
+    }
+    const int p_d = phase++;
+    {
+      MkPart P{};
+      P.kind = MK_D;
+      P.layer = int(l);
+      P.dtype = L.down.dtype;
+      P.K = F;
+      P.w[0] = L.down.ptr;
+      P.rows[0] = int(L.down.rows);
+      P.nseg = 1;
+      P.ngroups = int(L.down.rows) / 4;
+      P.phase = p_d;
+      P.dep = p_gu;
+      P.dep_target = grid;
+      P.first = P.last = 1;
+      parts.push_back(P);
+    }
+    prev_d = p_d;
+  }
+  {
+    MkPart P{};
+    P.kind = MK_LM;
+    P.layer = int(c.layers);
+    P.dtype = lm_head_.dtype;
+    P.K = H;
+    P.w[0] = lm_head_.ptr;
+    P.rows[0] = int(lm_head_.rows);
+    P.nseg = 1;
+    P.ngroups = int(lm_head_.rows) / 4;
+    P.phase = phase++;
+    P.dep = prev_d;
+    P.dep_target = grid;
+    P.norm = out_norm_;
+    P.eps = c.eps;
+    P.first = P.last = 1;
+    parts.push_back(P);
+  }
+  MkArgs a{};
+  a.nparts = int(parts.size());
+  a.nphases = phase;
+  a.n_kv = int(c.kv_heads);
+  a.n_heads = int(c.heads);
+  a.head_dim = int(c.head_dim());
+  if (!decode_step_plan(parts.data(), a.nparts, a, int(c.heads / c.kv_heads), &mk_smem_)) return;
+  MkPart* dparts = static_cast<MkPart*>(dalloc(sizeof(MkPart) * parts.size()));
+  check(cudaMemcpy(dparts, parts.data(), sizeof(MkPart) * parts.size(), cudaMemcpyHostToDevice), "upload step plan");
+  a.parts = dparts;
+  a.cnt = static_cast<int*>(dalloc(sizeof(int) * 32 * size_t(phase)));
+  check(cudaMemset(a.cnt, 0, sizeof(int) * 32 * size_t(phase)), "clear counters");
+  a.st = st_;
+  a.emb = emb_;
+  a.vocab = int(c.vocab);
+  a.hidden = H;
+  a.ffn = F;
+  a.max_seq = int(max_seq_);
+  a.kcache = kcache_;
+  a.vcache = vcache_;
+  a.kv_layer_elems = kv_layer_elems_;
+  a.kv_half = int(opt_.kv_half);
+  a.attn_scale = attn_scale_;
+  a.xa = x_;
+  a.xb = h_;
+  a.q = q_;
+  a.att = att_;
+  a.act = act_;
+  a.logits = logits_;
+  float* zero = static_cast<float*>(dalloc(sizeof(float) * H));
+  check(cudaMemset(zero, 0, sizeof(float) * H), "clear zero row");
+  a.zero = zero;
+  a.part = static_cast<float*>(
+      dalloc(sizeof(float) * size_t(c.heads) * size_t(a.max_splits) * (c.head_dim() + 2)));
+  a.ticket = static_cast<int*>(dalloc(sizeof(int) * c.kv_heads));
+  check(cudaMemset(a.ticket, 0, sizeof(int) * c.kv_heads), "clear tickets");
+  a.ids = ids_;
+  a.hist = hist_;
+  a.pen_cnt = pen_cnt_;
+  mk_ = a;
+  mk_ok_ = true;
+}
+
+void Model::launch_decode_step_kernel(bool gen) {
+  MkArgs a = mk_;
+  a.rope_cos = rope_cos_;
+  a.rope_sin = rope_sin_;
+  a.gen_mode = gen ? 1 : 0;
+  a.rep = rep_;
+  check(launch_decode_step(a, mk_smem_, stream_), "decode step");
 }
 
 void Model::decode_steps(int steps) {
   for (int i = 0; i < steps; ++i) {
-    if (decode_exec_) {
+    if (mk_ok_) {
+      launch_decode_step_kernel(true);
+    } else if (decode_exec_) {
       check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
     } else {
       enqueue_forward(nullptr, 1, true);
@@ -541,7 +744,12 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   }
   const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
   enqueue_lm_head(last_T, true);  // samples the first token (no EOS check)
-  if (!(opt_.flags & 1) && (!decode_exec_ || graph_rep_ != rep)) {
+  if (mk_ok_) {
+    // counters of a step that ended on an error are cleared here
+    check(cudaMemsetAsync(mk_.cnt, 0, sizeof(int) * 32 * size_t(mk_.nphases), stream_), "clear counters");
+    check(cudaMemsetAsync(mk_.ticket, 0, sizeof(int) * size_t(mk_.n_kv), stream_), "clear tickets");
+    launches_per_step_ = 1;
+  } else if (!(opt_.flags & 1) && (!decode_exec_ || graph_rep_ != rep)) {
     if (decode_exec_) {
       cudaGraphExecDestroy(decode_exec_);
       cudaGraphDestroy(decode_graph_);
@@ -560,6 +768,11 @@ void Model::sync_session_state() {
   check(cudaMemcpyAsync(&sess_state_, st_, sizeof(StepState), cudaMemcpyDeviceToHost, stream_), "read state");
   check(cudaStreamSynchronize(stream_), "generate");
   kv_len_ = size_t(sess_state_.kv_len);
+  if (sess_state_.err & 12) {
+    sess_done_ = true;
+    throw WcbError(E_BACKEND, "Backend error: decode step kernel: a bounded wait expired (device error word " +
+                                  std::to_string(sess_state_.err) + ")");
+  }
   if (sess_state_.err == 1) {
     sess_done_ = true;
     throw WcbError(E_GENERIC, "Runtime error: NaN logit");

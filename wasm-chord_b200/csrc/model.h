@@ -85,6 +85,8 @@ class Model {
   void check(cudaError_t e, const char* what);
   void decode_steps(int steps);
   void capture_decode_graph();
+  void build_decode_step();
+  void launch_decode_step_kernel(bool gen);
 
   ModelConfig cfg_;
   LoadOptions opt_;
@@ -144,6 +146,11 @@ class Model {
   std::vector<uint32_t> sess_tokens_;  // host-sampled path: generated ids
   uint32_t sess_last_ = 0;
   StepState sess_state_{};
+
+  // persistent decode step (one cooperative launch per token)
+  bool mk_ok_ = false;
+  MkArgs mk_{};
+  size_t mk_smem_ = 0;
 
   cudaGraphExec_t decode_exec_ = nullptr;
   cudaGraph_t decode_graph_ = nullptr;

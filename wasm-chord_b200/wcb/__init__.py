@@ -184,8 +184,9 @@ class Model:
     @classmethod
     def load_from_gguf(cls, path: str, device: int = 0, max_seq: int = 0, kv_dtype: int = KV_F32,
                        max_batch: int = 1, use_graphs: bool = True, use_pdl: bool = True,
-                       use_tensor_cores: bool = True) -> "Model":
-        flags = (0 if use_graphs else 1) | (0 if use_pdl else 2) | (0 if use_tensor_cores else 4)
+                       use_tensor_cores: bool = True, use_persistent: bool = True) -> "Model":
+        flags = ((0 if use_graphs else 1) | (0 if use_pdl else 2) | (0 if use_tensor_cores else 4)
+                 | (0 if use_persistent else 8))
         o = _LoadOpts(device, max_seq, kv_dtype, max_batch, flags)
         h = C.c_uint32(0)
         _check(lib().wcb_model_load(os.fsencode(path), C.byref(o), C.byref(h)))
