@@ -1,32 +1,33 @@
 // Persistent decode step: one cooperative launch per generated token.
 //
 // Every CTA (one per SM) owns a fixed share of the rows of every weight matrix
-// of the step. Its producer warp walks that share phase after phase (layer by
-// layer: [q;k;v], o, gate/up, down, then the LM head) and streams it into a
-// ring of shared-memory slots with cp.async.bulk copies completing on
-// mbarriers. Weights never depend on the activations, so the copies run ahead
-// across phase boundaries and HBM stays busy while the consumer warps wait for
-// the inputs of the next phase.
+// of the step; the host lists each CTA's tiles (whole-K row groups) in
+// consumption order: layer by layer [q;k;v], o, gate/up, down, then the LM
+// head. The tiles stream into a ring of shared-memory slots with cp.async.bulk
+// copies completing on mbarriers. A producer warp refills a slot with the tile
+// nslots further on as soon as every consumer warp has left it (an "empty"
+// mbarrier), so the copies run ahead across phase boundaries: weights never
+// depend on the activations.
 //
-// Consumer warps, per phase: wait until the phase's input vector is complete
-// (a per-phase counter that each CTA increments after writing its share, read
-// with acquire semantics; waits are bounded and flag an error word on expiry),
-// quantise the input into integer limbs (the same planes as the per-op GEMV,
-// with the RMSNorm of candle's rms_norm fused in), run the dp4a dot products of
-// each weight tile, reduce the K slices in a fixed order and apply the fused
-// epilogue (RoPE + KV append, residual add, SwiGLU, LM-head penalty + argmax).
-// The attention phase runs on the first n_kv * splits CTAs: split-K over the
-// keys with the previous steps' K/V staged before the wait, merged by the last
-// CTA of each KV head.
+// Activations that cross CTAs travel as (float bits, tag) pairs written with
+// one 64-bit store; the tag names the producing phase of this launch
+// (epoch * 1024 + phase + 1). A consumer thread spins (bounded) on the
+// elements it reads until they carry the expected tag, so a phase starts as
+// soon as its own inputs exist: there are no counters, fences or grid-wide
+// barriers between phases. Per phase a CTA quantises its input into integer
+// limbs (with candle's RMSNorm fused in), then its warps run the dp4a dot
+// products of the tiles and the fused epilogues (RoPE + KV append, residual
+// add, SwiGLU, LM-head penalty + argmax) independently of one another.
 //
-// Data written by one CTA and read by another inside the launch is read with
-// ld.global.cg (L2), never through the non-coherent L1.
-#include <cooperative_groups.h>
+// Attention runs on the first n_kv * splits CTAs: split-K over the keys, the
+// earlier steps' keys staged before this step's q / k / v are polled, merged
+// by the last CTA of each KV head (ticket).
 #include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <vector>
 
 #include "device_common.cuh"
 #include "kernels.h"
@@ -35,25 +36,65 @@ namespace wcb {
 
 namespace {
 
-constexpr int MK_CW = 15;               // consumer warps (16 warps per CTA: 128 registers a thread)
-constexpr int MK_CT = MK_CW * 32;       // consumer threads
-constexpr int MK_THREADS = MK_CT + 32;  // + the producer warp
-constexpr int MK_MAX_K = 16384;         // longest GEMV input kept in registers by the plane builder
-constexpr int MK_RND = (MK_MAX_K + MK_CT * 8 - 1) / (MK_CT * 8);
-constexpr int MK_TS = 32;               // keys per attention tile
-constexpr long long MK_WAIT_CYCLES = 4000000000ll;  // ~2 s at 2 GHz: bound of every spin wait
+constexpr int MK_W = 15;            // consumer warps per CTA
+constexpr int MK_T = MK_W * 32;     // consumer threads per CTA
+constexpr int MK_THREADS = MK_T + 32;  // + the producer warp (16 warps: 128 registers a thread)
+constexpr int MK_MAX_K = 16384;     // longest GEMV input (limb planes in shared memory)
+constexpr int MK_TS = 32;           // keys per attention tile
+constexpr int MK_MAX_TILES = 2048;  // tiles of one CTA per step (list kept in shared memory)
+constexpr int MK_GPT = 32;          // most groups in one tile
+constexpr long long MK_WAIT_NS = 2000000000ll;  // bound of every spin wait (2 s)
+constexpr uint32_t MK_MBAR_POLLS = 1u << 22;
 
-// named barrier of the consumer warps (the producer warp never joins it)
-__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(MK_CT) : "memory"); }
-
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+// barrier of the consumer warps (the producer warp never joins it)
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(MK_T) : "memory"); }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// (value, tag) pairs: one single-copy-atomic 64-bit access each
+__device__ __forceinline__ void st_tag(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void ld_tag2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint32_t tag_of(unsigned long long w) { return uint32_t(w >> 32); }
+__device__ __forceinline__ float val_of(unsigned long long w) { return __uint_as_float(uint32_t(w)); }
+
+// Reads N (even; 16-byte aligned start) tagged values, spinning until every
+// one carries `tag`; false when the bound expires. skip: read once, no wait.
+template <int N>
+__device__ __forceinline__ bool poll_tagged(const unsigned long long* p, uint32_t tag, float (&out)[N], bool skip) {
+  unsigned long long w[N];
+#pragma unroll
+  for (int i = 0; i < N; i += 2) ld_tag2(p + i, w[i], w[i + 1]);
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < N; ++i) ok &= tag_of(w[i]) == tag;
+  if (!ok && !skip) {
+    const unsigned long long t0 = gtime();
+    while (true) {
+#pragma unroll
+      for (int i = 0; i < N; i += 2)
+        if (tag_of(w[i]) != tag || tag_of(w[i + 1]) != tag) ld_tag2(p + i, w[i], w[i + 1]);
+      ok = true;
+#pragma unroll
+      for (int i = 0; i < N; ++i) ok &= tag_of(w[i]) == tag;
+      if (ok || gtime() - t0 > MK_WAIT_NS) break;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = val_of(w[i]);
+  return ok || skip;
 }
 
 template <typename KT>
@@ -70,441 +111,660 @@ __device__ __forceinline__ float4 ldcg_kv4<__half>(const __half* p) {
   return make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
+__device__ __forceinline__ bool mbar_wait_n(uint64_t* bar, uint32_t parity, uint32_t polls) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t it = 0; it < polls; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+// Limb planes of one GEMV input (K = 256 * NB values), laid out so that the
+// eight lanes of a quarter warp, which read the same 16-value piece of eight
+// consecutive blocks, hit consecutive 16-byte words:
+//   x[plane 0..2][piece s 0..3][pair pr 0..3] rows of RS bytes, 16 bytes per block
+//   (value o of block b: pr = o / 64, s = (o % 64) / 16)
+//   scale / sum32[sub-block j 0..7] rows of NBS floats, one per block
+// RS = 16 (mod 128) and NBS = 4 (mod 16) spread the writers over the banks.
+struct Planes {
+  uint32_t x;      // shared address of the limb rows
+  uint32_t scale;  // shared address of the scales
+  uint32_t sum32;
+  int RS, NBS;
+};
+
+__host__ __device__ __forceinline__ int planes_rs(int NB) { return ((NB * 16 + 111) / 128) * 128 + 16; }
+__host__ __device__ __forceinline__ int planes_nbs(int NB) { return ((NB + 11) / 16) * 16 + 4; }
+__host__ __device__ __forceinline__ size_t planes_bytes(int K) {
+  const int NB = K / QK_K;
+  return size_t(48) * planes_rs(NB) + 2 * sizeof(float) * 8 * size_t(planes_nbs(NB));
+}
+
+__device__ __forceinline__ Planes planes_at(uint32_t base, int K) {
+  Planes p;
+  const int NB = K / QK_K;
+  p.RS = planes_rs(NB);
+  p.NBS = planes_nbs(NB);
+  p.x = base;
+  p.scale = base + 48u * uint32_t(p.RS);
+  p.sum32 = p.scale + 4u * 8u * uint32_t(p.NBS);
+  return p;
+}
+
+__device__ __forceinline__ void sts2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void stsf(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Quantises the 8 values v[] at input index k (k % 8 == 0) into the planes.
+// Four consecutive lanes hold one 32-value group: X = rint(x / s) with
+// s = max|x| / (2^22 - 1), split into bytes X = 65536 x2 + 256 x1 + x0.
+__device__ __forceinline__ void quant8_planes(const float (&v)[8], int k, const Planes& p) {
+  float amax = 0.0f;
+  bool bad = false;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    amax = fmaxf(amax, fabsf(v[e]));
+    bad |= !(fabsf(v[e]) <= FLT_MAX);  // NaN / inf
+  }
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  bad = __shfl_xor_sync(0xffffffffu, int(bad), 1) | bad;
+  bad = __shfl_xor_sync(0xffffffffu, int(bad), 2) | bad;
+  int X[8];
+  float s;
+  if (!bad && amax > 0.0f) {
+    const float inv = XQ_MAX / amax;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) X[e] = max(-XQ_IMAX, min(XQ_IMAX, __float2int_rn(v[e] * inv)));
+    s = amax / XQ_MAX;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) X[e] = 0;
+    s = bad ? __int_as_float(0x7fc00000) : 0.0f;  // inf / NaN input -> NaN output
+  }
+  uint32_t w[3][2];
+  int sx = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int x = X[4 * h + e];
+      b0 |= uint32_t(x & 0xFF) << (8 * e);
+      b1 |= uint32_t((x >> 8) & 0xFF) << (8 * e);
+      b2 |= uint32_t((x >> 16) & 0xFF) << (8 * e);
+      sx += x;
+    }
+    w[0][h] = b0;
+    w[1][h] = b1;
+    w[2][h] = b2;
+  }
+  const int b = k >> 8, o = k & 255, pr = o >> 6, sp = (o >> 4) & 3, half = (o >> 3) & 1;
+#pragma unroll
+  for (int pl = 0; pl < 3; ++pl)
+    sts2(p.x + uint32_t(((pl * 4 + sp) * 4 + pr) * p.RS + b * 16 + half * 8), w[pl][0], w[pl][1]);
+  sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+  sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // |sum X| <= 32 * (2^22 - 1) < 2^31
+  if ((threadIdx.x & 3) == 0) {
+    const uint32_t j = uint32_t(o >> 5);
+    stsf(p.scale + 4u * (j * uint32_t(p.NBS) + uint32_t(b)), s);
+    stsf(p.sum32 + 4u * (j * uint32_t(p.NBS) + uint32_t(b)), s * float(sx));
+  }
+}
+
+// Dot products of one (4-row group, 64-value chunk) unit of a Q4_K tile for
+// the lane's chunk: pair pr = lane / 8 of block b. The same arithmetic as the
+// per-op GEMV: exact integer dp4a over the limbs, one scale per sub-block
+// (dequantize_q4_k, quant.rs:58-115, folded into the sum). Values 0-15 and
+// 16-31 of the two sub-blocks are taken in two passes to keep few limbs live.
+__device__ __forceinline__ void q4k_unit(const uint32_t (&ra)[ROWS], int b, int pr, const Planes& P,
+                                         float (&acc)[ROWS]) {
+  int du[ROWS][6];
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i)
+#pragma unroll
+    for (int j = 0; j < 6; ++j) du[i][j] = 0;
+  const uint32_t step = uint32_t(4 * P.RS);  // next piece s
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint4 xl[3], xh[3];
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      const uint32_t r0 = P.x + uint32_t(((l * 4) * 4 + pr) * P.RS + b * 16);
+      xl[l] = lds4(r0 + uint32_t(h) * step);        // sub-block 2pr, values 16h..16h+15
+      xh[l] = lds4(r0 + uint32_t(2 + h) * step);    // sub-block 2pr+1, same values
+    }
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) {
+      const uint4 qv = lds4(ra[i] + uint32_t(b * Q4K_BYTES + 16 + 32 * pr + 16 * h));
+      const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
+      const uint32_t xs[3][4] = {{xl[0].x, xl[0].y, xl[0].z, xl[0].w},
+                                 {xl[1].x, xl[1].y, xl[1].z, xl[1].w},
+                                 {xl[2].x, xl[2].y, xl[2].z, xl[2].w}};
+      const uint32_t ys[3][4] = {{xh[0].x, xh[0].y, xh[0].z, xh[0].w},
+                                 {xh[1].x, xh[1].y, xh[1].z, xh[1].w},
+                                 {xh[2].x, xh[2].y, xh[2].z, xh[2].w}};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t lo = q[e] & 0x0F0F0F0Fu, hi = (q[e] >> 4) & 0x0F0F0F0Fu;
+        du[i][0] = dp4a_uu(lo, xs[0][e], du[i][0]);
+        du[i][1] = dp4a_uu(lo, xs[1][e], du[i][1]);
+        du[i][2] = dp4a_us(lo, xs[2][e], du[i][2]);
+        du[i][3] = dp4a_uu(hi, ys[0][e], du[i][3]);
+        du[i][4] = dp4a_uu(hi, ys[1][e], du[i][4]);
+        du[i][5] = dp4a_us(hi, ys[2][e], du[i][5]);
+      }
+    }
+  }
+  const uint32_t jl = uint32_t(2 * pr), jh = jl + 1;
+  const float s_lo = ldsf(P.scale + 4u * (jl * uint32_t(P.NBS) + uint32_t(b)));
+  const float s_hi = ldsf(P.scale + 4u * (jh * uint32_t(P.NBS) + uint32_t(b)));
+  const float m_lo = ldsf(P.sum32 + 4u * (jl * uint32_t(P.NBS) + uint32_t(b)));
+  const float m_hi = ldsf(P.sum32 + 4u * (jh * uint32_t(P.NBS) + uint32_t(b)));
+  const bool upper = pr >= 2;
+  const int sh = 16 * (pr & 1);
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) {
+    const uint4 hd = lds4(ra[i] + uint32_t(b * Q4K_BYTES));
+    // get_scale_min_k4 (quant.rs:43-53) for sub-blocks 2pr and 2pr+1, branch-free
+    const uint32_t y = hd.y >> sh, z = hd.z >> sh, w = hd.w >> sh;
+    const uint32_t y0 = y & 0xFF, y1 = (y >> 8) & 0xFF, z0 = z & 0xFF, z1 = (z >> 8) & 0xFF;
+    const uint32_t w0 = w & 0xFF, w1 = (w >> 8) & 0xFF;
+    const uint32_t sc0 = upper ? ((w0 & 0xF) | ((y0 >> 6) << 4)) : (y0 & 63);
+    const uint32_t sc1 = upper ? ((w1 & 0xF) | ((y1 >> 6) << 4)) : (y1 & 63);
+    const uint32_t mn0 = upper ? ((w0 >> 4) | ((z0 >> 6) << 4)) : (z0 & 63);
+    const uint32_t mn1 = upper ? ((w1 >> 4) | ((z1 >> 6) << 4)) : (z1 & 63);
+    const float d = half_bits(hd.x & 0xFFFFu), dmin = half_bits(hd.x >> 16);
+    // |sum q*X| <= 32*15*(2^22-1) < 2^31: exact in int32
+    const int dlo = du[i][2] * 65536 + du[i][1] * 256 + du[i][0];
+    const int dhi = du[i][5] * 65536 + du[i][4] * 256 + du[i][3];
+    const float dot = float(sc0) * s_lo * float(dlo) + float(sc1) * s_hi * float(dhi);
+    const float mn = float(mn0) * m_lo + float(mn1) * m_hi;
+    acc[i] += d * dot - dmin * mn;
+  }
+}
+
+// Q6_K (224-byte padded blocks): chunk q = lane / 8 of block b = half hh = q/2,
+// 16-column slice aa = q%2 of the 32-wide interleave (quant.rs:206-261): four
+// 16-value pieces k = 0..3 at values 128 hh + 32 k + 16 aa; pieces k and k+2
+// share the low / high nibbles of one ql word set and are taken together.
+__device__ __forceinline__ void q6k_unit(const uint32_t (&ra)[ROWS], int b, int q, const Planes& P,
+                                         float (&acc)[ROWS]) {
+  const int hh = q >> 1, aa = q & 1;
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    uint4 xa[3], xb[3];
+    float sa, sb;
+    {
+      const int ka = kk, kb = kk + 2;  // pieces: pr = 2hh + (k >> 1), s = 2(k & 1) + aa
+      const int pra = 2 * hh + (ka >> 1), spa = 2 * (ka & 1) + aa;
+      const int prb = 2 * hh + (kb >> 1), spb = 2 * (kb & 1) + aa;
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        xa[l] = lds4(P.x + uint32_t(((l * 4 + spa) * 4 + pra) * P.RS + b * 16));
+        xb[l] = lds4(P.x + uint32_t(((l * 4 + spb) * 4 + prb) * P.RS + b * 16));
+      }
+      sa = ldsf(P.scale + 4u * (uint32_t(4 * hh + ka) * uint32_t(P.NBS) + uint32_t(b)));
+      sb = ldsf(P.scale + 4u * (uint32_t(4 * hh + kb) * uint32_t(P.NBS) + uint32_t(b)));
+    }
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) {
+      const uint32_t blk = ra[i] + uint32_t(b * Q6K_DEV_BYTES);
+      const uint4 ql = lds4(blk + 64 * hh + 32 * kk + 16 * aa);
+      const uint4 qh = lds4(blk + 128 + 32 * hh + 16 * aa);
+      const uint4 scw = lds4(blk + 192);
+      const float d = half_bits(lds4(blk + 208).x & 0xFFFFu);
+      const uint32_t L[4] = {ql.x, ql.y, ql.z, ql.w};
+      const uint32_t Q[4] = {qh.x, qh.y, qh.z, qh.w};
+      const uint32_t S[4] = {scw.x, scw.y, scw.z, scw.w};
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int k = kk + 2 * t;
+        const uint4* xx = t == 0 ? xa : xb;
+        uint32_t sq[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t nib = t == 0 ? (L[e] & 0x0F0F0F0Fu) : ((L[e] >> 4) & 0x0F0F0F0Fu);
+          const uint32_t hb = ((Q[e] >> (2 * k)) & 0x03030303u) << 4;
+          sq[e] = __vsub4(nib | hb, 0x20202020u);  // signed bytes q - 32
+        }
+        const int sidx = 8 * hh + aa + 2 * k;
+        const int scv = int(int8_t(byte_of(S[sidx >> 2], sidx & 3)));
+        int u0 = 0, u1 = 0, u2 = 0;
+        u0 = dp4a_su(sq[0], xx[0].x, u0); u0 = dp4a_su(sq[1], xx[0].y, u0); u0 = dp4a_su(sq[2], xx[0].z, u0); u0 = dp4a_su(sq[3], xx[0].w, u0);
+        u1 = dp4a_su(sq[0], xx[1].x, u1); u1 = dp4a_su(sq[1], xx[1].y, u1); u1 = dp4a_su(sq[2], xx[1].z, u1); u1 = dp4a_su(sq[3], xx[1].w, u1);
+        u2 = dp4a_ss(sq[0], xx[2].x, u2); u2 = dp4a_ss(sq[1], xx[2].y, u2); u2 = dp4a_ss(sq[2], xx[2].z, u2); u2 = dp4a_ss(sq[3], xx[2].w, u2);
+        const float fd = float(u2) * 65536.0f + float(u1) * 256.0f + float(u0);
+        acc[i] += d * float(scv) * (t == 0 ? sa : sb) * fd;
+      }
+    }
+  }
+}
+
 // Shared-memory carve-up of one CTA (sizes in MkArgs, set on the host):
-//   [slots]   nslots x slot_bytes weight tiles
-//   [region]  activation planes (GEMV phases) or attention staging
-//   [part]    2 x part_units x 16 floats: per-unit partial sums, ping-pong per tile
-//   [misc]    gacc[16], red[64], flags[8]
-//   [bars]    full[nslots], empty[nslots]
+//   [slots]  nslots x slot_bytes weight tiles
+//   [region] limb planes (GEMV phases) or attention staging
+//   [parts]  the part list; [tstart] this CTA's first tile of each part
+//   [tiles]  this CTA's tile list (8 bytes a tile)
+//   [rsd]    residual rows of this CTA's o / down share
+//   [rope]   cos, sin of this CTA's q / k rows (current layer)
+//   [pen]    penalty counts of this CTA's LM-head rows
+//   [misc]   red[64] floats, flags[8]
+//   [bars]   full[nslots]
 struct MkSmem {
   uint8_t* slots;
   uint8_t* region;
-  float* part;
-  float* gacc;
+  MkPart* parts;
+  int* tstart;
+  MkTile* tiles;
+  float* rsd;
+  float* rcos;
+  float* rsin;
+  uint32_t* pen;
   float* red;
-  int* flags;  // [0] abort
+  int* flags;  // [0] abort, [1] attention ticket result, [2] NaN seen
   uint64_t* full;
   uint64_t* empty;
 };
 
-__device__ __forceinline__ MkSmem mk_carve(uint8_t* smem, const MkArgs& a) {
+// Byte offsets of the carve-up (host and device agree on them).
+struct MkOffsets {
+  size_t region, parts, tstart, tiles, rsd, rcos, rsin, pen, red, flags, full, empty, total;
+};
+
+__host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
+  MkOffsets o;
+  size_t x = size_t(a.nslots) * a.slot_bytes;
+  o.region = x;
+  x += a.region_bytes;
+  o.parts = x;
+  x += sizeof(MkPart) * size_t(a.nparts);
+  o.tstart = x;
+  x += sizeof(int) * size_t(a.nparts + 1);
+  x = (x + 7) / 8 * 8;
+  o.tiles = x;
+  x += sizeof(MkTile) * size_t(a.max_tiles);
+  o.rsd = x;
+  x += sizeof(float) * size_t(a.res_rows);
+  o.rcos = x;
+  x += sizeof(float) * size_t(a.rope_rows);
+  o.rsin = x;
+  x += sizeof(float) * size_t(a.rope_rows);
+  o.pen = x;
+  x += sizeof(uint32_t) * size_t(a.lm_rows);
+  o.red = x;
+  x += sizeof(float) * 64;
+  o.flags = x;
+  x += sizeof(int) * 8;
+  x = (x + 7) / 8 * 8;
+  o.full = x;
+  x += sizeof(uint64_t) * size_t(a.nslots);
+  o.empty = x;
+  x += sizeof(uint64_t) * size_t(a.nslots);
+  o.total = x;
+  return o;
+}
+
+__device__ __forceinline__ MkSmem mk_carve(const MkArgs& a, uint8_t* b) {
+  const MkOffsets o = mk_offsets(a);
   MkSmem s;
-  s.slots = smem;
-  uint8_t* p = smem + size_t(a.nslots) * a.slot_bytes;
-  s.region = p;
-  p += a.region_bytes;
-  s.part = reinterpret_cast<float*>(p);
-  p += sizeof(float) * 2 * 16 * size_t(a.part_units);
-  s.gacc = reinterpret_cast<float*>(p);
-  s.red = s.gacc + 16;
-  s.flags = reinterpret_cast<int*>(s.red + 64);
-  s.full = reinterpret_cast<uint64_t*>(s.flags + 8);
-  s.empty = s.full + a.nslots;
+  s.slots = b;
+  s.region = b + o.region;
+  s.parts = reinterpret_cast<MkPart*>(b + o.parts);
+  s.tstart = reinterpret_cast<int*>(b + o.tstart);
+  s.tiles = reinterpret_cast<MkTile*>(b + o.tiles);
+  s.rsd = reinterpret_cast<float*>(b + o.rsd);
+  s.rcos = reinterpret_cast<float*>(b + o.rcos);
+  s.rsin = reinterpret_cast<float*>(b + o.rsin);
+  s.pen = reinterpret_cast<uint32_t*>(b + o.pen);
+  s.red = reinterpret_cast<float*>(b + o.red);
+  s.flags = reinterpret_cast<int*>(b + o.flags);
+  s.full = reinterpret_cast<uint64_t*>(b + o.full);
+  s.empty = reinterpret_cast<uint64_t*>(b + o.empty);
   return s;
 }
 
 // Groups [g0, g1) of a part owned by CTA c of n.
-__device__ __forceinline__ void cta_share(int ngroups, int c, int n, int& g0, int& g1) {
+__host__ __device__ __forceinline__ void cta_share(int ngroups, int c, int n, int& g0, int& g1) {
   g0 = int((long long)c * ngroups / n);
   g1 = int((long long)(c + 1) * ngroups / n);
 }
 
-// Tile t of this CTA's share: groups [g, g + ng), k-blocks [kb0, kb0 + nkb).
-struct Tile {
-  int g, ng, kb0, nkb;
-};
-
-__device__ __forceinline__ int tiles_of(const MkPart& P, int g0, int g1) {
-  const int nb = P.K / QK_K;
-  if (g1 <= g0) return 0;
-  if (P.kbt >= nb) return (g1 - g0 + P.gpt - 1) / P.gpt;
-  return (g1 - g0) * ((nb + P.kbt - 1) / P.kbt);
-}
-
-__device__ __forceinline__ Tile tile_at(const MkPart& P, int g0, int g1, int t) {
-  const int nb = P.K / QK_K;
-  Tile r;
-  if (P.kbt >= nb) {
-    r.g = g0 + t * P.gpt;
-    r.ng = min(P.gpt, g1 - r.g);
-    r.kb0 = 0;
-    r.nkb = nb;
-  } else {
-    const int kt = (nb + P.kbt - 1) / P.kbt;
-    r.g = g0 + t / kt;
-    r.ng = 1;
-    r.kb0 = (t % kt) * P.kbt;
-    r.nkb = min(P.kbt, nb - r.kb0);
-  }
-  return r;
-}
-
-// Global address of row r (0-based within the part) of a non-SwiGLU part.
-__device__ __forceinline__ const uint8_t* part_row(const MkPart& P, int r, size_t row_bytes) {
-  if (r < P.rows[0]) return P.w[0] + size_t(r) * row_bytes;
-  r -= P.rows[0];
-  if (P.nseg > 1 && r < P.rows[1]) return P.w[1] + size_t(r) * row_bytes;
-  r -= P.rows[1];
-  return P.w[2] + size_t(r) * row_bytes;
-}
-
-// Producer: the bulk copies of one tile into slot memory dst (completing on bar).
-__device__ void issue_tile(const MkPart& P, const Tile& T, uint8_t* dst, uint64_t* bar) {
-  const size_t bb = dev_block_bytes(P.dtype);
-  const size_t row_bytes = size_t(P.K / QK_K) * bb;
-  const uint32_t rb = uint32_t(size_t(T.nkb) * bb);
-  mbar_expect_tx(bar, 4u * uint32_t(T.ng) * rb);
-  const bool whole = T.nkb * bb == row_bytes;
-  if (P.kind == MK_GU) {
-    if (whole) {
-      const uint32_t bytes = 2u * uint32_t(T.ng) * rb;
-      bulk_g2s(dst, P.w[0] + size_t(2 * T.g) * row_bytes, bytes, bar);
-      bulk_g2s(dst + bytes, P.w[1] + size_t(2 * T.g) * row_bytes, bytes, bar);
-    } else {
-      for (int i = 0; i < 4; ++i)
-        bulk_g2s(dst + i * rb, P.w[i >> 1] + size_t(2 * T.g + (i & 1)) * row_bytes + size_t(T.kb0) * bb, rb, bar);
-    }
+// Bulk copies of one tile (ng whole-K groups from group g) into dst.
+__device__ void issue_tile(const MkPart* Pp, const MkTile& T, uint8_t* dst, uint64_t* bar) {
+  const int kind = Pp->kind, nseg = Pp->nseg;
+  const size_t row_bytes = size_t(Pp->K / QK_K) * dev_block_bytes(Pp->dtype);
+  const uint32_t bytes = uint32_t(4u * T.ng * row_bytes);
+  mbar_expect_tx(bar, bytes);
+  if (kind == MK_GU) {
+    const uint32_t half = bytes / 2;
+    bulk_g2s(dst, Pp->w[0] + size_t(2 * T.g) * row_bytes, half, bar);
+    bulk_g2s(dst + half, Pp->w[1] + size_t(2 * T.g) * row_bytes, half, bar);
     return;
   }
-  if (whole) {
-    int r0 = 4 * T.g;
-    const int r1 = 4 * (T.g + T.ng);
-    int base = 0;
-    for (int sg = 0; sg < 3 && r0 < r1; ++sg) {
-      const int s1 = base + (sg < P.nseg ? P.rows[sg] : 0);
-      if (r0 < s1) {
-        const int e = min(r1, s1);
-        const uint32_t bytes = uint32_t(size_t(e - r0) * row_bytes);
-        bulk_g2s(dst, P.w[sg] + size_t(r0 - base) * row_bytes, bytes, bar);
-        dst += bytes;
-        r0 = e;
-      }
-      base = s1;
+  int r0 = 4 * T.g;
+  const int r1 = 4 * (T.g + T.ng);
+  int base = 0;
+  for (int sg = 0; sg < 3 && r0 < r1; ++sg) {
+    const int s1 = sg == 0 ? Pp->rows0 : sg == 1 && nseg > 1 ? base + Pp->rows1 : r1;
+    if (r0 < s1) {
+      const int e = min(r1, s1);
+      const uint32_t nb = uint32_t(size_t(e - r0) * row_bytes);
+      bulk_g2s(dst, Pp->w[sg] + size_t(r0 - base) * row_bytes, nb, bar);
+      dst += nb;
+      r0 = e;
     }
-    return;
-  }
-  for (int i = 0; i < 4; ++i)
-    bulk_g2s(dst + i * rb, part_row(P, 4 * T.g + i, row_bytes) + size_t(T.kb0) * bb, rb, bar);
-}
-
-// Bounded wait of consumer thread 0 for counter >= target; 0 on expiry.
-__device__ __forceinline__ int wait_counter(const int* c, int target) {
-  if (ld_acquire(c) >= target) return 1;
-  const long long t0 = clock64();
-  while (ld_acquire(c) < target) {
-    if (clock64() - t0 > MK_WAIT_CYCLES) return 0;
-  }
-  return 1;
-}
-
-// Consumer thread 0 publishes this CTA's share of a phase (after a consumer
-// barrier, so every consumer thread's writes are ordered before it).
-__device__ __forceinline__ void signal_counter(int* c) {
-  __threadfence();
-  atomicAdd(c, 1);
-}
-
-// Limb planes (M = 1) of the input vector x[K] of a GEMV phase, K <= MK_MAX_K
-// and a multiple of 256. With norm: RMSNorm first, as candle's rms_norm
-// (candle_tensor_backend.rs:30-57): m = sqrt(sum(x^2)/K + eps), x / m * w, IEEE
-// divide and square root. All loads are issued before any use (one L2 round
-// trip); cg selects ld.global.cg for vectors written inside this launch.
-__device__ void mk_planes(const float* x, bool cg, const float* norm, float eps, int K, const XPlanes& p,
-                          float* red) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float4 v[MK_RND][2], g[MK_RND][2];
-#pragma unroll
-  for (int r = 0; r < MK_RND; ++r) {
-    const int k = r * MK_CT * 8 + tid * 8;
-    v[r][0] = v[r][1] = g[r][0] = g[r][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (k < K) {
-      const float4* src = reinterpret_cast<const float4*>(x + k);
-      if (cg) {
-        v[r][0] = __ldcg(src);
-        v[r][1] = __ldcg(src + 1);
-      } else {
-        v[r][0] = __ldg(src);
-        v[r][1] = __ldg(src + 1);
-      }
-      if (norm) {
-        g[r][0] = __ldg(reinterpret_cast<const float4*>(norm + k));
-        g[r][1] = __ldg(reinterpret_cast<const float4*>(norm + k + 4));
-      }
-    }
-  }
-  float m = 1.0f;
-  if (norm) {
-    float ss = 0.0f;
-#pragma unroll
-    for (int r = 0; r < MK_RND; ++r)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        ss = __fadd_rn(ss, __fmul_rn(v[r][h].x, v[r][h].x));
-        ss = __fadd_rn(ss, __fmul_rn(v[r][h].y, v[r][h].y));
-        ss = __fadd_rn(ss, __fmul_rn(v[r][h].z, v[r][h].z));
-        ss = __fadd_rn(ss, __fmul_rn(v[r][h].w, v[r][h].w));
-      }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    cbar();
-    float tot = 0.0f;
-    for (int w = 0; w < MK_CW; ++w) tot = __fadd_rn(tot, red[w]);
-    m = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(K)), eps));
-  }
-#pragma unroll
-  for (int r = 0; r < MK_RND; ++r) {
-    const int k = r * MK_CT * 8 + tid * 8;
-    if (k < K) {  // whole warps are in or out (K is a multiple of 256)
-      float e[8] = {v[r][0].x, v[r][0].y, v[r][0].z, v[r][0].w, v[r][1].x, v[r][1].y, v[r][1].z, v[r][1].w};
-      if (norm) {
-        const float w8[8] = {g[r][0].x, g[r][0].y, g[r][0].z, g[r][0].w, g[r][1].x, g[r][1].y, g[r][1].z, g[r][1].w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) e[i] = __fmul_rn(__fdiv_rn(e[i], m), w8[i]);
-      }
-      quant8(e, size_t(k), k, p, K, 0);
-    }
-  }
-  cbar();
-}
-
-// K slices per group of a tile: enough units to occupy the consumer warps, at
-// least 32 chunks (one per lane) per slice.
-__device__ __forceinline__ int mk_ksplit(int ng, int nch) {
-  return max(1, min((MK_CW + ng - 1) / ng, nch / 32));
-}
-
-// Dot products of one tile: unit u = (group gl, K slice ks) per warp; lanes
-// stride over the 64-value chunks; warp sums land in part[u][row].
-template <int DT>
-__device__ void mk_tile_dots(const MkPart& P, const Tile& T, const uint8_t* sbase, const uint8_t* region,
-                             float* part) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int BB = DT == DT_Q4K ? Q4K_BYTES : Q6K_DEV_BYTES;
-  const int rb = T.nkb * BB;
-  const int nch = T.nkb * 4;
-  const int KS = mk_ksplit(T.ng, nch);
-  const int units = T.ng * KS;
-  XPlanes p = carve(const_cast<uint8_t*>(region), 1, P.K);
-  const int ko = T.kb0 * QK_K;  // first input element of the tile
-  p.l0 += ko;
-  p.l1 += ko;
-  p.l2 += ko;
-  p.scale += ko / 32;
-  p.sum32 += ko / 32;
-  XAddr xad;
-  xad.l[0] = smem_u32(p.l0);
-  xad.l[1] = smem_u32(p.l1);
-  xad.l[2] = smem_u32(p.l2);
-  xad.scale = smem_u32(p.scale);
-  xad.sum32 = smem_u32(p.sum32);
-  const uint32_t sb = smem_u32(sbase);
-  for (int u = warp; u < units; u += MK_CW) {
-    const int gl = u / KS, ks = u - gl * KS;
-    int ro[ROWS];
-#pragma unroll
-    for (int i = 0; i < ROWS; ++i)
-      ro[i] = P.kind == MK_GU ? (i < 2 ? 2 * gl + i : 2 * T.ng + 2 * gl + (i - 2)) : ROWS * gl + i;
-    float acc[ROWS][1];
-#pragma unroll
-    for (int i = 0; i < ROWS; ++i) acc[i][0] = 0.0f;
-    const int c0 = ks * nch / KS, c1 = (ks + 1) * nch / KS;
-    if (DT == DT_Q4K) {
-      uint32_t ra[ROWS];
-#pragma unroll
-      for (int i = 0; i < ROWS; ++i) ra[i] = sb + uint32_t(ro[i] * rb);
-      for (int c = c0 + lane; c < c1; c += 32) q4k_chunk_rows<1>(ra, c, P.K, xad, acc);
-    } else {
-      for (int c = c0 + lane; c < c1; c += 32) {
-#pragma unroll
-        for (int i = 0; i < ROWS; ++i) q6k_chunk_smem<1>(sbase + size_t(ro[i]) * rb, c, P.K, p, acc[i]);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < ROWS; ++i) {
-      const float v = warp_sum(acc[i][0]);
-      if (lane == i) part[u * 16 + i] = v;
-    }
+    base = s1;
   }
 }
 
-// Per-launch values every consumer thread keeps.
-struct MkCtx {
+// Per-launch values every thread keeps.
+struct Ctx {
+  uint32_t tag0;  // epoch * 1024 + 1: tag of phase p is tag0 + p
   int position, kv_len;
   const float* x0;  // layer-0 input: the embedding row of the step's token
+  int R0;           // first row of this CTA's o / down share (residual stash)
+  int rope_base;    // stash index of the current QKV part's first row
+  int g0;           // first group of this CTA in the current part
+  float rm;  // 1 / RMSNorm divisor of the current phase's input (1 without norm)
   unsigned long long best;
   int nan;
 };
 
-// Fixed-order sum of a tile's K slices and the fused epilogue; warp gl handles
-// group gl of the tile, lane i < 4 its row i.
-__device__ void mk_epilogue(const MkArgs& a, const MkPart& P, const Tile& T, const float* part, float* gacc,
-                            MkCtx& c) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nb = P.K / QK_K;
-  const int KS = mk_ksplit(T.ng, T.nkb * 4);
-  for (int gl = warp; gl < T.ng; gl += MK_CW) {
-    float v = 0.0f;
-    if (lane < ROWS)
-      for (int ks = 0; ks < KS; ++ks) v += part[(gl * KS + ks) * 16 + lane];
-    if (T.nkb < nb) {  // one group's K range over several tiles (then T.ng == 1, warp 0)
-      if (T.kb0 > 0 && lane < ROWS) v = gacc[lane] + v;
-      if (T.kb0 + T.nkb < nb) {
-        if (lane < ROWS) gacc[lane] = v;
-        continue;
-      }
-    }
-    const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
-    const float v2 = __shfl_down_sync(0xffffffffu, v, 2);
-    if (lane >= ROWS) continue;
-    const int i = lane, g = T.g + gl;
-    if (P.kind == MK_QKV) {
-      const int hid = a.hidden, hd = a.head_dim, kvd = a.n_kv * a.head_dim;
-      const int vr = P.row_offset + ROWS * g + i;
-      const size_t esz = a.kv_half ? 2 : 4;
-      uint8_t* kc = static_cast<uint8_t*>(a.kcache) + size_t(P.layer) * a.kv_layer_elems * esz;
-      uint8_t* vc = static_cast<uint8_t*>(a.vcache) + size_t(P.layer) * a.kv_layer_elems * esz;
-      if (vr < hid + kvd) {
-        if ((i & 1) == 0) {  // RoPE on (2j, 2j+1) pairs (attention.rs:230-262), table values
-          const int col = vr < hid ? vr : vr - hid;
-          const int pi = (col % hd) >> 1;
-          const float cs = __ldg(a.rope_cos + size_t(c.position) * (hd / 2) + pi);
-          const float sn = __ldg(a.rope_sin + size_t(c.position) * (hd / 2) + pi);
-          const float n0 = __fsub_rn(__fmul_rn(v, cs), __fmul_rn(v1, sn));
-          const float n1 = __fadd_rn(__fmul_rn(v, sn), __fmul_rn(v1, cs));
-          if (vr < hid) {
-            a.q[vr] = n0;
-            a.q[vr + 1] = n1;
+__device__ __forceinline__ float pick4(const float (&v)[ROWS], int i) {
+  return i == 0 ? v[0] : i == 1 ? v[1] : i == 2 ? v[2] : v[3];
+}
+
+// Fused epilogue of group g (all lanes hold the four row sums v[]; lane i < 4
+// handles row i). gi: stash index of the group's first row.
+__device__ __forceinline__ void group_epilogue(const MkArgs& a, const MkPart& P, int g, const float (&v)[ROWS],
+                                               Ctx& c, const MkSmem& sm) {
+  const int lane = threadIdx.x & 31;
+  if (lane >= ROWS) return;
+  const int i = lane;
+  const int gi = ROWS * (g - c.g0);
+  const float vi = pick4(v, i);
+  const uint32_t tag = c.tag0 + uint32_t(P.phase);
+  if (P.kind == MK_QKV) {
+    const int hid = a.hidden, hd = a.head_dim, kvd = a.n_kv * a.head_dim;
+    const int vr = P.row_offset + ROWS * g + i;
+    const size_t esz = a.kv_half ? 2 : 4;
+    if (vr < hid + kvd) {
+      if ((i & 1) == 0) {  // RoPE on (2j, 2j+1) pairs (attention.rs:230-262), table values
+        const float x0 = vi, x1 = pick4(v, i + 1);
+        const float cs = sm.rcos[c.rope_base + gi + i], sn = sm.rsin[c.rope_base + gi + i];
+        const float n0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        const float n1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        if (vr < hid) {
+          st_tag(a.q + vr, n0, tag);
+          st_tag(a.q + vr + 1, n1, tag);
+        } else {
+          const int col = vr - hid;
+          const size_t off = size_t(P.phase / 5) * a.kv_layer_elems + (size_t(col / hd) * a.max_seq + c.kv_len) * hd +
+                             col % hd;
+          if (a.kv_half) {
+            reinterpret_cast<__half*>(a.kcache)[off] = __float2half_rn(n0);
+            reinterpret_cast<__half*>(a.kcache)[off + 1] = __float2half_rn(n1);
           } else {
-            const size_t off = (size_t(col / hd) * a.max_seq + c.kv_len) * hd + col % hd;
-            if (a.kv_half) {
-              reinterpret_cast<__half*>(kc)[off] = __float2half_rn(n0);
-              reinterpret_cast<__half*>(kc)[off + 1] = __float2half_rn(n1);
-            } else {
-              reinterpret_cast<float*>(kc)[off] = n0;
-              reinterpret_cast<float*>(kc)[off + 1] = n1;
-            }
+            reinterpret_cast<float*>(a.kcache)[off] = n0;
+            reinterpret_cast<float*>(a.kcache)[off + 1] = n1;
           }
+          // attention reads this step's row through the tagged copy, rounded like the cache
+          const float k0 = a.kv_half ? __half2float(__float2half_rn(n0)) : n0;
+          const float k1 = a.kv_half ? __half2float(__float2half_rn(n1)) : n1;
+          st_tag(a.knew + col, k0, tag);
+          st_tag(a.knew + col + 1, k1, tag);
         }
+      }
+    } else {
+      const int col = vr - hid - kvd;
+      const size_t off = size_t(P.phase / 5) * a.kv_layer_elems + (size_t(col / hd) * a.max_seq + c.kv_len) * hd +
+                         col % hd;
+      float vv = vi;
+      if (a.kv_half) {
+        reinterpret_cast<__half*>(a.vcache)[off] = __float2half_rn(vv);
+        vv = __half2float(__float2half_rn(vv));
       } else {
-        const int col = vr - hid - kvd;
-        const size_t off = (size_t(col / hd) * a.max_seq + c.kv_len) * hd + col % hd;
-        if (a.kv_half) reinterpret_cast<__half*>(vc)[off] = __float2half_rn(v);
-        else reinterpret_cast<float*>(vc)[off] = v;
+        reinterpret_cast<float*>(a.vcache)[off] = vv;
       }
-    } else if (P.kind == MK_O) {  // attention out + residual (layer.rs:68)
-      const int r = ROWS * g + i;
-      const float res = P.layer == 0 ? __ldg(c.x0 + r) : __ldcg(a.xa + r);
-      a.xb[r] = __fadd_rn(res, v);
-    } else if (P.kind == MK_D) {  // FFN out + residual (layer.rs:86)
-      const int r = ROWS * g + i;
-      a.xa[r] = __fadd_rn(__ldcg(a.xb + r), v);
-    } else if (P.kind == MK_GU) {  // ffn.rs:90-94: silu(g) * u
-      if (i < 2) {
-        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
-        a.act[2 * g + i] = __fmul_rn(__fmul_rn(v, sig), v2);
+      st_tag(a.vnew + col, vv, tag);
+    }
+    (void)esz;
+  } else if (P.kind == MK_O) {  // attention out + residual (layer.rs:68)
+    const int r = ROWS * g + i;
+    st_tag(a.xb + r, __fadd_rn(sm.rsd[r - c.R0], vi), tag);
+  } else if (P.kind == MK_D) {  // FFN out + residual (layer.rs:86)
+    const int r = ROWS * g + i;
+    st_tag(a.xa + r, __fadd_rn(sm.rsd[r - c.R0], vi), tag);
+  } else if (P.kind == MK_GU) {  // ffn.rs:90-94: silu(g) * u
+    if (i < 2) {
+      const float gv = vi, uv = pick4(v, i + 2);
+      const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+      st_tag(a.act + 2 * g + i, __fmul_rn(__fmul_rn(gv, sig), uv), tag);
+    }
+  } else {  // MK_LM
+    const int n = ROWS * g + i;
+    a.logits[n] = vi;
+    if (a.gen_mode) {
+      float pv = vi;
+      if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
+        const uint32_t cnt = sm.pen[gi + i];
+        for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, a.rep) : __fmul_rn(pv, a.rep);
       }
-    } else {  // MK_LM
-      const int n = ROWS * g + i;
-      a.logits[n] = v;
-      if (a.gen_mode) {
-        float pv = v;
-        if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
-          const uint32_t cnt = a.pen_cnt[n];
-          for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, a.rep) : __fmul_rn(pv, a.rep);
-        }
-        if (pv != pv) c.nan = 1;
-        else {
-          const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
-          c.best = key > c.best ? key : c.best;
-        }
+      if (pv != pv) c.nan = 1;
+      else {
+        const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
+        c.best = key > c.best ? key : c.best;
       }
     }
   }
 }
 
-// Attention of one (KV head kh, key split) item of a decode step (T = 1) over
-// the layer's cache, the n_rep query heads of kh together (repeat_kv,
-// attention.rs:297-322): scores (q.k) * scale with the dot in key order and no
-// contraction, causal limit j <= position, softmax with a running max, P.V
-// (attention.rs:332-435). Keys of earlier steps are staged before the wait on
-// the QKV phase; this step's key (slot kv_len), q and v after it. With several
-// splits the last CTA of kh (ticket) merges the partials. Returns after the
-// item's output is published on the attention counter (or on abort).
+// Input planes of the phase starting at part pi (R rounds of MK_T * 8 values).
+// With P.norm the planes hold x * w and each warp leaves its share of sum(x^2)
+// in red[]: candle's rms_norm (candle_tensor_backend.rs:30-57), x / m * w with
+// m = sqrt(sum(x^2)/K + eps), is applied as W(x * w) / m after the dot
+// products, so quantisation does not wait for the reduction.
+// Also stages what the phase's epilogues read: the residual rows of this
+// CTA's o / down share, the RoPE cos / sin of its q / k rows and the penalty
+// counts of its LM-head rows. Ends with every thread's planes written (the
+// caller's barrier publishes them). Returns false when a wait expired.
+template <int R>
+__device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx& c, const MkSmem& sm, bool skip) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = P.K;
+  const Planes pl = planes_at(smem_u32(sm.region), K);
+  // staged epilogue inputs that do not depend on this phase's input
+  if (P.kind == MK_QKV) {
+    const int hid = a.hidden, hd = a.head_dim, kvd = a.n_kv * a.head_dim;
+    int base = 0;
+    for (int qi = pi; qi < a.nparts; ++qi) {
+      const MkPart* Q = sm.parts + qi;
+      if (Q->phase != P.phase) break;
+      int g0, g1;
+      cta_share(Q->ngroups, blockIdx.x, gridDim.x, g0, g1);
+      const int n = ROWS * (g1 - g0), ro = Q->row_offset + ROWS * g0;
+      for (int r = tid; r < n; r += MK_T) {
+        const int vr = ro + r;
+        float cs = 0.0f, sn = 0.0f;
+        if (vr < hid + kvd) {
+          const int col = vr < hid ? vr : vr - hid;
+          const size_t ti = size_t(c.position) * (hd / 2) + ((col % hd) >> 1);
+          cs = __ldg(a.rope_cos + ti);
+          sn = __ldg(a.rope_sin + ti);
+        }
+        sm.rcos[base + r] = cs;
+        sm.rsin[base + r] = sn;
+      }
+      base += n;
+    }
+  } else if (P.kind == MK_LM) {
+    int g0, g1;
+    cta_share(P.ngroups, blockIdx.x, gridDim.x, g0, g1);
+    for (int r = tid; r < ROWS * (g1 - g0); r += MK_T) sm.pen[r] = __ldg(a.pen_cnt + ROWS * g0 + r);
+  }
+  const unsigned long long* src = nullptr;
+  const float* plain = nullptr;
+  switch (P.kind) {
+    case MK_QKV:
+      if (P.dep < 0) plain = c.x0;
+      else src = a.xa;
+      break;
+    case MK_O: src = a.att; break;
+    case MK_GU: src = a.xb; break;
+    case MK_D: src = a.act; break;
+    default: src = a.xa; break;  // MK_LM
+  }
+  const bool stash = P.kind == MK_QKV || P.kind == MK_GU;  // residual of the o / down share
+  const int R1 = c.R0 + a.res_rows;
+  const uint32_t tag = c.tag0 + uint32_t(P.dep);
+  float v[R][8], w[R][8];
+  bool ok = true;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int k = r * MK_T * 8 + tid * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[r][e] = w[r][e] = 0.0f;
+    if (k < K) {
+      if (P.norm) {
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(P.norm + k));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(P.norm + k + 4));
+        w[r][0] = w0.x; w[r][1] = w0.y; w[r][2] = w0.z; w[r][3] = w0.w;
+        w[r][4] = w1.x; w[r][5] = w1.y; w[r][6] = w1.z; w[r][7] = w1.w;
+      }
+      if (plain) {
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(plain + k));
+        const float4 x1 = __ldg(reinterpret_cast<const float4*>(plain + k + 4));
+        v[r][0] = x0.x; v[r][1] = x0.y; v[r][2] = x0.z; v[r][3] = x0.w;
+        v[r][4] = x1.x; v[r][5] = x1.y; v[r][6] = x1.z; v[r][7] = x1.w;
+      } else {
+        ok &= poll_tagged<8>(src + k, tag, v[r], skip);
+      }
+      if (stash)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (k + e >= c.R0 && k + e < R1) sm.rsd[k + e - c.R0] = v[r][e];
+    }
+  }
+  if (P.norm) {  // this warp's share of sum(x^2), summed over the warps after the caller's barrier
+    float ss = 0.0f;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(v[r][e], v[r][e]));
+    ss = warp_sum(ss);
+    if (lane == 0) sm.red[warp] = ss;
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int k = r * MK_T * 8 + tid * 8;
+    if (k < K) {  // whole warps are in or out (K is a multiple of 256)
+      float e8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) e8[e] = P.norm ? __fmul_rn(v[r][e], w[r][e]) : v[r][e];
+      quant8_planes(e8, k, pl);
+    }
+  }
+  return ok;
+}
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ float kv_to_float(float v) { return v; }
+__device__ __forceinline__ float kv_to_float(__half v) { return __half2float(v); }
+template <typename KT>
+__device__ __forceinline__ KT float_to_kv(float v);
+template <>
+__device__ __forceinline__ float float_to_kv<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half float_to_kv<__half>(float v) { return __float2half_rn(v); }
+
+// Attention of one (KV head kh, key split) item (T = 1) over the layer's
+// cache, the n_rep query heads of kh together (repeat_kv, attention.rs:
+// 297-322): scores (q.k) * scale with the dot in key order and no contraction,
+// causal limit j <= position, softmax with a running max, P.V
+// (attention.rs:332-435). Keys of earlier steps are copied from the cache into
+// shared memory (cp.async, in the cache's element type) before this step's q
+// and new K / V row are polled. With several splits the last CTA of kh
+// (ticket) merges the partials and writes the tagged output.
 template <int HD, typename KT>
-__device__ void mk_attention(const MkArgs& a, const MkSmem& sm, const MkPart& P, int kh, int split, int nsplit,
-                             int chunk, int nkeys, const MkCtx& c, int& abort_) {
+__device__ __forceinline__ void mk_attention(const MkArgs& a, const MkSmem& sm, const MkPart& P, int kh, int split,
+                                             int nsplit, int chunk, int nkeys, const Ctx& c) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_rep = a.n_heads / a.n_kv;
-  constexpr int TS = MK_TS, KP = HD + 1;
+  constexpr int TS = MK_TS;
+  constexpr int KP = sizeof(KT) == 4 ? HD + 1 : HD + 2;  // K row pitch (elements): odd word stride
   float* qs = reinterpret_cast<float*>(sm.region);  // [n_rep][HD]
-  float* Ks = qs + n_rep * HD;                      // [TS][HD+1]
-  float* Vs = Ks + TS * KP;                         // [TS][HD]
-  float* S = Vs + TS * HD;                          // [n_rep][TS]
+  float* S = qs + n_rep * HD;                       // [n_rep][TS]
   float* ml = S + n_rep * TS;                       // [n_rep][2] running (max, sum)
   float* corr = ml + 2 * n_rep;                     // [n_rep]
   float* mm = corr + n_rep;                         // [n_rep][nsplit]
-  const size_t esz = a.kv_half ? 2 : 4;
-  const KT* Kp = reinterpret_cast<const KT*>(static_cast<const uint8_t*>(a.kcache) +
-                                             size_t(P.layer) * a.kv_layer_elems * esz) +
-                 size_t(kh) * a.max_seq * HD;
-  const KT* Vp = reinterpret_cast<const KT*>(static_cast<const uint8_t*>(a.vcache) +
-                                             size_t(P.layer) * a.kv_layer_elems * esz) +
-                 size_t(kh) * a.max_seq * HD;
+  KT* Ks = reinterpret_cast<KT*>(sm.region + 4 * ((n_rep * HD + n_rep * TS + 3 * n_rep + n_rep * a.max_splits + 3) / 4 * 4));
+  KT* Vs = Ks + TS * KP;                            // [TS][HD], 16-byte aligned rows
+  const size_t lofs = size_t(P.phase / 5) * a.kv_layer_elems + size_t(kh) * a.max_seq * HD;
+  const KT* Kp = reinterpret_cast<const KT*>(a.kcache) + lofs;
+  const KT* Vp = reinterpret_cast<const KT*>(a.vcache) + lofs;
   const int j0 = split * chunk, j1 = min(j0 + chunk, nkeys);
-  constexpr int PER = (TS * HD / 4 + MK_CT - 1) / MK_CT;  // float4 per thread per matrix and tile
-  // stages the rows of keys [max(t0, lo), min(t0 + nt, hi)) of the tile at t0
-  auto stage = [&](int t0, int nt, int lo, int hi) {
-    float4 kv[PER];
-#pragma unroll
-    for (int e = 0; e < PER; ++e) {
-      const int i = tid + e * MK_CT;
-      const int row = (i * 4) / HD, key = t0 + row;
-      if (i < TS * HD / 4 && row < nt && key >= lo && key < hi) kv[e] = ldcg_kv4<KT>(Kp + size_t(t0) * HD + size_t(i) * 4);
+  const int old_end = min(c.kv_len, j1);  // keys written by earlier steps
+  constexpr int KW = 4 / sizeof(KT);       // elements per 4-byte K copy
+  constexpr int VW = 16 / sizeof(KT);      // elements per 16-byte V copy
+  auto stage = [&](int t0, int nt) {  // rows [t0, min(t0 + nt, old_end)) of earlier steps
+    const int rows = min(nt, old_end - t0);
+    for (int i = tid; i < rows * (HD / KW); i += MK_T) {
+      const int row = i / (HD / KW), col = (i % (HD / KW)) * KW;
+      cp_async4(Ks + row * KP + col, Kp + size_t(t0 + row) * HD + col);
     }
-#pragma unroll
-    for (int e = 0; e < PER; ++e) {
-      const int i = tid + e * MK_CT;
-      const int row = (i * 4) / HD, col = (i * 4) % HD, key = t0 + row;
-      if (i < TS * HD / 4 && row < nt && key >= lo && key < hi) {
-        float* kr = Ks + row * KP + col;
-        kr[0] = kv[e].x;
-        kr[1] = kv[e].y;
-        kr[2] = kv[e].z;
-        kr[3] = kv[e].w;
-      }
+    for (int i = tid; i < rows * (HD / VW); i += MK_T) {
+      const int row = i / (HD / VW), col = (i % (HD / VW)) * VW;
+      cp_async16(Vs + row * HD + col, Vp + size_t(t0 + row) * HD + col);
     }
-#pragma unroll
-    for (int e = 0; e < PER; ++e) {
-      const int i = tid + e * MK_CT;
-      const int row = (i * 4) / HD, key = t0 + row;
-      if (i < TS * HD / 4 && row < nt && key >= lo && key < hi) kv[e] = ldcg_kv4<KT>(Vp + size_t(t0) * HD + size_t(i) * 4);
-    }
-#pragma unroll
-    for (int e = 0; e < PER; ++e) {
-      const int i = tid + e * MK_CT;
-      const int row = (i * 4) / HD, col = (i * 4) % HD, key = t0 + row;
-      if (i < TS * HD / 4 && row < nt && key >= lo && key < hi) *reinterpret_cast<float4*>(Vs + row * HD + col) = kv[e];
+  };
+  const uint32_t tag = c.tag0 + uint32_t(P.dep);
+  // this step's row (slot kv_len) of the tile at t0, from the tagged copies
+  auto stage_new = [&](int t0, int nt) {
+    const int row = c.kv_len - t0;
+    if (row < 0 || row >= nt || c.kv_len >= nkeys) return;
+    for (int d = 2 * tid; d < HD; d += 2 * MK_T) {
+      float kk[2], vv[2];
+      bool ok = poll_tagged<2>(a.knew + kh * HD + d, tag, kk, false);
+      ok &= poll_tagged<2>(a.vnew + kh * HD + d, tag, vv, false);
+      if (!ok) sm.flags[0] = 1;
+      Ks[row * KP + d] = float_to_kv<KT>(kk[0]);
+      Ks[row * KP + d + 1] = float_to_kv<KT>(kk[1]);
+      Vs[row * HD + d] = float_to_kv<KT>(vv[0]);
+      Vs[row * HD + d + 1] = float_to_kv<KT>(vv[1]);
     }
   };
   const int nt0 = min(TS, j1 - j0);
-  stage(j0, nt0, 0, c.kv_len);  // keys of earlier steps: independent of this step
-  if (tid == 0) {
-    if (!abort_ && !wait_counter(a.cnt + P.dep * 32, P.dep_target)) {
-      atomicOr(&a.st->err, 8);
-      sm.flags[0] = 1;
-    }
+  stage(j0, nt0);
+  for (int i = 2 * tid; i < n_rep * HD; i += 2 * MK_T) {
+    float qq[2];
+    if (!poll_tagged<2>(a.q + size_t(kh) * n_rep * HD + i, tag, qq, false)) sm.flags[0] = 1;
+    qs[i] = qq[0];
+    qs[i + 1] = qq[1];
   }
-  cbar();
-  abort_ = *reinterpret_cast<volatile int*>(sm.flags);
-  if (abort_) return;
-  for (int i = tid; i < n_rep * HD / 4; i += MK_CT)
-    reinterpret_cast<float4*>(qs)[i] = __ldcg(reinterpret_cast<const float4*>(a.q + size_t(kh) * n_rep * HD) + i);
-  for (int r = tid; r < n_rep; r += MK_CT) {
+  stage_new(j0, nt0);
+  for (int r = tid; r < n_rep; r += MK_T) {
     ml[2 * r] = -INFINITY;
     ml[2 * r + 1] = 0.0f;
   }
-  stage(j0, nt0, c.kv_len, nkeys);  // this step's key
-  constexpr int MAXI = (16 * HD + MK_CT - 1) / MK_CT;  // outputs per thread, n_rep <= 16
+  constexpr int MAXI = (16 * HD + MK_T - 1) / MK_T;  // outputs per thread, n_rep <= 16
   float acc[MAXI];
 #pragma unroll
   for (int k = 0; k < MAXI; ++k) acc[k] = 0.0f;
@@ -512,17 +772,19 @@ __device__ void mk_attention(const MkArgs& a, const MkSmem& sm, const MkPart& P,
     const int nt = min(TS, j1 - t0);
     if (t0 != j0) {
       cbar();
-      stage(t0, nt, 0, nkeys);
+      stage(t0, nt);
+      stage_new(t0, nt);
     }
+    cp_async_wait_all();
     cbar();
-    for (int r = warp; r < n_rep; r += MK_CW) {
+    for (int r = warp; r < n_rep; r += MK_W) {
       float sc = -INFINITY;
       if (lane < nt) {
         float d = 0.0f;
         const float* qr = qs + r * HD;
-        const float* kr = Ks + lane * KP;
-#pragma unroll 4
-        for (int dd = 0; dd < HD; ++dd) d = __fadd_rn(d, __fmul_rn(qr[dd], kr[dd]));
+        const KT* kr = Ks + lane * KP;
+#pragma unroll 8
+        for (int dd = 0; dd < HD; ++dd) d = __fadd_rn(d, __fmul_rn(qr[dd], kv_to_float(kr[dd])));
         sc = __fmul_rn(d, a.attn_scale);
       }
       const float m_old = ml[2 * r];
@@ -540,36 +802,33 @@ __device__ void mk_attention(const MkArgs& a, const MkSmem& sm, const MkPart& P,
     cbar();
 #pragma unroll
     for (int k = 0; k < MAXI; ++k) {
-      const int idx = tid + k * MK_CT;
+      const int idx = tid + k * MK_T;
       if (idx < n_rep * HD) {
         const int r = idx / HD, d = idx % HD;
         float s2 = acc[k] * corr[r];
-        for (int jj = 0; jj < nt; ++jj) s2 += S[r * TS + jj] * Vs[jj * HD + d];
+        for (int jj = 0; jj < nt; ++jj) s2 += S[r * TS + jj] * kv_to_float(Vs[jj * HD + d]);
         acc[k] = s2;
       }
     }
   }
-  cbar();
-  int* cnt = a.cnt + P.phase * 32;
+  const uint32_t otag = c.tag0 + uint32_t(P.phase);
   if (nsplit == 1) {
 #pragma unroll
     for (int k = 0; k < MAXI; ++k) {
-      const int idx = tid + k * MK_CT;
+      const int idx = tid + k * MK_T;
       if (idx < n_rep * HD) {
         const int r = idx / HD, d = idx % HD;
         const float l = ml[2 * r + 1];
-        a.att[size_t(kh * n_rep + r) * HD + d] = l > 0.0f ? acc[k] / l : 0.0f;
+        st_tag(a.att + size_t(kh * n_rep + r) * HD + d, l > 0.0f ? acc[k] / l : 0.0f, otag);
       }
     }
-    cbar();
-    if (tid == 0) signal_counter(cnt);
     return;
   }
   const size_t pstride = HD + 2;
   const size_t hstride = size_t(a.max_splits) * pstride;
 #pragma unroll
   for (int k = 0; k < MAXI; ++k) {
-    const int idx = tid + k * MK_CT;
+    const int idx = tid + k * MK_T;
     if (idx < n_rep * HD) {
       const int r = idx / HD, d = idx % HD;
       float* pp = a.part + size_t(kh * n_rep + r) * hstride + size_t(split) * pstride;
@@ -591,12 +850,12 @@ __device__ void mk_attention(const MkArgs& a, const MkSmem& sm, const MkPart& P,
   __threadfence();
   if (tid == 0) a.ticket[kh] = 0;
   const float* pbase = a.part + size_t(kh) * n_rep * hstride;
-  for (int i = tid; i < n_rep * nsplit; i += MK_CT) {
+  for (int i = tid; i < n_rep * nsplit; i += MK_T) {
     const int r = i / nsplit, sp = i % nsplit;
     mm[r * nsplit + sp] = __ldcg(pbase + r * hstride + sp * pstride);
   }
   cbar();
-  for (int r = warp; r < n_rep; r += MK_CW) {
+  for (int r = warp; r < n_rep; r += MK_W) {
     float M = -INFINITY;
     for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, mm[r * nsplit + sp]);
     M = warp_max(M);
@@ -610,7 +869,7 @@ __device__ void mk_attention(const MkArgs& a, const MkSmem& sm, const MkPart& P,
     if (lane == 0) ml[2 * r + 1] = L;
   }
   cbar();
-  for (int i = tid; i < n_rep * HD; i += MK_CT) {
+  for (int i = tid; i < n_rep * HD; i += MK_T) {
     const int r = i / HD, d = i % HD;
     const float* pp = pbase + r * hstride + 2 + d;
     float O = 0.0f;
@@ -623,15 +882,12 @@ __device__ void mk_attention(const MkArgs& a, const MkSmem& sm, const MkPart& P,
     }
     for (; sp < nsplit; ++sp) O += __ldcg(pp + sp * pstride) * mm[r * nsplit + sp];
     const float L = ml[2 * r + 1];
-    a.att[size_t(kh * n_rep + r) * HD + d] = L > 0.0f ? O / L : 0.0f;
+    st_tag(a.att + size_t(kh * n_rep + r) * HD + d, L > 0.0f ? O / L : 0.0f, otag);
   }
-  cbar();
-  if (tid == 0) signal_counter(cnt);
 }
 
 template <int HD>
-__device__ void mk_attention_phase(const MkArgs& a, const MkSmem& sm, const MkPart& P, const MkCtx& c,
-                                   int& abort_) {
+__device__ __forceinline__ void attention_phase(const MkArgs& a, const MkSmem& sm, const MkPart& P, const Ctx& c) {
   // split rule: at most max_splits pieces of a multiple of 32 keys, so that
   // n_kv * splits <= grid and every item has a CTA of its own
   const int nkeys = min(c.kv_len + 1, c.position + 1);
@@ -639,122 +895,158 @@ __device__ void mk_attention_phase(const MkArgs& a, const MkSmem& sm, const MkPa
   chunk = max(MK_TS, (chunk + MK_TS - 1) / MK_TS * MK_TS);
   const int nsplit = (nkeys + chunk - 1) / chunk;
   const int item = blockIdx.x;
-  if (item >= a.n_kv * nsplit || abort_) return;
+  if (item >= a.n_kv * nsplit) return;
   const int kh = item / nsplit, split = item - kh * nsplit;
-  if (a.kv_half) mk_attention<HD, __half>(a, sm, P, kh, split, nsplit, chunk, nkeys, c, abort_);
-  else mk_attention<HD, float>(a, sm, P, kh, split, nsplit, chunk, nkeys, c, abort_);
+  if (a.kv_half) mk_attention<HD, __half>(a, sm, P, kh, split, nsplit, chunk, nkeys, c);
+  else mk_attention<HD, float>(a, sm, P, kh, split, nsplit, chunk, nkeys, c);
 }
 
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const MkSmem sm = mk_carve(smem, a);
+  const MkSmem sm = mk_carve(a, smem);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cta = blockIdx.x;
   StepState* st = a.st;
   if (st->done) return;  // the generate loop has ended: every CTA returns at once
-  if (tid == 0) {
+  const int ntiles = __ldg(a.tile_start + size_t(cta) * (a.nparts + 1) + a.nparts);
+  const MkTile* gtiles = a.tiles + size_t(cta) * a.max_tiles;
+  if (tid == MK_T) {  // producer lane: barriers, then the first tiles straight from the global list
     for (int s = 0; s < a.nslots; ++s) {
       mbar_init(sm.full + s, 1);
-      mbar_init(sm.empty + s, MK_CW);
+      mbar_init(sm.empty + s, MK_W);
     }
     mbar_fence_init();
-    sm.flags[0] = 0;
-    sm.flags[1] = 0;
-  }
-  __syncthreads();
-
-  if (warp == MK_CW) {  // ---- producer: this CTA's weight tiles, in consumption order
-    if (lane != 0) return;
-    int i = 0;
-    for (int pi = 0; pi < a.nparts; ++pi) {
-      const MkPart P = a.parts[pi];
-      if (P.kind == MK_ATT) continue;
-      int g0, g1;
-      cta_share(P.ngroups, blockIdx.x, gridDim.x, g0, g1);
-      const int nt = tiles_of(P, g0, g1);
-      for (int t = 0; t < nt; ++t, ++i) {
-        const int s = i % a.nslots, use = i / a.nslots;
-        if (use > 0 && !mbar_wait(sm.empty + s, uint32_t((use - 1) & 1))) {
-          atomicOr(&st->err, 8);  // the consumers stopped taking tiles: stop issuing
-          return;
-        }
-        fence_proxy_async();
-        issue_tile(P, tile_at(P, g0, g1, t), sm.slots + size_t(s) * a.slot_bytes, sm.full + s);
-      }
+    for (int k = 0; k < a.nslots && k < ntiles; ++k) {
+      const MkTile T = gtiles[k];
+      issue_tile(a.parts + T.part, T, sm.slots + size_t(k) * a.slot_bytes, sm.full + k);
     }
-    return;
   }
-
-  // ---- consumers
-  MkCtx c;
+  for (int i = tid; i < ntiles; i += MK_THREADS) sm.tiles[i] = gtiles[i];
+  {
+    const int4* src = reinterpret_cast<const int4*>(a.parts);
+    int4* dst = reinterpret_cast<int4*>(sm.parts);
+    for (int i = tid; i < a.nparts * int(sizeof(MkPart) / 16); i += MK_THREADS) dst[i] = src[i];
+    for (int i = tid; i <= a.nparts; i += MK_THREADS)
+      sm.tstart[i] = a.tile_start[size_t(cta) * (a.nparts + 1) + i];
+  }
+  if (tid < 8) sm.flags[tid] = 0;
+  Ctx c;
+  c.tag0 = uint32_t(st->epoch) * 1024u + 1u;
   c.position = st->position;
   c.kv_len = st->kv_len;
   {
     const uint32_t tok = a.gen_mode ? a.hist[st->nhist - 1] : a.ids[0];
     c.x0 = tok < uint32_t(a.vocab) ? a.emb + size_t(tok) * a.hidden : a.zero;  // model.rs:847-864
+    int g0, g1;
+    cta_share(a.hidden / ROWS, cta, gridDim.x, g0, g1);
+    c.R0 = ROWS * g0;
   }
+  c.rope_base = 0;
+  c.g0 = 0;
+  c.rm = 1.0f;
   c.best = 0ull;
   c.nan = 0;
-  int abort_ = 0;
-  int i = 0, pp = 0;
-  for (int pi = 0; pi < a.nparts; ++pi) {
-    const MkPart P = a.parts[pi];
-    if (P.kind == MK_ATT) {
-      if (a.head_dim == 64) mk_attention_phase<64>(a, sm, P, c, abort_);
-      else mk_attention_phase<128>(a, sm, P, c, abort_);
-      continue;
+  __syncthreads();
+  if (warp == MK_W) {  // ---- producer: refill each slot once the consumer warps have left it
+    if (lane != 0) return;
+    for (int k = a.nslots; k < ntiles; ++k) {
+      const int s = k % a.nslots, use = k / a.nslots;
+      if (!mbar_wait_n(sm.empty + s, uint32_t((use - 1) & 1), MK_MBAR_POLLS)) {
+        atomicOr(&st->err, 4);  // the consumers stopped taking tiles
+        return;
+      }
+      fence_proxy_async();
+      const MkTile T = sm.tiles[k];
+      issue_tile(sm.parts + T.part, T, sm.slots + size_t(s) * a.slot_bytes, sm.full + s);
     }
-    if (P.first) {
-      if (P.dep >= 0) {
-        if (tid == 0 && !abort_ && !wait_counter(a.cnt + P.dep * 32, P.dep_target)) {
-          atomicOr(&st->err, 8);
-          sm.flags[0] = 1;
-        }
-        cbar();
-        abort_ = *reinterpret_cast<volatile int*>(sm.flags);
-      }
+    return;
+  }
+
+  bool abort_ = false;
+  int k = 0, U = 0;
+  for (int pi = 0; pi < a.nparts; ++pi) {
+    const MkPart& P = sm.parts[pi];
+    if (P.kind == MK_ATT) {
+      cbar();  // the QKV phase is done with the region
       if (!abort_) {
-        const float* in;
-        bool cg = true;
-        switch (P.kind) {
-          case MK_QKV: in = P.layer == 0 ? c.x0 : a.xa; cg = P.layer != 0; break;
-          case MK_O: in = a.att; break;
-          case MK_GU: in = a.xb; break;
-          case MK_D: in = a.act; break;
-          default: in = a.xa; break;  // MK_LM
-        }
-        mk_planes(in, cg, P.norm, P.eps, P.K, carve(sm.region, 1, P.K), sm.red);
+        if (a.head_dim == 64) attention_phase<64>(a, sm, P, c);
+        else attention_phase<128>(a, sm, P, c);
       }
+      continue;
     }
     int g0, g1;
-    cta_share(P.ngroups, blockIdx.x, gridDim.x, g0, g1);
-    const int nt = tiles_of(P, g0, g1);
-    for (int t = 0; t < nt; ++t, ++i) {
-      const int s = i % a.nslots, use = i / a.nslots;
-      const Tile T = tile_at(P, g0, g1, t);
-      float* part = sm.part + size_t(pp) * a.part_units * 16;
-      if (!mbar_wait(sm.full + s, uint32_t(use & 1))) {
-        atomicOr(&st->err, 4);
+    cta_share(P.ngroups, cta, gridDim.x, g0, g1);
+    c.g0 = g0;
+    if (P.first) {
+      cbar();  // the previous phase is done with the region and the stashes
+      c.rope_base = 0;
+      bool ok;
+      const int rounds = (P.K + MK_T * 8 - 1) / (MK_T * 8);
+      if (rounds <= 1) ok = build_input<1>(a, pi, P, c, sm, abort_);
+      else if (rounds == 2) ok = build_input<2>(a, pi, P, c, sm, abort_);
+      else if (rounds == 3) ok = build_input<3>(a, pi, P, c, sm, abort_);
+      else ok = build_input<4>(a, pi, P, c, sm, abort_);
+      if (!ok) {
         sm.flags[0] = 1;
+        atomicOr(&st->err, 8);
       }
-      if (!abort_) {
-        if (P.dtype == DT_Q4K) mk_tile_dots<DT_Q4K>(P, T, sm.slots + size_t(s) * a.slot_bytes, sm.region, part);
-        else mk_tile_dots<DT_Q6K>(P, T, sm.slots + size_t(s) * a.slot_bytes, sm.region, part);
+      cbar();
+      abort_ = *reinterpret_cast<volatile int*>(sm.flags) != 0;
+      U = 0;
+      if (P.norm) {
+        float tot = 0.0f;
+        for (int i = 0; i < MK_W; ++i) tot = __fadd_rn(tot, sm.red[i]);
+        c.rm = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(P.K)), P.eps)));
+      } else {
+        c.rm = 1.0f;
       }
+    }
+    const int NB = P.K / QK_K;
+    const uint32_t row_bytes = uint32_t(NB * dev_block_bytes(P.dtype));
+    const Planes pl = planes_at(smem_u32(sm.region), P.K);
+    const int kend = sm.tstart[pi + 1];
+    for (; k < kend; ++k) {
+      const MkTile T = sm.tiles[k];
+      const int s = k % a.nslots, use = k / a.nslots;
+      // every consumer warp waits for every tile and arrives on its slot
+      if (!mbar_wait_n(sm.full + s, uint32_t(use & 1), abort_ ? 4096u : MK_MBAR_POLLS)) {
+        if (!abort_ && lane == 0) atomicOr(&st->err, 4);
+        abort_ = true;
+      }
+      const uint32_t sbase = smem_u32(sm.slots + size_t(s) * a.slot_bytes);
+      // one group (4 rows, whole K) per warp; lane = (pair lane / 8, block lane % 8 + 8 j)
+      for (int u = (warp - U % MK_W + MK_W) % MK_W; u < T.ng; u += MK_W) {
+        float acc[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (!abort_) {
+          uint32_t ra[ROWS];
+#pragma unroll
+          for (int i = 0; i < ROWS; ++i) {
+            const int ro = P.kind == MK_GU ? (i < 2 ? 2 * u + i : 2 * T.ng + 2 * u + (i - 2)) : ROWS * u + i;
+            ra[i] = sbase + uint32_t(ro) * row_bytes;
+          }
+          if (P.dtype == DT_Q4K)
+            for (int b = lane & 7; b < NB; b += 8) q4k_unit(ra, b, lane >> 3, pl, acc);
+          else
+            for (int b = lane & 7; b < NB; b += 8) q6k_unit(ra, b, lane >> 3, pl, acc);
+        }
+        float v[ROWS];
+#pragma unroll
+        for (int i = 0; i < ROWS; ++i) v[i] = warp_sum(acc[i]);
+        if (P.norm)
+#pragma unroll
+          for (int i = 0; i < ROWS; ++i) v[i] = __fmul_rn(v[i], c.rm);
+        if (!abort_) group_epilogue(a, P, T.g + u, v, c, sm);
+      }
+      U += T.ng;
+      // leave the slot: the producer refills it with the tile nslots further on
       __syncwarp();
       if (lane == 0) mbar_arrive(sm.empty + s);
-      cbar();
-      abort_ = *reinterpret_cast<volatile int*>(sm.flags);
-      if (!abort_) mk_epilogue(a, P, T, part, sm.gacc, c);
-      pp ^= 1;
     }
-    if (!P.last) continue;
-    if (P.kind != MK_LM) {
-      cbar();
-      if (tid == 0) signal_counter(a.cnt + P.phase * 32);
-      continue;
-    }
-    // LM head: CTA max of the argmax keys, one atomic per CTA; the last CTA
-    // to finish runs the sampler bookkeeping and clears the phase counters
+    if (P.kind == MK_QKV) c.rope_base += ROWS * (g1 - g0);
+    if (P.kind != MK_LM) continue;
+    // LM head: CTA max of the argmax keys, one atomic per CTA; the last CTA to
+    // finish runs the sampler bookkeeping and advances the epoch
+    cbar();
     unsigned long long* rb = reinterpret_cast<unsigned long long*>(sm.red);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -764,23 +1056,21 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
     }
     if (lane == 0) {
       rb[warp] = c.best;
-      sm.flags[2 + (warp & 3)] = 0;
+      if (c.nan) atomicOr(sm.flags + 2, 1);
     }
     cbar();
-    if (lane == 0 && c.nan) atomicOr(sm.flags + 2, 1);
-    cbar();
     if (tid == 0) {
-      unsigned long long b = 0ull;
-      for (int w = 0; w < MK_CW; ++w) b = rb[w] > b ? rb[w] : b;
+      unsigned long long bmax = 0ull;
+      for (int i = 0; i < MK_W; ++i) bmax = rb[i] > bmax ? rb[i] : bmax;
       if (a.gen_mode) {
-        if (b) atomicMax(&st->best, b);
+        if (bmax) atomicMax(&st->best, bmax);
         if (sm.flags[2]) atomicOr(&st->nan, 1);
       }
       __threadfence();
       const int prev = atomicAdd(&st->ticket, 1);
       if (prev == int(gridDim.x) - 1) {
         __threadfence();
-        for (int ph = 0; ph < a.nphases; ++ph) a.cnt[ph * 32] = 0;
+        st->epoch += 1;
         if (a.gen_mode) finish_sample_state(st, a.hist, a.pen_cnt);
         else st->ticket = 0;
       }
@@ -813,50 +1103,87 @@ cudaError_t decode_step_configure() {
   return cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(g_mk_smem_max));
 }
 
-bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* smem) {
+bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std::vector<MkTile>& tiles,
+                      std::vector<int>& tile_start, size_t* smem) {
   if (g_mk_smem_max == 0) return false;
   if (n_rep > 16 || (a.head_dim != 64 && a.head_dim != 128)) return false;
-  int kmax = 0;
-  for (int i = 0; i < nparts; ++i)
-    if (parts[i].kind != MK_ATT) kmax = std::max(kmax, parts[i].K);
-  if (kmax > MK_MAX_K || kmax % QK_K) return false;
   const int grid = decode_step_grid();
-  a.max_splits = std::max(1, grid / a.n_kv);
-  const size_t att_floats = size_t(n_rep) * a.head_dim + size_t(MK_TS) * (a.head_dim + 1) +
-                            size_t(MK_TS) * a.head_dim + size_t(n_rep) * MK_TS + 3 * size_t(n_rep) +
-                            size_t(n_rep) * a.max_splits;
-  size_t region = std::max(gemv_planes_bytes(1, kmax), att_floats * sizeof(float));
-  region = (region + 127) / 128 * 128;
-  const int slot = 32 * 1024;
-  // tile shapes and the widest tile's unit count
-  int units = 1;
+  int kmax = 0;
+  size_t gmax = 0;
   for (int i = 0; i < nparts; ++i) {
-    MkPart& P = parts[i];
-    if (P.kind == MK_ATT) continue;
-    const int nb = P.K / QK_K;
-    const size_t bb = dev_block_bytes(P.dtype);
-    const size_t group = 4 * size_t(nb) * bb;
-    if (group <= size_t(slot)) {
-      P.gpt = int(slot / group);
-      P.kbt = nb;
-    } else {
-      P.gpt = 1;
-      P.kbt = int(slot / (4 * bb));
-    }
-    const int nch = P.kbt * 4;
-    for (int ng = 1; ng <= P.gpt; ++ng) {
-      const int ks = std::max(1, std::min((MK_CW + ng - 1) / ng, nch / 32));
-      units = std::max(units, ng * ks);
-    }
+    if (parts[i].kind == MK_ATT) continue;
+    if (parts[i].K % QK_K || parts[i].K > MK_MAX_K) return false;
+    kmax = std::max(kmax, parts[i].K);
+    gmax = std::max(gmax, 4 * size_t(parts[i].K / QK_K) * dev_block_bytes(parts[i].dtype));
   }
-  const size_t fixed = region + sizeof(float) * 2 * 16 * size_t(units) + sizeof(float) * (16 + 64) + 8 * sizeof(int);
-  if (fixed + 2 * (size_t(slot) + 16) > g_mk_smem_max) return false;
-  const int nslots = int(std::min<size_t>(8, (g_mk_smem_max - fixed) / (size_t(slot) + 16)));
-  a.slot_bytes = slot;
-  a.nslots = nslots;
+  a.max_splits = std::max(1, grid / a.n_kv);
+  // attention: q, scores, running max / sum, split weights (floats), then K (row pitch
+  // hd + 1 floats or hd + 2 halves) and V tiles in the cache's element type
+  const size_t att_floats = (size_t(n_rep) * a.head_dim + size_t(n_rep) * MK_TS + 3 * size_t(n_rep) +
+                             size_t(n_rep) * a.max_splits + 3) / 4 * 4;
+  const size_t att_bytes = att_floats * sizeof(float) + size_t(MK_TS) * (2 * a.head_dim + 1) * sizeof(float);
+  size_t region = std::max(planes_bytes(kmax), att_bytes);
+  region = (region + 127) / 128 * 128;
+  const size_t slot = std::max<size_t>(32 * 1024, (gmax + 1023) / 1024 * 1024);
+  // per-CTA tile lists and the sizes of the stashes
+  std::vector<int> gpt(nparts, 0);
+  for (int i = 0; i < nparts; ++i) {
+    if (parts[i].kind == MK_ATT) continue;
+    const size_t group = 4 * size_t(parts[i].K / QK_K) * dev_block_bytes(parts[i].dtype);
+    gpt[i] = int(std::min<size_t>(MK_GPT, slot / group));
+  }
+  tile_start.assign(size_t(grid) * (nparts + 1), 0);
+  std::vector<std::vector<MkTile>> per(grid);
+  int max_tiles = 0, res_rows = 0, rope_rows = 0, lm_rows = 0;
+  for (int c = 0; c < grid; ++c) {
+    int rope = 0, rope_phase = -1;
+    for (int i = 0; i < nparts; ++i) {
+      tile_start[size_t(c) * (nparts + 1) + i] = int(per[c].size());
+      const MkPart& P = parts[i];
+      if (P.kind == MK_ATT) continue;
+      int g0, g1;
+      cta_share(P.ngroups, c, grid, g0, g1);
+      for (int g = g0; g < g1; g += gpt[i]) {
+        MkTile t{};
+        t.g = uint16_t(g);
+        t.part = uint16_t(i);
+        t.ng = uint8_t(std::min(gpt[i], g1 - g));
+        per[c].push_back(t);
+      }
+      const int rows = ROWS * (g1 - g0);
+      if (P.kind == MK_QKV) {
+        if (P.phase != rope_phase) rope = 0;
+        rope_phase = P.phase;
+        rope += rows;
+        rope_rows = std::max(rope_rows, rope);
+      }
+      if (P.kind == MK_O || P.kind == MK_D) res_rows = std::max(res_rows, rows);
+      if (P.kind == MK_LM) lm_rows = std::max(lm_rows, rows);
+    }
+    tile_start[size_t(c) * (nparts + 1) + nparts] = int(per[c].size());
+    max_tiles = std::max(max_tiles, int(per[c].size()));
+  }
+  if (max_tiles > MK_MAX_TILES || nparts > 65535) return false;
+  for (int i = 0; i < nparts; ++i)
+    if (parts[i].ngroups > 65535) return false;
+  tiles.assign(size_t(grid) * max_tiles, MkTile{});
+  for (int c = 0; c < grid; ++c)
+    std::copy(per[c].begin(), per[c].end(), tiles.begin() + size_t(c) * max_tiles);
+  a.nparts = nparts;
+  a.max_tiles = max_tiles;
+  a.slot_bytes = int(slot);
   a.region_bytes = int(region);
-  a.part_units = units;
-  *smem = size_t(nslots) * slot + fixed + 16 * size_t(nslots);
+  a.kmax = kmax;
+  a.res_rows = std::max(res_rows, 4);
+  a.rope_rows = std::max(rope_rows, 4);
+  a.lm_rows = std::max(lm_rows, 4);
+  a.nslots = 1;
+  const size_t fixed = mk_offsets(a).total - slot;
+  if (fixed + 3 * slot > g_mk_smem_max) return false;
+  a.nslots = int(std::min<size_t>(8, (g_mk_smem_max - fixed) / (slot + 16)));
+  while (a.nslots > 2 && mk_offsets(a).total > g_mk_smem_max) --a.nslots;
+  *smem = mk_offsets(a).total;
+  if (*smem > g_mk_smem_max) return false;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, MK_THREADS, *smem) != cudaSuccess ||
       per_sm < 1)

@@ -12,6 +12,8 @@
 #pragma once
 #include <cstddef>
 #include <cstdint>
+#include <vector>
+
 #include <cuda_runtime.h>
 
 namespace wcb {
@@ -45,7 +47,8 @@ struct StepState {
   int max_seq;   // KV capacity
   int ticket;    // LM-head CTAs finished (the last one runs the sampler bookkeeping)
   int nan;       // a penalised logit was NaN
-  int pad[2];
+  int epoch;     // persistent decode step: launches so far (tags of this launch's activations)
+  int pad;
 };
 static_assert(sizeof(StepState) == 64, "StepState layout");
 
@@ -141,44 +144,55 @@ constexpr int ATT_TILE = 32;  // keys staged in shared memory per pass
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 
 // ------------------------------------------------ persistent decode step --
-// One launch runs a whole greedy decode step (T = 1): every layer's QKV + RoPE
-// + KV append, attention, output projection + residual, gate/up + SwiGLU,
-// down + residual, then the final norm, LM head, penalty, argmax and
-// generate()'s bookkeeping. One CTA per SM (cooperative launch, so all CTAs
-// are resident). A producer warp streams this CTA's share of every weight
-// matrix, phase after phase, through a ring of shared-memory slots with bulk
-// copies, independent of the activations; consumer warps wait only for the
-// activations of each phase, on a per-phase counter that every CTA bumps when
-// its share of the phase is written.
+// One launch runs a whole decode step (T = 1): every layer's QKV + RoPE + KV
+// append, attention, output projection + residual, gate/up + SwiGLU, down +
+// residual, then the final norm, LM head and, in generate mode, penalty,
+// argmax and generate()'s bookkeeping. One CTA per SM (cooperative launch,
+// so all CTAs are resident). Each CTA owns a fixed share of every weight
+// matrix; its weight tiles stream through a ring of shared-memory slots with
+// bulk copies that run ahead across phases (weights do not depend on the
+// activations). Activations that cross CTAs are (value, tag) pairs written
+// with one 64-bit store: a consumer spins on the elements it reads until they
+// carry the tag of the producing phase of this step, so no counters, fences
+// or grid barriers sit between phases.
 enum MkKind { MK_QKV = 0, MK_ATT = 1, MK_O = 2, MK_GU = 3, MK_D = 4, MK_LM = 5 };
 
 // One weight "part" of a phase: rows of one quantisation type, processed in
-// groups of 4 rows (MK_GU: 2 gate + 2 up rows, giving 2 outputs).
+// groups of 4 rows (MK_GU: 2 gate + 2 up rows, giving 2 outputs). 64 bytes:
+// a launch keeps the whole list in shared memory. Phases are numbered 5 per
+// layer (QKV, attention, o, gate/up, down) and then the LM head, so a part's
+// layer is phase / 5.
 struct MkPart {
   const uint8_t* w[3];  // MK_QKV: segments of the virtual [q; k; v] matrix; MK_GU: gate, up; else w[0]
-  int rows[3];          // rows of each segment
-  int nseg;
-  int kind;             // MkKind
-  int layer;
-  int dtype;            // DT_Q4K / DT_Q6K (MK_ATT: unused)
+  const float* norm;    // RMSNorm weight of the phase input (null: none)
+  int rows0, rows1;     // rows of segments 0 and 1 (segment 2 holds the rest)
   int K;                // input length
   int ngroups;
   int row_offset;       // MK_QKV: row of the virtual matrix at this part's row 0
-  int gpt;              // groups per tile (whole-K tiles)
-  int kbt;              // k-blocks per tile (K/256 unless the tile holds one group's K range)
-  int first, last;      // first / last part of its phase
-  int phase;            // phase index (its counter)
-  int dep;              // phase whose counter this phase waits on (-1: none)
-  int dep_target;       // counter value that releases it
-  const float* norm;    // RMSNorm weight of the phase input (null: none)
   float eps;
+  int16_t phase;        // phase index (tags of its outputs)
+  int16_t dep;          // phase whose outputs this phase reads (-1: the embedding row)
+  uint8_t kind;         // MkKind
+  uint8_t first;        // first part of its phase (builds the input planes)
+  uint8_t dtype;        // DT_Q4K / DT_Q6K (MK_ATT: unused)
+  uint8_t nseg;
+};
+static_assert(sizeof(MkPart) == 64, "MkPart layout");
+
+// A tile: ng groups starting at group g of part `part` (whole K rows).
+struct MkTile {
+  uint16_t g;
+  uint16_t part;
+  uint8_t ng;
+  uint8_t pad[3];
 };
 
 struct MkArgs {
   const MkPart* parts;
   int nparts;
-  int nphases;
-  int* cnt;  // [nphases][32] phase counters (128-byte stride), zero between launches
+  const MkTile* tiles;     // [grid][max_tiles] each CTA's tiles in consumption order
+  const int* tile_start;   // [grid][nparts + 1] first tile of each part
+  int max_tiles;
   StepState* st;
   const float* emb;
   int vocab, hidden, ffn, n_heads, n_kv, head_dim, max_seq;
@@ -189,27 +203,35 @@ struct MkArgs {
   size_t kv_layer_elems;
   int kv_half;
   float attn_scale;
-  float* xa;            // residual stream between layers
-  float* xb;            // residual stream after attention
-  float* q;             // post-RoPE queries [hidden]
-  float* att;           // attention output [hidden]
-  float* act;           // SwiGLU output [ffn]
-  float* logits;        // [vocab]
-  const float* zero;    // [hidden] zeros (embedding of an out-of-vocabulary id)
-  float* part;          // attention split partials [n_heads][max_splits][hd + 2]
-  int* ticket;          // [n_kv], zero between launches
+  // tagged activations: (float bits, tag) in one 64-bit word
+  unsigned long long* xa;    // residual stream between layers [hidden]
+  unsigned long long* xb;    // residual stream after attention [hidden]
+  unsigned long long* q;     // post-RoPE queries [hidden]
+  unsigned long long* knew;  // this step's K / V rows [n_kv * head_dim]
+  unsigned long long* vnew;
+  unsigned long long* att;   // attention output [hidden]
+  unsigned long long* act;   // SwiGLU output [ffn]
+  float* logits;             // [vocab]
+  const float* zero;         // [hidden] zeros: the embedding of an out-of-vocabulary id
+  float* part;               // attention split partials [n_heads][max_splits][hd + 2]
+  int* ticket;               // [n_kv], zero between launches
   int max_splits;
-  int gen_mode;         // 1: token = hist[nhist - 1], penalty + argmax + bookkeeping
-  const uint32_t* ids;  // gen_mode 0: token = ids[0]
+  int gen_mode;              // 1: token = hist[nhist - 1], penalty + argmax + bookkeeping
+  const uint32_t* ids;       // gen_mode 0: token = ids[0]
   uint32_t* hist;
   uint32_t* pen_cnt;
   float rep;
   // shared-memory layout (from decode_step_plan)
-  int slot_bytes, nslots, region_bytes, part_units;
+  int slot_bytes, nslots, region_bytes, kmax;
+  int rope_rows;  // QKV rows of one layer a CTA owns (all QKV parts)
+  int res_rows;   // rows of an O / D share
+  int lm_rows;    // LM-head rows a CTA owns
 };
-// Fills the tile sizes of the parts and the shared-memory layout; false when
-// the model does not fit the persistent kernel (then the per-op kernels run).
-bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* smem);
+// Fills the tile lists and the shared-memory layout; false when the model
+// does not fit the persistent kernel (then the per-op kernels run).
+// tiles / tile_start receive the host copies of the tables.
+bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std::vector<MkTile>& tiles,
+                      std::vector<int>& tile_start, size_t* smem);
 int decode_step_grid();  // CTAs of one launch (one per SM)
 cudaError_t decode_step_configure();
 cudaError_t launch_decode_step(const MkArgs& a, size_t smem, cudaStream_t s);

@@ -486,7 +486,6 @@ void Model::build_decode_step() {
   }
   const ModelConfig& c = cfg_;
   const int H = int(c.hidden), F = int(c.ffn);
-  const int grid = decode_step_grid();
   std::vector<MkPart> parts;
   int phase = 0, prev_d = -1;
   for (uint32_t l = 0; l < c.layers; ++l) {
@@ -500,55 +499,49 @@ void Model::build_decode_step() {
       while (s1 < 3 && segs[s1]->dtype == segs[s0]->dtype) ++s1;
       MkPart P{};
       P.kind = MK_QKV;
-      P.layer = int(l);
-      P.dtype = segs[s0]->dtype;
+      P.dtype = uint8_t(segs[s0]->dtype);
       P.K = H;
       int rows = 0;
       for (int i = s0; i < s1; ++i) {
         P.w[i - s0] = segs[i]->ptr;
-        P.rows[i - s0] = int(segs[i]->rows);
+        if (i - s0 == 0) P.rows0 = int(segs[i]->rows);
+        if (i - s0 == 1) P.rows1 = int(segs[i]->rows);
         rows += int(segs[i]->rows);
       }
-      P.nseg = s1 - s0;
+      P.nseg = uint8_t(s1 - s0);
       P.ngroups = rows / 4;
       P.row_offset = row_off;
       row_off += rows;
-      P.phase = p_qkv;
-      P.dep = prev_d;
-      P.dep_target = grid;
+      P.phase = int16_t(p_qkv);
+      P.dep = int16_t(prev_d);
       P.norm = L.attn_norm;
       P.eps = 1e-6f;
       parts.push_back(P);
       s0 = s1;
     }
     parts[first].first = 1;
-    parts.back().last = 1;
     const int p_att = phase++;
     {
       MkPart P{};
       P.kind = MK_ATT;
-      P.layer = int(l);
-      P.phase = p_att;
-      P.dep = p_qkv;
-      P.dep_target = grid;
-      P.first = P.last = 1;
+      P.phase = int16_t(p_att);
+      P.dep = int16_t(p_qkv);
+      P.first = 1;
       parts.push_back(P);
     }
     const int p_o = phase++;
     {
       MkPart P{};
       P.kind = MK_O;
-      P.layer = int(l);
-      P.dtype = L.o.dtype;
+      P.dtype = uint8_t(L.o.dtype);
       P.K = H;
       P.w[0] = L.o.ptr;
-      P.rows[0] = int(L.o.rows);
+      P.rows0 = int(L.o.rows);
       P.nseg = 1;
       P.ngroups = int(L.o.rows) / 4;
-      P.phase = p_o;
-      P.dep = p_att;
-      P.dep_target = int(c.kv_heads);  // one signal per merged KV head
-      P.first = P.last = 1;
+      P.phase = int16_t(p_o);
+      P.dep = int16_t(p_att);
+      P.first = 1;
       parts.push_back(P);
     }
     if (L.gate.dtype != L.up.dtype) return;  // gate/up rows are paired inside one tile
@@ -556,38 +549,34 @@ void Model::build_decode_step() {
     {
       MkPart P{};
       P.kind = MK_GU;
-      P.layer = int(l);
-      P.dtype = L.gate.dtype;
+      P.dtype = uint8_t(L.gate.dtype);
       P.K = H;
       P.w[0] = L.gate.ptr;
       P.w[1] = L.up.ptr;
-      P.rows[0] = int(L.gate.rows);
-      P.rows[1] = int(L.up.rows);
+      P.rows0 = int(L.gate.rows);
+      P.rows1 = int(L.up.rows);
       P.nseg = 2;
       P.ngroups = int(L.gate.rows) / 2;
-      P.phase = p_gu;
-      P.dep = p_o;
-      P.dep_target = grid;
+      P.phase = int16_t(p_gu);
+      P.dep = int16_t(p_o);
       P.norm = L.ffn_norm;
       P.eps = 1e-6f;
-      P.first = P.last = 1;
+      P.first = 1;
       parts.push_back(P);
     }
     const int p_d = phase++;
     {
       MkPart P{};
       P.kind = MK_D;
-      P.layer = int(l);
-      P.dtype = L.down.dtype;
+      P.dtype = uint8_t(L.down.dtype);
       P.K = F;
       P.w[0] = L.down.ptr;
-      P.rows[0] = int(L.down.rows);
+      P.rows0 = int(L.down.rows);
       P.nseg = 1;
       P.ngroups = int(L.down.rows) / 4;
-      P.phase = p_d;
-      P.dep = p_gu;
-      P.dep_target = grid;
-      P.first = P.last = 1;
+      P.phase = int16_t(p_d);
+      P.dep = int16_t(p_gu);
+      P.first = 1;
       parts.push_back(P);
     }
     prev_d = p_d;
@@ -595,37 +584,41 @@ void Model::build_decode_step() {
   {
     MkPart P{};
     P.kind = MK_LM;
-    P.layer = int(c.layers);
-    P.dtype = lm_head_.dtype;
+    P.dtype = uint8_t(lm_head_.dtype);
     P.K = H;
     P.w[0] = lm_head_.ptr;
-    P.rows[0] = int(lm_head_.rows);
+    P.rows0 = int(lm_head_.rows);
     P.nseg = 1;
     P.ngroups = int(lm_head_.rows) / 4;
-    P.phase = phase++;
-    P.dep = prev_d;
-    P.dep_target = grid;
+    P.phase = int16_t(phase++);
+    P.dep = int16_t(prev_d);
     P.norm = out_norm_;
     P.eps = c.eps;
-    P.first = P.last = 1;
+    P.first = 1;
     parts.push_back(P);
   }
+  if (phase > 1023) return;  // tags hold the phase in 10 bits
   MkArgs a{};
-  a.nparts = int(parts.size());
-  a.nphases = phase;
   a.n_kv = int(c.kv_heads);
   a.n_heads = int(c.heads);
   a.head_dim = int(c.head_dim());
-  if (!decode_step_plan(parts.data(), a.nparts, a, int(c.heads / c.kv_heads), &mk_smem_)) return;
-  MkPart* dparts = static_cast<MkPart*>(dalloc(sizeof(MkPart) * parts.size()));
-  check(cudaMemcpy(dparts, parts.data(), sizeof(MkPart) * parts.size(), cudaMemcpyHostToDevice), "upload step plan");
-  a.parts = dparts;
-  a.cnt = static_cast<int*>(dalloc(sizeof(int) * 32 * size_t(phase)));
-  check(cudaMemset(a.cnt, 0, sizeof(int) * 32 * size_t(phase)), "clear counters");
+  a.hidden = H;
+  std::vector<MkTile> tiles;
+  std::vector<int> tile_start;
+  if (!decode_step_plan(parts.data(), int(parts.size()), a, int(c.heads / c.kv_heads), tiles, tile_start,
+                        &mk_smem_))
+    return;
+  auto upload = [&](const void* src, size_t bytes) {
+    void* d = dalloc(bytes);
+    check(cudaMemcpy(d, src, bytes, cudaMemcpyHostToDevice), "upload step plan");
+    return d;
+  };
+  a.parts = static_cast<const MkPart*>(upload(parts.data(), sizeof(MkPart) * parts.size()));
+  a.tiles = static_cast<const MkTile*>(upload(tiles.data(), sizeof(MkTile) * tiles.size()));
+  a.tile_start = static_cast<const int*>(upload(tile_start.data(), sizeof(int) * tile_start.size()));
   a.st = st_;
   a.emb = emb_;
   a.vocab = int(c.vocab);
-  a.hidden = H;
   a.ffn = F;
   a.max_seq = int(max_seq_);
   a.kcache = kcache_;
@@ -633,11 +626,19 @@ void Model::build_decode_step() {
   a.kv_layer_elems = kv_layer_elems_;
   a.kv_half = int(opt_.kv_half);
   a.attn_scale = attn_scale_;
-  a.xa = x_;
-  a.xb = h_;
-  a.q = q_;
-  a.att = att_;
-  a.act = act_;
+  const size_t kvd = size_t(c.kv_heads) * c.head_dim();
+  const size_t tagged = 4 * size_t(H) + size_t(F) + 2 * kvd;  // xa, xb, q, att, act, knew, vnew
+  unsigned long long* t = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * tagged));
+  check(cudaMemset(t, 0, sizeof(unsigned long long) * tagged), "clear activations");
+  mk_tagged_ = t;
+  mk_tagged_n_ = tagged;
+  a.xa = t;
+  a.xb = a.xa + H;
+  a.q = a.xb + H;
+  a.att = a.q + H;
+  a.act = a.att + H;
+  a.knew = a.act + F;
+  a.vnew = a.knew + kvd;
   a.logits = logits_;
   float* zero = static_cast<float*>(dalloc(sizeof(float) * H));
   check(cudaMemset(zero, 0, sizeof(float) * H), "clear zero row");
@@ -654,6 +655,13 @@ void Model::build_decode_step() {
 }
 
 void Model::launch_decode_step_kernel(bool gen) {
+  if (++mk_launches_ >= (1u << 21)) {
+    // tags are epoch * 1024 + phase + 1 in 32 bits: restart the epochs well
+    // before they wrap (no launch is in flight after these stream-ordered clears)
+    check(cudaMemsetAsync(mk_tagged_, 0, sizeof(unsigned long long) * mk_tagged_n_, stream_), "clear activations");
+    check(cudaMemsetAsync(&st_->epoch, 0, sizeof(int), stream_), "clear epoch");
+    mk_launches_ = 0;
+  }
   MkArgs a = mk_;
   a.rope_cos = rope_cos_;
   a.rope_sin = rope_sin_;
@@ -745,8 +753,7 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
   enqueue_lm_head(last_T, true);  // samples the first token (no EOS check)
   if (mk_ok_) {
-    // counters of a step that ended on an error are cleared here
-    check(cudaMemsetAsync(mk_.cnt, 0, sizeof(int) * 32 * size_t(mk_.nphases), stream_), "clear counters");
+    // tickets of a step that ended on an error are cleared here
     check(cudaMemsetAsync(mk_.ticket, 0, sizeof(int) * size_t(mk_.n_kv), stream_), "clear tickets");
     launches_per_step_ = 1;
   } else if (!(opt_.flags & 1) && (!decode_exec_ || graph_rep_ != rep)) {

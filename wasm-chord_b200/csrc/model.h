@@ -151,6 +151,9 @@ class Model {
   bool mk_ok_ = false;
   MkArgs mk_{};
   size_t mk_smem_ = 0;
+  unsigned long long* mk_tagged_ = nullptr;  // tagged activation buffers (one allocation)
+  size_t mk_tagged_n_ = 0;
+  uint32_t mk_launches_ = 0;
 
   cudaGraphExec_t decode_exec_ = nullptr;
   cudaGraph_t decode_graph_ = nullptr;
