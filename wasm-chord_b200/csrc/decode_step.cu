@@ -44,7 +44,7 @@ constexpr int MK_TS = 32;           // keys per attention tile
 constexpr int MK_MAX_TILES = 2048;  // tiles of one CTA per step (list kept in shared memory)
 constexpr int MK_GPT = 32;          // most groups in one tile
 constexpr long long MK_WAIT_NS = 2000000000ll;  // bound of every spin wait (2 s)
-constexpr uint32_t MK_MBAR_POLLS = 1u << 22;
+constexpr uint32_t MK_MBAR_POLLS = 1u << 21;  // ~1 us suspends: about 2 s in all
 
 // barrier of the consumer warps (the producer warp never joins it)
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(MK_T) : "memory"); }
@@ -111,14 +111,18 @@ __device__ __forceinline__ float4 ldcg_kv4<__half>(const __half* p) {
   return make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
+// Bounded wait for one phase of an mbarrier. Each try_wait suspends the
+// thread until the phase completes or about a microsecond passes (time hint),
+// so waiting warps (the producer most of all) do not take issue slots from
+// the computing ones.
 __device__ __forceinline__ bool mbar_wait_n(uint64_t* bar, uint32_t parity, uint32_t polls) {
   const uint32_t addr = smem_u32(bar);
   for (uint32_t it = 0; it < polls; ++it) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(addr), "r"(parity)
+        : "r"(addr), "r"(parity), "n"(1000)
         : "memory");
     if (ok) return true;
   }
