@@ -53,6 +53,15 @@ typedef struct wcb_load_opts {
   uint32_t flags;     /* bit 0: no CUDA graphs for decode steps; bit 1: no programmatic
                          dependent launch; bit 2: no tensor-core GEMM for prefill (GEMV only);
                          bit 3: no persistent decode-step kernel (one launch per op instead) */
+  /* Tensor parallelism (one process per GPU; no counterpart in the reference, whose
+     sharding.rs is bookkeeping only). tp_size 0 or 1: the whole model on `device`.
+     tp_size > 1: this process holds rank tp_rank's shard (query/KV heads, o and down
+     input columns, gate/up rows, LM-head vocabulary rows) and joins the NCCL group
+     named by tp_id (from wcb_tp_id on one rank, shared by the caller); all ranks
+     must make the same calls in the same order. */
+  uint32_t tp_rank;
+  uint32_t tp_size;
+  uint8_t tp_id[128];
 } wcb_load_opts;
 
 /* TransformerConfig — transformer/config.rs:6-41 (plus head_dim) */
@@ -152,6 +161,11 @@ size_t wcb_last_error(char* buf, size_t len);
 
 /* Library version string (wasmchord_version, abi.rs:225-228). */
 const char* wcb_version(void);
+
+/* A fresh tensor-parallel group id (ncclGetUniqueId) for wcb_load_opts.tp_id:
+ * one rank creates it and the caller hands the same 128 bytes to every rank.
+ * No counterpart in the reference. */
+uint32_t wcb_tp_id(uint8_t out[128]);
 
 /* ---- kernel-level entry points (device pointers, caller's stream) ----------
  * No counterpart in the reference's public API: they expose the hot kernels

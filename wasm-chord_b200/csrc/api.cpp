@@ -16,6 +16,7 @@
 #include "gguf.h"
 #include "kernels.h"
 #include "model.h"
+#include "nccl_rt.h"
 #include "sampler.h"
 
 namespace {
@@ -110,6 +111,11 @@ uint32_t wcb_model_load(const char* path, const wcb_load_opts* opts, uint32_t* o
       o.kv_half = opts->kv_dtype == WCB_KV_F16;
       o.max_batch = opts->max_batch ? opts->max_batch : 1;
       o.flags = opts->flags;
+      o.tp_rank = opts->tp_rank;
+      o.tp_size = opts->tp_size ? opts->tp_size : 1;
+      if (o.tp_size > 8 || o.tp_rank >= o.tp_size)
+        return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: tp_rank / tp_size");
+      std::memcpy(o.tp_id, opts->tp_id, sizeof(o.tp_id));
     }
     auto m = std::make_shared<wcb::Model>(path, o);
     std::lock_guard<std::mutex> lk(g_mu);
@@ -318,6 +324,19 @@ size_t wcb_last_error(char* buf, size_t len) {
 }
 
 const char* wcb_version(void) { return "wcb-0.1.0 (sm_100a)"; }
+
+uint32_t wcb_tp_id(uint8_t out[128]) {
+  if (!out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+  return guarded([&]() -> uint32_t {
+    ncclUniqueId id;
+    const ncclResult_t r = wcb::nccl().GetUniqueId(&id);
+    if (r != ncclSuccess)
+      throw wcb::WcbError(wcb::E_BACKEND, std::string("Backend error: ncclGetUniqueId: ") + wcb::nccl().GetErrorString(r));
+    static_assert(sizeof(id) == 128, "NCCL unique id size");
+    std::memcpy(out, &id, sizeof(id));
+    return WCB_OK;
+  });
+}
 
 uint32_t wcb_dequant_dev(const void* blocks, uint32_t dtype, size_t nblocks, float* out, void* stream) {
   if (dtype != WCB_DTYPE_Q4_K && dtype != WCB_DTYPE_Q6_K)

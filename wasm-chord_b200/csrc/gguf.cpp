@@ -163,6 +163,14 @@ ModelConfig GgufFile::config() const {  // extract_config (gguf.rs:208-276)
   return c;
 }
 
+void GgufFile::read_range(const GgufTensor& t, uint64_t offset, uint64_t bytes, void* dst) const {
+  if (offset + bytes > t.nbytes) throw WcbError(E_IO, "IO error: range outside tensor " + t.name);
+  if (std::fseek(f_, long(data_offset_ + t.offset + offset), SEEK_SET) != 0)
+    throw WcbError(E_IO, "IO error: seek failed for " + t.name);
+  if (bytes && std::fread(dst, 1, bytes, f_) != bytes)
+    throw WcbError(E_IO, "IO error: failed to fill whole buffer (" + t.name + ")");
+}
+
 void GgufFile::read(const GgufTensor& t, void* dst) const {
   if (std::fseek(f_, long(data_offset_ + t.offset), SEEK_SET) != 0)
     throw WcbError(E_IO, "IO error: seek failed for " + t.name);

@@ -57,6 +57,8 @@ class GgufFile {
   ModelConfig config() const;
   // reads the raw bytes of a tensor into dst (nbytes bytes)
   void read(const GgufTensor& t, void* dst) const;
+  // reads bytes [offset, offset + bytes) of a tensor's data into dst
+  void read_range(const GgufTensor& t, uint64_t offset, uint64_t bytes, void* dst) const;
   uint32_t version() const { return version_; }
   uint64_t data_offset() const { return data_offset_; }
   const std::vector<GgufTensor>& tensors() const { return tensors_; }

@@ -301,16 +301,17 @@ __global__ void __launch_bounds__(GEMV_THREADS, M == 1 ? 2 : 1) gemv_kernel(cons
         }
       } else if (EPI == EPI_LMHEAD) {
         const int n = ROWS * g + i;
+        const int tok_id = a.vocab_off + n;  // rows of this launch start at token vocab_off
         a.y[n] = v;
         if (a.gen_mode) {
           float pv = v;
           if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
-            const uint32_t cnt = a.pen_cnt[n];
+            const uint32_t cnt = a.pen_cnt[tok_id];
             for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, a.rep) : __fmul_rn(pv, a.rep);
           }
           if (pv != pv) nan = 1;
           else {
-            const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
+            const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(tok_id);
             best = key > best ? key : best;
           }
         }
@@ -385,11 +386,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, M == 1 ? 2 : 1) gemv_kernel(cons
       }
       if (b) atomicMax(&a.st->best, b);
       if (n) atomicOr(&a.st->nan, 1);
-      __threadfence();
-      const int prev = atomicAdd(&a.st->ticket, 1);
-      if (prev == int(gridDim.x) - 1) {
+      if (a.gen_mode == 1) {  // mode 2: the key is reduced over ranks before the bookkeeping
         __threadfence();
-        finish_sample(a);
+        const int prev = atomicAdd(&a.st->ticket, 1);
+        if (prev == int(gridDim.x) - 1) {
+          __threadfence();
+          finish_sample(a);
+        }
       }
     }
   }
@@ -720,6 +723,24 @@ __global__ void set_state_kernel(StepState* st, int position, int kv_len, int n_
   st->nan = 0;
 }
 
+__global__ void add_kernel(float* dst, const float* a, const float* b, size_t n, const StepState* st) {
+  if (st && st->done) return;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    dst[i] = __fadd_rn(a[i], b[i]);
+}
+
+__global__ void tp_pack_key_kernel(StepState* st, unsigned long long* key) {
+  key[0] = st->best;
+  key[1] = st->nan ? 1ull : 0ull;
+}
+
+__global__ void tp_finish_kernel(StepState* st, const unsigned long long* key, uint32_t* hist, uint32_t* pen_cnt) {
+  if (st->done) return;
+  st->best = key[0];
+  st->nan = key[1] ? 1 : 0;
+  finish_sample_state(st, hist, pen_cnt);
+}
+
 __global__ void init_gen_kernel(StepState* st, int max_gen, int eos, int max_seq) {
   st->best = 0ull;
   st->ticket = 0;
@@ -842,6 +863,24 @@ void set_pdl(bool on) { g_pdl = on; }
 
 cudaError_t launch_set_state(StepState* st, int position, int kv_len, int n_tokens, cudaStream_t s) {
   set_state_kernel<<<1, 1, 0, s>>>(st, position, kv_len, n_tokens);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add(float* dst, const float* a, const float* b, size_t n, const StepState* st, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const unsigned grid = unsigned(std::min<size_t>((n + 255) / 256, 1184));
+  add_kernel<<<grid, 256, 0, s>>>(dst, a, b, n, st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tp_pack_key(StepState* st, unsigned long long* key, cudaStream_t s) {
+  tp_pack_key_kernel<<<1, 1, 0, s>>>(st, key);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tp_finish(StepState* st, const unsigned long long* key, uint32_t* hist, uint32_t* pen_cnt,
+                             cudaStream_t s) {
+  tp_finish_kernel<<<1, 1, 0, s>>>(st, key, hist, pen_cnt);
   return cudaGetLastError();
 }
 

@@ -98,7 +98,8 @@ struct GemvArgs {
   int token_offset;   // first token of this launch within the forward (column groups)
   int row_offset;     // EPI_QKV: first q/k/v row of this launch
   // EPI_LMHEAD
-  int gen_mode;            // 1: penalty + argmax + generate bookkeeping
+  int gen_mode;            // 1: penalty + argmax + generate bookkeeping; 2: penalty + argmax key only
+  int vocab_off;           // token id of LM-head row 0 (tensor parallelism: this rank's first row)
   const uint32_t* pen_cnt; // occurrences of each token in the sampler history
   uint32_t* pen_cnt_w;     // same array, incremented when a token is pushed
   float rep;               // repetition penalty
@@ -242,6 +243,14 @@ cudaError_t launch_embed(const float* emb, int vocab, int hidden, const uint32_t
 // decode-step embedding: id = hist[nhist - 1]
 cudaError_t launch_embed_last(const float* emb, int vocab, int hidden, const uint32_t* hist, float* x,
                               const StepState* st, cudaStream_t s);
+
+// dst = a + b elementwise (the residual add after a tensor-parallel all-reduce)
+cudaError_t launch_add(float* dst, const float* a, const float* b, size_t n, const StepState* st, cudaStream_t s);
+// tensor-parallel LM head: st->best / st->nan -> key[0..1] before a max
+// all-reduce over the ranks, then the reduced key back and generate()'s bookkeeping
+cudaError_t launch_tp_pack_key(StepState* st, unsigned long long* key, cudaStream_t s);
+cudaError_t launch_tp_finish(StepState* st, const unsigned long long* key, uint32_t* hist, uint32_t* pen_cnt,
+                             cudaStream_t s);
 
 // StepState writers (single-thread kernels, so they order with the stream and
 // can sit inside a captured graph)

@@ -1,5 +1,7 @@
 #include "model.h"
 
+#include "nccl_rt.h"
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -63,8 +65,33 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
   max_seq_ = opt.max_seq ? opt.max_seq : c.max_seq;
   if (max_seq_ == 0) throw WcbError(E_INVALID, "Invalid tensor shape: context length 0");
 
+  tp_ = std::max<uint32_t>(opt.tp_size, 1);
+  rank_ = opt.tp_rank;
+  if (tp_ > 1) {
+    // Megatron split: heads and FFN rows column-parallel, o / down row-parallel
+    // (their input columns split), LM head split by vocabulary
+    if (c.heads % tp_ || c.kv_heads % tp_ || c.hidden % (QK_K * tp_) || c.ffn % (QK_K * tp_) ||
+        c.vocab % (4 * tp_) || (c.ffn / tp_) % 4)
+      throw WcbError(E_BACKEND, "Backend error: the model's heads, hidden, intermediate and vocab sizes do not "
+                                "split over " + std::to_string(tp_) + " tensor-parallel ranks");
+  }
+  hq_ = c.hidden / tp_;
+  kvd_l_ = c.kv_heads * hd / tp_;
+  heads_l_ = c.heads / tp_;
+  kv_l_ = c.kv_heads / tp_;
+  ffn_l_ = c.ffn / tp_;
+  vocab_l_ = c.vocab / tp_;
+  vocab_off_ = rank_ * vocab_l_;
+
   check(cudaSetDevice(device_), "cudaSetDevice");
   check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (tp_ > 1) {
+    ncclUniqueId id;
+    std::memcpy(&id, opt.tp_id, sizeof(id));
+    const ncclResult_t r = nccl().CommInitRank(&comm_, int(tp_), id, int(rank_));
+    if (r != ncclSuccess)
+      throw WcbError(E_BACKEND, std::string("Backend error: ncclCommInitRank: ") + nccl().GetErrorString(r));
+  }
   check(gemv_configure_all(), "configure GEMV kernels");
   check(gemm_tc_configure(), "configure GEMM kernels");
   set_pdl(!(opt.flags & 2));
@@ -110,7 +137,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     for (const char* n : {"output.weight", "lm_head.weight", "model.lm_head.weight"}) {
       const GgufTensor* t = f.find(n);
       if (!t || (t->dtype != DT_Q4K && t->dtype != DT_Q6K)) continue;
-      upload_weight(f, n, c.vocab, c.hidden, lm_head_, false);
+      upload_weight(f, n, c.vocab, c.hidden, lm_head_, false, vocab_off_, vocab_l_);
       have_head = true;
       break;
     }
@@ -123,18 +150,21 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     for (uint32_t l = 0; l < c.layers; ++l) {
       DevLayer& L = layers_[l];
       const std::string p = "blk." + std::to_string(l) + ".";
-      auto attn = [&](const char* base, uint32_t rows, DevWeight& w) {
+      auto attn = [&](const char* base, uint32_t rows, DevWeight& w, uint32_t row0, uint32_t nrows, uint32_t blk0,
+                      uint32_t nblk) {
         std::string n = p + base + ".weight";
         if (!f.find(n)) n = p + base;
-        upload_weight(f, n, rows, c.hidden, w, true);
+        upload_weight(f, n, rows, c.hidden, w, true, row0, nrows, blk0, nblk);
       };
-      attn("attn_q", c.hidden, L.q);
-      attn("attn_k", kvd, L.k);
-      attn("attn_v", kvd, L.v);
-      attn("attn_output", c.hidden, L.o);
-      upload_weight(f, p + "ffn_gate.weight", c.ffn, c.hidden, L.gate, true);
-      upload_weight(f, p + "ffn_up.weight", c.ffn, c.hidden, L.up, true);
-      upload_weight(f, p + "ffn_down.weight", c.hidden, c.ffn, L.down, true);
+      // this rank's heads (all of them with one rank)
+      attn("attn_q", c.hidden, L.q, rank_ * hq_, hq_, 0, 0);
+      attn("attn_k", kvd, L.k, rank_ * kvd_l_, kvd_l_, 0, 0);
+      attn("attn_v", kvd, L.v, rank_ * kvd_l_, kvd_l_, 0, 0);
+      attn("attn_output", c.hidden, L.o, 0, 0, rank_ * (hq_ / QK_K), hq_ / QK_K);
+      upload_weight(f, p + "ffn_gate.weight", c.ffn, c.hidden, L.gate, true, rank_ * ffn_l_, ffn_l_);
+      upload_weight(f, p + "ffn_up.weight", c.ffn, c.hidden, L.up, true, rank_ * ffn_l_, ffn_l_);
+      upload_weight(f, p + "ffn_down.weight", c.hidden, c.ffn, L.down, true, 0, 0, rank_ * (ffn_l_ / QK_K),
+                    ffn_l_ / QK_K);
       upload_vector(f, p + "attn_norm.weight", c.hidden, 1.0f, L.attn_norm);
       upload_vector(f, p + "ffn_norm.weight", c.hidden, 1.0f, L.ffn_norm);
       if (L.gate.dtype != L.up.dtype)
@@ -142,7 +172,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     }
 
     // KV cache (kv_cache.rs:6-34), [L][n_kv][max_seq][hd]
-    kv_layer_elems_ = size_t(c.kv_heads) * max_seq_ * hd;
+    kv_layer_elems_ = size_t(kv_l_) * max_seq_ * hd;
     const size_t kv_bytes = kv_layer_elems_ * c.layers * (opt.kv_half ? 2 : 4);
     kcache_ = dalloc(kv_bytes);
     vcache_ = dalloc(kv_bytes);
@@ -164,6 +194,10 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     att_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
     act_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.ffn));
     logits_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
+    if (tp_ > 1) {
+      part_y_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
+      tpkey_ = static_cast<unsigned long long*>(dalloc(2 * sizeof(unsigned long long)));
+    }
     row_m_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_)));
     pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab));
     check(cudaMemset(pen_cnt_, 0, sizeof(uint32_t) * c.vocab), "clear penalty counts");
@@ -180,6 +214,8 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     allocs_.clear();
     if (host_ids_) cudaFreeHost(host_ids_);
     host_ids_ = nullptr;
+    if (comm_) nccl().CommDestroy(comm_);
+    comm_ = nullptr;
     cudaStreamDestroy(stream_);
     stream_ = nullptr;
     throw;
@@ -190,7 +226,8 @@ Model::~Model() {
   cudaSetDevice(device_);
   if (stream_) cudaStreamSynchronize(stream_);
   if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
-  if (decode_graph_) cudaGraphDestroy(decode_graph_);
+  if (decode_graph_) cudaGraphDestroy(decode_graph_);  // graphs holding NCCL calls go before the comm
+  if (comm_) nccl().CommDestroy(comm_);
   for (void* p : allocs_) cudaFree(p);
   if (host_ids_) cudaFreeHost(host_ids_);
   if (stream_) cudaStreamDestroy(stream_);
@@ -200,15 +237,18 @@ Model::~Model() {
 // A missing tensor leaves zeros, as the reference's `if let Ok(..)` loads do
 // (model.rs:618-760): an all-zero Q4_K block dequantises to 0.
 void Model::upload_weight(const GgufFile& f, const std::string& name, uint32_t rows, uint32_t cols, DevWeight& w,
-                          bool missing_is_zero) {
-  w.rows = rows;
-  w.cols = cols;
+                          bool missing_is_zero, uint32_t row0, uint32_t nrows, uint32_t blk0, uint32_t nblk) {
   const size_t nb = size_t(cols) / QK_K;
+  if (nrows == 0) nrows = rows - row0;
+  if (nblk == 0) nblk = uint32_t(nb) - blk0;
+  if (row0 + nrows > rows || blk0 + nblk > nb) throw WcbError(E_GENERIC, "shard outside tensor " + name);
+  w.rows = nrows;
+  w.cols = nblk * QK_K;
   const GgufTensor* t = f.find(name);
   if (!t) {
     if (!missing_is_zero) throw WcbError(E_GENERIC, "Tensor not found: " + name);
     w.dtype = DT_Q4K;
-    const size_t bytes = size_t(rows) * nb * Q4K_BYTES;
+    const size_t bytes = size_t(nrows) * nblk * Q4K_BYTES;
     w.ptr = static_cast<uint8_t*>(dalloc(bytes));
     check(cudaMemset(w.ptr, 0, bytes), "zero weight");
     return;
@@ -220,18 +260,30 @@ void Model::upload_weight(const GgufFile& f, const std::string& name, uint32_t r
     throw WcbError(E_BACKEND, "Backend error: tensor " + name + " must be Q4_K or Q6_K (GGUF type " +
                                   std::to_string(t->dtype) + ")");
   w.dtype = int(t->dtype);
-  std::vector<uint8_t> raw(t->nbytes);
-  f.read(*t, raw.data());
+  const size_t bb = w.dtype == DT_Q4K ? Q4K_BYTES : Q6K_BYTES;
+  const size_t row_bytes = nb * bb, take = size_t(nblk) * bb;
+  std::vector<uint8_t> raw(size_t(nrows) * take);
+  if (take == row_bytes) {
+    f.read_range(*t, size_t(row0) * row_bytes, raw.size(), raw.data());  // whole rows: one read
+  } else {
+    for (uint32_t r = 0; r < nrows; ++r)  // a column slice: part of every row
+      f.read_range(*t, size_t(row0 + r) * row_bytes + size_t(blk0) * bb, take, raw.data() + size_t(r) * take);
+  }
   if (w.dtype == DT_Q4K) {
     w.ptr = static_cast<uint8_t*>(dalloc(raw.size()));
     check(cudaMemcpy(w.ptr, raw.data(), raw.size(), cudaMemcpyHostToDevice), "upload weight");
   } else {
-    const size_t nblk = raw.size() / Q6K_BYTES;
-    std::vector<uint8_t> pad(nblk * Q6K_DEV_BYTES, 0);
-    for (size_t b = 0; b < nblk; ++b) std::memcpy(&pad[b * Q6K_DEV_BYTES], &raw[b * Q6K_BYTES], Q6K_BYTES);
+    const size_t nblock = raw.size() / Q6K_BYTES;
+    std::vector<uint8_t> pad(nblock * Q6K_DEV_BYTES, 0);
+    for (size_t b = 0; b < nblock; ++b) std::memcpy(&pad[b * Q6K_DEV_BYTES], &raw[b * Q6K_BYTES], Q6K_BYTES);
     w.ptr = static_cast<uint8_t*>(dalloc(pad.size()));
     check(cudaMemcpy(w.ptr, pad.data(), pad.size(), cudaMemcpyHostToDevice), "upload weight");
   }
+}
+
+void Model::all_reduce_sum(float* buf, size_t n) {
+  const ncclResult_t r = nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, comm_, stream_);
+  if (r != ncclSuccess) throw WcbError(E_BACKEND, std::string("Backend error: ncclAllReduce: ") + nccl().GetErrorString(r));
 }
 
 void Model::upload_vector(const GgufFile& f, const std::string& name, uint32_t n, float fill, float*& dst) {
@@ -317,8 +369,8 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
     a.ldy = ldy;
     a.ldr = ldr;
     a.ldq = ldq;
-    a.hidden = int(cfg_.hidden);
-    a.kv_dim = int(cfg_.kv_heads * cfg_.head_dim());
+    a.hidden = int(hq_);     // query rows of the [q; k; v] segments held here
+    a.kv_dim = int(kvd_l_);
     a.head_dim = int(cfg_.head_dim());
     a.max_seq = int(max_seq_);
     a.kv_half = int(opt_.kv_half);
@@ -332,6 +384,7 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
     a.rope_sin = rope_sin_;
     a.st = st_;
     a.gen_mode = gen_mode_;
+    a.vocab_off = int(vocab_off_);
     a.pen_cnt = pen_cnt_;
     a.pen_cnt_w = pen_cnt_;
     a.rep = rep_;
@@ -375,13 +428,14 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
 
 void Model::enqueue_layers(int T) {
   const ModelConfig& c = cfg_;
-  const int H = int(c.hidden), F = int(c.ffn), hd = int(c.head_dim());
+  const int H = int(c.hidden), hd = int(c.head_dim());
+  const int HQ = int(hq_), FL = int(ffn_l_);
   for (uint32_t l = 0; l < c.layers; ++l) {
     const DevLayer& L = layers_[l];
     // RMSNorm(eps 1e-6, layer.rs:51-57) -> Q/K/V projections (attention.rs:80-129)
-    // -> RoPE (:140-143) -> KV append (:162)
+    // -> RoPE (:140-143) -> KV append (:162); this rank's heads only
     const DevWeight qkv[3] = {L.q, L.k, L.v};
-    gemv(qkv, 3, H, T, x_, H, L.attn_norm, 1e-6f, PRO_RMSNORM, EPI_QKV, nullptr, 0, nullptr, 0, q_, H, int(l), 0);
+    gemv(qkv, 3, H, T, x_, H, L.attn_norm, 1e-6f, PRO_RMSNORM, EPI_QKV, nullptr, 0, nullptr, 0, q_, HQ, int(l), 0);
     // attention over the cache (attention.rs:173, :332-435)
     AttnArgs a{};
     a.q = q_;
@@ -392,8 +446,8 @@ void Model::enqueue_layers(int T) {
     a.out = att_;
     a.part = part_;
     a.ticket = ticket_;
-    a.n_heads = int(c.heads);
-    a.n_kv = int(c.kv_heads);
+    a.n_heads = int(heads_l_);
+    a.n_kv = int(kv_l_);
     a.head_dim = hd;
     a.max_seq = int(max_seq_);
     a.T = T;
@@ -408,15 +462,30 @@ void Model::enqueue_layers(int T) {
     a.st = st_;
     check(launch_attention(a, stream_), "attention");
     ++launches_;
-    // output projection + residual (attention.rs:182-191, layer.rs:68)
+    // output projection + residual (attention.rs:182-191, layer.rs:68); with several
+    // ranks each holds the columns of its heads: partial sums, all-reduced
     const DevWeight o[1] = {L.o};
-    gemv(o, 1, H, T, att_, H, nullptr, 0.0f, PRO_NONE, EPI_RESID, h_, H, x_, H, nullptr, 0, -1, 0);
+    if (tp_ == 1) {
+      gemv(o, 1, HQ, T, att_, HQ, nullptr, 0.0f, PRO_NONE, EPI_RESID, h_, H, x_, H, nullptr, 0, -1, 0);
+    } else {
+      gemv(o, 1, HQ, T, att_, HQ, nullptr, 0.0f, PRO_NONE, EPI_STORE, part_y_, H, nullptr, 0, nullptr, 0, -1, 0);
+      all_reduce_sum(part_y_, size_t(T) * H);
+      check(launch_add(h_, x_, part_y_, size_t(T) * H, st_, stream_), "residual");
+      launches_ += 1;
+    }
     // RMSNorm(eps 1e-6, layer.rs:71-77) -> gate/up -> SwiGLU (ffn.rs:60-94)
     const DevWeight gu[2] = {L.gate, L.up};
-    gemv(gu, 2, H, T, h_, H, L.ffn_norm, 1e-6f, PRO_RMSNORM, EPI_SWIGLU, act_, F, nullptr, 0, nullptr, 0, -1, 0);
+    gemv(gu, 2, H, T, h_, H, L.ffn_norm, 1e-6f, PRO_RMSNORM, EPI_SWIGLU, act_, FL, nullptr, 0, nullptr, 0, -1, 0);
     // down projection + residual (ffn.rs:97-106, layer.rs:86)
     const DevWeight dn[1] = {L.down};
-    gemv(dn, 1, F, T, act_, F, nullptr, 0.0f, PRO_NONE, EPI_RESID, x_, H, h_, H, nullptr, 0, -1, 0);
+    if (tp_ == 1) {
+      gemv(dn, 1, FL, T, act_, FL, nullptr, 0.0f, PRO_NONE, EPI_RESID, x_, H, h_, H, nullptr, 0, -1, 0);
+    } else {
+      gemv(dn, 1, FL, T, act_, FL, nullptr, 0.0f, PRO_NONE, EPI_STORE, part_y_, H, nullptr, 0, nullptr, 0, -1, 0);
+      all_reduce_sum(part_y_, size_t(T) * H);
+      check(launch_add(x_, h_, part_y_, size_t(T) * H, st_, stream_), "residual");
+      launches_ += 1;
+    }
   }
 }
 
@@ -426,10 +495,20 @@ void Model::enqueue_layers(int T) {
 void Model::enqueue_lm_head(int T, bool gen) {
   const int H = int(cfg_.hidden);
   const DevWeight head[1] = {lm_head_};
-  gen_mode_ = gen ? 1 : 0;
+  // with several ranks each scores its vocabulary rows; the argmax key (order-
+  // preserving logit bits | token id) and the NaN flag are max-reduced over the
+  // ranks, then every rank runs the same sampler bookkeeping
+  gen_mode_ = gen ? (tp_ > 1 ? 2 : 1) : 0;
   gemv(head, 1, H, 1, x_ + size_t(T - 1) * H, H, out_norm_, cfg_.eps, PRO_RMSNORM, EPI_LMHEAD, logits_,
        int(cfg_.vocab), nullptr, 0, nullptr, 0, -1, 0);
   gen_mode_ = 0;
+  if (gen && tp_ > 1) {
+    check(launch_tp_pack_key(st_, tpkey_, stream_), "argmax key");
+    const ncclResult_t r = nccl().AllReduce(tpkey_, tpkey_, 2, ncclUint64, ncclMax, comm_, stream_);
+    if (r != ncclSuccess) throw WcbError(E_BACKEND, std::string("Backend error: ncclAllReduce: ") + nccl().GetErrorString(r));
+    check(launch_tp_finish(st_, tpkey_, hist_, pen_cnt_, stream_), "sampler bookkeeping");
+    launches_ += 2;
+  }
 }
 
 void Model::enqueue_forward(const uint32_t* dev_ids, int T, bool from_hist) {
@@ -460,8 +539,9 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
     const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
     enqueue_lm_head(last_T, false);
   }
-  if (logits_out)
-    check(cudaMemcpyAsync(logits_out, logits_, sizeof(float) * cfg_.vocab, cudaMemcpyDeviceToHost, stream_),
+  if (logits_out)  // with several ranks: this rank's vocabulary slice only
+    check(cudaMemcpyAsync(logits_out + vocab_off_, logits_, sizeof(float) * vocab_l_, cudaMemcpyDeviceToHost,
+                          stream_),
           "download logits");
   check(cudaStreamSynchronize(stream_), "forward");
   if (n == 1 && mk_ok_) {
@@ -479,7 +559,7 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
 // head. Each phase waits on the counter of the phase whose output it reads.
 void Model::build_decode_step() {
   mk_ok_ = false;
-  if (opt_.flags & 8) return;
+  if ((opt_.flags & 8) || tp_ > 1) return;  // tensor parallelism runs the per-op kernels
   if (decode_step_configure() != cudaSuccess) {
     cudaGetLastError();
     return;
@@ -716,6 +796,8 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   sess_params_ = g;
   sess_sampler_ = std::make_unique<Sampler>(g.seed, g.temperature, g.top_p, g.top_k, g.repetition_penalty);
   sess_greedy_ = sess_sampler_->greedy();
+  if (!sess_greedy_ && tp_ > 1)  // the host sampler would need every rank's logits
+    throw WcbError(E_BACKEND, "Backend error: sampled decoding (temperature > 0) with tensor parallelism");
   sess_delivered_ = 0;
   sess_tokens_.clear();
   sess_done_ = false;

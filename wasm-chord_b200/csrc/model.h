@@ -2,6 +2,7 @@
 // reference's Model (crates/wasm-chord-runtime/src/transformer/model.rs:19-44).
 #pragma once
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <cstdint>
 #include <memory>
@@ -32,6 +33,9 @@ struct LoadOptions {
   uint32_t kv_half = 0;
   uint32_t max_batch = 1;
   uint32_t flags = 0;
+  uint32_t tp_rank = 0;  // tensor parallelism: this process's rank of tp_size
+  uint32_t tp_size = 1;
+  uint8_t tp_id[128] = {};  // NCCL unique id of the group
 };
 
 struct GenParams {
@@ -70,8 +74,12 @@ class Model {
   int launches_per_decode_step() const { return launches_per_step_; }
 
  private:
+  // rows [row0, row0 + nrows) and 256-value blocks [blk0, blk0 + nblk) of a
+  // [rows][cols] tensor (nrows / nblk 0: all)
   void upload_weight(const GgufFile& f, const std::string& name, uint32_t rows, uint32_t cols, DevWeight& w,
-                     bool required_shape_only);
+                     bool required_shape_only, uint32_t row0 = 0, uint32_t nrows = 0, uint32_t blk0 = 0,
+                     uint32_t nblk = 0);
+  void all_reduce_sum(float* buf, size_t n);  // tensor parallelism: sum over the ranks, in place
   void upload_vector(const GgufFile& f, const std::string& name, uint32_t n, float fill, float*& dst);
   void build_rope(uint32_t len);
   void* dalloc(size_t bytes);
@@ -90,6 +98,16 @@ class Model {
 
   ModelConfig cfg_;
   LoadOptions opt_;
+  // tensor parallelism (Megatron split over tp_ ranks; tp_ == 1: the whole model)
+  uint32_t tp_ = 1, rank_ = 0;
+  uint32_t hq_ = 0;      // query rows held: hidden / tp
+  uint32_t kvd_l_ = 0;   // K (and V) rows held: kv_heads * head_dim / tp
+  uint32_t heads_l_ = 0, kv_l_ = 0;
+  uint32_t ffn_l_ = 0;   // gate / up rows held and down input columns: ffn / tp
+  uint32_t vocab_l_ = 0, vocab_off_ = 0;  // LM-head rows held and the first one's token id
+  ncclComm_t comm_ = nullptr;
+  float* part_y_ = nullptr;                 // [t_max][hidden] partial o / down outputs
+  unsigned long long* tpkey_ = nullptr;    // argmax key and NaN flag exchanged by the LM head
   int device_ = 0;
   cudaStream_t stream_ = nullptr;
   std::vector<void*> allocs_;

@@ -34,7 +34,7 @@ EXPORTED = [
     "wcb_sampler_sample", "wcb_sampler_free", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
     "wcb_repack_q6k_dev", "wcb_gemv_dev", "wcb_model_stream", "wcb_infer", "wcb_next_tokens",
     "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_attention_dev",
-    "wcb_attention_dev_noalloc",
+    "wcb_attention_dev_noalloc", "wcb_tp_id",
 ]
 
 
@@ -47,7 +47,8 @@ class WcbError(RuntimeError):
 
 class _LoadOpts(C.Structure):
     _fields_ = [("device", C.c_int32), ("max_seq", C.c_uint32), ("kv_dtype", C.c_uint32),
-                ("max_batch", C.c_uint32), ("flags", C.c_uint32)]
+                ("max_batch", C.c_uint32), ("flags", C.c_uint32), ("tp_rank", C.c_uint32),
+                ("tp_size", C.c_uint32), ("tp_id", C.c_uint8 * 128)]
 
 
 class _ModelConfig(C.Structure):
@@ -66,6 +67,20 @@ class _GenConfig(C.Structure):
 _LIB = None
 
 
+def _point_at_shared_nccl() -> None:
+    """The library loads NCCL at run time; point it at the copy PyTorch ships
+    so a process that uses both loads one NCCL, whichever is imported first."""
+    if os.environ.get("WCB_NCCL_LIB"):
+        return
+    import importlib.util
+    spec = importlib.util.find_spec("nvidia")
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        cand = os.path.join(base, "nccl", "lib", "libnccl.so.2")
+        if os.path.exists(cand):
+            os.environ["WCB_NCCL_LIB"] = cand
+            return
+
+
 def lib() -> C.CDLL:
     """Loads libwcb.so (building it first if it is missing)."""
     global _LIB
@@ -74,6 +89,7 @@ def lib() -> C.CDLL:
     if not os.path.exists(LIB_PATH):
         from . import build
         build.build_lib()
+    _point_at_shared_nccl()
     L = C.CDLL(LIB_PATH)
     u32, sz, vp = C.c_uint32, C.c_size_t, C.c_void_p
     L.wcb_gen_config_default.argtypes = [C.POINTER(_GenConfig)]
@@ -104,6 +120,7 @@ def lib() -> C.CDLL:
     L.wcb_model_launches_per_step.argtypes = [u32, C.POINTER(u32)]
     L.wcb_attention_dev.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     L.wcb_attention_dev_noalloc.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
+    L.wcb_tp_id.argtypes = [vp]
     for name in EXPORTED:
         f = getattr(L, name)
         if f.restype is C.c_int and name != "wcb_next_token":  # ctypes default
@@ -184,10 +201,19 @@ class Model:
     @classmethod
     def load_from_gguf(cls, path: str, device: int = 0, max_seq: int = 0, kv_dtype: int = KV_F32,
                        max_batch: int = 1, use_graphs: bool = True, use_pdl: bool = True,
-                       use_tensor_cores: bool = True, use_persistent: bool = True) -> "Model":
+                       use_tensor_cores: bool = True, use_persistent: bool = True, tp_rank: int = 0,
+                       tp_size: int = 1, tp_id: bytes = b"") -> "Model":
+        """Loads a GGUF file. tp_size > 1: this process holds tensor-parallel rank
+        tp_rank's shard and joins the group named by tp_id (tp_unique_id() on one
+        rank, the same bytes on every rank); forward() then fills only this rank's
+        vocabulary slice of the logits."""
         flags = ((0 if use_graphs else 1) | (0 if use_pdl else 2) | (0 if use_tensor_cores else 4)
                  | (0 if use_persistent else 8))
-        o = _LoadOpts(device, max_seq, kv_dtype, max_batch, flags)
+        o = _LoadOpts(device, max_seq, kv_dtype, max_batch, flags, tp_rank, tp_size)
+        if tp_size > 1:
+            if len(tp_id) != 128:
+                raise ValueError("tp_id must be the 128 bytes of tp_unique_id()")
+            C.memmove(o.tp_id, tp_id, 128)
         h = C.c_uint32(0)
         _check(lib().wcb_model_load(os.fsencode(path), C.byref(o), C.byref(h)))
         return cls(h.value)
@@ -352,3 +378,10 @@ def attention_dev_noalloc(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, n_to
     """wcb_attention_dev with the library's fixed scratch array (no GPU allocation)."""
     _check(lib().wcb_attention_dev_noalloc(q_ptr, k_ptr, v_ptr, out_ptr, n_tokens, n_heads, n_kv_heads, head_dim,
                                            max_seq, kv_len, position, stream or None))
+
+
+def tp_unique_id() -> bytes:
+    """A fresh tensor-parallel group id (128 bytes) for Model.load_from_gguf(tp_id=...)."""
+    buf = (C.c_uint8 * 128)()
+    _check(lib().wcb_tp_id(buf))
+    return bytes(buf)

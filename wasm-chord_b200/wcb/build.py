@@ -25,7 +25,7 @@ LIB = os.path.join(PKG, "libwcb.so")
 SYNTH_LIB = os.path.join(PKG, "libwcb_synth.so")
 
 CUDA_SOURCES = ["kernels.cu", "gemm_tc.cu", "decode_step.cu", "noalloc.cu"]
-HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "api.cpp"]
+HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "api.cpp", "nccl_rt.cpp"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -94,7 +94,7 @@ def build_lib(verbose: bool = False, ptxas_verbose: bool = False) -> str:
                 if verbose and (r.stdout or r.stderr):
                     print(r.stdout, r.stderr, file=sys.stderr)
     if jobs or _stale(LIB, objs):
-        _run([nvcc, "-shared"] + GENCODE + ["-o", LIB + ".tmp"] + objs + ["-lpthread"])
+        _run([nvcc, "-shared"] + GENCODE + ["-o", LIB + ".tmp"] + objs + ["-ldl", "-lpthread"])
         os.replace(LIB + ".tmp", LIB)
         if verbose:
             print("built", LIB)

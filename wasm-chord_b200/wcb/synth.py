@@ -160,6 +160,9 @@ PRESETS = {
     "tiny_mix": SynthConfig(vocab_size=768, hidden_size=512, num_layers=2, num_heads=8,
                             num_kv_heads=8, intermediate_size=768, context_length=160,
                             quant_mix="q4_k_m"),
+    # splits over 2 tensor-parallel ranks (hidden / 2 and intermediate / 2 multiples of 256)
+    "tiny_tp": SynthConfig(vocab_size=1024, hidden_size=512, num_layers=2, num_heads=8,
+                           num_kv_heads=4, intermediate_size=1024, context_length=256),
 }
 
 
