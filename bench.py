@@ -8,6 +8,8 @@ LM head + on-device argmax). The weights (582 MB) exceed the 126 MB L2, so no
 L2 flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N --tp [--layers L] [--prompt P]
+      (the Llama-2-70B shape, tensor-parallel over N GPUs; not the headline line)
 
 N > 1 runs under torchrun as N independent data-parallel replicas (no
 collective on the data path); value is the total tokens/s over all ranks with
@@ -327,6 +329,73 @@ def run_ours(args, rank, world, dist):
     m.close()
 
 
+def run_tp(args, rank, world, dist):
+    """The Llama-2-70B shape (hidden 8192, FFN 28672, 64 / 8 heads, vocab 32000, Q4_K),
+    tensor-parallel over the `world` ranks of this torchrun: one sequence, greedy
+    decode after a `--prompt`-token prompt; value = the group's tokens/s."""
+    import torch
+    import wcb
+    from wcb import synth
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    layers = args.layers
+    path = [synth.cached_model("llama70b", MODEL_DIR, num_layers=layers) if local == 0 else None]
+    if world > 1:
+        dist.barrier()
+        dist.broadcast_object_list(path, src=0)
+    path = path[0]
+    tp_id = [wcb.tp_unique_id() if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(tp_id, src=0)
+    m = wcb.Model.load_from_gguf(path, device=local, tp_rank=rank, tp_size=world, tp_id=tp_id[0],
+                                 max_seq=args.prompt + args.warmup + args.steps + 8)
+    cfg = m.config
+    s = torch.cuda.ExternalStream(m.stream())
+    prompt = synth.random_prompt(args.prompt, cfg.vocab_size, seed=1)
+    K, W = args.steps, args.warmup
+    gc = wcb.GenerationConfig(max_tokens=W + K + 1, temperature=0.0, repetition_penalty=1.0, eos_id=None)
+    stream = m.infer(prompt.tolist(), gc)
+    stream.next_tokens(1 + W)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(s)
+        toks = stream.next_tokens(K)
+        e1.record(s)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    assert len(toks) == K, (len(toks), K)
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    peak, peak_kind = peaks()
+    wbytes = weight_bytes(cfg, path) / world  # each rank streams its shard
+    per_rank_gbs = wbytes / (ms / K * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode tok/s (Llama-2-70B shape Q4_K, batch 1, tensor parallel)", "value": K / (ms * 1e-3),
+            "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 activations, Q4_K weights", "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K)",
+            "config": {"workload": f"Llama-2-70B shape, {layers} of its 80 layers, greedy decode after a "
+                                   f"{args.prompt}-token prompt", "layers": layers, "prompt_len": args.prompt,
+                       "parallelism": f"tp{world} (NCCL all-reduce after attn-out and ffn-down)",
+                       "l2": "weights > 126 MB L2, no flush"},
+            "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": per_rank_gbs / peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "whole decode step per rank (shard weights / ms per token)",
+                         "bytes_per_launch": wbytes},
+            "gpu_launches": m.launches_per_step() * K,
+            "clocks": clk.summary(),
+        }), flush=True)
+    stream.close()
+    m.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -336,6 +405,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv-only", type=int, default=0, metavar="REPS",
                     help="only time the dominant GEMV (REPS launches per weight copy) and print its line")
+    ap.add_argument("--tp", action="store_true",
+                    help="the Llama-2-70B shape, tensor-parallel over the torchrun ranks, instead of the headline")
+    ap.add_argument("--layers", type=int, default=80, help="--tp: layers of the 70B shape to build")
+    ap.add_argument("--prompt", type=int, default=1024, help="--tp: prompt tokens before the timed decode")
     args = ap.parse_args()
     if args.gemv_only:
         import torch
@@ -362,7 +435,10 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     try:
-        run_ours(args, rank, world, dist)
+        if args.tp:
+            run_tp(args, rank, world, dist)
+        else:
+            run_ours(args, rank, world, dist)
     finally:
         if dist is not None:
             dist.destroy_process_group()
