@@ -349,6 +349,12 @@ def run_tp(args, rank, world, dist):
         dist.broadcast_object_list(tp_id, src=0)
     m = wcb.Model.load_from_gguf(path, device=local, tp_rank=rank, tp_size=world, tp_id=tp_id[0],
                                  max_seq=args.prompt + args.warmup + args.steps + 8)
+    exchange = "nccl"
+    if world > 1 and not args.tp_nccl:  # decode steps: partial sums by peer stores over NVLink
+        handles = [None] * world
+        dist.all_gather_object(handles, m.tp_ipc_handle())
+        m.tp_connect(handles)
+        exchange = "peer stores"
     cfg = m.config
     s = torch.cuda.ExternalStream(m.stream())
     prompt = synth.random_prompt(args.prompt, cfg.vocab_size, seed=1)
@@ -383,7 +389,8 @@ def run_tp(args, rank, world, dist):
             "dtype": "f32 activations, Q4_K weights", "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K)",
             "config": {"workload": f"Llama-2-70B shape, {layers} of its 80 layers, greedy decode after a "
                                    f"{args.prompt}-token prompt", "layers": layers, "prompt_len": args.prompt,
-                       "parallelism": f"tp{world} (NCCL all-reduce after attn-out and ffn-down)",
+                       "parallelism": f"tp{world} (partial sums of attn-out and ffn-down all-reduced by {exchange}; "
+                                      "prefill: NCCL)",
                        "l2": "weights > 126 MB L2, no flush"},
             "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": peak, "unit": "GB/s",
                          "frac": per_rank_gbs / peak, "traffic": None, "peak_kind": peak_kind,
@@ -409,6 +416,7 @@ def main():
                     help="the Llama-2-70B shape, tensor-parallel over the torchrun ranks, instead of the headline")
     ap.add_argument("--layers", type=int, default=80, help="--tp: layers of the 70B shape to build")
     ap.add_argument("--prompt", type=int, default=1024, help="--tp: prompt tokens before the timed decode")
+    ap.add_argument("--tp-nccl", action="store_true", help="--tp: all-reduce decode steps with NCCL too")
     args = ap.parse_args()
     if args.gemv_only:
         import torch

@@ -167,6 +167,15 @@ const char* wcb_version(void);
  * No counterpart in the reference. */
 uint32_t wcb_tp_id(uint8_t out[128]);
 
+/* Tensor parallelism, decode steps without NCCL: each rank exports the CUDA IPC
+ * handle (64 bytes) of its receive buffer, the caller gathers them in rank order
+ * and hands all of them to every rank; decode steps then write their attn-out /
+ * ffn-down partial sums straight into every rank's buffer over NVLink and sum
+ * them in rank order (prefill keeps the NCCL all-reduce). No counterpart in the
+ * reference. */
+uint32_t wcb_model_tp_handle(uint32_t h, uint8_t out[64]);
+uint32_t wcb_model_tp_connect(uint32_t h, const uint8_t* handles, uint32_t n_ranks);
+
 /* ---- kernel-level entry points (device pointers, caller's stream) ----------
  * No counterpart in the reference's public API: they expose the hot kernels
  * (the reference's quant.rs dequantisers and gemm.rs matmul_transposed) for

@@ -17,11 +17,18 @@ def _gpus():
     return torch.cuda.device_count()
 
 
-def _rank_main(rank, world, path, tp_id, prompt, q):
+def _rank_main(rank, world, path, tp_id, prompt, q, port):
     try:
         import torch
         torch.cuda.set_device(rank)
         m = wcb.Model.load_from_gguf(path, device=rank, tp_rank=rank, tp_size=world, tp_id=tp_id)
+        if port:  # decode steps exchange partial sums by peer stores (IPC handles over gloo)
+            import torch.distributed as dist
+            dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+            handles = [None] * world
+            dist.all_gather_object(handles, m.tp_ipc_handle())
+            dist.destroy_process_group()
+            m.tp_connect(handles)
         logits = m.forward(prompt, 0)
         vocab = m.config.vocab_size
         part = vocab // world
@@ -33,16 +40,27 @@ def _rank_main(rank, world, path, tp_id, prompt, q):
         q.put((rank, None, None, repr(e)))
 
 
-def test_tp2_matches_oracle(model_dir, gpu):
+def _free_port():
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_tp2_matches_oracle(model_dir, gpu, exchange):
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     path = synth.cached_model("tiny_tp", model_dir)
     prompt = synth.random_prompt(21, 1024, seed=40).tolist()
     tp_id = wcb.tp_unique_id()
+    port = _free_port() if exchange == "peer" else 0
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, path, tp_id, prompt, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, path, tp_id, prompt, q, port)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}

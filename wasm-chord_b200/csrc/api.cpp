@@ -505,6 +505,22 @@ uint32_t wcb_attention_dev(const float* q, const float* k_cache, const float* v_
   return e == cudaSuccess ? WCB_OK : cuda_fail(e, "attention");
 }
 
+uint32_t wcb_model_tp_handle(uint32_t h, uint8_t out[64]) {
+  return guarded([&]() -> uint32_t {
+    if (!out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    get_model(h)->tp_ipc_handle(out);
+    return WCB_OK;
+  });
+}
+
+uint32_t wcb_model_tp_connect(uint32_t h, const uint8_t* handles, uint32_t n_ranks) {
+  return guarded([&]() -> uint32_t {
+    if (!handles) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    get_model(h)->tp_connect(handles, n_ranks);
+    return WCB_OK;
+  });
+}
+
 uint32_t wcb_model_stream(uint32_t h, void** out) {
   return guarded([&]() -> uint32_t {
     if (!out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");

@@ -287,7 +287,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, M == 1 ? 2 : 1) gemv_kernel(cons
       const float v = sm.fin[o];
       const float* fin = sm.fin + gl * 16;
       const int tok = t;  // column within this launch
-      if (EPI == EPI_STORE) {
+      if (EPI == EPI_PEER) {
+        const int n = ROWS * g + i;
+        const unsigned long long w =
+            (static_cast<unsigned long long>(uint32_t(a.st->epoch) * 512u + uint32_t(a.peer_phase) + 1u) << 32) |
+            __float_as_uint(v);
+        for (int r = 0; r < a.tp_size; ++r)  // one 64-bit store per rank: value and tag arrive together
+          asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.peers[r] + size_t(a.tp_rank) * a.ldy + n),
+                       "l"(w)
+                       : "memory");
+      } else if (EPI == EPI_STORE) {
         a.y[size_t(tok) * a.ldy + ROWS * g + i] = v;
       } else if (EPI == EPI_RESID) {
         const size_t off = size_t(tok) * a.ldy + ROWS * g + i;
@@ -468,6 +477,7 @@ cudaError_t launch_gemv_t(const GemvArgs& a0, cudaStream_t s) {
 
 #define WCB_GEMV_CASES(F)   \
   F(PRO_NONE, EPI_STORE)    \
+  F(PRO_NONE, EPI_PEER)     \
   F(PRO_NONE, EPI_RESID)    \
   F(PRO_RMSNORM, EPI_QKV)   \
   F(PRO_RMSNORM, EPI_SWIGLU) \
@@ -721,12 +731,43 @@ __global__ void set_state_kernel(StepState* st, int position, int kv_len, int n_
   st->best = 0ull;
   st->ticket = 0;
   st->nan = 0;
+  st->epoch += 1;  // tags of this forward's partial sums (tensor parallelism)
 }
 
 __global__ void add_kernel(float* dst, const float* a, const float* b, size_t n, const StepState* st) {
   if (st && st->done) return;
   for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
     dst[i] = __fadd_rn(a[i], b[i]);
+}
+
+__global__ void tp_reduce_add_kernel(float* dst, const float* resid, const unsigned long long* recv, int tp, size_t n,
+                                     int phase, StepState* st) {
+  if (st->done) return;
+  const uint32_t tag = uint32_t(st->epoch) * 512u + uint32_t(phase) + 1u;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    float sum = 0.0f;
+    for (int r = 0; r < tp; ++r) {
+      const unsigned long long* p = recv + size_t(r) * n + i;
+      unsigned long long w;
+      asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+      if (uint32_t(w >> 32) != tag) {
+        unsigned long long t0;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        while (true) {
+          asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+          if (uint32_t(w >> 32) == tag) break;
+          unsigned long long t1;
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+          if (t1 - t0 > 2000000000ull) {  // 2 s: a rank stopped; report, do not hang
+            atomicOr(&st->err, 16);
+            break;
+          }
+        }
+      }
+      sum = __fadd_rn(sum, __uint_as_float(uint32_t(w)));
+    }
+    dst[i] = __fadd_rn(resid[i], sum);
+  }
 }
 
 __global__ void tp_pack_key_kernel(StepState* st, unsigned long long* key) {
@@ -739,6 +780,7 @@ __global__ void tp_finish_kernel(StepState* st, const unsigned long long* key, u
   st->best = key[0];
   st->nan = key[1] ? 1 : 0;
   finish_sample_state(st, hist, pen_cnt);
+  st->epoch += 1;  // tags of the next step's partial sums
 }
 
 __global__ void init_gen_kernel(StepState* st, int max_gen, int eos, int max_seq) {
@@ -870,6 +912,13 @@ cudaError_t launch_add(float* dst, const float* a, const float* b, size_t n, con
   if (n == 0) return cudaSuccess;
   const unsigned grid = unsigned(std::min<size_t>((n + 255) / 256, 1184));
   add_kernel<<<grid, 256, 0, s>>>(dst, a, b, n, st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tp_reduce_add(float* dst, const float* resid, const unsigned long long* recv, int tp_size,
+                                 size_t n, int phase, StepState* st, cudaStream_t s) {
+  const unsigned grid = unsigned(std::min<size_t>((n + 255) / 256, 148));
+  tp_reduce_add_kernel<<<grid, 256, 0, s>>>(dst, resid, recv, tp_size, n, phase, st);
   return cudaGetLastError();
 }
 

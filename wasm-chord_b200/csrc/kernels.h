@@ -57,7 +57,10 @@ enum GemvPro { PRO_NONE = 0, PRO_RMSNORM = 1 };
 // EPI_LMHEAD: store the logits and, in generate mode, fuse the repetition
 // penalty, the argmax and generate()'s bookkeeping (sampling.rs:86-125,
 // model.rs:1380-1409) into the LM-head launch.
-enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_LMHEAD = 4 };
+// EPI_PEER (tensor parallelism, one token): each output is a partial sum; it is
+// written as a (value, tag) pair into slot `tp_rank` of every rank's receive
+// buffer over NVLink, and launch_tp_reduce_add sums the slots on each rank.
+enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_LMHEAD = 4, EPI_PEER = 5 };
 
 struct GemvSeg {
   const uint8_t* w;
@@ -104,6 +107,10 @@ struct GemvArgs {
   uint32_t* pen_cnt_w;     // same array, incremented when a token is pushed
   float rep;               // repetition penalty
   uint32_t* hist;          // sampler history
+  // EPI_PEER
+  unsigned long long* const* peers;  // [tp_size] receive buffers [tp_size][ldy] (device array of pointers)
+  int tp_rank, tp_size;
+  int peer_phase;                    // tag of these partials: epoch * 512 + peer_phase + 1
   // 1: launch with programmatic dependent launch. Only for static weights: the
   // kernel reads its weights before waiting on the previous kernel.
   int pdl;
@@ -249,6 +256,11 @@ cudaError_t launch_add(float* dst, const float* a, const float* b, size_t n, con
 // tensor-parallel LM head: st->best / st->nan -> key[0..1] before a max
 // all-reduce over the ranks, then the reduced key back and generate()'s bookkeeping
 cudaError_t launch_tp_pack_key(StepState* st, unsigned long long* key, cudaStream_t s);
+// dst[i] = resid[i] + sum over ranks r (in rank order) of recv[r * n + i], each
+// value waited for (bounded) until it carries the tag epoch * 512 + phase + 1;
+// an expired wait sets st->err bit 16
+cudaError_t launch_tp_reduce_add(float* dst, const float* resid, const unsigned long long* recv, int tp_size,
+                                 size_t n, int phase, StepState* st, cudaStream_t s);
 cudaError_t launch_tp_finish(StepState* st, const unsigned long long* key, uint32_t* hist, uint32_t* pen_cnt,
                              cudaStream_t s);
 

@@ -197,6 +197,9 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     if (tp_ > 1) {
       part_y_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
       tpkey_ = static_cast<unsigned long long*>(dalloc(2 * sizeof(unsigned long long)));
+      recv_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * tp_ * c.hidden));
+      check(cudaMemset(recv_, 0, sizeof(unsigned long long) * tp_ * c.hidden), "clear receive buffer");
+      peers_dev_ = static_cast<unsigned long long**>(dalloc(sizeof(void*) * tp_));
     }
     row_m_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_)));
     pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab));
@@ -228,6 +231,7 @@ Model::~Model() {
   if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
   if (decode_graph_) cudaGraphDestroy(decode_graph_);  // graphs holding NCCL calls go before the comm
   if (comm_) nccl().CommDestroy(comm_);
+  for (void* p : ipc_opened_) cudaIpcCloseMemHandle(p);
   for (void* p : allocs_) cudaFree(p);
   if (host_ids_) cudaFreeHost(host_ids_);
   if (stream_) cudaStreamDestroy(stream_);
@@ -338,6 +342,7 @@ void Model::build_rope(uint32_t len) {
 }
 
 void Model::set_state(int position, int kv_len, int n_tokens) {
+  ++mk_launches_;  // the state kernel advances the epoch too
   check(launch_set_state(st_, position, kv_len, n_tokens, stream_), "set state");
 }
 
@@ -385,6 +390,10 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
     a.st = st_;
     a.gen_mode = gen_mode_;
     a.vocab_off = int(vocab_off_);
+    a.peers = peers_dev_;
+    a.tp_rank = int(rank_);
+    a.tp_size = int(tp_);
+    a.peer_phase = peer_phase_;
     a.pen_cnt = pen_cnt_;
     a.pen_cnt_w = pen_cnt_;
     a.rep = rep_;
@@ -426,7 +435,11 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
   }
 }
 
-void Model::enqueue_layers(int T) {
+void Model::enqueue_layers(int T, bool decode) {
+  // decode steps of a connected tensor-parallel group exchange partial sums by
+  // peer stores; prefill chunks and forward() use NCCL (whose collectives also
+  // order the ranks before the first peer store of a session)
+  const bool peer = tp_ > 1 && p2p_ && decode && T == 1;
   const ModelConfig& c = cfg_;
   const int H = int(c.hidden), hd = int(c.head_dim());
   const int HQ = int(hq_), FL = int(ffn_l_);
@@ -467,6 +480,11 @@ void Model::enqueue_layers(int T) {
     const DevWeight o[1] = {L.o};
     if (tp_ == 1) {
       gemv(o, 1, HQ, T, att_, HQ, nullptr, 0.0f, PRO_NONE, EPI_RESID, h_, H, x_, H, nullptr, 0, -1, 0);
+    } else if (peer) {
+      peer_phase_ = int(2 * l);
+      gemv(o, 1, HQ, T, att_, HQ, nullptr, 0.0f, PRO_NONE, EPI_PEER, nullptr, H, nullptr, 0, nullptr, 0, -1, 0);
+      check(launch_tp_reduce_add(h_, x_, recv_, int(tp_), size_t(H), int(2 * l), st_, stream_), "peer reduce");
+      launches_ += 1;
     } else {
       gemv(o, 1, HQ, T, att_, HQ, nullptr, 0.0f, PRO_NONE, EPI_STORE, part_y_, H, nullptr, 0, nullptr, 0, -1, 0);
       all_reduce_sum(part_y_, size_t(T) * H);
@@ -480,6 +498,11 @@ void Model::enqueue_layers(int T) {
     const DevWeight dn[1] = {L.down};
     if (tp_ == 1) {
       gemv(dn, 1, FL, T, act_, FL, nullptr, 0.0f, PRO_NONE, EPI_RESID, x_, H, h_, H, nullptr, 0, -1, 0);
+    } else if (peer) {
+      peer_phase_ = int(2 * l + 1);
+      gemv(dn, 1, FL, T, act_, FL, nullptr, 0.0f, PRO_NONE, EPI_PEER, nullptr, H, nullptr, 0, nullptr, 0, -1, 0);
+      check(launch_tp_reduce_add(x_, h_, recv_, int(tp_), size_t(H), int(2 * l + 1), st_, stream_), "peer reduce");
+      launches_ += 1;
     } else {
       gemv(dn, 1, FL, T, act_, FL, nullptr, 0.0f, PRO_NONE, EPI_STORE, part_y_, H, nullptr, 0, nullptr, 0, -1, 0);
       all_reduce_sum(part_y_, size_t(T) * H);
@@ -515,7 +538,44 @@ void Model::enqueue_forward(const uint32_t* dev_ids, int T, bool from_hist) {
   if (from_hist) check(launch_embed_last(emb_, int(cfg_.vocab), int(cfg_.hidden), hist_, x_, st_, stream_), "embed");
   else check(launch_embed(emb_, int(cfg_.vocab), int(cfg_.hidden), dev_ids, T, x_, st_, stream_), "embed");
   ++launches_;
-  enqueue_layers(T);
+  enqueue_layers(T, from_hist);
+}
+
+void Model::tp_ipc_handle(void* out) const {
+  if (tp_ < 2) throw WcbError(E_INVALID, "Invalid argument: the model is not tensor-parallel");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, recv_);
+  if (e != cudaSuccess) throw WcbError(E_BACKEND, std::string("Backend error: cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  std::memcpy(out, &h, sizeof(h));
+}
+
+void Model::tp_connect(const uint8_t* handles, uint32_t n) {
+  if (tp_ < 2 || n != tp_) throw WcbError(E_INVALID, "Invalid argument: one IPC handle per tensor-parallel rank");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  std::vector<unsigned long long*> ptrs(tp_);
+  for (uint32_t r = 0; r < tp_; ++r) {
+    if (r == rank_) {
+      ptrs[r] = recv_;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handles + 64 * size_t(r), sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess)
+      throw WcbError(E_BACKEND, std::string("Backend error: cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+    ipc_opened_.push_back(p);
+    ptrs[r] = static_cast<unsigned long long*>(p);
+  }
+  check(cudaMemcpy(peers_dev_, ptrs.data(), sizeof(void*) * tp_, cudaMemcpyHostToDevice), "peer table");
+  p2p_ = true;
+  if (decode_exec_) {  // re-capture the decode step with the peer exchange
+    cudaGraphExecDestroy(decode_exec_);
+    cudaGraphDestroy(decode_graph_);
+    decode_exec_ = nullptr;
+    decode_graph_ = nullptr;
+  }
 }
 
 void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logits_out) {

@@ -70,6 +70,10 @@ class Model {
   void start(const uint32_t* prompt, size_t n, const GenParams& g);
   std::vector<uint32_t> next(size_t max_tokens, bool* finished);
   uint64_t session_id() const { return session_; }
+  // tensor parallelism: the IPC handle of this rank's receive buffer, and the
+  // handles of every rank's (in rank order) to write partial sums into peers
+  void tp_ipc_handle(void* out) const;
+  void tp_connect(const uint8_t* handles, uint32_t n);
   // kernels launched by one greedy decode step
   int launches_per_decode_step() const { return launches_per_step_; }
 
@@ -85,7 +89,7 @@ class Model {
   void* dalloc(size_t bytes);
   void set_state(int position, int kv_len, int n_tokens);
   void enqueue_forward(const uint32_t* dev_ids, int T, bool from_hist);
-  void enqueue_layers(int T);
+  void enqueue_layers(int T, bool decode = false);
   void enqueue_lm_head(int T, bool gen);
   void gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, int ldx, const float* norm_w, float eps,
             int pro, int epi, float* y, int ldy, const float* resid, int ldr, float* q, int ldq, int layer,
@@ -108,6 +112,13 @@ class Model {
   ncclComm_t comm_ = nullptr;
   float* part_y_ = nullptr;                 // [t_max][hidden] partial o / down outputs
   unsigned long long* tpkey_ = nullptr;    // argmax key and NaN flag exchanged by the LM head
+  // decode steps exchange o / down partial sums by stores into every rank's
+  // receive buffer [tp][hidden] of tagged values (CUDA IPC over NVLink)
+  unsigned long long* recv_ = nullptr;
+  unsigned long long** peers_dev_ = nullptr;  // [tp] device pointers to every rank's recv_
+  std::vector<void*> ipc_opened_;
+  bool p2p_ = false;
+  int peer_phase_ = 0;  // tag phase of the partial sums of the GEMV being enqueued
   int device_ = 0;
   cudaStream_t stream_ = nullptr;
   std::vector<void*> allocs_;

@@ -34,7 +34,7 @@ EXPORTED = [
     "wcb_sampler_sample", "wcb_sampler_free", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
     "wcb_repack_q6k_dev", "wcb_gemv_dev", "wcb_model_stream", "wcb_infer", "wcb_next_tokens",
     "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_attention_dev",
-    "wcb_attention_dev_noalloc", "wcb_tp_id",
+    "wcb_attention_dev_noalloc", "wcb_tp_id", "wcb_model_tp_handle", "wcb_model_tp_connect",
 ]
 
 
@@ -121,6 +121,8 @@ def lib() -> C.CDLL:
     L.wcb_attention_dev.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     L.wcb_attention_dev_noalloc.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     L.wcb_tp_id.argtypes = [vp]
+    L.wcb_model_tp_handle.argtypes = [u32, vp]
+    L.wcb_model_tp_connect.argtypes = [u32, vp, u32]
     for name in EXPORTED:
         f = getattr(L, name)
         if f.restype is C.c_int and name != "wcb_next_token":  # ctypes default
@@ -283,6 +285,19 @@ class Model:
         s = C.c_uint32(0)
         _check(lib().wcb_infer(self._h, ids.ctypes.data, ids.size, C.byref(c), C.byref(s)))
         return TokenStream(s.value)
+
+    def tp_ipc_handle(self) -> bytes:
+        """This rank's receive-buffer IPC handle (64 bytes) for tp_connect."""
+        buf = (C.c_uint8 * 64)()
+        _check(lib().wcb_model_tp_handle(self._h, buf))
+        return bytes(buf)
+
+    def tp_connect(self, handles) -> None:
+        """Every rank's tp_ipc_handle() in rank order: decode steps then exchange
+        partial sums by peer stores instead of NCCL."""
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _check(lib().wcb_model_tp_connect(self._h, buf, len(handles)))
 
     def launches_per_step(self) -> int:
         n = C.c_uint32(0)
