@@ -35,6 +35,9 @@ import numpy as np  # noqa: E402
 MODEL_DIR = os.environ.get("WCB_MODEL_DIR", "/tmp/wcb_models")
 PROMPT_LEN = 128
 METRIC = "decode tok/s (TinyLlama-1.1B Q4_K, batch 1)"
+# --model llama7b: the Llama-2-7B shape with the Q4_K_M mix, 512-token prompt (not the headline)
+MODELS = {"tinyllama": ("TinyLlama-1.1B Q4_K", "tinyllama-1.1b-arch", 128),
+          "llama7b": ("Llama-2-7B Q4_K_M", "llama-2-7b-arch", 512)}
 
 
 def peaks():
@@ -109,12 +112,12 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def ensure_model(rank, world, dist):
+def ensure_model(rank, world, dist, preset="tinyllama"):
     from wcb import synth
-    path = os.path.join(MODEL_DIR, "wcb_tinyllama.gguf")
+    path = os.path.join(MODEL_DIR, f"wcb_{preset}.gguf")
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if local == 0:
-        synth.cached_model("tinyllama", MODEL_DIR)
+        synth.cached_model(preset, MODEL_DIR)
     if world > 1:
         dist.barrier()
     return path
@@ -227,7 +230,10 @@ def run_ours(args, rank, world, dist):
     import wcb
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    path = ensure_model(rank, world, dist)
+    global PROMPT_LEN, METRIC
+    label, arch, PROMPT_LEN = MODELS[args.model]
+    METRIC = f"decode tok/s ({label}, batch 1)"
+    path = ensure_model(rank, world, dist, args.model)
     m = wcb.Model.load_from_gguf(path, device=local)
     cfg = m.config
     sp = m.stream()
@@ -283,8 +289,8 @@ def run_ours(args, rank, world, dist):
     e2e_ms = float(et.item())
     e2e = {"value": world * len(out) / (e2e_ms * 1e-3), "unit": "tok/s",
            "h2d_bytes_per_step": PROMPT_LEN * 4 / len(out), "d2h_bytes_per_step": 4 + 64 / len(out),
-           "call": "wcb_generate_tokens: 128-token prompt from host memory -> %d generated ids to host memory, "
-                   "prefill included" % len(out)}
+           "call": "wcb_generate_tokens: %d-token prompt from host memory -> %d generated ids to host memory, "
+                   "prefill included" % (PROMPT_LEN, len(out))}
 
     roof = gemv_roofline(torch, wcb, sp, cfg, peak) if rank == 0 else None
     if m.launches_per_step() == 1:
@@ -307,11 +313,12 @@ def run_ours(args, rank, world, dist):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 activations, Q4_K weights (int8 dp4a on exact 24-bit activation limbs)",
-            "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K; 128 uniform-random prompt ids)",
-            "config": {"workload": "TinyLlama-1.1B Q4_K greedy decode after a 128-token prompt, batch 1 per GPU",
-                       "model": "tinyllama-1.1b-arch", "prompt_len": PROMPT_LEN, "global_batch": world,
+            "data": f"synthetic (seeded N(0,0.02) weights quantised to {label.split()[-1]}; "
+                    f"{PROMPT_LEN} uniform-random prompt ids)",
+            "config": {"workload": f"{label} greedy decode after a {PROMPT_LEN}-token prompt, batch 1 per GPU",
+                       "model": arch, "prompt_len": PROMPT_LEN, "global_batch": world,
                        "seq_len": PROMPT_LEN + 1 + W + K, "parallelism": f"dp{world} (independent replicas)",
-                       "l2": "weights 582 MB > 126 MB L2, no flush", "kv_cache": "f32",
+                       "l2": f"weights {wbytes / 1e6:.0f} MB > 126 MB L2, no flush", "kv_cache": "f32",
                        "cuda_graph": m.launches_per_step() > 1},
             "roofline": roofline,
             "step_roofline": {"bytes_per_step": step_bytes, "weight_bytes": wbytes, "achieved_gbs": step_gbs,
@@ -412,6 +419,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv-only", type=int, default=0, metavar="REPS",
                     help="only time the dominant GEMV (REPS launches per weight copy) and print its line")
+    ap.add_argument("--model", choices=sorted(MODELS), default="tinyllama",
+                    help="the decoder shape of the decode line (the headline is tinyllama)")
     ap.add_argument("--tp", action="store_true",
                     help="the Llama-2-70B shape, tensor-parallel over the torchrun ranks, instead of the headline")
     ap.add_argument("--layers", type=int, default=80, help="--tp: layers of the 70B shape to build")
