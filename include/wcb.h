@@ -117,12 +117,22 @@ uint32_t wcb_kv_len(uint32_t handle, size_t* out_len);
 uint32_t wcb_generate_tokens(uint32_t handle, const uint32_t* prompt, size_t n, const wcb_gen_config* cfg,
                              uint32_t* out, size_t cap, size_t* n_out);
 
-/* Data-parallel serving: n_seq independent generate() runs batched through one
- * replica (each sequence has its own KV cache and sampler). prompts holds the
- * n_seq prompts back to back with lengths lens[]; out is n_seq x cap;
- * n_out receives n_seq counts. n_seq <= wcb_load_opts.max_batch. */
+/* Data-parallel serving: n_seq independent generate() runs through one replica
+ * (each sequence has its own KV cache and sampler), each result equal to that
+ * sequence's wcb_generate_tokens result. prompts holds the n_seq prompts back
+ * to back with lengths lens[]; out is n_seq x cap; n_out receives n_seq counts.
+ * Greedy configs on a model loaded with max_batch > 1 prefill the sequences
+ * one by one into their own KV slots, then run their decode steps together,
+ * min(max_batch, 32) sequences per batched step (the weights are read once per
+ * step for all of them); otherwise the sequences run one after the other.
+ * Replaces the reference's one-sequence-at-a-time serving loop
+ * (Model::generate, crates/wasm-chord-runtime/src/transformer/model.rs:1322). */
 uint32_t wcb_generate_batch(uint32_t handle, const uint32_t* prompts, const size_t* lens, size_t n_seq,
                             const wcb_gen_config* cfg, uint32_t* out, size_t cap, size_t* n_out);
+
+/* KV slots of one batched decode step (1: no batched path) and the kernels one
+ * batched step launches (0 before the first batched wcb_generate_batch). */
+uint32_t wcb_batch_info(uint32_t handle, uint32_t* slots, uint32_t* launches_per_step);
 
 /* Streaming generation, the token-id form of the reference's wasmchord_infer /
  * wasmchord_next_token / wasmchord_close_stream (abi.rs:119-200, placeholders

@@ -204,13 +204,11 @@ uint32_t wcb_generate_batch(uint32_t h, const uint32_t* prompts, const size_t* l
     if (!cfg || !n_out || !lens || (!out && cap) || !prompts)
       return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
     auto m = get_model(h);
-    size_t off = 0;
+    for (size_t s = 0; s < n_seq; ++s) n_out[s] = 0;
+    const std::vector<std::vector<uint32_t>> toks = m->generate_batch(prompts, lens, n_seq, params_of(cfg));
     for (size_t s = 0; s < n_seq; ++s) {
-      n_out[s] = 0;
-      std::vector<uint32_t> toks = m->generate(prompts + off, lens[s], params_of(cfg));
-      n_out[s] = toks.size();
-      std::memcpy(out + s * cap, toks.data(), sizeof(uint32_t) * std::min(cap, toks.size()));
-      off += lens[s];
+      n_out[s] = toks[s].size();
+      std::memcpy(out + s * cap, toks[s].data(), sizeof(uint32_t) * std::min(cap, toks[s].size()));
     }
     return WCB_OK;
   });
@@ -269,6 +267,16 @@ uint32_t wcb_close_stream(uint32_t sid) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_streams.erase(sid)) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid stream handle");
   return WCB_OK;
+}
+
+uint32_t wcb_batch_info(uint32_t h, uint32_t* slots, uint32_t* launches_per_step) {
+  return guarded([&]() -> uint32_t {
+    if (!slots || !launches_per_step) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    auto m = get_model(h);
+    *slots = m->batch_slots();
+    *launches_per_step = uint32_t(m->launches_per_batch_step());
+    return WCB_OK;
+  });
 }
 
 uint32_t wcb_model_launches_per_step(uint32_t h, uint32_t* out) {

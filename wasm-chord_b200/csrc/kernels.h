@@ -147,6 +147,10 @@ struct AttnArgs {
   int max_splits;
   float scale;        // 1 / sqrt(head_dim)
   const StepState* st;
+  // batched decode: "token" t is sequence t with one query at st[t].position over
+  // its own cache (kc / vc + t * seq_stride elements); 0: the T tokens of one sequence
+  int batch;
+  size_t seq_stride;
 };
 constexpr int ATT_TILE = 32;  // keys staged in shared memory per pass
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
@@ -243,6 +247,65 @@ bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std
 int decode_step_grid();  // CTAs of one launch (one per SM)
 cudaError_t decode_step_configure();
 cudaError_t launch_decode_step(const MkArgs& a, size_t smem, cudaStream_t s);
+
+// ------------------------------------------------ batched decode (serving) --
+// One greedy decode step of B independent sequences (generate_batch): the
+// weight contractions run on the tensor cores (tcgen05.mma, kind::f16) with the
+// 128 weight rows of a tile as the MMA M dimension and the B sequences as N.
+// The 4- / 6-bit quants are integers, exact in fp16, so the A operand is the
+// raw quant and the B operand the activation split into fp16 hi + lo halves;
+// each Q4_K sub-block (32 values) / Q6_K sub-block (16) accumulates into its
+// own TMEM columns and the CUDA cores apply y += d*sc * dot - dmin*m * sum(x).
+// K is split over CTAs for occupancy; the last CTA of a tile sums the slices
+// in slice order (deterministic) and runs the fused epilogue.
+enum BatchEpi { BEPI_STORE = 0, BEPI_RESID = 1, BEPI_SWIGLU = 2, BEPI_QKV = 3 };
+constexpr int BATCH_MAX = 32;   // sequences of one batched step (MMA N <= 32)
+constexpr int BATCH_TILE = 128; // weight rows of one tile (BEPI_SWIGLU: 64 gate + 64 up rows)
+
+struct BatchGemmArgs {
+  GemvSeg seg[3];        // rows of the virtual matrix: seg 0, then 1, then 2 (BEPI_SWIGLU: gate, up)
+  int nseg;
+  int rows;              // virtual rows (BEPI_SWIGLU: gate rows = up rows = outputs)
+  int K;                 // input length, a multiple of 256
+  int B;                 // sequences (1..BATCH_MAX)
+  const float* x;        // [B][ldx]
+  int ldx;
+  const float* norm_w;   // RMSNorm weight of the input (null: no norm)
+  const float* sq_in;    // [sq_tiles][B] partial sums of squares of x (summed in tile order)
+  int sq_tiles;
+  float eps;
+  int splits;            // K slices (set by launch_batch_gemm)
+  int sb_per_split;      // super-blocks per slice (set by launch_batch_gemm)
+  float* part;           // [splits][B][rows] slice results
+  int* ticket;           // [tiles] zero between launches
+  float* y;              // BEPI_STORE / RESID / SWIGLU output [B][ldy]
+  int ldy;
+  const float* resid;    // BEPI_RESID [B][ldr]
+  int ldr;
+  float* sq_out;         // BEPI_RESID: [tiles][B] sums of squares of the tile's outputs
+  // BEPI_QKV: RoPE'd queries to q, RoPE'd keys and values appended to each sequence's cache
+  float* q;
+  int ldq;
+  void* kc;              // this layer's caches of sequence 0 [n_kv][max_seq][hd]
+  void* vc;
+  size_t seq_stride;     // elements from one sequence's cache to the next
+  int kv_half, hidden, kv_dim, head_dim, max_seq;
+  const float* rope_cos;
+  const float* rope_sin;
+  StepState* st;         // [B]
+};
+// tiles and slices of a launch (CTAs = tiles * splits) and its shared memory
+int batch_gemm_tiles(const BatchGemmArgs& a, int epi);
+void batch_gemm_plan(BatchGemmArgs& a, int epi);
+cudaError_t batch_configure();
+cudaError_t launch_batch_gemm(BatchGemmArgs a, int epi, cudaStream_t s);
+// x[b] = embedding row of sequence b's last token; sq[b] = sum of squares of x[b]
+cudaError_t launch_batch_embed(const float* emb, int vocab, int hidden, const StepState* st, const uint32_t* hist,
+                               int hist_cap, float* x, float* sq, int B, cudaStream_t s);
+// per sequence: repetition penalty, argmax (last maximum wins) and generate()'s
+// bookkeeping into st[b], hist + b * hist_cap, pen_cnt + b * vocab
+cudaError_t launch_batch_sample(const float* logits, int vocab, StepState* st, uint32_t* hist, int hist_cap,
+                                uint32_t* pen_cnt, float rep, int B, cudaStream_t s);
 
 // ------------------------------------------------------------ elementwise --
 cudaError_t launch_embed(const float* emb, int vocab, int hidden, const uint32_t* ids, int T, float* x,

@@ -12,6 +12,7 @@ namespace {
 
 constexpr int T_MAX = 256;        // tokens per forward launch (longer prompts are split, same results)
 constexpr int DECODE_CHUNK = 32;  // keys per attention split in decode steps
+constexpr int BATCH_CHUNK = 256;  // keys per attention split in batched decode steps
 
 float f16_to_f32_host(uint16_t h) {
   const uint32_t sign = uint32_t(h & 0x8000u) << 16;
@@ -171,11 +172,20 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
         throw WcbError(E_BACKEND, "Backend error: ffn_gate and ffn_up must share a quantisation type");
     }
 
-    // KV cache (kv_cache.rs:6-34), [L][n_kv][max_seq][hd]
+    // batched decode slots (generate_batch): each holds its own KV cache, state,
+    // sampler history and penalty counts; the tensor-core step needs 128-row
+    // tiles that never straddle q / k / v, and 64-row gate / up halves
+    bslots_ = tp_ == 1 ? std::min<uint32_t>(std::max<uint32_t>(opt.max_batch, 1), BATCH_MAX) : 1;
+    batch_ok_ = bslots_ > 1 && c.hidden % BATCH_TILE == 0 && kvd % BATCH_TILE == 0 && c.ffn % 64 == 0;
+    if (!batch_ok_) bslots_ = 1;
+    // KV cache (kv_cache.rs:6-34), [slot][L][n_kv][max_seq][hd]
     kv_layer_elems_ = size_t(kv_l_) * max_seq_ * hd;
-    const size_t kv_bytes = kv_layer_elems_ * c.layers * (opt.kv_half ? 2 : 4);
+    seq_kv_elems_ = kv_layer_elems_ * c.layers;
+    const size_t kv_bytes = seq_kv_elems_ * bslots_ * (opt.kv_half ? 2 : 4);
     kcache_ = dalloc(kv_bytes);
     vcache_ = dalloc(kv_bytes);
+    kc_base_ = kcache_;
+    vc_base_ = vcache_;
     check(cudaMemset(kcache_, 0, kv_bytes), "clear KV");
     check(cudaMemset(vcache_, 0, kv_bytes), "clear KV");
 
@@ -183,11 +193,13 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     attn_scale_ = 1.0f / std::sqrt(float(hd));  // attention.rs:363
 
     t_max_ = T_MAX;
-    st_ = static_cast<StepState*>(dalloc(sizeof(StepState)));
-    check(cudaMemset(st_, 0, sizeof(StepState)), "clear state");
+    st_ = static_cast<StepState*>(dalloc(sizeof(StepState) * bslots_));
+    check(cudaMemset(st_, 0, sizeof(StepState) * bslots_), "clear state");
+    st_base_ = st_;
     ids_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * std::max<size_t>(max_seq_, 1)));
     hist_cap_ = max_seq_ + 2;
-    hist_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * hist_cap_));
+    hist_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * hist_cap_ * bslots_));
+    hist_base_ = hist_;
     x_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
     h_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
     q_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
@@ -202,14 +214,50 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
       peers_dev_ = static_cast<unsigned long long**>(dalloc(sizeof(void*) * tp_));
     }
     row_m_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_)));
-    pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab));
-    check(cudaMemset(pen_cnt_, 0, sizeof(uint32_t) * c.vocab), "clear penalty counts");
+    pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab * bslots_));
+    check(cudaMemset(pen_cnt_, 0, sizeof(uint32_t) * c.vocab * bslots_), "clear penalty counts");
+    pen_base_ = pen_cnt_;
     // attention partials of one decode token split into DECODE_CHUNK-key pieces
     max_splits_ = int((max_seq_ + DECODE_CHUNK - 1) / DECODE_CHUNK);
     part_ = static_cast<float*>(dalloc(sizeof(float) * size_t(c.heads) * max_splits_ * (hd + 2)));
     ticket_ = static_cast<int*>(dalloc(sizeof(int) * size_t(t_max_) * c.kv_heads));
     check(cudaMemset(ticket_, 0, sizeof(int) * size_t(t_max_) * c.kv_heads), "clear tickets");
     check(cudaMallocHost(&host_ids_, sizeof(uint32_t) * std::max<size_t>(max_seq_, 1)), "cudaMallocHost");
+    if (batch_ok_) {
+      const size_t B = bslots_, H = c.hidden;
+      logits_b_ = static_cast<float*>(dalloc(sizeof(float) * B * c.vocab));
+      sqx_ = static_cast<float*>(dalloc(sizeof(float) * B * (H / BATCH_TILE)));
+      sqh_ = static_cast<float*>(dalloc(sizeof(float) * B * (H / BATCH_TILE)));
+      // K-slice scratch and tickets: the largest need over the step's contractions
+      size_t part = 0;
+      int tiles_max = 0;
+      auto need = [&](int rows, int K, int epi, int dtype) {
+        BatchGemmArgs a{};
+        a.nseg = 1;
+        a.seg[0].dtype = dtype;
+        a.rows = rows;
+        a.K = K;
+        batch_gemm_plan(a, epi);
+        const int tiles = batch_gemm_tiles(a, epi);
+        tiles_max = std::max(tiles_max, tiles);
+        part = std::max(part, size_t(a.splits) * B * size_t(tiles) * BATCH_TILE);
+      };
+      for (int dt : {DT_Q4K, DT_Q6K}) {
+        need(int(c.hidden + 2 * kvd), int(H), BEPI_QKV, dt);
+        need(int(H), int(H), BEPI_RESID, dt);
+        need(int(c.ffn), int(H), BEPI_SWIGLU, dt);
+        need(int(H), int(c.ffn), BEPI_RESID, dt);
+        need(int(c.vocab), int(H), BEPI_STORE, dt);
+      }
+      bpart_ = static_cast<float*>(dalloc(sizeof(float) * part));
+      bticket_ = static_cast<int*>(dalloc(sizeof(int) * size_t(tiles_max)));
+      check(cudaMemset(bticket_, 0, sizeof(int) * size_t(tiles_max)), "clear tickets");
+      asplits_ = int((max_seq_ + BATCH_CHUNK - 1) / BATCH_CHUNK);
+      apart_ = static_cast<float*>(dalloc(sizeof(float) * B * c.heads * size_t(asplits_) * (hd + 2)));
+      aticket_ = static_cast<int*>(dalloc(sizeof(int) * B * c.kv_heads));
+      check(cudaMemset(aticket_, 0, sizeof(int) * B * c.kv_heads), "clear tickets");
+      check(batch_configure(), "batched decode configure");
+    }
     build_decode_step();
     check(cudaDeviceSynchronize(), "load");
   } catch (...) {
@@ -230,6 +278,8 @@ Model::~Model() {
   if (stream_) cudaStreamSynchronize(stream_);
   if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
   if (decode_graph_) cudaGraphDestroy(decode_graph_);  // graphs holding NCCL calls go before the comm
+  if (batch_exec_) cudaGraphExecDestroy(batch_exec_);
+  if (batch_graph_) cudaGraphDestroy(batch_graph_);
   if (comm_) nccl().CommDestroy(comm_);
   for (void* p : ipc_opened_) cudaIpcCloseMemHandle(p);
   for (void* p : allocs_) cudaFree(p);
@@ -877,23 +927,8 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   }
   // greedy: the decode loop runs on the device (argmax + repetition penalty +
   // EOS / max_tokens bookkeeping in the sampler kernel), no host round trip per token
-  if (n > max_seq_)
-    throw WcbError(E_PARSE, "Parse error: KV cache overflow: 0 + " + std::to_string(n) + " > " +
-                                std::to_string(max_seq_));
-  const int eos = g.eos == 0xFFFFFFFFu ? -1 : int(g.eos);
-  check(launch_init_gen(st_, int(std::max<uint32_t>(g.max_tokens, 1)), eos, int(max_seq_), stream_), "init");
-  check(cudaMemsetAsync(pen_cnt_, 0, sizeof(uint32_t) * cfg_.vocab, stream_), "clear penalty counts");
+  prefill_greedy(prompt, n, g);
   const float rep = g.repetition_penalty;
-  rep_ = rep;
-  std::memcpy(host_ids_, prompt, n * sizeof(uint32_t));
-  check(cudaMemcpyAsync(ids_, host_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "upload ids");
-  for (size_t c0 = 0; c0 < n; c0 += size_t(t_max_)) {
-    const int T = int(std::min(n - c0, size_t(t_max_)));
-    set_state(int(c0), int(c0), T);
-    enqueue_forward(ids_ + c0, T, false);
-  }
-  const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
-  enqueue_lm_head(last_T, true);  // samples the first token (no EOS check)
   if (mk_ok_) {
     // tickets of a step that ended on an error are cleared here
     check(cudaMemsetAsync(mk_.ticket, 0, sizeof(int) * size_t(mk_.n_kv), stream_), "clear tickets");
@@ -987,6 +1022,243 @@ std::vector<uint32_t> Model::generate(const uint32_t* prompt, size_t n, const Ge
     if (part.empty() && !fin) break;
   }
   return all;
+}
+
+}  // namespace wcb
+
+namespace wcb {
+
+void Model::prefill_greedy(const uint32_t* prompt, size_t n, const GenParams& g) {
+  if (n > max_seq_)
+    throw WcbError(E_PARSE, "Parse error: KV cache overflow: 0 + " + std::to_string(n) + " > " +
+                                std::to_string(max_seq_));
+  const int eos = g.eos == 0xFFFFFFFFu ? -1 : int(g.eos);
+  check(launch_init_gen(st_, int(std::max<uint32_t>(g.max_tokens, 1)), eos, int(max_seq_), stream_), "init");
+  check(cudaMemsetAsync(pen_cnt_, 0, sizeof(uint32_t) * cfg_.vocab, stream_), "clear penalty counts");
+  rep_ = g.repetition_penalty;
+  check(cudaStreamSynchronize(stream_), "prefill");  // the pinned staging buffer is free again
+  std::memcpy(host_ids_, prompt, n * sizeof(uint32_t));
+  check(cudaMemcpyAsync(ids_, host_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "upload ids");
+  for (size_t c0 = 0; c0 < n; c0 += size_t(t_max_)) {
+    const int T = int(std::min(n - c0, size_t(t_max_)));
+    set_state(int(c0), int(c0), T);
+    enqueue_forward(ids_ + c0, T, false);
+  }
+  const int last_T = int(n - ((n - 1) / size_t(t_max_)) * size_t(t_max_));
+  enqueue_lm_head(last_T, true);  // samples the first token (no EOS check)
+}
+
+void Model::bind_seq(uint32_t b) {
+  const size_t esz = opt_.kv_half ? 2 : 4;
+  kcache_ = static_cast<uint8_t*>(kc_base_) + size_t(b) * seq_kv_elems_ * esz;
+  vcache_ = static_cast<uint8_t*>(vc_base_) + size_t(b) * seq_kv_elems_ * esz;
+  st_ = st_base_ + b;
+  hist_ = hist_base_ + size_t(b) * hist_cap_;
+  pen_cnt_ = pen_base_ + size_t(b) * cfg_.vocab;
+}
+
+void Model::batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, const float* x, int ldx,
+                       const float* norm_w, const float* sq_in, int sq_tiles, float eps, int epi, float* y, int ldy,
+                       const float* resid, int ldr, float* sq_out, int layer) {
+  BatchGemmArgs a{};
+  for (int i = 0; i < nseg; ++i) {
+    a.seg[i].w = segs[i].ptr;
+    a.seg[i].dtype = segs[i].dtype;
+    a.seg[i].rows = int(segs[i].rows);
+  }
+  a.nseg = nseg;
+  a.rows = rows;
+  a.K = K;
+  a.B = B;
+  a.x = x;
+  a.ldx = ldx;
+  a.norm_w = norm_w;
+  a.sq_in = sq_in;
+  a.sq_tiles = sq_tiles;
+  a.eps = eps;
+  a.part = bpart_;
+  a.ticket = bticket_;
+  a.y = y;
+  a.ldy = ldy;
+  a.resid = resid;
+  a.ldr = ldr;
+  a.sq_out = sq_out;
+  a.q = q_;
+  a.ldq = int(hq_);
+  if (layer >= 0) {
+    const size_t esz = opt_.kv_half ? 2 : 4;
+    a.kc = static_cast<uint8_t*>(kc_base_) + size_t(layer) * kv_layer_elems_ * esz;
+    a.vc = static_cast<uint8_t*>(vc_base_) + size_t(layer) * kv_layer_elems_ * esz;
+  }
+  a.seq_stride = seq_kv_elems_;
+  a.kv_half = int(opt_.kv_half);
+  a.hidden = int(hq_);
+  a.kv_dim = int(kvd_l_);
+  a.head_dim = int(cfg_.head_dim());
+  a.max_seq = int(max_seq_);
+  a.rope_cos = rope_cos_;
+  a.rope_sin = rope_sin_;
+  a.st = st_base_;
+  check(launch_batch_gemm(a, epi, stream_), "batched GEMM");
+  ++batch_launches_;
+}
+
+// One greedy decode step of slots 0..B-1 (the per-sequence semantics of the
+// decode step in enqueue_forward + enqueue_lm_head): every contraction reads
+// its weights once for all B sequences.
+void Model::enqueue_batch_step(int B) {
+  const ModelConfig& c = cfg_;
+  const int H = int(c.hidden), F = int(ffn_l_), HQ = int(hq_), V = int(c.vocab);
+  const int qkv_rows = HQ + 2 * int(kvd_l_);
+  const int res_tiles = H / BATCH_TILE;
+  batch_launches_ = 0;
+  check(launch_batch_embed(emb_, V, H, st_base_, hist_base_, int(hist_cap_), x_, sqx_, B, stream_), "embed");
+  ++batch_launches_;
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    const DevLayer& L = layers_[l];
+    const int sq_tiles = l == 0 ? 1 : res_tiles;  // layer 0 reads the embedding's whole-row sums
+    const DevWeight qkv[3] = {L.q, L.k, L.v};
+    batch_gemm(qkv, 3, qkv_rows, H, B, x_, H, L.attn_norm, sqx_, sq_tiles, 1e-6f, BEPI_QKV, nullptr, 0, nullptr, 0,
+               nullptr, int(l));
+    AttnArgs a{};
+    a.q = q_;
+    const size_t esz = opt_.kv_half ? 2 : 4;
+    a.kc = static_cast<uint8_t*>(kc_base_) + size_t(l) * kv_layer_elems_ * esz;
+    a.vc = static_cast<uint8_t*>(vc_base_) + size_t(l) * kv_layer_elems_ * esz;
+    a.kv_half = int(opt_.kv_half);
+    a.out = att_;
+    a.part = apart_;
+    a.ticket = aticket_;
+    a.n_heads = int(heads_l_);
+    a.n_kv = int(kv_l_);
+    a.head_dim = int(c.head_dim());
+    a.max_seq = int(max_seq_);
+    a.T = B;
+    a.chunk = BATCH_CHUNK;
+    a.max_splits = asplits_;
+    a.scale = attn_scale_;
+    a.st = st_base_;
+    a.batch = 1;
+    a.seq_stride = seq_kv_elems_;
+    check(launch_attention(a, stream_), "attention");
+    ++batch_launches_;
+    const DevWeight o[1] = {L.o};
+    batch_gemm(o, 1, H, HQ, B, att_, HQ, nullptr, nullptr, 0, 0.0f, BEPI_RESID, h_, H, x_, H, sqh_, -1);
+    const DevWeight gu[2] = {L.gate, L.up};
+    batch_gemm(gu, 2, F, H, B, h_, H, L.ffn_norm, sqh_, res_tiles, 1e-6f, BEPI_SWIGLU, act_, F, nullptr, 0, nullptr,
+               -1);
+    const DevWeight dn[1] = {L.down};
+    batch_gemm(dn, 1, H, F, B, act_, F, nullptr, nullptr, 0, 0.0f, BEPI_RESID, x_, H, h_, H, sqx_, -1);
+  }
+  const DevWeight head[1] = {lm_head_};
+  batch_gemm(head, 1, V, H, B, x_, H, out_norm_, sqx_, c.layers ? res_tiles : 1, c.eps, BEPI_STORE, logits_b_, V,
+             nullptr, 0, nullptr, -1);
+  check(launch_batch_sample(logits_b_, V, st_base_, hist_base_, int(hist_cap_), pen_base_, rep_, B, stream_),
+        "sampler");
+  ++batch_launches_;
+}
+
+std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts, const size_t* lens, size_t n,
+                                                         const GenParams& g) {
+  std::vector<std::vector<uint32_t>> out(n);
+  const Sampler probe(g.seed, g.temperature, g.top_p, g.top_k, g.repetition_penalty);
+  if (!batch_ok_ || !probe.greedy() || n < 2) {
+    size_t off = 0;
+    for (size_t s = 0; s < n; ++s) {
+      out[s] = generate(prompts + off, lens[s], g);
+      off += lens[s];
+    }
+    return out;
+  }
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  ++session_;  // slot 0 is the single-sequence KV cache: an open session ends here
+  sess_active_ = false;
+  sess_done_ = true;
+  kv_len_ = 0;
+  std::vector<size_t> offs(n, 0);
+  for (size_t s = 1; s < n; ++s) offs[s] = offs[s - 1] + lens[s - 1];
+  for (size_t s = 0; s < n; ++s)
+    if (lens[s] == 0) throw WcbError(E_PARSE, "Parse error: Empty token sequence");
+  std::vector<StepState> hs(bslots_);
+  for (size_t g0 = 0; g0 < n; g0 += bslots_) {
+    const int B = int(std::min<size_t>(bslots_, n - g0));
+    try {
+      for (int b = 0; b < B; ++b) {
+        bind_seq(uint32_t(b));
+        prefill_greedy(prompts + offs[g0 + b], lens[g0 + b], g);
+      }
+    } catch (...) {
+      bind_seq(0);
+      throw;
+    }
+    bind_seq(0);
+    if (!batch_exec_ || batch_graph_b_ != B || batch_graph_rep_ != rep_) {
+      if (batch_exec_) {
+        cudaGraphExecDestroy(batch_exec_);
+        cudaGraphDestroy(batch_graph_);
+        batch_exec_ = nullptr;
+        batch_graph_ = nullptr;
+      }
+      cudaGraph_t gr = nullptr;
+      check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+      try {
+        enqueue_batch_step(B);
+      } catch (...) {
+        cudaStreamEndCapture(stream_, &gr);
+        if (gr) cudaGraphDestroy(gr);
+        throw;
+      }
+      check(cudaStreamEndCapture(stream_, &gr), "end capture");
+      cudaGraphExec_t e = nullptr;
+      const cudaError_t r = cudaGraphInstantiate(&e, gr, 0);
+      if (r != cudaSuccess) {
+        cudaGraphDestroy(gr);
+        check(r, "graph instantiate");
+      }
+      batch_graph_ = gr;
+      batch_exec_ = e;
+      batch_graph_b_ = B;
+      batch_graph_rep_ = rep_;
+    }
+    // decode steps for the whole group; finished sequences are skipped by the
+    // sampler and their KV caches are no longer written
+    size_t steps_left = g.max_tokens > 1 ? size_t(g.max_tokens) - 1 : 0;
+    auto read_states = [&]() {
+      check(cudaMemcpyAsync(hs.data(), st_base_, sizeof(StepState) * size_t(B), cudaMemcpyDeviceToHost, stream_),
+            "read states");
+      check(cudaStreamSynchronize(stream_), "batched decode");
+      for (int b = 0; b < B; ++b) {
+        if (hs[b].err & 12)
+          throw WcbError(E_BACKEND, "Backend error: batched decode: a bounded wait expired (device error word " +
+                                        std::to_string(hs[b].err) + ")");
+        if (hs[b].err == 1) throw WcbError(E_GENERIC, "Runtime error: NaN logit");
+      }
+    };
+    read_states();
+    auto all_done = [&]() {
+      for (int b = 0; b < B; ++b)
+        if (!hs[b].done) return false;
+      return true;
+    };
+    while (steps_left > 0 && !all_done()) {
+      const size_t k = std::min<size_t>(steps_left, 16);
+      for (size_t i = 0; i < k; ++i) check(cudaGraphLaunch(batch_exec_, stream_), "graph launch");
+      steps_left -= k;
+      read_states();
+    }
+    for (int b = 0; b < B; ++b) {
+      if (hs[b].err == 2)  // the KV append of a further step would overflow (kv_cache.rs:48-53)
+        throw WcbError(E_PARSE, "Parse error: KV cache overflow: " + std::to_string(hs[b].kv_len) + " + 1 > " +
+                                    std::to_string(max_seq_));
+      std::vector<uint32_t>& o = out[g0 + size_t(b)];
+      o.resize(size_t(hs[b].nhist));
+      if (!o.empty())
+        check(cudaMemcpy(o.data(), hist_base_ + size_t(b) * hist_cap_, sizeof(uint32_t) * o.size(),
+                         cudaMemcpyDeviceToHost),
+              "read tokens");
+    }
+  }
+  return out;
 }
 
 }  // namespace wcb

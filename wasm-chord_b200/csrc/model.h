@@ -76,6 +76,17 @@ class Model {
   void tp_connect(const uint8_t* handles, uint32_t n);
   // kernels launched by one greedy decode step
   int launches_per_decode_step() const { return launches_per_step_; }
+  // generate() for n independent sequences. Greedy decoding with room for
+  // several sequences (LoadOptions::max_batch > 1) prefills each sequence into
+  // its own KV cache and then runs their decode steps together, up to
+  // BATCH_MAX at a time, on the tensor cores; otherwise the sequences run one
+  // after the other. Each result is the sequence's generate() result.
+  std::vector<std::vector<uint32_t>> generate_batch(const uint32_t* prompts, const size_t* lens, size_t n,
+                                                    const GenParams& g);
+  // sequences one batched decode step can hold (1: no batched path)
+  uint32_t batch_slots() const { return batch_ok_ ? bslots_ : 1; }
+  // kernels launched by one batched decode step (0 before the first batched call)
+  int launches_per_batch_step() const { return batch_launches_; }
 
  private:
   // rows [row0, row0 + nrows) and 256-value blocks [blk0, blk0 + nblk) of a
@@ -97,6 +108,16 @@ class Model {
   void check(cudaError_t e, const char* what);
   void decode_steps(int steps);
   void capture_decode_graph();
+  // greedy prefill of one sequence into the bound KV cache / state, sampling
+  // its first token on the device (start()'s greedy path)
+  void prefill_greedy(const uint32_t* prompt, size_t n, const GenParams& g);
+  // points the per-sequence state (KV cache, StepState, history, penalty
+  // counts) at batch slot b; slot 0 is the single-sequence state
+  void bind_seq(uint32_t b);
+  void enqueue_batch_step(int B);
+  void batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, const float* x, int ldx,
+                  const float* norm_w, const float* sq_in, int sq_tiles, float eps, int epi, float* y, int ldy,
+                  const float* resid, int ldr, float* sq_out, int layer);
   void build_decode_step();
   void launch_decode_step_kernel(bool gen);
 
@@ -183,6 +204,30 @@ class Model {
   unsigned long long* mk_tagged_ = nullptr;  // tagged activation buffers (one allocation)
   size_t mk_tagged_n_ = 0;
   uint32_t mk_launches_ = 0;
+
+  // batched decode (generate_batch): per-slot state lives in bslots_-long arrays
+  // whose slot 0 is the single-sequence state above
+  bool batch_ok_ = false;
+  uint32_t bslots_ = 1;
+  size_t seq_kv_elems_ = 0;     // KV elements of one sequence (all layers)
+  void* kc_base_ = nullptr;     // slot 0 caches
+  void* vc_base_ = nullptr;
+  StepState* st_base_ = nullptr;
+  uint32_t* hist_base_ = nullptr;
+  uint32_t* pen_base_ = nullptr;
+  float* logits_b_ = nullptr;   // [bslots][vocab]
+  float* sqx_ = nullptr;        // [hidden / 128][bslots] sums of squares of the residual stream x
+  float* sqh_ = nullptr;        // the same for h (after attention)
+  float* bpart_ = nullptr;      // K-slice partial sums of the batched GEMMs
+  int* bticket_ = nullptr;
+  float* apart_ = nullptr;      // attention split partials [bslots][heads][asplits][hd + 2]
+  int* aticket_ = nullptr;      // [bslots][kv_heads]
+  int asplits_ = 0;
+  int batch_launches_ = 0;
+  int batch_graph_b_ = 0;
+  float batch_graph_rep_ = -1.0f;
+  cudaGraphExec_t batch_exec_ = nullptr;
+  cudaGraph_t batch_graph_ = nullptr;
 
   cudaGraphExec_t decode_exec_ = nullptr;
   cudaGraph_t decode_graph_ = nullptr;

@@ -11,7 +11,7 @@ from __future__ import annotations
 import ctypes as C
 import dataclasses
 import os
-from typing import List, Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -33,7 +33,7 @@ EXPORTED = [
     "wcb_clear_kv", "wcb_kv_len", "wcb_generate_tokens", "wcb_generate_batch", "wcb_sampler_new",
     "wcb_sampler_sample", "wcb_sampler_free", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
     "wcb_repack_q6k_dev", "wcb_gemv_dev", "wcb_model_stream", "wcb_infer", "wcb_next_tokens",
-    "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_attention_dev",
+    "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_batch_info", "wcb_attention_dev",
     "wcb_attention_dev_noalloc", "wcb_tp_id", "wcb_model_tp_handle", "wcb_model_tp_connect",
 ]
 
@@ -118,6 +118,7 @@ def lib() -> C.CDLL:
     L.wcb_next_token.restype = C.c_int32
     L.wcb_close_stream.argtypes = [u32]
     L.wcb_model_launches_per_step.argtypes = [u32, C.POINTER(u32)]
+    L.wcb_batch_info.argtypes = [u32, C.POINTER(u32), C.POINTER(u32)]
     L.wcb_attention_dev.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     L.wcb_attention_dev_noalloc.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     L.wcb_tp_id.argtypes = [vp]
@@ -298,6 +299,12 @@ class Model:
         blob = b"".join(handles)
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         _check(lib().wcb_model_tp_connect(self._h, buf, len(handles)))
+
+    def batch_info(self) -> Tuple[int, int]:
+        """(KV slots of one batched decode step, kernels one batched step launches)."""
+        slots, launches = C.c_uint32(0), C.c_uint32(0)
+        _check(lib().wcb_batch_info(self._h, C.byref(slots), C.byref(launches)))
+        return int(slots.value), int(launches.value)
 
     def launches_per_step(self) -> int:
         n = C.c_uint32(0)
