@@ -34,27 +34,28 @@
 namespace wcb {
 namespace {
 
-constexpr int BD_THREADS = 128;
-constexpr int BD_STEP = 128;                    // K values per MMA round (half a super-block)
-constexpr int BD_A_BYTES = BATCH_TILE * BD_STEP * 2;  // fp16 A tile of one round (32 KB)
+constexpr int BD_THREADS = 256;                        // 8 warps: two threads per weight row
+constexpr int BD_A_BYTES = BATCH_TILE * QK_K * 2;      // fp16 quants of one super-block (64 KB)
 constexpr int BD_LBO_A = (BATCH_TILE / 8) * 128;       // next 8-column K chunk of A (2048 B)
+constexpr int BD_MAX_SPLITS = 8;                       // K slices of a tile = CTAs of one cluster
 
 // shared-memory carve-up of one CTA (NB = MMA N)
 template <int NB>
 struct BdLayout {
-  static constexpr int X_BYTES = NB * BD_STEP * 2;      // one fp16 half of the activations
-  static constexpr int A_OFF = 0;
+  static constexpr int X_BYTES = NB * QK_K * 2;             // one fp16 half of a super-block's activations
+  static constexpr int CP = NB + 1;                         // padded row of the result slice
+  static constexpr int A_OFF = 0;                           // A tile; then the K-slice result
   static constexpr int XH_OFF = A_OFF + BD_A_BYTES;
   static constexpr int XL_OFF = XH_OFF + X_BYTES;
-  static constexpr int XS_OFF = XL_OFF + X_BYTES;           // float [4][NB] Q4_K sub-block sums of x
-  static constexpr int CS_OFF = XS_OFF + 4 * NB * 4;        // float [NB][16] sums of 8-value chunks
-  static constexpr int RM_OFF = CS_OFF + NB * 16 * 4;       // float [NB] RMSNorm divisors
+  static constexpr int XS_OFF = XL_OFF + X_BYTES;           // float [8][NB] Q4_K sub-block sums of x w
+  static constexpr int C_OFF = A_OFF;                       // float [128][CP] this CTA's K-slice result (after the MMAs)
+  static constexpr int RM_OFF = XS_OFF + 8 * NB * 4;        // float [NB] RMSNorm divisors
   static constexpr int SI_OFF = RM_OFF + NB * 4;            // int [3][NB] position, KV slot, done
-  static constexpr int EX_OFF = SI_OFF + 3 * NB * 4;        // float [64][NB] epilogue exchange
-  static constexpr int BAR_OFF = EX_OFF + 64 * NB * 4;      // mbarrier of the MMAs
+  static constexpr int RED_OFF = SI_OFF + 3 * NB * 4;       // float [16][NB] partial sums of squares
+  static constexpr int NW_OFF = RED_OFF + 16 * NB * 4;      // float [2][256] RMSNorm weights of the ring's blocks
+  static constexpr int BAR_OFF = NW_OFF + 2 * QK_K * 4;     // mbarrier of the MMAs
   static constexpr int TS_OFF = BAR_OFF + 8;                // TMEM base address
   static constexpr int RAW_OFF = (TS_OFF + 4 + 127) / 128 * 128;  // [2][128][block bytes] ring
-  static constexpr int TMEM_COLS = 8 * NB;                  // 8 sub-block accumulators of NB columns
 };
 
 template <int NB>
@@ -172,26 +173,74 @@ __device__ __forceinline__ int bd_tile_dtype(const BatchGemmArgs& a, int epi, in
   return a.seg[sg].dtype;
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory location in cluster CTA `rank`
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// (not volatile: the slices only change before the cluster barrier that precedes
+// these loads, so the compiler may issue them together)
+__device__ __forceinline__ float ld_cluster(uint32_t addr) {
+  float v;
+  asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+// bounded spin on an mbarrier phase (no suspension: the waiters have nothing else to do)
+__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t it = 0; it < (1u << 24); ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+// One CTA: a 128-row tile x a slice of the K super-blocks. 256 threads: thread
+// t owns weight row t % 128 and K half t / 128 of every super-block (its 128
+// quants and its 4 Q4_K / 8 Q6_K sub-block scales). Per super-block the CTA
+// unpacks the quants and stages the activations, one thread issues the MMAs
+// (one TMEM accumulator of NB columns per sub-block), then every thread reads
+// back the accumulators of its half and scales them into its running sums.
+// The slices of a tile form one thread-block cluster: each CTA leaves its
+// 128 x B result in shared memory, and after a cluster barrier CTA c adds the
+// slices (in slice order, over distributed shared memory) for rows
+// [c*128/S, (c+1)*128/S) and runs the epilogue on them.
 template <int NB>
-__global__ void __launch_bounds__(BD_THREADS) bgemm_kernel(const BatchGemmArgs a, const int epi) {
+__global__ void __launch_bounds__(BD_THREADS, 1) bgemm_kernel(const BatchGemmArgs a, const int epi) {
   using L = BdLayout<NB>;
   constexpr uint32_t LBO_X = (NB / 8) * 128;
+  constexpr int CP = L::CP;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* At = sm + L::A_OFF;
   uint8_t* Xh = sm + L::XH_OFF;
   uint8_t* Xl = sm + L::XL_OFF;
   float* xs = reinterpret_cast<float*>(sm + L::XS_OFF);
-  float* cs = reinterpret_cast<float*>(sm + L::CS_OFF);
+  float* C = reinterpret_cast<float*>(sm + L::C_OFF);
   float* rm = reinterpret_cast<float*>(sm + L::RM_OFF);
   int* si = reinterpret_cast<int*>(sm + L::SI_OFF);
-  float* ex = reinterpret_cast<float*>(sm + L::EX_OFF);
+  float* red = reinterpret_cast<float*>(sm + L::RED_OFF);
+  float* nw = reinterpret_cast<float*>(sm + L::NW_OFF);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L::TS_OFF);
   uint8_t* raw = sm + L::RAW_OFF;
   __shared__ const uint8_t* rp[BATCH_TILE];  // this tile's weight rows
-  __shared__ int s_last;
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (BATCH_TILE - 1), hk = tid >> 7;
   const int tile = blockIdx.x, split = blockIdx.y;
   const int nsb = a.K / QK_K;
   const int sb0 = split * a.sb_per_split;
@@ -200,317 +249,404 @@ __global__ void __launch_bounds__(BD_THREADS) bgemm_kernel(const BatchGemmArgs a
   const bool q4 = tdt == DT_Q4K;
   const int bb = q4 ? Q4K_BYTES : Q6K_DEV_BYTES;
   const size_t row_bytes = size_t(nsb) * bb;
+  // TMEM: Q4_K one accumulator of 2NB columns (hi | lo halves of the activations);
+  // Q6_K one per sub-block of a K half (8 x 2NB)
+  const uint32_t tcols = uint32_t(q4 ? 2 * NB : 16 * NB);
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
-                 "r"(L::TMEM_COLS));
+                 "r"(tcols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
     mbar_init(bar, 1);
     mbar_fence_init();
   }
-  rp[tid] = bd_row(a, epi, tile, tid, row_bytes);
+  if (tid < BATCH_TILE) rp[tid] = bd_row(a, epi, tile, tid, row_bytes);
   // the padding sequences (b >= B) stay zero in both activation halves
   for (int i = tid; i < 2 * L::X_BYTES / 16; i += BD_THREADS)
     reinterpret_cast<uint4*>(Xh)[i] = make_uint4(0u, 0u, 0u, 0u);
   pdl_trigger();
   __syncthreads();
   const int chunks = bb / 16;
-  auto load_sb = [&](int j) {  // super-block j of the slice into ring slot j & 1
+  auto load_sb = [&](int j) {  // super-block j of the slice (+ its norm weights) into ring slot j & 1
     uint8_t* dst = raw + (j & 1) * BATCH_TILE * bb;
     const size_t src_off = size_t(sb0 + j) * bb;
     for (int c = tid; c < BATCH_TILE * chunks; c += BD_THREADS) {
       const int r = c / chunks, pc = c - r * chunks;
       cp_async16(dst + r * bb + pc * 16, rp[r] + src_off + pc * 16);
     }
+    if (a.norm_w && tid < QK_K / 4)
+      cp_async16(nw + (j & 1) * QK_K + 4 * tid, a.norm_w + size_t(sb0 + j) * QK_K + 4 * tid);
   };
   load_sb(0);
   cp_async_commit();
   if (nloc > 1) load_sb(1);
   cp_async_commit();
-  pdl_wait();  // activations, norms and sequence states come from earlier kernels
-  if (tid < a.B) {
-    const StepState* st = a.st + tid;
-    si[tid] = st->position;
-    si[NB + tid] = st->kv_len;
-    si[2 * NB + tid] = st->done;
-    if (a.norm_w) {  // x / sqrt(mean(x^2) + eps) * w (candle_tensor_backend.rs:30-57)
-      float tot = 0.0f;
-      for (int t = 0; t < a.sq_tiles; ++t) tot = __fadd_rn(tot, a.sq_in[t * a.B + tid]);
-      rm[tid] = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(a.K)), a.eps));
+  pdl_wait();  // activations, norm statistics and sequence states come from earlier kernels
+
+  // sequence states; RMSNorm divisors from the producer's partial sums of squares,
+  // added in a fixed order (BD_THREADS / NB parts of consecutive entries, then the parts)
+  constexpr int PARTS = BD_THREADS / NB;
+  {
+    const int b = tid % NB, part = tid / NB;
+    if (part == 0 && b < a.B) {
+      const StepState* st = a.st + b;
+      si[b] = st->position;
+      si[NB + b] = st->kv_len;
+      si[2 * NB + b] = st->done;
     }
+    if (a.norm_w) {
+      const int per = (a.sq_tiles + PARTS - 1) / PARTS;
+      const int t0 = part * per, t1 = min(a.sq_tiles, t0 + per);
+      float tot = 0.0f;
+      if (b < a.B) {
+#pragma unroll 8
+        for (int t = t0; t < t1; ++t) tot = __fadd_rn(tot, a.sq_in[t * a.B + b]);
+      }
+      red[part * NB + b] = tot;
+    }
+  }
+  __syncthreads();
+  if (a.norm_w && tid < a.B) {  // x / sqrt(mean(x^2) + eps) * w (candle_tensor_backend.rs:30-57)
+    float tot = 0.0f;
+    for (int p = 0; p < PARTS; ++p) tot = __fadd_rn(tot, red[p * NB + tid]);
+    rm[tid] = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(a.K)), a.eps));
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t lane_tmem = tmem + (uint32_t(warp * 32) << 16);
+  const uint32_t lane_tmem = tmem + (uint32_t((warp & 3) * 32) << 16);
 
   float acc[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
   bool ok = true;
   uint32_t phase = 0;
+  // activation staging: thread (b = tid % NB, g = tid / NB) owns values [g*NB, g*NB + NB)
+  // of sequence b in each super-block (a whole Q4_K sub-block when NB = 32, half of
+  // one when NB = 16: the other half is lane tid ^ 16). The B operand holds the fp16
+  // hi halves in rows 0..NB-1 and the lo halves in rows NB..2NB-1, so one MMA (N = 2NB)
+  // takes both.
+  constexpr uint32_t LBO_X2 = (2 * NB / 8) * 128;
+  const int xb = tid % NB, xg = tid / NB;
+  const float* xrow = a.x + size_t(xb) * a.ldx;
+  const bool xon = xb < a.B;
+  // descriptors: the address field (bits 0-13, 16-byte units) advances by 2 * LBO per 16-value step
+  const uint64_t adesc0 = bd_desc(smem_u32(At), BD_LBO_A);
+  const uint64_t xdesc0 = bd_desc(smem_u32(Xh), LBO_X2);
   for (int j = 0; j < nloc; ++j) {
+    const int kg = (sb0 + j) * QK_K;
+    // this thread's activations of the super-block, loaded first so their latency
+    // hides behind the unpacking
+    float4 xq[NB / 4];
+    if (xon) {
+      const float4* src = reinterpret_cast<const float4*>(xrow + kg + xg * NB);
+#pragma unroll
+      for (int e = 0; e < NB / 4; ++e) xq[e] = src[e];
+    }
     cp_async_wait<1>();
-    __syncthreads();  // every thread's copies of super-block j have landed
-    const uint8_t* blk = raw + (j & 1) * BATCH_TILE * bb + tid * bb;  // this thread's row
-#pragma unroll 1
-    for (int h = 0; h < 2; ++h) {
-      const int kg = (sb0 + j) * QK_K + h * BD_STEP;
-      // (1) the row's 128 quants of this round as fp16 integers, and its sub-block scales
-      float d1[8], m1[4];
-      if (q4) {
-        const uint4 hd = *reinterpret_cast<const uint4*>(blk);
-        const float d = half_bits(hd.x & 0xFFFFu), dmin = half_bits(hd.x >> 16);
+    __syncthreads();  // super-block j (and its norm weights) have landed
+    const uint8_t* blk = raw + (j & 1) * BATCH_TILE * bb + row * bb;
+    // (1) this thread's 128 quants (K half hk) as fp16 integers. Q4_K: sc_s * q (at most
+    // 63 * 15 = 945, exact), so the whole super-block shares the scale d and one
+    // accumulator; the dmin * m_s * sum(x) terms are added on the CUDA cores.
+    // Q6_K: q - 32 with d * sc_s per 16-value sub-block applied after the MMA.
+    float d1[8], m1[4], dq = 0.0f, dmq = 0.0f;
+    if (q4) {
+      const uint4 hd = *reinterpret_cast<const uint4*>(blk);
+      dq = half_bits(hd.x & 0xFFFFu);
+      dmq = half_bits(hd.x >> 16);
+      const __half2 bias = __float2half2_rn(1024.0f);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          uint32_t sc, mn;
-          scale_min(4 * h + u, hd.y, hd.z, hd.w, sc, mn);
-          d1[u] = __fmul_rn(d, float(sc));
-          m1[u] = __fmul_rn(dmin, float(mn));
-        }
-        const __half2 bias = __float2half2_rn(1024.0f);
+      for (int p = 0; p < 2; ++p) {  // sub-block pair 2hk+p: low nibbles = sub-block 2p, high = 2p+1
+        uint32_t sc0, mn0, sc1, mn1;
+        scale_min(4 * hk + 2 * p, hd.y, hd.z, hd.w, sc0, mn0);
+        scale_min(4 * hk + 2 * p + 1, hd.y, hd.z, hd.w, sc1, mn1);
+        m1[2 * p] = float(mn0);
+        m1[2 * p + 1] = float(mn1);
+        const __half2 s0 = __float2half2_rn(float(sc0)), s1 = __float2half2_rn(float(sc1));
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {  // sub-block pair 2h+p: low nibbles = sub-block 2p, high = 2p+1
-          const uint8_t* qs = blk + 16 + 32 * (2 * h + p);
+        for (int w = 0; w < 2; ++w) {  // 16 bytes = values 16w..16w+15 of both sub-blocks
+          const uint4 q16 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * (2 * hk + p) + 16 * w);
+          const uint32_t qw[4] = {q16.x, q16.y, q16.z, q16.w};
+          uint32_t lo[8], hi[8];
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint2 q8 = *reinterpret_cast<const uint2*>(qs + 8 * w);
-            uint4 lo, hi;
-            quads_to_half(q8.x & 0x0F0F0F0Fu, bias, lo.x, lo.y);
-            quads_to_half(q8.y & 0x0F0F0F0Fu, bias, lo.z, lo.w);
-            quads_to_half((q8.x >> 4) & 0x0F0F0F0Fu, bias, hi.x, hi.y);
-            quads_to_half((q8.y >> 4) & 0x0F0F0F0Fu, bias, hi.z, hi.w);
-            *reinterpret_cast<uint4*>(At + op_off(tid, 64 * p + 8 * w, BD_LBO_A)) = lo;
-            *reinterpret_cast<uint4*>(At + op_off(tid, 64 * p + 32 + 8 * w, BD_LBO_A)) = hi;
+          for (int e = 0; e < 4; ++e) {
+            quads_to_half(qw[e] & 0x0F0F0F0Fu, bias, lo[2 * e], lo[2 * e + 1]);
+            quads_to_half((qw[e] >> 4) & 0x0F0F0F0Fu, bias, hi[2 * e], hi[2 * e + 1]);
           }
-        }
-      } else {  // Q6_K half h: value 32g + l = ql nibble | 2 bits of qh (quant.rs:206-261)
-        const float d = half_bits(uint32_t(blk[208]) | (uint32_t(blk[209]) << 8));
-        const int8_t* scv = reinterpret_cast<const int8_t*>(blk + 192 + 8 * h);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) d1[u] = __fmul_rn(d, float(scv[u]));
-        const uint8_t* ql = blk + 64 * h;
-        const uint8_t* qh = blk + 128 + 32 * h;
-        const __half2 bias = __float2half2_rn(1056.0f);  // 1024 + the Q6_K offset 32
-#pragma unroll
-        for (int l8 = 0; l8 < 4; ++l8) {
-          const uint2 a0 = *reinterpret_cast<const uint2*>(ql + 8 * l8);
-          const uint2 a1 = *reinterpret_cast<const uint2*>(ql + 32 + 8 * l8);
-          const uint2 hb = *reinterpret_cast<const uint2*>(qh + 8 * l8);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const uint2 src = (g & 1) ? a1 : a0;
-            const int sh = g < 2 ? 0 : 4;
-            const uint32_t q0 = ((src.x >> sh) & 0x0F0F0F0Fu) | (((hb.x >> (2 * g)) & 0x03030303u) << 4);
-            const uint32_t q1 = ((src.y >> sh) & 0x0F0F0F0Fu) | (((hb.y >> (2 * g)) & 0x03030303u) << 4);
-            uint4 o;
-            quads_to_half(q0, bias, o.x, o.y);
-            quads_to_half(q1, bias, o.z, o.w);
-            *reinterpret_cast<uint4*>(At + op_off(tid, 32 * g + 8 * l8, BD_LBO_A)) = o;
+          for (int e = 0; e < 8; ++e) {
+            __half2 l2 = __hmul2(*reinterpret_cast<__half2*>(&lo[e]), s0);
+            __half2 h2 = __hmul2(*reinterpret_cast<__half2*>(&hi[e]), s1);
+            lo[e] = *reinterpret_cast<uint32_t*>(&l2);
+            hi[e] = *reinterpret_cast<uint32_t*>(&h2);
           }
+          const int k = 128 * hk + 64 * p + 16 * w;
+          *reinterpret_cast<uint4*>(At + op_off(row, k, BD_LBO_A)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(At + op_off(row, k + 8, BD_LBO_A)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+          *reinterpret_cast<uint4*>(At + op_off(row, k + 32, BD_LBO_A)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(At + op_off(row, k + 40, BD_LBO_A)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
         }
       }
-      // (2) the activations of this round (RMSNorm applied), split into fp16 hi + lo
-      for (int i = tid; i < NB * 16; i += BD_THREADS) {
-        const int b = i % NB, kc = i / NB;
-        if (b >= a.B) continue;
-        const float* xr = a.x + size_t(b) * a.ldx + kg + 8 * kc;
-        const float4 f0 = *reinterpret_cast<const float4*>(xr);
-        const float4 f1 = *reinterpret_cast<const float4*>(xr + 4);
-        float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-        if (a.norm_w) {
-          const float* nw = a.norm_w + kg + 8 * kc;
-          const float m = rm[b];
+    } else {  // Q6_K half hk: value 32g + l = ql nibble | 2 bits of qh (quant.rs:206-261)
+      const float d = half_bits(uint32_t(blk[208]) | (uint32_t(blk[209]) << 8));
+      const int8_t* scv = reinterpret_cast<const int8_t*>(blk + 192 + 8 * hk);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fdiv_rn(v[e], m), nw[e]);
+      for (int u = 0; u < 8; ++u) d1[u] = __fmul_rn(d, float(scv[u]));
+      const uint8_t* ql = blk + 64 * hk;
+      const uint8_t* qh = blk + 128 + 32 * hk;
+      const __half2 bias = __float2half2_rn(1056.0f);  // 1024 + the Q6_K offset 32
+#pragma unroll
+      for (int l16 = 0; l16 < 2; ++l16) {
+        const uint4 a0 = *reinterpret_cast<const uint4*>(ql + 16 * l16);
+        const uint4 a1 = *reinterpret_cast<const uint4*>(ql + 32 + 16 * l16);
+        const uint4 hb = *reinterpret_cast<const uint4*>(qh + 16 * l16);
+        const uint32_t w0[4] = {a0.x, a0.y, a0.z, a0.w}, w1[4] = {a1.x, a1.y, a1.z, a1.w};
+        const uint32_t wh[4] = {hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int sh = g < 2 ? 0 : 4;
+          uint32_t o[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t src = (g & 1) ? w1[e] : w0[e];
+            const uint32_t q = ((src >> sh) & 0x0F0F0F0Fu) | (((wh[e] >> (2 * g)) & 0x03030303u) << 4);
+            quads_to_half(q, bias, o[2 * e], o[2 * e + 1]);
+          }
+          const int k = 128 * hk + 32 * g + 16 * l16;
+          *reinterpret_cast<uint4*>(At + op_off(row, k, BD_LBO_A)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(At + op_off(row, k + 8, BD_LBO_A)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      }
+    }
+    // (2) the activations x * w (the RMSNorm divisor is applied to the sums at the
+    // end: sum W (x w / m) = (1/m) sum W (x w)), split into fp16 hi + lo
+    float sum = 0.0f;
+    if (xon) {
+#pragma unroll
+      for (int c = 0; c < NB / 8; ++c) {
+        float v[8] = {xq[2 * c].x, xq[2 * c].y, xq[2 * c].z, xq[2 * c].w,
+                      xq[2 * c + 1].x, xq[2 * c + 1].y, xq[2 * c + 1].z, xq[2 * c + 1].w};
+        if (a.norm_w) {
+          const float4* w4 = reinterpret_cast<const float4*>(nw + (j & 1) * QK_K + xg * NB + 8 * c);
+          const float4 w0 = w4[0], w1 = w4[1];
+          const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], wv[e]);
         }
         __half hv[8], lv[8];
-        float sum = 0.0f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           hv[e] = __float2half_rn(v[e]);
           lv[e] = __float2half_rn(__fsub_rn(v[e], __half2float(hv[e])));
           sum = __fadd_rn(sum, v[e]);
         }
-        const int off = op_off(b, 8 * kc, LBO_X);
-        *reinterpret_cast<uint4*>(Xh + off) = *reinterpret_cast<const uint4*>(hv);
-        *reinterpret_cast<uint4*>(Xl + off) = *reinterpret_cast<const uint4*>(lv);
-        cs[b * 16 + kc] = sum;
+        const int k = xg * NB + 8 * c;
+        *reinterpret_cast<uint4*>(Xh + op_off(xb, k, LBO_X2)) = *reinterpret_cast<const uint4*>(hv);
+        *reinterpret_cast<uint4*>(Xh + op_off(NB + xb, k, LBO_X2)) = *reinterpret_cast<const uint4*>(lv);
       }
-      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
-      tc_fence_before();
-      __syncthreads();
-      // (3) one thread issues the MMAs: sub-block u accumulates into columns u*NB..
+    }
+    if (NB == 16) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 16));  // lanes g, g^1 of a sub-block
+    if (xon && (NB == 32 || (xg & 1) == 0)) xs[(xg * NB / 32) * NB + xb] = sum;  // sum of x w over the sub-block
+    fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+    tc_fence_before();
+    __syncthreads();
+    if (q4) {
+      // (3) one thread issues the 16 MMAs of the super-block into the one accumulator
       if (tid == 0) {
         tc_fence_after();
-        const uint32_t a0 = smem_u32(At), xh0 = smem_u32(Xh), xl0 = smem_u32(Xl);
-        const int nsub = q4 ? 4 : 8, kper = q4 ? 2 : 1;  // 16-value MMA steps per sub-block
-        for (int u = 0; u < nsub; ++u) {
-          for (int kk = 0; kk < kper; ++kk) {
-            const uint32_t c16 = uint32_t(u * kper + kk);
-            const uint64_t ad = bd_desc(a0 + c16 * 2 * BD_LBO_A, BD_LBO_A);
-            bd_mma<NB>(tmem + uint32_t(u * NB), ad, bd_desc(xh0 + c16 * 2 * LBO_X, LBO_X), kk > 0 ? 1u : 0u);
-            bd_mma<NB>(tmem + uint32_t(u * NB), ad, bd_desc(xl0 + c16 * 2 * LBO_X, LBO_X), 1u);
-          }
-        }
+#pragma unroll 1
+        for (int c16 = 0; c16 < QK_K / 16; ++c16)
+          bd_mma<2 * NB>(tmem, adesc0 + uint64_t(c16) * (2 * BD_LBO_A / 16),
+                         xdesc0 + uint64_t(c16) * (2 * LBO_X2 / 16), c16 > 0 ? 1u : 0u);
         bd_commit(bar);
       }
-      if (q4 && tid < 4 * NB) {  // sums of x over each 32-value sub-block (the dmin*m term)
-        const int u = tid / NB, b = tid % NB;
-        const float* c = cs + b * 16 + 4 * u;
-        xs[u * NB + b] = __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[1]), c[2]), c[3]);
+      // (4) thread (row, hk) reads the hi (hk = 0) or lo (hk = 1) half of its row's
+      // accumulator: acc += d * dot - dmin * sum_s m_s * sum(x w) over its 4 sub-blocks
+#pragma unroll
+      for (int uu = 0; uu < 4; ++uu) {  // the min terms while the MMAs run
+        const float mm = dmq * m1[uu];
+        const float4* x4 = reinterpret_cast<const float4*>(xs + (4 * hk + uu) * NB);
+#pragma unroll
+        for (int b4 = 0; b4 < NB / 4; ++b4) {
+          const float4 s4 = x4[b4];
+          acc[4 * b4 + 0] -= mm * s4.x;
+          acc[4 * b4 + 1] -= mm * s4.y;
+          acc[4 * b4 + 2] -= mm * s4.z;
+          acc[4 * b4 + 3] -= mm * s4.w;
+        }
       }
-      __syncthreads();
-      // (4) accumulators -> scaled into this row's running sums
-      ok &= mbar_wait(bar, phase);
+      ok &= mbar_spin(bar, phase);
       phase ^= 1u;
       tc_fence_after();
-      if (q4) {
+      float v[NB];
+      tmem_ld<NB>(lane_tmem + uint32_t(hk * NB), v);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float v[NB];
-          tmem_ld<NB>(lane_tmem + uint32_t(u * NB), v);
-#pragma unroll
-          for (int b = 0; b < NB; ++b) acc[b] += d1[u] * v[b] - m1[u] * xs[u * NB + b];
+      for (int b = 0; b < NB; ++b) acc[b] += dq * v[b];
+    } else {
+      // Q6_K: sub-blocks 0-7 (K half 0), then 8-15 (K half 1), 8 accumulators of 2NB
+      // columns each pass; the threads of that half read them back
+#pragma unroll 1
+      for (int pass = 0; pass < 2; ++pass) {
+        if (tid == 0) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int u = 0; u < 8; ++u) {
+            const uint64_t c16 = uint64_t(8 * pass + u);
+            bd_mma<2 * NB>(tmem + uint32_t(u * 2 * NB), adesc0 + c16 * (2 * BD_LBO_A / 16),
+                           xdesc0 + c16 * (2 * LBO_X2 / 16), 0u);
+          }
+          bd_commit(bar);
         }
-      } else {
+        ok &= mbar_spin(bar, phase);
+        phase ^= 1u;
+        tc_fence_after();
+        if (hk == pass) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          float v[NB];
-          tmem_ld<NB>(lane_tmem + uint32_t(u * NB), v);
+          for (int u = 0; u < 8; ++u) {
 #pragma unroll
-          for (int b = 0; b < NB; ++b) acc[b] += d1[u] * v[b];
+            for (int half = 0; half < 2; ++half) {
+              float v[NB];
+              tmem_ld<NB>(lane_tmem + uint32_t(u * 2 * NB + half * NB), v);
+#pragma unroll
+              for (int b = 0; b < NB; ++b) acc[b] += d1[u] * v[b];
+            }
+          }
         }
+        tc_fence_before();
+        __syncthreads();  // the accumulators are free for the next pass
       }
-      tc_fence_before();
     }
-    if (j + 2 < nloc) load_sb(j + 2);  // every thread is past its reads of slot j & 1
+    tc_fence_before();
+    if (j + 2 < nloc) load_sb(j + 2);  // every thread is past its unpacking of ring slot j & 1
     cp_async_commit();
+  }
+  if (a.norm_w) {  // the RMSNorm divisor of each sequence (candle_tensor_backend.rs:30-57)
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[b] = __fdiv_rn(acc[b], rm[b < a.B ? b : 0]);
   }
   cp_async_wait<0>();
   const bool all_ok = __syncthreads_and(ok);
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols));
   }
-  if (!all_ok) {  // a bounded wait expired: report it, store nothing
-    if (tid == 0) atomicOr(&a.st[0].err, 4);
-    return;
+  // the two K halves of each row, added in a fixed order
+  if (hk == 1) {
+#pragma unroll
+    for (int b = 0; b < NB; ++b) C[row * CP + b] = acc[b];
   }
+  __syncthreads();
+  if (hk == 0) {
+#pragma unroll
+    for (int b = 0; b < NB; ++b) C[row * CP + b] = __fadd_rn(acc[b], C[row * CP + b]);
+  }
+  const int S = a.splits;
+  if (S > 1) cluster_sync_all();  // every slice's C is complete and visible to the cluster
+  else __syncthreads();
+  const int crank = S > 1 ? int(cluster_rank()) : 0;
+  uint32_t cbase[BD_MAX_SPLITS];
+#pragma unroll
+  for (int q = 0; q < BD_MAX_SPLITS; ++q) cbase[q] = q < S ? cluster_map(smem_u32(C), uint32_t(q)) : 0u;
+  auto reduced = [&](int r, int b) {  // row r of the tile, sequence b, over the slices in order
+    float v = 0.0f;
+    const uint32_t off = uint32_t(r * CP + b) * 4u;
+#pragma unroll
+    for (int q = 0; q < BD_MAX_SPLITS; ++q)
+      if (q < S) v = __fadd_rn(v, ld_cluster(cbase[q] + off));
+    return v;
+  };
+  if (!all_ok && tid == 0) atomicOr(&a.st[0].err, 4);  // a bounded wait expired: store nothing
 
-  // K slices: the last CTA of the tile sums them in slice order
-  if (a.splits > 1) {
-    const size_t P = size_t(gridDim.x) * BATCH_TILE;  // slice row stride
-    float* pp = a.part + size_t(split) * a.B * P + size_t(tile) * BATCH_TILE + tid;
+  if (all_ok) {
+    float* sq = reinterpret_cast<float*>(Xh);  // the activation tile is free: [pairs][NB] sums of squares
+    const int* pos = si;
+    const int* slot = si + NB;
+    const int* done = si + 2 * NB;
+    if (epi == BEPI_SWIGLU) {  // ffn.rs:90-94: g * (1 / (1 + exp(-g))) * u
+      const int O = ((BATCH_TILE / 2 + S - 1) / S + 1) & ~1;  // outputs of this CTA (even)
+      const int o0 = crank * O, o1 = min(BATCH_TILE / 2, o0 + O);
+      const int P2 = (o1 - o0 + 1) / 2;
+      for (int u = tid; u < P2 * a.B; u += BD_THREADS) {
+        const int pr = u % P2, b = u / P2, o = o0 + 2 * pr;
 #pragma unroll
-    for (int b = 0; b < NB; ++b)
-      if (b < a.B) pp[size_t(b) * P] = acc[b];
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(a.ticket + tile, 1) == a.splits - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    if (tid == 0) a.ticket[tile] = 0;
-    const float* p0 = a.part + size_t(tile) * BATCH_TILE + tid;
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      if (b >= a.B) continue;
-      float s2 = 0.0f;
-      for (int sp = 0; sp < a.splits; ++sp) s2 = __fadd_rn(s2, __ldcg(p0 + (size_t(sp) * a.B + b) * P));
-      acc[b] = s2;
-    }
-  }
-
-  if (epi == BEPI_SWIGLU) {  // ffn.rs:90-94: g * (1 / (1 + exp(-g))) * u
-    if (tid >= 64) {
-#pragma unroll
-      for (int b = 0; b < NB; ++b) ex[(tid - 64) * NB + b] = acc[b];
-    }
-    __syncthreads();
-    const int r = tile * (BATCH_TILE / 2) + tid;
-    if (tid < 64 && r < a.rows) {
-#pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        if (b >= a.B) continue;
-        const float gv = acc[b], uv = ex[tid * NB + b];
-        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
-        a.y[size_t(b) * a.ldy + r] = __fmul_rn(__fmul_rn(gv, sig), uv);
+        for (int e = 0; e < 2; ++e) {
+          const int r = tile * (BATCH_TILE / 2) + o + e;
+          if (o + e >= o1 || r >= a.rows) continue;
+          const float gv = reduced(o + e, b), uv = reduced(BATCH_TILE / 2 + o + e, b);
+          const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+          a.y[size_t(b) * a.ldy + r] = __fmul_rn(__fmul_rn(gv, sig), uv);
+        }
+      }
+    } else {
+      const int RPC = ((BATCH_TILE + S - 1) / S + 1) & ~1;  // rows of this CTA (even)
+      const int r0 = crank * RPC, r1 = min(BATCH_TILE, r0 + RPC);
+      const int P2 = (r1 - r0 + 1) / 2;
+      for (int u = tid; u < P2 * a.B; u += BD_THREADS) {
+        const int pr = u % P2, b = u / P2, r = r0 + 2 * pr;
+        const int n = tile * BATCH_TILE + r;
+        const bool ok0 = r < r1 && n < a.rows, ok1 = r + 1 < r1 && n + 1 < a.rows;
+        const float v0 = ok0 ? reduced(r, b) : 0.0f, v1 = ok1 ? reduced(r + 1, b) : 0.0f;
+        if (epi == BEPI_STORE) {
+          if (ok0) a.y[size_t(b) * a.ldy + n] = v0;
+          if (ok1) a.y[size_t(b) * a.ldy + n + 1] = v1;
+        } else if (epi == BEPI_RESID) {  // layer.rs:68 / :86
+          const float* rr = a.resid + size_t(b) * a.ldr + n;
+          const float y0 = ok0 ? __fadd_rn(rr[0], v0) : 0.0f;
+          const float y1 = ok1 ? __fadd_rn(rr[1], v1) : 0.0f;
+          if (ok0) a.y[size_t(b) * a.ldy + n] = y0;
+          if (ok1) a.y[size_t(b) * a.ldy + n + 1] = y1;
+          sq[pr * NB + b] = __fadd_rn(__fmul_rn(y0, y0), __fmul_rn(y1, y1));
+        } else if (ok0) {  // BEPI_QKV: RoPE on (2i, 2i+1) pairs of q and k (attention.rs:230-262),
+          // K / V appended at each sequence's KV slot (kv_cache.rs:44-67)
+          const int hd = a.head_dim;
+          if (n < a.hidden + a.kv_dim) {
+            const int col = n < a.hidden ? n : n - a.hidden;
+            const int pi = (col % hd) >> 1;
+            const float cs_ = a.rope_cos[size_t(pos[b]) * (hd / 2) + pi];
+            const float sn_ = a.rope_sin[size_t(pos[b]) * (hd / 2) + pi];
+            const float n0 = __fsub_rn(__fmul_rn(v0, cs_), __fmul_rn(v1, sn_));
+            const float n1 = __fadd_rn(__fmul_rn(v0, sn_), __fmul_rn(v1, cs_));
+            if (n < a.hidden) {
+              a.q[size_t(b) * a.ldq + n] = n0;
+              a.q[size_t(b) * a.ldq + n + 1] = n1;
+            } else if (!done[b]) {
+              const size_t off = size_t(b) * a.seq_stride + (size_t(col / hd) * a.max_seq + slot[b]) * hd + col % hd;
+              if (a.kv_half) {
+                reinterpret_cast<__half*>(a.kc)[off] = __float2half_rn(n0);
+                reinterpret_cast<__half*>(a.kc)[off + 1] = __float2half_rn(n1);
+              } else {
+                reinterpret_cast<float*>(a.kc)[off] = n0;
+                reinterpret_cast<float*>(a.kc)[off + 1] = n1;
+              }
+            }
+          } else if (!done[b]) {
+            const int col = n - a.hidden - a.kv_dim;
+            const size_t off = size_t(b) * a.seq_stride + (size_t(col / hd) * a.max_seq + slot[b]) * hd + col % hd;
+            if (a.kv_half) {
+              reinterpret_cast<__half*>(a.vc)[off] = __float2half_rn(v0);
+              reinterpret_cast<__half*>(a.vc)[off + 1] = __float2half_rn(v1);
+            } else {
+              reinterpret_cast<float*>(a.vc)[off] = v0;
+              reinterpret_cast<float*>(a.vc)[off + 1] = v1;
+            }
+          }
+        }
+      }
+      if (epi == BEPI_RESID) {  // this slice's sums of squares per sequence, pairs added in order
+        __syncthreads();
+        if (tid < a.B) {
+          float t = 0.0f;
+          for (int pr = 0; pr < P2; ++pr) t = __fadd_rn(t, sq[pr * NB + tid]);
+          a.sq_out[(size_t(tile) * S + crank) * a.B + tid] = t;
+        }
       }
     }
-    return;
   }
-  const int n = tile * BATCH_TILE + tid;
-  const bool valid = n < a.rows;
-  if (epi == BEPI_STORE) {
-    if (valid) {
-#pragma unroll
-      for (int b = 0; b < NB; ++b)
-        if (b < a.B) a.y[size_t(b) * a.ldy + n] = acc[b];
-    }
-    return;
-  }
-  if (epi == BEPI_RESID) {  // layer.rs:68 / :86, and the sums of squares of the new stream
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      float v = 0.0f;
-      if (valid && b < a.B) {
-        v = __fadd_rn(a.resid[size_t(b) * a.ldr + n], acc[b]);
-        a.y[size_t(b) * a.ldy + n] = v;
-      }
-      const float s2 = warp_sum(__fmul_rn(v, v));
-      if (lane == 0) ex[warp * NB + b] = s2;
-    }
-    __syncthreads();
-    if (tid < a.B)
-      a.sq_out[tile * a.B + tid] =
-          __fadd_rn(__fadd_rn(__fadd_rn(ex[tid], ex[NB + tid]), ex[2 * NB + tid]), ex[3 * NB + tid]);
-    return;
-  }
-  // BEPI_QKV: RoPE on (2i, 2i+1) pairs of q and k (attention.rs:230-262), the
-  // pair's other value from the neighbouring lane; K / V appended at each
-  // sequence's KV slot (kv_cache.rs:44-67)
-  float other[NB];
-#pragma unroll
-  for (int b = 0; b < NB; ++b) other[b] = __shfl_xor_sync(0xffffffffu, acc[b], 1);
-  if (!valid) return;
-  const int hd = a.head_dim;
-  const int* pos = si;
-  const int* slot = si + NB;
-  const int* done = si + 2 * NB;
-  if (n < a.hidden + a.kv_dim) {
-    const int col = n < a.hidden ? n : n - a.hidden;
-    const int pi = (col % hd) >> 1;
-    const bool odd = n & 1;
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      if (b >= a.B) continue;
-      const float cs_ = a.rope_cos[size_t(pos[b]) * (hd / 2) + pi];
-      const float sn_ = a.rope_sin[size_t(pos[b]) * (hd / 2) + pi];
-      const float x0 = odd ? other[b] : acc[b], x1 = odd ? acc[b] : other[b];
-      const float r = odd ? __fadd_rn(__fmul_rn(x0, sn_), __fmul_rn(x1, cs_))
-                          : __fsub_rn(__fmul_rn(x0, cs_), __fmul_rn(x1, sn_));
-      if (n < a.hidden) {
-        a.q[size_t(b) * a.ldq + n] = r;
-      } else if (!done[b]) {
-        const size_t off = size_t(b) * a.seq_stride + (size_t(col / hd) * a.max_seq + slot[b]) * hd + col % hd;
-        if (a.kv_half) reinterpret_cast<__half*>(a.kc)[off] = __float2half_rn(r);
-        else reinterpret_cast<float*>(a.kc)[off] = r;
-      }
-    }
-  } else {
-    const int col = n - a.hidden - a.kv_dim;
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      if (b >= a.B || done[b]) continue;
-      const size_t off = size_t(b) * a.seq_stride + (size_t(col / hd) * a.max_seq + slot[b]) * hd + col % hd;
-      if (a.kv_half) reinterpret_cast<__half*>(a.vc)[off] = __float2half_rn(acc[b]);
-      else reinterpret_cast<float*>(a.vc)[off] = acc[b];
-    }
-  }
+  if (S > 1) cluster_sync_all();  // no CTA leaves while others still read its slice
 }
 
 __global__ void bembed_kernel(const float* emb, int vocab, int hidden, const StepState* st, const uint32_t* hist,
@@ -542,7 +678,10 @@ __global__ void bembed_kernel(const float* emb, int vocab, int hidden, const Ste
 
 // LogitsProcessor::sample for temperature 0 (sampling.rs:57-125) on sequence b:
 // repetition penalty once per occurrence, argmax with the last maximum winning,
-// then generate()'s bookkeeping (model.rs:1380-1409)
+// then generate()'s bookkeeping (model.rs:1380-1409). BS_SPLIT CTAs per sequence
+// each scan a slice of the vocabulary; the last to finish runs the bookkeeping.
+constexpr int BS_SPLIT = 8;
+
 __global__ void bsample_kernel(const float* logits, int vocab, StepState* st, uint32_t* hist, int hist_cap,
                                uint32_t* pen_cnt, float rep) {
   pdl_trigger();
@@ -554,16 +693,29 @@ __global__ void bsample_kernel(const float* logits, int vocab, StepState* st, ui
   uint32_t* pc = pen_cnt + size_t(b) * vocab;
   unsigned long long best = 0ull;
   int nan = 0;
-  for (int n = tid; n < vocab; n += blockDim.x) {
-    float pv = lg[n];
-    if (rep != 1.0f) {
-      const uint32_t cnt = pc[n];
-      for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, rep) : __fmul_rn(pv, rep);
+  const int per = (vocab + BS_SPLIT - 1) / BS_SPLIT;
+  const int v0 = blockIdx.y * per, v1 = min(vocab, v0 + per);
+  constexpr int U = 8;  // independent loads in flight per thread
+  for (int n0 = v0 + tid; n0 < v1; n0 += U * blockDim.x) {
+    float v[U];
+    uint32_t cnt[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int n = n0 + u * blockDim.x;
+      v[u] = n < v1 ? lg[n] : 0.0f;
+      cnt[u] = (n < v1 && rep != 1.0f) ? pc[n] : 0u;
     }
-    if (pv != pv) nan = 1;
-    else {
-      const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
-      best = key > best ? key : best;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int n = n0 + u * blockDim.x;
+      if (n >= v1) continue;
+      float pv = v[u];
+      for (uint32_t k = 0; k < cnt[u]; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, rep) : __fmul_rn(pv, rep);
+      if (pv != pv) nan = 1;
+      else {
+        const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
+        best = key > best ? key : best;
+      }
     }
   }
 #pragma unroll
@@ -586,13 +738,220 @@ __global__ void bsample_kernel(const float* logits, int vocab, StepState* st, ui
       bb = s_best[w] > bb ? s_best[w] : bb;
       nn |= s_nan[w];
     }
-    s->best = bb;
-    s->nan = nn;
-    finish_sample_state(s, hist + size_t(b) * hist_cap, pc);
+    if (bb) atomicMax(&s->best, bb);
+    if (nn) atomicOr(&s->nan, 1);
+    __threadfence();
+    if (atomicAdd(&s->ticket, 1) == BS_SPLIT - 1) {  // the last slice runs the bookkeeping
+      __threadfence();
+      finish_sample_state(s, hist + size_t(b) * hist_cap, pc);
+    }
+  }
+}
+
+// Decode attention of one (kv head, sequence, split) for the batched step
+// (attention.rs:332-435 for one query token at position kv_len): the n_rep <= 8
+// query heads of the kv head are processed together. Each warp takes 32 keys at
+// a time, one per lane: the lane reads its key's K row straight from the cache
+// and scores it against all query heads (queries broadcast from shared memory);
+// the warp keeps a running max / sum per head, writes its probabilities to
+// shared memory and accumulates P.V with each lane owning HD/32 dimensions of
+// every head (V rows read coalesced). The 4 warps merge in shared memory, the
+// splits through a partial buffer and a ticket (the last CTA merges).
+template <typename KT>
+__device__ __forceinline__ void load8(const KT* p, float (&f)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&f)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+template <int N, typename KT>
+__device__ __forceinline__ void loadn(const KT* p, float (&f)[N]) {
+  if constexpr (N == 2) {
+    if constexpr (sizeof(KT) == 2) {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(p));
+      f[0] = t.x; f[1] = t.y;
+    } else {
+      const float2 t = *reinterpret_cast<const float2*>(p);
+      f[0] = t.x; f[1] = t.y;
+    }
+  } else {
+    if constexpr (sizeof(KT) == 2) {
+      const uint2 u = *reinterpret_cast<const uint2*>(p);
+      const float2 t0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 t1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      f[0] = t0.x; f[1] = t0.y; f[2] = t1.x; f[3] = t1.y;
+    } else {
+      const float4 t = *reinterpret_cast<const float4*>(p);
+      f[0] = t.x; f[1] = t.y; f[2] = t.z; f[3] = t.w;
+    }
+  }
+}
+
+constexpr int BA_THREADS = 128;
+constexpr int BA_NR = 8;  // query heads per kv head (at most)
+
+template <int HD, typename KT>
+__global__ void __launch_bounds__(BA_THREADS) battn_kernel(const AttnArgs a) {
+  constexpr int DPL = HD / 32;  // output dimensions per lane
+  __shared__ __align__(16) float qs[BA_NR * HD];
+  __shared__ __align__(16) float ps[4][32][BA_NR];
+  __shared__ float wm[4][BA_NR], wl[4][BA_NR];
+  __shared__ __align__(16) float wo[4][BA_NR][HD];
+  __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int kh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;
+  const StepState* st = a.st + b;
+  if (st->done) return;
+  const int nkeys = st->kv_len + 1;  // keys 0..position, this step's included
+  const int nsplit = (nkeys + a.chunk - 1) / a.chunk;
+  if (split >= nsplit) return;
+  const int j0 = split * a.chunk, j1 = min(j0 + a.chunk, nkeys);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_rep = a.n_heads / a.n_kv;
+  const float* qsrc = a.q + (size_t(b) * a.n_heads + size_t(kh) * n_rep) * HD;
+  for (int i = tid; i < BA_NR * HD; i += BA_THREADS) qs[i] = i < n_rep * HD ? qsrc[i] : 0.0f;
+  __syncthreads();
+  const size_t base = size_t(b) * a.seq_stride + size_t(kh) * a.max_seq * HD;
+  const KT* Kp = reinterpret_cast<const KT*>(a.kc) + base;
+  const KT* Vp = reinterpret_cast<const KT*>(a.vc) + base;
+
+  float m[BA_NR], l[BA_NR], o[BA_NR][DPL];
+#pragma unroll
+  for (int r = 0; r < BA_NR; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.0f;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) o[r][d] = 0.0f;
+  }
+  for (int k0 = j0 + warp * 32; k0 < j1; k0 += 4 * 32) {
+    const int j = k0 + lane;
+    const bool valid = j < j1;
+    float s[BA_NR];
+#pragma unroll
+    for (int r = 0; r < BA_NR; ++r) s[r] = 0.0f;
+    if (valid) {
+      const KT* kr = Kp + size_t(j) * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 8) {
+        float kf[8];
+        load8<KT>(kr + c, kf);
+#pragma unroll
+        for (int r = 0; r < BA_NR; ++r) {
+          const float4 q0 = *reinterpret_cast<const float4*>(qs + r * HD + c);
+          const float4 q1 = *reinterpret_cast<const float4*>(qs + r * HD + c + 4);
+          s[r] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] + q1.y * kf[5] +
+                  q1.z * kf[6] + q1.w * kf[7];
+        }
+      }
+    }
+    // running softmax per head (attention.rs:380-410)
+#pragma unroll
+    for (int r = 0; r < BA_NR; ++r) {
+      const float sc = valid ? s[r] * a.scale : -INFINITY;
+      const float mn = fmaxf(m[r], warp_max(sc));
+      const float p = valid ? expf(sc - mn) : 0.0f;
+      const float cf = expf(m[r] - mn);
+      l[r] = l[r] * cf + warp_sum(p);
+      m[r] = mn;
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[r][d] *= cf;
+      ps[warp][lane][r] = p;
+    }
+    __syncwarp();
+    const int nk = min(32, j1 - k0);
+    const KT* vb = Vp + size_t(k0) * HD + lane * DPL;
+#pragma unroll 4
+    for (int jj = 0; jj < nk; ++jj) {
+      float v[DPL];
+      loadn<DPL, KT>(vb + size_t(jj) * HD, v);
+      const float4 p0 = *reinterpret_cast<const float4*>(&ps[warp][jj][0]);
+      const float4 p1 = *reinterpret_cast<const float4*>(&ps[warp][jj][4]);
+      const float pr[BA_NR] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+      for (int r = 0; r < BA_NR; ++r)
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o[r][d] += pr[r] * v[d];
+    }
+    __syncwarp();
+  }
+  // merge the 4 warps (a warp without keys has m = -inf, l = 0)
+#pragma unroll
+  for (int r = 0; r < BA_NR; ++r) {
+    if (lane == 0) {
+      wm[warp][r] = m[r];
+      wl[warp][r] = l[r];
+    }
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) wo[warp][r][lane * DPL + d] = o[r][d];
+  }
+  __syncthreads();
+  const size_t pstride = HD + 2;
+  for (int i = tid; i < n_rep * HD; i += BA_THREADS) {
+    const int r = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][r]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float f = expf(wm[w][r] - M);
+      L += wl[w][r] * f;
+      O += wo[w][r][d] * f;
+    }
+    const size_t head = size_t(b) * a.n_heads + size_t(kh) * n_rep + r;
+    if (nsplit == 1) {
+      a.out[head * HD + d] = L > 0.0f ? O / L : 0.0f;
+    } else {
+      float* pp = a.part + (head * a.max_splits + split) * pstride;
+      pp[2 + d] = O;
+      if (d == 0) {
+        pp[0] = M;
+        pp[1] = L;
+      }
+    }
+  }
+  if (nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(a.ticket + b * a.n_kv + kh, 1) == nsplit - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid == 0) a.ticket[b * a.n_kv + kh] = 0;
+  for (int i = tid; i < n_rep * HD; i += BA_THREADS) {
+    const int r = i / HD, d = i % HD;
+    const size_t head = size_t(b) * a.n_heads + size_t(kh) * n_rep + r;
+    const float* pb = a.part + head * a.max_splits * pstride;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(pb + sp * pstride));
+    float L = 0.0f, O = 0.0f;
+#pragma unroll 4
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float f = expf(__ldcg(pb + sp * pstride) - M);
+      L += __ldcg(pb + sp * pstride + 1) * f;
+      O += __ldcg(pb + sp * pstride + 2 + d) * f;
+    }
+    a.out[head * HD + d] = L > 0.0f ? O / L : 0.0f;
   }
 }
 
 int g_bd_sms = 0;
+// thread-block clusters of 1, 2, 4, 8 CTAs that fit on the GPU at once, per
+// [NB = 16, 32][Q4_K-only, with Q6_K] shared-memory footprint (0: not queried)
+int g_bd_cap[2][2][4] = {};
 
 template <typename Kern, typename... Args>
 cudaError_t bd_launch(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
@@ -623,14 +982,48 @@ void batch_gemm_plan(BatchGemmArgs& a, int epi) {
     if (cudaDeviceGetAttribute(&g_bd_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_bd_sms <= 0)
       g_bd_sms = 148;
   }
+  // K slices (one cluster per tile): the most that still run as a single wave,
+  // i.e. every tile's cluster resident at once (more slices = less K per CTA)
   const int tiles = batch_gemm_tiles(a, epi), nsb = a.K / QK_K;
   bool q6 = false;
   for (int i = 0; i < a.nseg; ++i) q6 |= a.seg[i].dtype == DT_Q6K;
-  const int target = (q6 ? 1 : 2) * g_bd_sms;  // resident CTAs of one wave
-  int splits = std::min(nsb, std::max(1, (target + tiles - 1) / tiles));
+  const int* cap = g_bd_cap[a.B > 16 ? 1 : 0][q6 ? 1 : 0];
+  int splits = 1;
+  for (int si = 3; si >= 1; --si) {
+    const int sz = 1 << si;
+    const int c = cap[si] > 0 ? cap[si] : g_bd_sms / sz;
+    if (sz <= nsb && tiles <= c) {
+      splits = sz;
+      break;
+    }
+  }
   const int per = (nsb + splits - 1) / splits;
   a.sb_per_split = per;
   a.splits = (nsb + per - 1) / per;
+}
+
+template <int NB>
+void bd_query_capacity(int (&cap)[2][4]) {
+  for (int q6 = 0; q6 < 2; ++q6)
+    for (int si = 0; si < 4; ++si) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 1u << si);
+      cfg.blockDim = dim3(BD_THREADS);
+      cfg.dynamicSmemBytes = bd_smem<NB>(q6 ? Q6K_DEV_BYTES : Q4K_BYTES);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1;
+      attr[0].val.clusterDim.y = 1u << si;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, bgemm_kernel<NB>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+      cap[q6][si] = n;
+    }
 }
 
 cudaError_t batch_configure() {
@@ -639,6 +1032,14 @@ cudaError_t batch_configure() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(bgemm_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(bd_smem<32>(Q6K_DEV_BYTES)));
+  if (e == cudaSuccess) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&g_bd_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_bd_sms <= 0)
+      g_bd_sms = 148;
+    bd_query_capacity<16>(g_bd_cap[0]);
+    bd_query_capacity<32>(g_bd_cap[1]);
+  }
   return e;
 }
 
@@ -648,10 +1049,37 @@ cudaError_t launch_batch_gemm(BatchGemmArgs a, int epi, cudaStream_t s) {
   int bb = Q4K_BYTES;
   for (int i = 0; i < a.nseg; ++i)
     if (a.seg[i].dtype == DT_Q6K) bb = Q6K_DEV_BYTES;
-  const dim3 grid(batch_gemm_tiles(a, epi), a.splits);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(batch_gemm_tiles(a, epi), a.splits);
+  cfg.blockDim = dim3(BD_THREADS);
+  cfg.dynamicSmemBytes = a.B <= 16 ? bd_smem<16>(bb) : bd_smem<32>(bb);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;  // the K slices of a tile: one cluster
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = unsigned(a.splits);
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = a.B <= 16 ? cudaLaunchKernelEx(&cfg, bgemm_kernel<16>, a, epi)
+                                  : cudaLaunchKernelEx(&cfg, bgemm_kernel<32>, a, epi);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t launch_batch_attention(const AttnArgs& a, cudaStream_t s) {
+  if (a.n_heads % a.n_kv != 0 || a.n_heads / a.n_kv > BA_NR || a.chunk < 1) return cudaErrorInvalidValue;
+  const dim3 grid(a.n_kv, a.T, a.max_splits);
   cudaError_t e;
-  if (a.B <= 16) e = bd_launch(bgemm_kernel<16>, grid, dim3(BD_THREADS), bd_smem<16>(bb), s, a, epi);
-  else e = bd_launch(bgemm_kernel<32>, grid, dim3(BD_THREADS), bd_smem<32>(bb), s, a, epi);
+  if (a.head_dim == 64)
+    e = a.kv_half ? bd_launch(battn_kernel<64, __half>, grid, dim3(BA_THREADS), 0, s, a)
+                  : bd_launch(battn_kernel<64, float>, grid, dim3(BA_THREADS), 0, s, a);
+  else if (a.head_dim == 128)
+    e = a.kv_half ? bd_launch(battn_kernel<128, __half>, grid, dim3(BA_THREADS), 0, s, a)
+                  : bd_launch(battn_kernel<128, float>, grid, dim3(BA_THREADS), 0, s, a);
+  else
+    return cudaErrorInvalidValue;
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
@@ -665,7 +1093,7 @@ cudaError_t launch_batch_embed(const float* emb, int vocab, int hidden, const St
 cudaError_t launch_batch_sample(const float* logits, int vocab, StepState* st, uint32_t* hist, int hist_cap,
                                 uint32_t* pen_cnt, float rep, int B, cudaStream_t s) {
   const cudaError_t e =
-      bd_launch(bsample_kernel, dim3(B), dim3(512), 0, s, logits, vocab, st, hist, hist_cap, pen_cnt, rep);
+      bd_launch(bsample_kernel, dim3(B, BS_SPLIT), dim3(512), 0, s, logits, vocab, st, hist, hist_cap, pen_cnt, rep);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 

@@ -521,13 +521,12 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) float asmem[];
   pdl_trigger();
   pdl_wait();
-  const int kh = blockIdx.x, t = blockIdx.y, split = blockIdx.z;
-  const StepState* st = a.batch ? a.st + t : a.st;
+  const StepState* st = a.st;
   if (st->done) return;
+  const int kh = blockIdx.x, t = blockIdx.y, split = blockIdx.z;
   const int n_rep = a.n_heads / a.n_kv;
-  // batched decode: sequence t, one query at its position, its own cache
-  const int kv_total = a.batch ? st->kv_len + 1 : st->kv_len + a.T;
-  const int limit = a.batch ? st->position : st->position + t;
+  const int kv_total = st->kv_len + a.T;
+  const int limit = st->position + t;
   const int nkeys = min(kv_total, limit + 1);
   const int nsplit = (nkeys + a.chunk - 1) / a.chunk;
   if (split >= nsplit) return;
@@ -548,9 +547,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnArgs a) {
     ml[2 * r] = -INFINITY;
     ml[2 * r + 1] = 0.0f;
   }
-  const size_t seq_off = a.batch ? size_t(t) * a.seq_stride : 0;
-  const KT* Kp = reinterpret_cast<const KT*>(a.kc) + seq_off + size_t(kh) * a.max_seq * HD;
-  const KT* Vp = reinterpret_cast<const KT*>(a.vc) + seq_off + size_t(kh) * a.max_seq * HD;
+  const KT* Kp = reinterpret_cast<const KT*>(a.kc) + size_t(kh) * a.max_seq * HD;
+  const KT* Vp = reinterpret_cast<const KT*>(a.vc) + size_t(kh) * a.max_seq * HD;
   constexpr int MAXI = 16;  // (n_rep * HD) / ATT_THREADS <= 16
   const int ni = (n_rep * HD + ATT_THREADS - 1) / ATT_THREADS;
   float acc[MAXI];

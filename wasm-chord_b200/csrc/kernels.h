@@ -147,9 +147,8 @@ struct AttnArgs {
   int max_splits;
   float scale;        // 1 / sqrt(head_dim)
   const StepState* st;
-  // batched decode: "token" t is sequence t with one query at st[t].position over
-  // its own cache (kc / vc + t * seq_stride elements); 0: the T tokens of one sequence
-  int batch;
+  // launch_batch_attention: "token" t is sequence t with one query at
+  // st[t].position over its own cache (kc / vc + t * seq_stride elements)
   size_t seq_stride;
 };
 constexpr int ATT_TILE = 32;  // keys staged in shared memory per pass
@@ -256,8 +255,9 @@ cudaError_t launch_decode_step(const MkArgs& a, size_t smem, cudaStream_t s);
 // raw quant and the B operand the activation split into fp16 hi + lo halves;
 // each Q4_K sub-block (32 values) / Q6_K sub-block (16) accumulates into its
 // own TMEM columns and the CUDA cores apply y += d*sc * dot - dmin*m * sum(x).
-// K is split over CTAs for occupancy; the last CTA of a tile sums the slices
-// in slice order (deterministic) and runs the fused epilogue.
+// K is split over the CTAs of one thread-block cluster per tile; the slices are
+// added in slice order over distributed shared memory (deterministic) and the
+// cluster's CTAs share the fused epilogue.
 enum BatchEpi { BEPI_STORE = 0, BEPI_RESID = 1, BEPI_SWIGLU = 2, BEPI_QKV = 3 };
 constexpr int BATCH_MAX = 32;   // sequences of one batched step (MMA N <= 32)
 constexpr int BATCH_TILE = 128; // weight rows of one tile (BEPI_SWIGLU: 64 gate + 64 up rows)
@@ -271,18 +271,16 @@ struct BatchGemmArgs {
   const float* x;        // [B][ldx]
   int ldx;
   const float* norm_w;   // RMSNorm weight of the input (null: no norm)
-  const float* sq_in;    // [sq_tiles][B] partial sums of squares of x (summed in tile order)
+  const float* sq_in;    // [sq_tiles][B] partial sums of squares of x (summed in order)
   int sq_tiles;
   float eps;
-  int splits;            // K slices (set by launch_batch_gemm)
-  int sb_per_split;      // super-blocks per slice (set by launch_batch_gemm)
-  float* part;           // [splits][B][rows] slice results
-  int* ticket;           // [tiles] zero between launches
+  int splits;            // K slices = CTAs of a tile's cluster (set by batch_gemm_plan, <= 8)
+  int sb_per_split;      // super-blocks per slice (set by batch_gemm_plan)
   float* y;              // BEPI_STORE / RESID / SWIGLU output [B][ldy]
   int ldy;
   const float* resid;    // BEPI_RESID [B][ldr]
   int ldr;
-  float* sq_out;         // BEPI_RESID: [tiles][B] sums of squares of the tile's outputs
+  float* sq_out;         // BEPI_RESID: [tiles * splits][B] sums of squares of each CTA's outputs
   // BEPI_QKV: RoPE'd queries to q, RoPE'd keys and values appended to each sequence's cache
   float* q;
   int ldq;
@@ -294,11 +292,16 @@ struct BatchGemmArgs {
   const float* rope_sin;
   StepState* st;         // [B]
 };
-// tiles and slices of a launch (CTAs = tiles * splits) and its shared memory
+// tiles and slices of a launch (CTAs = tiles * splits; a BEPI_RESID launch
+// writes tiles * splits partial sums of squares per sequence)
 int batch_gemm_tiles(const BatchGemmArgs& a, int epi);
 void batch_gemm_plan(BatchGemmArgs& a, int epi);
 cudaError_t batch_configure();
 cudaError_t launch_batch_gemm(BatchGemmArgs a, int epi, cudaStream_t s);
+// Decode attention of B sequences (one query each, n_heads / n_kv <= 8): grid
+// (n_kv, B, max_splits), a.chunk keys per split, merged by the last CTA of a
+// (sequence, kv head); K rows and V rows are read straight from the cache
+cudaError_t launch_batch_attention(const AttnArgs& a, cudaStream_t s);
 // x[b] = embedding row of sequence b's last token; sq[b] = sum of squares of x[b]
 cudaError_t launch_batch_embed(const float* emb, int vocab, int hidden, const StepState* st, const uint32_t* hist,
                                int hist_cap, float* x, float* sq, int B, cudaStream_t s);

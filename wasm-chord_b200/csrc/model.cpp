@@ -176,7 +176,8 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     // sampler history and penalty counts; the tensor-core step needs 128-row
     // tiles that never straddle q / k / v, and 64-row gate / up halves
     bslots_ = tp_ == 1 ? std::min<uint32_t>(std::max<uint32_t>(opt.max_batch, 1), BATCH_MAX) : 1;
-    batch_ok_ = bslots_ > 1 && c.hidden % BATCH_TILE == 0 && kvd % BATCH_TILE == 0 && c.ffn % 64 == 0;
+    batch_ok_ = bslots_ > 1 && c.hidden % BATCH_TILE == 0 && kvd % BATCH_TILE == 0 && c.ffn % 64 == 0 &&
+                c.heads / c.kv_heads <= 8;
     if (!batch_ok_) bslots_ = 1;
     // KV cache (kv_cache.rs:6-34), [slot][L][n_kv][max_seq][hd]
     kv_layer_elems_ = size_t(kv_l_) * max_seq_ * hd;
@@ -226,32 +227,9 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     if (batch_ok_) {
       const size_t B = bslots_, H = c.hidden;
       logits_b_ = static_cast<float*>(dalloc(sizeof(float) * B * c.vocab));
-      sqx_ = static_cast<float*>(dalloc(sizeof(float) * B * (H / BATCH_TILE)));
-      sqh_ = static_cast<float*>(dalloc(sizeof(float) * B * (H / BATCH_TILE)));
-      // K-slice scratch and tickets: the largest need over the step's contractions
-      size_t part = 0;
-      int tiles_max = 0;
-      auto need = [&](int rows, int K, int epi, int dtype) {
-        BatchGemmArgs a{};
-        a.nseg = 1;
-        a.seg[0].dtype = dtype;
-        a.rows = rows;
-        a.K = K;
-        batch_gemm_plan(a, epi);
-        const int tiles = batch_gemm_tiles(a, epi);
-        tiles_max = std::max(tiles_max, tiles);
-        part = std::max(part, size_t(a.splits) * B * size_t(tiles) * BATCH_TILE);
-      };
-      for (int dt : {DT_Q4K, DT_Q6K}) {
-        need(int(c.hidden + 2 * kvd), int(H), BEPI_QKV, dt);
-        need(int(H), int(H), BEPI_RESID, dt);
-        need(int(c.ffn), int(H), BEPI_SWIGLU, dt);
-        need(int(H), int(c.ffn), BEPI_RESID, dt);
-        need(int(c.vocab), int(H), BEPI_STORE, dt);
-      }
-      bpart_ = static_cast<float*>(dalloc(sizeof(float) * part));
-      bticket_ = static_cast<int*>(dalloc(sizeof(int) * size_t(tiles_max)));
-      check(cudaMemset(bticket_, 0, sizeof(int) * size_t(tiles_max)), "clear tickets");
+      // per-CTA sums of squares of the residual stream: tiles x K slices (<= 8) per sequence
+      sqx_ = static_cast<float*>(dalloc(sizeof(float) * B * (H / BATCH_TILE) * 8));
+      sqh_ = static_cast<float*>(dalloc(sizeof(float) * B * (H / BATCH_TILE) * 8));
       asplits_ = int((max_seq_ + BATCH_CHUNK - 1) / BATCH_CHUNK);
       apart_ = static_cast<float*>(dalloc(sizeof(float) * B * c.heads * size_t(asplits_) * (hd + 2)));
       aticket_ = static_cast<int*>(dalloc(sizeof(int) * B * c.kv_heads));
@@ -1057,9 +1035,9 @@ void Model::bind_seq(uint32_t b) {
   pen_cnt_ = pen_base_ + size_t(b) * cfg_.vocab;
 }
 
-void Model::batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, const float* x, int ldx,
-                       const float* norm_w, const float* sq_in, int sq_tiles, float eps, int epi, float* y, int ldy,
-                       const float* resid, int ldr, float* sq_out, int layer) {
+int Model::batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, const float* x, int ldx,
+                      const float* norm_w, const float* sq_in, int sq_tiles, float eps, int epi, float* y, int ldy,
+                      const float* resid, int ldr, float* sq_out, int layer) {
   BatchGemmArgs a{};
   for (int i = 0; i < nseg; ++i) {
     a.seg[i].w = segs[i].ptr;
@@ -1076,8 +1054,6 @@ void Model::batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, 
   a.sq_in = sq_in;
   a.sq_tiles = sq_tiles;
   a.eps = eps;
-  a.part = bpart_;
-  a.ticket = bticket_;
   a.y = y;
   a.ldy = ldy;
   a.resid = resid;
@@ -1101,6 +1077,8 @@ void Model::batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, 
   a.st = st_base_;
   check(launch_batch_gemm(a, epi, stream_), "batched GEMM");
   ++batch_launches_;
+  batch_gemm_plan(a, epi);
+  return batch_gemm_tiles(a, epi) * a.splits;  // partial sums of squares a BEPI_RESID launch leaves
 }
 
 // One greedy decode step of slots 0..B-1 (the per-sequence semantics of the
@@ -1110,16 +1088,15 @@ void Model::enqueue_batch_step(int B) {
   const ModelConfig& c = cfg_;
   const int H = int(c.hidden), F = int(ffn_l_), HQ = int(hq_), V = int(c.vocab);
   const int qkv_rows = HQ + 2 * int(kvd_l_);
-  const int res_tiles = H / BATCH_TILE;
+  int sq_x = 1;  // entries of the running sums of squares of x (the embedding kernel writes one)
   batch_launches_ = 0;
   check(launch_batch_embed(emb_, V, H, st_base_, hist_base_, int(hist_cap_), x_, sqx_, B, stream_), "embed");
   ++batch_launches_;
   for (uint32_t l = 0; l < c.layers; ++l) {
     const DevLayer& L = layers_[l];
-    const int sq_tiles = l == 0 ? 1 : res_tiles;  // layer 0 reads the embedding's whole-row sums
     const DevWeight qkv[3] = {L.q, L.k, L.v};
-    batch_gemm(qkv, 3, qkv_rows, H, B, x_, H, L.attn_norm, sqx_, sq_tiles, 1e-6f, BEPI_QKV, nullptr, 0, nullptr, 0,
-               nullptr, int(l));
+    batch_gemm(qkv, 3, qkv_rows, H, B, x_, H, L.attn_norm, sqx_, sq_x, 1e-6f, BEPI_QKV, nullptr, 0, nullptr, 0, nullptr,
+               int(l));
     AttnArgs a{};
     a.q = q_;
     const size_t esz = opt_.kv_half ? 2 : 4;
@@ -1138,21 +1115,18 @@ void Model::enqueue_batch_step(int B) {
     a.max_splits = asplits_;
     a.scale = attn_scale_;
     a.st = st_base_;
-    a.batch = 1;
     a.seq_stride = seq_kv_elems_;
-    check(launch_attention(a, stream_), "attention");
+    check(launch_batch_attention(a, stream_), "attention");
     ++batch_launches_;
     const DevWeight o[1] = {L.o};
-    batch_gemm(o, 1, H, HQ, B, att_, HQ, nullptr, nullptr, 0, 0.0f, BEPI_RESID, h_, H, x_, H, sqh_, -1);
+    const int sq_h = batch_gemm(o, 1, H, HQ, B, att_, HQ, nullptr, nullptr, 0, 0.0f, BEPI_RESID, h_, H, x_, H, sqh_, -1);
     const DevWeight gu[2] = {L.gate, L.up};
-    batch_gemm(gu, 2, F, H, B, h_, H, L.ffn_norm, sqh_, res_tiles, 1e-6f, BEPI_SWIGLU, act_, F, nullptr, 0, nullptr,
-               -1);
+    batch_gemm(gu, 2, F, H, B, h_, H, L.ffn_norm, sqh_, sq_h, 1e-6f, BEPI_SWIGLU, act_, F, nullptr, 0, nullptr, -1);
     const DevWeight dn[1] = {L.down};
-    batch_gemm(dn, 1, H, F, B, act_, F, nullptr, nullptr, 0, 0.0f, BEPI_RESID, x_, H, h_, H, sqx_, -1);
+    sq_x = batch_gemm(dn, 1, H, F, B, act_, F, nullptr, nullptr, 0, 0.0f, BEPI_RESID, x_, H, h_, H, sqx_, -1);
   }
   const DevWeight head[1] = {lm_head_};
-  batch_gemm(head, 1, V, H, B, x_, H, out_norm_, sqx_, c.layers ? res_tiles : 1, c.eps, BEPI_STORE, logits_b_, V,
-             nullptr, 0, nullptr, -1);
+  batch_gemm(head, 1, V, H, B, x_, H, out_norm_, sqx_, sq_x, c.eps, BEPI_STORE, logits_b_, V, nullptr, 0, nullptr, -1);
   check(launch_batch_sample(logits_b_, V, st_base_, hist_base_, int(hist_cap_), pen_base_, rep_, B, stream_),
         "sampler");
   ++batch_launches_;

@@ -115,9 +115,10 @@ class Model {
   // counts) at batch slot b; slot 0 is the single-sequence state
   void bind_seq(uint32_t b);
   void enqueue_batch_step(int B);
-  void batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, const float* x, int ldx,
-                  const float* norm_w, const float* sq_in, int sq_tiles, float eps, int epi, float* y, int ldy,
-                  const float* resid, int ldr, float* sq_out, int layer);
+  // one batched contraction; returns the partial sums of squares it leaves in sq_out
+  int batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, const float* x, int ldx,
+                 const float* norm_w, const float* sq_in, int sq_tiles, float eps, int epi, float* y, int ldy,
+                 const float* resid, int ldr, float* sq_out, int layer);
   void build_decode_step();
   void launch_decode_step_kernel(bool gen);
 
@@ -216,10 +217,8 @@ class Model {
   uint32_t* hist_base_ = nullptr;
   uint32_t* pen_base_ = nullptr;
   float* logits_b_ = nullptr;   // [bslots][vocab]
-  float* sqx_ = nullptr;        // [hidden / 128][bslots] sums of squares of the residual stream x
+  float* sqx_ = nullptr;        // [tiles x slices][bslots] partial sums of squares of the residual stream x
   float* sqh_ = nullptr;        // the same for h (after attention)
-  float* bpart_ = nullptr;      // K-slice partial sums of the batched GEMMs
-  int* bticket_ = nullptr;
   float* apart_ = nullptr;      // attention split partials [bslots][heads][asplits][hd + 2]
   int* aticket_ = nullptr;      // [bslots][kv_heads]
   int asplits_ = 0;
