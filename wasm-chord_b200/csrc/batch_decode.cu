@@ -836,9 +836,29 @@ __global__ void __launch_bounds__(BA_THREADS) battn_kernel(const AttnArgs a) {
 #pragma unroll
     for (int d = 0; d < DPL; ++d) o[r][d] = 0.0f;
   }
+  // V rows of the warp's 32 keys are requested before the scores are computed
+  // (raw 32-bit words, when they fit in registers), so their latency overlaps it
+  constexpr int RW = DPL * int(sizeof(KT)) / 4;  // 32-bit words of V per lane per key
+  constexpr bool PRE = RW <= 2;
   for (int k0 = j0 + warp * 32; k0 < j1; k0 += 4 * 32) {
     const int j = k0 + lane;
     const bool valid = j < j1;
+    const int nk = min(32, j1 - k0);
+    const KT* vb = Vp + size_t(k0) * HD + lane * DPL;
+    uint32_t vr[PRE ? 32 : 1][PRE ? RW : 1];
+    if constexpr (PRE) {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        if (jj < nk) {
+          const uint32_t* src = reinterpret_cast<const uint32_t*>(vb + size_t(jj) * HD);
+#pragma unroll
+          for (int w = 0; w < RW; ++w) vr[jj][w] = src[w];
+        } else {
+#pragma unroll
+          for (int w = 0; w < RW; ++w) vr[jj][w] = 0u;
+        }
+      }
+    }
     float s[BA_NR];
 #pragma unroll
     for (int r = 0; r < BA_NR; ++r) s[r] = 0.0f;
@@ -871,19 +891,52 @@ __global__ void __launch_bounds__(BA_THREADS) battn_kernel(const AttnArgs a) {
       ps[warp][lane][r] = p;
     }
     __syncwarp();
-    const int nk = min(32, j1 - k0);
-    const KT* vb = Vp + size_t(k0) * HD + lane * DPL;
-#pragma unroll 4
-    for (int jj = 0; jj < nk; ++jj) {
-      float v[DPL];
-      loadn<DPL, KT>(vb + size_t(jj) * HD, v);
-      const float4 p0 = *reinterpret_cast<const float4*>(&ps[warp][jj][0]);
-      const float4 p1 = *reinterpret_cast<const float4*>(&ps[warp][jj][4]);
-      const float pr[BA_NR] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    if constexpr (PRE) {
 #pragma unroll
-      for (int r = 0; r < BA_NR; ++r)
+      for (int jj = 0; jj < 32; ++jj) {
+        if (jj >= nk) break;
+        float v[DPL];
+        if constexpr (sizeof(KT) == 2) {
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) o[r][d] += pr[r] * v[d];
+          for (int w = 0; w < RW; ++w) {
+            const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&vr[jj][w]));
+            v[2 * w] = t.x;
+            v[2 * w + 1] = t.y;
+          }
+        } else {
+#pragma unroll
+          for (int w = 0; w < RW; ++w) v[w] = __uint_as_float(vr[jj][w]);
+        }
+        const float4 p0 = *reinterpret_cast<const float4*>(&ps[warp][jj][0]);
+        const float4 p1 = *reinterpret_cast<const float4*>(&ps[warp][jj][4]);
+        const float pr[BA_NR] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+        for (int r = 0; r < BA_NR; ++r)
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) o[r][d] += pr[r] * v[d];
+      }
+    } else {
+      for (int j8 = 0; j8 < nk; j8 += 8) {  // 8 rows in flight at a time
+        float v[8][DPL];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (j8 + e < nk) loadn<DPL, KT>(vb + size_t(j8 + e) * HD, v[e]);
+          else {
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) v[e][d] = 0.0f;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float4 p0 = *reinterpret_cast<const float4*>(&ps[warp][min(j8 + e, 31)][0]);
+          const float4 p1 = *reinterpret_cast<const float4*>(&ps[warp][min(j8 + e, 31)][4]);
+          const float pr[BA_NR] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+          for (int r = 0; r < BA_NR; ++r)
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) o[r][d] += pr[r] * v[e][d];
+        }
+      }
     }
     __syncwarp();
   }
