@@ -10,7 +10,7 @@ namespace wcb {
 
 namespace {
 
-constexpr int T_MAX = 256;        // tokens per forward launch (longer prompts are split, same results)
+constexpr int T_MAX = 2048;       // tokens per forward launch (longer prompts are split, same results)
 constexpr int DECODE_CHUNK = 32;  // keys per attention split in decode steps
 constexpr int BATCH_CHUNK = 256;  // keys per attention split in batched decode steps
 
@@ -193,7 +193,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     build_rope(max_seq_);
     attn_scale_ = 1.0f / std::sqrt(float(hd));  // attention.rs:363
 
-    t_max_ = T_MAX;
+    t_max_ = int(std::min<uint32_t>(T_MAX, std::max<uint32_t>(max_seq_, 1)));
     st_ = static_cast<StepState*>(dalloc(sizeof(StepState) * bslots_));
     check(cudaMemset(st_, 0, sizeof(StepState) * bslots_), "clear state");
     st_base_ = st_;
