@@ -114,11 +114,21 @@ __device__ __forceinline__ void split_store(uint8_t* hi_tile, uint8_t* lo_tile, 
   *reinterpret_cast<uint4*>(lo_tile + off) = *reinterpret_cast<const uint4*>(l);
 }
 
+// the three 16-byte words of a Q4_K block that 64 values [64*kq, 64*kq+64) need
+struct Q4Raw {
+  uint4 hd, qa, qb;
+};
+__device__ __forceinline__ Q4Raw q4k_raw(const uint8_t* blk, int kq) {
+  Q4Raw r;
+  r.hd = *reinterpret_cast<const uint4*>(blk);
+  r.qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * kq);
+  r.qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * kq);
+  return r;
+}
+
 // 64 dequantised values [64*kq, 64*kq+64) of a Q4_K block (quant.rs:58-115)
-__device__ __forceinline__ void deq_q4k_64(const uint8_t* blk, int kq, float (&w)[64]) {
-  const uint4 hd = *reinterpret_cast<const uint4*>(blk);
-  const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * kq);
-  const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * kq);
+__device__ __forceinline__ void deq_q4k_64(const Q4Raw& raw, int kq, float (&w)[64]) {
+  const uint4 hd = raw.hd, qa = raw.qa, qb = raw.qb;
   const float d = halfbits(hd.x & 0xFFFFu), dmin = halfbits(hd.x >> 16);
   const uint8_t* sc = reinterpret_cast<const uint8_t*>(&hd) + 4;
   uint32_t s0, m0, s1, m1;
@@ -201,6 +211,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
+  // the weight thread's first block, then each next one requested before the current is used
+  Q4Raw wraw{};
+  const uint8_t* wrow = nullptr;
+  if (DT == DT_Q4K && tid < TILE_N && r0 + tid < total_rows) {
+    wrow = weight_row<DT>(a, r0 + tid, EPI, row_bytes);
+    wraw = q4k_raw(wrow, 0);
+  }
   for (int kb = 0; kb < nkb; ++kb) {
     const int buf = kb & 1;
     if (kb >= 2) ok &= bar_wait(bar + buf, uint32_t(((kb - 2) >> 1) & 1));
@@ -214,8 +231,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a
       if (r < total_rows) {
         const uint8_t* row = weight_row<DT>(a, r, EPI, row_bytes);
         const int b = (kb * KB) / QK_K, kq = (kb * KB / 64) & 3;
-        if (DT == DT_Q4K) deq_q4k_64(row + size_t(b) * Q4K_BYTES, kq, w);
-        else deq_q6k_64(row + size_t(b) * Q6K_DEV_BYTES, kq, w);
+        if (DT == DT_Q4K) {
+          deq_q4k_64(wraw, kq, w);
+          if (kb + 1 < nkb) {
+            const int b1 = ((kb + 1) * KB) / QK_K, kq1 = ((kb + 1) * KB / 64) & 3;
+            wraw = q4k_raw(wrow + size_t(b1) * Q4K_BYTES, kq1);
+          }
+        } else {
+          deq_q6k_64(row + size_t(b) * Q6K_DEV_BYTES, kq, w);
+        }
       } else {
 #pragma unroll
         for (int j = 0; j < 64; ++j) w[j] = 0.0f;
@@ -237,11 +261,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a
           const float4 f = *reinterpret_cast<const float4*>(xr + j);
           xv[j] = f.x; xv[j + 1] = f.y; xv[j + 2] = f.z; xv[j + 3] = f.w;
         }
-        if (PRO == PRO_RMSNORM) {  // x = h / m * w (candle_tensor_backend.rs:30-57)
-          const float m = row_m[t];
+        if (PRO == PRO_RMSNORM) {  // x = h / m * w (candle_tensor_backend.rs:30-57): h * w staged
+          // here, the per-token 1/m applied to the sums (sum W (h w / m) = (1/m) sum W (h w))
           const float* nw = a.norm_w + kb * KB;
 #pragma unroll
-          for (int j = 0; j < 64; ++j) xv[j] = __fmul_rn(__fdiv_rn(xv[j], m), nw[j]);
+          for (int j = 0; j < 64; ++j) xv[j] = __fmul_rn(xv[j], nw[j]);
         }
       } else {
 #pragma unroll
@@ -285,6 +309,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a
     float v[16];
     tmem_ld16(tmem + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(cbase + c16), v);
     if (!ok || t >= a.M) continue;
+    if (PRO == PRO_RMSNORM) {
+      const float m = row_m[t];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = __fdiv_rn(v[e], m);
+    }
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int r = r0 + cbase + c16 + e;  // virtual weight row

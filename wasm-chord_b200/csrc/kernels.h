@@ -153,6 +153,12 @@ struct AttnArgs {
 };
 constexpr int ATT_TILE = 32;  // keys staged in shared memory per pass
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+// Prefill attention on the tensor cores (mma.sync, fp16 hi/lo operands, fp32
+// accumulate): the T query tokens of a forward chunk (a.chunk / a.max_splits /
+// a.part / a.ticket unused). Head dims 64 / 128, n_heads / n_kv in {1, 2, 4, 8}.
+cudaError_t attention_prefill_configure();
+bool attention_prefill_supported(int n_heads, int n_kv, int head_dim);
+cudaError_t launch_attention_prefill(const AttnArgs& a, cudaStream_t s);
 
 // ------------------------------------------------ persistent decode step --
 // One launch runs a whole decode step (T = 1): every layer's QKV + RoPE + KV

@@ -95,6 +95,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
   }
   check(gemv_configure_all(), "configure GEMV kernels");
   check(gemm_tc_configure(), "configure GEMM kernels");
+  check(attention_prefill_configure(), "configure prefill attention");
   set_pdl(!(opt.flags & 2));
   try {
     // token embeddings (model.rs:432-446): first name that loads
@@ -501,7 +502,10 @@ void Model::enqueue_layers(int T, bool decode) {
     }
     a.scale = attn_scale_;
     a.st = st_;
-    check(launch_attention(a, stream_), "attention");
+    if (T >= TC_MIN_TOKENS && !(opt_.flags & 4) && attention_prefill_supported(a.n_heads, a.n_kv, hd))
+      check(launch_attention_prefill(a, stream_), "attention");  // prefill chunk: tensor cores
+    else
+      check(launch_attention(a, stream_), "attention");
     ++launches_;
     // output projection + residual (attention.rs:182-191, layer.rs:68); with several
     // ranks each holds the columns of its heads: partial sums, all-reduced
