@@ -25,33 +25,6 @@ namespace {
 constexpr int FA_THREADS = 256;  // 8 warps
 constexpr int FA_BK = 64;        // keys per tile
 
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// two 8 x 8 fp16 matrices, transposed: lanes 0-7 give the row addresses of
-// matrix 0, lanes 8-15 those of matrix 1
-__device__ __forceinline__ void ldsm_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];\n" : "=r"(r0), "=r"(r1) : "r"(addr));
-}
-
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// v = hi + lo with hi = fp16(v), lo = fp16(v - hi), for a pair of values
-__device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
-  const __half2 h = __floats2half2_rn(x, y);
-  const float2 hf = __half22float2(h);
-  hi = *reinterpret_cast<const uint32_t*>(&h);
-  lo = pack_half2(x - hf.x, y - hf.y);
-}
-
 template <int HD, bool F32KV>
 struct FaSmem {
   static constexpr int PITCH = HD + 8;  // halves per staged row (conflict-free fragment loads)

@@ -1001,6 +1001,199 @@ __global__ void __launch_bounds__(BA_THREADS) battn_kernel(const AttnArgs a) {
   }
 }
 
+// The same decode attention on the tensor cores, for an fp16 cache: per warp,
+// 32-key tiles of its 64 keys are staged in shared memory (cp.async), the n_rep
+// query heads are the rows of a 16-row mma.sync.m16n8k16 operand (rows n_rep..15
+// are zero), S = Q K^T and O += P V run as fp16 products with q and p split
+// into hi + lo halves, and the running softmax works on the accumulator
+// fragments. Warps and splits merge as in battn_kernel.
+constexpr int BF_TS = 32;  // keys per staged tile
+
+template <int HD>
+__global__ void __launch_bounds__(BA_THREADS) bfa_kernel(const AttnArgs a) {
+  constexpr int P = HD + 8;  // halves per staged row (conflict-free fragment loads)
+  extern __shared__ __align__(16) uint8_t fsm[];
+  __half* Kw = reinterpret_cast<__half*>(fsm) + (threadIdx.x >> 5) * (2 * BF_TS * P);
+  __half* Vw = Kw + BF_TS * P;
+  __shared__ float wm[4][BA_NR], wl[4][BA_NR];
+  __shared__ __align__(16) float wo[4][BA_NR][HD];
+  __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int kh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;
+  const StepState* st = a.st + b;
+  if (st->done) return;
+  const int nkeys = st->kv_len + 1;
+  const int nsplit = (nkeys + a.chunk - 1) / a.chunk;
+  if (split >= nsplit) return;
+  const int j0 = split * a.chunk, j1 = min(j0 + a.chunk, nkeys);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int n_rep = a.n_heads / a.n_kv;
+  const size_t base = size_t(b) * a.seq_stride + size_t(kh) * a.max_seq * HD;
+  const __half* Kg = reinterpret_cast<const __half*>(a.kc) + base;
+  const __half* Vg = reinterpret_cast<const __half*>(a.vc) + base;
+  // Q rows: head g of the kv head (zero for g >= n_rep); rows 8..15 are zero
+  uint32_t qh[HD / 16][4], ql[HD / 16][4];
+  {
+    const float* qr = a.q + (size_t(b) * a.n_heads + size_t(kh) * n_rep + min(g, n_rep - 1)) * HD;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      const int c = ks * 16 + 2 * tq;
+      float2 x0 = *reinterpret_cast<const float2*>(qr + c), x2 = *reinterpret_cast<const float2*>(qr + c + 8);
+      if (g >= n_rep) x0 = x2 = make_float2(0.f, 0.f);
+      split2(x0.x, x0.y, qh[ks][0], ql[ks][0]);
+      split2(x2.x, x2.y, qh[ks][2], ql[ks][2]);
+      qh[ks][1] = ql[ks][1] = qh[ks][3] = ql[ks][3] = 0u;
+    }
+  }
+  float o[HD / 8][4];
+#pragma unroll
+  for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  float m = -INFINITY, l = 0.0f;  // row g
+  const int wk0 = j0 + warp * (a.chunk / 4), wk1 = min(j1, wk0 + a.chunk / 4);
+  for (int t0 = wk0; t0 < wk1; t0 += BF_TS) {
+    const int nt = min(BF_TS, wk1 - t0);
+    __syncwarp();
+    constexpr int CH = HD / 8;  // 16-byte chunks per row
+    for (int i = lane; i < BF_TS * CH; i += 32) {
+      const int row = i / CH, c = (i % CH) * 8;
+      if (row < nt) {
+        cp_async16(Kw + row * P + c, Kg + size_t(t0 + row) * HD + c);
+        cp_async16(Vw + row * P + c, Vg + size_t(t0 + row) * HD + c);
+      } else {
+        *reinterpret_cast<uint4*>(Kw + row * P + c) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(Vw + row * P + c) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+    float sc[BF_TS / 8][4];
+#pragma unroll
+    for (int nb = 0; nb < BF_TS / 8; ++nb) {
+      sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.0f;
+      const __half* kr = Kw + (nb * 8 + g) * P + 2 * tq;
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ++ks) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + ks * 16);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + 8);
+        mma16816(sc[nb], qh[ks], b0, b1);
+        mma16816(sc[nb], ql[ks], b0, b1);
+      }
+    }
+    float mx = m;
+#pragma unroll
+    for (int nb = 0; nb < BF_TS / 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = nb * 8 + 2 * tq + e;
+        const float v = key < nt ? sc[nb][e] * a.scale : -INFINITY;
+        sc[nb][e] = v;
+        mx = fmaxf(mx, v);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float cf = expf(m - mx);  // m = -inf on the first tile: 0
+    float ps = 0.0f;
+#pragma unroll
+    for (int nb = 0; nb < BF_TS / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float p = sc[nb][e] == -INFINITY ? 0.0f : expf(sc[nb][e] - mx);
+        sc[nb][e] = p;
+        ps += p;
+      }
+      sc[nb][2] = sc[nb][3] = 0.0f;  // rows 8..15 carry nothing
+    }
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    l = l * cf + ps;
+    m = mx;
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) {
+      o[n][0] *= cf;
+      o[n][1] *= cf;
+    }
+#pragma unroll
+    for (int ks = 0; ks < BF_TS / 16; ++ks) {
+      uint32_t ph[4], pl[4];
+      split2(sc[2 * ks][0], sc[2 * ks][1], ph[0], pl[0]);
+      split2(sc[2 * ks + 1][0], sc[2 * ks + 1][1], ph[2], pl[2]);
+      ph[1] = pl[1] = ph[3] = pl[3] = 0u;
+      const int vrow = ks * 16 + (lane & 15);
+#pragma unroll
+      for (int n = 0; n < HD / 8; ++n) {
+        uint32_t b0, b1;
+        ldsm_x2_trans(smem_u32(Vw + vrow * P + n * 8), b0, b1);
+        mma16816(o[n], ph, b0, b1);
+        mma16816(o[n], pl, b0, b1);
+      }
+    }
+  }
+  // merge the 4 warps (a warp without keys has m = -inf, l = 0)
+  if (g < n_rep) {
+    if (tq == 0) {
+      wm[warp][g] = m;
+      wl[warp][g] = l;
+    }
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) {
+      wo[warp][g][n * 8 + 2 * tq] = o[n][0];
+      wo[warp][g][n * 8 + 2 * tq + 1] = o[n][1];
+    }
+  }
+  __syncthreads();
+  const size_t pstride = HD + 2;
+  for (int i = tid; i < n_rep * HD; i += BA_THREADS) {
+    const int r = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][r]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float f = expf(wm[w][r] - M);
+      L += wl[w][r] * f;
+      O += wo[w][r][d] * f;
+    }
+    const size_t head = size_t(b) * a.n_heads + size_t(kh) * n_rep + r;
+    if (nsplit == 1) {
+      a.out[head * HD + d] = L > 0.0f ? O / L : 0.0f;
+    } else {
+      float* pp = a.part + (head * a.max_splits + split) * pstride;
+      pp[2 + d] = O;
+      if (d == 0) {
+        pp[0] = M;
+        pp[1] = L;
+      }
+    }
+  }
+  if (nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(a.ticket + b * a.n_kv + kh, 1) == nsplit - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid == 0) a.ticket[b * a.n_kv + kh] = 0;
+  for (int i = tid; i < n_rep * HD; i += BA_THREADS) {
+    const int r = i / HD, d = i % HD;
+    const size_t head = size_t(b) * a.n_heads + size_t(kh) * n_rep + r;
+    const float* pb = a.part + head * a.max_splits * pstride;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(pb + sp * pstride));
+    float L = 0.0f, O = 0.0f;
+#pragma unroll 4
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float f = expf(__ldcg(pb + sp * pstride) - M);
+      L += __ldcg(pb + sp * pstride + 1) * f;
+      O += __ldcg(pb + sp * pstride + 2 + d) * f;
+    }
+    a.out[head * HD + d] = L > 0.0f ? O / L : 0.0f;
+  }
+}
+
 int g_bd_sms = 0;
 // thread-block clusters of 1, 2, 4, 8 CTAs that fit on the GPU at once, per
 // [NB = 16, 32][Q4_K-only, with Q6_K] shared-memory footprint (0: not queried)
@@ -1085,6 +1278,9 @@ cudaError_t batch_configure() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(bgemm_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(bd_smem<32>(Q6K_DEV_BYTES)));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(bfa_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             4 * 2 * BF_TS * (128 + 8) * 2);
   if (e == cudaSuccess) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1125,6 +1321,13 @@ cudaError_t launch_batch_attention(const AttnArgs& a, cudaStream_t s) {
   if (a.n_heads % a.n_kv != 0 || a.n_heads / a.n_kv > BA_NR || a.chunk < 1) return cudaErrorInvalidValue;
   const dim3 grid(a.n_kv, a.T, a.max_splits);
   cudaError_t e;
+  if (a.kv_half && a.chunk % (4 * BF_TS) == 0) {  // fp16 cache: the tensor-core kernel
+    const size_t smem = size_t(4) * 2 * BF_TS * (a.head_dim + 8) * 2;
+    if (a.head_dim == 64) e = bd_launch(bfa_kernel<64>, grid, dim3(BA_THREADS), smem, s, a);
+    else if (a.head_dim == 128) e = bd_launch(bfa_kernel<128>, grid, dim3(BA_THREADS), smem, s, a);
+    else return cudaErrorInvalidValue;
+    return e != cudaSuccess ? e : cudaGetLastError();
+  }
   if (a.head_dim == 64)
     e = a.kv_half ? bd_launch(battn_kernel<64, __half>, grid, dim3(BA_THREADS), 0, s, a)
                   : bd_launch(battn_kernel<64, float>, grid, dim3(BA_THREADS), 0, s, a);
