@@ -52,7 +52,12 @@ typedef struct wcb_load_opts {
   uint32_t max_batch; /* sequences per wcb_generate_batch call; 0 = 1 */
   uint32_t flags;     /* bit 0: no CUDA graphs for decode steps; bit 1: no programmatic
                          dependent launch; bit 2: no tensor-core GEMM for prefill (GEMV only);
-                         bit 3: no persistent decode-step kernel (one launch per op instead) */
+                         bit 3: no persistent decode-step kernel (one launch per op instead);
+                         bit 4: stream the layer weights from pinned host memory through a
+                         two-layer device ring, one layer ahead of the compute (models that do
+                         not fit in GPU memory; replaces the reference's Memory64 layer
+                         manager, memory64_layer_manager.rs:76-300, async_prefetch.rs:83-190).
+                         Single GPU, per-op kernels, no batched path. */
   /* Tensor parallelism (one process per GPU; no counterpart in the reference, whose
      sharding.rs is bookkeeping only). tp_size 0 or 1: the whole model on `device`.
      tp_size > 1: this process holds rank tp_rank's shard (query/KV heads, o and down

@@ -149,6 +149,9 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
 
     const uint32_t kvd = c.kv_heads * hd;
     layers_.resize(c.layers);
+    // weight streaming: layer weights to a pinned host copy, streamed through a device ring
+    wstream_ = (opt.flags & 16) && tp_ == 1 && c.layers > 0;
+    const bool th = wstream_;
     for (uint32_t l = 0; l < c.layers; ++l) {
       DevLayer& L = layers_[l];
       const std::string p = "blk." + std::to_string(l) + ".";
@@ -156,27 +159,56 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
                       uint32_t nblk) {
         std::string n = p + base + ".weight";
         if (!f.find(n)) n = p + base;
-        upload_weight(f, n, rows, c.hidden, w, true, row0, nrows, blk0, nblk);
+        upload_weight(f, n, rows, c.hidden, w, true, row0, nrows, blk0, nblk, th);
       };
+      const size_t layer_begin = (wstage_.size() + 255) / 256 * 256;
       // this rank's heads (all of them with one rank)
       attn("attn_q", c.hidden, L.q, rank_ * hq_, hq_, 0, 0);
       attn("attn_k", kvd, L.k, rank_ * kvd_l_, kvd_l_, 0, 0);
       attn("attn_v", kvd, L.v, rank_ * kvd_l_, kvd_l_, 0, 0);
       attn("attn_output", c.hidden, L.o, 0, 0, rank_ * (hq_ / QK_K), hq_ / QK_K);
-      upload_weight(f, p + "ffn_gate.weight", c.ffn, c.hidden, L.gate, true, rank_ * ffn_l_, ffn_l_);
-      upload_weight(f, p + "ffn_up.weight", c.ffn, c.hidden, L.up, true, rank_ * ffn_l_, ffn_l_);
+      upload_weight(f, p + "ffn_gate.weight", c.ffn, c.hidden, L.gate, true, rank_ * ffn_l_, ffn_l_, 0, 0, th);
+      upload_weight(f, p + "ffn_up.weight", c.ffn, c.hidden, L.up, true, rank_ * ffn_l_, ffn_l_, 0, 0, th);
       upload_weight(f, p + "ffn_down.weight", c.hidden, c.ffn, L.down, true, 0, 0, rank_ * (ffn_l_ / QK_K),
-                    ffn_l_ / QK_K);
+                    ffn_l_ / QK_K, th);
+      if (th) {
+        layer_off_.push_back(layer_begin);
+        layer_bytes_.push_back(wstage_.size() - layer_begin);
+      }
       upload_vector(f, p + "attn_norm.weight", c.hidden, 1.0f, L.attn_norm);
       upload_vector(f, p + "ffn_norm.weight", c.hidden, 1.0f, L.ffn_norm);
       if (L.gate.dtype != L.up.dtype)
         throw WcbError(E_BACKEND, "Backend error: ffn_gate and ffn_up must share a quantisation type");
     }
 
+    if (wstream_) {
+      // one pinned host copy of every layer, a ring of wslots_ device slots, and
+      // each weight pointed at its place in its layer's slot
+      wslots_ = std::min<uint32_t>(2, c.layers);
+      for (size_t b : layer_bytes_) wslot_bytes_ = std::max(wslot_bytes_, (b + 255) / 256 * 256);
+      check(cudaHostAlloc(reinterpret_cast<void**>(&whost_), std::max<size_t>(wstage_.size(), 16),
+                          cudaHostAllocDefault),
+            "cudaHostAlloc");
+      std::memcpy(whost_, wstage_.data(), wstage_.size());
+      std::vector<uint8_t>().swap(wstage_);
+      wring_ = static_cast<uint8_t*>(dalloc(wslot_bytes_ * wslots_));
+      for (uint32_t l = 0; l < c.layers; ++l) {
+        uint8_t* base = wring_ + size_t(l % wslots_) * wslot_bytes_;
+        DevLayer& L = layers_[l];
+        for (DevWeight* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down})
+          w->ptr = base + (w->host_off - layer_off_[l]);
+      }
+      check(cudaStreamCreateWithFlags(&cstream_, cudaStreamNonBlocking), "copy stream");
+      for (uint32_t i = 0; i < 2; ++i) {
+        check(cudaEventCreateWithFlags(&ev_loaded_[i], cudaEventDisableTiming), "event");
+        check(cudaEventCreateWithFlags(&ev_free_[i], cudaEventDisableTiming), "event");
+      }
+    }
+
     // batched decode slots (generate_batch): each holds its own KV cache, state,
     // sampler history and penalty counts; the tensor-core step needs 128-row
     // tiles that never straddle q / k / v, and 64-row gate / up halves
-    bslots_ = tp_ == 1 ? std::min<uint32_t>(std::max<uint32_t>(opt.max_batch, 1), BATCH_MAX) : 1;
+    bslots_ = (tp_ == 1 && !wstream_) ? std::min<uint32_t>(std::max<uint32_t>(opt.max_batch, 1), BATCH_MAX) : 1;
     batch_ok_ = bslots_ > 1 && c.hidden % BATCH_TILE == 0 && kvd % BATCH_TILE == 0 && c.ffn % 64 == 0 &&
                 c.heads / c.kv_heads <= 8;
     if (!batch_ok_) bslots_ = 1;
@@ -244,6 +276,14 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     allocs_.clear();
     if (host_ids_) cudaFreeHost(host_ids_);
     host_ids_ = nullptr;
+    if (whost_) cudaFreeHost(whost_);
+    whost_ = nullptr;
+    for (cudaEvent_t& e : ev_loaded_)
+      if (e) cudaEventDestroy(e), e = nullptr;
+    for (cudaEvent_t& e : ev_free_)
+      if (e) cudaEventDestroy(e), e = nullptr;
+    if (cstream_) cudaStreamDestroy(cstream_);
+    cstream_ = nullptr;
     if (comm_) nccl().CommDestroy(comm_);
     comm_ = nullptr;
     cudaStreamDestroy(stream_);
@@ -261,8 +301,13 @@ Model::~Model() {
   if (batch_graph_) cudaGraphDestroy(batch_graph_);
   if (comm_) nccl().CommDestroy(comm_);
   for (void* p : ipc_opened_) cudaIpcCloseMemHandle(p);
+  if (cstream_) cudaStreamSynchronize(cstream_);
   for (void* p : allocs_) cudaFree(p);
   if (host_ids_) cudaFreeHost(host_ids_);
+  if (whost_) cudaFreeHost(whost_);
+  for (cudaEvent_t e : {ev_loaded_[0], ev_loaded_[1], ev_free_[0], ev_free_[1]})
+    if (e) cudaEventDestroy(e);
+  if (cstream_) cudaStreamDestroy(cstream_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -270,7 +315,17 @@ Model::~Model() {
 // A missing tensor leaves zeros, as the reference's `if let Ok(..)` loads do
 // (model.rs:618-760): an all-zero Q4_K block dequantises to 0.
 void Model::upload_weight(const GgufFile& f, const std::string& name, uint32_t rows, uint32_t cols, DevWeight& w,
-                          bool missing_is_zero, uint32_t row0, uint32_t nrows, uint32_t blk0, uint32_t nblk) {
+                          bool missing_is_zero, uint32_t row0, uint32_t nrows, uint32_t blk0, uint32_t nblk,
+                          bool to_host) {
+  // weight streaming: the blocks go to the host copy (256-byte aligned), placed in
+  // the device ring once every layer is staged
+  auto to_stage = [&](const uint8_t* data, size_t bytes) {
+    const size_t off = (wstage_.size() + 255) / 256 * 256;
+    wstage_.resize(off + bytes, 0);
+    if (data) std::memcpy(wstage_.data() + off, data, bytes);
+    w.host_off = off;
+    w.ptr = nullptr;
+  };
   const size_t nb = size_t(cols) / QK_K;
   if (nrows == 0) nrows = rows - row0;
   if (nblk == 0) nblk = uint32_t(nb) - blk0;
@@ -282,6 +337,10 @@ void Model::upload_weight(const GgufFile& f, const std::string& name, uint32_t r
     if (!missing_is_zero) throw WcbError(E_GENERIC, "Tensor not found: " + name);
     w.dtype = DT_Q4K;
     const size_t bytes = size_t(nrows) * nblk * Q4K_BYTES;
+    if (to_host) {
+      to_stage(nullptr, bytes);
+      return;
+    }
     w.ptr = static_cast<uint8_t*>(dalloc(bytes));
     check(cudaMemset(w.ptr, 0, bytes), "zero weight");
     return;
@@ -303,15 +362,32 @@ void Model::upload_weight(const GgufFile& f, const std::string& name, uint32_t r
       f.read_range(*t, size_t(row0 + r) * row_bytes + size_t(blk0) * bb, take, raw.data() + size_t(r) * take);
   }
   if (w.dtype == DT_Q4K) {
+    if (to_host) {
+      to_stage(raw.data(), raw.size());
+      return;
+    }
     w.ptr = static_cast<uint8_t*>(dalloc(raw.size()));
     check(cudaMemcpy(w.ptr, raw.data(), raw.size(), cudaMemcpyHostToDevice), "upload weight");
   } else {
     const size_t nblock = raw.size() / Q6K_BYTES;
     std::vector<uint8_t> pad(nblock * Q6K_DEV_BYTES, 0);
     for (size_t b = 0; b < nblock; ++b) std::memcpy(&pad[b * Q6K_DEV_BYTES], &raw[b * Q6K_BYTES], Q6K_BYTES);
+    if (to_host) {
+      to_stage(pad.data(), pad.size());
+      return;
+    }
     w.ptr = static_cast<uint8_t*>(dalloc(pad.size()));
     check(cudaMemcpy(w.ptr, pad.data(), pad.size(), cudaMemcpyHostToDevice), "upload weight");
   }
+}
+
+void Model::issue_layer_copy(uint32_t l) {
+  const uint32_t s = l % wslots_;
+  check(cudaStreamWaitEvent(cstream_, ev_free_[s], 0), "wait slot");
+  check(cudaMemcpyAsync(wring_ + size_t(s) * wslot_bytes_, whost_ + layer_off_[l], layer_bytes_[l],
+                        cudaMemcpyHostToDevice, cstream_),
+        "stream layer");
+  check(cudaEventRecord(ev_loaded_[s], cstream_), "record layer");
 }
 
 void Model::all_reduce_sum(float* buf, size_t n) {
@@ -472,8 +548,13 @@ void Model::enqueue_layers(int T, bool decode) {
   const ModelConfig& c = cfg_;
   const int H = int(c.hidden), hd = int(c.head_dim());
   const int HQ = int(hq_), FL = int(ffn_l_);
+  if (wstream_ && !wprimed_) {
+    for (uint32_t l = 0; l < wslots_; ++l) issue_layer_copy(l);
+    wprimed_ = true;
+  }
   for (uint32_t l = 0; l < c.layers; ++l) {
     const DevLayer& L = layers_[l];
+    if (wstream_) check(cudaStreamWaitEvent(stream_, ev_loaded_[l % wslots_], 0), "wait layer");
     // RMSNorm(eps 1e-6, layer.rs:51-57) -> Q/K/V projections (attention.rs:80-129)
     // -> RoPE (:140-143) -> KV append (:162); this rank's heads only
     const DevWeight qkv[3] = {L.q, L.k, L.v};
@@ -541,7 +622,13 @@ void Model::enqueue_layers(int T, bool decode) {
       check(launch_add(x_, h_, part_y_, size_t(T) * H, st_, stream_), "residual");
       launches_ += 1;
     }
+    if (wstream_) {  // the slot is free once this layer's kernels ran; refill it ahead
+      check(cudaEventRecord(ev_free_[l % wslots_], stream_), "free slot");
+      if (l + wslots_ < c.layers) issue_layer_copy(l + wslots_);
+    }
   }
+  if (wstream_)  // the next forward's first layers, behind this one's last users of their slots
+    for (uint32_t l = 0; l < wslots_; ++l) issue_layer_copy(l);
 }
 
 // final RMSNorm with the config eps (model.rs:937-943) + LM head on the last
@@ -651,7 +738,8 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
 // head. Each phase waits on the counter of the phase whose output it reads.
 void Model::build_decode_step() {
   mk_ok_ = false;
-  if ((opt_.flags & 8) || tp_ > 1) return;  // tensor parallelism runs the per-op kernels
+  // tensor parallelism and weight streaming run the per-op kernels
+  if ((opt_.flags & 8) || tp_ > 1 || wstream_) return;
   if (decode_step_configure() != cudaSuccess) {
     cudaGetLastError();
     return;
@@ -915,7 +1003,7 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
     // tickets of a step that ended on an error are cleared here
     check(cudaMemsetAsync(mk_.ticket, 0, sizeof(int) * size_t(mk_.n_kv), stream_), "clear tickets");
     launches_per_step_ = 1;
-  } else if (!(opt_.flags & 1) && (!decode_exec_ || graph_rep_ != rep)) {
+  } else if (!(opt_.flags & 1) && !wstream_ && (!decode_exec_ || graph_rep_ != rep)) {
     if (decode_exec_) {
       cudaGraphExecDestroy(decode_exec_);
       cudaGraphDestroy(decode_graph_);

@@ -19,6 +19,7 @@ struct DevWeight {
   uint8_t* ptr = nullptr;
   int dtype = DT_Q4K;
   uint32_t rows = 0, cols = 0;
+  size_t host_off = 0;  // weight streaming: offset in the pinned host copy
 };
 
 struct DevLayer {
@@ -93,7 +94,10 @@ class Model {
   // [rows][cols] tensor (nrows / nblk 0: all)
   void upload_weight(const GgufFile& f, const std::string& name, uint32_t rows, uint32_t cols, DevWeight& w,
                      bool required_shape_only, uint32_t row0 = 0, uint32_t nrows = 0, uint32_t blk0 = 0,
-                     uint32_t nblk = 0);
+                     uint32_t nblk = 0, bool to_host = false);
+  // weight streaming: copy layer l's weights from the pinned host copy into its
+  // device ring slot on the copy stream, after the slot's previous user is done
+  void issue_layer_copy(uint32_t l);
   void all_reduce_sum(float* buf, size_t n);  // tensor parallelism: sum over the ranks, in place
   void upload_vector(const GgufFile& f, const std::string& name, uint32_t n, float fill, float*& dst);
   void build_rope(uint32_t len);
@@ -206,6 +210,30 @@ class Model {
   size_t mk_tagged_n_ = 0;
   uint32_t mk_launches_ = 0;
 
+  // weight streaming (LoadOptions::flags bit 4, models larger than the GPU's memory):
+  // the layer weights live in pinned host memory and stream through a ring of
+  // wslots_ device slots on a copy stream, wslots_ - 1 layers ahead of the compute
+  bool wstream_ = false;
+  std::vector<uint8_t> wstage_;          // load-time staging of the host copy
+  uint8_t* whost_ = nullptr;             // pinned host copy of every layer's weights
+  std::vector<size_t> layer_off_, layer_bytes_;
+  uint8_t* wring_ = nullptr;             // [wslots_][wslot_bytes_]
+  size_t wslot_bytes_ = 0;
+  uint32_t wslots_ = 2;
+  bool wprimed_ = false;                 // the next forward's first layers are in flight
+  cudaStream_t cstream_ = nullptr;
+  cudaEvent_t ev_loaded_[2] = {nullptr, nullptr};
+  cudaEvent_t ev_free_[2] = {nullptr, nullptr};
+
+ public:
+  // weight streaming: host-to-device bytes one forward pass copies (0: weights resident)
+  size_t streamed_bytes_per_forward() const {
+    size_t t = 0;
+    for (size_t b : layer_bytes_) t += b;
+    return wstream_ ? t : 0;
+  }
+
+ private:
   // batched decode (generate_batch): per-slot state lives in bslots_-long arrays
   // whose slot 0 is the single-sequence state above
   bool batch_ok_ = false;
