@@ -177,6 +177,30 @@ size_t wcb_last_error(char* buf, size_t len);
 /* Library version string (wasmchord_version, abi.rs:225-228). */
 const char* wcb_version(void);
 
+/* ---- Tokenizer (crates/wasm-chord-core/src/tokenizer.rs) and generate(&str) ----
+ * wcb_tokenizer_load: Tokenizer::from_gguf (tokenizer.rs:82-147) from a GGUF file's
+ * tokenizer.ggml.tokens / tokenizer.ggml.merges / *_token_id metadata; a handle > 0.
+ * wcb_tokenize: Tokenizer::encode (tokenizer.rs:207-311): NUL-terminated UTF-8 text
+ * (other bytes: WCB_ERR_INVALID_ARGUMENT), BOS first when add_special; *n_out = the
+ * id count, min(cap, *n_out) ids written.
+ * wcb_detokenize: Tokenizer::decode (tokenizer.rs:353-395): *n_out = the text's byte
+ * length; out receives it NUL-terminated, truncated to cap - 1 bytes.
+ * wcb_generate_text: Model::generate(prompt, tokenizer, config) (model.rs:1322-1415):
+ * encode with BOS, greedy or sampled decoding ended by max_tokens or the tokenizer's
+ * EOS (cfg->eos_id is ignored), the prompt and the generated ids decoded together
+ * without special tokens; out as for wcb_detokenize. */
+uint32_t wcb_tokenizer_load(const char* gguf_path, uint32_t* out_handle);
+uint32_t wcb_tokenizer_free(uint32_t tokenizer);
+uint32_t wcb_tokenizer_info(uint32_t tokenizer, uint32_t* vocab_size, uint32_t* bos, uint32_t* eos, uint32_t* unk);
+/* Tokenizer::set_add_bos_token / set_add_eos_token (tokenizer.rs:417-425) */
+uint32_t wcb_tokenizer_set_special(uint32_t tokenizer, uint32_t add_bos, uint32_t add_eos);
+uint32_t wcb_tokenize(uint32_t tokenizer, const char* text, uint32_t add_special, uint32_t* out, size_t cap,
+                      size_t* n_out);
+uint32_t wcb_detokenize(uint32_t tokenizer, const uint32_t* ids, size_t n, uint32_t skip_special, char* out,
+                        size_t cap, size_t* n_out);
+uint32_t wcb_generate_text(uint32_t model, uint32_t tokenizer, const char* prompt, const wcb_gen_config* cfg,
+                           char* out, size_t cap, size_t* n_out);
+
 /* A fresh tensor-parallel group id (ncclGetUniqueId) for wcb_load_opts.tp_id:
  * one rank creates it and the caller hands the same 128 bytes to every rank.
  * No counterpart in the reference. */

@@ -18,6 +18,7 @@
 #include "model.h"
 #include "nccl_rt.h"
 #include "sampler.h"
+#include "tokenizer.h"
 
 namespace {
 
@@ -34,6 +35,51 @@ std::map<uint32_t, Stream> g_streams;
 uint32_t g_next_model = 1;
 uint32_t g_next_sampler = 1;
 uint32_t g_next_stream = 1;
+std::map<uint32_t, std::shared_ptr<wcb::Tokenizer>> g_tokenizers;
+uint32_t g_next_tokenizer = 1;
+
+std::shared_ptr<wcb::Tokenizer> get_tokenizer(uint32_t h) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_tokenizers.find(h);
+  if (it == g_tokenizers.end()) throw wcb::WcbError(WCB_ERR_INVALID_ARGUMENT, "Invalid tokenizer handle");
+  return it->second;
+}
+
+// the reference takes &str: the text must be well-formed UTF-8
+bool valid_utf8(const char* s, size_t n) {
+  size_t i = 0;
+  while (i < n) {
+    const unsigned char c = static_cast<unsigned char>(s[i]);
+    size_t need;
+    unsigned char lo = 0x80, hi = 0xBF;
+    if (c < 0x80) need = 0;
+    else if (c >= 0xC2 && c <= 0xDF) need = 1;
+    else if (c == 0xE0) need = 2, lo = 0xA0;
+    else if ((c >= 0xE1 && c <= 0xEC) || c == 0xEE || c == 0xEF) need = 2;
+    else if (c == 0xED) need = 2, hi = 0x9F;
+    else if (c == 0xF0) need = 3, lo = 0x90;
+    else if (c >= 0xF1 && c <= 0xF3) need = 3;
+    else if (c == 0xF4) need = 3, hi = 0x8F;
+    else return false;
+    if (need && i + need >= n) return false;  // truncated sequence
+    for (size_t k = 1; k <= need; ++k) {
+      const unsigned char d = static_cast<unsigned char>(s[i + k]);
+      if (d < (k == 1 ? lo : 0x80) || d > (k == 1 ? hi : 0xBF)) return false;
+    }
+    i += need + 1;
+  }
+  return true;
+}
+
+// copies a string into a caller buffer (NUL-terminated, truncated to cap - 1 bytes)
+void copy_out(const std::string& s, char* out, size_t cap, size_t* n_out) {
+  *n_out = s.size();
+  if (out && cap) {
+    const size_t k = std::min(cap - 1, s.size());
+    std::memcpy(out, s.data(), k);
+    out[k] = '\0';
+  }
+}
 
 uint32_t fail(uint32_t code, const std::string& msg) {
   g_last_error = msg;
@@ -533,6 +579,94 @@ uint32_t wcb_model_stream(uint32_t h, void** out) {
   return guarded([&]() -> uint32_t {
     if (!out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
     *out = get_model(h)->stream();
+    return WCB_OK;
+  });
+}
+
+}  // extern "C"
+
+extern "C" {
+
+uint32_t wcb_tokenizer_load(const char* gguf_path, uint32_t* out_handle) {
+  return guarded([&]() -> uint32_t {
+    if (!gguf_path || !out_handle) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    *out_handle = 0;
+    const wcb::GgufFile f(gguf_path);
+    auto t = std::make_shared<wcb::Tokenizer>(wcb::Tokenizer::from_gguf(f));
+    std::lock_guard<std::mutex> lk(g_mu);
+    const uint32_t h = g_next_tokenizer++;
+    g_tokenizers[h] = std::move(t);
+    *out_handle = h;
+    return WCB_OK;
+  });
+}
+
+uint32_t wcb_tokenizer_free(uint32_t h) {
+  return guarded([&]() -> uint32_t {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_tokenizers.erase(h)) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid tokenizer handle");
+    return WCB_OK;
+  });
+}
+
+uint32_t wcb_tokenizer_info(uint32_t h, uint32_t* vocab_size, uint32_t* bos, uint32_t* eos, uint32_t* unk) {
+  return guarded([&]() -> uint32_t {
+    if (!vocab_size || !bos || !eos || !unk) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    auto t = get_tokenizer(h);
+    *vocab_size = uint32_t(t->vocab_size());
+    *bos = t->special().bos;
+    *eos = t->special().eos;
+    *unk = t->special().unk;
+    return WCB_OK;
+  });
+}
+
+uint32_t wcb_tokenizer_set_special(uint32_t h, uint32_t add_bos, uint32_t add_eos) {
+  return guarded([&]() -> uint32_t {
+    auto t = get_tokenizer(h);
+    t->set_add_bos(add_bos != 0);
+    t->set_add_eos(add_eos != 0);
+    return WCB_OK;
+  });
+}
+
+uint32_t wcb_tokenize(uint32_t h, const char* text, uint32_t add_special, uint32_t* out, size_t cap, size_t* n_out) {
+  return guarded([&]() -> uint32_t {
+    if (!text || !n_out || (!out && cap)) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    const size_t n = std::strlen(text);
+    if (!valid_utf8(text, n)) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: text is not valid UTF-8");
+    const std::vector<uint32_t> ids = get_tokenizer(h)->encode(std::string(text, n), add_special != 0);
+    *n_out = ids.size();
+    if (cap) std::memcpy(out, ids.data(), sizeof(uint32_t) * std::min(cap, ids.size()));
+    return WCB_OK;
+  });
+}
+
+uint32_t wcb_detokenize(uint32_t h, const uint32_t* ids, size_t n, uint32_t skip_special, char* out, size_t cap,
+                        size_t* n_out) {
+  return guarded([&]() -> uint32_t {
+    if (!n_out || (!ids && n)) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    copy_out(get_tokenizer(h)->decode(ids, n, skip_special != 0), out, cap, n_out);
+    return WCB_OK;
+  });
+}
+
+uint32_t wcb_generate_text(uint32_t model, uint32_t tokenizer, const char* prompt, const wcb_gen_config* cfg,
+                           char* out, size_t cap, size_t* n_out) {
+  return guarded([&]() -> uint32_t {
+    if (!prompt || !cfg || !n_out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    const size_t n = std::strlen(prompt);
+    if (!valid_utf8(prompt, n)) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: text is not valid UTF-8");
+    auto t = get_tokenizer(tokenizer);
+    auto m = get_model(model);
+    // Model::generate (model.rs:1322-1415): encode with BOS, the tokenizer's EOS ends
+    // the loop, and the whole sequence (prompt + generated) is decoded without specials
+    std::vector<uint32_t> ids = t->encode(std::string(prompt, n), true);
+    wcb::GenParams g = params_of(cfg);
+    g.eos = t->special().eos;
+    const std::vector<uint32_t> gen = m->generate(ids.data(), ids.size(), g);
+    ids.insert(ids.end(), gen.begin(), gen.end());
+    copy_out(t->decode(ids.data(), ids.size(), true), out, cap, n_out);
     return WCB_OK;
   });
 }

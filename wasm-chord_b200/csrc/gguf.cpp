@@ -65,7 +65,13 @@ GgufValue GgufFile::rd_value(uint32_t t, bool allow_array) {
       if (!allow_array) throw WcbError(E_PARSE, "Parse error: Unknown typed value: 9");
       const uint32_t et = rd<uint32_t>();
       const uint64_t n = rd<uint64_t>();
-      for (uint64_t k = 0; k < n; ++k) rd_value(et, false);  // arrays are skipped: no config key is an array
+      if (et == 8) {  // strings are kept (the tokenizer's vocabulary and merges)
+        if (n > (uint64_t(1) << 26)) throw WcbError(E_PARSE, "Parse error: array length out of range");
+        v.strs.reserve(size_t(n));
+        for (uint64_t k = 0; k < n; ++k) v.strs.push_back(rd_str());
+      } else {
+        for (uint64_t k = 0; k < n; ++k) rd_value(et, false);  // numeric arrays: no key needs one
+      }
       break;
     }
     case 10: v.u = rd<uint64_t>(); break;

@@ -27,6 +27,7 @@ struct GgufValue {
   int64_t i = 0;
   double f = 0.0;
   std::string s;
+  std::vector<std::string> strs;  // an array of strings (tokenizer.ggml.tokens / merges); other arrays are skipped
   bool as_u32(uint32_t* out) const;
   bool as_f32(float* out) const;
 };
@@ -54,6 +55,7 @@ class GgufFile {
   GgufFile& operator=(const GgufFile&) = delete;
 
   const GgufTensor* find(const std::string& name) const;
+  const GgufValue* value(const std::string& key) const { return get(key); }
   ModelConfig config() const;
   // reads the raw bytes of a tensor into dst (nbytes bytes)
   void read(const GgufTensor& t, void* dst) const;

@@ -33,7 +33,9 @@ EXPORTED = [
     "wcb_clear_kv", "wcb_kv_len", "wcb_generate_tokens", "wcb_generate_batch", "wcb_sampler_new",
     "wcb_sampler_sample", "wcb_sampler_free", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
     "wcb_repack_q6k_dev", "wcb_gemv_dev", "wcb_model_stream", "wcb_infer", "wcb_next_tokens",
-    "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_batch_info", "wcb_attention_dev",
+    "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_batch_info", "wcb_tokenizer_load", "wcb_tokenizer_free",
+    "wcb_tokenizer_info", "wcb_tokenizer_set_special", "wcb_tokenize", "wcb_detokenize", "wcb_generate_text",
+    "wcb_attention_dev",
     "wcb_attention_dev_noalloc", "wcb_tp_id", "wcb_model_tp_handle", "wcb_model_tp_connect",
 ]
 
@@ -119,6 +121,13 @@ def lib() -> C.CDLL:
     L.wcb_close_stream.argtypes = [u32]
     L.wcb_model_launches_per_step.argtypes = [u32, C.POINTER(u32)]
     L.wcb_batch_info.argtypes = [u32, C.POINTER(u32), C.POINTER(u32)]
+    L.wcb_tokenizer_load.argtypes = [C.c_char_p, C.POINTER(u32)]
+    L.wcb_tokenizer_free.argtypes = [u32]
+    L.wcb_tokenizer_info.argtypes = [u32, C.POINTER(u32), C.POINTER(u32), C.POINTER(u32), C.POINTER(u32)]
+    L.wcb_tokenizer_set_special.argtypes = [u32, u32, u32]
+    L.wcb_tokenize.argtypes = [u32, C.c_char_p, u32, vp, sz, C.POINTER(sz)]
+    L.wcb_detokenize.argtypes = [u32, vp, sz, u32, C.c_char_p, sz, C.POINTER(sz)]
+    L.wcb_generate_text.argtypes = [u32, u32, C.c_char_p, C.POINTER(_GenConfig), C.c_char_p, sz, C.POINTER(sz)]
     L.wcb_attention_dev.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     L.wcb_attention_dev_noalloc.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp]
     L.wcb_tp_id.argtypes = [vp]
@@ -269,6 +278,19 @@ class Model:
                                          C.byref(n)))
         return out[: min(n.value, cap)].tolist()
 
+    def generate_text(self, prompt: str, tokenizer: "Tokenizer", config: GenerationConfig) -> str:
+        """Model::generate(prompt, tokenizer, config) (model.rs:1322-1415): the prompt and
+        the generated text, decoded together; the tokenizer's EOS ends the loop."""
+        c = config._c()
+        n = C.c_size_t(0)
+        p = prompt.encode("utf-8")
+        # room for the prompt and 256 bytes per generated token
+        buf = C.create_string_buffer(len(p) + 256 * (max(1, int(config.max_tokens)) + 8))
+        _check(lib().wcb_generate_text(self._h, tokenizer._h, p, C.byref(c), buf, len(buf), C.byref(n)))
+        if n.value + 1 > len(buf):
+            raise WcbError(1, f"generated text of {n.value} bytes exceeds the {len(buf)}-byte buffer")
+        return buf.raw[: n.value].decode("utf-8")
+
     def generate_batch(self, prompts: Sequence[Sequence[int]], config: GenerationConfig) -> List[List[int]]:
         flat = _u32([t for p in prompts for t in p])
         lens = np.asarray([len(p) for p in prompts], dtype=np.uintp)
@@ -316,6 +338,60 @@ class Model:
         s = C.c_void_p(0)
         _check(lib().wcb_model_stream(self._h, C.byref(s)))
         return s.value or 0
+
+
+class Tokenizer:
+    """Tokenizer (crates/wasm-chord-core/src/tokenizer.rs) loaded from a GGUF file's
+    tokenizer.ggml.* metadata."""
+
+    def __init__(self, path: str):
+        h = C.c_uint32(0)
+        _check(lib().wcb_tokenizer_load(path.encode(), C.byref(h)))
+        self._h = h.value
+
+    def close(self) -> None:
+        if self._h:
+            lib().wcb_tokenizer_free(self._h)
+            self._h = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self) -> Tuple[int, int, int, int]:
+        """(vocab size, bos id, eos id, unk id)"""
+        v = [C.c_uint32(0) for _ in range(4)]
+        _check(lib().wcb_tokenizer_info(self._h, *[C.byref(x) for x in v]))
+        return tuple(int(x.value) for x in v)
+
+    def set_special(self, add_bos: bool, add_eos: bool) -> None:
+        _check(lib().wcb_tokenizer_set_special(self._h, int(add_bos), int(add_eos)))
+
+    def encode(self, text: str, add_special_tokens: bool = True) -> List[int]:
+        b = text.encode("utf-8")
+        n = C.c_size_t(0)
+        _check(lib().wcb_tokenize(self._h, b, int(add_special_tokens), None, 0, C.byref(n)))
+        out = np.zeros(max(1, n.value), dtype=np.uint32)
+        _check(lib().wcb_tokenize(self._h, b, int(add_special_tokens), out.ctypes.data, out.size, C.byref(n)))
+        return out[: n.value].tolist()
+
+    def encode_bytes(self, text: bytes, add_special_tokens: bool = True) -> List[int]:
+        """encode() of raw bytes (the library rejects bytes that are not UTF-8)."""
+        n = C.c_size_t(0)
+        out = np.zeros(4 * len(text) + 8, dtype=np.uint32)
+        _check(lib().wcb_tokenize(self._h, text, int(add_special_tokens), out.ctypes.data, out.size, C.byref(n)))
+        return out[: n.value].tolist()
+
+    def decode(self, ids: Sequence[int], skip_special_tokens: bool = True) -> str:
+        a = _u32(ids)
+        n = C.c_size_t(0)
+        _check(lib().wcb_detokenize(self._h, a.ctypes.data, a.size, int(skip_special_tokens), None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value + 1)
+        _check(lib().wcb_detokenize(self._h, a.ctypes.data, a.size, int(skip_special_tokens), buf, len(buf),
+                                    C.byref(n)))
+        return buf.raw[: n.value].decode("utf-8")
 
 
 class TokenStream:

@@ -25,7 +25,7 @@ LIB = os.path.join(PKG, "libwcb.so")
 SYNTH_LIB = os.path.join(PKG, "libwcb_synth.so")
 
 CUDA_SOURCES = ["kernels.cu", "gemm_tc.cu", "decode_step.cu", "noalloc.cu", "batch_decode.cu", "attn_prefill.cu"]
-HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "api.cpp", "nccl_rt.cpp"]
+HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "api.cpp", "nccl_rt.cpp", "tokenizer.cpp"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
