@@ -57,7 +57,9 @@ typedef struct wcb_load_opts {
                          two-layer device ring, one layer ahead of the compute (models that do
                          not fit in GPU memory; replaces the reference's Memory64 layer
                          manager, memory64_layer_manager.rs:76-300, async_prefetch.rs:83-190).
-                         Single GPU, per-op kernels, no batched path. */
+                         Single GPU, per-op kernels, no batched path;
+                         bit 5: sample on the host even where the device sampler applies
+                         (temperature > 0 with 1 <= top_k <= 1024); both draw the same tokens. */
   /* Tensor parallelism (one process per GPU; no counterpart in the reference, whose
      sharding.rs is bookkeeping only). tp_size 0 or 1: the whole model on `device`.
      tp_size > 1: this process holds rank tp_rank's shard (query/KV heads, o and down

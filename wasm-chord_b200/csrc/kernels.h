@@ -316,6 +316,15 @@ cudaError_t launch_batch_embed(const float* emb, int vocab, int hidden, const St
 cudaError_t launch_batch_sample(const float* logits, int vocab, StepState* st, uint32_t* hist, int hist_cap,
                                 uint32_t* pen_cnt, float rep, int B, cudaStream_t s);
 
+// ------------------------------------------------------------ sampling ----
+// Temperature + top-k (+ top-p) draw on the device for one sequence (1 <= top_k
+// <= 1024): penalty into `scratch` [n], the draw with the splitmix64 state *rng
+// (the host Sampler's fixed-order path, operation for operation), then
+// generate()'s bookkeeping on st / hist / pen_cnt
+cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
+                          uint32_t* pen_cnt, float rep, float temperature, int top_k, float top_p,
+                          unsigned long long* rng, cudaStream_t s);
+
 // ------------------------------------------------------------ elementwise --
 cudaError_t launch_embed(const float* emb, int vocab, int hidden, const uint32_t* ids, int T, float* x,
                          const StepState* st, cudaStream_t s);

@@ -248,6 +248,10 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
       peers_dev_ = static_cast<unsigned long long**>(dalloc(sizeof(void*) * tp_));
     }
     row_m_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_)));
+    if (tp_ == 1) {  // device sampling: the penalised logits and the splitmix64 state
+      plog_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
+      rng_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long)));
+    }
     pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab * bslots_));
     check(cudaMemset(pen_cnt_, 0, sizeof(uint32_t) * c.vocab * bslots_), "clear penalty counts");
     pen_base_ = pen_cnt_;
@@ -640,10 +644,17 @@ void Model::enqueue_lm_head(int T, bool gen) {
   // with several ranks each scores its vocabulary rows; the argmax key (order-
   // preserving logit bits | token id) and the NaN flag are max-reduced over the
   // ranks, then every rank runs the same sampler bookkeeping
-  gen_mode_ = gen ? (tp_ > 1 ? 2 : 1) : 0;
+  const bool dev_sample = gen && sample_mode_ == 1;
+  gen_mode_ = (gen && !dev_sample) ? (tp_ > 1 ? 2 : 1) : 0;
   gemv(head, 1, H, 1, x_ + size_t(T - 1) * H, H, out_norm_, cfg_.eps, PRO_RMSNORM, EPI_LMHEAD, logits_,
        int(cfg_.vocab), nullptr, 0, nullptr, 0, -1, 0);
   gen_mode_ = 0;
+  if (dev_sample) {  // penalty, top-k / top-p draw and generate()'s bookkeeping on the device
+    check(launch_sample(logits_, plog_, int(cfg_.vocab), st_, hist_, pen_cnt_, rep_, samp_t_, samp_k_, samp_tp_, rng_,
+                        stream_),
+          "sampler");
+    ++launches_;
+  }
   if (gen && tp_ > 1) {
     check(launch_tp_pack_key(st_, tpkey_, stream_), "argmax key");
     const ncclResult_t r = nccl().AllReduce(tpkey_, tpkey_, 2, ncclUint64, ncclMax, comm_, stream_);
@@ -932,7 +943,7 @@ void Model::launch_decode_step_kernel(bool gen) {
 
 void Model::decode_steps(int steps) {
   for (int i = 0; i < steps; ++i) {
-    if (mk_ok_) {
+    if (mk_ok_ && sample_mode_ == 0) {
       launch_decode_step_kernel(true);
     } else if (decode_exec_) {
       check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
@@ -982,7 +993,21 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   sess_tokens_.clear();
   sess_done_ = false;
   sess_steps_left_ = g.max_tokens > 1 ? size_t(g.max_tokens) - 1 : 0;
-  if (!sess_greedy_) {
+  // top-k sampling runs on the device (sample_dev.cu, the host sampler's fixed order):
+  // the same device-driven loop as greedy decoding; other sampled configurations
+  // sample on the host from each step's logits
+  const bool dev_sample = !sess_greedy_ && plog_ && !(opt_.flags & 32) && sess_sampler_->fixed_path(cfg_.vocab);
+  sess_host_ = !sess_greedy_ && !dev_sample;
+  sample_mode_ = dev_sample ? 1 : 0;
+  if (dev_sample) {
+    samp_t_ = sess_sampler_->temperature();
+    samp_k_ = int(sess_sampler_->top_k());
+    samp_tp_ = sess_sampler_->top_p();
+    const unsigned long long seed = sess_sampler_->seed_state();
+    check(cudaMemcpyAsync(rng_, &seed, sizeof(seed), cudaMemcpyHostToDevice, stream_), "seed");
+    check(cudaStreamSynchronize(stream_), "seed");
+  }
+  if (sess_host_) {
     // host-sampled path: Model::generate's loop with the LogitsProcessor on the host
     std::vector<float> logits(cfg_.vocab);
     for (size_t cs = 0; cs < n; cs += size_t(t_max_)) {
@@ -999,11 +1024,13 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   // EOS / max_tokens bookkeeping in the sampler kernel), no host round trip per token
   prefill_greedy(prompt, n, g);
   const float rep = g.repetition_penalty;
-  if (mk_ok_) {
+  const bool same_graph = graph_rep_ == rep && graph_mode_ == sample_mode_ &&
+                          (sample_mode_ == 0 || (graph_t_ == samp_t_ && graph_k_ == samp_k_ && graph_tp_ == samp_tp_));
+  if (mk_ok_ && sample_mode_ == 0) {
     // tickets of a step that ended on an error are cleared here
     check(cudaMemsetAsync(mk_.ticket, 0, sizeof(int) * size_t(mk_.n_kv), stream_), "clear tickets");
     launches_per_step_ = 1;
-  } else if (!(opt_.flags & 1) && !wstream_ && (!decode_exec_ || graph_rep_ != rep)) {
+  } else if (!(opt_.flags & 1) && !wstream_ && (!decode_exec_ || !same_graph)) {
     if (decode_exec_) {
       cudaGraphExecDestroy(decode_exec_);
       cudaGraphDestroy(decode_graph_);
@@ -1014,6 +1041,10 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
     capture_decode_graph();
   }
   graph_rep_ = rep;
+  graph_mode_ = sample_mode_;
+  graph_t_ = samp_t_;
+  graph_k_ = samp_k_;
+  graph_tp_ = samp_tp_;
   sync_session_state();
   sess_active_ = true;
 }
@@ -1038,7 +1069,7 @@ std::vector<uint32_t> Model::next(size_t max_tokens, bool* finished) {
   if (!sess_active_) throw WcbError(E_INVALID, "Invalid argument: no active generation on this model");
   check(cudaSetDevice(device_), "cudaSetDevice");
   std::vector<uint32_t> out;
-  if (!sess_greedy_) {
+  if (sess_host_) {
     std::vector<float> logits(cfg_.vocab);
     while (sess_tokens_.size() - sess_delivered_ < max_tokens && !sess_done_) {
       if (sess_steps_left_ == 0) { sess_done_ = true; break; }
@@ -1237,6 +1268,7 @@ std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts
     return out;
   }
   check(cudaSetDevice(device_), "cudaSetDevice");
+  sample_mode_ = 0;  // greedy here: the per-slot prefill takes the argmax path
   ++session_;  // slot 0 is the single-sequence KV cache: an open session ends here
   sess_active_ = false;
   sess_done_ = true;

@@ -259,6 +259,16 @@ class Model {
   cudaGraphExec_t decode_exec_ = nullptr;
   cudaGraph_t decode_graph_ = nullptr;
   float graph_rep_ = -1.0f;
+  int graph_mode_ = -1;                 // sampling mode / parameters the decode graph was captured for
+  float graph_t_ = -1.0f, graph_tp_ = -1.0f;
+  int graph_k_ = -1;
+  // device sampling (sample_dev.cu): mode 1 = top-k / top-p draw on the device
+  int sample_mode_ = 0;
+  float samp_t_ = 0.0f, samp_tp_ = 0.0f;
+  int samp_k_ = 0;
+  float* plog_ = nullptr;                 // [vocab] penalised logits
+  unsigned long long* rng_ = nullptr;     // splitmix64 state
+  bool sess_host_ = false;                // this session samples on the host
 };
 
 }  // namespace wcb

@@ -5,6 +5,7 @@
 #include <numeric>
 
 #include "gguf.h"
+#include "wcb_exp.h"
 
 namespace wcb {
 
@@ -86,11 +87,63 @@ void Sampler::keep_top_k(std::vector<float>& p, size_t k) {
   renormalize(p);
 }
 
+uint32_t Sampler::sample_fixed(const float* l, size_t n) {
+  for (size_t i = 0; i < n; ++i)
+    if (std::isnan(l[i])) throw WcbError(E_GENERIC, "Runtime error: NaN logit at index " + std::to_string(i));
+  const size_t K = std::min(top_k_, n);
+  std::vector<uint32_t> idx(n);
+  std::iota(idx.begin(), idx.end(), 0u);
+  std::partial_sort(idx.begin(), idx.begin() + long(K), idx.end(),
+                    [&](uint32_t a, uint32_t b) { return l[a] > l[b] || (l[a] == l[b] && a < b); });
+  std::vector<uint32_t> cand(idx.begin(), idx.begin() + long(K));
+  std::sort(cand.begin(), cand.end());
+  const float tf = float(temperature_);
+  std::vector<float> x(K), q(K);
+  float mx = -INFINITY;
+  for (size_t j = 0; j < K; ++j) {
+    x[j] = l[cand[j]] / tf;
+    mx = std::fmax(mx, x[j]);
+  }
+  float s = 0.0f;
+  for (size_t j = 0; j < K; ++j) {
+    q[j] = wcb_exp_nonpos(x[j] + (-mx));
+    s += q[j];
+  }
+  for (size_t j = 0; j < K; ++j) q[j] = q[j] / s;
+  const float tp = float(top_p_);
+  if (!(tp <= 0.0f || tp >= 1.0f)) {
+    std::vector<uint32_t> ord(K);
+    std::iota(ord.begin(), ord.end(), 0u);
+    std::stable_sort(ord.begin(), ord.end(), [&](uint32_t a, uint32_t b) { return q[a] > q[b]; });
+    float cum = 0.0f;
+    for (uint32_t j : ord) {
+      if (cum >= tp) q[j] = 0.0f;
+      else cum += q[j];
+    }
+    float s2 = 0.0f;
+    for (size_t j = 0; j < K; ++j) s2 += q[j];
+    if (s2 > 0.0f)
+      for (size_t j = 0; j < K; ++j) q[j] = q[j] / s2;
+  }
+  float tot = 0.0f;
+  for (size_t j = 0; j < K; ++j) tot += q[j];
+  if (!(tot > 0.0f)) throw WcbError(E_GENERIC, "Failed to create weighted index: all weights zero");
+  const float u = uniform() * tot;
+  float c = 0.0f;
+  for (size_t j = 0; j < K; ++j) {
+    c += q[j];
+    if (c > u) return cand[j];
+  }
+  return cand[K - 1];
+}
+
 uint32_t Sampler::sample(float* l, size_t n) {
   penalize(l, n);
   uint32_t tok;
   if (kind_ == ARGMAX) {
     tok = argmax(l, n);
+  } else if (fixed_path(n)) {
+    tok = sample_fixed(l, n);
   } else {
     // compute_probabilities (sampling.rs:106-115)
     std::vector<float> p(n);

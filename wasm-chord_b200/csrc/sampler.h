@@ -6,7 +6,13 @@
 // softmax + top-k / top-p + a weighted draw (:106-229). The weighted draw uses a
 // splitmix64 stream seeded with `seed`; the reference's rand 0.9 StdRng stream
 // is not reproduced, so sampled (temperature > 0) sequences differ from it.
+// Top-k configurations take a fixed evaluation order (sample_fixed) that the
+// device sampler repeats operation for operation: the top-k candidates by
+// (logit desc, index asc) (the reference's select_nth_unstable leaves ties at
+// the boundary unspecified), softmax over them with wcb_exp_nonpos
+// (mathematically the reference's softmax-then-renormalise), top-p and the draw.
 #pragma once
+#include <algorithm>
 #include <cstdint>
 #include <vector>
 
@@ -20,12 +26,22 @@ class Sampler {
   void penalize(float* logits, size_t n) const;
   static uint32_t argmax(const float* logits, size_t n);
   Kind kind() const { return kind_; }
+  // top-k configurations (1 <= min(top_k, n) <= 1024) take the fixed-order path that
+  // the device sampler (sample_dev.cu) reproduces exactly
+  bool fixed_path(size_t n) const {
+    return (kind_ == TOPK || kind_ == TOPK_TOPP) && top_k_ >= 1 && std::min(top_k_, n) <= 1024;
+  }
+  float temperature() const { return float(temperature_); }
+  float top_p() const { return float(top_p_); }
+  uint32_t top_k() const { return uint32_t(top_k_); }
+  uint64_t seed_state() const { return state_; }
   bool greedy() const { return kind_ == ARGMAX; }
   float repetition_penalty() const { return rep_; }
   std::vector<uint32_t>& history() { return prev_; }
 
  private:
   float uniform();
+  uint32_t sample_fixed(const float* logits, size_t n);
   uint32_t multinomial(const std::vector<float>& p);
   uint32_t top_p(std::vector<float>& p, float tp);
   static void keep_top_k(std::vector<float>& p, size_t k);

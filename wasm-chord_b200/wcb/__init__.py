@@ -214,14 +214,15 @@ class Model:
     def load_from_gguf(cls, path: str, device: int = 0, max_seq: int = 0, kv_dtype: int = KV_F32,
                        max_batch: int = 1, use_graphs: bool = True, use_pdl: bool = True,
                        use_tensor_cores: bool = True, use_persistent: bool = True, tp_rank: int = 0,
-                       tp_size: int = 1, tp_id: bytes = b"", stream_weights: bool = False) -> "Model":
+                       tp_size: int = 1, tp_id: bytes = b"", stream_weights: bool = False,
+                       host_sampling: bool = False) -> "Model":
         """Loads a GGUF file. tp_size > 1: this process holds tensor-parallel rank
         tp_rank's shard and joins the group named by tp_id (tp_unique_id() on one
         rank, the same bytes on every rank); forward() then fills only this rank's
         vocabulary slice of the logits. stream_weights: the layer weights stay in pinned
         host memory and stream to the GPU layer by layer (models larger than its memory)."""
         flags = ((0 if use_graphs else 1) | (0 if use_pdl else 2) | (0 if use_tensor_cores else 4)
-                 | (0 if use_persistent else 8) | (16 if stream_weights else 0))
+                 | (0 if use_persistent else 8) | (16 if stream_weights else 0) | (32 if host_sampling else 0))
         o = _LoadOpts(device, max_seq, kv_dtype, max_batch, flags, tp_rank, tp_size)
         if tp_size > 1:
             if len(tp_id) != 128:

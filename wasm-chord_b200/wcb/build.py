@@ -24,7 +24,7 @@ BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG, "libwcb.so")
 SYNTH_LIB = os.path.join(PKG, "libwcb_synth.so")
 
-CUDA_SOURCES = ["kernels.cu", "gemm_tc.cu", "decode_step.cu", "noalloc.cu", "batch_decode.cu", "attn_prefill.cu"]
+CUDA_SOURCES = ["kernels.cu", "gemm_tc.cu", "decode_step.cu", "noalloc.cu", "batch_decode.cu", "attn_prefill.cu", "sample_dev.cu"]
 HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "api.cpp", "nccl_rt.cpp", "tokenizer.cpp"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
