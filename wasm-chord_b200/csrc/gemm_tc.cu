@@ -152,6 +152,29 @@ __device__ __forceinline__ void deq_q4k_64(const Q4Raw& raw, int kq, float (&w)[
   }
 }
 
+// the 32 values of sub-block 2*kq + half of a Q4_K block: the low (half 0) or high
+// (half 1) nibbles of the pair's 32 quant bytes, exactly as deq_q4k_64 computes them
+__device__ __forceinline__ void deq_q4k_32(const Q4Raw& raw, int kq, int half, float (&w)[32]) {
+  const uint4 hd = raw.hd, qa = raw.qa, qb = raw.qb;
+  const float d = halfbits(hd.x & 0xFFFFu), dmin = halfbits(hd.x >> 16);
+  const uint8_t* sc = reinterpret_cast<const uint8_t*>(&hd) + 4;
+  const int j = 2 * kq + half;
+  uint32_t s0, m0;
+  if (j < 4) {
+    s0 = sc[j] & 63; m0 = sc[j + 4] & 63;
+  } else {
+    s0 = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4); m0 = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+  }
+  const float d1 = __fmul_rn(d, float(s0)), mm1 = __fmul_rn(dmin, float(m0));
+  const uint8_t* q = reinterpret_cast<const uint8_t*>(&qa);
+  const uint8_t* q2 = reinterpret_cast<const uint8_t*>(&qb);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint32_t b = i < 16 ? q[i] : q2[i - 16];
+    w[i] = __fsub_rn(__fmul_rn(d1, float(half ? (b >> 4) : (b & 0xF))), mm1);
+  }
+}
+
 // 64 dequantised values [64*kq, 64*kq+64) of a padded Q6_K block (quant.rs:206-261)
 __device__ __forceinline__ void deq_q6k_64(const uint8_t* blk, int kq, float (&w)[64]) {
   const float d = halfbits(uint32_t(blk[208]) | (uint32_t(blk[209]) << 8));
@@ -169,6 +192,33 @@ __device__ __forceinline__ void deq_q6k_64(const uint8_t* blk, int kq, float (&w
   }
 }
 
+// 32 dequantised values [64*kq + 32*half, +32) of a padded Q6_K block
+__device__ __forceinline__ void deq_q6k_32(const uint8_t* blk, int kq, int half, float (&w)[32]) {
+  const float d = halfbits(uint32_t(blk[208]) | (uint32_t(blk[209]) << 8));
+#pragma unroll 8
+  for (int j = 0; j < 32; ++j) {
+    const int v = 64 * kq + 32 * half + j;
+    const int hh = v / 128, r = v % 128, k = r / 32, l = r % 32;
+    const uint8_t* ql = blk + 64 * hh;
+    const uint8_t* qh = blk + 128 + 32 * hh;
+    const int8_t* s = reinterpret_cast<const int8_t*>(blk + 192) + 8 * hh;
+    const int lo = (k & 1) ? ql[l + 32] : ql[l];
+    const int nib = (k < 2) ? (lo & 0xF) : (lo >> 4);
+    const int qv = (nib | (((qh[l] >> (2 * k)) & 3) << 4)) - 32;
+    w[j] = __fmul_rn(__fmul_rn(d, float(s[l / 16 + 2 * k])), float(qv));
+  }
+}
+
+__device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
 template <int DT>
 __device__ __forceinline__ const uint8_t* weight_row(const GemvArgs& a, int r, int epi, size_t row_bytes) {
   // r: row within the virtual (concatenated or gate/up interleaved) weight
@@ -178,13 +228,18 @@ __device__ __forceinline__ const uint8_t* weight_row(const GemvArgs& a, int r, i
   return a.seg[sg].w + size_t(r) * row_bytes;
 }
 
-template <int PRO, int EPI, int DT>
+// XP: the activation tiles come prepared (fp16 hi / lo, core-matrix layout, the
+// RMSNorm weight applied) from stage_x_kernel and are fetched with two bulk copies
+// per K block, and all 256 threads dequantise weights (two per row, 32 values
+// each); otherwise threads 128..255 stage the activations themselves.
+template <int PRO, int EPI, int DT, bool XP>
 __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a, const float* row_m) {
   extern __shared__ __align__(1024) uint8_t tsm[];
-  // [buf][A_hi, A_lo, B_hi, B_lo] tiles, then 2 mbarriers and the TMEM address
+  // [buf][A_hi, A_lo, B_hi, B_lo] tiles, then the MMA and activation-load mbarriers and the TMEM address
   uint8_t* tiles = tsm;
   uint64_t* bar = reinterpret_cast<uint64_t*>(tsm + 2 * 4 * TILE_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
+  uint64_t* bar_a = bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = a.K, NB = K / QK_K;
   const size_t row_bytes = size_t(NB) * (DT == DT_Q4K ? Q4K_BYTES : Q6K_DEV_BYTES);
@@ -201,6 +256,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a
   if (tid == 0) {
     bar_init(bar);
     bar_init(bar + 1);
+    bar_init(bar_a);
+    bar_init(bar_a + 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -212,10 +269,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a
   bool ok = true;
 
   // the weight thread's first block, then each next one requested before the current is used
+  const int wr = XP ? (tid & (TILE_N - 1)) : tid;  // weight row of this thread
+  const int wh = XP ? (tid >> 7) : 0;               // XP: which 32 of the block's 64 values
   Q4Raw wraw{};
   const uint8_t* wrow = nullptr;
-  if (DT == DT_Q4K && tid < TILE_N && r0 + tid < total_rows) {
-    wrow = weight_row<DT>(a, r0 + tid, EPI, row_bytes);
+  if (DT == DT_Q4K && (XP || tid < TILE_N) && r0 + wr < total_rows) {
+    wrow = weight_row<DT>(a, r0 + wr, EPI, row_bytes);
     wraw = q4k_raw(wrow, 0);
   }
   for (int kb = 0; kb < nkb; ++kb) {
@@ -225,7 +284,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a
     uint8_t* Alo = tiles + (buf * 4 + 1) * TILE_BYTES;
     uint8_t* Bhi = tiles + (buf * 4 + 2) * TILE_BYTES;
     uint8_t* Blo = tiles + (buf * 4 + 3) * TILE_BYTES;
-    if (tid < TILE_N) {  // weight row tid of the tile
+    if (XP) {
+      if (tid == 0) {  // the buffer's previous MMAs are done: fetch this block's activation tiles
+        const uint8_t* src = a.xprep + (size_t(blockIdx.y) * nkb + kb) * 2 * TILE_BYTES;
+        expect_tx(bar_a + buf, 2 * TILE_BYTES);
+        bulk_load(Ahi, src, TILE_BYTES, bar_a + buf);
+        bulk_load(Alo, src + TILE_BYTES, TILE_BYTES, bar_a + buf);
+      }
+      const int r = r0 + wr;
+      float w[32];
+      if (r < total_rows) {
+        const uint8_t* row = weight_row<DT>(a, r, EPI, row_bytes);
+        const int b = (kb * KB) / QK_K, kq = (kb * KB / 64) & 3;
+        if (DT == DT_Q4K) {
+          deq_q4k_32(wraw, kq, wh, w);
+          if (kb + 1 < nkb) {
+            const int b1 = ((kb + 1) * KB) / QK_K, kq1 = ((kb + 1) * KB / 64) & 3;
+            wraw = q4k_raw(wrow + size_t(b1) * Q4K_BYTES, kq1);
+          }
+        } else {
+          deq_q6k_32(row + size_t(b) * Q6K_DEV_BYTES, kq, wh, w);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = 0.0f;
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = w[8 * c + e];
+        split_store(Bhi, Blo, wr, 32 * wh + 8 * c, v);
+      }
+    } else if (tid < TILE_N) {  // weight row tid of the tile
       const int r = r0 + tid;
       float w[64];
       if (r < total_rows) {
@@ -283,6 +374,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const GemvArgs a
     fence_before_sync();
     __syncthreads();
     if (tid == 0) {
+      if (XP) ok &= bar_wait(bar_a + buf, uint32_t((kb >> 1) & 1));  // the activation tiles landed
       fence_after_sync();
       const uint32_t ah = smem_addr(Ahi), al = smem_addr(Alo), bh = smem_addr(Bhi), bl = smem_addr(Blo);
 #pragma unroll
@@ -424,19 +516,60 @@ template <int PRO, int EPI, int DT>
 cudaError_t launch_tc_t(const GemvArgs& a, const float* row_m, cudaStream_t s) {
   const int rows = a.ngroups * 4;
   const dim3 grid((rows + TILE_N - 1) / TILE_N, (a.M + TILE_T - 1) / TILE_T);
-  const cudaError_t e = launch_pdl(gemm_tc_kernel<PRO, EPI, DT>, grid, dim3(TC_THREADS), TC_SMEM, s, a.pdl != 0, a,
-                                   row_m);
+  const cudaError_t e =
+      a.xprep ? launch_pdl(gemm_tc_kernel<PRO, EPI, DT, true>, grid, dim3(TC_THREADS), TC_SMEM, s, a.pdl != 0, a, row_m)
+              : launch_pdl(gemm_tc_kernel<PRO, EPI, DT, false>, grid, dim3(TC_THREADS), TC_SMEM, s, a.pdl != 0, a,
+                           row_m);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int PRO, int EPI>
 cudaError_t configure_tc_pe() {
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<PRO, EPI, DT_Q4K>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(TC_SMEM));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gemm_tc_kernel<PRO, EPI, DT_Q6K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(TC_SMEM));
+  cudaError_t e = cudaSuccess;
+  auto set = [&](auto kern) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(TC_SMEM));
+  };
+  set(gemm_tc_kernel<PRO, EPI, DT_Q4K, false>);
+  set(gemm_tc_kernel<PRO, EPI, DT_Q6K, false>);
+  set(gemm_tc_kernel<PRO, EPI, DT_Q4K, true>);
+  set(gemm_tc_kernel<PRO, EPI, DT_Q6K, true>);
   return e;
+}
+
+// the activations of a GEMM as the kernel's A tiles: [token tile][K block] pairs of
+// 16 KB fp16 tiles (hi, lo) in the core-matrix layout, times the RMSNorm weight when
+// given (its per-token divisor is applied in the GEMM epilogue); rows past T are zero
+__global__ void stage_x_kernel(const float* x, int ldx, int T, int K, const float* norm_w, uint8_t* out) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int kb = blockIdx.x, tt = blockIdx.y, nkb = K / KB;
+  const int r = threadIdx.x >> 1, h = threadIdx.x & 1;  // token row of the tile, which 32 values
+  const int t = tt * TILE_T + r;
+  float v[32];
+  if (t < T) {
+    const float* xr = x + size_t(t) * ldx + kb * KB + 32 * h;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 f = *reinterpret_cast<const float4*>(xr + j);
+      v[j] = f.x; v[j + 1] = f.y; v[j + 2] = f.z; v[j + 3] = f.w;
+    }
+    if (norm_w) {
+      const float* nw = norm_w + kb * KB + 32 * h;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], nw[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+  }
+  uint8_t* hi = out + (size_t(tt) * nkb + kb) * 2 * TILE_BYTES;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float w8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w8[e] = v[8 * c + e];
+    split_store(hi, hi + TILE_BYTES, r, 32 * h + 8 * c, w8);
+  }
 }
 
 }  // namespace
@@ -448,6 +581,15 @@ cudaError_t gemm_tc_configure() {
   if (e == cudaSuccess) e = configure_tc_pe<PRO_RMSNORM, EPI_SWIGLU>();
   return e;
 }
+
+cudaError_t launch_stage_x(const float* x, int ldx, int T, int K, const float* norm_w, uint8_t* out, cudaStream_t s) {
+  if (K % KB != 0 || T < 1) return cudaErrorInvalidValue;
+  const cudaError_t e = launch_pdl(stage_x_kernel, dim3(K / KB, (T + TILE_T - 1) / TILE_T), dim3(TC_THREADS), 0, s,
+                                   true, x, ldx, T, K, norm_w, out);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+size_t stage_x_bytes(int T, int K) { return size_t((T + TILE_T - 1) / TILE_T) * (K / KB) * 2 * TILE_BYTES; }
 
 cudaError_t launch_row_rms(const float* x, int ldx, int T, int K, float eps, float* m, bool pdl, cudaStream_t s) {
   const cudaError_t e = launch_pdl(row_rms_kernel, dim3(T), dim3(256), 0, s, pdl, x, ldx, K, eps, m);

@@ -114,6 +114,8 @@ struct GemvArgs {
   // 1: launch with programmatic dependent launch. Only for static weights: the
   // kernel reads its weights before waiting on the previous kernel.
   int pdl;
+  // tensor-core GEMM: the activations prepared by launch_stage_x (null: staged in the kernel)
+  const uint8_t* xprep;
 };
 
 // shared memory of the activation planes of M columns of K values (+ a
@@ -130,6 +132,10 @@ cudaError_t launch_gemv(const GemvArgs& a, int pro, int epi, cudaStream_t s);
 cudaError_t gemm_tc_configure();
 cudaError_t launch_gemm_tc(const GemvArgs& a, int pro, int epi, const float* row_m, cudaStream_t s);
 cudaError_t launch_row_rms(const float* x, int ldx, int T, int K, float eps, float* m, bool pdl, cudaStream_t s);
+// the A tiles of launch_gemm_tc (fp16 hi / lo, times norm_w when not null) into out,
+// stage_x_bytes(T, K) bytes
+cudaError_t launch_stage_x(const float* x, int ldx, int T, int K, const float* norm_w, uint8_t* out, cudaStream_t s);
+size_t stage_x_bytes(int T, int K);
 constexpr int TC_MIN_TOKENS = 16;  // below this the GEMV (dp4a) path is used
 
 // ----------------------------------------------------------- attention ----

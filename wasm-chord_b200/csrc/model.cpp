@@ -248,6 +248,8 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
       peers_dev_ = static_cast<unsigned long long**>(dalloc(sizeof(void*) * tp_));
     }
     row_m_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_)));
+    xprep_ = static_cast<uint8_t*>(
+        dalloc(stage_x_bytes(t_max_, int(std::max({c.hidden, hq_, ffn_l_})))));
     if (tp_ == 1) {  // device sampling: the penalised logits and the splitmix64 state
       plog_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
       rng_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long)));
@@ -521,6 +523,10 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
         check(launch_row_rms(x, ldx, M, K, eps, row_m_, true, stream_), "row rms");
         ++launches_;
       }
+      // the activations once as the GEMM's fp16 hi / lo A tiles, shared by all row tiles
+      check(launch_stage_x(x, ldx, M, K, pro == PRO_RMSNORM ? norm_w : nullptr, xprep_, stream_), "stage x");
+      ++launches_;
+      b.xprep = xprep_;
       check(launch_gemm_tc(b, pro, epi, row_m_, stream_), "gemm");
       ++launches_;
       row_offset += rows;

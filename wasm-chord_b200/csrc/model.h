@@ -178,6 +178,7 @@ class Model {
   float* logits_ = nullptr;
   uint32_t* pen_cnt_ = nullptr;  // occurrences of each token in the sampler history
   float* row_m_ = nullptr;       // per-token RMSNorm divisors for the prefill GEMM
+  uint8_t* xprep_ = nullptr;     // the prefill GEMM's activations as fp16 hi / lo tiles
   int gen_mode_ = 0;
   float rep_ = 1.0f;
   int launches_ = 0;
