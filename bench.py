@@ -442,6 +442,78 @@ def run_tp(args, rank, world, dist):
     m.close()
 
 
+def run_tp_batch(args, rank, world, dist):
+    """The Llama-2-70B shape tensor-parallel over the ranks with `--tp-batch` sequences
+    decoded together (the batched tensor-core step, partial sums all-reduced by NCCL):
+    greedy decode after `--prompt`-token prompts. Decode time = wcb_generate_batch with
+    max_tokens steps + 1 minus the same call with max_tokens 1, maxed over the ranks."""
+    import torch
+    import wcb
+    from wcb import synth
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    layers, B, P, K, W = args.layers, args.tp_batch, args.prompt, args.steps, args.warmup
+    path = [synth.cached_model("llama70b", MODEL_DIR, num_layers=layers) if local == 0 else None]
+    if world > 1:
+        dist.barrier()
+        dist.broadcast_object_list(path, src=0)
+    path = path[0]
+    tp_id = [wcb.tp_unique_id() if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(tp_id, src=0)
+    m = wcb.Model.load_from_gguf(path, device=local, tp_rank=rank, tp_size=world, tp_id=tp_id[0],
+                                 max_seq=P + K + 8, max_batch=B)
+    cfg = m.config
+    s = torch.cuda.ExternalStream(m.stream())
+    prompts = [synth.random_prompt(P, cfg.vocab_size, seed=1 + i).tolist() for i in range(B)]
+
+    def timed(max_tokens):
+        gc = wcb.GenerationConfig(max_tokens=max_tokens, temperature=0.0, repetition_penalty=1.0, eos_id=None)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(s)
+        out = m.generate_batch(prompts, gc)
+        e1.record(s)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()), out
+
+    timed(W + 1)
+    t_pre, _ = timed(1)
+    with ClockSampler(local) as clk:
+        t_full, out = timed(K + 1)
+    assert all(len(o) == K + 1 for o in out)
+    slots, launches = m.batch_info()
+    dec_ms = t_full - t_pre
+    peak, peak_kind = peaks()
+    wbytes = weight_bytes(cfg, path) / world
+    per_rank_gbs = wbytes / (dec_ms / K * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"decode tok/s (Llama-2-70B shape Q4_K, batch {B}, tensor parallel)",
+            "value": B * K / (dec_ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": dec_ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 activations (fp16 hi+lo tensor-core operands), Q4_K weights",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K)",
+            "config": {"workload": f"Llama-2-70B shape, {layers} of its 80 layers, {B} sequences x {P}-token "
+                                   f"prompts, greedy", "layers": layers, "prompt_len": P, "batch": B,
+                       "parallelism": f"tp{world} (batched step; partial sums all-reduced by NCCL)",
+                       "l2": "weights > 126 MB L2, no flush"},
+            "roofline": {"bound": "hbm", "achieved": per_rank_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": per_rank_gbs / peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "whole batched decode step per rank (shard weights / ms per step)",
+                         "bytes_per_launch": wbytes},
+            "prefill": {"value": B * P / (t_pre * 1e-3), "unit": "tok/s", "ms": t_pre},
+            "gpu_launches": launches * K, "launches_per_step": launches,
+            "clocks": clk.summary(),
+        }), flush=True)
+    m.close()
+
+
 def run_serve(args, rank, world, dist):
     """Batched serving on the TinyLlama shape: `sequences` prompts of `prompt`
     uniform-random ids split evenly over the ranks (independent replicas), each
@@ -538,6 +610,7 @@ def main():
     ap.add_argument("--layers", type=int, default=80, help="--tp: layers of the 70B shape to build")
     ap.add_argument("--prompt", type=int, default=1024, help="--tp: prompt tokens before the timed decode")
     ap.add_argument("--tp-nccl", action="store_true", help="--tp: all-reduce decode steps with NCCL too")
+    ap.add_argument("--tp-batch", type=int, default=1, help="--tp: sequences decoded together (batched step)")
     ap.add_argument("--stream-weights", action="store_true",
                     help="decode line with the layer weights streamed from pinned host memory (not the headline)")
     ap.add_argument("--serve", action="store_true",
@@ -571,7 +644,9 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     try:
-        if args.tp:
+        if args.tp and args.tp_batch > 1:
+            run_tp_batch(args, rank, world, dist)
+        elif args.tp:
             run_tp(args, rank, world, dist)
         elif args.serve:
             run_serve(args, rank, world, dist)

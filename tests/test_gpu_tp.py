@@ -79,3 +79,47 @@ def test_tp2_matches_oracle(model_dir, gpu, exchange):
     o.clear_kv_cache()
     ref_toks = o.generate(prompt, 40, repetition_penalty=1.1, eos_id=None)
     assert res[0][1] == ref_toks and res[1][1] == ref_toks
+
+
+def _batch_rank_main(rank, world, path, tp_id, prompts, q):
+    try:
+        import torch
+        torch.cuda.set_device(rank)
+        m = wcb.Model.load_from_gguf(path, device=rank, tp_rank=rank, tp_size=world, tp_id=tp_id, max_batch=4)
+        cfg = wcb.GenerationConfig(max_tokens=24, temperature=0.0, repetition_penalty=1.1, eos_id=None)
+        out = m.generate_batch(prompts, cfg)
+        slots, launches = m.batch_info()
+        m.close()
+        q.put((rank, out, slots, None))
+    except Exception as e:  # reported to the parent
+        q.put((rank, None, None, repr(e)))
+
+
+def test_tp2_batched_decode_matches_oracle(model_dir, gpu):
+    """generate_batch on a tensor-parallel model: the batched tensor-core step with
+    row-parallel partial sums all-reduced and a vocabulary-split LM head."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    path = synth.cached_model("tiny_tp", model_dir)
+    prompts = [synth.random_prompt(n, 1024, seed=60 + n).tolist() for n in (9, 21, 4, 33, 16)]  # 5 > 4 slots
+    tp_id = wcb.tp_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_batch_rank_main, args=(r, 2, path, tp_id, prompts, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, out, slots, err = q.get(timeout=600)
+        res[r] = (out, slots, err)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert res[r][2] is None, res[r][2]
+        assert res[r][1] == 4
+    o = oracle.OracleModel(path)
+    for i, p in enumerate(prompts):
+        o.clear_kv_cache()
+        want = o.generate(p, 24, repetition_penalty=1.1, eos_id=None)
+        assert res[0][0][i] == want and res[1][0][i] == want, i

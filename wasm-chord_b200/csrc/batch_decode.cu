@@ -1001,6 +1001,82 @@ __global__ void __launch_bounds__(BA_THREADS) battn_kernel(const AttnArgs a) {
   }
 }
 
+// Tensor parallelism: y = resid + (the all-reduced partial sums), and the
+// per-128-row-tile sums of squares of y for the next RMSNorm (grid: tiles x B)
+__global__ void bresid_kernel(float* y, const float* resid, const float* add, int B, int H, float* sq) {
+  pdl_trigger();
+  pdl_wait();
+  const int tile = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, n = tile * BATCH_TILE + tid;
+  float v = 0.0f;
+  if (n < H) {
+    v = __fadd_rn(resid[size_t(b) * H + n], add[size_t(b) * H + n]);
+    y[size_t(b) * H + n] = v;
+  }
+  __shared__ float red[BATCH_TILE / 32];
+  const float s2 = warp_sum(__fmul_rn(v, v));
+  if ((tid & 31) == 0) red[tid >> 5] = s2;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.0f;
+    for (int w = 0; w < BATCH_TILE / 32; ++w) t = __fadd_rn(t, red[w]);
+    sq[size_t(tile) * B + b] = t;
+  }
+}
+
+// Tensor parallelism, LM head split by vocabulary: each sequence's best
+// (order-preserving logit bits << 32 | token id) over this rank's rows after
+// the repetition penalty, and a NaN flag, max-reduced into keys[2b], keys[2b+1]
+// (zeroed before); the ranks then max all-reduce the keys
+__global__ void bkey_kernel(const float* logits, int vl, int vocab_off, int vocab, const StepState* st,
+                            const uint32_t* pen_cnt, float rep, unsigned long long* keys) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x, tid = threadIdx.x;
+  if (st[b].done) return;
+  const float* lg = logits + size_t(b) * vl;
+  const uint32_t* pc = pen_cnt + size_t(b) * vocab + vocab_off;
+  const int per = (vl + gridDim.y - 1) / gridDim.y;
+  const int v0 = blockIdx.y * per, v1 = min(vl, v0 + per);
+  unsigned long long best = 0ull;
+  int nan = 0;
+  for (int n = v0 + tid; n < v1; n += blockDim.x) {
+    float pv = lg[n];
+    if (rep != 1.0f) {
+      const uint32_t cnt = pc[n];
+      for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, rep) : __fmul_rn(pv, rep);
+    }
+    if (pv != pv) nan = 1;
+    else {
+      const unsigned long long key =
+          (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(vocab_off + n);
+      best = key > best ? key : best;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+    best = ob > best ? ob : best;
+    nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+  }
+  if ((tid & 31) == 0) {
+    if (best) atomicMax(keys + 2 * b, best);
+    if (nan) atomicMax(keys + 2 * b + 1, 1ull);
+  }
+}
+
+// generate()'s bookkeeping of every unfinished sequence from the reduced keys
+__global__ void bfinish_kernel(StepState* st, const unsigned long long* keys, uint32_t* hist, int hist_cap,
+                               uint32_t* pen_cnt, int vocab) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x;
+  StepState* s = st + b;
+  if (threadIdx.x != 0 || s->done) return;
+  s->best = keys[2 * b];
+  s->nan = keys[2 * b + 1] ? 1 : 0;
+  finish_sample_state(s, hist + size_t(b) * hist_cap, pen_cnt + size_t(b) * vocab);
+}
+
 // The same decode attention on the tensor cores, for an fp16 cache: per warp,
 // 32-key tiles of its 64 keys are staged in shared memory (cp.async), the n_rep
 // query heads are the rows of a 16-row mma.sync.m16n8k16 operand (rows n_rep..15
@@ -1336,6 +1412,26 @@ cudaError_t launch_batch_attention(const AttnArgs& a, cudaStream_t s) {
                   : bd_launch(battn_kernel<128, float>, grid, dim3(BA_THREADS), 0, s, a);
   else
     return cudaErrorInvalidValue;
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t launch_batch_resid(float* y, const float* resid, const float* add, int B, int H, float* sq,
+                               cudaStream_t s) {
+  if (H % BATCH_TILE != 0) return cudaErrorInvalidValue;
+  const cudaError_t e = bd_launch(bresid_kernel, dim3(H / BATCH_TILE, B), dim3(BATCH_TILE), 0, s, y, resid, add, B, H, sq);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t launch_batch_keys(const float* logits, int vl, int vocab_off, int vocab, const StepState* st,
+                              const uint32_t* pen_cnt, float rep, unsigned long long* keys, int B, cudaStream_t s) {
+  const cudaError_t e = bd_launch(bkey_kernel, dim3(B, 8), dim3(512), 0, s, logits, vl, vocab_off, vocab, st, pen_cnt,
+                                  rep, keys);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t launch_batch_finish(StepState* st, const unsigned long long* keys, uint32_t* hist, int hist_cap,
+                                uint32_t* pen_cnt, int vocab, int B, cudaStream_t s) {
+  const cudaError_t e = bd_launch(bfinish_kernel, dim3(B), dim3(32), 0, s, st, keys, hist, hist_cap, pen_cnt, vocab);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 

@@ -314,6 +314,16 @@ cudaError_t launch_batch_gemm(BatchGemmArgs a, int epi, cudaStream_t s);
 // (n_kv, B, max_splits), a.chunk keys per split, merged by the last CTA of a
 // (sequence, kv head); K rows and V rows are read straight from the cache
 cudaError_t launch_batch_attention(const AttnArgs& a, cudaStream_t s);
+// tensor parallelism: y[b] = resid[b] + add[b] (the all-reduced partial sums) with
+// per-128-row-tile sums of squares sq[tile][b]; the vocabulary-split LM head's
+// per-sequence keys (keys[2b] = best (logit bits << 32 | id), keys[2b+1] = NaN seen,
+// zeroed before, max all-reduced after) and the bookkeeping from the reduced keys
+cudaError_t launch_batch_resid(float* y, const float* resid, const float* add, int B, int H, float* sq,
+                               cudaStream_t s);
+cudaError_t launch_batch_keys(const float* logits, int vl, int vocab_off, int vocab, const StepState* st,
+                              const uint32_t* pen_cnt, float rep, unsigned long long* keys, int B, cudaStream_t s);
+cudaError_t launch_batch_finish(StepState* st, const unsigned long long* keys, uint32_t* hist, int hist_cap,
+                                uint32_t* pen_cnt, int vocab, int B, cudaStream_t s);
 // x[b] = embedding row of sequence b's last token; sq[b] = sum of squares of x[b]
 cudaError_t launch_batch_embed(const float* emb, int vocab, int hidden, const StepState* st, const uint32_t* hist,
                                int hist_cap, float* x, float* sq, int B, cudaStream_t s);

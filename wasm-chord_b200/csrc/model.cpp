@@ -208,9 +208,11 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     // batched decode slots (generate_batch): each holds its own KV cache, state,
     // sampler history and penalty counts; the tensor-core step needs 128-row
     // tiles that never straddle q / k / v, and 64-row gate / up halves
-    bslots_ = (tp_ == 1 && !wstream_) ? std::min<uint32_t>(std::max<uint32_t>(opt.max_batch, 1), BATCH_MAX) : 1;
-    batch_ok_ = bslots_ > 1 && c.hidden % BATCH_TILE == 0 && kvd % BATCH_TILE == 0 && c.ffn % 64 == 0 &&
-                c.heads / c.kv_heads <= 8;
+    // (with tensor parallelism: this rank's q / k / v / gate / up rows)
+    bslots_ = !wstream_ ? std::min<uint32_t>(std::max<uint32_t>(opt.max_batch, 1), BATCH_MAX) : 1;
+    batch_ok_ = bslots_ > 1 && c.hidden % BATCH_TILE == 0 && hq_ % BATCH_TILE == 0 && kvd_l_ % BATCH_TILE == 0 &&
+                ffn_l_ % 64 == 0 && c.heads / c.kv_heads <= 8;
+    (void)kvd;
     if (!batch_ok_) bslots_ = 1;
     // KV cache (kv_cache.rs:6-34), [slot][L][n_kv][max_seq][hd]
     kv_layer_elems_ = size_t(kv_l_) * max_seq_ * hd;
@@ -269,6 +271,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
       // per-CTA sums of squares of the residual stream: tiles x K slices (<= 8) per sequence
       sqx_ = static_cast<float*>(dalloc(sizeof(float) * B * (H / BATCH_TILE) * 8));
       sqh_ = static_cast<float*>(dalloc(sizeof(float) * B * (H / BATCH_TILE) * 8));
+      if (tp_ > 1) tpkeys_b_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * 2 * B));
       asplits_ = int((max_seq_ + BATCH_CHUNK - 1) / BATCH_CHUNK);
       apart_ = static_cast<float*>(dalloc(sizeof(float) * B * c.heads * size_t(asplits_) * (hd + 2)));
       aticket_ = static_cast<int*>(dalloc(sizeof(int) * B * c.kv_heads));
@@ -1248,17 +1251,48 @@ void Model::enqueue_batch_step(int B) {
     check(launch_batch_attention(a, stream_), "attention");
     ++batch_launches_;
     const DevWeight o[1] = {L.o};
-    const int sq_h = batch_gemm(o, 1, H, HQ, B, att_, HQ, nullptr, nullptr, 0, 0.0f, BEPI_RESID, h_, H, x_, H, sqh_, -1);
     const DevWeight gu[2] = {L.gate, L.up};
-    batch_gemm(gu, 2, F, H, B, h_, H, L.ffn_norm, sqh_, sq_h, 1e-6f, BEPI_SWIGLU, act_, F, nullptr, 0, nullptr, -1);
     const DevWeight dn[1] = {L.down};
-    sq_x = batch_gemm(dn, 1, H, F, B, act_, F, nullptr, nullptr, 0, 0.0f, BEPI_RESID, x_, H, h_, H, sqx_, -1);
+    int sq_h;
+    if (tp_ == 1) {
+      sq_h = batch_gemm(o, 1, H, HQ, B, att_, HQ, nullptr, nullptr, 0, 0.0f, BEPI_RESID, h_, H, x_, H, sqh_, -1);
+    } else {  // row-parallel: this rank's partial sums, all-reduced, then the residual
+      batch_gemm(o, 1, H, HQ, B, att_, HQ, nullptr, nullptr, 0, 0.0f, BEPI_STORE, part_y_, H, nullptr, 0, nullptr, -1);
+      all_reduce_sum(part_y_, size_t(B) * H);
+      check(launch_batch_resid(h_, x_, part_y_, B, H, sqh_, stream_), "residual");
+      ++batch_launches_;
+      sq_h = H / BATCH_TILE;
+    }
+    batch_gemm(gu, 2, F, H, B, h_, H, L.ffn_norm, sqh_, sq_h, 1e-6f, BEPI_SWIGLU, act_, F, nullptr, 0, nullptr, -1);
+    if (tp_ == 1) {
+      sq_x = batch_gemm(dn, 1, H, F, B, act_, F, nullptr, nullptr, 0, 0.0f, BEPI_RESID, x_, H, h_, H, sqx_, -1);
+    } else {
+      batch_gemm(dn, 1, H, F, B, act_, F, nullptr, nullptr, 0, 0.0f, BEPI_STORE, part_y_, H, nullptr, 0, nullptr, -1);
+      all_reduce_sum(part_y_, size_t(B) * H);
+      check(launch_batch_resid(x_, h_, part_y_, B, H, sqx_, stream_), "residual");
+      ++batch_launches_;
+      sq_x = H / BATCH_TILE;
+    }
   }
   const DevWeight head[1] = {lm_head_};
-  batch_gemm(head, 1, V, H, B, x_, H, out_norm_, sqx_, sq_x, c.eps, BEPI_STORE, logits_b_, V, nullptr, 0, nullptr, -1);
-  check(launch_batch_sample(logits_b_, V, st_base_, hist_base_, int(hist_cap_), pen_base_, rep_, B, stream_),
-        "sampler");
-  ++batch_launches_;
+  const int VL = int(vocab_l_);  // this rank's LM-head rows (all of them with one rank)
+  batch_gemm(head, 1, VL, H, B, x_, H, out_norm_, sqx_, sq_x, c.eps, BEPI_STORE, logits_b_, VL, nullptr, 0, nullptr,
+             -1);
+  if (tp_ == 1) {
+    check(launch_batch_sample(logits_b_, V, st_base_, hist_base_, int(hist_cap_), pen_base_, rep_, B, stream_),
+          "sampler");
+    ++batch_launches_;
+  } else {  // vocabulary split: per-sequence keys, max all-reduced, then the bookkeeping
+    check(cudaMemsetAsync(tpkeys_b_, 0, sizeof(unsigned long long) * 2 * size_t(B), stream_), "clear keys");
+    check(launch_batch_keys(logits_b_, VL, int(vocab_off_), V, st_base_, pen_base_, rep_, tpkeys_b_, B, stream_),
+          "argmax keys");
+    const ncclResult_t r = nccl().AllReduce(tpkeys_b_, tpkeys_b_, 2 * size_t(B), ncclUint64, ncclMax, comm_, stream_);
+    if (r != ncclSuccess)
+      throw WcbError(E_BACKEND, std::string("Backend error: ncclAllReduce: ") + nccl().GetErrorString(r));
+    check(launch_batch_finish(st_base_, tpkeys_b_, hist_base_, int(hist_cap_), pen_base_, V, B, stream_),
+          "sampler bookkeeping");
+    batch_launches_ += 2;
+  }
 }
 
 std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts, const size_t* lens, size_t n,

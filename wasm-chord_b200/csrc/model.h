@@ -248,6 +248,7 @@ class Model {
   float* logits_b_ = nullptr;   // [bslots][vocab]
   float* sqx_ = nullptr;        // [tiles x slices][bslots] partial sums of squares of the residual stream x
   float* sqh_ = nullptr;        // the same for h (after attention)
+  unsigned long long* tpkeys_b_ = nullptr;  // tensor parallelism: [bslots][2] LM-head keys
   float* apart_ = nullptr;      // attention split partials [bslots][heads][asplits][hd + 2]
   int* aticket_ = nullptr;      // [bslots][kv_heads]
   int asplits_ = 0;
