@@ -13,6 +13,9 @@ L2 flush is needed between steps.
   [torchrun ...] bench.py --serve [--sequences S] [--prompt P]
       (batched serving: S sequences of a P-token prompt + --steps decode tokens,
       split evenly over the ranks, fp16 KV; not the headline line)
+  python bench.py --microbench REPS
+      (Q4_K GEMV/GEMM through wcb_gemv_dev at 5 weight shapes x M = 1, 16, 512;
+      one JSON line each; not the headline line)
 
 N > 1 runs under torchrun as N independent data-parallel replicas (no
 collective on the data path); value is the total tokens/s over all ranks with
@@ -126,35 +129,83 @@ def ensure_model(rank, world, dist, preset="tinyllama"):
     return path
 
 
-def gemv_roofline(torch, wcb, stream_ptr, cfg, peak, reps_per_copy=8):
-    """Times the dominant kernel of the decode step — the fused Q4_K dequant-GEMV
-    at the FFN gate+up shape [2*F, H], M = 1 — on the stream it is launched on,
-    rotating over enough weight copies that each launch reads from HBM."""
+def time_gemv(torch, wcb, stream_ptr, n, k, m, reps_per_copy=8, seed=99):
+    """Times wcb_gemv_dev (y[m][n] = x[m][k] W[n][k]^T, W Q4_K) on the stream it is
+    launched on, rotating over enough weight copies that each launch reads its
+    weights from HBM, not from the 126 MB L2. Returns (bytes, flops, us per launch)."""
     from wcb import synth
-    n, k = 2 * cfg.intermediate_size, cfg.hidden_size
-    blocks = synth.quantize_q4_k_fast(synth.normal(99, 1, n * k, 0.0, 0.02))
+    blocks = synth.quantize_q4_k_fast(synth.normal(seed, 1, n * k, 0.0, 0.02))
     nbytes = blocks.nbytes
     copies = max(4, int(2 * 126e6 // nbytes) + 1)
     dev = torch.from_numpy(blocks.reshape(-1)).cuda()
     ws = [dev.clone() for _ in range(copies)]
-    x = torch.from_numpy(synth.normal(98, 1, k, 0.0, 1.0)).cuda()
-    y = torch.empty(n, dtype=torch.float32, device="cuda")
+    del dev
+    x = torch.from_numpy(synth.normal(seed - 1, 1, m * k, 0.0, 1.0)).cuda()
+    y = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()  # the copies above ran on torch's stream, the launches below on stream_ptr
     s = torch.cuda.ExternalStream(stream_ptr)
     reps = reps_per_copy * copies
     with torch.cuda.stream(s):
         for i in range(min(2, reps_per_copy) * copies):
-            wcb.gemv_dev(ws[i % copies].data_ptr(), wcb.DTYPE_Q4_K, n, k, x.data_ptr(), 1, y.data_ptr(), stream_ptr)
+            wcb.gemv_dev(ws[i % copies].data_ptr(), wcb.DTYPE_Q4_K, n, k, x.data_ptr(), m, y.data_ptr(), stream_ptr)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
         for i in range(reps):
-            wcb.gemv_dev(ws[i % copies].data_ptr(), wcb.DTYPE_Q4_K, n, k, x.data_ptr(), 1, y.data_ptr(), stream_ptr)
+            wcb.gemv_dev(ws[i % copies].data_ptr(), wcb.DTYPE_Q4_K, n, k, x.data_ptr(), m, y.data_ptr(), stream_ptr)
         e1.record(s)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    algo = nbytes + 4 * k + 4 * n
-    gbs = algo / (ms * 1e-3) / 1e9
+    us = e0.elapsed_time(e1) / reps * 1e3
+    return nbytes + 4 * m * k + 4 * m * n, 2 * m * n * k, us, copies
+
+
+def gemv_roofline(torch, wcb, stream_ptr, cfg, peak, reps_per_copy=8):
+    """Times the dominant kernel of the decode step — the fused Q4_K dequant-GEMV
+    at the FFN gate+up shape [2*F, H], M = 1 — on the stream it is launched on."""
+    n, k = 2 * cfg.intermediate_size, cfg.hidden_size
+    algo, _, us, copies = time_gemv(torch, wcb, stream_ptr, n, k, 1, reps_per_copy)
+    gbs = algo / (us * 1e-6) / 1e9
     return {"kernel": "gemv_kernel<1,PRO_NONE,EPI_STORE> (Q4_K)", "shape_nk": [n, k], "m": 1,
-            "bytes_per_launch": algo, "us_per_launch": ms * 1e3, "achieved": gbs, "copies_rotated": copies}
+            "bytes_per_launch": algo, "us_per_launch": us, "achieved": gbs, "copies_rotated": copies}
+
+
+# the Q4_K GEMV / GEMM microbenchmark: weight shapes [N, K] at M activation rows
+MICRO_SHAPES = ((2048, 2048), (5632, 2048), (4096, 4096), (11008, 4096), (32000, 4096))
+MICRO_M = (1, 16, 512)
+
+
+def run_microbench(reps_per_copy):
+    """One JSON line per (shape, M) through wcb_gemv_dev: M < 16 runs the dp4a
+    GEMV, M >= 16 the tcgen05 tensor-core GEMM. M <= 16 is bound by the weight
+    bytes (HBM roofline), M = 512 by the tensor cores (arithmetic intensity
+    2*512 / 0.5625 = 1820 flop per weight byte)."""
+    import torch
+    import wcb
+    hbm, kind = peaks()
+    tf = None
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        tf = float(json.load(open(p))["bf16_tflops"])
+    tf = tf or 1590.0
+    st = torch.cuda.Stream()  # a created stream: the library and the events order on the same handle
+    sp = st.cuda_stream
+    for n, k in MICRO_SHAPES:
+        for m in MICRO_M:
+            algo, flops, us, copies = time_gemv(torch, wcb, sp, n, k, m, reps_per_copy)
+            gbs = algo / (us * 1e-6) / 1e9
+            tfs = flops / (us * 1e-6) / 1e12
+            tensor = m >= 256
+            frac = (tfs / tf) if tensor else (gbs / hbm)
+            print(json.dumps({
+                "metric": "Q4_K GEMV/GEMM microbenchmark", "shape_nk": [n, k], "m": m,
+                "kernel": "gemm_tc_kernel (tcgen05)" if m >= 16 else "gemv_kernel (dp4a)",
+                "us_per_launch": round(us, 3), "bytes_per_launch": algo, "flops_per_launch": flops,
+                "roofline": {"bound": "tensor" if tensor else "hbm",
+                             "achieved": tfs if tensor else gbs, "peak": tf if tensor else hbm,
+                             "unit": "TFLOP/s" if tensor else "GB/s",
+                             "frac": frac, "peak_kind": kind},
+                "valid": frac < 1.5,  # far above the measured peak: the timed launches did not do the work
+                "gbs": round(gbs, 1), "tflops": round(tfs, 2), "copies_rotated": copies,
+                "l2": "weight copies rotated so each launch reads its weights from HBM"}), flush=True)
 
 
 def cpu_baseline(path, budget_s=20.0, prompt_len=8):
@@ -603,6 +654,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv-only", type=int, default=0, metavar="REPS",
                     help="only time the dominant GEMV (REPS launches per weight copy) and print its line")
+    ap.add_argument("--microbench", type=int, default=0, metavar="REPS",
+                    help="Q4_K GEMV/GEMM sweep over 5 weight shapes x M in (1, 16, 512), REPS launches per weight copy")
     ap.add_argument("--model", choices=sorted(MODELS), default="tinyllama",
                     help="the decoder shape of the decode line (the headline is tinyllama)")
     ap.add_argument("--tp", action="store_true",
@@ -624,9 +677,13 @@ def main():
         import wcb
         from wcb import synth
         cfg = synth.PRESETS["tinyllama"]
-        stream_ptr = torch.cuda.current_stream().cuda_stream
+        st = torch.cuda.Stream()
+        stream_ptr = st.cuda_stream
         r = gemv_roofline(torch, wcb, stream_ptr, cfg, peaks()[0], reps_per_copy=args.gemv_only)
         print(json.dumps(r), flush=True)
+        return
+    if args.microbench:
+        run_microbench(args.microbench)
         return
     if args.warmup < 3:
         args.warmup = 3

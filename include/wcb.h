@@ -235,8 +235,9 @@ uint32_t wcb_repack_q6k_dev(const void* packed, size_t nblocks, void* padded, vo
 /* y[m][n] = sum_k x[m][k] * W[n][k] (matmul_transposed, gemm.rs:83-143) with W
  * an [n, k] tensor in device layout: raw Q4_K blocks (dtype WCB_DTYPE_Q4_K) or
  * padded Q6_K blocks (WCB_DTYPE_Q6_K, see wcb_repack_q6k_dev). x is [m][k] and
- * y is [m][n], f32, row-major. k % 256 == 0, n % 4 == 0, 1 <= m <= 4096.
- * m >= 16 runs the tcgen05 tensor-core GEMM, smaller m the dp4a GEMV. */
+ * y is [m][n], f32, row-major. k % 256 == 0, n % 4 == 0, 1 <= m <= 4096; w and
+ * x 16-byte aligned. m <= 4 runs the dp4a GEMV, 5 <= m <= 32 the batched decode
+ * GEMM (tcgen05, one launch), larger m the tcgen05 prefill GEMM. */
 uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const float* x, size_t m, float* y,
                       void* stream);
 

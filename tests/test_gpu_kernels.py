@@ -97,6 +97,17 @@ def test_gemv_q6k(gpu, n, k, m):
     assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max() * np.sqrt(k / 256)
 
 
+# 5..32 activation rows run the batched decode GEMM (tcgen05, one launch): ragged
+# row counts, one-super-block K, Q6_K, and the largest microbenchmark shape
+@pytest.mark.parametrize("n,k,m,dtype", [
+    (2048, 2048, 32, wcb.DTYPE_Q4_K), (11008, 4096, 24, wcb.DTYPE_Q4_K), (260, 768, 7, wcb.DTYPE_Q4_K),
+    (4, 256, 5, wcb.DTYPE_Q4_K), (32000, 4096, 16, wcb.DTYPE_Q4_K), (4096, 4096, 17, wcb.DTYPE_Q6_K),
+    (388, 1280, 32, wcb.DTYPE_Q6_K)])
+def test_gemv_batched_rows(gpu, n, k, m, dtype):
+    got, ref = _gemv_case(n, k, m, dtype, seed=13)
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max() * np.sqrt(k / 256)
+
+
 def test_gemv_m512_prefill_shape(gpu):
     got, ref = _gemv_case(2048, 2048, 512, wcb.DTYPE_Q4_K, seed=9)
     assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max() * np.sqrt(2048 / 256)
@@ -120,4 +131,11 @@ def test_gemv_linearity_at_full_size(gpu):
 def test_gemv_rejects_bad_shapes(gpu):
     with pytest.raises(wcb.WcbError) as e:
         wcb.gemv_dev(1, wcb.DTYPE_Q4_K, 4, 100, 1, 1, 1)
+    assert e.value.code == 3
+    # x or W off a 16-byte boundary is refused on the host (the kernels read 16-byte vectors)
+    with pytest.raises(wcb.WcbError) as e:
+        wcb.gemv_dev(4096, wcb.DTYPE_Q4_K, 4, 256, 4096 + 4, 8, 8192)
+    assert e.value.code == 3
+    with pytest.raises(wcb.WcbError) as e:
+        wcb.gemv_dev(4096 + 8, wcb.DTYPE_Q4_K, 4, 256, 4096, 1, 8192)
     assert e.value.code == 3

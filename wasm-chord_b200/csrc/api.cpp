@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdint>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -123,6 +124,40 @@ wcb::GenParams params_of(const wcb_gen_config* c) {
 uint32_t cuda_fail(cudaError_t e, const char* what) {
   return fail(e == cudaErrorMemoryAllocation ? WCB_ERR_OOM : WCB_ERR_BACKEND_UNSUPPORTED,
               std::string("Backend error: ") + what + ": " + cudaGetErrorString(e));
+}
+
+// Per device, for wcb_gemv_dev: kernel attributes set once, and BATCH_MAX zeroed
+// sequence states for the batched tensor-core GEMM (it reads position / kv_len /
+// done of each activation row and records an expired bounded wait in state 0).
+struct GemvDevice {
+  bool configured = false;
+  wcb::StepState* states = nullptr;
+};
+std::mutex g_gemv_mu;
+std::map<int, GemvDevice> g_gemv_dev;
+
+cudaError_t gemv_device(GemvDevice** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(g_gemv_mu);
+  GemvDevice& g = g_gemv_dev[dev];
+  if (!g.configured) {
+    e = wcb::gemv_configure_all();
+    if (e == cudaSuccess) e = wcb::gemm_tc_configure();
+    if (e == cudaSuccess) e = wcb::batch_configure();
+    if (e == cudaSuccess && !g.states) {
+      void* p = nullptr;
+      e = cudaMalloc(&p, sizeof(wcb::StepState) * wcb::BATCH_MAX);
+      if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(wcb::StepState) * wcb::BATCH_MAX);
+      if (e == cudaSuccess) g.states = static_cast<wcb::StepState*>(p);
+      else if (p) cudaFree(p);
+    }
+    if (e != cudaSuccess) return e;
+    g.configured = true;
+  }
+  *out = &g;
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -413,12 +448,31 @@ uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const f
   if (!w || !x || !y) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
   if (k == 0 || k % 256 || n == 0 || n % 4 || m == 0 || m > 4096 || k > (1u << 20) || n > (1u << 28))
     return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid tensor shape: need k % 256 == 0, n % 4 == 0, 1 <= m <= 4096");
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = wcb::gemv_configure_all();
-    if (e == cudaSuccess) e = wcb::gemm_tc_configure();
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15)
+    return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: x and w must be 16-byte aligned");
+  GemvDevice* gd = nullptr;
+  {
+    const cudaError_t e = gemv_device(&gd);
     if (e != cudaSuccess) return cuda_fail(e, "configure");
-    configured = true;
+  }
+  if (m > 4 && m <= size_t(wcb::BATCH_MAX)) {
+    // 5..32 rows: the batched decode GEMM (tcgen05, M = 128 weight rows, N = 2 x rows),
+    // every weight byte read once by one single-wave launch
+    wcb::BatchGemmArgs b{};
+    b.seg[0].w = static_cast<const uint8_t*>(w);
+    b.seg[0].dtype = int(dtype);
+    b.seg[0].rows = int(n);
+    b.nseg = 1;
+    b.rows = int(n);
+    b.K = int(k);
+    b.B = int(m);
+    b.x = x;
+    b.ldx = int(k);
+    b.y = y;
+    b.ldy = int(n);
+    b.st = gd->states;
+    const cudaError_t e = wcb::launch_batch_gemm(b, wcb::BEPI_STORE, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WCB_OK : cuda_fail(e, "batched gemm");
   }
   wcb::GemvArgs a{};
   a.seg[0].w = static_cast<const uint8_t*>(w);
