@@ -93,6 +93,24 @@ def test_last_error_is_taken_once():
     assert wcb.last_error() == "No error"
 
 
+def test_gemv_argument_errors_without_touching_the_gpu():
+    # wcb_gemv_dev validates dtype, pointers, shape and 16-byte alignment on the host,
+    # before any CUDA call; the addresses below are never dereferenced
+    cases = [
+        (4096, 99, 4, 256, 4096, 1),        # unsupported dtype
+        (0, wcb.DTYPE_Q4_K, 4, 256, 4096, 1),  # null weights
+        (4096, wcb.DTYPE_Q4_K, 4, 100, 4096, 1),  # k % 256 != 0
+        (4096, wcb.DTYPE_Q4_K, 6, 256, 4096, 1),  # n % 4 != 0
+        (4096, wcb.DTYPE_Q4_K, 4, 256, 4096, 4097),  # m > 4096
+        (4096, wcb.DTYPE_Q4_K, 4, 256, 4096 + 4, 8),  # x off a 16-byte boundary
+        (4096 + 8, wcb.DTYPE_Q4_K, 4, 256, 4096, 1),  # W off a 16-byte boundary
+    ]
+    for w, dt, n, k, x, m in cases:
+        with pytest.raises(wcb.WcbError) as e:
+            wcb.gemv_dev(w, dt, n, k, x, m, 8192)
+        assert e.value.code == 3, (w, dt, n, k, x, m)
+
+
 def test_invalid_handles():
     L = wcb.lib()
     assert L.wcb_model_free(12345) == 3
