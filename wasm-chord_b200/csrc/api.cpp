@@ -457,7 +457,7 @@ uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const f
   }
   if (m > 4 && m <= size_t(wcb::BATCH_MAX)) {
     // 5..32 rows: the batched decode GEMM (tcgen05, M = 128 weight rows, N = 2 x rows),
-    // every weight byte read once by one single-wave launch
+    // one launch that reads every weight byte once
     wcb::BatchGemmArgs b{};
     b.seg[0].w = static_cast<const uint8_t*>(w);
     b.seg[0].dtype = int(dtype);
