@@ -854,9 +854,13 @@ __device__ __forceinline__ void mk_attention(const MkArgs& a, const MkSmem& sm, 
   __threadfence();
   if (tid == 0) a.ticket[kh] = 0;
   const float* pbase = a.part + size_t(kh) * n_rep * hstride;
+  // the split maxima and sums in one round of loads; the sums go to the K staging
+  // area, which the tiles no longer use
+  float* ls = reinterpret_cast<float*>(Ks);  // [n_rep][nsplit]
   for (int i = tid; i < n_rep * nsplit; i += MK_T) {
     const int r = i / nsplit, sp = i % nsplit;
     mm[r * nsplit + sp] = __ldcg(pbase + r * hstride + sp * pstride);
+    ls[r * nsplit + sp] = __ldcg(pbase + r * hstride + sp * pstride + 1);
   }
   cbar();
   for (int r = warp; r < n_rep; r += MK_W) {
@@ -866,25 +870,38 @@ __device__ __forceinline__ void mk_attention(const MkArgs& a, const MkSmem& sm, 
     float L = 0.0f;
     for (int sp = lane; sp < nsplit; sp += 32) {
       const float f = expf(mm[r * nsplit + sp] - M);
-      L += __ldcg(pbase + r * hstride + sp * pstride + 1) * f;
+      L += ls[r * nsplit + sp] * f;
       mm[r * nsplit + sp] = f;
     }
     L = warp_sum(L);
     if (lane == 0) ml[2 * r + 1] = L;
   }
   cbar();
+  // weighted sum of the split outputs: the loads of up to 8 splits are issued
+  // together, the additions keep their order (groups of 4, then single splits)
+  constexpr int MB = 8;
   for (int i = tid; i < n_rep * HD; i += MK_T) {
     const int r = i / HD, d = i % HD;
     const float* pp = pbase + r * hstride + 2 + d;
+    const float* w = mm + r * nsplit;
+    const int full4 = nsplit / 4 * 4;
     float O = 0.0f;
-    int sp = 0;
-    for (; sp + 4 <= nsplit; sp += 4) {
-      const float o0 = __ldcg(pp + (sp + 0) * pstride), o1 = __ldcg(pp + (sp + 1) * pstride);
-      const float o2 = __ldcg(pp + (sp + 2) * pstride), o3 = __ldcg(pp + (sp + 3) * pstride);
-      O += o0 * mm[r * nsplit + sp] + o1 * mm[r * nsplit + sp + 1] + o2 * mm[r * nsplit + sp + 2] +
-           o3 * mm[r * nsplit + sp + 3];
+    for (int s0 = 0; s0 < nsplit; s0 += MB) {
+      float o[MB];
+#pragma unroll
+      for (int e = 0; e < MB; ++e) o[e] = s0 + e < nsplit ? __ldcg(pp + (s0 + e) * pstride) : 0.0f;
+#pragma unroll
+      for (int e = 0; e < MB; e += 4) {
+        const int sp = s0 + e;
+        if (sp + 4 <= full4) {
+          O += o[e] * w[sp] + o[e + 1] * w[sp + 1] + o[e + 2] * w[sp + 2] + o[e + 3] * w[sp + 3];
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (sp + q < nsplit) O += o[e + q] * w[sp + q];
+        }
+      }
     }
-    for (; sp < nsplit; ++sp) O += __ldcg(pp + sp * pstride) * mm[r * nsplit + sp];
     const float L = ml[2 * r + 1];
     st_tag(a.att + size_t(kh * n_rep + r) * HD + d, L > 0.0f ? O / L : 0.0f, otag);
   }
