@@ -463,6 +463,9 @@ def repack_q6k_dev(packed_ptr: int, nblocks: int, padded_ptr: int, stream: int =
 
 
 def gemv_dev(w_ptr: int, dtype: int, n: int, k: int, x_ptr: int, m: int, y_ptr: int, stream: int = 0) -> None:
+    """wcb_gemv_dev: y[m][n] = x[m][k] . W[n][k] on device pointers (matmul_transposed,
+    gemm.rs:83-143). W and x 16-byte aligned, k % 256 == 0, n % 4 == 0, 1 <= m <= 4096;
+    m <= 4 runs the dp4a GEMV, 5..32 the batched tensor-core GEMM, larger m the prefill GEMM."""
     _check(lib().wcb_gemv_dev(w_ptr, dtype, n, k, x_ptr, m, y_ptr, stream or None))
 
 
