@@ -118,12 +118,23 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def model_file(preset="tinyllama"):
+    """Path of the synthetic GGUF for ``preset``, written first if missing. The
+    generator runs in a child process, so the timing process never loads the
+    generator's native library (the reference arm loads nothing of this package)."""
+    path = os.path.join(MODEL_DIR, f"wcb_{preset}.gguf")
+    if not os.path.exists(path):
+        code = ("import sys; sys.path.insert(0, %r); from wcb import synth; "
+                "synth.cached_model(%r, %r)" % (PKG, preset, MODEL_DIR))
+        subprocess.run([sys.executable, "-c", code], check=True)
+    return path
+
+
 def ensure_model(rank, world, dist, preset="tinyllama"):
-    from wcb import synth
     path = os.path.join(MODEL_DIR, f"wcb_{preset}.gguf")
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if local == 0:
-        synth.cached_model(preset, MODEL_DIR)
+        model_file(preset)
     if world > 1:
         dist.barrier()
     return path
@@ -242,13 +253,13 @@ def run_reference(args, rank, world):
     reference cannot be built without a Rust toolchain) on this host."""
     if rank != 0:
         return
+    path = model_file("tinyllama")
     import oracle
-    from wcb import synth
-    path = synth.cached_model("tinyllama", MODEL_DIR)
     cores = os.cpu_count() or 1
     oracle.set_threads(cores, cores)
     o = oracle.OracleModel(path)
-    prompt = synth.random_prompt(PROMPT_LEN, o.vocab, seed=1).tolist()
+    # the prompt of our arm (wcb.synth.random_prompt), drawn here with numpy alone
+    prompt = np.random.default_rng(1).integers(3, o.vocab, size=PROMPT_LEN, dtype=np.int64).tolist()
     logits = o.forward(prompt, 0)  # untimed prefill
     oracle.set_threads(cores, 1)  # the reference's threading for the timed decode steps
     oracle.set_faithful(True)  # and its one-row-at-a-time matmul loop

@@ -37,15 +37,24 @@ enum {
   WCB_ERR_IO = 7
 };
 
-/* GGUF tensor types accepted for 2-D weights */
-enum { WCB_DTYPE_F32 = 0, WCB_DTYPE_Q4_K = 12, WCB_DTYPE_Q6_K = 14 };
+/* GGUF tensor types of 2-D weights (gguf.rs:446-467; the raw blocks are
+ * uploaded unchanged). wcb_gemv_dev takes the two quantised types only. */
+enum { WCB_DTYPE_F32 = 0, WCB_DTYPE_F16 = 1, WCB_DTYPE_Q4_K = 12, WCB_DTYPE_Q6_K = 14 };
 
 /* KV cache element type */
 enum { WCB_KV_F32 = 0, WCB_KV_F16 = 1 };
 
 /* Load options (no counterpart in the reference, whose Model::new takes only a
- * TransformerConfig: model.rs:188). Zero-initialised options are valid. */
+ * TransformerConfig: model.rs:188). Fill them with wcb_load_opts_init, which
+ * writes the defaults and struct_size = sizeof(wcb_load_opts), then change the
+ * fields you need. The library reads only the first struct_size bytes, so a
+ * caller compiled against an older, shorter version of this struct keeps
+ * working when fields are appended; fields beyond struct_size take their
+ * defaults. struct_size must be at least WCB_LOAD_OPTS_V1_SIZE (the fields up to
+ * and including tp_id). A NULL options pointer means all defaults. Layout: every
+ * field is 4-byte aligned, no padding (see wcb_struct_layout). */
 typedef struct wcb_load_opts {
+  uint32_t struct_size; /* bytes of this struct the caller initialised */
   int32_t device;     /* CUDA device ordinal */
   uint32_t max_seq;   /* KV capacity in tokens; 0 = GGUF context_length (kv_cache.rs:48-53) */
   uint32_t kv_dtype;  /* WCB_KV_F32 (reference numerics) or WCB_KV_F16 */
@@ -69,7 +78,25 @@ typedef struct wcb_load_opts {
   uint32_t tp_rank;
   uint32_t tp_size;
   uint8_t tp_id[128];
+  /* Bound, in milliseconds, of every device-side wait on another rank's or
+     another CTA's data (tensor-parallel partial sums, the decode step's tagged
+     activations). A wait that runs out makes the call fail with
+     WCB_ERR_BACKEND_UNSUPPORTED instead of hanging. 0 = 2000 ms; at most 60000. */
+  uint32_t wait_ms;
 } wcb_load_opts;
+
+/* Bytes of the fields every caller must initialise (struct_size .. tp_id). */
+#define WCB_LOAD_OPTS_V1_SIZE 160u
+
+/* Defaults: device 0, max_seq = context_length, f32 KV cache, max_batch 1,
+ * flags 0, one rank, wait_ms 2000; struct_size = sizeof(wcb_load_opts). */
+void wcb_load_opts_init(wcb_load_opts* opts);
+
+/* Size (field == NULL) or byte offset of a field of a struct of this header:
+ * "wcb_load_opts", "wcb_gen_config" or "wcb_model_config". SIZE_MAX for an
+ * unknown struct or field. A binding generated by hand (ctypes, Rust repr(C))
+ * checks its own layout against these once at start-up. */
+size_t wcb_struct_layout(const char* struct_name, const char* field);
 
 /* TransformerConfig — transformer/config.rs:6-41 (plus head_dim) */
 typedef struct wcb_model_config {

@@ -136,3 +136,55 @@ def test_host_sampler_nan_is_generic_failure():
     with pytest.raises(wcb.WcbError) as e:
         s.sample(np.array([0.0, np.nan], np.float32))
     assert e.value.code == 1
+
+
+def test_struct_layouts_match_the_library():
+    # every ctypes mirror has the library's size and field offsets
+    wcb.check_layouts()
+    L = wcb.lib()
+    assert L.wcb_struct_layout(b"wcb_load_opts", b"tp_id") + 128 == 160  # WCB_LOAD_OPTS_V1_SIZE
+    assert L.wcb_struct_layout(b"wcb_load_opts", b"wait_ms") == 160
+    assert L.wcb_struct_layout(b"wcb_load_opts", b"no_such_field") == C.c_size_t(-1).value
+    assert L.wcb_struct_layout(b"no_such_struct", None) == C.c_size_t(-1).value
+
+
+def test_load_opts_init_and_struct_size_checks():
+    L = wcb.lib()
+    o = wcb._LoadOpts()
+    L.wcb_load_opts_init(C.byref(o))
+    assert (o.struct_size, o.max_batch, o.tp_size, o.wait_ms, o.device) == (C.sizeof(wcb._LoadOpts), 1, 1, 2000, 0)
+    h = C.c_uint32(0)
+    # a zero struct_size (options never initialised) is refused before any file or GPU access
+    z = wcb._LoadOpts()
+    assert L.wcb_model_load(b"/nonexistent/x.gguf", C.byref(z), C.byref(h)) == 3
+    assert "struct_size" in wcb.last_error()
+    # an older caller's shorter struct (no wait_ms) is accepted: the next failure is the missing file
+    o.struct_size = 160
+    o.wait_ms = 0xDEAD  # past struct_size: never read
+    assert L.wcb_model_load(b"/nonexistent/x.gguf", C.byref(o), C.byref(h)) == 7
+    o.struct_size = C.sizeof(wcb._LoadOpts)
+    o.wait_ms = 60001
+    assert L.wcb_model_load(b"/nonexistent/x.gguf", C.byref(o), C.byref(h)) == 3
+    assert "wait_ms" in wcb.last_error()
+
+
+@pytest.mark.parametrize("entry", ["wcb_attention_dev", "wcb_attention_dev_noalloc"])
+def test_attention_argument_errors_without_touching_the_gpu(entry):
+    # both attention entry points validate pointers, alignment and shapes on the host
+    # before any CUDA call; the addresses below are never dereferenced
+    f = getattr(wcb.lib(), entry)
+    base = 1 << 20
+    ok = dict(q=base, k=base + 4096, v=base + 8192, out=base + 12288)
+    cases = [
+        dict(ok, q=0),
+        dict(ok, q=base + 4),          # q off a 16-byte boundary
+        dict(ok, k=base + 4096 + 8),   # K cache
+        dict(ok, v=base + 8192 + 12),  # V cache
+        dict(ok, out=base + 12288 + 4),
+    ]
+    for c in cases:
+        assert f(c["q"], c["k"], c["v"], c["out"], 1, 8, 2, 64, 128, 16, 15, None) == 3, c
+    assert "aligned" in wcb.last_error() or "null" in wcb.last_error()
+    # shape errors: head_dim 96, kv_len > max_seq, n_heads not a multiple of n_kv_heads
+    for args in [(1, 8, 2, 96, 128, 16, 15), (1, 8, 2, 64, 128, 129, 128), (1, 6, 4, 64, 128, 16, 15)]:
+        assert f(ok["q"], ok["k"], ok["v"], ok["out"], *args, None) == 3, args

@@ -4,7 +4,9 @@
 // read by wcb_last_error; no C++ exception crosses the boundary.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
+#include <cstddef>
 #include <cstdint>
 #include <cstring>
 #include <map>
@@ -14,6 +16,7 @@
 #include <string>
 
 #include "../../include/wcb.h"
+#include "attn_host.h"
 #include "gguf.h"
 #include "kernels.h"
 #include "model.h"
@@ -180,23 +183,74 @@ void wcb_gen_config_default(wcb_gen_config* c) {
   c->eos_id = 2;
 }
 
+static_assert(offsetof(wcb_load_opts, wait_ms) == WCB_LOAD_OPTS_V1_SIZE, "v1 fields end where wait_ms starts");
+static_assert(sizeof(wcb_load_opts) == WCB_LOAD_OPTS_V1_SIZE + 4, "wcb_load_opts has no padding");
+
+void wcb_load_opts_init(wcb_load_opts* o) {
+  if (!o) return;
+  std::memset(o, 0, sizeof(*o));
+  o->struct_size = uint32_t(sizeof(wcb_load_opts));
+  o->kv_dtype = WCB_KV_F32;
+  o->max_batch = 1;
+  o->tp_size = 1;
+  o->wait_ms = 2000;
+}
+
+size_t wcb_struct_layout(const char* s, const char* f) {
+  if (!s) return SIZE_MAX;
+  const std::string st(s), fl(f ? f : "");
+#define WCB_FIELD(T, F) \
+  if (fl == #F) return offsetof(T, F);
+  if (st == "wcb_load_opts") {
+    if (!f) return sizeof(wcb_load_opts);
+    WCB_FIELD(wcb_load_opts, struct_size) WCB_FIELD(wcb_load_opts, device) WCB_FIELD(wcb_load_opts, max_seq)
+    WCB_FIELD(wcb_load_opts, kv_dtype) WCB_FIELD(wcb_load_opts, max_batch) WCB_FIELD(wcb_load_opts, flags)
+    WCB_FIELD(wcb_load_opts, tp_rank) WCB_FIELD(wcb_load_opts, tp_size) WCB_FIELD(wcb_load_opts, tp_id)
+    WCB_FIELD(wcb_load_opts, wait_ms)
+  } else if (st == "wcb_gen_config") {
+    if (!f) return sizeof(wcb_gen_config);
+    WCB_FIELD(wcb_gen_config, max_tokens) WCB_FIELD(wcb_gen_config, temperature) WCB_FIELD(wcb_gen_config, top_p)
+    WCB_FIELD(wcb_gen_config, top_k) WCB_FIELD(wcb_gen_config, repetition_penalty) WCB_FIELD(wcb_gen_config, seed)
+    WCB_FIELD(wcb_gen_config, eos_id)
+  } else if (st == "wcb_model_config") {
+    if (!f) return sizeof(wcb_model_config);
+    WCB_FIELD(wcb_model_config, vocab_size) WCB_FIELD(wcb_model_config, hidden_size)
+    WCB_FIELD(wcb_model_config, num_layers) WCB_FIELD(wcb_model_config, num_heads)
+    WCB_FIELD(wcb_model_config, num_kv_heads) WCB_FIELD(wcb_model_config, intermediate_size)
+    WCB_FIELD(wcb_model_config, max_seq_len) WCB_FIELD(wcb_model_config, head_dim)
+    WCB_FIELD(wcb_model_config, rms_norm_eps) WCB_FIELD(wcb_model_config, rope_theta)
+  }
+#undef WCB_FIELD
+  return SIZE_MAX;
+}
+
 uint32_t wcb_model_load(const char* path, const wcb_load_opts* opts, uint32_t* out_handle) {
   return guarded([&]() -> uint32_t {
     if (!path || !out_handle) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
     *out_handle = 0;
     wcb::LoadOptions o;
     if (opts) {
-      o.device = opts->device;
-      o.max_seq = opts->max_seq;
-      if (opts->kv_dtype > WCB_KV_F16) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: kv_dtype");
-      o.kv_half = opts->kv_dtype == WCB_KV_F16;
-      o.max_batch = opts->max_batch ? opts->max_batch : 1;
-      o.flags = opts->flags;
-      o.tp_rank = opts->tp_rank;
-      o.tp_size = opts->tp_size ? opts->tp_size : 1;
+      // read only the bytes the caller initialised; later fields keep their defaults
+      if (opts->struct_size < WCB_LOAD_OPTS_V1_SIZE)
+        return fail(WCB_ERR_INVALID_ARGUMENT,
+                    "Invalid argument: wcb_load_opts.struct_size is " + std::to_string(opts->struct_size) +
+                        " (initialise the options with wcb_load_opts_init)");
+      wcb_load_opts v;
+      wcb_load_opts_init(&v);
+      std::memcpy(&v, opts, std::min<size_t>(opts->struct_size, sizeof(v)));
+      o.device = v.device;
+      o.max_seq = v.max_seq;
+      if (v.kv_dtype > WCB_KV_F16) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: kv_dtype");
+      o.kv_half = v.kv_dtype == WCB_KV_F16;
+      o.max_batch = v.max_batch ? v.max_batch : 1;
+      o.flags = v.flags;
+      o.tp_rank = v.tp_rank;
+      o.tp_size = v.tp_size ? v.tp_size : 1;
       if (o.tp_size > 8 || o.tp_rank >= o.tp_size)
         return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: tp_rank / tp_size");
-      std::memcpy(o.tp_id, opts->tp_id, sizeof(o.tp_id));
+      std::memcpy(o.tp_id, v.tp_id, sizeof(o.tp_id));
+      if (v.wait_ms > 60000) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: wait_ms > 60000");
+      o.wait_ms = v.wait_ms ? v.wait_ms : 2000;
     }
     auto m = std::make_shared<wcb::Model>(path, o);
     std::lock_guard<std::mutex> lk(g_mu);
@@ -504,25 +558,16 @@ uint32_t wcb_gemv_dev(const void* w, uint32_t dtype, size_t n, size_t k, const f
 
 }  // extern "C"
 
-namespace {
-// Scratch of wcb_attention_dev (StepState, split tickets, split partials),
-// allocated once per device with cudaMalloc and grown on demand.
-std::mutex g_attn_mu;
-std::map<int, std::pair<void*, size_t>> g_attn_scratch;
+namespace wcb {
+namespace attn_host {
 
-// Key splits of a single-token call: at most 64 splits of a multiple of 32 keys.
-void attn_split(uint32_t kv_len, int* chunk, int* splits) {
-  int s = int((kv_len + 31) / 32);
-  s = s < 1 ? 1 : (s > 64 ? 64 : s);
-  int c = int((kv_len + uint32_t(s) - 1) / uint32_t(s));
-  c = (c + 31) / 32 * 32;
-  *chunk = c;
-  *splits = int((kv_len + uint32_t(c) - 1) / uint32_t(c));
-}
-
-uint32_t check_attn_args(const float* q, const float* k, const float* v, float* out, uint32_t T, uint32_t nh,
-                         uint32_t nkv, uint32_t hd, uint32_t max_seq, uint32_t kv_len) {
+uint32_t check_args(const float* q, const float* k, const float* v, const float* out, uint32_t T, uint32_t nh,
+                    uint32_t nkv, uint32_t hd, uint32_t max_seq, uint32_t kv_len) {
   if (!q || !k || !v || !out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+  // the kernel reads q and the K / V rows and writes out with 16-byte accesses
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: q, k_cache, v_cache and out must be 16-byte aligned");
   if ((hd != 64 && hd != 128) || nkv == 0 || nh % nkv || nh / nkv > 16 || T == 0 || T > 4096 || kv_len < T ||
       kv_len > max_seq)
     return fail(WCB_ERR_INVALID_ARGUMENT,
@@ -531,9 +576,9 @@ uint32_t check_attn_args(const float* q, const float* k, const float* v, float* 
   return WCB_OK;
 }
 
-wcb::AttnArgs attn_args(const float* q, const float* k, const float* v, float* out, uint32_t T, uint32_t nh,
-                        uint32_t nkv, uint32_t hd, uint32_t max_seq, uint32_t kv_len) {
-  wcb::AttnArgs a{};
+AttnArgs make_args(const float* q, const float* k, const float* v, float* out, uint32_t T, uint32_t nh,
+                   uint32_t nkv, uint32_t hd, uint32_t max_seq, uint32_t kv_len) {
+  AttnArgs a{};
   a.q = q;
   a.kc = k;
   a.vc = v;
@@ -545,8 +590,13 @@ wcb::AttnArgs attn_args(const float* q, const float* k, const float* v, float* o
   a.max_seq = int(max_seq);
   a.T = int(T);
   a.scale = 1.0f / std::sqrt(float(hd));
-  if (T == 1) {
-    attn_split(kv_len, &a.chunk, &a.max_splits);
+  if (T == 1) {  // at most 64 splits of a multiple of 32 keys
+    int sp = int((kv_len + 31) / 32);
+    sp = sp < 1 ? 1 : (sp > 64 ? 64 : sp);
+    int c = int((kv_len + uint32_t(sp) - 1) / uint32_t(sp));
+    c = (c + 31) / 32 * 32;
+    a.chunk = c;
+    a.max_splits = int((kv_len + uint32_t(c) - 1) / uint32_t(c));
   } else {
     a.chunk = int(max_seq);
     a.max_splits = 1;
@@ -554,22 +604,33 @@ wcb::AttnArgs attn_args(const float* q, const float* k, const float* v, float* o
   return a;
 }
 
-// StepState | tickets [T][n_kv] | partials [T==1: n_heads][splits][hd+2]
-size_t attn_scratch_bytes(const wcb::AttnArgs& a) {
-  const size_t tickets = (sizeof(int) * size_t(a.T) * a.n_kv + 255) / 256 * 256;
+size_t ticket_bytes(const AttnArgs& a) { return (sizeof(int) * size_t(a.T) * a.n_kv + 255) / 256 * 256; }
+
+size_t scratch_bytes(const AttnArgs& a) {
   const size_t part = a.T == 1 ? sizeof(float) * size_t(a.n_heads) * a.max_splits * (a.head_dim + 2) : 0;
-  return 256 + tickets + part;
+  return 256 + ticket_bytes(a) + part;
 }
 
-cudaError_t attn_run(wcb::AttnArgs a, uint8_t* scratch, uint32_t kv_len, uint32_t position, cudaStream_t s) {
-  wcb::StepState* st = reinterpret_cast<wcb::StepState*>(scratch);
+cudaError_t run(AttnArgs a, uint8_t* scratch, uint32_t kv_len, uint32_t position, cudaStream_t s) {
+  StepState* st = reinterpret_cast<StepState*>(scratch);
   a.ticket = reinterpret_cast<int*>(scratch + 256);
-  a.part = reinterpret_cast<float*>(scratch + 256 + (sizeof(int) * size_t(a.T) * a.n_kv + 255) / 256 * 256);
+  a.part = reinterpret_cast<float*>(scratch + 256 + ticket_bytes(a));
   a.st = st;
-  cudaError_t e = wcb::launch_set_state(st, int(position), int(kv_len - uint32_t(a.T)), a.T, s);
-  if (e == cudaSuccess) e = wcb::launch_attention(a, s);
+  cudaError_t e = launch_set_state(st, int(position), int(kv_len - uint32_t(a.T)), a.T, s);
+  if (e == cudaSuccess) e = launch_attention(a, s);
   return e;
 }
+
+}  // namespace attn_host
+}  // namespace wcb
+
+namespace {
+// Scratch of wcb_attention_dev (StepState, split tickets, split partials),
+// allocated once per device with cudaMalloc and grown on demand, and the
+// devices whose kernel attributes (shared-memory limits) are set.
+std::mutex g_attn_mu;
+std::map<int, std::pair<void*, size_t>> g_attn_scratch;
+std::map<int, bool> g_attn_configured;
 }  // namespace
 
 extern "C" {
@@ -577,17 +638,24 @@ extern "C" {
 uint32_t wcb_attention_dev(const float* q, const float* k_cache, const float* v_cache, float* out, uint32_t n_tokens,
                            uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t max_seq,
                            uint32_t kv_len, uint32_t position, void* stream) {
-  const uint32_t rc = check_attn_args(q, k_cache, v_cache, out, n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
-                                      kv_len);
+  namespace ah = wcb::attn_host;
+  const uint32_t rc = ah::check_args(q, k_cache, v_cache, out, n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
+                                     kv_len);
   if (rc != WCB_OK) return rc;
-  const wcb::AttnArgs a = attn_args(q, k_cache, v_cache, out, n_tokens, n_heads, n_kv_heads, head_dim, max_seq, kv_len);
-  const size_t need = attn_scratch_bytes(a);
+  const wcb::AttnArgs a = ah::make_args(q, k_cache, v_cache, out, n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
+                                        kv_len);
+  const size_t need = ah::scratch_bytes(a);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   uint8_t* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_attn_mu);
+    if (!g_attn_configured[dev]) {  // kernel attributes are per device
+      e = wcb::gemv_configure_all();
+      if (e != cudaSuccess) return cuda_fail(e, "configure");
+      g_attn_configured[dev] = true;
+    }
     auto& slot = g_attn_scratch[dev];
     if (slot.second < need) {
       if (slot.first) {
@@ -603,13 +671,7 @@ uint32_t wcb_attention_dev(const float* q, const float* k_cache, const float* v_
     }
     scratch = static_cast<uint8_t*>(slot.first);
   }
-  static bool configured = false;
-  if (!configured) {
-    e = wcb::gemv_configure_all();
-    if (e != cudaSuccess) return cuda_fail(e, "configure");
-    configured = true;
-  }
-  e = attn_run(a, scratch, kv_len, position, static_cast<cudaStream_t>(stream));
+  e = ah::run(a, scratch, kv_len, position, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? WCB_OK : cuda_fail(e, "attention");
 }
 

@@ -744,6 +744,7 @@ __global__ void tp_reduce_add_kernel(float* dst, const float* resid, const unsig
                                      int phase, StepState* st) {
   if (st->done) return;
   const uint32_t tag = uint32_t(st->epoch) * 512u + uint32_t(phase) + 1u;
+  const unsigned long long limit_ns = 1000000ull * unsigned(st->wait_ms > 0 ? st->wait_ms : 2000);
   for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
     float sum = 0.0f;
     for (int r = 0; r < tp; ++r) {
@@ -758,10 +759,14 @@ __global__ void tp_reduce_add_kernel(float* dst, const float* resid, const unsig
           if (uint32_t(w >> 32) == tag) break;
           unsigned long long t1;
           asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-          if (t1 - t0 > 2000000000ull) {  // 2 s: a rank stopped; report, do not hang
+          // a rank stopped: report it, end this step (later kernels see done and
+          // return at once) and let every other waiting thread give up too
+          if (t1 - t0 > limit_ns) {
             atomicOr(&st->err, 16);
+            st->done = 1;
             break;
           }
+          if (*reinterpret_cast<volatile int*>(&st->err) & 16) break;
         }
       }
       sum = __fadd_rn(sum, __uint_as_float(uint32_t(w)));

@@ -48,7 +48,7 @@ struct StepState {
   int ticket;    // LM-head CTAs finished (the last one runs the sampler bookkeeping)
   int nan;       // a penalised logit was NaN
   int epoch;     // persistent decode step: launches so far (tags of this launch's activations)
-  int pad;
+  int wait_ms;   // bound of the device-side waits on other ranks / CTAs (0: 2000 ms)
 };
 static_assert(sizeof(StepState) == 64, "StepState layout");
 

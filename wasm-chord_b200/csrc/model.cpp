@@ -231,6 +231,10 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     t_max_ = int(std::min<uint32_t>(T_MAX, std::max<uint32_t>(max_seq_, 1)));
     st_ = static_cast<StepState*>(dalloc(sizeof(StepState) * bslots_));
     check(cudaMemset(st_, 0, sizeof(StepState) * bslots_), "clear state");
+    for (uint32_t b = 0; b < bslots_; ++b) {  // bound of the device-side waits (no kernel rewrites it)
+      const int wms = int(opt_.wait_ms ? opt_.wait_ms : 2000);
+      check(cudaMemcpy(&st_[b].wait_ms, &wms, sizeof(int), cudaMemcpyHostToDevice), "wait bound");
+    }
     st_base_ = st_;
     ids_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * std::max<size_t>(max_seq_, 1)));
     hist_cap_ = max_seq_ + 2;
@@ -743,12 +747,15 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
                           stream_),
           "download logits");
   check(cudaStreamSynchronize(stream_), "forward");
-  if (n == 1 && mk_ok_) {
+  {
+    // bounded device waits that expired: 4 / 8 in the persistent decode step, 16 in
+    // the tensor-parallel exchange (a rank stopped sending its partial sums)
     int err = 0;
     check(cudaMemcpy(&err, &st_->err, sizeof(int), cudaMemcpyDeviceToHost), "read state");
-    if (err)
-      throw WcbError(E_BACKEND, "Backend error: decode step kernel: a bounded wait expired (device error word " +
-                                    std::to_string(err) + ")");
+    if (err & 28)
+      throw WcbError(E_BACKEND, std::string("Backend error: ") +
+                                    (err & 16 ? "tensor-parallel exchange" : "decode step kernel") +
+                                    ": a bounded wait expired (device error word " + std::to_string(err) + ")");
   }
   kv_len_ += n;
 }
@@ -1062,12 +1069,14 @@ void Model::sync_session_state() {
   check(cudaMemcpyAsync(&sess_state_, st_, sizeof(StepState), cudaMemcpyDeviceToHost, stream_), "read state");
   check(cudaStreamSynchronize(stream_), "generate");
   kv_len_ = size_t(sess_state_.kv_len);
-  if (sess_state_.err & 12) {
+  if (sess_state_.err & 28) {
     sess_done_ = true;
-    throw WcbError(E_BACKEND, "Backend error: decode step kernel: a bounded wait expired (device error word " +
-                                  std::to_string(sess_state_.err) + ")");
+    throw WcbError(E_BACKEND, std::string("Backend error: ") +
+                                  (sess_state_.err & 16 ? "tensor-parallel exchange" : "decode step kernel") +
+                                  ": a bounded wait expired (device error word " + std::to_string(sess_state_.err) +
+                                  ")");
   }
-  if (sess_state_.err == 1) {
+  if (sess_state_.err & 1) {
     sess_done_ = true;
     throw WcbError(E_GENERIC, "Runtime error: NaN logit");
   }
@@ -1366,10 +1375,10 @@ std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts
             "read states");
       check(cudaStreamSynchronize(stream_), "batched decode");
       for (int b = 0; b < B; ++b) {
-        if (hs[b].err & 12)
+        if (hs[b].err & 28)
           throw WcbError(E_BACKEND, "Backend error: batched decode: a bounded wait expired (device error word " +
                                         std::to_string(hs[b].err) + ")");
-        if (hs[b].err == 1) throw WcbError(E_GENERIC, "Runtime error: NaN logit");
+        if (hs[b].err & 1) throw WcbError(E_GENERIC, "Runtime error: NaN logit");
       }
     };
     read_states();

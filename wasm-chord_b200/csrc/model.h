@@ -37,6 +37,7 @@ struct LoadOptions {
   uint32_t tp_rank = 0;  // tensor parallelism: this process's rank of tp_size
   uint32_t tp_size = 1;
   uint8_t tp_id[128] = {};  // NCCL unique id of the group
+  uint32_t wait_ms = 2000;  // bound of every device-side wait on another rank / CTA
 };
 
 struct GenParams {

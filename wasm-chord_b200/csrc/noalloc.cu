@@ -12,13 +12,13 @@
 // and the output.
 #include <cuda_runtime.h>
 
-#include <cmath>
 #include <cstdint>
 #include <map>
 #include <mutex>
 #include <string>
 
 #include "../../include/wcb.h"
+#include "attn_host.h"
 #include "kernels.h"
 
 namespace {
@@ -75,39 +75,14 @@ extern "C" uint32_t wcb_attention_dev_noalloc(const float* q, const float* k_cac
                                               uint32_t n_tokens, uint32_t n_heads, uint32_t n_kv_heads,
                                               uint32_t head_dim, uint32_t max_seq, uint32_t kv_len, uint32_t position,
                                               void* stream) {
-  if (!q || !k_cache || !v_cache || !out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
-  if ((head_dim != 64 && head_dim != 128) || n_kv_heads == 0 || n_heads % n_kv_heads ||
-      n_heads / n_kv_heads > 16 || n_tokens == 0 || n_tokens > 4096 || kv_len < n_tokens || kv_len > max_seq)
-    return fail(WCB_ERR_INVALID_ARGUMENT,
-                "Invalid tensor shape: need head_dim 64|128, n_heads % n_kv_heads == 0 (<= 16 per kv head), "
-                "1 <= n_tokens <= kv_len <= max_seq");
-  wcb::AttnArgs a{};
-  a.q = q;
-  a.kc = k_cache;
-  a.vc = v_cache;
-  a.kv_half = 0;
-  a.out = out;
-  a.n_heads = int(n_heads);
-  a.n_kv = int(n_kv_heads);
-  a.head_dim = int(head_dim);
-  a.max_seq = int(max_seq);
-  a.T = int(n_tokens);
-  a.scale = 1.0f / std::sqrt(float(head_dim));
-  if (n_tokens == 1) {  // the split rule of wcb_attention_dev: <= 64 splits of a multiple of 32 keys
-    int sp = int((kv_len + 31) / 32);
-    sp = sp < 1 ? 1 : (sp > 64 ? 64 : sp);
-    int ch = int((kv_len + uint32_t(sp) - 1) / uint32_t(sp));
-    ch = (ch + 31) / 32 * 32;
-    a.chunk = ch;
-    a.max_splits = int((kv_len + uint32_t(ch) - 1) / uint32_t(ch));
-  } else {
-    a.chunk = int(max_seq);
-    a.max_splits = 1;
-  }
-  // layout: step state | tickets | partials (same as wcb_attention_dev)
-  const size_t tickets = (sizeof(int) * size_t(a.T) * a.n_kv + 255) / 256 * 256;
-  const size_t part = a.T == 1 ? sizeof(float) * size_t(a.n_heads) * a.max_splits * (a.head_dim + 2) : 0;
-  const size_t need = 256 + tickets + part;
+  namespace ah = wcb::attn_host;
+  // the same checks, split rule and scratch layout as wcb_attention_dev (attn_host.h)
+  const uint32_t rc0 = ah::check_args(q, k_cache, v_cache, out, n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
+                                      kv_len);
+  if (rc0 != WCB_OK) return rc0;
+  const wcb::AttnArgs a = ah::make_args(q, k_cache, v_cache, out, n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
+                                        kv_len);
+  const size_t need = ah::scratch_bytes(a);
   if (need > kScratchBytes)
     return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid tensor shape: this call needs " + std::to_string(need) +
                                               " bytes of scratch, more than the fixed " +
@@ -116,14 +91,9 @@ extern "C" uint32_t wcb_attention_dev_noalloc(const float* q, const float* k_cac
   const uint32_t rc = scratch_for_current_device(&scratch);
   if (rc != WCB_OK) return rc;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  wcb::StepState* st = reinterpret_cast<wcb::StepState*>(scratch);
-  a.ticket = reinterpret_cast<int*>(scratch + 256);
-  a.part = reinterpret_cast<float*>(scratch + 256 + tickets);
-  a.st = st;
   // the array keeps whatever the previous call left: the split tickets must start at zero
-  cudaError_t e = cudaMemsetAsync(a.ticket, 0, tickets, s);
-  if (e == cudaSuccess) e = wcb::launch_set_state(st, int(position), int(kv_len - n_tokens), a.T, s);
-  if (e == cudaSuccess) e = wcb::launch_attention(a, s);
+  cudaError_t e = cudaMemsetAsync(scratch + 256, 0, ah::ticket_bytes(a), s);
+  if (e == cudaSuccess) e = ah::run(a, scratch, kv_len, position, s);
   if (e != cudaSuccess) return fail(WCB_ERR_BACKEND_UNSUPPORTED, std::string("Backend error: attention: ") +
                                                                  cudaGetErrorString(e));
   return WCB_OK;

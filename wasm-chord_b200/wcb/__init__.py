@@ -37,7 +37,12 @@ EXPORTED = [
     "wcb_tokenizer_info", "wcb_tokenizer_set_special", "wcb_tokenize", "wcb_detokenize", "wcb_generate_text",
     "wcb_attention_dev",
     "wcb_attention_dev_noalloc", "wcb_tp_id", "wcb_model_tp_handle", "wcb_model_tp_connect",
+    "wcb_load_opts_init", "wcb_struct_layout",
 ]
+
+# the ctypes mirrors of include/wcb.h's structs, checked against the library's
+# own sizes and offsets by check_layouts()
+STRUCTS = {}
 
 
 class WcbError(RuntimeError):
@@ -48,9 +53,10 @@ class WcbError(RuntimeError):
 
 
 class _LoadOpts(C.Structure):
-    _fields_ = [("device", C.c_int32), ("max_seq", C.c_uint32), ("kv_dtype", C.c_uint32),
-                ("max_batch", C.c_uint32), ("flags", C.c_uint32), ("tp_rank", C.c_uint32),
-                ("tp_size", C.c_uint32), ("tp_id", C.c_uint8 * 128)]
+    _fields_ = [("struct_size", C.c_uint32), ("device", C.c_int32), ("max_seq", C.c_uint32),
+                ("kv_dtype", C.c_uint32), ("max_batch", C.c_uint32), ("flags", C.c_uint32),
+                ("tp_rank", C.c_uint32), ("tp_size", C.c_uint32), ("tp_id", C.c_uint8 * 128),
+                ("wait_ms", C.c_uint32)]
 
 
 class _ModelConfig(C.Structure):
@@ -65,6 +71,8 @@ class _GenConfig(C.Structure):
                 ("top_k", C.c_uint32), ("repetition_penalty", C.c_float), ("seed", C.c_uint64),
                 ("eos_id", C.c_uint32)]
 
+
+STRUCTS.update({"wcb_load_opts": _LoadOpts, "wcb_model_config": _ModelConfig, "wcb_gen_config": _GenConfig})
 
 _LIB = None
 
@@ -133,12 +141,31 @@ def lib() -> C.CDLL:
     L.wcb_tp_id.argtypes = [vp]
     L.wcb_model_tp_handle.argtypes = [u32, vp]
     L.wcb_model_tp_connect.argtypes = [u32, vp, u32]
+    L.wcb_load_opts_init.argtypes = [C.POINTER(_LoadOpts)]
+    L.wcb_load_opts_init.restype = None
+    L.wcb_struct_layout.argtypes = [C.c_char_p, C.c_char_p]
+    L.wcb_struct_layout.restype = sz
     for name in EXPORTED:
         f = getattr(L, name)
         if f.restype is C.c_int and name != "wcb_next_token":  # ctypes default
             f.restype = u32
     _LIB = L
     return L
+
+
+def check_layouts() -> None:
+    """Raises if a ctypes struct of this binding differs in size or field
+    offsets from the library's (wcb_struct_layout)."""
+    L = lib()
+    for name, cls in STRUCTS.items():
+        want = L.wcb_struct_layout(name.encode(), None)
+        if want != C.sizeof(cls):
+            raise RuntimeError(f"{name}: library size {want}, binding size {C.sizeof(cls)}")
+        for fname, _ in cls._fields_:
+            off = L.wcb_struct_layout(name.encode(), fname.encode())
+            if off != getattr(cls, fname).offset:
+                raise RuntimeError(f"{name}.{fname}: library offset {off}, binding offset "
+                                   f"{getattr(cls, fname).offset}")
 
 
 def last_error() -> str:
@@ -215,15 +242,21 @@ class Model:
                        max_batch: int = 1, use_graphs: bool = True, use_pdl: bool = True,
                        use_tensor_cores: bool = True, use_persistent: bool = True, tp_rank: int = 0,
                        tp_size: int = 1, tp_id: bytes = b"", stream_weights: bool = False,
-                       host_sampling: bool = False) -> "Model":
+                       host_sampling: bool = False, wait_ms: int = 0) -> "Model":
         """Loads a GGUF file. tp_size > 1: this process holds tensor-parallel rank
         tp_rank's shard and joins the group named by tp_id (tp_unique_id() on one
         rank, the same bytes on every rank); forward() then fills only this rank's
         vocabulary slice of the logits. stream_weights: the layer weights stay in pinned
-        host memory and stream to the GPU layer by layer (models larger than its memory)."""
+        host memory and stream to the GPU layer by layer (models larger than its memory).
+        wait_ms: bound of the device-side waits on other ranks (0: the library's 2000 ms)."""
         flags = ((0 if use_graphs else 1) | (0 if use_pdl else 2) | (0 if use_tensor_cores else 4)
                  | (0 if use_persistent else 8) | (16 if stream_weights else 0) | (32 if host_sampling else 0))
-        o = _LoadOpts(device, max_seq, kv_dtype, max_batch, flags, tp_rank, tp_size)
+        o = _LoadOpts()
+        lib().wcb_load_opts_init(C.byref(o))
+        o.device, o.max_seq, o.kv_dtype, o.max_batch = device, max_seq, kv_dtype, max_batch
+        o.flags, o.tp_rank, o.tp_size = flags, tp_rank, tp_size
+        if wait_ms:
+            o.wait_ms = wait_ms
         if tp_size > 1:
             if len(tp_id) != 128:
                 raise ValueError("tp_id must be the 128 bytes of tp_unique_id()")
