@@ -50,7 +50,9 @@ def test_noalloc_matches_allocating_entry_on_consecutive_calls(gpu):
 
 
 def test_noalloc_rejects_more_than_its_scratch(gpu):
-    # 128 query heads of 128 dims at 64 splits need 4.26 MB > 4 MiB
+    # 128 query heads of 128 dims at 64 splits need 4.26 MB > 4 MiB; the size is checked
+    # on the host before any device access, so these 16-byte aligned addresses are never read
+    a = 1 << 20
     with pytest.raises(wcb.WcbError) as e:
-        wcb.attention_dev_noalloc(1, 1, 1, 1, 1, 128, 8, 128, 4096, 4096, 4095)
+        wcb.attention_dev_noalloc(a, a + 256, a + 512, a + 768, 1, 128, 8, 128, 4096, 4096, 4095)
     assert e.value.code == 3 and "scratch" in e.value.message
