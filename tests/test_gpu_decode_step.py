@@ -101,3 +101,29 @@ def test_tinyllama_long_context(model_dir, gpu):
     _close(p.forward([123], 1500), q.forward([123], 1500))
     p.close()
     q.close()
+
+
+@pytest.mark.parametrize("kv", [wcb.KV_F32, wcb.KV_F16])
+def test_split_attention_matches_oracle(model_dir, gpu, kv):
+    """A 700-token context: each query head's attention runs as several key
+    splits (2 with an f16 cache, 3 with f32), merged by the O-projection phase;
+    greedy tokens equal the oracle's (f32 cache) and the per-op kernels', and
+    one-token logits agree, also at a position below the KV length."""
+    path = synth.cached_model("tiny", model_dir, context_length=2048)
+    p, q = _pair(path, kv_dtype=kv)
+    prompt = synth.random_prompt(700, 512, seed=36).tolist()
+    cfg = wcb.GenerationConfig(max_tokens=20, temperature=0.0, repetition_penalty=1.1, eos_id=None)
+    got = p.generate_tokens(prompt, cfg)
+    assert got == q.generate_tokens(prompt, cfg)
+    assert p.launches_per_step() == 1
+    if kv == wcb.KV_F32:
+        o = oracle.OracleModel(path)
+        assert got == o.generate(prompt, 20, repetition_penalty=1.1, eos_id=None)
+    for m in (p, q):
+        m.clear_kv_cache()
+        m.forward(prompt, 0)
+    for i, t in enumerate([17, 300]):
+        _close(p.forward([t], 700 + i), q.forward([t], 700 + i))
+    _close(p.forward([9], 250), q.forward([9], 250))
+    p.close()
+    q.close()

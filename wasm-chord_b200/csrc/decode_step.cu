@@ -19,9 +19,13 @@
 // products of the tiles and the fused epilogues (RoPE + KV append, residual
 // add, SwiGLU, LM-head penalty + argmax) independently of one another.
 //
-// Attention runs on the first n_kv * splits CTAs: split-K over the keys, the
-// earlier steps' keys staged before this step's q / k / v are polled, merged
-// by the last CTA of each KV head (ticket).
+// Attention runs on the first n_heads * S CTAs, one per (query head, key
+// split): each reads its keys' K / V rows straight from the cache into
+// registers (issued before this step's q is polled), keeps a running softmax
+// per warp, merges the warps in shared memory and writes its normalised
+// partial output with the split's (max, sum). The O-projection phase merges
+// the S splits of a head while it builds its input, so no CTA waits for a
+// ticket or re-reads partials.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -40,10 +44,18 @@ constexpr int MK_W = 15;            // consumer warps per CTA
 constexpr int MK_T = MK_W * 32;     // consumer threads per CTA
 constexpr int MK_THREADS = MK_T + 32;  // + the producer warp (16 warps: 128 registers a thread)
 constexpr int MK_MAX_K = 16384;     // longest GEMV input (limb planes in shared memory)
-constexpr int MK_TS = 32;           // keys per attention tile
 constexpr int MK_MAX_TILES = 2048;  // tiles of one CTA per step (list kept in shared memory)
 constexpr int MK_GPT = 32;          // most groups in one tile
-constexpr long long MK_WAIT_NS = 2000000000ll;  // bound of every spin wait (2 s)
+constexpr int MK_ANB = 8;          // attention: cache rows per lane in flight (K and V each)
+constexpr int MK_ASMAX = 4;        // most key splits of one query head
+
+// Key splits of one query head: as few as hold every row in flight at once
+// (MK_W warps x MK_ANB loads of 512 bytes), at most smax; never an empty split.
+__host__ __device__ __forceinline__ int att_splits(int nkeys, int head_dim, int kv_half, int smax) {
+  const int cap = MK_W * MK_ANB * (512 / (head_dim * (kv_half ? 2 : 4)));
+  const int sp = (nkeys + cap - 1) / cap;
+  return sp < 1 ? 1 : (sp > smax ? smax : sp);
+}
 constexpr uint32_t MK_MBAR_POLLS = 1u << 21;  // ~1 us suspends: about 2 s in all
 
 // barrier of the consumer warps (the producer warp never joins it)
@@ -73,7 +85,8 @@ __device__ __forceinline__ float val_of(unsigned long long w) { return __uint_as
 // Reads N (even; 16-byte aligned start) tagged values, spinning until every
 // one carries `tag`; false when the bound expires. skip: read once, no wait.
 template <int N>
-__device__ __forceinline__ bool poll_tagged(const unsigned long long* p, uint32_t tag, float (&out)[N], bool skip) {
+__device__ __forceinline__ bool poll_tagged(const unsigned long long* p, uint32_t tag, float (&out)[N], bool skip,
+                                            unsigned long long limit_ns) {
   unsigned long long w[N];
 #pragma unroll
   for (int i = 0; i < N; i += 2) ld_tag2(p + i, w[i], w[i + 1]);
@@ -89,26 +102,12 @@ __device__ __forceinline__ bool poll_tagged(const unsigned long long* p, uint32_
       ok = true;
 #pragma unroll
       for (int i = 0; i < N; ++i) ok &= tag_of(w[i]) == tag;
-      if (ok || gtime() - t0 > MK_WAIT_NS) break;
+      if (ok || gtime() - t0 > limit_ns) break;
     }
   }
 #pragma unroll
   for (int i = 0; i < N; ++i) out[i] = val_of(w[i]);
   return ok || skip;
-}
-
-template <typename KT>
-__device__ __forceinline__ float4 ldcg_kv4(const KT* p);
-template <>
-__device__ __forceinline__ float4 ldcg_kv4<float>(const float* p) {
-  return __ldcg(reinterpret_cast<const float4*>(p));
-}
-template <>
-__device__ __forceinline__ float4 ldcg_kv4<__half>(const __half* p) {
-  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
-  const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-  const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-  return make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
 // Bounded wait for one phase of an mbarrier. Each try_wait suspends the
@@ -482,6 +481,8 @@ struct Ctx {
   float rm;  // 1 / RMSNorm divisor of the current phase's input (1 without norm)
   unsigned long long best;
   int nan;
+  int S;                         // key splits of each query head's attention (att_splits)
+  unsigned long long wait_ns;    // bound of every spin wait on another CTA's data
 };
 
 __device__ __forceinline__ float pick4(const float (&v)[ROWS], int i) {
@@ -573,6 +574,33 @@ __device__ __forceinline__ void group_epilogue(const MkArgs& a, const MkPart& P,
   }
 }
 
+// The O phase's inputs k .. k + 7 (one head h = k / head_dim) from S > 1 key
+// splits: sum_s e^(m_s - M) l_s o_s / sum_s e^(m_s - M) l_s with M = max m_s,
+// o_s the split's normalised output.
+__device__ __forceinline__ bool poll_att_merged(const MkArgs& a, int k, int S, uint32_t tag, float (&v)[8], bool skip,
+                                                unsigned long long limit_ns) {
+  const int h = k / a.head_dim;
+  bool ok = true;
+  float M = -INFINITY, L = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+  for (int s = 0; s < S; ++s) {
+    float o[8], ml[2];
+    ok &= poll_tagged<2>(a.attml + (size_t(s) * a.n_heads + h) * 2, tag, ml, skip, limit_ns);
+    ok &= poll_tagged<8>(a.att + size_t(s) * a.hidden + k, tag, o, skip, limit_ns);
+    const float mn = fmaxf(M, ml[0]);
+    const float c0 = M == -INFINITY ? 0.0f : expf(M - mn), c1 = expf(ml[0] - mn) * ml[1];
+    L = L * c0 + c1;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = v[e] * c0 + o[e] * c1;
+    M = mn;
+  }
+  const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] *= inv;
+  return ok;
+}
+
 // Input planes of the phase starting at part pi (R rounds of MK_T * 8 values).
 // With P.norm the planes hold x * w and each warp leaves its share of sum(x^2)
 // in red[]: candle's rms_norm (candle_tensor_backend.rs:30-57), x / m * w with
@@ -650,8 +678,10 @@ __device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx&
         const float4 x1 = __ldg(reinterpret_cast<const float4*>(plain + k + 4));
         v[r][0] = x0.x; v[r][1] = x0.y; v[r][2] = x0.z; v[r][3] = x0.w;
         v[r][4] = x1.x; v[r][5] = x1.y; v[r][6] = x1.z; v[r][7] = x1.w;
+      } else if (P.kind == MK_O && c.S > 1) {
+        ok &= poll_att_merged(a, k, c.S, tag, v[r], skip, c.wait_ns);
       } else {
-        ok &= poll_tagged<8>(src + k, tag, v[r], skip);
+        ok &= poll_tagged<8>(src + k, tag, v[r], skip, c.wait_ns);
       }
       if (stash)
 #pragma unroll
@@ -681,245 +711,215 @@ __device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx&
   return ok;
 }
 
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+// 16 bytes of a cache row as floats: 4 f32 or 8 f16 values
+__device__ __forceinline__ void kv_unpack(const uint4& u, float (&f)[4]) {
+  f[0] = __uint_as_float(u.x);
+  f[1] = __uint_as_float(u.y);
+  f[2] = __uint_as_float(u.z);
+  f[3] = __uint_as_float(u.w);
 }
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void kv_unpack(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
-}
-__device__ __forceinline__ float kv_to_float(float v) { return v; }
-__device__ __forceinline__ float kv_to_float(__half v) { return __half2float(v); }
-template <typename KT>
-__device__ __forceinline__ KT float_to_kv(float v);
-template <>
-__device__ __forceinline__ float float_to_kv<float>(float v) { return v; }
-template <>
-__device__ __forceinline__ __half float_to_kv<__half>(float v) { return __float2half_rn(v); }
 
-// Attention of one (KV head kh, key split) item (T = 1) over the layer's
-// cache, the n_rep query heads of kh together (repeat_kv, attention.rs:
-// 297-322): scores (q.k) * scale with the dot in key order and no contraction,
-// causal limit j <= position, softmax with a running max, P.V
-// (attention.rs:332-435). Keys of earlier steps are copied from the cache into
-// shared memory (cp.async, in the cache's element type) before this step's q
-// and new K / V row are polled. With several splits the last CTA of kh
-// (ticket) merges the partials and writes the tagged output.
+// Attention of one (query head h, key split s of S) item of a decode step over
+// layer `layer`'s cache: keys [j0, j1) of the keys the query at `position`
+// sees (attention.rs:332-435: scores (q.k) * scale, causal limit j <= position,
+// softmax, weighted sum of V; repeat_kv, attention.rs:297-322, reads KV head
+// h / n_rep). Keys written by earlier steps come from the cache, this step's
+// key (slot kv_len) from the tagged copy of the QKV phase. Each lane holds 16
+// bytes of a row, LPK lanes one row; a warp takes every (MK_W * KPL)-th row
+// from row j0 + warp * KPL, MK_ANB rows per lane in flight (the first ones
+// requested before q is polled, the rest prefetched into L2 meanwhile), and
+// keeps a running softmax; the warps are merged in shared memory. The output
+// is this split's normalised partial (S == 1: the attention output) and, with
+// S > 1, the split's maximum and sum for the merge in the O phase.
 template <int HD, typename KT>
-__device__ __forceinline__ void mk_attention(const MkArgs& a, const MkSmem& sm, const MkPart& P, int kh, int split,
-                                             int nsplit, int chunk, int nkeys, const Ctx& c) {
+__device__ __forceinline__ void mk_attention(const MkArgs& a, const MkSmem& sm, int layer, int h, int s, int S,
+                                             int j0, int j1, const Ctx& c, uint32_t qtag, uint32_t otag) {
+  constexpr int EPL = 16 / int(sizeof(KT));  // values per lane of a row
+  constexpr int LPK = HD / EPL;               // lanes per row
+  constexpr int KPL = 32 / LPK;               // rows per warp-wide load
+  constexpr int NB = MK_ANB;                  // rows per lane in flight
+  constexpr int STRIDE = MK_W * KPL;          // rows between a lane's consecutive rows
+  constexpr int RW = HD * int(sizeof(KT)) / 16;  // 16-byte words per row
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_rep = a.n_heads / a.n_kv;
-  constexpr int TS = MK_TS;
-  constexpr int KP = sizeof(KT) == 4 ? HD + 1 : HD + 2;  // K row pitch (elements): odd word stride
-  float* qs = reinterpret_cast<float*>(sm.region);  // [n_rep][HD]
-  float* S = qs + n_rep * HD;                       // [n_rep][TS]
-  float* ml = S + n_rep * TS;                       // [n_rep][2] running (max, sum)
-  float* corr = ml + 2 * n_rep;                     // [n_rep]
-  float* mm = corr + n_rep;                         // [n_rep][nsplit]
-  KT* Ks = reinterpret_cast<KT*>(sm.region + 4 * ((n_rep * HD + n_rep * TS + 3 * n_rep + n_rep * a.max_splits + 3) / 4 * 4));
-  KT* Vs = Ks + TS * KP;                            // [TS][HD], 16-byte aligned rows
-  const size_t lofs = size_t(P.phase / 5) * a.kv_layer_elems + size_t(kh) * a.max_seq * HD;
-  const KT* Kp = reinterpret_cast<const KT*>(a.kcache) + lofs;
-  const KT* Vp = reinterpret_cast<const KT*>(a.vcache) + lofs;
-  const int j0 = split * chunk, j1 = min(j0 + chunk, nkeys);
-  const int old_end = min(c.kv_len, j1);  // keys written by earlier steps
-  constexpr int KW = 4 / sizeof(KT);       // elements per 4-byte K copy
-  constexpr int VW = 16 / sizeof(KT);      // elements per 16-byte V copy
-  auto stage = [&](int t0, int nt) {  // rows [t0, min(t0 + nt, old_end)) of earlier steps
-    const int rows = min(nt, old_end - t0);
-    for (int i = tid; i < rows * (HD / KW); i += MK_T) {
-      const int row = i / (HD / KW), col = (i % (HD / KW)) * KW;
-      cp_async4(Ks + row * KP + col, Kp + size_t(t0 + row) * HD + col);
-    }
-    for (int i = tid; i < rows * (HD / VW); i += MK_T) {
-      const int row = i / (HD / VW), col = (i % (HD / VW)) * VW;
-      cp_async16(Vs + row * HD + col, Vp + size_t(t0 + row) * HD + col);
-    }
-  };
-  const uint32_t tag = c.tag0 + uint32_t(P.dep);
-  // this step's row (slot kv_len) of the tile at t0, from the tagged copies
-  auto stage_new = [&](int t0, int nt) {
-    const int row = c.kv_len - t0;
-    if (row < 0 || row >= nt || c.kv_len >= nkeys) return;
-    for (int d = 2 * tid; d < HD; d += 2 * MK_T) {
-      float kk[2], vv[2];
-      bool ok = poll_tagged<2>(a.knew + kh * HD + d, tag, kk, false);
-      ok &= poll_tagged<2>(a.vnew + kh * HD + d, tag, vv, false);
-      if (!ok) sm.flags[0] = 1;
-      Ks[row * KP + d] = float_to_kv<KT>(kk[0]);
-      Ks[row * KP + d + 1] = float_to_kv<KT>(kk[1]);
-      Vs[row * HD + d] = float_to_kv<KT>(vv[0]);
-      Vs[row * HD + d + 1] = float_to_kv<KT>(vv[1]);
-    }
-  };
-  const int nt0 = min(TS, j1 - j0);
-  stage(j0, nt0);
-  for (int i = 2 * tid; i < n_rep * HD; i += 2 * MK_T) {
-    float qq[2];
-    if (!poll_tagged<2>(a.q + size_t(kh) * n_rep * HD + i, tag, qq, false)) sm.flags[0] = 1;
-    qs[i] = qq[0];
-    qs[i + 1] = qq[1];
-  }
-  stage_new(j0, nt0);
-  for (int r = tid; r < n_rep; r += MK_T) {
-    ml[2 * r] = -INFINITY;
-    ml[2 * r + 1] = 0.0f;
-  }
-  constexpr int MAXI = (16 * HD + MK_T - 1) / MK_T;  // outputs per thread, n_rep <= 16
-  float acc[MAXI];
+  const int sub = lane / LPK, li = lane - sub * LPK;
+  const int kh = h / (a.n_heads / a.n_kv);
+  const size_t lofs = size_t(layer) * a.kv_layer_elems + size_t(kh) * a.max_seq * HD + size_t(li) * EPL;
+  const uint4* Kp = reinterpret_cast<const uint4*>(reinterpret_cast<const KT*>(a.kcache) + lofs);
+  const uint4* Vp = reinterpret_cast<const uint4*>(reinterpret_cast<const KT*>(a.vcache) + lofs);
+  const int old_end = min(j1, c.kv_len);            // rows written by earlier steps
+  const bool has_new = c.kv_len >= j0 && c.kv_len < j1;  // this step's row
+  const bool new_here = has_new && warp == MK_W - 1;     // the warp that takes it
+  const int wb = j0 + warp * KPL;                   // this warp's first row (warp-uniform)
+  float* wm = reinterpret_cast<float*>(sm.region);  // [MK_W] maxima, [MK_W] sums
+  float* wl = wm + MK_W;
+  float* wa = wl + MK_W;                            // [MK_W][HD] outputs
+  float* knew = wa + MK_W * HD;                     // [HD] this step's K row
+  float* vnew = knew + HD;                          // [HD] this step's V row
+  // the first rows of this lane go to registers, the rest into L2, before q is
+  // polled: the rows do not depend on this step. Rows past the end re-read the
+  // last row and are masked out.
+  uint4 kr[NB], vr[NB];
+  const int last = max(old_end - 1, 0);
 #pragma unroll
-  for (int k = 0; k < MAXI; ++k) acc[k] = 0.0f;
-  for (int t0 = j0; t0 < j1; t0 += TS) {
-    const int nt = min(TS, j1 - t0);
-    if (t0 != j0) {
-      cbar();
-      stage(t0, nt);
-      stage_new(t0, nt);
-    }
-    cp_async_wait_all();
-    cbar();
-    for (int r = warp; r < n_rep; r += MK_W) {
-      float sc = -INFINITY;
-      if (lane < nt) {
-        float d = 0.0f;
-        const float* qr = qs + r * HD;
-        const KT* kr = Ks + lane * KP;
-#pragma unroll 8
-        for (int dd = 0; dd < HD; ++dd) d = __fadd_rn(d, __fmul_rn(qr[dd], kv_to_float(kr[dd])));
-        sc = __fmul_rn(d, a.attn_scale);
-      }
-      const float m_old = ml[2 * r];
-      const float m_new = fmaxf(m_old, warp_max(sc));
-      const float pr = lane < nt ? expf(sc - m_new) : 0.0f;
-      const float psum = warp_sum(pr);
-      S[r * TS + lane] = pr;
-      if (lane == 0) {
-        const float cf = expf(m_old - m_new);
-        ml[2 * r] = m_new;
-        ml[2 * r + 1] = ml[2 * r + 1] * cf + psum;
-        corr[r] = cf;
-      }
-    }
-    cbar();
+  for (int e = 0; e < NB; ++e) {
+    const size_t jj = size_t(min(wb + sub + e * STRIDE, last));
+    kr[e] = __ldcg(Kp + jj * RW);
+    vr[e] = __ldcg(Vp + jj * RW);
+  }
+  for (int jj = wb + sub + NB * STRIDE; jj < old_end; jj += STRIDE) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(Kp + size_t(jj) * RW));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(Vp + size_t(jj) * RW));
+  }
+  float q[EPL];
+  if (!poll_tagged<EPL>(a.q + size_t(h) * HD + size_t(li) * EPL, qtag, q, false, c.wait_ns)) {
+    sm.flags[0] = 1;
+    atomicOr(&a.st->err, 8);
+  }
+  if (new_here && sub == 0) {  // this step's K and V rows, from the tagged copies of the QKV phase
+    bool ok;
+    {
+      float f[EPL];
+      ok = poll_tagged<EPL>(a.knew + size_t(kh) * HD + size_t(li) * EPL, qtag, f, false, c.wait_ns);
 #pragma unroll
-    for (int k = 0; k < MAXI; ++k) {
-      const int idx = tid + k * MK_T;
-      if (idx < n_rep * HD) {
-        const int r = idx / HD, d = idx % HD;
-        float s2 = acc[k] * corr[r];
-        for (int jj = 0; jj < nt; ++jj) s2 += S[r * TS + jj] * kv_to_float(Vs[jj * HD + d]);
-        acc[k] = s2;
-      }
+      for (int i = 0; i < EPL; ++i) knew[li * EPL + i] = f[i];
+    }
+    {
+      float f[EPL];
+      ok &= poll_tagged<EPL>(a.vnew + size_t(kh) * HD + size_t(li) * EPL, qtag, f, false, c.wait_ns);
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) vnew[li * EPL + i] = f[i];
+    }
+    if (!ok) {
+      sm.flags[0] = 1;
+      atomicOr(&a.st->err, 8);
     }
   }
-  const uint32_t otag = c.tag0 + uint32_t(P.phase);
-  if (nsplit == 1) {
+  __syncwarp();
+  // running softmax of this warp's rows (max m, sum l, weighted V sum acc)
+  float m = -INFINITY, l = 0.0f, acc[EPL];
 #pragma unroll
-    for (int k = 0; k < MAXI; ++k) {
-      const int idx = tid + k * MK_T;
-      if (idx < n_rep * HD) {
-        const int r = idx / HD, d = idx % HD;
-        const float l = ml[2 * r + 1];
-        st_tag(a.att + size_t(kh * n_rep + r) * HD + d, l > 0.0f ? acc[k] / l : 0.0f, otag);
+  for (int i = 0; i < EPL; ++i) acc[i] = 0.0f;
+  for (int b0 = wb; b0 < old_end; b0 += NB * STRIDE) {
+    if (b0 != wb) {
+#pragma unroll
+      for (int e = 0; e < NB; ++e) {
+        const size_t jj = size_t(min(b0 + sub + e * STRIDE, last));
+        kr[e] = __ldcg(Kp + jj * RW);
+        vr[e] = __ldcg(Vp + jj * RW);
       }
     }
-    return;
-  }
-  const size_t pstride = HD + 2;
-  const size_t hstride = size_t(a.max_splits) * pstride;
+    float sc[NB];
+    float mx = m;
 #pragma unroll
-  for (int k = 0; k < MAXI; ++k) {
-    const int idx = tid + k * MK_T;
-    if (idx < n_rep * HD) {
-      const int r = idx / HD, d = idx % HD;
-      float* pp = a.part + size_t(kh * n_rep + r) * hstride + size_t(split) * pstride;
-      pp[2 + d] = acc[k];
-      if (d == 0) {
-        pp[0] = ml[2 * r];
-        pp[1] = ml[2 * r + 1];
+    for (int e = 0; e < NB; ++e) {
+      float kf[EPL];
+      kv_unpack(kr[e], kf);
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) d = fmaf(q[i], kf[i], d);
+#pragma unroll
+      for (int o = 1; o < LPK; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      sc[e] = b0 + sub + e * STRIDE < old_end ? d * a.attn_scale : -INFINITY;
+      mx = fmaxf(mx, sc[e]);
+    }
+    if (mx != -INFINITY) {  // rescale to the new maximum, then add this batch's rows
+      const float cf = expf(m - mx);
+      l *= cf;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) acc[i] *= cf;
+#pragma unroll
+      for (int e = 0; e < NB; ++e) {
+        const float p = sc[e] == -INFINITY ? 0.0f : expf(sc[e] - mx);
+        float vf[EPL];
+        kv_unpack(vr[e], vf);
+        l += p;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) acc[i] = fmaf(p, vf[i], acc[i]);
       }
+      m = mx;
+    }
+  }
+  if (new_here) {  // this step's row (first lane group)
+    float d = 0.0f;
+    if (sub == 0) {
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) d = fmaf(q[i], knew[li * EPL + i], d);
+    }
+#pragma unroll
+    for (int o = 1; o < LPK; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    if (sub == 0) {
+      const float sc = d * a.attn_scale, mx = fmaxf(m, sc);
+      const float cf = expf(m - mx), p = expf(sc - mx);
+      l = l * cf + p;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) acc[i] = fmaf(p, vnew[li * EPL + i], acc[i] * cf);
+      m = mx;
+    }
+  }
+  // merge the lane groups of the warp, then the warps
+#pragma unroll
+  for (int o = LPK; o < 32; o <<= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m, o), lo = __shfl_xor_sync(0xffffffffu, l, o);
+    const float mn = fmaxf(m, mo);
+    const float c0 = mn == -INFINITY ? 0.0f : expf(m - mn), c1 = mn == -INFINITY ? 0.0f : expf(mo - mn);
+    l = l * c0 + lo * c1;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) acc[i] = acc[i] * c0 + __shfl_xor_sync(0xffffffffu, acc[i], o) * c1;
+    m = mn;
+  }
+  if (lane < LPK) {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) wa[warp * HD + li * EPL + i] = acc[i];
+    if (lane == 0) {
+      wm[warp] = m;
+      wl[warp] = l;
     }
   }
   cbar();
-  if (tid == 0) {
-    __threadfence();
-    const int prev = atomicAdd(a.ticket + kh, 1);
-    sm.flags[1] = prev == nsplit - 1;
-  }
-  cbar();
-  if (!*reinterpret_cast<volatile int*>(sm.flags + 1)) return;
-  __threadfence();
-  if (tid == 0) a.ticket[kh] = 0;
-  const float* pbase = a.part + size_t(kh) * n_rep * hstride;
-  // the split maxima and sums in one round of loads; the sums go to the K staging
-  // area, which the tiles no longer use
-  float* ls = reinterpret_cast<float*>(Ks);  // [n_rep][nsplit]
-  for (int i = tid; i < n_rep * nsplit; i += MK_T) {
-    const int r = i / nsplit, sp = i % nsplit;
-    mm[r * nsplit + sp] = __ldcg(pbase + r * hstride + sp * pstride);
-    ls[r * nsplit + sp] = __ldcg(pbase + r * hstride + sp * pstride + 1);
-  }
-  cbar();
-  for (int r = warp; r < n_rep; r += MK_W) {
+  for (int d = tid; d < HD; d += MK_T) {
     float M = -INFINITY;
-    for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, mm[r * nsplit + sp]);
-    M = warp_max(M);
-    float L = 0.0f;
-    for (int sp = lane; sp < nsplit; sp += 32) {
-      const float f = expf(mm[r * nsplit + sp] - M);
-      L += ls[r * nsplit + sp] * f;
-      mm[r * nsplit + sp] = f;
+#pragma unroll
+    for (int w = 0; w < MK_W; ++w) M = fmaxf(M, wm[w]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < MK_W; ++w) {
+      const float f = wm[w] == -INFINITY ? 0.0f : expf(wm[w] - M);  // a warp without rows adds nothing
+      L += wl[w] * f;
+      O += wa[w * HD + d] * f;
     }
-    L = warp_sum(L);
-    if (lane == 0) ml[2 * r + 1] = L;
-  }
-  cbar();
-  // weighted sum of the split outputs: the loads of up to 8 splits are issued
-  // together, the additions keep their order (groups of 4, then single splits)
-  constexpr int MB = 8;
-  for (int i = tid; i < n_rep * HD; i += MK_T) {
-    const int r = i / HD, d = i % HD;
-    const float* pp = pbase + r * hstride + 2 + d;
-    const float* w = mm + r * nsplit;
-    const int full4 = nsplit / 4 * 4;
-    float O = 0.0f;
-    for (int s0 = 0; s0 < nsplit; s0 += MB) {
-      float o[MB];
-#pragma unroll
-      for (int e = 0; e < MB; ++e) o[e] = s0 + e < nsplit ? __ldcg(pp + (s0 + e) * pstride) : 0.0f;
-#pragma unroll
-      for (int e = 0; e < MB; e += 4) {
-        const int sp = s0 + e;
-        if (sp + 4 <= full4) {
-          O += o[e] * w[sp] + o[e + 1] * w[sp + 1] + o[e + 2] * w[sp + 2] + o[e + 3] * w[sp + 3];
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (sp + q < nsplit) O += o[e + q] * w[sp + q];
-        }
+    const float out = L > 0.0f ? O / L : 0.0f;
+    if (S == 1) {
+      st_tag(a.att + size_t(h) * HD + d, out, otag);
+    } else {
+      st_tag(a.att + size_t(s) * a.hidden + size_t(h) * HD + d, out, otag);
+      if (d == 0) {
+        st_tag(a.attml + (size_t(s) * a.n_heads + h) * 2, M, otag);
+        st_tag(a.attml + (size_t(s) * a.n_heads + h) * 2 + 1, L, otag);
       }
     }
-    const float L = ml[2 * r + 1];
-    st_tag(a.att + size_t(kh * n_rep + r) * HD + d, L > 0.0f ? O / L : 0.0f, otag);
   }
 }
 
 template <int HD>
 __device__ __forceinline__ void attention_phase(const MkArgs& a, const MkSmem& sm, const MkPart& P, const Ctx& c) {
-  // split rule: at most max_splits pieces of a multiple of 32 keys, so that
-  // n_kv * splits <= grid and every item has a CTA of its own
+  const int S = c.S;
+  if (int(blockIdx.x) >= a.n_heads * S) return;
+  const int h = int(blockIdx.x) / S, s = int(blockIdx.x) - h * S;
   const int nkeys = min(c.kv_len + 1, c.position + 1);
-  int chunk = (nkeys + a.max_splits - 1) / a.max_splits;
-  chunk = max(MK_TS, (chunk + MK_TS - 1) / MK_TS * MK_TS);
-  const int nsplit = (nkeys + chunk - 1) / chunk;
-  const int item = blockIdx.x;
-  if (item >= a.n_kv * nsplit) return;
-  const int kh = item / nsplit, split = item - kh * nsplit;
-  if (a.kv_half) mk_attention<HD, __half>(a, sm, P, kh, split, nsplit, chunk, nkeys, c);
-  else mk_attention<HD, float>(a, sm, P, kh, split, nsplit, chunk, nkeys, c);
+  const int chunk = (nkeys + S - 1) / S;
+  const int j0 = s * chunk, j1 = min(nkeys, j0 + chunk);
+  const uint32_t qtag = c.tag0 + uint32_t(P.dep), otag = c.tag0 + uint32_t(P.phase);
+  if (a.kv_half) mk_attention<HD, __half>(a, sm, P.phase / 5, h, s, S, j0, j1, c, qtag, otag);
+  else mk_attention<HD, float>(a, sm, P.phase / 5, h, s, S, j0, j1, c, qtag, otag);
 }
 
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs a) {
@@ -967,6 +967,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
   c.rm = 1.0f;
   c.best = 0ull;
   c.nan = 0;
+  c.S = att_splits(min(c.kv_len + 1, c.position + 1), a.head_dim, a.kv_half, a.att_smax);
+  c.wait_ns = 1000000ull * unsigned(st->wait_ms > 0 ? st->wait_ms : 2000);
   __syncthreads();
   if (warp == MK_W) {  // ---- producer: refill each slot once the consumer warps have left it
     if (lane != 0) return;
@@ -988,7 +990,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
   for (int pi = 0; pi < a.nparts; ++pi) {
     const MkPart& P = sm.parts[pi];
     if (P.kind == MK_ATT) {
-      cbar();  // the QKV phase is done with the region
+      // the QKV phase is done with the region; a warp whose weight wait expired has
+      // raised the abort flag before this barrier, so every warp takes the same branch
+      // (the attention has barriers of its own)
+      cbar();
+      abort_ = *reinterpret_cast<volatile int*>(sm.flags) != 0;
       if (!abort_) {
         if (a.head_dim == 64) attention_phase<64>(a, sm, P, c);
         else attention_phase<128>(a, sm, P, c);
@@ -1031,7 +1037,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       const int s = k % a.nslots, use = k / a.nslots;
       // every consumer warp waits for every tile and arrives on its slot
       if (!mbar_wait_n(sm.full + s, uint32_t(use & 1), abort_ ? 4096u : MK_MBAR_POLLS)) {
-        if (!abort_ && lane == 0) atomicOr(&st->err, 4);
+        if (!abort_ && lane == 0) {
+          atomicOr(&st->err, 4);
+          sm.flags[0] = 1;
+        }
         abort_ = true;
       }
       const uint32_t sbase = smem_u32(sm.slots + size_t(s) * a.slot_bytes);
@@ -1137,12 +1146,11 @@ bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std
     kmax = std::max(kmax, parts[i].K);
     gmax = std::max(gmax, 4 * size_t(parts[i].K / QK_K) * dev_block_bytes(parts[i].dtype));
   }
-  a.max_splits = std::max(1, grid / a.n_kv);
-  // attention: q, scores, running max / sum, split weights (floats), then K (row pitch
-  // hd + 1 floats or hd + 2 halves) and V tiles in the cache's element type
-  const size_t att_floats = (size_t(n_rep) * a.head_dim + size_t(n_rep) * MK_TS + 3 * size_t(n_rep) +
-                             size_t(n_rep) * a.max_splits + 3) / 4 * 4;
-  const size_t att_bytes = att_floats * sizeof(float) + size_t(MK_TS) * (2 * a.head_dim + 1) * sizeof(float);
+  // attention: one CTA per (query head, key split), at most MK_ASMAX splits
+  a.att_smax = std::min(MK_ASMAX, grid / std::max(1, a.n_heads));
+  if (a.att_smax < 1) return false;
+  // attention's shared memory: the warps' maxima, sums and outputs, this step's K and V rows
+  const size_t att_bytes = sizeof(float) * (size_t(MK_W) * (a.head_dim + 2) + 2 * a.head_dim);
   size_t region = std::max(planes_bytes(kmax), att_bytes);
   region = (region + 127) / 128 * 128;
   const size_t slot = std::max<size_t>(32 * 1024, (gmax + 1023) / 1024 * 1024);

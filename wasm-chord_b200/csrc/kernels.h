@@ -232,13 +232,12 @@ struct MkArgs {
   unsigned long long* q;     // post-RoPE queries [hidden]
   unsigned long long* knew;  // this step's K / V rows [n_kv * head_dim]
   unsigned long long* vnew;
-  unsigned long long* att;   // attention output [hidden]
+  unsigned long long* att;   // attention output [att_smax][hidden]: key split s's normalised partial
+  unsigned long long* attml; // [att_smax][n_heads][2] each split's softmax max and sum (splits > 1)
   unsigned long long* act;   // SwiGLU output [ffn]
   float* logits;             // [vocab]
   const float* zero;         // [hidden] zeros: the embedding of an out-of-vocabulary id
-  float* part;               // attention split partials [n_heads][max_splits][hd + 2]
-  int* ticket;               // [n_kv], zero between launches
-  int max_splits;
+  int att_smax;              // most key splits of a query head (set by decode_step_plan)
   int gen_mode;              // 1: token = hist[nhist - 1], penalty + argmax + bookkeeping
   const uint32_t* ids;       // gen_mode 0: token = ids[0]
   uint32_t* hist;

@@ -914,7 +914,9 @@ void Model::build_decode_step() {
   a.kv_half = int(opt_.kv_half);
   a.attn_scale = attn_scale_;
   const size_t kvd = size_t(c.kv_heads) * c.head_dim();
-  const size_t tagged = 4 * size_t(H) + size_t(F) + 2 * kvd;  // xa, xb, q, att, act, knew, vnew
+  // xa, xb, q, att (one row per key split), the splits' (max, sum), act, knew, vnew
+  const size_t smax = size_t(a.att_smax);
+  const size_t tagged = (3 + smax) * size_t(H) + smax * c.heads * 2 + size_t(F) + 2 * kvd;
   unsigned long long* t = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * tagged));
   check(cudaMemset(t, 0, sizeof(unsigned long long) * tagged), "clear activations");
   mk_tagged_ = t;
@@ -923,17 +925,14 @@ void Model::build_decode_step() {
   a.xb = a.xa + H;
   a.q = a.xb + H;
   a.att = a.q + H;
-  a.act = a.att + H;
+  a.attml = a.att + smax * H;
+  a.act = a.attml + smax * c.heads * 2;
   a.knew = a.act + F;
   a.vnew = a.knew + kvd;
   a.logits = logits_;
   float* zero = static_cast<float*>(dalloc(sizeof(float) * H));
   check(cudaMemset(zero, 0, sizeof(float) * H), "clear zero row");
   a.zero = zero;
-  a.part = static_cast<float*>(
-      dalloc(sizeof(float) * size_t(c.heads) * size_t(a.max_splits) * (c.head_dim() + 2)));
-  a.ticket = static_cast<int*>(dalloc(sizeof(int) * c.kv_heads));
-  check(cudaMemset(a.ticket, 0, sizeof(int) * c.kv_heads), "clear tickets");
   a.ids = ids_;
   a.hist = hist_;
   a.pen_cnt = pen_cnt_;
@@ -1043,8 +1042,6 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   const bool same_graph = graph_rep_ == rep && graph_mode_ == sample_mode_ &&
                           (sample_mode_ == 0 || (graph_t_ == samp_t_ && graph_k_ == samp_k_ && graph_tp_ == samp_tp_));
   if (mk_ok_ && sample_mode_ == 0) {
-    // tickets of a step that ended on an error are cleared here
-    check(cudaMemsetAsync(mk_.ticket, 0, sizeof(int) * size_t(mk_.n_kv), stream_), "clear tickets");
     launches_per_step_ = 1;
   } else if (!(opt_.flags & 1) && !wstream_ && (!decode_exec_ || !same_graph)) {
     if (decode_exec_) {
