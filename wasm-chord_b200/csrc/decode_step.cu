@@ -116,6 +116,15 @@ __device__ __forceinline__ bool poll_tagged(const unsigned long long* p, uint32_
 // the computing ones.
 __device__ __forceinline__ bool mbar_wait_n(uint64_t* bar, uint32_t parity, uint32_t polls) {
   const uint32_t addr = smem_u32(bar);
+  {  // the phase is usually complete already: a non-blocking test first
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
   for (uint32_t it = 0; it < polls; ++it) {
     uint32_t ok;
     asm volatile(
@@ -359,7 +368,7 @@ __device__ __forceinline__ void q6k_unit(const uint32_t (&ra)[ROWS], int b, int 
 //   [parts]  the part list; [tstart] this CTA's first tile of each part
 //   [tiles]  this CTA's tile list (8 bytes a tile)
 //   [rsd]    residual rows of this CTA's o / down share
-//   [rope]   cos, sin of this CTA's q / k rows (current layer)
+//   [rope]   cos, sin of the step's position (head_dim / 2 each)
 //   [pen]    penalty counts of this CTA's LM-head rows
 //   [misc]   red[64] floats, flags[8]
 //   [bars]   full[nslots]
@@ -399,9 +408,9 @@ __host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
   o.rsd = x;
   x += sizeof(float) * size_t(a.res_rows);
   o.rcos = x;
-  x += sizeof(float) * size_t(a.rope_rows);
+  x += sizeof(float) * size_t(a.head_dim / 2);
   o.rsin = x;
-  x += sizeof(float) * size_t(a.rope_rows);
+  x += sizeof(float) * size_t(a.head_dim / 2);
   o.pen = x;
   x += sizeof(uint32_t) * size_t(a.lm_rows);
   o.red = x;
@@ -476,7 +485,6 @@ struct Ctx {
   int position, kv_len;
   const float* x0;  // layer-0 input: the embedding row of the step's token
   int R0;           // first row of this CTA's o / down share (residual stash)
-  int rope_base;    // stash index of the current QKV part's first row
   int g0;           // first group of this CTA in the current part
   float rm;  // 1 / RMSNorm divisor of the current phase's input (1 without norm)
   unsigned long long best;
@@ -506,7 +514,8 @@ __device__ __forceinline__ void group_epilogue(const MkArgs& a, const MkPart& P,
     if (vr < hid + kvd) {
       if ((i & 1) == 0) {  // RoPE on (2j, 2j+1) pairs (attention.rs:230-262), table values
         const float x0 = vi, x1 = pick4(v, i + 1);
-        const float cs = sm.rcos[c.rope_base + gi + i], sn = sm.rsin[c.rope_base + gi + i];
+        const int pi2 = ((vr < hid ? vr : vr - hid) % hd) >> 1;  // rotation pair of the row
+        const float cs = sm.rcos[pi2], sn = sm.rsin[pi2];
         const float n0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
         const float n1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
         if (vr < hid) {
@@ -615,31 +624,9 @@ __device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx&
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = P.K;
   const Planes pl = planes_at(smem_u32(sm.region), K);
-  // staged epilogue inputs that do not depend on this phase's input
-  if (P.kind == MK_QKV) {
-    const int hid = a.hidden, hd = a.head_dim, kvd = a.n_kv * a.head_dim;
-    int base = 0;
-    for (int qi = pi; qi < a.nparts; ++qi) {
-      const MkPart* Q = sm.parts + qi;
-      if (Q->phase != P.phase) break;
-      int g0, g1;
-      cta_share(Q->ngroups, blockIdx.x, gridDim.x, g0, g1);
-      const int n = ROWS * (g1 - g0), ro = Q->row_offset + ROWS * g0;
-      for (int r = tid; r < n; r += MK_T) {
-        const int vr = ro + r;
-        float cs = 0.0f, sn = 0.0f;
-        if (vr < hid + kvd) {
-          const int col = vr < hid ? vr : vr - hid;
-          const size_t ti = size_t(c.position) * (hd / 2) + ((col % hd) >> 1);
-          cs = __ldg(a.rope_cos + ti);
-          sn = __ldg(a.rope_sin + ti);
-        }
-        sm.rcos[base + r] = cs;
-        sm.rsin[base + r] = sn;
-      }
-      base += n;
-    }
-  } else if (P.kind == MK_LM) {
+  // staged epilogue inputs that do not depend on this phase's input (the RoPE
+  // table of the step's position is staged once per launch)
+  if (P.kind == MK_LM) {
     int g0, g1;
     cta_share(P.ngroups, blockIdx.x, gridDim.x, g0, g1);
     for (int r = tid; r < ROWS * (g1 - g0); r += MK_T) sm.pen[r] = __ldg(a.pen_cnt + ROWS * g0 + r);
@@ -909,7 +896,7 @@ __device__ __forceinline__ void mk_attention(const MkArgs& a, const MkSmem& sm, 
   }
 }
 
-template <int HD>
+template <int HD, typename KT>
 __device__ __forceinline__ void attention_phase(const MkArgs& a, const MkSmem& sm, const MkPart& P, const Ctx& c) {
   const int S = c.S;
   if (int(blockIdx.x) >= a.n_heads * S) return;
@@ -918,10 +905,12 @@ __device__ __forceinline__ void attention_phase(const MkArgs& a, const MkSmem& s
   const int chunk = (nkeys + S - 1) / S;
   const int j0 = s * chunk, j1 = min(nkeys, j0 + chunk);
   const uint32_t qtag = c.tag0 + uint32_t(P.dep), otag = c.tag0 + uint32_t(P.phase);
-  if (a.kv_half) mk_attention<HD, __half>(a, sm, P.phase / 5, h, s, S, j0, j1, c, qtag, otag);
-  else mk_attention<HD, float>(a, sm, P.phase / 5, h, s, S, j0, j1, c, qtag, otag);
+  mk_attention<HD, KT>(a, sm, P.phase / 5, h, s, S, j0, j1, c, qtag, otag);
 }
 
+// One instantiation per (head_dim, KV cache type, Q6_K weights present), so a
+// kernel carries only the code its model runs.
+template <int HD, typename KT, bool Q6>
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const MkSmem sm = mk_carve(a, smem);
@@ -951,6 +940,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       sm.tstart[i] = a.tile_start[size_t(cta) * (a.nparts + 1) + i];
   }
   if (tid < 8) sm.flags[tid] = 0;
+  for (int i = tid; i < a.head_dim / 2; i += MK_THREADS) {  // cos / sin of this step's position (attention.rs:230-248)
+    sm.rcos[i] = __ldg(a.rope_cos + size_t(st->position) * (a.head_dim / 2) + i);
+    sm.rsin[i] = __ldg(a.rope_sin + size_t(st->position) * (a.head_dim / 2) + i);
+  }
   Ctx c;
   c.tag0 = uint32_t(st->epoch) * 1024u + 1u;
   c.position = st->position;
@@ -962,7 +955,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
     cta_share(a.hidden / ROWS, cta, gridDim.x, g0, g1);
     c.R0 = ROWS * g0;
   }
-  c.rope_base = 0;
   c.g0 = 0;
   c.rm = 1.0f;
   c.best = 0ull;
@@ -996,8 +988,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       cbar();
       abort_ = *reinterpret_cast<volatile int*>(sm.flags) != 0;
       if (!abort_) {
-        if (a.head_dim == 64) attention_phase<64>(a, sm, P, c);
-        else attention_phase<128>(a, sm, P, c);
+        attention_phase<HD, KT>(a, sm, P, c);
       }
       continue;
     }
@@ -1006,8 +997,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
     c.g0 = g0;
     if (P.first) {
       cbar();  // the previous phase is done with the region and the stashes
-      c.rope_base = 0;
-      bool ok;
+          bool ok;
       const int rounds = (P.K + MK_T * 8 - 1) / (MK_T * 8);
       if (rounds <= 1) ok = build_input<1>(a, pi, P, c, sm, abort_);
       else if (rounds == 2) ok = build_input<2>(a, pi, P, c, sm, abort_);
@@ -1054,7 +1044,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
             const int ro = P.kind == MK_GU ? (i < 2 ? 2 * u + i : 2 * T.ng + 2 * u + (i - 2)) : ROWS * u + i;
             ra[i] = sbase + uint32_t(ro) * row_bytes;
           }
-          if (P.dtype == DT_Q4K)
+          if (!Q6 || P.dtype == DT_Q4K)
             for (int b = lane & 7; b < NB; b += 8) q4k_unit(ra, b, lane >> 3, pl, acc);
           else
             for (int b = lane & 7; b < NB; b += 8) q6k_unit(ra, b, lane >> 3, pl, acc);
@@ -1072,7 +1062,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       __syncwarp();
       if (lane == 0) mbar_arrive(sm.empty + s);
     }
-    if (P.kind == MK_QKV) c.rope_base += ROWS * (g1 - g0);
     if (P.kind != MK_LM) continue;
     // LM head: CTA max of the argmax keys, one atomic per CTA; the last CTA to
     // finish runs the sampler bookkeeping and advances the epoch
@@ -1111,6 +1100,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
 int g_mk_sms = 0;
 size_t g_mk_smem_max = 0;
 
+using StepKernel = void (*)(MkArgs);
+StepKernel step_kernel(int head_dim, int kv_half, int has_q6) {
+  const int i = (head_dim == 128 ? 4 : 0) + (kv_half ? 2 : 0) + (has_q6 ? 1 : 0);
+  static const StepKernel k[8] = {
+      decode_step_kernel<64, float, false>,  decode_step_kernel<64, float, true>,
+      decode_step_kernel<64, __half, false>, decode_step_kernel<64, __half, true>,
+      decode_step_kernel<128, float, false>, decode_step_kernel<128, float, true>,
+      decode_step_kernel<128, __half, false>, decode_step_kernel<128, __half, true>};
+  return k[i];
+}
+
 }  // namespace
 
 int decode_step_grid() {
@@ -1130,7 +1130,12 @@ cudaError_t decode_step_configure() {
   if (e != cudaSuccess) return e;
   g_mk_smem_max = size_t(optin) - 1024;
   decode_step_grid();
-  return cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(g_mk_smem_max));
+  for (int i = 0; i < 8; ++i) {
+    e = cudaFuncSetAttribute(step_kernel(i & 4 ? 128 : 64, i & 2, i & 1), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(g_mk_smem_max));
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std::vector<MkTile>& tiles,
@@ -1163,9 +1168,8 @@ bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std
   }
   tile_start.assign(size_t(grid) * (nparts + 1), 0);
   std::vector<std::vector<MkTile>> per(grid);
-  int max_tiles = 0, res_rows = 0, rope_rows = 0, lm_rows = 0;
+  int max_tiles = 0, res_rows = 0, lm_rows = 0;
   for (int c = 0; c < grid; ++c) {
-    int rope = 0, rope_phase = -1;
     for (int i = 0; i < nparts; ++i) {
       tile_start[size_t(c) * (nparts + 1) + i] = int(per[c].size());
       const MkPart& P = parts[i];
@@ -1180,12 +1184,6 @@ bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std
         per[c].push_back(t);
       }
       const int rows = ROWS * (g1 - g0);
-      if (P.kind == MK_QKV) {
-        if (P.phase != rope_phase) rope = 0;
-        rope_phase = P.phase;
-        rope += rows;
-        rope_rows = std::max(rope_rows, rope);
-      }
       if (P.kind == MK_O || P.kind == MK_D) res_rows = std::max(res_rows, rows);
       if (P.kind == MK_LM) lm_rows = std::max(lm_rows, rows);
     }
@@ -1204,7 +1202,6 @@ bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std
   a.region_bytes = int(region);
   a.kmax = kmax;
   a.res_rows = std::max(res_rows, 4);
-  a.rope_rows = std::max(rope_rows, 4);
   a.lm_rows = std::max(lm_rows, 4);
   a.nslots = 1;
   const size_t fixed = mk_offsets(a).total - slot;
@@ -1214,7 +1211,11 @@ bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std
   *smem = mk_offsets(a).total;
   if (*smem > g_mk_smem_max) return false;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, MK_THREADS, *smem) != cudaSuccess ||
+  a.has_q6 = 0;
+  for (int i = 0; i < nparts; ++i)
+    if (parts[i].kind != MK_ATT && parts[i].dtype == DT_Q6K) a.has_q6 = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel(a.head_dim, a.kv_half, a.has_q6), MK_THREADS,
+                                                    *smem) != cudaSuccess ||
       per_sm < 1)
     return false;
   return true;
@@ -1231,7 +1232,7 @@ cudaError_t launch_decode_step(const MkArgs& a, size_t smem, cudaStream_t s) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_step_kernel, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, step_kernel(a.head_dim, a.kv_half, a.has_q6), a);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 

@@ -238,6 +238,7 @@ struct MkArgs {
   float* logits;             // [vocab]
   const float* zero;         // [hidden] zeros: the embedding of an out-of-vocabulary id
   int att_smax;              // most key splits of a query head (set by decode_step_plan)
+  int has_q6;                // a weight of the step is Q6_K (set by decode_step_plan)
   int gen_mode;              // 1: token = hist[nhist - 1], penalty + argmax + bookkeeping
   const uint32_t* ids;       // gen_mode 0: token = ids[0]
   uint32_t* hist;
@@ -245,7 +246,6 @@ struct MkArgs {
   float rep;
   // shared-memory layout (from decode_step_plan)
   int slot_bytes, nslots, region_bytes, kmax;
-  int rope_rows;  // QKV rows of one layer a CTA owns (all QKV parts)
   int res_rows;   // rows of an O / D share
   int lm_rows;    // LM-head rows a CTA owns
 };

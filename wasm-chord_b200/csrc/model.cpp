@@ -889,6 +889,7 @@ void Model::build_decode_step() {
   a.n_kv = int(c.kv_heads);
   a.n_heads = int(c.heads);
   a.head_dim = int(c.head_dim());
+  a.kv_half = int(opt_.kv_half);  // selects the kernel instantiation the plan checks
   a.hidden = H;
   std::vector<MkTile> tiles;
   std::vector<int> tile_start;
