@@ -67,8 +67,9 @@ typedef struct wcb_load_opts {
                          not fit in GPU memory; replaces the reference's Memory64 layer
                          manager, memory64_layer_manager.rs:76-300, async_prefetch.rs:83-190).
                          Single GPU, per-op kernels, no batched path;
-                         bit 5: sample on the host even where the device sampler applies
-                         (temperature > 0 with 1 <= top_k <= 1024); both draw the same tokens. */
+                         bit 5: sampled decoding (temperature > 0) samples on the host from
+                         each step's logits instead of on the device; both draw the same
+                         tokens for a seed. */
   /* Tensor parallelism (one process per GPU; no counterpart in the reference, whose
      sharding.rs is bookkeeping only). tp_size 0 or 1: the whole model on `device`.
      tp_size > 1: this process holds rank tp_rank's shard (query/KV heads, o and down
@@ -198,6 +199,10 @@ uint32_t wcb_model_launches_per_step(uint32_t handle, uint32_t* out);
 uint32_t wcb_sampler_new(const wcb_gen_config* cfg, uint32_t* out_sampler);
 uint32_t wcb_sampler_sample(uint32_t sampler, float* logits, size_t n, uint32_t* out_token);
 uint32_t wcb_sampler_free(uint32_t sampler);
+/* The distribution the last sampled (temperature > 0) wcb_sampler_sample drew
+ * from: n probabilities (compute_probabilities, top-k, top-p and the
+ * renormalisation of sampling.rs:106-229), zero outside the kept candidates. */
+uint32_t wcb_sampler_probs(uint32_t sampler, float* out, size_t n);
 
 /* Last error message of the calling thread (wasmchord_last_error, abi.rs:209-222):
  * NUL-terminated, returns bytes copied excluding the NUL. */

@@ -85,6 +85,8 @@ def lib() -> C.CDLL:
     L.oracle_sampler_penalize.restype = None
     L.oracle_sampler_kind.argtypes = [vp]
     L.oracle_sampler_kind.restype = C.c_int
+    L.oracle_sampler_distribution.argtypes = [vp, vp, sz, vp]
+    L.oracle_sampler_distribution.restype = None
     _LIB = L
     return L
 
@@ -211,6 +213,13 @@ class Sampler:
 
     def penalize(self, logits: np.ndarray) -> None:
         lib().oracle_sampler_penalize(self._h, f32p(logits), logits.size)
+
+    def distribution(self, logits: np.ndarray) -> np.ndarray:
+        """The probabilities sample() would draw from (penalty, compute_probabilities,
+        top-k, top-p, renormalisation; sampling.rs:106-229), without drawing."""
+        out = np.empty(logits.size, dtype=np.float32)
+        lib().oracle_sampler_distribution(self._h, f32p(logits), logits.size, out.ctypes.data)
+        return out
 
     def __del__(self):
         try:

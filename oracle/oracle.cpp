@@ -622,6 +622,37 @@ struct LogitsProcessor {
     for (size_t i = top_k; i < idx.size(); ++i) pr[idx[i]] = 0.0f;
     renorm(pr);
   }
+  // the distribution sample() draws from, without the draw: penalty on a copy,
+  // compute_probabilities, top-k, top-p, renormalisation (sampling.rs:106-229)
+  std::vector<float> distribution(const float* logits, size_t n) const {
+    std::vector<float> l(logits, logits + n);
+    penalize(l.data(), n);
+    std::vector<float> pr = probs(l.data(), n);
+    auto nucleus = [&](std::vector<float>& q, float top_p) {  // sample_topp's mask (sampling.rs:138-163)
+      std::vector<size_t> idx(q.size());
+      std::iota(idx.begin(), idx.end(), 0);
+      std::stable_sort(idx.begin(), idx.end(), [&](size_t a, size_t b) { return q[a] > q[b]; });
+      float cum = 0.0f;
+      for (size_t i : idx) {
+        if (cum >= top_p) q[i] = 0.0f;
+        else cum += q[i];
+      }
+      renorm(q);
+    };
+    const bool tp = !(p <= 0.0 || p >= 1.0);
+    if (kind == TOPP) {
+      if (tp) nucleus(pr, float(p));
+    } else if (kind == TOPK) {
+      if (k < n) keep_topk(pr, k);
+    } else if (kind == TOPK_TOPP) {
+      if (k >= n) nucleus(pr, float(p));
+      else {
+        keep_topk(pr, k);
+        if (tp) nucleus(pr, float(p));
+      }
+    }
+    return pr;
+  }
   // sample — sampling.rs:232-264
   uint32_t sample(float* logits, size_t n) {
     penalize(logits, n);
@@ -999,5 +1030,9 @@ uint32_t oracle_sampler_sample(void* s, float* logits, size_t n, uint32_t* tok) 
 }
 void oracle_sampler_penalize(void* s, float* logits, size_t n) { static_cast<LogitsProcessor*>(s)->penalize(logits, n); }
 int oracle_sampler_kind(void* s) { return static_cast<LogitsProcessor*>(s)->kind; }
+void oracle_sampler_distribution(void* s, const float* logits, size_t n, float* out) {
+  const std::vector<float> d = static_cast<LogitsProcessor*>(s)->distribution(logits, n);
+  std::copy(d.begin(), d.end(), out);
+}
 
 }  // extern "C"

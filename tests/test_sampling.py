@@ -1,10 +1,12 @@
 """Sampled decoding (LogitsProcessor::sample, sampling.rs:106-229). The
 reference's rand StdRng stream is not reproduced, so sampled token sequences
-are checked by distribution: the host sampler's top-k / top-k + top-p path (the
-fixed evaluation order the device sampler repeats) must only draw tokens of
-the top-k set / nucleus, and its draw frequencies must match the exact
-probabilities computed here in float64 from the reference's definitions. The
-device sampler must then draw exactly the host sampler's tokens (gpu)."""
+are checked by distribution: for every sampling kind (top-k, top-k + top-p,
+top-p alone, all tokens, top-k above 1024) the host sampler's probabilities
+must equal the oracle's (compute_probabilities, top-k, top-p, renormalisation
+as the reference computes them), it must draw only kept tokens, and its draw
+frequencies must match the exact probabilities (chi-squared). The device
+sampler must then draw exactly the host sampler's tokens (gpu)."""
+import oracle
 import numpy as np
 import pytest
 
@@ -53,6 +55,54 @@ def test_host_topk_topp_draws_match_the_distribution(top_k, top_p):
     assert chi2 < dof + 6 * np.sqrt(2 * dof) + 10, (chi2, dof)
 
 
+ORACLE_CASES = [  # (vocab, top_k, top_p): every sampling kind of sampling.rs:57-78
+    (300, 20, 0.8),     # top-k then top-p, 20 <= 1024 candidates (fixed-order path)
+    (300, 0, 0.9),      # top-p alone over all tokens
+    (300, 0, 1.0),      # all tokens
+    (3000, 1500, 0.8),  # top-k above 1024 then top-p
+    (3000, 2000, 1.0),  # top-k above 1024
+    (3000, 5000, 0.7),  # top_k >= vocab: top-p over all tokens
+]
+
+
+@pytest.mark.parametrize("n,top_k,top_p", ORACLE_CASES)
+def test_host_probabilities_match_the_oracle(n, top_k, top_p):
+    """The distribution each draw uses equals the oracle's within f32 rounding: the
+    same kept tokens, probabilities within 2e-6 absolute and 1e-4 relative."""
+    rng = np.random.default_rng(n + top_k)
+    for trial in range(4):
+        logits = rng.normal(0.0, 1.2, n).astype(np.float32)
+        s = wcb.LogitsProcessor(17 + trial, 0.9, top_p, top_k, 1.0)
+        o = oracle.Sampler(17 + trial, 0.9, top_p, top_k, 1.0)
+        want = o.distribution(logits)
+        s.sample(logits.copy())
+        got = s.last_probs(n)
+        assert np.array_equal(got > 0, want > 0), (trial, int((got > 0).sum()), int((want > 0).sum()))
+        err = np.abs(got.astype(np.float64) - want)
+        assert np.all(err <= 2e-6 + 1e-4 * want), (trial, float(err.max()))
+
+
+@pytest.mark.parametrize("top_k,top_p", [(0, 0.9), (0, 1.0), (1500, 0.85)])
+def test_host_full_path_draws_match_the_oracle_distribution(top_k, top_p):
+    """chi-squared of the draws of the configurations without a 1024-candidate bound
+    against the oracle's probabilities (the logits are drawn so that no token
+    has a vanishing probability)."""
+    n = 2000 if top_k else 400
+    rng = np.random.default_rng(11)
+    logits = rng.normal(0.0, 0.5, n).astype(np.float32)
+    s = wcb.LogitsProcessor(99, 1.0, top_p, top_k, 1.0)
+    want = oracle.Sampler(99, 1.0, top_p, top_k, 1.0).distribution(logits).astype(np.float64)
+    draws = 60000
+    counts = np.zeros(n)
+    for _ in range(draws):
+        counts[s.sample(logits.copy())] += 1
+    assert counts[want == 0].sum() == 0
+    live = want > 0
+    chi2 = (((counts[live] - draws * want[live]) ** 2) / (draws * want[live])).sum()
+    dof = live.sum() - 1
+    assert chi2 < dof + 6 * np.sqrt(2 * dof) + 10, (chi2, dof)
+
+
 def test_host_sampler_is_seeded():
     rng = np.random.default_rng(5)
     logits = rng.normal(0.0, 2.0, 1000).astype(np.float32)
@@ -63,7 +113,9 @@ def test_host_sampler_is_seeded():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("cfg", [dict(top_k=40, top_p=1.0, rep=1.0), dict(top_k=40, top_p=0.9, rep=1.1),
-                                 dict(top_k=200, top_p=0.95, rep=1.3), dict(top_k=1, top_p=0.5, rep=1.0)])
+                                 dict(top_k=200, top_p=0.95, rep=1.3), dict(top_k=1, top_p=0.5, rep=1.0),
+                                 dict(top_k=0, top_p=0.9, rep=1.1), dict(top_k=0, top_p=1.0, rep=1.0),
+                                 dict(top_k=600, top_p=0.8, rep=1.2)])
 def test_device_sampler_draws_the_host_samplers_tokens(tiny_gguf, gpu, cfg):
     dev = wcb.Model.load_from_gguf(tiny_gguf, use_persistent=False)
     host = wcb.Model.load_from_gguf(tiny_gguf, use_persistent=False, host_sampling=True)
@@ -89,3 +141,22 @@ def test_device_sampling_on_the_default_model(tiny_gguf, gpu):
     g1 = m.generate_tokens(prompt, greedy)  # the persistent greedy path still follows
     assert g1 == m.generate_tokens(prompt, greedy)
     m.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("top_k,top_p", [(1500, 0.9), (2500, 1.0), (0, 0.95)])
+def test_device_full_sampler_on_a_large_vocabulary(model_dir, gpu, top_k, top_p):
+    """top_k above 1024 (and no top_k) over a 3072-token vocabulary: the device's
+    sample_full_kernel draws exactly the host sampler's tokens, with no host round trip
+    per token (one launch of the decode graph per step)."""
+    path = synth.cached_model("tiny", model_dir, vocab_size=3072)
+    dev = wcb.Model.load_from_gguf(path, use_persistent=False)
+    host = wcb.Model.load_from_gguf(path, use_persistent=False, host_sampling=True)
+    prompt = synth.random_prompt(20, 3072, seed=12).tolist()
+    for seed in (4, 5):
+        g = wcb.GenerationConfig(max_tokens=40, temperature=1.1, top_p=top_p, top_k=top_k,
+                                 repetition_penalty=1.1, seed=seed, eos_id=None)
+        assert dev.generate_tokens(prompt, g) == host.generate_tokens(prompt, g)
+    assert dev.launches_per_step() > 1
+    dev.close()
+    host.close()

@@ -450,6 +450,25 @@ uint32_t wcb_sampler_sample(uint32_t sid, float* logits, size_t n, uint32_t* tok
   });
 }
 
+uint32_t wcb_sampler_probs(uint32_t sid, float* out, size_t n) {
+  return guarded([&]() -> uint32_t {
+    if (!out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");
+    std::shared_ptr<wcb::Sampler> s;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      auto it = g_samplers.find(sid);
+      if (it == g_samplers.end()) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid sampler handle");
+      s = it->second;
+    }
+    const std::vector<float>& p = s->last_probs();
+    if (p.size() != n)
+      return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: the last sampled draw had " + std::to_string(p.size()) +
+                                                " probabilities (none after an argmax), not " + std::to_string(n));
+    std::copy(p.begin(), p.end(), out);
+    return WCB_OK;
+  });
+}
+
 uint32_t wcb_sampler_free(uint32_t sid) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_samplers.erase(sid)) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid sampler handle");

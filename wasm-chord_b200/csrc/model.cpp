@@ -657,15 +657,20 @@ void Model::enqueue_lm_head(int T, bool gen) {
   // with several ranks each scores its vocabulary rows; the argmax key (order-
   // preserving logit bits | token id) and the NaN flag are max-reduced over the
   // ranks, then every rank runs the same sampler bookkeeping
-  const bool dev_sample = gen && sample_mode_ == 1;
+  const bool dev_sample = gen && sample_mode_ != 0;
   gen_mode_ = (gen && !dev_sample) ? (tp_ > 1 ? 2 : 1) : 0;
   gemv(head, 1, H, 1, x_ + size_t(T - 1) * H, H, out_norm_, cfg_.eps, PRO_RMSNORM, EPI_LMHEAD, logits_,
        int(cfg_.vocab), nullptr, 0, nullptr, 0, -1, 0);
   gen_mode_ = 0;
   if (dev_sample) {  // penalty, top-k / top-p draw and generate()'s bookkeeping on the device
-    check(launch_sample(logits_, plog_, int(cfg_.vocab), st_, hist_, pen_cnt_, rep_, samp_t_, samp_k_, samp_tp_, rng_,
-                        stream_),
-          "sampler");
+    if (sample_mode_ == 1)  // 1 <= top_k <= 1024
+      check(launch_sample(logits_, plog_, int(cfg_.vocab), st_, hist_, pen_cnt_, rep_, samp_t_, samp_k_, samp_tp_,
+                          rng_, stream_),
+            "sampler");
+    else  // every other sampled configuration
+      check(launch_sample_full(logits_, plog_, int(cfg_.vocab), st_, hist_, pen_cnt_, rep_, samp_t_, samp_k_,
+                               samp_tp_, rng_, nullptr, stream_),
+            "sampler");
     ++launches_;
   }
   if (gen && tp_ > 1) {
@@ -1009,12 +1014,13 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   sess_tokens_.clear();
   sess_done_ = false;
   sess_steps_left_ = g.max_tokens > 1 ? size_t(g.max_tokens) - 1 : 0;
-  // top-k sampling runs on the device (sample_dev.cu, the host sampler's fixed order):
-  // the same device-driven loop as greedy decoding; other sampled configurations
-  // sample on the host from each step's logits
-  const bool dev_sample = !sess_greedy_ && plog_ && !(opt_.flags & 32) && sess_sampler_->fixed_path(cfg_.vocab);
+  // sampled decoding runs on the device (sample_dev.cu; the host sampler's order of
+  // operations, so a seed draws the same tokens): the same device-driven loop as
+  // greedy decoding. Mode 1: 1 <= top_k <= 1024; mode 2: every other configuration.
+  // Load flag bit 5 keeps the host sampler (each step's logits copied back).
+  const bool dev_sample = !sess_greedy_ && plog_ && !(opt_.flags & 32);
   sess_host_ = !sess_greedy_ && !dev_sample;
-  sample_mode_ = dev_sample ? 1 : 0;
+  sample_mode_ = dev_sample ? (sess_sampler_->fixed_path(cfg_.vocab) ? 1 : 2) : 0;
   if (dev_sample) {
     samp_t_ = sess_sampler_->temperature();
     samp_k_ = int(sess_sampler_->top_k());

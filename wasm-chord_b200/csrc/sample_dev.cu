@@ -16,6 +16,7 @@
 
 #include "device_common.cuh"
 #include "kernels.h"
+#include "sample_int.h"
 #include "wcb_exp.h"
 
 namespace wcb {
@@ -225,6 +226,249 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
   }
 }
 
+
+// ---- any number of candidates (top_k = 0 or top_k > 1024): integer weights ----
+
+// inclusive warp scan / block-wide exclusive scan and total of a u64 per thread
+__device__ __forceinline__ unsigned long long warp_incl_u64(unsigned long long v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+__device__ unsigned long long block_excl_u64(unsigned long long v, unsigned long long* total, unsigned long long* ws) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned long long inc = warp_incl_u64(v);
+  __syncthreads();  // ws may still be read by a previous call
+  if (lane == 31) ws[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned long long w = warp_incl_u64(ws[lane]);
+    ws[lane] = w;  // inclusive totals of the warps
+  }
+  __syncthreads();
+  *total = ws[SD_THREADS / 32 - 1];
+  return (warp ? ws[warp - 1] : 0ull) + inc - v;
+}
+
+// LogitsProcessor::sample for top_k = 0 or top_k > 1024 (sampling.rs:106-229),
+// with the weights of sample_int.h: the repetition penalty into plog, the top-k
+// candidates (k = 0: all) by a radix select of the order-preserving logit bits
+// (ties at the threshold to the lowest indices), x = l / T, the maximum, the
+// integer weights E (stored over plog), top-p by a radix search over E with
+// per-bucket counts and exact sums, the draw, generate()'s bookkeeping.
+// probs (may be null) receives each token's final probability.
+__global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* logits, float* plog, int n, StepState* st,
+                                                                 uint32_t* hist, uint32_t* pen_cnt, float rep,
+                                                                 float temp, int top_k, float top_p,
+                                                                 unsigned long long* rng, float* probs) {
+  __shared__ unsigned int hcount[256];
+  __shared__ unsigned long long hsum[256];
+  __shared__ unsigned long long ws[SD_THREADS / 32];
+  __shared__ unsigned int s_prefix, s_rem, s_nan, s_keq, s_tok;
+  __shared__ unsigned long long s_c, s_t;
+  __shared__ float s_max;
+  __shared__ float wmax[SD_THREADS / 32];
+  pdl_trigger();
+  pdl_wait();
+  if (st->done) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (n + SD_THREADS - 1) / SD_THREADS;
+  const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
+  if (tid == 0) s_nan = 0;
+  __syncthreads();
+  bool nan = false;
+  for (int i = i0; i < i1; ++i) {  // repetition penalty once per occurrence (sampling.rs:86-103)
+    float v = logits[i];
+    if (rep != 1.0f) {
+      const uint32_t c = pen_cnt[i];
+      for (uint32_t k = 0; k < c; ++k) v = v > 0.0f ? __fdiv_rn(v, rep) : __fmul_rn(v, rep);
+    }
+    nan |= v != v;
+    plog[i] = v;
+  }
+  if (nan) atomicOr(&s_nan, 1u);
+  __syncthreads();
+  if (s_nan) {  // partial_cmp().unwrap() panics on NaN in the reference
+    if (tid == 0) {
+      st->err = 1;
+      st->done = 1;
+    }
+    return;
+  }
+  // top-k candidates (0 < top_k < n): the threshold key and how many of its ties are taken
+  const bool topk = top_k > 0 && top_k < n;
+  unsigned int prefix = 0, rem = 0;
+  if (topk) {
+    unsigned int pmask = 0;
+    rem = unsigned(top_k);
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += SD_THREADS) hcount[b] = 0;
+      __syncthreads();
+      for (int i = i0; i < i1; ++i) {
+        const uint32_t key = order_key(plog[i]);
+        if ((key & pmask) == prefix) atomicAdd(&hcount[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        unsigned int cum = 0;
+        for (int b = 255; b >= 0; --b) {
+          if (cum + hcount[b] >= rem) {
+            s_prefix = prefix | (unsigned(b) << shift);
+            s_rem = rem - cum;
+            break;
+          }
+          cum += hcount[b];
+        }
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      rem = s_rem;
+      pmask |= 255u << shift;
+    }
+  }
+  // x = l / T over the candidates (-inf elsewhere) into plog, and the maximum
+  {
+    unsigned long long eq = 0;
+    if (topk)
+      for (int i = i0; i < i1; ++i) eq += order_key(plog[i]) == prefix;
+    unsigned long long eq_tot;
+    unsigned int eq_rank = unsigned(block_excl_u64(eq, &eq_tot, ws));
+    float mx = -INFINITY;
+    for (int i = i0; i < i1; ++i) {
+      bool take = true;
+      if (topk) {
+        const uint32_t key = order_key(plog[i]);
+        take = key > prefix;
+        if (key == prefix) take = eq_rank++ < rem;
+      }
+      const float x = take ? __fdiv_rn(plog[i], temp) : -INFINITY;
+      plog[i] = x;
+      mx = fmaxf(mx, x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) wmax[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+      float m = -INFINITY;
+      for (int w = 0; w < SD_THREADS / 32; ++w) m = fmaxf(m, wmax[w]);
+      s_max = m;
+    }
+    __syncthreads();
+  }
+  // integer weights (stored over plog) and their total
+  uint32_t* E = reinterpret_cast<uint32_t*>(plog);
+  const float M = s_max;
+  unsigned long long mine = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t w = int_weight(wcb_exp_nonpos(__fadd_rn(plog[i], -M)));
+    E[i] = w;
+    mine += w;
+  }
+  unsigned long long S;
+  block_excl_u64(mine, &S, ws);
+  // top-p: the last kept weight v* (radix search over E from the top, exact sums)
+  const bool tp_on = !(top_p <= 0.0f || top_p >= 1.0f);  // TOPP / TOPK_TOPP (sampling.rs:57-78)
+  unsigned int vstar = 0, keq = 0xFFFFFFFFu;
+  if (tp_on) {
+    const TopP tpp = top_p_parts(top_p);
+    unsigned int pfx = 0, pmask = 0;
+    unsigned long long C = 0;  // sum of the weights above the current range
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += SD_THREADS) {
+        hcount[b] = 0;
+        hsum[b] = 0;
+      }
+      __syncthreads();
+      for (int i = i0; i < i1; ++i) {
+        const uint32_t w = E[i];
+        if ((w & pmask) == pfx) {
+          atomicAdd(&hcount[(w >> shift) & 255u], 1u);
+          atomicAdd(&hsum[(w >> shift) & 255u], (unsigned long long)w);
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int b = 255;
+        for (; b > 0; --b) {  // whole buckets whose last weight still starts below top_p * S
+          if (!hcount[b]) continue;
+          if (!below_top_p(C + hsum[b], tpp, S)) break;
+          C += hsum[b];
+        }
+        s_prefix = pfx | (unsigned(b) << shift);
+        s_c = C;
+        if (shift == 0) {  // v* reached: how many of its ties (lowest indices first) are kept
+          const unsigned int cnt = hcount[b];
+          const unsigned long long v = (unsigned long long)((pfx | unsigned(b)) & 0xFFFFFFFFu);
+          unsigned int lo = 0, hi = cnt;  // largest r in [0, cnt] with every r' < r kept
+          while (lo < hi) {
+            const unsigned int mid = (lo + hi + 1) / 2;
+            if (below_top_p(C + (unsigned long long)(mid - 1) * v, tpp, S)) lo = mid;
+            else hi = mid - 1;
+          }
+          s_keq = lo;
+        }
+      }
+      __syncthreads();
+      pfx = s_prefix;
+      C = s_c;
+      pmask |= 255u << shift;
+    }
+    vstar = pfx;
+    keq = s_keq;
+  }
+  // kept weights and their running sum in index order
+  unsigned long long eqn = 0;
+  if (tp_on)
+    for (int i = i0; i < i1; ++i) eqn += E[i] == vstar;
+  unsigned long long eqt;
+  unsigned long long er = block_excl_u64(eqn, &eqt, ws);
+  unsigned long long kept = 0;
+  {
+    unsigned long long r = er;
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t w = E[i];
+      const bool k = !tp_on || w > vstar || (w == vstar && r++ < keq);
+      kept += k ? w : 0u;
+    }
+  }
+  unsigned long long S_kept;
+  const unsigned long long before = block_excl_u64(kept, &S_kept, ws);
+  if (tid == 0) {
+    s_tok = 0xFFFFFFFFu;
+    if (S_kept == 0) {  // no positive weight (WeightedIndex fails in the reference)
+      st->err = 1;
+      st->done = 1;
+    } else {
+      s_t = draw_target(splitmix64_next(reinterpret_cast<uint64_t*>(rng)), S_kept);
+    }
+  }
+  __syncthreads();
+  if (S_kept == 0) return;
+  const unsigned long long t = s_t;
+  {
+    unsigned long long r = er, cum = before;
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t w = E[i];
+      const bool k = !tp_on || w > vstar || (w == vstar && r++ < keq);
+      if (probs) probs[i] = k ? float(double(w) / double(S_kept)) : 0.0f;
+      if (!k) continue;
+      cum += w;
+      if (cum > t && before <= t && s_tok == 0xFFFFFFFFu) s_tok = unsigned(i);  // first token past t
+    }
+  }
+  __syncthreads();
+  if (tid == 0 && s_tok != 0xFFFFFFFFu) {
+    st->best = (unsigned long long)s_tok;  // the key's low word carries the token
+    st->nan = 0;
+    finish_sample_state(st, hist, pen_cnt);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
@@ -242,6 +486,28 @@ cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState*
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, sample_kernel, logits, scratch, n, st, hist, pen_cnt, rep,
                                            temperature, top_k, top_p, rng);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+}  // namespace wcb
+
+namespace wcb {
+
+cudaError_t launch_sample_full(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
+                               uint32_t* pen_cnt, float rep, float temperature, int top_k, float top_p,
+                               unsigned long long* rng, float* probs, cudaStream_t s) {
+  if (top_k < 0 || n < 1 || !(temperature > 0.0f)) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(SD_THREADS);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, sample_full_kernel, logits, scratch, n, st, hist, pen_cnt, rep,
+                                           temperature, top_k, top_p, rng, probs);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 

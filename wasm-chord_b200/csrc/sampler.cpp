@@ -5,6 +5,7 @@
 #include <numeric>
 
 #include "gguf.h"
+#include "sample_int.h"
 #include "wcb_exp.h"
 
 namespace wcb {
@@ -43,48 +44,6 @@ uint32_t Sampler::argmax(const float* l, size_t n) {
     if (i && !(l[best] > l[i])) best = i;
   }
   return uint32_t(best);
-}
-
-void Sampler::renormalize(std::vector<float>& p) {
-  float s = 0.0f;
-  for (float v : p) s += v;
-  if (s > 0.0f)
-    for (float& v : p) v /= s;
-}
-
-uint32_t Sampler::multinomial(const std::vector<float>& p) {
-  std::vector<float> cum(p.size());
-  float tot = 0.0f;
-  for (size_t i = 0; i < p.size(); ++i) {
-    if (!(p[i] >= 0.0f)) throw WcbError(E_GENERIC, "Failed to create weighted index: invalid weight");
-    tot += p[i];
-    cum[i] = tot;
-  }
-  if (!(tot > 0.0f)) throw WcbError(E_GENERIC, "Failed to create weighted index: all weights zero");
-  const float u = uniform() * tot;
-  const size_t i = size_t(std::upper_bound(cum.begin(), cum.end(), u) - cum.begin());
-  return uint32_t(std::min(i, p.size() - 1));
-}
-
-uint32_t Sampler::top_p(std::vector<float>& p, float tp) {
-  std::vector<size_t> idx(p.size());
-  std::iota(idx.begin(), idx.end(), size_t(0));
-  std::stable_sort(idx.begin(), idx.end(), [&](size_t a, size_t b) { return p[a] > p[b]; });
-  float cum = 0.0f;
-  for (size_t i : idx) {
-    if (cum >= tp) p[i] = 0.0f;
-    else cum += p[i];
-  }
-  renormalize(p);
-  return multinomial(p);
-}
-
-void Sampler::keep_top_k(std::vector<float>& p, size_t k) {
-  std::vector<size_t> idx(p.size());
-  std::iota(idx.begin(), idx.end(), size_t(0));
-  std::nth_element(idx.begin(), idx.begin() + long(k), idx.end(), [&](size_t a, size_t b) { return p[a] > p[b]; });
-  for (size_t i = k; i < idx.size(); ++i) p[idx[i]] = 0.0f;
-  renormalize(p);
 }
 
 uint32_t Sampler::sample_fixed(const float* l, size_t n) {
@@ -128,6 +87,8 @@ uint32_t Sampler::sample_fixed(const float* l, size_t n) {
   float tot = 0.0f;
   for (size_t j = 0; j < K; ++j) tot += q[j];
   if (!(tot > 0.0f)) throw WcbError(E_GENERIC, "Failed to create weighted index: all weights zero");
+  last_probs_.assign(n, 0.0f);
+  for (size_t j = 0; j < K; ++j) last_probs_[cand[j]] = q[j] / tot;
   const float u = uniform() * tot;
   float c = 0.0f;
   for (size_t j = 0; j < K; ++j) {
@@ -137,43 +98,66 @@ uint32_t Sampler::sample_fixed(const float* l, size_t n) {
   return cand[K - 1];
 }
 
+uint32_t Sampler::sample_int(const float* l, size_t n) {
+  for (size_t i = 0; i < n; ++i)
+    if (std::isnan(l[i])) throw WcbError(E_GENERIC, "Runtime error: NaN logit at index " + std::to_string(i));
+  // candidates: the top-k by (logit desc, index asc) when 0 < top_k < n, else all
+  std::vector<uint8_t> cand(n, 1);
+  if (top_k_ > 0 && top_k_ < n) {
+    std::fill(cand.begin(), cand.end(), 0);
+    std::vector<uint32_t> idx(n);
+    std::iota(idx.begin(), idx.end(), 0u);
+    std::nth_element(idx.begin(), idx.begin() + long(top_k_), idx.end(),
+                     [&](uint32_t a, uint32_t b) { return l[a] > l[b] || (l[a] == l[b] && a < b); });
+    for (size_t j = 0; j < top_k_; ++j) cand[idx[j]] = 1;
+  }
+  const float tf = float(temperature_);
+  std::vector<float> x(n);
+  float mx = -INFINITY;
+  for (size_t i = 0; i < n; ++i) {
+    x[i] = cand[i] ? l[i] / tf : -INFINITY;
+    mx = std::fmax(mx, x[i]);
+  }
+  std::vector<uint32_t> E(n);
+  uint64_t S = 0;
+  for (size_t i = 0; i < n; ++i) {
+    E[i] = int_weight(wcb_exp_nonpos(x[i] + (-mx)));
+    S += E[i];
+  }
+  std::vector<uint8_t> kept(n, 1);
+  const float tp = float(top_p_);
+  if (!(tp <= 0.0f || tp >= 1.0f)) {  // top-p in exact arithmetic, (E desc, index asc)
+    const TopP t = top_p_parts(tp);
+    std::vector<uint32_t> ord(n);
+    std::iota(ord.begin(), ord.end(), 0u);
+    std::stable_sort(ord.begin(), ord.end(), [&](uint32_t a, uint32_t b) { return E[a] > E[b]; });
+    uint64_t cum = 0;
+    for (uint32_t i : ord) {
+      kept[i] = below_top_p(cum, t, S) ? 1 : 0;
+      cum += E[i];
+    }
+  }
+  uint64_t S_kept = 0;
+  for (size_t i = 0; i < n; ++i) S_kept += kept[i] ? E[i] : 0u;
+  if (S_kept == 0) throw WcbError(E_GENERIC, "Failed to create weighted index: all weights zero");
+  last_probs_.assign(n, 0.0f);
+  for (size_t i = 0; i < n; ++i) last_probs_[i] = kept[i] ? float(double(E[i]) / double(S_kept)) : 0.0f;
+  const uint64_t target = draw_target(splitmix64_next(&state_), S_kept);
+  uint64_t cum = 0;
+  for (size_t i = 0; i < n; ++i) {
+    if (!kept[i]) continue;
+    cum += E[i];
+    if (cum > target) return uint32_t(i);
+  }
+  return uint32_t(n - 1);  // unreachable: target < S_kept
+}
+
 uint32_t Sampler::sample(float* l, size_t n) {
   penalize(l, n);
   uint32_t tok;
-  if (kind_ == ARGMAX) {
-    tok = argmax(l, n);
-  } else if (fixed_path(n)) {
-    tok = sample_fixed(l, n);
-  } else {
-    // compute_probabilities (sampling.rs:106-115)
-    std::vector<float> p(n);
-    const float tf = float(temperature_);
-    float mx = -INFINITY;
-    for (size_t i = 0; i < n; ++i) {
-      p[i] = l[i] / tf;
-      mx = std::fmax(mx, p[i]);
-    }
-    float sum = 0.0f;
-    for (size_t i = 0; i < n; ++i) sum += std::exp(p[i] - mx);
-    for (size_t i = 0; i < n; ++i) p[i] = std::exp(p[i] - mx) / sum;
-    const float tp = float(top_p_);
-    const bool tp_active = !(top_p_ <= 0.0 || top_p_ >= 1.0);
-    switch (kind_) {
-      case ALL: tok = multinomial(p); break;
-      case TOPP: tok = tp_active ? top_p(p, tp) : multinomial(p); break;
-      case TOPK:
-        if (top_k_ < n) keep_top_k(p, top_k_);
-        tok = multinomial(p);
-        break;
-      default:  // TOPK_TOPP (sampling.rs:195-229)
-        if (top_k_ >= n) {
-          tok = top_p(p, tp);
-        } else {
-          keep_top_k(p, top_k_);
-          tok = tp_active ? top_p(p, tp) : multinomial(p);
-        }
-    }
-  }
+  if (kind_ == ARGMAX) tok = argmax(l, n);
+  else if (fixed_path(n)) tok = sample_fixed(l, n);
+  else tok = sample_int(l, n);
   prev_.push_back(tok);
   return tok;
 }

@@ -11,6 +11,9 @@
 // (logit desc, index asc) (the reference's select_nth_unstable leaves ties at
 // the boundary unspecified), softmax over them with wcb_exp_nonpos
 // (mathematically the reference's softmax-then-renormalise), top-p and the draw.
+// Every other sampled configuration (top_k = 0, or top_k > 1024) takes
+// sample_int: integer weights (sample_int.h), exact sums, the same draw as the
+// device's sample_full_kernel.
 #pragma once
 #include <algorithm>
 #include <cstdint>
@@ -38,14 +41,13 @@ class Sampler {
   bool greedy() const { return kind_ == ARGMAX; }
   float repetition_penalty() const { return rep_; }
   std::vector<uint32_t>& history() { return prev_; }
+  // the probabilities the last sample_int / sample_fixed drew from (one per token)
+  const std::vector<float>& last_probs() const { return last_probs_; }
 
  private:
   float uniform();
   uint32_t sample_fixed(const float* logits, size_t n);
-  uint32_t multinomial(const std::vector<float>& p);
-  uint32_t top_p(std::vector<float>& p, float tp);
-  static void keep_top_k(std::vector<float>& p, size_t k);
-  static void renormalize(std::vector<float>& p);
+  uint32_t sample_int(const float* logits, size_t n);
 
   uint64_t state_;
   Kind kind_;
@@ -53,6 +55,7 @@ class Sampler {
   size_t top_k_;
   float rep_;
   std::vector<uint32_t> prev_;
+  std::vector<float> last_probs_;
 };
 
 }  // namespace wcb

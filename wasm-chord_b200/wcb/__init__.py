@@ -31,7 +31,7 @@ KV_F16 = 1
 EXPORTED = [
     "wcb_gen_config_default", "wcb_model_load", "wcb_model_free", "wcb_model_config_get", "wcb_forward",
     "wcb_clear_kv", "wcb_kv_len", "wcb_generate_tokens", "wcb_generate_batch", "wcb_sampler_new",
-    "wcb_sampler_sample", "wcb_sampler_free", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
+    "wcb_sampler_sample", "wcb_sampler_free", "wcb_sampler_probs", "wcb_last_error", "wcb_version", "wcb_dequant_dev",
     "wcb_repack_q6k_dev", "wcb_gemv_dev", "wcb_model_stream", "wcb_infer", "wcb_next_tokens",
     "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_batch_info", "wcb_tokenizer_load", "wcb_tokenizer_free",
     "wcb_tokenizer_info", "wcb_tokenizer_set_special", "wcb_tokenize", "wcb_detokenize", "wcb_generate_text",
@@ -115,6 +115,7 @@ def lib() -> C.CDLL:
     L.wcb_sampler_new.argtypes = [C.POINTER(_GenConfig), C.POINTER(u32)]
     L.wcb_sampler_sample.argtypes = [u32, vp, sz, C.POINTER(u32)]
     L.wcb_sampler_free.argtypes = [u32]
+    L.wcb_sampler_probs.argtypes = [u32, vp, sz]
     L.wcb_last_error.argtypes = [C.c_char_p, sz]
     L.wcb_last_error.restype = sz
     L.wcb_version.restype = C.c_char_p
@@ -478,6 +479,12 @@ class LogitsProcessor:
         t = C.c_uint32(0)
         _check(lib().wcb_sampler_sample(self._h, logits.ctypes.data, logits.size, C.byref(t)))
         return t.value
+
+    def last_probs(self, n: int) -> np.ndarray:
+        """The n probabilities the last sampled draw used (zero outside the kept candidates)."""
+        out = np.empty(n, dtype=np.float32)
+        _check(lib().wcb_sampler_probs(self._h, out.ctypes.data, n))
+        return out
 
     def __del__(self):
         try:
