@@ -249,6 +249,16 @@ uint32_t wcb_tp_id(uint8_t out[128]);
 uint32_t wcb_model_tp_handle(uint32_t h, uint8_t out[64]);
 uint32_t wcb_model_tp_connect(uint32_t h, const uint8_t* handles, uint32_t n_ranks);
 
+/* Tensor parallelism, failure handling: abandons this rank's group after the
+ * caller's own failure detector (a heartbeat, a store) found another rank gone.
+ * Aborts the NCCL communicator (ncclCommAbort), which also ends a collective
+ * still waiting for that rank; every later call on the model then fails with
+ * WCB_ERR_BACKEND_UNSUPPORTED, and wcb_model_free releases it without waiting
+ * for the other ranks. The one call that may run while another call on the
+ * same handle is in progress. A bounded device wait that expires (wait_ms)
+ * fails the group the same way. No counterpart in the reference. */
+uint32_t wcb_model_tp_abort(uint32_t h);
+
 /* ---- kernel-level entry points (device pointers, caller's stream) ----------
  * No counterpart in the reference's public API: they expose the hot kernels
  * (the reference's quant.rs dequantisers and gemm.rs matmul_transposed) for

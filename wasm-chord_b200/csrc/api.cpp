@@ -710,6 +710,13 @@ uint32_t wcb_model_tp_connect(uint32_t h, const uint8_t* handles, uint32_t n_ran
   });
 }
 
+uint32_t wcb_model_tp_abort(uint32_t h) {
+  return guarded([&]() -> uint32_t {
+    get_model(h)->tp_abort();
+    return WCB_OK;
+  });
+}
+
 uint32_t wcb_model_stream(uint32_t h, void** out) {
   return guarded([&]() -> uint32_t {
     if (!out) return fail(WCB_ERR_INVALID_ARGUMENT, "Invalid argument: null pointer");

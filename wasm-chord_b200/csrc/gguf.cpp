@@ -117,6 +117,16 @@ GgufFile::GgufFile(const std::string& path) {
     }
     const uint64_t pos = uint64_t(std::ftell(f_));
     data_offset_ = (pos + 31) & ~uint64_t(31);
+    // a truncated file is reported here, before any device work, rather than by
+    // the read of its first missing tensor (tensor_loader.rs:50-149 fails there
+    // with "failed to fill whole buffer")
+    if (std::fseek(f_, 0, SEEK_END) != 0) throw WcbError(E_IO, "IO error: seek failed");
+    const uint64_t size = uint64_t(std::ftell(f_));
+    for (const GgufTensor& t : tensors_)
+      if (t.dtype != 255u && data_offset_ + t.offset + t.nbytes > size)
+        throw WcbError(E_IO, "IO error: failed to fill whole buffer: tensor " + t.name + " ends at byte " +
+                                 std::to_string(data_offset_ + t.offset + t.nbytes) + " of a " +
+                                 std::to_string(size) + "-byte file (truncated)");
     auto it = meta_.find("general.architecture");
     arch_ = (it != meta_.end() && it->second.type == 8) ? it->second.s : "unknown";
   } catch (...) {

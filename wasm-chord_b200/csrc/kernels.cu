@@ -788,6 +788,47 @@ __global__ void tp_finish_kernel(StepState* st, const unsigned long long* key, u
   st->epoch += 1;  // tags of the next step's partial sums
 }
 
+__global__ void tp_key_exchange_kernel(StepState* st, unsigned long long* const* peers, const unsigned long long* own,
+                                       int rank, int tp, size_t key_off, uint32_t* hist, uint32_t* pen_cnt) {
+  if (st->done) return;
+  const unsigned long long tag = (unsigned long long)(uint32_t(st->epoch) * 512u + 512u) << 32;
+  const unsigned long long best = st->best;
+  const uint32_t hi = uint32_t(best >> 32), lo = (uint32_t(best) & 0x7FFFFFFFu) | (st->nan ? 0x80000000u : 0u);
+  for (int r = 0; r < tp; ++r) {  // one 64-bit store per word: value and tag arrive together
+    unsigned long long* p = peers[r] + key_off + 2 * size_t(rank);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(tag | hi) : "memory");
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p + 1), "l"(tag | lo) : "memory");
+  }
+  const unsigned long long limit_ns = 1000000ull * unsigned(st->wait_ms > 0 ? st->wait_ms : 2000);
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  unsigned long long kmax = 0;
+  int nan = 0;
+  for (int r = 0; r < tp; ++r) {
+    const unsigned long long* p = own + key_off + 2 * size_t(r);
+    unsigned long long a, b;
+    while (true) {
+      asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+      asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(b) : "l"(p + 1) : "memory");
+      if ((a >> 32) == (tag >> 32) && (b >> 32) == (tag >> 32)) break;
+      unsigned long long t1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+      if (t1 - t0 > limit_ns) {  // a rank stopped: report it and end the step
+        atomicOr(&st->err, 16);
+        st->done = 1;
+        return;
+      }
+    }
+    const unsigned long long k = ((a & 0xFFFFFFFFull) << 32) | (b & 0x7FFFFFFFull);
+    kmax = k > kmax ? k : kmax;
+    nan |= int((b >> 31) & 1u);
+  }
+  st->best = kmax;
+  st->nan = nan;
+  finish_sample_state(st, hist, pen_cnt);
+  st->epoch += 1;  // tags of the next step's partial sums
+}
+
 __global__ void init_gen_kernel(StepState* st, int max_gen, int eos, int max_seq) {
   st->best = 0ull;
   st->ticket = 0;
@@ -935,6 +976,13 @@ cudaError_t launch_tp_pack_key(StepState* st, unsigned long long* key, cudaStrea
 cudaError_t launch_tp_finish(StepState* st, const unsigned long long* key, uint32_t* hist, uint32_t* pen_cnt,
                              cudaStream_t s) {
   tp_finish_kernel<<<1, 1, 0, s>>>(st, key, hist, pen_cnt);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tp_key_exchange(StepState* st, unsigned long long* const* peers, const unsigned long long* own,
+                                   int tp_rank, int tp_size, size_t key_off, uint32_t* hist, uint32_t* pen_cnt,
+                                   cudaStream_t s) {
+  tp_key_exchange_kernel<<<1, 1, 0, s>>>(st, peers, own, tp_rank, tp_size, key_off, hist, pen_cnt);
   return cudaGetLastError();
 }
 

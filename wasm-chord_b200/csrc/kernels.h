@@ -366,6 +366,14 @@ cudaError_t launch_tp_reduce_add(float* dst, const float* resid, const unsigned 
                                  size_t n, int phase, StepState* st, cudaStream_t s);
 cudaError_t launch_tp_finish(StepState* st, const unsigned long long* key, uint32_t* hist, uint32_t* pen_cnt,
                              cudaStream_t s);
+// the same reduction of the LM-head keys without NCCL: this rank's key goes as two
+// tagged 64-bit words (tag epoch * 512 + 512: the high and low key words, the NaN
+// flag in bit 31 of the low one) into slot tp_rank of every rank's receive buffer
+// at key_off; then a bounded wait for every rank's pair, the maximum key, the
+// bookkeeping. An expired wait sets st->err bit 16 and ends the step (st->done).
+cudaError_t launch_tp_key_exchange(StepState* st, unsigned long long* const* peers, const unsigned long long* own,
+                                   int tp_rank, int tp_size, size_t key_off, uint32_t* hist, uint32_t* pen_cnt,
+                                   cudaStream_t s);
 
 // StepState writers (single-thread kernels, so they order with the stream and
 // can sit inside a captured graph)

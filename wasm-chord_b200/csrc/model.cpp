@@ -65,6 +65,9 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
   if (c.vocab % 4) throw WcbError(E_BACKEND, "Backend error: vocab size must be a multiple of 4");
   max_seq_ = opt.max_seq ? opt.max_seq : c.max_seq;
   if (max_seq_ == 0) throw WcbError(E_INVALID, "Invalid tensor shape: context length 0");
+  // the one tensor the reference requires (model.rs:432-446), checked before any device work
+  if (!f.find("token_embd.weight") && !f.find("model.embed_tokens.weight") && !f.find("embed_tokens.weight"))
+    throw WcbError(E_PARSE, "Parse error: Missing token embeddings");
 
   tp_ = std::max<uint32_t>(opt.tp_size, 1);
   rank_ = opt.tp_rank;
@@ -249,8 +252,10 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     if (tp_ > 1) {
       part_y_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
       tpkey_ = static_cast<unsigned long long*>(dalloc(2 * sizeof(unsigned long long)));
-      recv_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * tp_ * c.hidden));
-      check(cudaMemset(recv_, 0, sizeof(unsigned long long) * tp_ * c.hidden), "clear receive buffer");
+      // [tp][hidden] partial sums, then [tp][2] LM-head argmax keys (tagged words)
+      const size_t rn = size_t(tp_) * c.hidden + 2 * size_t(tp_);
+      recv_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * rn));
+      check(cudaMemset(recv_, 0, sizeof(unsigned long long) * rn), "clear receive buffer");
       peers_dev_ = static_cast<unsigned long long**>(dalloc(sizeof(void*) * tp_));
     }
     row_m_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_)));
@@ -312,7 +317,8 @@ Model::~Model() {
   if (decode_graph_) cudaGraphDestroy(decode_graph_);  // graphs holding NCCL calls go before the comm
   if (batch_exec_) cudaGraphExecDestroy(batch_exec_);
   if (batch_graph_) cudaGraphDestroy(batch_graph_);
-  if (comm_) nccl().CommDestroy(comm_);
+  // a failed group is aborted, not destroyed: destroying waits for the other ranks
+  if (comm_) (tp_failed_ ? nccl().CommAbort : nccl().CommDestroy)(comm_);
   for (void* p : ipc_opened_) cudaIpcCloseMemHandle(p);
   if (cstream_) cudaStreamSynchronize(cstream_);
   for (void* p : allocs_) cudaFree(p);
@@ -673,7 +679,14 @@ void Model::enqueue_lm_head(int T, bool gen) {
             "sampler");
     ++launches_;
   }
-  if (gen && tp_ > 1) {
+  if (gen && tp_ > 1 && p2p_) {
+    // the argmax keys exchanged by peer stores too: a decode step then makes no NCCL
+    // call, so every wait on another rank in it is bounded
+    check(launch_tp_key_exchange(st_, peers_dev_, recv_, int(rank_), int(tp_), size_t(tp_) * cfg_.hidden, hist_,
+                                 pen_cnt_, stream_),
+          "argmax key exchange");
+    ++launches_;
+  } else if (gen && tp_ > 1) {
     check(launch_tp_pack_key(st_, tpkey_, stream_), "argmax key");
     const ncclResult_t r = nccl().AllReduce(tpkey_, tpkey_, 2, ncclUint64, ncclMax, comm_, stream_);
     if (r != ncclSuccess) throw WcbError(E_BACKEND, std::string("Backend error: ncclAllReduce: ") + nccl().GetErrorString(r));
@@ -726,7 +739,22 @@ void Model::tp_connect(const uint8_t* handles, uint32_t n) {
   }
 }
 
+void Model::tp_abort() {
+  tp_failed_ = true;
+  if (comm_) {
+    nccl().CommAbort(comm_);
+    comm_ = nullptr;
+  }
+}
+
+void Model::check_group() const {
+  if (tp_failed_)
+    throw WcbError(E_BACKEND, "Backend error: the tensor-parallel group has failed (a rank stopped or the group "
+                              "was aborted); free this model and load the group again");
+}
+
 void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logits_out) {
+  check_group();
   check(cudaSetDevice(device_), "cudaSetDevice");
   if (n == 0) throw WcbError(E_INVALID, "Invalid tensor shape: empty token sequence");
   if (kv_len_ + n > max_seq_)
@@ -757,6 +785,7 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
     // the tensor-parallel exchange (a rank stopped sending its partial sums)
     int err = 0;
     check(cudaMemcpy(&err, &st_->err, sizeof(int), cudaMemcpyDeviceToHost), "read state");
+    if (err & 16) tp_failed_ = true;  // the ranks' exchange epochs no longer agree
     if (err & 28)
       throw WcbError(E_BACKEND, std::string("Backend error: ") +
                                     (err & 16 ? "tensor-parallel exchange" : "decode step kernel") +
@@ -1000,6 +1029,7 @@ void Model::capture_decode_graph() {
 }
 
 void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
+  check_group();
   check(cudaSetDevice(device_), "cudaSetDevice");
   ++session_;
   sess_active_ = false;
@@ -1075,6 +1105,7 @@ void Model::sync_session_state() {
   kv_len_ = size_t(sess_state_.kv_len);
   if (sess_state_.err & 28) {
     sess_done_ = true;
+    if (sess_state_.err & 16) tp_failed_ = true;
     throw WcbError(E_BACKEND, std::string("Backend error: ") +
                                   (sess_state_.err & 16 ? "tensor-parallel exchange" : "decode step kernel") +
                                   ": a bounded wait expired (device error word " + std::to_string(sess_state_.err) +
@@ -1089,6 +1120,7 @@ void Model::sync_session_state() {
 
 std::vector<uint32_t> Model::next(size_t max_tokens, bool* finished) {
   if (!sess_active_) throw WcbError(E_INVALID, "Invalid argument: no active generation on this model");
+  check_group();
   check(cudaSetDevice(device_), "cudaSetDevice");
   std::vector<uint32_t> out;
   if (sess_host_) {
@@ -1310,6 +1342,7 @@ void Model::enqueue_batch_step(int B) {
 
 std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts, const size_t* lens, size_t n,
                                                          const GenParams& g) {
+  check_group();
   std::vector<std::vector<uint32_t>> out(n);
   const Sampler probe(g.seed, g.temperature, g.top_p, g.top_k, g.repetition_penalty);
   if (!batch_ok_ || !probe.greedy() || n < 2) {

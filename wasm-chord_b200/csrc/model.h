@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <cstdint>
 #include <memory>
 #include <string>
@@ -76,6 +77,11 @@ class Model {
   // handles of every rank's (in rank order) to write partial sums into peers
   void tp_ipc_handle(void* out) const;
   void tp_connect(const uint8_t* handles, uint32_t n);
+  // tensor parallelism: abandons the group after another rank failed (the
+  // caller's watchdog saw it stop): aborts the NCCL communicator, which ends any
+  // collective still waiting for that rank; every later call on this model fails.
+  // May be called from another thread while a call on this model is blocked.
+  void tp_abort();
   // kernels launched by one greedy decode step
   int launches_per_decode_step() const { return launches_per_step_; }
   // generate() for n independent sequences. Greedy decoding with room for
@@ -137,6 +143,8 @@ class Model {
   uint32_t ffn_l_ = 0;   // gate / up rows held and down input columns: ffn / tp
   uint32_t vocab_l_ = 0, vocab_off_ = 0;  // LM-head rows held and the first one's token id
   ncclComm_t comm_ = nullptr;
+  std::atomic<bool> tp_failed_{false};  // the group was aborted or a peer wait expired
+  void check_group() const;             // throws once the group has failed
   float* part_y_ = nullptr;                 // [t_max][hidden] partial o / down outputs
   unsigned long long* tpkey_ = nullptr;    // argmax key and NaN flag exchanged by the LM head
   // decode steps exchange o / down partial sums by stores into every rank's

@@ -35,6 +35,7 @@ const NcclApi& nccl() {
   api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(sym(h, "ncclGetUniqueId"));
   api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(sym(h, "ncclCommInitRank"));
   api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym(h, "ncclCommDestroy"));
+  api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(sym(h, "ncclCommAbort"));
   api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(sym(h, "ncclAllReduce"));
   api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym(h, "ncclGetErrorString"));
   ready = true;

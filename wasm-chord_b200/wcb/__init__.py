@@ -36,7 +36,7 @@ EXPORTED = [
     "wcb_next_token", "wcb_close_stream", "wcb_model_launches_per_step", "wcb_batch_info", "wcb_tokenizer_load", "wcb_tokenizer_free",
     "wcb_tokenizer_info", "wcb_tokenizer_set_special", "wcb_tokenize", "wcb_detokenize", "wcb_generate_text",
     "wcb_attention_dev",
-    "wcb_attention_dev_noalloc", "wcb_tp_id", "wcb_model_tp_handle", "wcb_model_tp_connect",
+    "wcb_attention_dev_noalloc", "wcb_tp_id", "wcb_model_tp_handle", "wcb_model_tp_connect", "wcb_model_tp_abort",
     "wcb_load_opts_init", "wcb_struct_layout",
 ]
 
@@ -142,6 +142,7 @@ def lib() -> C.CDLL:
     L.wcb_tp_id.argtypes = [vp]
     L.wcb_model_tp_handle.argtypes = [u32, vp]
     L.wcb_model_tp_connect.argtypes = [u32, vp, u32]
+    L.wcb_model_tp_abort.argtypes = [u32]
     L.wcb_load_opts_init.argtypes = [C.POINTER(_LoadOpts)]
     L.wcb_load_opts_init.restype = None
     L.wcb_struct_layout.argtypes = [C.c_char_p, C.c_char_p]
@@ -357,6 +358,12 @@ class Model:
         blob = b"".join(handles)
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         _check(lib().wcb_model_tp_connect(self._h, buf, len(handles)))
+
+    def tp_abort(self) -> None:
+        """Abandons this rank's tensor-parallel group after another rank failed
+        (ncclCommAbort); every later call on the model fails, close() does not wait
+        for the other ranks. Safe to call from a watchdog thread."""
+        _check(lib().wcb_model_tp_abort(self._h))
 
     def batch_info(self) -> Tuple[int, int]:
         """(KV slots of one batched decode step, kernels one batched step launches)."""
