@@ -127,3 +127,26 @@ def test_split_attention_matches_oracle(model_dir, gpu, kv):
     _close(p.forward([9], 250), q.forward([9], 250))
     p.close()
     q.close()
+
+
+def test_bounded_tag_wait_expires_into_an_error(tiny_gguf, gpu, monkeypatch):
+    """The persistent step's waits for other CTAs' data are bounded: with the outputs
+    of one phase withheld (a test hook: phase 3, layer 0's gate/up) and wait_ms = 200,
+    their consumers' waits run out and generate fails with BackendUnsupported naming
+    the expired wait within seconds, instead of hanging or returning tokens; with the
+    hook removed the same model generates the oracle's tokens again."""
+    import time
+    m = wcb.Model.load_from_gguf(tiny_gguf, wait_ms=200)
+    o = oracle.OracleModel(tiny_gguf)
+    prompt = synth.random_prompt(20, 512, seed=37).tolist()
+    cfg = wcb.GenerationConfig(max_tokens=8, temperature=0.0, repetition_penalty=1.0, eos_id=None)
+    monkeypatch.setenv("WCB_TEST_DROP_PHASE", "3")
+    t0 = time.time()
+    with pytest.raises(wcb.WcbError) as e:
+        m.generate_tokens(prompt, cfg)
+    assert e.value.code == 5 and "bounded wait expired" in e.value.message, e.value.message
+    assert time.time() - t0 < 10.0
+    monkeypatch.delenv("WCB_TEST_DROP_PHASE")
+    assert m.generate_tokens(prompt, cfg) == o.generate(prompt, 8, repetition_penalty=1.0, eos_id=None)
+    assert m.launches_per_step() == 1
+    m.close()

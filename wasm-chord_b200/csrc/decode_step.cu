@@ -502,7 +502,7 @@ __device__ __forceinline__ float pick4(const float (&v)[ROWS], int i) {
 __device__ __forceinline__ void group_epilogue(const MkArgs& a, const MkPart& P, int g, const float (&v)[ROWS],
                                                Ctx& c, const MkSmem& sm) {
   const int lane = threadIdx.x & 31;
-  if (lane >= ROWS) return;
+  if (lane >= ROWS || P.phase == a.drop_phase) return;  // drop_phase: a test withholds this phase's outputs
   const int i = lane;
   const int gi = ROWS * (g - c.g0);
   const float vi = pick4(v, i);

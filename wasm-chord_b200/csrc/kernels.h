@@ -239,6 +239,9 @@ struct MkArgs {
   const float* zero;         // [hidden] zeros: the embedding of an out-of-vocabulary id
   int att_smax;              // most key splits of a query head (set by decode_step_plan)
   int has_q6;                // a weight of the step is Q6_K (set by decode_step_plan)
+  // tests of the bounded waits: the outputs of this phase are never written, so the
+  // waits of its consumers run out (wait_ms) and the launch ends with an error (-1: none)
+  int drop_phase;
   int gen_mode;              // 1: token = hist[nhist - 1], penalty + argmax + bookkeeping
   const uint32_t* ids;       // gen_mode 0: token = ids[0]
   uint32_t* hist;

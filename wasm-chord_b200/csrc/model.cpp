@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 namespace wcb {
@@ -988,6 +989,9 @@ void Model::launch_decode_step_kernel(bool gen) {
   a.rope_sin = rope_sin_;
   a.gen_mode = gen ? 1 : 0;
   a.rep = rep_;
+  // test hook for the bounded waits (unset in normal use): withhold one phase's outputs
+  const char* drop = std::getenv("WCB_TEST_DROP_PHASE");
+  a.drop_phase = drop && *drop ? std::atoi(drop) : -1;
   check(launch_decode_step(a, mk_smem_, stream_), "decode step");
 }
 
