@@ -125,8 +125,12 @@ void wcb_gen_config_default(wcb_gen_config* cfg);
 
 /* Model::new + Model::load_from_gguf (model.rs:188, :364) from a GGUF file:
  * parses the header and config (gguf.rs:111-276), uploads raw Q4_K / Q6_K
- * blocks to HBM unchanged (Q6_K blocks padded from 210 to 224 bytes for 16-byte
- * alignment), allocates the device KV cache. */
+ * blocks (Q6_K padded from 210 to 224 bytes for 16-byte alignment) and F32 /
+ * F16 weights to HBM unchanged, allocates the device KV cache. Without an
+ * output.weight the LM head is the reference's weight tying,
+ * transpose_matrix(token embeddings, hidden, vocab) (model.rs:596-606). Models
+ * with F32 / F16 2-D weights run the per-op kernels (no persistent decode step,
+ * no batched decode step). */
 uint32_t wcb_model_load(const char* gguf_path, const wcb_load_opts* opts, uint32_t* out_handle);
 
 /* Releases a handle (wasmchord_free_model, abi.rs:95-108). */

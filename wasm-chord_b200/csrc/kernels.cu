@@ -114,6 +114,226 @@ __device__ void build_planes(const GemvArgs& a, const XPlanes& p) {
 __device__ void finish_sample(const GemvArgs& a) { finish_sample_state(a.st, a.hist, a.pen_cnt_w); }
 
 
+// Fused epilogue of output j (= row i * M + token t) of row group g: v is the
+// output, fin the group's 16 values (SwiGLU pairs a gate row with its up row,
+// RoPE a row with the next). Shared by the quantised and the dense GEMV.
+template <int M, int EPI>
+__device__ __forceinline__ void gemv_out(const GemvArgs& a, int g, int j, float v, const float* fin,
+                                         unsigned long long& best, int& nan) {
+  const int i = j / M, t = j % M;
+  const int tok = t;  // column within this launch
+  if (EPI == EPI_PEER) {
+    const int n = ROWS * g + i;
+    const unsigned long long w =
+        (static_cast<unsigned long long>(uint32_t(a.st->epoch) * 512u + uint32_t(a.peer_phase) + 1u) << 32) |
+        __float_as_uint(v);
+    for (int r = 0; r < a.tp_size; ++r)  // one 64-bit store per rank: value and tag arrive together
+      asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.peers[r] + size_t(a.tp_rank) * a.ldy + n),
+                   "l"(w)
+                   : "memory");
+  } else if (EPI == EPI_STORE) {
+    a.y[size_t(tok) * a.ldy + ROWS * g + i] = v;
+  } else if (EPI == EPI_RESID) {
+    const size_t off = size_t(tok) * a.ldy + ROWS * g + i;
+    a.y[off] = __fadd_rn(a.resid[size_t(tok) * a.ldr + ROWS * g + i], v);
+  } else if (EPI == EPI_SWIGLU) {
+    if (i < 2) {
+      const float gv = v, uv = fin[(i + 2) * M + t];
+      // ffn.rs:90-94: sigmoid = 1/(1+exp(-g)); silu = g*sigmoid; g = silu*u
+      const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+      a.y[size_t(tok) * a.ldy + 2 * g + i] = __fmul_rn(__fmul_rn(gv, sig), uv);
+    }
+  } else if (EPI == EPI_LMHEAD) {
+    const int n = ROWS * g + i;
+    const int tok_id = a.vocab_off + n;  // rows of this launch start at token vocab_off
+    a.y[n] = v;
+    if (a.gen_mode) {
+      float pv = v;
+      if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
+        const uint32_t cnt = a.pen_cnt[tok_id];
+        for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, a.rep) : __fmul_rn(pv, a.rep);
+      }
+      if (pv != pv) nan = 1;
+      else {
+        const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(tok_id);
+        best = key > best ? key : best;
+      }
+    }
+  } else {  // EPI_QKV
+    const int vr = a.row_offset + ROWS * g + i;
+    const int gtok = a.token_offset + tok;
+    const int pos = a.st->position + gtok;
+    const int slot_kv = a.st->kv_len + gtok;
+    const int hd = a.head_dim;
+    if (vr < a.hidden + a.kv_dim) {
+      // RoPE on (2i, 2i+1) pairs (attention.rs:230-262), cos/sin from the table
+      if ((i & 1) == 0) {
+        const float x0 = v, x1 = fin[(i + 1) * M + t];
+        const int col = vr < a.hidden ? vr : vr - a.hidden;
+        const int pi = (col % hd) >> 1;
+        const float cs = a.rope_cos[size_t(pos) * (hd / 2) + pi];
+        const float sn = a.rope_sin[size_t(pos) * (hd / 2) + pi];
+        const float n0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        const float n1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        if (vr < a.hidden) {
+          a.q[size_t(tok) * a.ldq + vr] = n0;
+          a.q[size_t(tok) * a.ldq + vr + 1] = n1;
+        } else {
+          const int kh = col / hd, dd = col % hd;
+          const size_t off = (size_t(kh) * a.max_seq + slot_kv) * hd + dd;
+          if (a.kv_half) {
+            reinterpret_cast<__half*>(a.kc)[off] = __float2half_rn(n0);
+            reinterpret_cast<__half*>(a.kc)[off + 1] = __float2half_rn(n1);
+          } else {
+            reinterpret_cast<float*>(a.kc)[off] = n0;
+            reinterpret_cast<float*>(a.kc)[off + 1] = n1;
+          }
+        }
+      }
+    } else {
+      const int col = vr - a.hidden - a.kv_dim;
+      const int kh = col / hd, dd = col % hd;
+      const size_t off = (size_t(kh) * a.max_seq + slot_kv) * hd + dd;
+      if (a.kv_half) reinterpret_cast<__half*>(a.vc)[off] = __float2half_rn(v);
+      else reinterpret_cast<float*>(a.vc)[off] = v;
+    }
+  }
+}
+
+// End of an LM-head launch in generate mode: CTA-wide max of the argmax keys,
+// one atomic per CTA; the last CTA to finish runs the sampler bookkeeping (no
+// CTA ever waits for another). GEMV_THREADS threads.
+__device__ __forceinline__ void lmhead_reduce(const GemvArgs& a, unsigned long long best, int nan) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+    best = ob > best ? ob : best;
+    nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+  }
+  __shared__ unsigned long long s_best[GEMV_WARPS];
+  __shared__ int s_nan[GEMV_WARPS];
+  if (lane == 0) {
+    s_best[warp] = best;
+    s_nan[warp] = nan;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    unsigned long long b = 0ull;
+    int n = 0;
+    for (int w = 0; w < GEMV_WARPS; ++w) {
+      b = s_best[w] > b ? s_best[w] : b;
+      n |= s_nan[w];
+    }
+    if (b) atomicMax(&a.st->best, b);
+    if (n) atomicOr(&a.st->nan, 1);
+    if (a.gen_mode == 1) {  // mode 2: the key is reduced over ranks before the bookkeeping
+      __threadfence();
+      const int prev = atomicAdd(&a.st->ticket, 1);
+      if (prev == int(gridDim.x) - 1) {
+        __threadfence();
+        finish_sample(a);
+      }
+    }
+  }
+}
+
+// Dense weights (GGUF F32 / F16, gguf.rs:446-467, stored as read): y = x W^T for
+// M <= 4 activation rows with the fused epilogues of the quantised GEMV. A CTA
+// takes two row groups (8 rows) at a time, one warp per weight row; the lanes
+// stride over 16-byte pieces of the row (coalesced) and read the activations
+// through L1, normalised on the fly as candle's rms_norm does (x / m * w, m =
+// sqrt(sum(x^2)/K + eps)). The dot products are fp32 like the reference's
+// matmul_transposed (gemm.rs:83-143), in a different order.
+template <int M, int PRO, int EPI, int DT>
+__global__ void __launch_bounds__(GEMV_THREADS) dense_gemv_kernel(const GemvArgs a) {
+  __shared__ float s_fin[2][16];
+  __shared__ float s_part[GEMV_WARPS];
+  __shared__ float s_m[4];
+  pdl_trigger();
+  pdl_wait();
+  if (a.st && a.st->done) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.K;
+  if (PRO == PRO_RMSNORM) {
+    for (int t = 0; t < M; ++t) {
+      const float* x = a.x + size_t(t) * a.ldx;
+      float ss = 0.0f;
+      for (int k = tid; k < K; k += GEMV_THREADS) ss = __fadd_rn(ss, __fmul_rn(x[k], x[k]));
+      ss = warp_sum(ss);
+      if (lane == 0) s_part[warp] = ss;
+      __syncthreads();
+      if (tid == 0) {
+        float tot = 0.0f;
+        for (int w = 0; w < GEMV_WARPS; ++w) tot = __fadd_rn(tot, s_part[w]);
+        s_m[t] = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(K)), a.eps));
+      }
+      __syncthreads();
+    }
+  }
+  constexpr int EPL = DT == DT_F32 ? 4 : 8;  // values in one 16-byte piece
+  const size_t row_bytes = size_t(K) * (DT == DT_F32 ? 4 : 2);
+  unsigned long long best = 0ull;
+  int nan = 0;
+  for (int gb = 2 * int(blockIdx.x); gb < a.ngroups; gb += 2 * int(gridDim.x)) {
+    const int gl = warp >> 2, i = warp & 3, g = gb + gl;
+    if (g < a.ngroups) {
+      const uint8_t* row;
+      if (EPI == EPI_SWIGLU) {
+        row = a.seg[i < 2 ? 0 : 1].w + size_t(2 * g + (i & 1)) * row_bytes;  // gate rows, then up rows
+      } else {
+        int vr = ROWS * g + i, sg = 0;
+        while (sg + 1 < a.nseg && vr >= a.seg[sg].rows) vr -= a.seg[sg++].rows;
+        row = a.seg[sg].w + size_t(vr) * row_bytes;
+      }
+      float acc[M];
+#pragma unroll
+      for (int t = 0; t < M; ++t) acc[t] = 0.0f;
+      for (int c = lane; c < K / EPL; c += 32) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(row) + c);
+        float w[EPL];
+        if (DT == DT_F32) {
+          w[0] = __uint_as_float(u.x);
+          w[1] = __uint_as_float(u.y);
+          w[2] = __uint_as_float(u.z);
+          w[3] = __uint_as_float(u.w);
+        } else {
+          const uint32_t h[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[e]));
+            w[(2 * e) % EPL] = f.x;
+            w[(2 * e + 1) % EPL] = f.y;
+          }
+        }
+        const int k = c * EPL;
+#pragma unroll
+        for (int t = 0; t < M; ++t) {
+          const float* x = a.x + size_t(t) * a.ldx + k;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            float xv = __ldg(x + e);
+            if (PRO == PRO_RMSNORM) xv = __fmul_rn(__fdiv_rn(xv, s_m[t]), __ldg(a.norm_w + k + e));
+            acc[t] = fmaf(w[e], xv, acc[t]);
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < M; ++t) {
+        const float v = warp_sum(acc[t]);
+        if (lane == 0) s_fin[gl][i * M + t] = v;
+      }
+    }
+    __syncthreads();
+    if (tid < 32) {
+      const int gl2 = tid >> 4, j = tid & 15, g2 = gb + gl2;
+      if (g2 < a.ngroups && j < ROWS * M) gemv_out<M, EPI>(a, g2, j, s_fin[gl2][j], s_fin[gl2], best, nan);
+    }
+    __syncthreads();
+  }
+  if (EPI == EPI_LMHEAD && a.gen_mode) lmhead_reduce(a, best, nan);
+}
+
 // Shared-memory layout of one GEMV CTA (sizes from the host, GemvArgs):
 //   [slot 0][slot 1]   weight stages: stage_groups groups of 4 rows, raw blocks
 //   [planes]           activation limbs (XPlanes)
@@ -282,87 +502,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, M == 1 ? 2 : 1) gemv_kernel(cons
     for (int o = tid; o < ng * 16; o += GEMV_THREADS) {
       const int gl = o >> 4, j = o & 15;
       if (j >= ROWS * M) continue;
-      const int g = gs + gl;
-      const int i = j / M, t = j % M;
-      const float v = sm.fin[o];
-      const float* fin = sm.fin + gl * 16;
-      const int tok = t;  // column within this launch
-      if (EPI == EPI_PEER) {
-        const int n = ROWS * g + i;
-        const unsigned long long w =
-            (static_cast<unsigned long long>(uint32_t(a.st->epoch) * 512u + uint32_t(a.peer_phase) + 1u) << 32) |
-            __float_as_uint(v);
-        for (int r = 0; r < a.tp_size; ++r)  // one 64-bit store per rank: value and tag arrive together
-          asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.peers[r] + size_t(a.tp_rank) * a.ldy + n),
-                       "l"(w)
-                       : "memory");
-      } else if (EPI == EPI_STORE) {
-        a.y[size_t(tok) * a.ldy + ROWS * g + i] = v;
-      } else if (EPI == EPI_RESID) {
-        const size_t off = size_t(tok) * a.ldy + ROWS * g + i;
-        a.y[off] = __fadd_rn(a.resid[size_t(tok) * a.ldr + ROWS * g + i], v);
-      } else if (EPI == EPI_SWIGLU) {
-        if (i < 2) {
-          const float gv = v, uv = fin[(i + 2) * M + t];
-          // ffn.rs:90-94: sigmoid = 1/(1+exp(-g)); silu = g*sigmoid; g = silu*u
-          const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
-          a.y[size_t(tok) * a.ldy + 2 * g + i] = __fmul_rn(__fmul_rn(gv, sig), uv);
-        }
-      } else if (EPI == EPI_LMHEAD) {
-        const int n = ROWS * g + i;
-        const int tok_id = a.vocab_off + n;  // rows of this launch start at token vocab_off
-        a.y[n] = v;
-        if (a.gen_mode) {
-          float pv = v;
-          if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
-            const uint32_t cnt = a.pen_cnt[tok_id];
-            for (uint32_t k = 0; k < cnt; ++k) pv = pv > 0.0f ? __fdiv_rn(pv, a.rep) : __fmul_rn(pv, a.rep);
-          }
-          if (pv != pv) nan = 1;
-          else {
-            const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(tok_id);
-            best = key > best ? key : best;
-          }
-        }
-      } else {  // EPI_QKV
-        const int vr = a.row_offset + ROWS * g + i;
-        const int gtok = a.token_offset + tok;
-        const int pos = a.st->position + gtok;
-        const int slot_kv = a.st->kv_len + gtok;
-        const int hd = a.head_dim;
-        if (vr < a.hidden + a.kv_dim) {
-          // RoPE on (2i, 2i+1) pairs (attention.rs:230-262), cos/sin from the table
-          if ((i & 1) == 0) {
-            const float x0 = v, x1 = fin[(i + 1) * M + t];
-            const int col = vr < a.hidden ? vr : vr - a.hidden;
-            const int pi = (col % hd) >> 1;
-            const float cs = a.rope_cos[size_t(pos) * (hd / 2) + pi];
-            const float sn = a.rope_sin[size_t(pos) * (hd / 2) + pi];
-            const float n0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-            const float n1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-            if (vr < a.hidden) {
-              a.q[size_t(tok) * a.ldq + vr] = n0;
-              a.q[size_t(tok) * a.ldq + vr + 1] = n1;
-            } else {
-              const int kh = col / hd, dd = col % hd;
-              const size_t off = (size_t(kh) * a.max_seq + slot_kv) * hd + dd;
-              if (a.kv_half) {
-                reinterpret_cast<__half*>(a.kc)[off] = __float2half_rn(n0);
-                reinterpret_cast<__half*>(a.kc)[off + 1] = __float2half_rn(n1);
-              } else {
-                reinterpret_cast<float*>(a.kc)[off] = n0;
-                reinterpret_cast<float*>(a.kc)[off + 1] = n1;
-              }
-            }
-          }
-        } else {
-          const int col = vr - a.hidden - a.kv_dim;
-          const int kh = col / hd, dd = col % hd;
-          const size_t off = (size_t(kh) * a.max_seq + slot_kv) * hd + dd;
-          if (a.kv_half) reinterpret_cast<__half*>(a.vc)[off] = __float2half_rn(v);
-          else reinterpret_cast<float*>(a.vc)[off] = v;
-        }
-      }
+      gemv_out<M, EPI>(a, gs + gl, j, sm.fin[o], sm.fin + gl * 16, best, nan);
     }
     __syncthreads();  // the slot, part and fin are free again
     if (tid == 0 && st + 2 < nstages) {
@@ -370,41 +510,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, M == 1 ? 2 : 1) gemv_kernel(cons
       issue_stage<EPI>(a, sm, slot, g_begin + (st + 2) * SG, min(g_end, g_begin + (st + 3) * SG), row_bytes);
     }
   }
-  if (EPI == EPI_LMHEAD && a.gen_mode) {
-    // CTA-wide max of the keys, one atomic per CTA; the last CTA to finish runs
-    // the sampler bookkeeping (no CTA ever waits for another)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
-      best = ob > best ? ob : best;
-      nan |= __shfl_xor_sync(0xffffffffu, nan, o);
-    }
-    __shared__ unsigned long long s_best[GEMV_WARPS];
-    __shared__ int s_nan[GEMV_WARPS];
-    if (lane == 0) {
-      s_best[warp] = best;
-      s_nan[warp] = nan;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      unsigned long long b = 0ull;
-      int n = 0;
-      for (int w = 0; w < GEMV_WARPS; ++w) {
-        b = s_best[w] > b ? s_best[w] : b;
-        n |= s_nan[w];
-      }
-      if (b) atomicMax(&a.st->best, b);
-      if (n) atomicOr(&a.st->nan, 1);
-      if (a.gen_mode == 1) {  // mode 2: the key is reduced over ranks before the bookkeeping
-        __threadfence();
-        const int prev = atomicAdd(&a.st->ticket, 1);
-        if (prev == int(gridDim.x) - 1) {
-          __threadfence();
-          finish_sample(a);
-        }
-      }
-    }
-  }
+  if (EPI == EPI_LMHEAD && a.gen_mode) lmhead_reduce(a, best, nan);
 }
 
 int g_sms = 0;
@@ -484,9 +590,24 @@ cudaError_t launch_gemv_t(const GemvArgs& a0, cudaStream_t s) {
   F(PRO_RMSNORM, EPI_STORE) \
   F(PRO_RMSNORM, EPI_LMHEAD)
 
+template <int M, int P, int E, int DT>
+cudaError_t launch_dense_t(const GemvArgs& a, cudaStream_t s) {
+  const int grid = std::max(1, std::min((a.ngroups + 1) / 2, 4 * (g_sms > 0 ? g_sms : 148)));
+  const cudaError_t e = launch_ex(dense_gemv_kernel<M, P, E, DT>, dim3(grid), dim3(GEMV_THREADS), 0, s, a.pdl != 0, a);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 template <int M>
 cudaError_t launch_gemv_m(const GemvArgs& a, int pro, int epi, cudaStream_t s) {
   const int dt = a.seg[0].dtype;
+  if (dt == DT_F32 || dt == DT_F16) {  // dense weights
+#define WCB_DENSE_CASE(P, E)                                                  \
+  if (pro == P && epi == E)                                                   \
+    return dt == DT_F32 ? launch_dense_t<M, P, E, DT_F32>(a, s) : launch_dense_t<M, P, E, DT_F16>(a, s);
+    WCB_GEMV_CASES(WCB_DENSE_CASE)
+#undef WCB_DENSE_CASE
+    return cudaErrorInvalidValue;
+  }
 #define WCB_GEMV_CASE(P, E)                                                  \
   if (pro == P && epi == E)                                                  \
     return dt == DT_Q4K ? launch_gemv_t<M, P, E, DT_Q4K>(a, s) : launch_gemv_t<M, P, E, DT_Q6K>(a, s);

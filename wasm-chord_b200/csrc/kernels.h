@@ -22,6 +22,8 @@ constexpr int QK_K = 256;
 constexpr int Q4K_BYTES = 144;
 constexpr int Q6K_BYTES = 210;
 constexpr int Q6K_DEV_BYTES = 224;
+constexpr int DT_F32 = 0;   // dense weights (GGUF types 0 / 1): per-op kernels only
+constexpr int DT_F16 = 1;
 constexpr int DT_Q4K = 12;
 constexpr int DT_Q6K = 14;
 
@@ -30,7 +32,11 @@ constexpr int DT_Q6K = 14;
 #else
 #define WCB_HD
 #endif
-WCB_HD inline size_t dev_block_bytes(int dtype) { return dtype == DT_Q4K ? Q4K_BYTES : Q6K_DEV_BYTES; }
+// bytes of 256 consecutive values of a row in device memory
+WCB_HD inline size_t dev_block_bytes(int dtype) {
+  return dtype == DT_Q4K ? Q4K_BYTES : dtype == DT_Q6K ? Q6K_DEV_BYTES : dtype == DT_F32 ? 1024 : 512;
+}
+WCB_HD inline bool dense_dtype(int dtype) { return dtype == DT_F32 || dtype == DT_F16; }
 
 // State shared by the kernels of one forward / decode step (device memory).
 struct StepState {

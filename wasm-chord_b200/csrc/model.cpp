@@ -142,14 +142,27 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     bool have_head = false;
     for (const char* n : {"output.weight", "lm_head.weight", "model.lm_head.weight"}) {
       const GgufTensor* t = f.find(n);
-      if (!t || (t->dtype != DT_Q4K && t->dtype != DT_Q6K)) continue;
+      if (!t || (t->dtype != DT_Q4K && t->dtype != DT_Q6K && !dense_dtype(int(t->dtype)))) continue;
       upload_weight(f, n, c.vocab, c.hidden, lm_head_, false, vocab_off_, vocab_l_);
       have_head = true;
       break;
     }
-    if (!have_head)
-      throw WcbError(E_BACKEND,
-                     "Backend error: the LM head must be a Q4_K or Q6_K tensor (tied embeddings are not supported)");
+    if (!have_head) {
+      // weight tying (model.rs:596-606): the LM head is transpose_matrix(token_embeddings,
+      // hidden, vocab), the embedding buffer read as a [hidden][vocab] matrix and
+      // transposed to [vocab][hidden] (model.rs:47-55); f32, this rank's vocabulary rows
+      const size_t H = c.hidden, V = c.vocab;
+      std::vector<float> e(H * V);
+      check(cudaMemcpy(e.data(), emb_, sizeof(float) * e.size(), cudaMemcpyDeviceToHost), "read embeddings");
+      std::vector<float> head(size_t(vocab_l_) * H);
+      for (size_t j = 0; j < vocab_l_; ++j)
+        for (size_t i = 0; i < H; ++i) head[j * H + i] = e[i * V + (vocab_off_ + j)];
+      lm_head_.dtype = DT_F32;
+      lm_head_.rows = vocab_l_;
+      lm_head_.cols = uint32_t(H);
+      lm_head_.ptr = static_cast<uint8_t*>(dalloc(sizeof(float) * head.size()));
+      check(cudaMemcpy(lm_head_.ptr, head.data(), sizeof(float) * head.size(), cudaMemcpyHostToDevice), "LM head");
+    }
 
     const uint32_t kvd = c.kv_heads * hd;
     layers_.resize(c.layers);
@@ -215,7 +228,7 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     // (with tensor parallelism: this rank's q / k / v / gate / up rows)
     bslots_ = !wstream_ ? std::min<uint32_t>(std::max<uint32_t>(opt.max_batch, 1), BATCH_MAX) : 1;
     batch_ok_ = bslots_ > 1 && c.hidden % BATCH_TILE == 0 && hq_ % BATCH_TILE == 0 && kvd_l_ % BATCH_TILE == 0 &&
-                ffn_l_ % 64 == 0 && c.heads / c.kv_heads <= 8;
+                ffn_l_ % 64 == 0 && c.heads / c.kv_heads <= 8 && !has_dense_weights();
     (void)kvd;
     if (!batch_ok_) bslots_ = 1;
     // KV cache (kv_cache.rs:6-34), [slot][L][n_kv][max_seq][hd]
@@ -368,11 +381,12 @@ void Model::upload_weight(const GgufFile& f, const std::string& name, uint32_t r
   if (t->numel != uint64_t(rows) * cols)
     throw WcbError(E_GENERIC, "tensor " + name + " has " + std::to_string(t->numel) + " elements, expected " +
                                   std::to_string(uint64_t(rows) * cols));
-  if (t->dtype != DT_Q4K && t->dtype != DT_Q6K)
-    throw WcbError(E_BACKEND, "Backend error: tensor " + name + " must be Q4_K or Q6_K (GGUF type " +
+  if (t->dtype != DT_Q4K && t->dtype != DT_Q6K && !dense_dtype(int(t->dtype)))
+    throw WcbError(E_BACKEND, "Backend error: tensor " + name + " must be F32, F16, Q4_K or Q6_K (GGUF type " +
                                   std::to_string(t->dtype) + ")");
   w.dtype = int(t->dtype);
-  const size_t bb = w.dtype == DT_Q4K ? Q4K_BYTES : Q6K_BYTES;
+  // bytes of 256 consecutive values as stored in the file
+  const size_t bb = w.dtype == DT_Q4K ? Q4K_BYTES : w.dtype == DT_Q6K ? Q6K_BYTES : dev_block_bytes(w.dtype);
   const size_t row_bytes = nb * bb, take = size_t(nblk) * bb;
   std::vector<uint8_t> raw(size_t(nrows) * take);
   if (take == row_bytes) {
@@ -381,7 +395,7 @@ void Model::upload_weight(const GgufFile& f, const std::string& name, uint32_t r
     for (uint32_t r = 0; r < nrows; ++r)  // a column slice: part of every row
       f.read_range(*t, size_t(row0 + r) * row_bytes + size_t(blk0) * bb, take, raw.data() + size_t(r) * take);
   }
-  if (w.dtype == DT_Q4K) {
+  if (w.dtype != DT_Q6K) {  // Q4_K, F32, F16: uploaded as read
     if (to_host) {
       to_stage(raw.data(), raw.size());
       return;
@@ -524,7 +538,7 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
     a.rep = rep_;
     a.hist = hist_;
     a.pdl = 1;
-    if (M >= TC_MIN_TOKENS && epi != EPI_LMHEAD && !(opt_.flags & 4)) {
+    if (M >= TC_MIN_TOKENS && epi != EPI_LMHEAD && !(opt_.flags & 4) && !dense_dtype(segs[s0].dtype)) {
       // prefill: one tensor-core GEMM over all M tokens
       GemvArgs b = a;
       b.M = M;
@@ -547,7 +561,7 @@ void Model::gemv(const DevWeight* segs, int nseg, int K, int M, const float* x, 
       s0 = s1;
       continue;
     }
-    const int mmax = epi == EPI_LMHEAD ? 1 : gemv_max_cols(K);
+    const int mmax = epi == EPI_LMHEAD ? 1 : dense_dtype(segs[s0].dtype) ? 4 : gemv_max_cols(K);
     for (int c0 = 0; c0 < M; c0 += mmax) {
       GemvArgs b = a;
       b.M = std::min(mmax, M - c0);
@@ -800,8 +814,8 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
 // head. Each phase waits on the counter of the phase whose output it reads.
 void Model::build_decode_step() {
   mk_ok_ = false;
-  // tensor parallelism and weight streaming run the per-op kernels
-  if ((opt_.flags & 8) || tp_ > 1 || wstream_) return;
+  // tensor parallelism, weight streaming and dense (F32 / F16) weights run the per-op kernels
+  if ((opt_.flags & 8) || tp_ > 1 || wstream_ || has_dense_weights()) return;
   if (decode_step_configure() != cudaSuccess) {
     cudaGetLastError();
     return;

@@ -131,6 +131,13 @@ class Model {
                  const float* norm_w, const float* sq_in, int sq_tiles, float eps, int epi, float* y, int ldy,
                  const float* resid, int ldr, float* sq_out, int layer);
   void build_decode_step();
+  bool has_dense_weights() const {  // F32 / F16 2-D weights (the per-op kernels only)
+    if (dense_dtype(lm_head_.dtype)) return true;
+    for (const DevLayer& L : layers_)
+      for (const DevWeight* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down})
+        if (dense_dtype(w->dtype)) return true;
+    return false;
+  }
   void launch_decode_step_kernel(bool gen);
 
   ModelConfig cfg_;

@@ -256,6 +256,8 @@ def _gen_tensor(index, name, ne, ggml_type, cfg: SynthConfig) -> bytes:
     vals = normal(cfg.seed, index, n, mean, cfg.weight_std)
     if ggml_type == GGML_F32:
         return vals.tobytes()
+    if ggml_type == GGML_F16:
+        return vals.astype(np.float16).tobytes()
     if ggml_type == GGML_Q4_K:
         return quantize_q4_k_fast(vals).tobytes()
     if ggml_type == GGML_Q6_K:
