@@ -46,6 +46,7 @@ constexpr int MK_THREADS = MK_T + 32;  // + the producer warp (16 warps: 128 reg
 constexpr int MK_MAX_K = 16384;     // longest GEMV input (limb planes in shared memory)
 constexpr int MK_MAX_TILES = 2048;  // tiles of one CTA per step (list kept in shared memory)
 constexpr int MK_GPT = 32;          // most groups in one tile
+constexpr int MK_SPLIT_G = 15;      // parts whose CTA share has fewer groups split K over the warps
 constexpr int MK_ANB = 8;          // attention: cache rows per lane in flight (K and V each)
 constexpr int MK_ASMAX = 4;        // most key splits of one query head
 
@@ -370,7 +371,7 @@ __device__ __forceinline__ void q6k_unit(const uint32_t (&ra)[ROWS], int b, int 
 //   [rsd]    residual rows of this CTA's o / down share
 //   [rope]   cos, sin of the step's position (head_dim / 2 each)
 //   [pen]    penalty counts of this CTA's LM-head rows
-//   [misc]   red[64] floats, flags[8]
+//   [misc]   red[64] floats, part[MK_SPLIT_G][8][4] floats, flags[8]
 //   [bars]   full[nslots]
 struct MkSmem {
   uint8_t* slots;
@@ -383,6 +384,7 @@ struct MkSmem {
   float* rsin;
   uint32_t* pen;
   float* red;
+  float* part;  // [MK_SPLIT_G][8][ROWS] partial sums of the 8-block chunks of a split part
   int* flags;  // [0] abort, [1] attention ticket result, [2] NaN seen
   uint64_t* full;
   uint64_t* empty;
@@ -390,7 +392,7 @@ struct MkSmem {
 
 // Byte offsets of the carve-up (host and device agree on them).
 struct MkOffsets {
-  size_t region, parts, tstart, tiles, rsd, rcos, rsin, pen, red, flags, full, empty, total;
+  size_t region, parts, tstart, tiles, rsd, rcos, rsin, pen, red, part, flags, full, empty, total;
 };
 
 __host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
@@ -415,6 +417,8 @@ __host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
   x += sizeof(uint32_t) * size_t(a.lm_rows);
   o.red = x;
   x += sizeof(float) * 64;
+  o.part = x;
+  x += sizeof(float) * MK_SPLIT_G * 8 * ROWS;
   o.flags = x;
   x += sizeof(int) * 8;
   x = (x + 7) / 8 * 8;
@@ -439,6 +443,7 @@ __device__ __forceinline__ MkSmem mk_carve(const MkArgs& a, uint8_t* b) {
   s.rsin = reinterpret_cast<float*>(b + o.rsin);
   s.pen = reinterpret_cast<uint32_t*>(b + o.pen);
   s.red = reinterpret_cast<float*>(b + o.red);
+  s.part = reinterpret_cast<float*>(b + o.part);
   s.flags = reinterpret_cast<int*>(b + o.flags);
   s.full = reinterpret_cast<uint64_t*>(b + o.full);
   s.empty = reinterpret_cast<uint64_t*>(b + o.empty);
@@ -648,6 +653,7 @@ __device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx&
   const uint32_t tag = c.tag0 + uint32_t(P.dep);
   float v[R][8], w[R][8];
   bool ok = true;
+  uint32_t pending = 0;  // bit 4 r + q: value pair q of round r still carries an older tag
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int k = r * MK_T * 8 + tid * 8;
@@ -667,15 +673,50 @@ __device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx&
         v[r][4] = x1.x; v[r][5] = x1.y; v[r][6] = x1.z; v[r][7] = x1.w;
       } else if (P.kind == MK_O && c.S > 1) {
         ok &= poll_att_merged(a, k, c.S, tag, v[r], skip, c.wait_ns);
-      } else {
-        ok &= poll_tagged<8>(src + k, tag, v[r], skip, c.wait_ns);
+      } else {  // first reads of every round issued together; the pairs not there yet are re-read below
+#pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) {
+          unsigned long long w0, w1;
+          ld_tag2(src + k + 2 * q2, w0, w1);
+          v[r][2 * q2] = val_of(w0);
+          v[r][2 * q2 + 1] = val_of(w1);
+          if (tag_of(w0) != tag || tag_of(w1) != tag) pending |= 1u << (4 * r + q2);
+        }
       }
-      if (stash)
+    }
+  }
+  if (pending && !skip) {  // bounded wait for the values of later producers
+    const unsigned long long t0 = gtime();
+    while (true) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) {
+          if (!(pending & (1u << (4 * r + q2)))) continue;
+          unsigned long long w0, w1;
+          ld_tag2(src + r * MK_T * 8 + tid * 8 + 2 * q2, w0, w1);
+          if (tag_of(w0) == tag && tag_of(w1) == tag) {
+            v[r][2 * q2] = val_of(w0);
+            v[r][2 * q2 + 1] = val_of(w1);
+            pending &= ~(1u << (4 * r + q2));
+          }
+        }
+      if (!pending) break;
+      if (gtime() - t0 > c.wait_ns) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  if (stash)
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int k = r * MK_T * 8 + tid * 8;
+      if (k < K)
 #pragma unroll
         for (int e = 0; e < 8; ++e)
           if (k + e >= c.R0 && k + e < R1) sm.rsd[k + e - c.R0] = v[r][e];
     }
-  }
   if (P.norm) {  // this warp's share of sum(x^2), summed over the warps after the caller's barrier
     float ss = 0.0f;
 #pragma unroll
@@ -1022,6 +1063,60 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
     const uint32_t row_bytes = uint32_t(NB * dev_block_bytes(P.dtype));
     const Planes pl = planes_at(smem_u32(sm.region), P.K);
     const int kend = sm.tstart[pi + 1];
+    if (NB > 8 && g1 - g0 < MK_SPLIT_G && P.kind != MK_LM) {
+      // Few groups of long rows (the down projection): whole-K units would leave most
+      // warps idle, so the units are (group, 8-block chunk), dealt round-robin to the
+      // warps; the chunks' partial sums meet in part and are added in chunk order.
+      const int CH = (NB + 7) / 8;
+      int gb = 0;  // CTA-local index of the tile's first group
+      for (; k < kend; ++k) {
+        const MkTile T = sm.tiles[k];
+        const int s = k % a.nslots, use = k / a.nslots;
+        if (!mbar_wait_n(sm.full + s, uint32_t(use & 1), abort_ ? 4096u : MK_MBAR_POLLS)) {
+          if (!abort_ && lane == 0) {
+            atomicOr(&st->err, 4);
+            sm.flags[0] = 1;
+          }
+          abort_ = true;
+        }
+        const uint32_t sbase = smem_u32(sm.slots + size_t(s) * a.slot_bytes);
+        for (int ul = (warp - (gb * CH) % MK_W + MK_W) % MK_W; ul < T.ng * CH; ul += MK_W) {
+          const int gl = ul / CH, b = (ul - gl * CH) * 8 + (lane & 7);
+          float acc[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
+          if (!abort_ && b < NB) {
+            uint32_t ra[ROWS];
+#pragma unroll
+            for (int i = 0; i < ROWS; ++i) {
+              const int ro = P.kind == MK_GU ? (i < 2 ? 2 * gl + i : 2 * T.ng + 2 * gl + (i - 2)) : ROWS * gl + i;
+              ra[i] = sbase + uint32_t(ro) * row_bytes;
+            }
+            if (!Q6 || P.dtype == DT_Q4K) q4k_unit(ra, b, lane >> 3, pl, acc);
+            else q6k_unit(ra, b, lane >> 3, pl, acc);
+          }
+#pragma unroll
+          for (int i = 0; i < ROWS; ++i) acc[i] = warp_sum(acc[i]);
+          if (lane == 0)
+#pragma unroll
+            for (int i = 0; i < ROWS; ++i) sm.part[((gb + gl) * 8 + (ul - gl * CH)) * ROWS + i] = acc[i];
+        }
+        gb += T.ng;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.empty + s);  // this warp is done with the slot
+      }
+      cbar();  // every chunk's partial sums are in part
+      for (int gl = warp; gl < g1 - g0; gl += MK_W) {
+        float v[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int ch = 0; ch < CH; ++ch)
+#pragma unroll
+          for (int i = 0; i < ROWS; ++i) v[i] += sm.part[(gl * 8 + ch) * ROWS + i];
+        if (P.norm)
+#pragma unroll
+          for (int i = 0; i < ROWS; ++i) v[i] = __fmul_rn(v[i], c.rm);
+        if (!abort_) group_epilogue(a, P, g0 + gl, v, c, sm);
+      }
+      cbar();  // part is free for the next split part
+      continue;
+    }
     for (; k < kend; ++k) {
       const MkTile T = sm.tiles[k];
       const int s = k % a.nslots, use = k / a.nslots;
