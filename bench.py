@@ -45,6 +45,13 @@ METRIC = "decode tok/s (TinyLlama-1.1B Q4_K, batch 1)"
 MODELS = {"tinyllama": ("TinyLlama-1.1B Q4_K", "tinyllama-1.1b-arch", 128),
           "llama7b": ("Llama-2-7B Q4_K_M", "llama-2-7b-arch", 512)}
 
+# DRAM bytes (read + write) of one decode_step_kernel launch from an ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum of the 5th decode step of
+# `bench.py --steps 16 --warmup 3 --no-cpu-baseline`) and the KV position of the captured step; the f32 KV rows read grow with the
+# position, so the figure is moved to the bench's mean position by the KV bytes
+# in between.
+NCU_STEP_TRAFFIC = {"tinyllama-1.1b-arch": (588723712 + 3977472, 133)}
+
 
 def peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
@@ -388,9 +395,17 @@ def run_ours(args, rank, world, dist):
         roofline = roofline_stream
     elif m.launches_per_step() == 1:
         # one persistent kernel per decode step: its bytes are the step's weights + KV reads
+        traffic = None
+        if arch in NCU_STEP_TRAFFIC:
+            cap_bytes, cap_pos = NCU_STEP_TRAFFIC[arch]
+            kv_row = 2 * cfg.num_layers * cfg.num_kv_heads * cfg.head_dim * 4
+            traffic = cap_bytes + kv_row * (avg_pos - cap_pos)
         roofline = {"bound": "hbm", "achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
-                    "traffic": None, "peak_kind": peak_kind, "kernel": "decode_step_kernel (persistent decode step)",
-                    "us_per_launch": ms_max / K * 1e3, "bytes_per_launch": step_bytes}
+                    "traffic": traffic, "peak_kind": peak_kind, "kernel": "decode_step_kernel (persistent decode step)",
+                    "us_per_launch": ms_max / K * 1e3, "bytes_per_launch": step_bytes,
+                    "traffic_note": None if traffic is None else
+                    "ncu DRAM read+write bytes of one launch at KV position %d, moved to the mean position %.1f by "
+                    "the f32 KV row bytes in between" % (NCU_STEP_TRAFFIC[arch][1], avg_pos)}
     elif roof is not None:
         roofline = {"bound": "hbm", "achieved": roof["achieved"], "peak": peak, "unit": "GB/s",
                     "frac": roof["achieved"] / peak, "traffic": None, "peak_kind": peak_kind,
