@@ -455,7 +455,8 @@ def run_tp(args, rank, world, dist):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     layers = args.layers
-    path = [synth.cached_model("llama70b", MODEL_DIR, num_layers=layers) if local == 0 else None]
+    path = [synth.cached_model("llama70b", MODEL_DIR, num_layers=layers, layer_period=2)
+            if local == 0 else None]
     if world > 1:
         dist.barrier()
         dist.broadcast_object_list(path, src=0)
@@ -505,6 +506,8 @@ def run_tp(args, rank, world, dist):
             "dtype": "f32 activations, Q4_K weights", "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K)",
             "config": {"workload": f"Llama-2-70B shape, {layers} of its 80 layers, greedy decode after a "
                                    f"{args.prompt}-token prompt", "layers": layers, "prompt_len": args.prompt,
+                       "weights": "two distinct layers' synthetic weights, repeated (every layer's bytes are read)",
+                       "persistent_step": m.launches_per_step() == 1,
                        "parallelism": f"tp{world} (partial sums of attn-out and ffn-down all-reduced by {exchange}; "
                                       "prefill: NCCL)",
                        "l2": "weights > 126 MB L2, no flush"},
@@ -530,7 +533,8 @@ def run_tp_batch(args, rank, world, dist):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     layers, B, P, K, W = args.layers, args.tp_batch, args.prompt, args.steps, args.warmup
-    path = [synth.cached_model("llama70b", MODEL_DIR, num_layers=layers) if local == 0 else None]
+    path = [synth.cached_model("llama70b", MODEL_DIR, num_layers=layers, layer_period=2)
+            if local == 0 else None]
     if world > 1:
         dist.barrier()
         dist.broadcast_object_list(path, src=0)

@@ -17,11 +17,12 @@ def _gpus():
     return torch.cuda.device_count()
 
 
-def _rank_main(rank, world, path, tp_id, prompt, q, port):
+def _rank_main(rank, world, path, tp_id, prompt, q, port, persistent=True):
     try:
         import torch
         torch.cuda.set_device(rank)
-        m = wcb.Model.load_from_gguf(path, device=rank, tp_rank=rank, tp_size=world, tp_id=tp_id)
+        m = wcb.Model.load_from_gguf(path, device=rank, tp_rank=rank, tp_size=world, tp_id=tp_id,
+                                     use_persistent=persistent)
         if port:  # decode steps exchange partial sums by peer stores (IPC handles over gloo)
             import torch.distributed as dist
             dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
@@ -34,8 +35,9 @@ def _rank_main(rank, world, path, tp_id, prompt, q, port):
         part = vocab // world
         cfg = wcb.GenerationConfig(max_tokens=40, temperature=0.0, repetition_penalty=1.1, eos_id=None)
         toks = m.generate_tokens(prompt, cfg)
+        steps = m.launches_per_step()
         m.close()
-        q.put((rank, logits[rank * part:(rank + 1) * part].copy(), toks, None))
+        q.put((rank, logits[rank * part:(rank + 1) * part].copy(), (toks, steps), None))
     except Exception as e:  # reported to the parent
         q.put((rank, None, None, repr(e)))
 
@@ -49,28 +51,26 @@ def _free_port():
     return port
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def _check_launches(res, world, exchange):
+    """Decode steps of a connected group run the persistent single-launch step;
+    NCCL-only groups and use_persistent=False run the per-op kernels."""
+    for r in range(world):
+        steps = res[r][1][1]
+        if exchange == "peer":
+            assert steps == 1, (r, steps)
+        else:
+            assert steps > 1, (r, steps)
+
+
+@pytest.mark.parametrize("exchange", ["nccl", "peer", "peer_per_op"])
 def test_tp2_matches_oracle(model_dir, gpu, exchange):
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
-    import torch.multiprocessing as mp
     path = synth.cached_model("tiny_tp", model_dir)
     prompt = synth.random_prompt(21, 1024, seed=40).tolist()
-    tp_id = wcb.tp_unique_id()
-    port = _free_port() if exchange == "peer" else 0
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, path, tp_id, prompt, q, port)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = {}
-    for _ in procs:
-        r, lg, toks, err = q.get(timeout=600)
-        res[r] = (lg, toks, err)
-    for p in procs:
-        p.join(timeout=120)
-    for r in range(2):
-        assert res[r][2] is None, res[r][2]
+    res = _run_ranks(2, path, prompt, exchange)
+    _check_launches(res, 2, exchange)
+    res = {r: (lg, toks[0], err) for r, (lg, toks, err) in res.items()}
     o = oracle.OracleModel(path)
     ref = o.forward(prompt, 0)
     got = np.concatenate([res[0][0], res[1][0]])
@@ -128,10 +128,11 @@ def test_tp2_batched_decode_matches_oracle(model_dir, gpu):
 def _run_ranks(world, path, prompt, exchange):
     import torch.multiprocessing as mp
     tp_id = wcb.tp_unique_id()
-    port = _free_port() if exchange == "peer" else 0
+    port = _free_port() if exchange.startswith("peer") else 0
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, path, tp_id, prompt, q, port)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, path, tp_id, prompt, q, port, exchange != "peer_per_op"))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -145,16 +146,20 @@ def _run_ranks(world, path, prompt, exchange):
     return res
 
 
-@pytest.mark.parametrize("world,exchange", [(2, "nccl"), (2, "peer"), (4, "peer"), (8, "peer")])
+@pytest.mark.parametrize("world,exchange", [(2, "nccl"), (2, "peer"), (2, "peer_per_op"), (4, "peer"),
+                                            (8, "peer")])
 def test_tp_70b_width_matches_oracle(model_dir, gpu, world, exchange):
     """The Llama-2-70B widths (hidden 8192, 64 / 8 heads, head_dim 128, FFN 28672),
-    one layer, split over 2 / 4 / 8 ranks: every rank's logits slice within the
-    tolerance and 40 greedy tokens identical to the oracle."""
+    two layers, split over 2 / 4 / 8 ranks: every rank's logits slice within the
+    tolerance and 40 greedy tokens identical to the oracle, through the persistent
+    single-launch decode step (peer exchange) and the per-op kernels."""
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
-    path = synth.cached_model("llama70b", model_dir, num_layers=1, context_length=1024)
+    path = synth.cached_model("llama70b", model_dir, num_layers=2, context_length=1024)
     prompt = synth.random_prompt(33, 32000, seed=41).tolist()
     res = _run_ranks(world, path, prompt, exchange)
+    _check_launches(res, world, exchange)
+    res = {r: (lg, toks[0], err) for r, (lg, toks, err) in res.items()}
     import os
     oracle.set_threads(os.cpu_count() or 1, os.cpu_count() or 1)
     o = oracle.OracleModel(path)

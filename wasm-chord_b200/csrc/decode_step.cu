@@ -44,7 +44,6 @@ constexpr int MK_W = 15;            // consumer warps per CTA
 constexpr int MK_T = MK_W * 32;     // consumer threads per CTA
 constexpr int MK_THREADS = MK_T + 32;  // + the producer warp (16 warps: 128 registers a thread)
 constexpr int MK_MAX_K = 16384;     // longest GEMV input (limb planes in shared memory)
-constexpr int MK_MAX_TILES = 2048;  // tiles of one CTA per step (list kept in shared memory)
 constexpr int MK_GPT = 32;          // most groups in one tile
 constexpr int MK_SPLIT_G = 15;      // parts whose CTA share has fewer groups split K over the warps
 constexpr int MK_ANB = 8;          // attention: cache rows per lane in flight (K and V each)
@@ -82,6 +81,22 @@ __device__ __forceinline__ void ld_tag2(const unsigned long long* p, unsigned lo
 }
 __device__ __forceinline__ uint32_t tag_of(unsigned long long w) { return uint32_t(w >> 32); }
 __device__ __forceinline__ float val_of(unsigned long long w) { return __uint_as_float(uint32_t(w)); }
+
+// Tensor parallelism: words written by other GPUs (peer stores over NVLink) are
+// read and written at system scope.
+__device__ __forceinline__ unsigned long long ld_sys(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ void st_sys(unsigned long long* p, unsigned long long w) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// first word of rank r's partial sums of the o (kd 0) or down (kd 1) projection of
+// `layer` in an exchange buffer; consecutive layers alternate between two copies
+__device__ __forceinline__ size_t xslot(const MkArgs& a, int kd, int layer, int r) {
+  return a.xofs + ((size_t(kd) * 2 + size_t(layer & 1)) * size_t(a.tp_size) + size_t(r)) * size_t(a.hidden);
+}
 
 // Reads N (even; 16-byte aligned start) tagged values, spinning until every
 // one carries `tag`; false when the bound expires. skip: read once, no wait.
@@ -366,8 +381,7 @@ __device__ __forceinline__ void q6k_unit(const uint32_t (&ra)[ROWS], int b, int 
 // Shared-memory carve-up of one CTA (sizes in MkArgs, set on the host):
 //   [slots]  nslots x slot_bytes weight tiles
 //   [region] limb planes (GEMV phases) or attention staging
-//   [parts]  the part list; [tstart] this CTA's first tile of each part
-//   [tiles]  this CTA's tile list (8 bytes a tile)
+//   [parts]  the part list
 //   [rsd]    residual rows of this CTA's o / down share
 //   [rope]   cos, sin of the step's position (head_dim / 2 each)
 //   [pen]    penalty counts of this CTA's LM-head rows
@@ -377,8 +391,6 @@ struct MkSmem {
   uint8_t* slots;
   uint8_t* region;
   MkPart* parts;
-  int* tstart;
-  MkTile* tiles;
   float* rsd;
   float* rcos;
   float* rsin;
@@ -392,7 +404,7 @@ struct MkSmem {
 
 // Byte offsets of the carve-up (host and device agree on them).
 struct MkOffsets {
-  size_t region, parts, tstart, tiles, rsd, rcos, rsin, pen, red, part, flags, full, empty, total;
+  size_t region, parts, rsd, rcos, rsin, pen, red, part, flags, full, empty, total;
 };
 
 __host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
@@ -402,11 +414,6 @@ __host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
   x += a.region_bytes;
   o.parts = x;
   x += sizeof(MkPart) * size_t(a.nparts);
-  o.tstart = x;
-  x += sizeof(int) * size_t(a.nparts + 1);
-  x = (x + 7) / 8 * 8;
-  o.tiles = x;
-  x += sizeof(MkTile) * size_t(a.max_tiles);
   o.rsd = x;
   x += sizeof(float) * size_t(a.res_rows);
   o.rcos = x;
@@ -436,8 +443,6 @@ __device__ __forceinline__ MkSmem mk_carve(const MkArgs& a, uint8_t* b) {
   s.slots = b;
   s.region = b + o.region;
   s.parts = reinterpret_cast<MkPart*>(b + o.parts);
-  s.tstart = reinterpret_cast<int*>(b + o.tstart);
-  s.tiles = reinterpret_cast<MkTile*>(b + o.tiles);
   s.rsd = reinterpret_cast<float*>(b + o.rsd);
   s.rcos = reinterpret_cast<float*>(b + o.rcos);
   s.rsin = reinterpret_cast<float*>(b + o.rsin);
@@ -484,6 +489,29 @@ __device__ void issue_tile(const MkPart* Pp, const MkTile& T, uint8_t* dst, uint
   }
 }
 
+// Cursor over one CTA's tiles in consumption order: part by part, gpt groups of
+// the CTA's share of each part at a time (attention parts have no weights).
+struct TileCursor {
+  int pi, g, g1;  // part, next group, end of the CTA's share of the part
+};
+
+__device__ __forceinline__ bool next_tile(const MkPart* parts, int nparts, TileCursor& t, MkTile& T) {
+  while (t.g >= t.g1) {
+    if (++t.pi >= nparts) return false;
+    if (parts[t.pi].kind == MK_ATT) {
+      t.g = t.g1 = 0;
+      continue;
+    }
+    cta_share(parts[t.pi].ngroups, blockIdx.x, gridDim.x, t.g, t.g1);
+  }
+  const int gpt = parts[t.pi].gpt;
+  T.g = uint16_t(t.g);
+  T.part = uint16_t(t.pi);
+  T.ng = uint8_t(min(gpt, t.g1 - t.g));
+  t.g += gpt;
+  return true;
+}
+
 // Per-launch values every thread keeps.
 struct Ctx {
   uint32_t tag0;  // epoch * 1024 + 1: tag of phase p is tag0 + p
@@ -513,7 +541,7 @@ __device__ __forceinline__ void group_epilogue(const MkArgs& a, const MkPart& P,
   const float vi = pick4(v, i);
   const uint32_t tag = c.tag0 + uint32_t(P.phase);
   if (P.kind == MK_QKV) {
-    const int hid = a.hidden, hd = a.head_dim, kvd = a.n_kv * a.head_dim;
+    const int hid = a.qdim, hd = a.head_dim, kvd = a.n_kv * a.head_dim;
     const int vr = P.row_offset + ROWS * g + i;
     const size_t esz = a.kv_half ? 2 : 4;
     if (vr < hid + kvd) {
@@ -558,19 +586,24 @@ __device__ __forceinline__ void group_epilogue(const MkArgs& a, const MkPart& P,
       st_tag(a.vnew + col, vv, tag);
     }
     (void)esz;
-  } else if (P.kind == MK_O) {  // attention out + residual (layer.rs:68)
+  } else if (P.kind == MK_O || P.kind == MK_D) {  // attention / FFN out + residual (layer.rs:68, :86)
     const int r = ROWS * g + i;
-    st_tag(a.xb + r, __fadd_rn(sm.rsd[r - c.R0], vi), tag);
-  } else if (P.kind == MK_D) {  // FFN out + residual (layer.rs:86)
-    const int r = ROWS * g + i;
-    st_tag(a.xa + r, __fadd_rn(sm.rsd[r - c.R0], vi), tag);
+    if (a.tp_size > 1) {
+      // this rank's partial sum (its heads / FFN rows) to slot tp_rank of every rank;
+      // the owner of row r adds the residual when the next phase builds its input
+      const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(vi);
+      const size_t off = xslot(a, P.kind == MK_D, P.phase / 5, a.tp_rank) + size_t(r);
+      for (int rr = 0; rr < a.tp_size; ++rr) st_sys(a.peers[rr] + off, w);
+    } else {
+      st_tag((P.kind == MK_O ? a.xb : a.xa) + r, __fadd_rn(sm.rsd[r - c.R0], vi), tag);
+    }
   } else if (P.kind == MK_GU) {  // ffn.rs:90-94: silu(g) * u
     if (i < 2) {
       const float gv = vi, uv = pick4(v, i + 2);
       const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
       st_tag(a.act + 2 * g + i, __fmul_rn(__fmul_rn(gv, sig), uv), tag);
     }
-  } else {  // MK_LM
+  } else {  // MK_LM (rows of this rank's vocabulary slice)
     const int n = ROWS * g + i;
     a.logits[n] = vi;
     if (a.gen_mode) {
@@ -581,7 +614,8 @@ __device__ __forceinline__ void group_epilogue(const MkArgs& a, const MkPart& P,
       }
       if (pv != pv) c.nan = 1;
       else {
-        const unsigned long long key = (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(n);
+        const unsigned long long key =
+            (static_cast<unsigned long long>(order_key(pv)) << 32) | uint32_t(a.vocab_off + n);
         c.best = key > c.best ? key : c.best;
       }
     }
@@ -615,6 +649,42 @@ __device__ __forceinline__ bool poll_att_merged(const MkArgs& a, int k, int S, u
   return ok;
 }
 
+// Tensor parallelism: this CTA's rows of the residual stream are the previous
+// residual (stashed in rsd) plus every rank's partial sum of the o (kd 0) or down
+// (kd 1) projection of phase `dep`, added in rank order as the per-op exchange does
+// (the same sum on every rank); they are published for all CTAs under the
+// producing phase's tag. Kept out of line (arguments by value): it runs once per
+// phase and would add to the register pressure of the input build. xr: rank 0's
+// partial sums in this rank's exchange buffer. False when a wait expired.
+__device__ __noinline__ bool tp_residual_rows(const unsigned long long* xr, unsigned long long* dst, int hidden,
+                                              int tp, uint32_t tag, int R0, const float* rsd, bool skip,
+                                              unsigned long long wait_ns, StepState* st) {
+  int h0, h1;
+  cta_share(hidden / ROWS, blockIdx.x, gridDim.x, h0, h1);
+  bool ok = true;
+  for (int j = ROWS * h0 + int(threadIdx.x); j < ROWS * h1; j += MK_T) {
+    float sum = 0.0f;
+    for (int r = 0; r < tp; ++r) {
+      const unsigned long long* p = xr + size_t(r) * hidden + j;
+      unsigned long long wv = ld_sys(p);
+      if (tag_of(wv) != tag && !skip) {  // bounded: a rank that stopped ends the step with an error
+        const unsigned long long t0 = gtime();
+        while (tag_of(wv) != tag) {
+          if (gtime() - t0 > wait_ns) {
+            atomicOr(&st->err, 16);
+            ok = false;
+            break;
+          }
+          wv = ld_sys(p);
+        }
+      }
+      sum = __fadd_rn(sum, val_of(wv));
+    }
+    st_tag(dst + j, __fadd_rn(rsd[j - R0], sum), tag);
+  }
+  return ok;
+}
+
 // Input planes of the phase starting at part pi (R rounds of MK_T * 8 values).
 // With P.norm the planes hold x * w and each warp leaves its share of sum(x^2)
 // in red[]: candle's rms_norm (candle_tensor_backend.rs:30-57), x / m * w with
@@ -634,7 +704,7 @@ __device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx&
   if (P.kind == MK_LM) {
     int g0, g1;
     cta_share(P.ngroups, blockIdx.x, gridDim.x, g0, g1);
-    for (int r = tid; r < ROWS * (g1 - g0); r += MK_T) sm.pen[r] = __ldg(a.pen_cnt + ROWS * g0 + r);
+    for (int r = tid; r < ROWS * (g1 - g0); r += MK_T) sm.pen[r] = __ldg(a.pen_cnt + a.vocab_off + ROWS * g0 + r);
   }
   const unsigned long long* src = nullptr;
   const float* plain = nullptr;
@@ -651,8 +721,12 @@ __device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx&
   const bool stash = P.kind == MK_QKV || P.kind == MK_GU;  // residual of the o / down share
   const int R1 = c.R0 + a.res_rows;
   const uint32_t tag = c.tag0 + uint32_t(P.dep);
-  float v[R][8], w[R][8];
   bool ok = true;
+  if (a.tp_size > 1 && (P.kind == MK_GU || P.kind == MK_LM || (P.kind == MK_QKV && P.dep >= 0)))
+    ok = tp_residual_rows(a.peers[a.tp_rank] + xslot(a, P.kind == MK_GU ? 0 : 1, P.dep / 5, 0),
+                          P.kind == MK_GU ? a.xb : a.xa, a.hidden, a.tp_size, tag, c.R0, sm.rsd, skip, c.wait_ns,
+                          a.st);
+  float v[R][8], w[R][8];
   uint32_t pending = 0;  // bit 4 r + q: value pair q of round r still carries an older tag
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -949,6 +1023,48 @@ __device__ __forceinline__ void attention_phase(const MkArgs& a, const MkSmem& s
   mk_attention<HD, KT>(a, sm, P.phase / 5, h, s, S, j0, j1, c, qtag, otag);
 }
 
+// Tensor parallelism, end of a generate step (the last CTA of each rank): the
+// rank's argmax key (order-preserving logit bits | token id, NaN flag in bit 31 of
+// the low word) goes to slot tp_rank of every rank's key words, then the ranks'
+// keys are max-reduced (the same result on every rank). Bounded: a rank that
+// stopped ends the generate loop with error 16. keys: offset (words) of the key
+// words in each exchange buffer.
+__device__ __noinline__ bool exchange_keys(StepState* st, unsigned long long* const* peers, size_t keys, int rank,
+                                           int tp, uint32_t tag0, unsigned long long wait_ns) {
+  const unsigned long long tag = static_cast<unsigned long long>(tag0 + 1023u) << 32;  // no phase has this tag
+  const unsigned long long best = atomicExch(&st->best, 0ull);
+  const int nan = atomicExch(&st->nan, 0);
+  const uint32_t hi = uint32_t(best >> 32), lo = (uint32_t(best) & 0x7FFFFFFFu) | (nan ? 0x80000000u : 0u);
+  for (int r = 0; r < tp; ++r) {  // one 64-bit store per word: value and tag arrive together
+    st_sys(peers[r] + keys + 2 * size_t(rank), tag | hi);
+    st_sys(peers[r] + keys + 2 * size_t(rank) + 1, tag | lo);
+  }
+  const unsigned long long* own = peers[rank] + keys;
+  unsigned long long kmax = 0ull;
+  int n = 0;
+  const unsigned long long t0 = gtime();
+  for (int r = 0; r < tp; ++r) {
+    unsigned long long x, y;
+    while (true) {
+      x = ld_sys(own + 2 * r);
+      y = ld_sys(own + 2 * r + 1);
+      if ((x >> 32) == (tag >> 32) && (y >> 32) == (tag >> 32)) break;
+      if (gtime() - t0 > wait_ns) {
+        atomicOr(&st->err, 16);
+        st->ticket = 0;
+        st->done = 1;
+        return false;
+      }
+    }
+    const unsigned long long k = ((x & 0xFFFFFFFFull) << 32) | (y & 0x7FFFFFFFull);
+    kmax = k > kmax ? k : kmax;
+    n |= int((y >> 31) & 1u);
+  }
+  st->best = kmax;
+  st->nan = n;
+  return true;
+}
+
 // One instantiation per (head_dim, KV cache type, Q6_K weights present), so a
 // kernel carries only the code its model runs.
 template <int HD, typename KT, bool Q6>
@@ -959,26 +1075,22 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
   const int cta = blockIdx.x;
   StepState* st = a.st;
   if (st->done) return;  // the generate loop has ended: every CTA returns at once
-  const int ntiles = __ldg(a.tile_start + size_t(cta) * (a.nparts + 1) + a.nparts);
-  const MkTile* gtiles = a.tiles + size_t(cta) * a.max_tiles;
-  if (tid == MK_T) {  // producer lane: barriers, then the first tiles straight from the global list
+  TileCursor cur{-1, 0, 0};  // the producer lane's next tile
+  int kp = 0;                // tiles the producer lane has issued
+  if (tid == MK_T) {  // producer lane: barriers, then the first tiles straight from the global part list
     for (int s = 0; s < a.nslots; ++s) {
       mbar_init(sm.full + s, 1);
       mbar_init(sm.empty + s, MK_W);
     }
     mbar_fence_init();
-    for (int k = 0; k < a.nslots && k < ntiles; ++k) {
-      const MkTile T = gtiles[k];
-      issue_tile(a.parts + T.part, T, sm.slots + size_t(k) * a.slot_bytes, sm.full + k);
-    }
+    MkTile T;
+    for (; kp < a.nslots && next_tile(a.parts, a.nparts, cur, T); ++kp)
+      issue_tile(a.parts + T.part, T, sm.slots + size_t(kp) * a.slot_bytes, sm.full + kp);
   }
-  for (int i = tid; i < ntiles; i += MK_THREADS) sm.tiles[i] = gtiles[i];
   {
     const int4* src = reinterpret_cast<const int4*>(a.parts);
     int4* dst = reinterpret_cast<int4*>(sm.parts);
     for (int i = tid; i < a.nparts * int(sizeof(MkPart) / 16); i += MK_THREADS) dst[i] = src[i];
-    for (int i = tid; i <= a.nparts; i += MK_THREADS)
-      sm.tstart[i] = a.tile_start[size_t(cta) * (a.nparts + 1) + i];
   }
   if (tid < 8) sm.flags[tid] = 0;
   for (int i = tid; i < a.head_dim / 2; i += MK_THREADS) {  // cos / sin of this step's position (attention.rs:230-248)
@@ -1005,14 +1117,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
   __syncthreads();
   if (warp == MK_W) {  // ---- producer: refill each slot once the consumer warps have left it
     if (lane != 0) return;
-    for (int k = a.nslots; k < ntiles; ++k) {
-      const int s = k % a.nslots, use = k / a.nslots;
+    MkTile T;
+    for (; next_tile(sm.parts, a.nparts, cur, T); ++kp) {
+      const int s = kp % a.nslots, use = kp / a.nslots;
       if (!mbar_wait_n(sm.empty + s, uint32_t((use - 1) & 1), MK_MBAR_POLLS)) {
         atomicOr(&st->err, 4);  // the consumers stopped taking tiles
         return;
       }
       fence_proxy_async();
-      const MkTile T = sm.tiles[k];
       issue_tile(sm.parts + T.part, T, sm.slots + size_t(s) * a.slot_bytes, sm.full + s);
     }
     return;
@@ -1062,15 +1174,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
     const int NB = P.K / QK_K;
     const uint32_t row_bytes = uint32_t(NB * dev_block_bytes(P.dtype));
     const Planes pl = planes_at(smem_u32(sm.region), P.K);
-    const int kend = sm.tstart[pi + 1];
+    const int gpt = P.gpt;
     if (NB > 8 && g1 - g0 < MK_SPLIT_G && P.kind != MK_LM) {
       // Few groups of long rows (the down projection): whole-K units would leave most
       // warps idle, so the units are (group, 8-block chunk), dealt round-robin to the
       // warps; the chunks' partial sums meet in part and are added in chunk order.
       const int CH = (NB + 7) / 8;
       int gb = 0;  // CTA-local index of the tile's first group
-      for (; k < kend; ++k) {
-        const MkTile T = sm.tiles[k];
+      for (int tg = g0; tg < g1; tg += gpt, ++k) {
+        const int tng = min(gpt, g1 - tg);
         const int s = k % a.nslots, use = k / a.nslots;
         if (!mbar_wait_n(sm.full + s, uint32_t(use & 1), abort_ ? 4096u : MK_MBAR_POLLS)) {
           if (!abort_ && lane == 0) {
@@ -1080,14 +1192,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
           abort_ = true;
         }
         const uint32_t sbase = smem_u32(sm.slots + size_t(s) * a.slot_bytes);
-        for (int ul = (warp - (gb * CH) % MK_W + MK_W) % MK_W; ul < T.ng * CH; ul += MK_W) {
+        for (int ul = (warp - (gb * CH) % MK_W + MK_W) % MK_W; ul < tng * CH; ul += MK_W) {
           const int gl = ul / CH, b = (ul - gl * CH) * 8 + (lane & 7);
           float acc[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
           if (!abort_ && b < NB) {
             uint32_t ra[ROWS];
 #pragma unroll
             for (int i = 0; i < ROWS; ++i) {
-              const int ro = P.kind == MK_GU ? (i < 2 ? 2 * gl + i : 2 * T.ng + 2 * gl + (i - 2)) : ROWS * gl + i;
+              const int ro = P.kind == MK_GU ? (i < 2 ? 2 * gl + i : 2 * tng + 2 * gl + (i - 2)) : ROWS * gl + i;
               ra[i] = sbase + uint32_t(ro) * row_bytes;
             }
             if (!Q6 || P.dtype == DT_Q4K) q4k_unit(ra, b, lane >> 3, pl, acc);
@@ -1099,7 +1211,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
 #pragma unroll
             for (int i = 0; i < ROWS; ++i) sm.part[((gb + gl) * 8 + (ul - gl * CH)) * ROWS + i] = acc[i];
         }
-        gb += T.ng;
+        gb += tng;
         __syncwarp();
         if (lane == 0) mbar_arrive(sm.empty + s);  // this warp is done with the slot
       }
@@ -1117,8 +1229,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       cbar();  // part is free for the next split part
       continue;
     }
-    for (; k < kend; ++k) {
-      const MkTile T = sm.tiles[k];
+    for (int tg = g0; tg < g1; tg += gpt, ++k) {
+      const int tng = min(gpt, g1 - tg);
       const int s = k % a.nslots, use = k / a.nslots;
       // every consumer warp waits for every tile and arrives on its slot
       if (!mbar_wait_n(sm.full + s, uint32_t(use & 1), abort_ ? 4096u : MK_MBAR_POLLS)) {
@@ -1130,13 +1242,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       }
       const uint32_t sbase = smem_u32(sm.slots + size_t(s) * a.slot_bytes);
       // one group (4 rows, whole K) per warp; lane = (pair lane / 8, block lane % 8 + 8 j)
-      for (int u = (warp - U % MK_W + MK_W) % MK_W; u < T.ng; u += MK_W) {
+      for (int u = (warp - U % MK_W + MK_W) % MK_W; u < tng; u += MK_W) {
         float acc[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (!abort_) {
           uint32_t ra[ROWS];
 #pragma unroll
           for (int i = 0; i < ROWS; ++i) {
-            const int ro = P.kind == MK_GU ? (i < 2 ? 2 * u + i : 2 * T.ng + 2 * u + (i - 2)) : ROWS * u + i;
+            const int ro = P.kind == MK_GU ? (i < 2 ? 2 * u + i : 2 * tng + 2 * u + (i - 2)) : ROWS * u + i;
             ra[i] = sbase + uint32_t(ro) * row_bytes;
           }
           if (!Q6 || P.dtype == DT_Q4K)
@@ -1150,9 +1262,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
         if (P.norm)
 #pragma unroll
           for (int i = 0; i < ROWS; ++i) v[i] = __fmul_rn(v[i], c.rm);
-        if (!abort_) group_epilogue(a, P, T.g + u, v, c, sm);
+        if (!abort_) group_epilogue(a, P, tg + u, v, c, sm);
       }
-      U += T.ng;
+      U += tng;
       // leave the slot: the producer refills it with the tile nslots further on
       __syncwarp();
       if (lane == 0) mbar_arrive(sm.empty + s);
@@ -1184,9 +1296,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       const int prev = atomicAdd(&st->ticket, 1);
       if (prev == int(gridDim.x) - 1) {
         __threadfence();
+        const bool ok = !(a.gen_mode && a.tp_size > 1) ||
+                        exchange_keys(st, a.peers, a.xofs + 4 * size_t(a.tp_size) * size_t(a.hidden), a.tp_rank,
+                                      a.tp_size, c.tag0, c.wait_ns);
         st->epoch += 1;
-        if (a.gen_mode) finish_sample_state(st, a.hist, a.pen_cnt);
-        else st->ticket = 0;
+        if (a.gen_mode) {
+          if (ok) finish_sample_state(st, a.hist, a.pen_cnt);
+        } else {
+          st->ticket = 0;
+        }
       }
     }
   }
@@ -1233,8 +1351,7 @@ cudaError_t decode_step_configure() {
   return cudaSuccess;
 }
 
-bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std::vector<MkTile>& tiles,
-                      std::vector<int>& tile_start, size_t* smem) {
+bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* smem) {
   if (g_mk_smem_max == 0) return false;
   if (n_rep > 16 || (a.head_dim != 64 && a.head_dim != 128)) return false;
   const int grid = decode_step_grid();
@@ -1242,7 +1359,7 @@ bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std
   size_t gmax = 0;
   for (int i = 0; i < nparts; ++i) {
     if (parts[i].kind == MK_ATT) continue;
-    if (parts[i].K % QK_K || parts[i].K > MK_MAX_K) return false;
+    if (parts[i].K % QK_K || parts[i].K > MK_MAX_K || parts[i].ngroups < 1) return false;
     kmax = std::max(kmax, parts[i].K);
     gmax = std::max(gmax, 4 * size_t(parts[i].K / QK_K) * dev_block_bytes(parts[i].dtype));
   }
@@ -1254,45 +1371,22 @@ bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std
   size_t region = std::max(planes_bytes(kmax), att_bytes);
   region = (region + 127) / 128 * 128;
   const size_t slot = std::max<size_t>(32 * 1024, (gmax + 1023) / 1024 * 1024);
-  // per-CTA tile lists and the sizes of the stashes
-  std::vector<int> gpt(nparts, 0);
+  // groups of one tile (whole-K rows that fit a slot); the kernel walks each CTA's
+  // share of every part in tiles of gpt groups
+  int res_rows = 0, lm_rows = 0;
   for (int i = 0; i < nparts; ++i) {
     if (parts[i].kind == MK_ATT) continue;
     const size_t group = 4 * size_t(parts[i].K / QK_K) * dev_block_bytes(parts[i].dtype);
-    gpt[i] = int(std::min<size_t>(MK_GPT, slot / group));
-  }
-  tile_start.assign(size_t(grid) * (nparts + 1), 0);
-  std::vector<std::vector<MkTile>> per(grid);
-  int max_tiles = 0, res_rows = 0, lm_rows = 0;
-  for (int c = 0; c < grid; ++c) {
-    for (int i = 0; i < nparts; ++i) {
-      tile_start[size_t(c) * (nparts + 1) + i] = int(per[c].size());
-      const MkPart& P = parts[i];
-      if (P.kind == MK_ATT) continue;
+    parts[i].gpt = uint16_t(std::min<size_t>(MK_GPT, slot / group));
+    for (int c = 0; c < grid; ++c) {
       int g0, g1;
-      cta_share(P.ngroups, c, grid, g0, g1);
-      for (int g = g0; g < g1; g += gpt[i]) {
-        MkTile t{};
-        t.g = uint16_t(g);
-        t.part = uint16_t(i);
-        t.ng = uint8_t(std::min(gpt[i], g1 - g));
-        per[c].push_back(t);
-      }
+      cta_share(parts[i].ngroups, c, grid, g0, g1);
       const int rows = ROWS * (g1 - g0);
-      if (P.kind == MK_O || P.kind == MK_D) res_rows = std::max(res_rows, rows);
-      if (P.kind == MK_LM) lm_rows = std::max(lm_rows, rows);
+      if (parts[i].kind == MK_O || parts[i].kind == MK_D) res_rows = std::max(res_rows, rows);
+      if (parts[i].kind == MK_LM) lm_rows = std::max(lm_rows, rows);
     }
-    tile_start[size_t(c) * (nparts + 1) + nparts] = int(per[c].size());
-    max_tiles = std::max(max_tiles, int(per[c].size()));
   }
-  if (max_tiles > MK_MAX_TILES || nparts > 65535) return false;
-  for (int i = 0; i < nparts; ++i)
-    if (parts[i].ngroups > 65535) return false;
-  tiles.assign(size_t(grid) * max_tiles, MkTile{});
-  for (int c = 0; c < grid; ++c)
-    std::copy(per[c].begin(), per[c].end(), tiles.begin() + size_t(c) * max_tiles);
   a.nparts = nparts;
-  a.max_tiles = max_tiles;
   a.slot_bytes = int(slot);
   a.region_bytes = int(region);
   a.kmax = kmax;

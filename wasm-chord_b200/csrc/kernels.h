@@ -196,7 +196,8 @@ struct MkPart {
   const float* norm;    // RMSNorm weight of the phase input (null: none)
   int rows0, rows1;     // rows of segments 0 and 1 (segment 2 holds the rest)
   int K;                // input length
-  int ngroups;
+  uint16_t ngroups;     // 4-row groups (gate / up: 2 gate + 2 up rows)
+  uint16_t gpt;         // groups of one weight tile (set by decode_step_plan)
   int row_offset;       // MK_QKV: row of the virtual matrix at this part's row 0
   float eps;
   int16_t phase;        // phase index (tags of its outputs)
@@ -213,15 +214,11 @@ struct MkTile {
   uint16_t g;
   uint16_t part;
   uint8_t ng;
-  uint8_t pad[3];
 };
 
 struct MkArgs {
   const MkPart* parts;
   int nparts;
-  const MkTile* tiles;     // [grid][max_tiles] each CTA's tiles in consumption order
-  const int* tile_start;   // [grid][nparts + 1] first tile of each part
-  int max_tiles;
   StepState* st;
   const float* emb;
   int vocab, hidden, ffn, n_heads, n_kv, head_dim, max_seq;
@@ -253,16 +250,23 @@ struct MkArgs {
   uint32_t* hist;
   uint32_t* pen_cnt;
   float rep;
+  // tensor parallelism (tp_size > 1): this rank holds its shard (heads, FFN rows and
+  // vocabulary rows); the o / down partial sums and the LM-head argmax keys reach
+  // every rank by peer stores into its exchange buffer, whose decode-step region is
+  // [o, down][layer parity][rank][hidden] tagged words, then [rank][2] key words
+  int tp_size, tp_rank;
+  int qdim;                          // query rows of the [q; k; v] part (hidden with one rank)
+  int vocab_off;                     // token id of this rank's first LM-head row
+  unsigned long long* const* peers;  // [tp_size] every rank's exchange buffer
+  size_t xofs;                       // offset (words) of the decode step's region in each buffer
   // shared-memory layout (from decode_step_plan)
   int slot_bytes, nslots, region_bytes, kmax;
   int res_rows;   // rows of an O / D share
   int lm_rows;    // LM-head rows a CTA owns
 };
-// Fills the tile lists and the shared-memory layout; false when the model
-// does not fit the persistent kernel (then the per-op kernels run).
-// tiles / tile_start receive the host copies of the tables.
-bool decode_step_plan(const MkPart* parts, int nparts, MkArgs& a, int n_rep, std::vector<MkTile>& tiles,
-                      std::vector<int>& tile_start, size_t* smem);
+// Sets each part's tile size (gpt) and the shared-memory layout; false when the
+// model does not fit the persistent kernel (then the per-op kernels run).
+bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* smem);
 int decode_step_grid();  // CTAs of one launch (one per SM)
 cudaError_t decode_step_configure();
 cudaError_t launch_decode_step(const MkArgs& a, size_t smem, cudaStream_t s);

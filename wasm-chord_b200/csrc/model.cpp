@@ -266,8 +266,10 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     if (tp_ > 1) {
       part_y_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_) * c.hidden));
       tpkey_ = static_cast<unsigned long long*>(dalloc(2 * sizeof(unsigned long long)));
-      // [tp][hidden] partial sums, then [tp][2] LM-head argmax keys (tagged words)
-      const size_t rn = size_t(tp_) * c.hidden + 2 * size_t(tp_);
+      // per-op decode steps: [tp][hidden] partial sums, then [tp][2] LM-head argmax keys;
+      // the persistent decode step: [o, down][layer parity][tp][hidden], then [tp][2]
+      // (tagged words, written by every rank's peer stores)
+      const size_t rn = mk_xofs() + 4 * size_t(tp_) * c.hidden + 2 * size_t(tp_);
       recv_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * rn));
       check(cudaMemset(recv_, 0, sizeof(unsigned long long) * rn), "clear receive buffer");
       peers_dev_ = static_cast<unsigned long long**>(dalloc(sizeof(void*) * tp_));
@@ -778,7 +780,7 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
   if (position + n > rope_len_) build_rope(uint32_t(std::max<size_t>(position + n, size_t(rope_len_) * 2)));
   std::memcpy(host_ids_, ids, n * sizeof(uint32_t));
   check(cudaMemcpyAsync(ids_, host_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "upload ids");
-  if (n == 1 && mk_ok_) {  // one token: the persistent decode step
+  if (n == 1 && use_mk()) {  // one token: the persistent decode step
     set_state(int(position), int(kv_len_), 1);
     launch_decode_step_kernel(false);
   } else {
@@ -814,16 +816,22 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
 // head. Each phase waits on the counter of the phase whose output it reads.
 void Model::build_decode_step() {
   mk_ok_ = false;
-  // tensor parallelism, weight streaming and dense (F32 / F16) weights run the per-op kernels
-  if ((opt_.flags & 8) || tp_ > 1 || wstream_ || has_dense_weights()) return;
+  // weight streaming and dense (F32 / F16) weights run the per-op kernels
+  if ((opt_.flags & 8) || wstream_ || has_dense_weights()) return;
   if (decode_step_configure() != cudaSuccess) {
     cudaGetLastError();
     return;
   }
   const ModelConfig& c = cfg_;
-  const int H = int(c.hidden), F = int(c.ffn);
+  // this rank's shard: all hidden rows of o / down, its query / KV heads and FFN rows
+  const int H = int(c.hidden), F = int(ffn_l_), HQ = int(hq_);
   std::vector<MkPart> parts;
   int phase = 0, prev_d = -1;
+  bool too_many = false;  // 4-row groups of a part are counted in 16 bits
+  auto groups = [&](size_t n) {
+    too_many |= n > 65535 || n == 0;
+    return uint16_t(n);
+  };
   for (uint32_t l = 0; l < c.layers; ++l) {
     const DevLayer& L = layers_[l];
     const int p_qkv = phase++;
@@ -845,7 +853,7 @@ void Model::build_decode_step() {
         rows += int(segs[i]->rows);
       }
       P.nseg = uint8_t(s1 - s0);
-      P.ngroups = rows / 4;
+      P.ngroups = groups(size_t(rows) / 4);
       P.row_offset = row_off;
       row_off += rows;
       P.phase = int16_t(p_qkv);
@@ -870,11 +878,11 @@ void Model::build_decode_step() {
       MkPart P{};
       P.kind = MK_O;
       P.dtype = uint8_t(L.o.dtype);
-      P.K = H;
+      P.K = HQ;
       P.w[0] = L.o.ptr;
       P.rows0 = int(L.o.rows);
       P.nseg = 1;
-      P.ngroups = int(L.o.rows) / 4;
+      P.ngroups = groups(L.o.rows / 4);
       P.phase = int16_t(p_o);
       P.dep = int16_t(p_att);
       P.first = 1;
@@ -892,7 +900,7 @@ void Model::build_decode_step() {
       P.rows0 = int(L.gate.rows);
       P.rows1 = int(L.up.rows);
       P.nseg = 2;
-      P.ngroups = int(L.gate.rows) / 2;
+      P.ngroups = groups(L.gate.rows / 2);
       P.phase = int16_t(p_gu);
       P.dep = int16_t(p_o);
       P.norm = L.ffn_norm;
@@ -909,7 +917,7 @@ void Model::build_decode_step() {
       P.w[0] = L.down.ptr;
       P.rows0 = int(L.down.rows);
       P.nseg = 1;
-      P.ngroups = int(L.down.rows) / 4;
+      P.ngroups = groups(L.down.rows / 4);
       P.phase = int16_t(p_d);
       P.dep = int16_t(p_gu);
       P.first = 1;
@@ -925,7 +933,7 @@ void Model::build_decode_step() {
     P.w[0] = lm_head_.ptr;
     P.rows0 = int(lm_head_.rows);
     P.nseg = 1;
-    P.ngroups = int(lm_head_.rows) / 4;
+    P.ngroups = groups(lm_head_.rows / 4);
     P.phase = int16_t(phase++);
     P.dep = int16_t(prev_d);
     P.norm = out_norm_;
@@ -935,24 +943,22 @@ void Model::build_decode_step() {
   }
   if (phase > 1023) return;  // tags hold the phase in 10 bits
   MkArgs a{};
-  a.n_kv = int(c.kv_heads);
-  a.n_heads = int(c.heads);
+  a.n_kv = int(kv_l_);
+  a.n_heads = int(heads_l_);
   a.head_dim = int(c.head_dim());
   a.kv_half = int(opt_.kv_half);  // selects the kernel instantiation the plan checks
   a.hidden = H;
-  std::vector<MkTile> tiles;
-  std::vector<int> tile_start;
-  if (!decode_step_plan(parts.data(), int(parts.size()), a, int(c.heads / c.kv_heads), tiles, tile_start,
-                        &mk_smem_))
-    return;
+  a.qdim = HQ;
+  a.tp_size = int(tp_);
+  a.tp_rank = int(rank_);
+  if (too_many) return;
+  if (!decode_step_plan(parts.data(), int(parts.size()), a, int(c.heads / c.kv_heads), &mk_smem_)) return;
   auto upload = [&](const void* src, size_t bytes) {
     void* d = dalloc(bytes);
     check(cudaMemcpy(d, src, bytes, cudaMemcpyHostToDevice), "upload step plan");
     return d;
   };
   a.parts = static_cast<const MkPart*>(upload(parts.data(), sizeof(MkPart) * parts.size()));
-  a.tiles = static_cast<const MkTile*>(upload(tiles.data(), sizeof(MkTile) * tiles.size()));
-  a.tile_start = static_cast<const int*>(upload(tile_start.data(), sizeof(int) * tile_start.size()));
   a.st = st_;
   a.emb = emb_;
   a.vocab = int(c.vocab);
@@ -963,10 +969,10 @@ void Model::build_decode_step() {
   a.kv_layer_elems = kv_layer_elems_;
   a.kv_half = int(opt_.kv_half);
   a.attn_scale = attn_scale_;
-  const size_t kvd = size_t(c.kv_heads) * c.head_dim();
+  const size_t kvd = kvd_l_;
   // xa, xb, q, att (one row per key split), the splits' (max, sum), act, knew, vnew
   const size_t smax = size_t(a.att_smax);
-  const size_t tagged = (3 + smax) * size_t(H) + smax * c.heads * 2 + size_t(F) + 2 * kvd;
+  const size_t tagged = (3 + smax) * size_t(H) + smax * heads_l_ * 2 + size_t(F) + 2 * kvd;
   unsigned long long* t = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * tagged));
   check(cudaMemset(t, 0, sizeof(unsigned long long) * tagged), "clear activations");
   mk_tagged_ = t;
@@ -976,7 +982,7 @@ void Model::build_decode_step() {
   a.q = a.xb + H;
   a.att = a.q + H;
   a.attml = a.att + smax * H;
-  a.act = a.attml + smax * c.heads * 2;
+  a.act = a.attml + smax * heads_l_ * 2;
   a.knew = a.act + F;
   a.vnew = a.knew + kvd;
   a.logits = logits_;
@@ -986,6 +992,9 @@ void Model::build_decode_step() {
   a.ids = ids_;
   a.hist = hist_;
   a.pen_cnt = pen_cnt_;
+  a.vocab_off = int(vocab_off_);
+  a.peers = peers_dev_;  // filled by tp_connect
+  a.xofs = mk_xofs();
   mk_ = a;
   mk_ok_ = true;
 }
@@ -1011,7 +1020,7 @@ void Model::launch_decode_step_kernel(bool gen) {
 
 void Model::decode_steps(int steps) {
   for (int i = 0; i < steps; ++i) {
-    if (mk_ok_ && sample_mode_ == 0) {
+    if (use_mk() && sample_mode_ == 0) {
       launch_decode_step_kernel(true);
     } else if (decode_exec_) {
       check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
@@ -1096,7 +1105,7 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   const float rep = g.repetition_penalty;
   const bool same_graph = graph_rep_ == rep && graph_mode_ == sample_mode_ &&
                           (sample_mode_ == 0 || (graph_t_ == samp_t_ && graph_k_ == samp_k_ && graph_tp_ == samp_tp_));
-  if (mk_ok_ && sample_mode_ == 0) {
+  if (use_mk() && sample_mode_ == 0) {
     launches_per_step_ = 1;
   } else if (!(opt_.flags & 1) && !wstream_ && (!decode_exec_ || !same_graph)) {
     if (decode_exec_) {

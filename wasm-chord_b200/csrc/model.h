@@ -219,8 +219,12 @@ class Model {
   uint32_t sess_last_ = 0;
   StepState sess_state_{};
 
-  // persistent decode step (one cooperative launch per token)
+  // persistent decode step (one cooperative launch per token); with tensor
+  // parallelism it runs once the ranks' exchange buffers are connected
   bool mk_ok_ = false;
+  bool use_mk() const { return mk_ok_ && (tp_ == 1 || p2p_); }
+  // words of the per-op exchange in front of the decode step's region of an exchange buffer
+  size_t mk_xofs() const { return size_t(tp_) * cfg_.hidden + 2 * size_t(tp_); }
   MkArgs mk_{};
   size_t mk_smem_ = 0;
   unsigned long long* mk_tagged_ = nullptr;  // tagged activation buffers (one allocation)

@@ -139,6 +139,9 @@ class SynthConfig:
     quant_mix: str = "q4_k"
     seed: int = 0
     weight_std: float = 0.02
+    # > 0: layer i repeats the tensors of layer i % layer_period (deep models for
+    # timing runs without generating every layer's values)
+    layer_period: int = 0
 
     @property
     def head_dim(self) -> int:
@@ -321,10 +324,20 @@ def write_gguf(path: str, cfg: SynthConfig, plan=None, extra_kv=None) -> str:
     header = b"GGUF" + struct.pack("<IQQ", 3, len(plan), len(kvs)) + b"".join(kvs) + b"".join(infos)
     pad = (-len(header)) % ALIGN
     tmp = path + ".tmp"
+    cache = {}  # layer_period: (layer % period, tensor) -> bytes of its first occurrence
     with open(tmp, "wb") as f:
         f.write(header + b"\0" * pad)
         for index, ((name, ne, t), off) in enumerate(zip(plan, offsets)):
-            data = _gen_tensor(index, name, ne, t, cfg)
+            key = None
+            if cfg.layer_period > 0 and name.startswith("blk."):
+                layer, rest = name[4:].split(".", 1)
+                key = (int(layer) % cfg.layer_period, rest)
+            if key is None:
+                data = _gen_tensor(index, name, ne, t, cfg)
+            else:
+                if key not in cache:
+                    cache[key] = _gen_tensor(index, name, ne, t, cfg)
+                data = cache[key]
             f.write(data)
             f.write(b"\0" * ((-len(data)) % ALIGN))
     os.replace(tmp, path)
