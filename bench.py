@@ -309,6 +309,11 @@ def run_ours(args, rank, world, dist):
     m = wcb.Model.load_from_gguf(path, device=local, stream_weights=args.stream_weights)
     if args.stream_weights:
         METRIC = f"decode tok/s ({label}, batch 1, layer weights streamed from pinned host memory)"
+    # --sampled: the reference's default GenerationConfig (config.rs:74-78), drawn on the device
+    samp = dict(temperature=0.7, top_p=0.9, top_k=40, repetition_penalty=1.1, seed=1) if args.sampled else \
+        dict(temperature=0.0, repetition_penalty=1.0)
+    if args.sampled:
+        METRIC = f"decode tok/s ({label}, batch 1, sampled: temperature 0.7, top-p 0.9, top-k 40, penalty 1.1)"
     cfg = m.config
     sp = m.stream()
     s = torch.cuda.ExternalStream(sp)
@@ -316,7 +321,7 @@ def run_ours(args, rank, world, dist):
     K, W = args.steps, args.warmup
     if PROMPT_LEN + W + K + 1 > cfg.max_seq_len:
         raise SystemExit(f"steps + warmup exceed the context ({cfg.max_seq_len})")
-    gc = wcb.GenerationConfig(max_tokens=W + K + 1, temperature=0.0, repetition_penalty=1.0, eos_id=None)
+    gc = wcb.GenerationConfig(max_tokens=W + K + 1, eos_id=None, **samp)
     stream = m.infer(prompt.tolist(), gc)
     stream.next_tokens(1 + W)  # first token + W warm-up decode steps
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -348,7 +353,7 @@ def run_ours(args, rank, world, dist):
     step_gbs = step_bytes / (ms_max / K * 1e-3) / 1e9
 
     # end to end through the public generate() call with host buffers
-    gc2 = wcb.GenerationConfig(max_tokens=K + 1, temperature=0.0, repetition_penalty=1.0, eos_id=None)
+    gc2 = wcb.GenerationConfig(max_tokens=K + 1, eos_id=None, **samp)
     m.generate_tokens(prompt.tolist(), gc2)  # warm
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -393,8 +398,9 @@ def run_ours(args, rank, world, dist):
                            "bytes_per_step": layer_bytes}
     if args.stream_weights:
         roofline = roofline_stream
-    elif m.launches_per_step() == 1:
-        # one persistent kernel per decode step: its bytes are the step's weights + KV reads
+    elif m.launches_per_step() == 1 or (args.sampled and m.launches_per_step() == 2):
+        # one persistent kernel per decode step (+ the sampler kernel of a sampled
+        # config): its bytes are the step's weights + KV reads
         traffic = None
         if arch in NCU_STEP_TRAFFIC:
             cap_bytes, cap_pos = NCU_STEP_TRAFFIC[arch]
@@ -465,7 +471,8 @@ def run_tp(args, rank, world, dist):
     if world > 1:
         dist.broadcast_object_list(tp_id, src=0)
     m = wcb.Model.load_from_gguf(path, device=local, tp_rank=rank, tp_size=world, tp_id=tp_id[0],
-                                 max_seq=args.prompt + args.warmup + args.steps + 8)
+                                 max_seq=args.prompt + args.warmup + args.steps + 8,
+                                 use_persistent=not args.tp_per_op)
     exchange = "nccl"
     if world > 1 and not args.tp_nccl:  # decode steps: partial sums by peer stores over NVLink
         handles = [None] * world
@@ -693,9 +700,13 @@ def main():
     ap.add_argument("--layers", type=int, default=80, help="--tp: layers of the 70B shape to build")
     ap.add_argument("--prompt", type=int, default=1024, help="--tp: prompt tokens before the timed decode")
     ap.add_argument("--tp-nccl", action="store_true", help="--tp: all-reduce decode steps with NCCL too")
+    ap.add_argument("--tp-per-op", action="store_true",
+                    help="--tp: decode steps on the per-op kernels (CUDA graph) instead of the single-launch step")
     ap.add_argument("--tp-batch", type=int, default=1, help="--tp: sequences decoded together (batched step)")
     ap.add_argument("--stream-weights", action="store_true",
                     help="decode line with the layer weights streamed from pinned host memory (not the headline)")
+    ap.add_argument("--sampled", action="store_true",
+                    help="decode with the reference's default sampling config instead of greedy")
     ap.add_argument("--serve", action="store_true",
                     help="batched serving of --sequences prompts of --prompt tokens (default 2048) over the ranks")
     ap.add_argument("--sequences", type=int, default=32, help="--serve: sequences over all ranks")

@@ -116,47 +116,57 @@ def test_host_sampler_is_seeded():
                                  dict(top_k=200, top_p=0.95, rep=1.3), dict(top_k=1, top_p=0.5, rep=1.0),
                                  dict(top_k=0, top_p=0.9, rep=1.1), dict(top_k=0, top_p=1.0, rep=1.0),
                                  dict(top_k=600, top_p=0.8, rep=1.2)])
-def test_device_sampler_draws_the_host_samplers_tokens(tiny_gguf, gpu, cfg):
-    dev = wcb.Model.load_from_gguf(tiny_gguf, use_persistent=False)
-    host = wcb.Model.load_from_gguf(tiny_gguf, use_persistent=False, host_sampling=True)
+@pytest.mark.parametrize("persistent", [False, True])
+def test_device_sampler_draws_the_host_samplers_tokens(tiny_gguf, gpu, cfg, persistent):
+    """Per-op decode graph + sampler kernel, or the single-launch decode step + sampler
+    kernel (2 launches per step): the host sampler's tokens for every seed."""
+    dev = wcb.Model.load_from_gguf(tiny_gguf, use_persistent=persistent)
+    host = wcb.Model.load_from_gguf(tiny_gguf, use_persistent=persistent, host_sampling=True)
     prompt = synth.random_prompt(24, 512, seed=9).tolist()
     for seed in (1, 2, 3):
         g = wcb.GenerationConfig(max_tokens=48, temperature=0.8, top_p=cfg["top_p"], top_k=cfg["top_k"],
                                  repetition_penalty=cfg["rep"], seed=seed, eos_id=None)
         assert dev.generate_tokens(prompt, g) == host.generate_tokens(prompt, g)
+    assert (dev.launches_per_step() == 2) == persistent
     dev.close()
     host.close()
 
 
 @pytest.mark.gpu
 def test_device_sampling_on_the_default_model(tiny_gguf, gpu):
-    """A model with the persistent greedy kernel samples through the per-op decode graph."""
+    """The reference's default configuration (T 0.7-0.9, top-p 0.9, top-k 40, penalty
+    1.1) samples through the single-launch decode step and the sampler kernel; greedy
+    decoding on the same model follows with one launch per step."""
     m = wcb.Model.load_from_gguf(tiny_gguf)
     prompt = synth.random_prompt(24, 512, seed=9).tolist()
     g = wcb.GenerationConfig(max_tokens=32, temperature=0.9, top_p=0.9, top_k=40, repetition_penalty=1.1,
                              seed=5, eos_id=None)
     a, b = m.generate_tokens(prompt, g), m.generate_tokens(prompt, g)
     assert a == b and len(a) == 32 and all(0 <= t < 512 for t in a)
+    assert m.launches_per_step() == 2
     greedy = wcb.GenerationConfig(max_tokens=16, temperature=0.0, repetition_penalty=1.0, eos_id=None)
     g1 = m.generate_tokens(prompt, greedy)  # the persistent greedy path still follows
     assert g1 == m.generate_tokens(prompt, greedy)
+    assert m.launches_per_step() == 1
     m.close()
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("top_k,top_p", [(1500, 0.9), (2500, 1.0), (0, 0.95)])
-def test_device_full_sampler_on_a_large_vocabulary(model_dir, gpu, top_k, top_p):
+@pytest.mark.parametrize("persistent", [False, True])
+def test_device_full_sampler_on_a_large_vocabulary(model_dir, gpu, top_k, top_p, persistent):
     """top_k above 1024 (and no top_k) over a 3072-token vocabulary: the device's
     sample_full_kernel draws exactly the host sampler's tokens, with no host round trip
-    per token (one launch of the decode graph per step)."""
+    per token (per step one launch of the decode graph, or the single-launch decode
+    step and the sampler kernel)."""
     path = synth.cached_model("tiny", model_dir, vocab_size=3072)
-    dev = wcb.Model.load_from_gguf(path, use_persistent=False)
-    host = wcb.Model.load_from_gguf(path, use_persistent=False, host_sampling=True)
+    dev = wcb.Model.load_from_gguf(path, use_persistent=persistent)
+    host = wcb.Model.load_from_gguf(path, use_persistent=persistent, host_sampling=True)
     prompt = synth.random_prompt(20, 3072, seed=12).tolist()
     for seed in (4, 5):
         g = wcb.GenerationConfig(max_tokens=40, temperature=1.1, top_p=top_p, top_k=top_k,
                                  repetition_penalty=1.1, seed=seed, eos_id=None)
         assert dev.generate_tokens(prompt, g) == host.generate_tokens(prompt, g)
-    assert dev.launches_per_step() > 1
+    assert dev.launches_per_step() == 2 if persistent else dev.launches_per_step() > 2
     dev.close()
     host.close()

@@ -45,7 +45,6 @@ constexpr int MK_T = MK_W * 32;     // consumer threads per CTA
 constexpr int MK_THREADS = MK_T + 32;  // + the producer warp (16 warps: 128 registers a thread)
 constexpr int MK_MAX_K = 16384;     // longest GEMV input (limb planes in shared memory)
 constexpr int MK_GPT = 32;          // most groups in one tile
-constexpr int MK_SPLIT_G = 15;      // parts whose CTA share has fewer groups split K over the warps
 constexpr int MK_ANB = 8;          // attention: cache rows per lane in flight (K and V each)
 constexpr int MK_ASMAX = 4;        // most key splits of one query head
 
@@ -385,7 +384,7 @@ __device__ __forceinline__ void q6k_unit(const uint32_t (&ra)[ROWS], int b, int 
 //   [rsd]    residual rows of this CTA's o / down share
 //   [rope]   cos, sin of the step's position (head_dim / 2 each)
 //   [pen]    penalty counts of this CTA's LM-head rows
-//   [misc]   red[64] floats, part[MK_SPLIT_G][8][4] floats, flags[8]
+//   [misc]   red[64] floats, part[part_floats] floats, flags[8]
 //   [bars]   full[nslots]
 struct MkSmem {
   uint8_t* slots;
@@ -396,7 +395,7 @@ struct MkSmem {
   float* rsin;
   uint32_t* pen;
   float* red;
-  float* part;  // [MK_SPLIT_G][8][ROWS] partial sums of the 8-block chunks of a split part
+  float* part;  // [groups of the CTA's share][chunks][ROWS] partial sums of a split part's 8-block chunks
   int* flags;  // [0] abort, [1] attention ticket result, [2] NaN seen
   uint64_t* full;
   uint64_t* empty;
@@ -425,7 +424,7 @@ __host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
   o.red = x;
   x += sizeof(float) * 64;
   o.part = x;
-  x += sizeof(float) * MK_SPLIT_G * 8 * ROWS;
+  x += sizeof(float) * size_t(a.part_floats);
   o.flags = x;
   x += sizeof(int) * 8;
   x = (x + 7) / 8 * 8;
@@ -606,7 +605,7 @@ __device__ __forceinline__ void group_epilogue(const MkArgs& a, const MkPart& P,
   } else {  // MK_LM (rows of this rank's vocabulary slice)
     const int n = ROWS * g + i;
     a.logits[n] = vi;
-    if (a.gen_mode) {
+    if (a.gen_mode == 1) {
       float pv = vi;
       if (a.rep != 1.0f) {  // apply_repetition_penalty: once per occurrence (sampling.rs:86-103)
         const uint32_t cnt = sm.pen[gi + i];
@@ -1175,10 +1174,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
     const uint32_t row_bytes = uint32_t(NB * dev_block_bytes(P.dtype));
     const Planes pl = planes_at(smem_u32(sm.region), P.K);
     const int gpt = P.gpt;
-    if (NB > 8 && g1 - g0 < MK_SPLIT_G && P.kind != MK_LM) {
-      // Few groups of long rows (the down projection): whole-K units would leave most
-      // warps idle, so the units are (group, 8-block chunk), dealt round-robin to the
-      // warps; the chunks' partial sums meet in part and are added in chunk order.
+    if (NB > 8) {
+      // Rows longer than 2048 values: a tile holds few whole-K groups (one for K >= 7168),
+      // so whole-K units would leave most warps idle while the ring's few tiles are in
+      // flight. The units are (group, 8-block chunk) pairs dealt round-robin to the warps
+      // across tiles; the chunks' partial sums meet in part and are added in chunk order
+      // once the part's last tile is done, then the epilogues run.
       const int CH = (NB + 7) / 8;
       int gb = 0;  // CTA-local index of the tile's first group
       for (int tg = g0; tg < g1; tg += gpt, ++k) {
@@ -1209,7 +1210,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
           for (int i = 0; i < ROWS; ++i) acc[i] = warp_sum(acc[i]);
           if (lane == 0)
 #pragma unroll
-            for (int i = 0; i < ROWS; ++i) sm.part[((gb + gl) * 8 + (ul - gl * CH)) * ROWS + i] = acc[i];
+            for (int i = 0; i < ROWS; ++i) sm.part[((gb + gl) * CH + (ul - gl * CH)) * ROWS + i] = acc[i];
         }
         gb += tng;
         __syncwarp();
@@ -1220,54 +1221,54 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
         float v[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
         for (int ch = 0; ch < CH; ++ch)
 #pragma unroll
-          for (int i = 0; i < ROWS; ++i) v[i] += sm.part[(gl * 8 + ch) * ROWS + i];
+          for (int i = 0; i < ROWS; ++i) v[i] += sm.part[(gl * CH + ch) * ROWS + i];
         if (P.norm)
 #pragma unroll
           for (int i = 0; i < ROWS; ++i) v[i] = __fmul_rn(v[i], c.rm);
         if (!abort_) group_epilogue(a, P, g0 + gl, v, c, sm);
       }
       cbar();  // part is free for the next split part
-      continue;
-    }
-    for (int tg = g0; tg < g1; tg += gpt, ++k) {
-      const int tng = min(gpt, g1 - tg);
-      const int s = k % a.nslots, use = k / a.nslots;
-      // every consumer warp waits for every tile and arrives on its slot
-      if (!mbar_wait_n(sm.full + s, uint32_t(use & 1), abort_ ? 4096u : MK_MBAR_POLLS)) {
-        if (!abort_ && lane == 0) {
-          atomicOr(&st->err, 4);
-          sm.flags[0] = 1;
-        }
-        abort_ = true;
-      }
-      const uint32_t sbase = smem_u32(sm.slots + size_t(s) * a.slot_bytes);
-      // one group (4 rows, whole K) per warp; lane = (pair lane / 8, block lane % 8 + 8 j)
-      for (int u = (warp - U % MK_W + MK_W) % MK_W; u < tng; u += MK_W) {
-        float acc[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (!abort_) {
-          uint32_t ra[ROWS];
-#pragma unroll
-          for (int i = 0; i < ROWS; ++i) {
-            const int ro = P.kind == MK_GU ? (i < 2 ? 2 * u + i : 2 * tng + 2 * u + (i - 2)) : ROWS * u + i;
-            ra[i] = sbase + uint32_t(ro) * row_bytes;
+    } else {
+      for (int tg = g0; tg < g1; tg += gpt, ++k) {
+        const int tng = min(gpt, g1 - tg);
+        const int s = k % a.nslots, use = k / a.nslots;
+        // every consumer warp waits for every tile and arrives on its slot
+        if (!mbar_wait_n(sm.full + s, uint32_t(use & 1), abort_ ? 4096u : MK_MBAR_POLLS)) {
+          if (!abort_ && lane == 0) {
+            atomicOr(&st->err, 4);
+            sm.flags[0] = 1;
           }
-          if (!Q6 || P.dtype == DT_Q4K)
-            for (int b = lane & 7; b < NB; b += 8) q4k_unit(ra, b, lane >> 3, pl, acc);
-          else
-            for (int b = lane & 7; b < NB; b += 8) q6k_unit(ra, b, lane >> 3, pl, acc);
+          abort_ = true;
         }
-        float v[ROWS];
+        const uint32_t sbase = smem_u32(sm.slots + size_t(s) * a.slot_bytes);
+        // one group (4 rows, whole K) per warp; lane = (pair lane / 8, block lane % 8 + 8 j)
+        for (int u = (warp - U % MK_W + MK_W) % MK_W; u < tng; u += MK_W) {
+          float acc[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
+          if (!abort_) {
+            uint32_t ra[ROWS];
 #pragma unroll
-        for (int i = 0; i < ROWS; ++i) v[i] = warp_sum(acc[i]);
-        if (P.norm)
+            for (int i = 0; i < ROWS; ++i) {
+              const int ro = P.kind == MK_GU ? (i < 2 ? 2 * u + i : 2 * tng + 2 * u + (i - 2)) : ROWS * u + i;
+              ra[i] = sbase + uint32_t(ro) * row_bytes;
+            }
+            if (!Q6 || P.dtype == DT_Q4K)
+              for (int b = lane & 7; b < NB; b += 8) q4k_unit(ra, b, lane >> 3, pl, acc);
+            else
+              for (int b = lane & 7; b < NB; b += 8) q6k_unit(ra, b, lane >> 3, pl, acc);
+          }
+          float v[ROWS];
 #pragma unroll
-          for (int i = 0; i < ROWS; ++i) v[i] = __fmul_rn(v[i], c.rm);
-        if (!abort_) group_epilogue(a, P, tg + u, v, c, sm);
+          for (int i = 0; i < ROWS; ++i) v[i] = warp_sum(acc[i]);
+          if (P.norm)
+#pragma unroll
+            for (int i = 0; i < ROWS; ++i) v[i] = __fmul_rn(v[i], c.rm);
+          if (!abort_) group_epilogue(a, P, tg + u, v, c, sm);
+        }
+        U += tng;
+        // leave the slot: the producer refills it with the tile nslots further on
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.empty + s);
       }
-      U += tng;
-      // leave the slot: the producer refills it with the tile nslots further on
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sm.empty + s);
     }
     if (P.kind != MK_LM) continue;
     // LM head: CTA max of the argmax keys, one atomic per CTA; the last CTA to
@@ -1288,7 +1289,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
     if (tid == 0) {
       unsigned long long bmax = 0ull;
       for (int i = 0; i < MK_W; ++i) bmax = rb[i] > bmax ? rb[i] : bmax;
-      if (a.gen_mode) {
+      if (a.gen_mode == 1) {
         if (bmax) atomicMax(&st->best, bmax);
         if (sm.flags[2]) atomicOr(&st->nan, 1);
       }
@@ -1296,11 +1297,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       const int prev = atomicAdd(&st->ticket, 1);
       if (prev == int(gridDim.x) - 1) {
         __threadfence();
-        const bool ok = !(a.gen_mode && a.tp_size > 1) ||
+        const bool ok = !(a.gen_mode == 1 && a.tp_size > 1) ||
                         exchange_keys(st, a.peers, a.xofs + 4 * size_t(a.tp_size) * size_t(a.hidden), a.tp_rank,
                                       a.tp_size, c.tag0, c.wait_ns);
         st->epoch += 1;
-        if (a.gen_mode) {
+        if (a.gen_mode == 1) {
           if (ok) finish_sample_state(st, a.hist, a.pen_cnt);
         } else {
           st->ticket = 0;
@@ -1373,7 +1374,7 @@ bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* s
   const size_t slot = std::max<size_t>(32 * 1024, (gmax + 1023) / 1024 * 1024);
   // groups of one tile (whole-K rows that fit a slot); the kernel walks each CTA's
   // share of every part in tiles of gpt groups
-  int res_rows = 0, lm_rows = 0;
+  int res_rows = 0, lm_rows = 0, part_floats = ROWS;
   for (int i = 0; i < nparts; ++i) {
     if (parts[i].kind == MK_ATT) continue;
     const size_t group = 4 * size_t(parts[i].K / QK_K) * dev_block_bytes(parts[i].dtype);
@@ -1384,9 +1385,13 @@ bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* s
       const int rows = ROWS * (g1 - g0);
       if (parts[i].kind == MK_O || parts[i].kind == MK_D) res_rows = std::max(res_rows, rows);
       if (parts[i].kind == MK_LM) lm_rows = std::max(lm_rows, rows);
+      const int NB = parts[i].K / QK_K;
+      if (NB > 8)  // split part: a float per (group, 8-block chunk, row)
+        part_floats = std::max(part_floats, (g1 - g0) * ((NB + 7) / 8) * ROWS);
     }
   }
   a.nparts = nparts;
+  a.part_floats = part_floats;
   a.slot_bytes = int(slot);
   a.region_bytes = int(region);
   a.kmax = kmax;

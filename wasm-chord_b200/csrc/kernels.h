@@ -245,7 +245,8 @@ struct MkArgs {
   // tests of the bounded waits: the outputs of this phase are never written, so the
   // waits of its consumers run out (wait_ms) and the launch ends with an error (-1: none)
   int drop_phase;
-  int gen_mode;              // 1: token = hist[nhist - 1], penalty + argmax + bookkeeping
+  int gen_mode;              // 1: token = hist[nhist - 1], penalty + argmax + bookkeeping;
+                             // 2: token = hist[nhist - 1], logits only (a sampler kernel follows)
   const uint32_t* ids;       // gen_mode 0: token = ids[0]
   uint32_t* hist;
   uint32_t* pen_cnt;
@@ -261,6 +262,7 @@ struct MkArgs {
   size_t xofs;                       // offset (words) of the decode step's region in each buffer
   // shared-memory layout (from decode_step_plan)
   int slot_bytes, nslots, region_bytes, kmax;
+  int part_floats;  // partial sums of a split part's chunks (longest share x chunks x 4)
   int res_rows;   // rows of an O / D share
   int lm_rows;    // LM-head rows a CTA owns
 };

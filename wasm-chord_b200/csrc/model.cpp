@@ -685,17 +685,7 @@ void Model::enqueue_lm_head(int T, bool gen) {
   gemv(head, 1, H, 1, x_ + size_t(T - 1) * H, H, out_norm_, cfg_.eps, PRO_RMSNORM, EPI_LMHEAD, logits_,
        int(cfg_.vocab), nullptr, 0, nullptr, 0, -1, 0);
   gen_mode_ = 0;
-  if (dev_sample) {  // penalty, top-k / top-p draw and generate()'s bookkeeping on the device
-    if (sample_mode_ == 1)  // 1 <= top_k <= 1024
-      check(launch_sample(logits_, plog_, int(cfg_.vocab), st_, hist_, pen_cnt_, rep_, samp_t_, samp_k_, samp_tp_,
-                          rng_, stream_),
-            "sampler");
-    else  // every other sampled configuration
-      check(launch_sample_full(logits_, plog_, int(cfg_.vocab), st_, hist_, pen_cnt_, rep_, samp_t_, samp_k_,
-                               samp_tp_, rng_, nullptr, stream_),
-            "sampler");
-    ++launches_;
-  }
+  if (dev_sample) enqueue_sampler();
   if (gen && tp_ > 1 && p2p_) {
     // the argmax keys exchanged by peer stores too: a decode step then makes no NCCL
     // call, so every wait on another rank in it is bounded
@@ -710,6 +700,19 @@ void Model::enqueue_lm_head(int T, bool gen) {
     check(launch_tp_finish(st_, tpkey_, hist_, pen_cnt_, stream_), "sampler bookkeeping");
     launches_ += 2;
   }
+}
+
+// penalty, top-k / top-p draw and generate()'s bookkeeping on the device
+void Model::enqueue_sampler() {
+  if (sample_mode_ == 1)  // 1 <= top_k <= 1024
+    check(launch_sample(logits_, plog_, int(cfg_.vocab), st_, hist_, pen_cnt_, rep_, samp_t_, samp_k_, samp_tp_, rng_,
+                        stream_),
+          "sampler");
+  else  // every other sampled configuration
+    check(launch_sample_full(logits_, plog_, int(cfg_.vocab), st_, hist_, pen_cnt_, rep_, samp_t_, samp_k_, samp_tp_,
+                             rng_, nullptr, stream_),
+          "sampler");
+  ++launches_;
 }
 
 void Model::enqueue_forward(const uint32_t* dev_ids, int T, bool from_hist) {
@@ -782,7 +785,7 @@ void Model::forward(const uint32_t* ids, size_t n, size_t position, float* logit
   check(cudaMemcpyAsync(ids_, host_ids_, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "upload ids");
   if (n == 1 && use_mk()) {  // one token: the persistent decode step
     set_state(int(position), int(kv_len_), 1);
-    launch_decode_step_kernel(false);
+    launch_decode_step_kernel(0);
   } else {
     for (size_t c0 = 0; c0 < n; c0 += size_t(t_max_)) {
       const int T = int(std::min(n - c0, size_t(t_max_)));
@@ -999,7 +1002,7 @@ void Model::build_decode_step() {
   mk_ok_ = true;
 }
 
-void Model::launch_decode_step_kernel(bool gen) {
+void Model::launch_decode_step_kernel(int gen_mode) {
   if (++mk_launches_ >= (1u << 21)) {
     // tags are epoch * 1024 + phase + 1 in 32 bits: restart the epochs well
     // before they wrap (no launch is in flight after these stream-ordered clears)
@@ -1010,7 +1013,7 @@ void Model::launch_decode_step_kernel(bool gen) {
   MkArgs a = mk_;
   a.rope_cos = rope_cos_;
   a.rope_sin = rope_sin_;
-  a.gen_mode = gen ? 1 : 0;
+  a.gen_mode = gen_mode;
   a.rep = rep_;
   // test hook for the bounded waits (unset in normal use): withhold one phase's outputs
   const char* drop = std::getenv("WCB_TEST_DROP_PHASE");
@@ -1020,8 +1023,9 @@ void Model::launch_decode_step_kernel(bool gen) {
 
 void Model::decode_steps(int steps) {
   for (int i = 0; i < steps; ++i) {
-    if (use_mk() && sample_mode_ == 0) {
-      launch_decode_step_kernel(true);
+    if (use_mk()) {  // the single-launch step (+ the device sampler of a sampled config)
+      launch_decode_step_kernel(sample_mode_ == 0 ? 1 : 2);
+      if (sample_mode_ != 0) enqueue_sampler();
     } else if (decode_exec_) {
       check(cudaGraphLaunch(decode_exec_, stream_), "graph launch");
     } else {
@@ -1105,8 +1109,8 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
   const float rep = g.repetition_penalty;
   const bool same_graph = graph_rep_ == rep && graph_mode_ == sample_mode_ &&
                           (sample_mode_ == 0 || (graph_t_ == samp_t_ && graph_k_ == samp_k_ && graph_tp_ == samp_tp_));
-  if (use_mk() && sample_mode_ == 0) {
-    launches_per_step_ = 1;
+  if (use_mk()) {
+    launches_per_step_ = sample_mode_ == 0 ? 1 : 2;
   } else if (!(opt_.flags & 1) && !wstream_ && (!decode_exec_ || !same_graph)) {
     if (decode_exec_) {
       cudaGraphExecDestroy(decode_exec_);

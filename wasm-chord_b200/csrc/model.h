@@ -138,7 +138,9 @@ class Model {
         if (dense_dtype(w->dtype)) return true;
     return false;
   }
-  void launch_decode_step_kernel(bool gen);
+  // gen_mode 0: forward of ids_[0]; 1: greedy generate step; 2: logits of a sampled step
+  void launch_decode_step_kernel(int gen_mode);
+  void enqueue_sampler();  // sampled decoding: penalty, draw and generate()'s bookkeeping
 
   ModelConfig cfg_;
   LoadOptions opt_;
