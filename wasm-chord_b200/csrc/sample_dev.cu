@@ -5,8 +5,9 @@
 // One CTA of 1024 threads over the logits of one sequence: the repetition
 // penalty (:86-103) into a scratch copy, a NaN check, then the top-k candidates
 // by (logit desc, index asc) with a radix select on the order-preserving bits
-// (4 passes of 8 bits; the ties at the threshold go to the lowest indices,
-// through a block scan in index order), and the candidates sorted by index.
+// (4 passes of 8 bits over keys held in registers, warp-aggregated histogram
+// counts; the ties at the threshold go to the lowest indices, through a block
+// scan in index order), and the candidates ordered by index (rank counting).
 // From there the arithmetic is the fixed sequence the host sampler uses
 // (sampler.cpp, Sampler::sample_fixed): x = l / T, e = exp(x - max) with
 // wcb_exp_nonpos, probabilities over the candidates in index order, top-p
@@ -32,57 +33,179 @@ __device__ __forceinline__ float sd_uniform(unsigned long long* state) {
   return __fmul_rn(float(z >> 40), 1.0f / 16777216.0f);
 }
 
-// block-wide bitonic sort of SD_THREADS 64-bit keys, descending
-__device__ void bitonic_desc(unsigned long long* k) {
-  const int tid = threadIdx.x;
-  for (int size = 2; size <= SD_THREADS; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      __syncthreads();
-      const int j = tid ^ stride;
-      if (j > tid) {
-        const bool desc = (tid & size) == 0;
-        const unsigned long long a = k[tid], b = k[j];
-        if (desc ? (a < b) : (a > b)) {
-          k[tid] = b;
-          k[j] = a;
-        }
-      }
-    }
+// inclusive warp scan / block-wide exclusive scan and total of a u64 per thread
+__device__ __forceinline__ unsigned long long warp_incl_u64(unsigned long long v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+__device__ unsigned long long block_excl_u64(unsigned long long v, unsigned long long* total, unsigned long long* ws) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned long long inc = warp_incl_u64(v);
+  __syncthreads();  // ws may still be read by a previous call
+  if (lane == 31) ws[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned long long w = warp_incl_u64(ws[lane]);
+    ws[lane] = w;  // inclusive totals of the warps
   }
   __syncthreads();
+  *total = ws[SD_THREADS / 32 - 1];
+  return (warp ? ws[warp - 1] : 0ull) + inc - v;
 }
 
+constexpr int SD_REG = 32;  // logits per thread held on chip (vocabularies up to 32768)
+// staged penalised logits: value i at i + i / 32, so thread t's contiguous run
+// t * SD_REG + j (j < 32) sits at t * 33 + j, one bank per lane
+constexpr int SD_STAGE_BYTES = (SD_THREADS * SD_REG + SD_THREADS) * 4;
+__device__ __forceinline__ int stage_at(int i) { return i + (i >> 5); }
+
+// One histogram count per element of the radix pass; the lanes of a warp that hit
+// the same bin add together with one atomic, one round per distinct wanted bin (the
+// largest logits crowd into a few bins; later passes have few wanted lanes). Every
+// lane of the warp calls it.
+__device__ __forceinline__ void hist_add(unsigned int* h, bool want, unsigned int bin) {
+  const int lane = threadIdx.x & 31;
+  unsigned int pending = __ballot_sync(0xffffffffu, want);
+  while (pending) {
+    const int src = __ffs(pending) - 1;
+    const unsigned int b = __shfl_sync(0xffffffffu, bin, src);
+    const unsigned int m = __ballot_sync(0xffffffffu, want && bin == b);
+    if (lane == src) atomicAdd(&h[b], unsigned(__popc(m)));
+    pending &= ~m;
+  }
+}
+
+// The same into this warp's own histogram row: one shared atomic per wanted element
+// (the lanes that hit one bin are combined by the hardware; no other warp adds to
+// the row).
+__device__ __forceinline__ void hist_add_warp(unsigned int* hw, bool want, unsigned int bin) {
+  if (want) atomicAdd(&hw[bin], 1u);
+}
+
+// The penalised logits (repetition penalty once per occurrence, sampling.rs:86-103)
+// into the stage with coalesced loads; true when one is NaN.
+__device__ __forceinline__ bool stage_penalised(const float* logits, const uint32_t* pen_cnt, float rep, int n,
+                                                float* stage) {
+  bool nan = false;
+  for (int i = threadIdx.x; i < n; i += SD_THREADS) {
+    float v = logits[i];
+    if (rep != 1.0f) {
+      const uint32_t c = pen_cnt[i];
+      for (uint32_t r = 0; r < c; ++r) v = v > 0.0f ? __fdiv_rn(v, rep) : __fmul_rn(v, rep);
+    }
+    nan |= v != v;
+    stage[stage_at(i)] = v;
+  }
+  return nan;
+}
+
+// Radix step (warp 0): the highest bin at which the count of keys in it and above
+// reaches rem, 8 bins a lane; the bin joins the prefix, rem drops by the count above.
+__device__ __forceinline__ void pick_bin(const unsigned int* h, unsigned int prefix, int shift, unsigned int rem,
+                                         unsigned int* s_prefix, unsigned int* s_rem) {
+  const int lane = threadIdx.x & 31;
+  unsigned int c[8], tot = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {  // bins from the top: 255 - 8 lane - k
+    c[k] = h[255 - (8 * lane + k)];
+    tot += c[k];
+  }
+  unsigned int inc = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned int t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  unsigned int cum = inc - tot, before = 0;
+  int hit = -1;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    if (hit < 0 && cum + c[k] >= rem) {
+      hit = k;
+      before = cum;
+    }
+    cum += c[k];
+  }
+  const unsigned int hm = __ballot_sync(0xffffffffu, hit >= 0);
+  if (hm != 0u && lane == __ffs(hm) - 1) {
+    *s_prefix = prefix | (unsigned(255 - (8 * lane + hit)) << shift);
+    *s_rem = rem - before;
+  }
+}
+
+// REG: the penalised logits are staged in shared memory (coalesced loads) and every
+// thread keeps the order keys of its contiguous run in registers; otherwise plog.
+template <bool REG>
 __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits, float* plog, int n, StepState* st,
                                                             uint32_t* hist, uint32_t* pen_cnt, float rep, float temp,
                                                             int top_k, float top_p, unsigned long long* rng) {
   __shared__ unsigned int hcount[256];
   __shared__ unsigned int s_prefix, s_rem, s_nan, s_ncand, s_tok;
-  __shared__ unsigned int scan[SD_THREADS];
-  __shared__ unsigned long long keys[SD_THREADS];
+  __shared__ int sorted[SD_THREADS];
+  __shared__ int ord[SD_THREADS];
   __shared__ float q[SD_THREADS];
   __shared__ int cidx[SD_THREADS];
+  __shared__ unsigned long long ws[SD_THREADS / 32];
   __shared__ float s_sum, s_max;
+  // dynamic: REG: the penalised logits (stage_at); then [warps][256] per-warp counts of a radix pass
+  extern __shared__ __align__(16) uint8_t dyn[];
+  float* stage = reinterpret_cast<float*>(dyn);
+  unsigned int* hwarp = reinterpret_cast<unsigned int*>(dyn + (REG ? SD_STAGE_BYTES : 0));
   pdl_trigger();
   pdl_wait();
   if (st->done) return;
   const int tid = threadIdx.x;
-  const int per = (n + SD_THREADS - 1) / SD_THREADS;
+  const int per = (n + SD_THREADS - 1) / SD_THREADS;  // REG: per <= SD_REG
   const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
+  const int cnt = i1 - i0;
+  uint32_t kr[REG ? SD_REG : 1];
+  auto logit_at = [&](int i) -> float {
+    if constexpr (REG) return stage[stage_at(i)];
+    else return plog[i];
+  };
+  // the same trip count on every thread (the histogram's warp-wide match needs it)
+  auto each = [&](auto&& f) {
+    if constexpr (REG) {
+#pragma unroll
+      for (int j = 0; j < SD_REG; ++j) f(j);
+    } else {
+      for (int j = 0; j < per; ++j) f(j);
+    }
+  };
+  auto key_at = [&](int j) -> uint32_t {
+    if constexpr (REG) return kr[j];
+    else return j < cnt ? order_key(plog[i0 + j]) : 0u;
+  };
   if (tid == 0) {
     s_nan = 0;
     s_ncand = 0;
   }
   __syncthreads();
-  // repetition penalty once per occurrence (sampling.rs:86-103), into the scratch copy
+  // repetition penalty once per occurrence (sampling.rs:86-103), into the stage (REG)
+  // or the scratch copy
   bool nan = false;
-  for (int i = i0; i < i1; ++i) {
-    float v = logits[i];
-    if (rep != 1.0f) {
-      const uint32_t c = pen_cnt[i];
-      for (uint32_t k = 0; k < c; ++k) v = v > 0.0f ? __fdiv_rn(v, rep) : __fmul_rn(v, rep);
-    }
-    nan |= v != v;
-    plog[i] = v;
+  if constexpr (REG) {
+    nan = stage_penalised(logits, pen_cnt, rep, n, stage);
+    __syncthreads();
+    each([&](int j) { kr[j] = j < cnt ? order_key(stage[stage_at(i0 + j)]) : 0u; });
+  } else {
+    each([&](int j) {
+      if (j < cnt) {
+        const int i = i0 + j;
+        float v = logits[i];
+        if (rep != 1.0f) {
+          const uint32_t c = pen_cnt[i];
+          for (uint32_t r = 0; r < c; ++r) v = v > 0.0f ? __fdiv_rn(v, rep) : __fmul_rn(v, rep);
+        }
+        nan |= v != v;
+        plog[i] = v;
+      }
+    });
   }
   if (nan) atomicOr(&s_nan, 1u);
   __syncthreads();
@@ -97,24 +220,21 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
   // radix select of the K-th largest order key (8 bits at a time)
   unsigned int prefix = 0, pmask = 0, rem = unsigned(K);
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = tid; b < 256; b += SD_THREADS) hcount[b] = 0;
+    for (int b = tid; b < (SD_THREADS / 32) * 256; b += SD_THREADS) hwarp[b] = 0;
     __syncthreads();
-    for (int i = i0; i < i1; ++i) {
-      const uint32_t key = order_key(plog[i]);
-      if ((key & pmask) == prefix) atomicAdd(&hcount[(key >> shift) & 255u], 1u);
+    each([&](int j) {
+      const uint32_t key = key_at(j);
+      hist_add_warp(hwarp + (tid >> 5) * 256, j < cnt && (key & pmask) == prefix, (key >> shift) & 255u);
+    });
+    __syncthreads();
+    if (tid < 256) {  // the warps' counts of each bin
+      unsigned int c = 0;
+#pragma unroll 8
+      for (int w = 0; w < SD_THREADS / 32; ++w) c += hwarp[w * 256 + tid];
+      hcount[tid] = c;
     }
     __syncthreads();
-    if (tid == 0) {
-      unsigned int cum = 0;
-      for (int b = 255; b >= 0; --b) {
-        if (cum + hcount[b] >= rem) {
-          s_prefix = prefix | (unsigned(b) << shift);
-          s_rem = rem - cum;
-          break;
-        }
-        cum += hcount[b];
-      }
-    }
+    if (tid < 32) pick_bin(hcount, prefix, shift, rem, &s_prefix, &s_rem);
     __syncthreads();
     prefix = s_prefix;
     rem = s_rem;
@@ -122,46 +242,42 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
   }
   // candidates: every key above the threshold, and the `rem` lowest-indexed keys equal to it
   unsigned int n_eq = 0;
-  for (int i = i0; i < i1; ++i) n_eq += order_key(plog[i]) == prefix;
-  scan[tid] = n_eq;
-  __syncthreads();
-  for (int off = 1; off < SD_THREADS; off <<= 1) {  // inclusive scan in thread (= index) order
-    const unsigned int v = tid >= off ? scan[tid - off] : 0u;
-    __syncthreads();
-    scan[tid] += v;
-    __syncthreads();
-  }
-  unsigned int eq_rank = scan[tid] - n_eq;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t key = order_key(plog[i]);
-    bool take = key > prefix;
-    if (key == prefix) take = eq_rank++ < rem;
-    if (take) cidx[atomicAdd(&s_ncand, 1u)] = i;
-  }
+  each([&](int j) { n_eq += (j < cnt && key_at(j) == prefix) ? 1u : 0u; });
+  unsigned long long eq_total;
+  unsigned int eq_rank = unsigned(block_excl_u64(n_eq, &eq_total, ws));  // equal keys in lower threads
+  each([&](int j) {
+    if (j < cnt) {
+      const uint32_t key = key_at(j);
+      bool take = key > prefix;
+      if (key == prefix) take = eq_rank++ < rem;
+      if (take) cidx[atomicAdd(&s_ncand, 1u)] = i0 + j;
+    }
+  });
   __syncthreads();
   const int nc = int(s_ncand);  // == K
-  // candidates in index order: sort (index desc with INT_MAX padding first), read back reversed
-  keys[tid] = tid < nc ? (unsigned long long)(unsigned)cidx[tid] : 0xFFFFFFFFFFFFFFFFull;
-  bitonic_desc(keys);
-  // keys sorted descending: the nc valid indices occupy slots [SD_THREADS - nc, SD_THREADS) in
-  // descending order, so candidate tid (ascending) is at slot SD_THREADS - 1 - tid
-  const int cand = tid < nc ? int(keys[SD_THREADS - 1 - tid]) : -1;
+  // candidates in index order: each one's rank among the (distinct) candidate indices
+  if (tid < nc) {
+    const int my = cidx[tid];
+    int r = 0;
+    for (int j = 0; j < nc; ++j) r += cidx[j] < my;
+    sorted[r] = my;
+  }
   __syncthreads();
+  const int cand = tid < nc ? sorted[tid] : -1;
   // x = l / T, max, e = exp(x - max)
   float x = -INFINITY;
-  if (cand >= 0) x = __fdiv_rn(plog[cand], temp);
-  if (tid == 0) s_max = -INFINITY;
-  __syncthreads();
+  if (cand >= 0) x = __fdiv_rn(logit_at(cand), temp);
   // the maximum is exact in any order
   float m = x;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((tid & 31) == 0) q[tid >> 5] = m;
   __syncthreads();
-  if (tid == 0) {
-    float mm = -INFINITY;
-    for (int w = 0; w < SD_THREADS / 32; ++w) mm = fmaxf(mm, q[w]);
-    s_max = mm;
+  if (tid < 32) {
+    float mm = q[tid];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+    if (tid == 0) s_max = mm;
   }
   __syncthreads();
   const float e = cand >= 0 ? wcb_exp_nonpos(__fadd_rn(x, -s_max)) : 0.0f;
@@ -176,14 +292,22 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
   float p = cand >= 0 ? __fdiv_rn(e, s_sum) : 0.0f;
   const bool tp_on = !(top_p <= 0.0f || top_p >= 1.0f);
   if (tp_on) {
-    // order by (probability desc, index asc): key = (p bits, ~slot); p >= 0 so its bits order it
-    keys[tid] = cand >= 0 ? (((unsigned long long)__float_as_uint(p) << 32) | (0xFFFFFFFFu - unsigned(tid))) : 0ull;
     q[tid] = p;
-    bitonic_desc(keys);
+    __syncthreads();
+    // order by (probability desc, index asc): each candidate's rank
+    if (tid < nc) {
+      int r = 0;
+      for (int j = 0; j < nc; ++j) {
+        const float pj = q[j];
+        r += (pj > p || (pj == p && j < tid)) ? 1 : 0;
+      }
+      ord[r] = tid;
+    }
+    __syncthreads();
     if (tid == 0) {  // top_p (sampling.rs:152-193): keep while the sum before the token is < top_p
       float cum = 0.0f;
       for (int r = 0; r < nc; ++r) {
-        const int slot = int(0xFFFFFFFFu - unsigned(keys[r] & 0xFFFFFFFFull));
+        const int slot = ord[r];
         if (cum >= top_p) q[slot] = 0.0f;
         else cum = __fadd_rn(cum, q[slot]);
       }
@@ -229,31 +353,6 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
 
 // ---- any number of candidates (top_k = 0 or top_k > 1024): integer weights ----
 
-// inclusive warp scan / block-wide exclusive scan and total of a u64 per thread
-__device__ __forceinline__ unsigned long long warp_incl_u64(unsigned long long v) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned long long t = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += t;
-  }
-  return v;
-}
-__device__ unsigned long long block_excl_u64(unsigned long long v, unsigned long long* total, unsigned long long* ws) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const unsigned long long inc = warp_incl_u64(v);
-  __syncthreads();  // ws may still be read by a previous call
-  if (lane == 31) ws[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    const unsigned long long w = warp_incl_u64(ws[lane]);
-    ws[lane] = w;  // inclusive totals of the warps
-  }
-  __syncthreads();
-  *total = ws[SD_THREADS / 32 - 1];
-  return (warp ? ws[warp - 1] : 0ull) + inc - v;
-}
-
 // LogitsProcessor::sample for top_k = 0 or top_k > 1024 (sampling.rs:106-229),
 // with the weights of sample_int.h: the repetition penalty into plog, the top-k
 // candidates (k = 0: all) by a radix select of the order-preserving logit bits
@@ -261,6 +360,32 @@ __device__ unsigned long long block_excl_u64(unsigned long long v, unsigned long
 // integer weights E (stored over plog), top-p by a radix search over E with
 // per-bucket counts and exact sums, the draw, generate()'s bookkeeping.
 // probs (may be null) receives each token's final probability.
+// count and weight sum per histogram bin; the lanes of a warp that hit the same
+// bin add together (one pass per distinct bin of the warp). Every lane calls it.
+__device__ __forceinline__ void hist_add_sum(unsigned int* hc, unsigned long long* hs, bool want, unsigned int bin,
+                                             unsigned long long w) {
+  const int lane = threadIdx.x & 31;
+  unsigned int pending = __ballot_sync(0xffffffffu, want);
+  while (pending) {
+    const int src = __ffs(pending) - 1;
+    const unsigned int b = __shfl_sync(0xffffffffu, bin, src);
+    const bool mine = want && bin == b;
+    const unsigned int m = __ballot_sync(0xffffffffu, mine);
+    unsigned long long sum = mine ? w : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == src) {
+      atomicAdd(&hc[b], unsigned(__popc(m)));
+      atomicAdd(&hs[b], sum);
+    }
+    pending &= ~m;
+  }
+}
+
+// SM: the penalised logits, then their x = l / T, then their integer weights, in
+// dynamic shared memory (stage_at: each thread's contiguous run conflict-free, the
+// logits loaded coalesced); otherwise in plog.
+template <bool SM>
 __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* logits, float* plog, int n, StepState* st,
                                                                  uint32_t* hist, uint32_t* pen_cnt, float rep,
                                                                  float temp, int top_k, float top_p,
@@ -276,19 +401,53 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
   pdl_wait();
   if (st->done) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (n + SD_THREADS - 1) / SD_THREADS;
+  const int per = (n + SD_THREADS - 1) / SD_THREADS;  // REG: per <= SD_REG
   const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
+  const int cnt = i1 - i0;
+  extern __shared__ uint32_t sv[];  // SM: value i at stage_at(i)
+  uint32_t* E = reinterpret_cast<uint32_t*>(plog);
+  auto each = [&](auto&& f) {  // the same trip count on every thread
+    if constexpr (SM) {
+#pragma unroll 8
+      for (int j = 0; j < SD_REG; ++j) f(j);
+    } else {
+      for (int j = 0; j < per; ++j) f(j);
+    }
+  };
+  auto getf = [&](int j) -> float {
+    if constexpr (SM) return __uint_as_float(sv[stage_at(i0 + j)]);
+    else return plog[i0 + j];
+  };
+  auto setf = [&](int j, float v) {
+    if constexpr (SM) sv[stage_at(i0 + j)] = __float_as_uint(v);
+    else plog[i0 + j] = v;
+  };
+  auto getw = [&](int j) -> uint32_t {
+    if constexpr (SM) return sv[stage_at(i0 + j)];
+    else return E[i0 + j];
+  };
+  auto setw = [&](int j, uint32_t w) {
+    if constexpr (SM) sv[stage_at(i0 + j)] = w;
+    else E[i0 + j] = w;
+  };
   if (tid == 0) s_nan = 0;
   __syncthreads();
   bool nan = false;
-  for (int i = i0; i < i1; ++i) {  // repetition penalty once per occurrence (sampling.rs:86-103)
-    float v = logits[i];
-    if (rep != 1.0f) {
-      const uint32_t c = pen_cnt[i];
-      for (uint32_t k = 0; k < c; ++k) v = v > 0.0f ? __fdiv_rn(v, rep) : __fmul_rn(v, rep);
-    }
-    nan |= v != v;
-    plog[i] = v;
+  if constexpr (SM) {
+    nan = stage_penalised(logits, pen_cnt, rep, n, reinterpret_cast<float*>(sv));
+  } else {
+    each([&](int j) {  // repetition penalty once per occurrence (sampling.rs:86-103)
+      if (j < cnt) {
+        const int i = i0 + j;
+        float v = logits[i];
+        if (rep != 1.0f) {
+          const uint32_t c = pen_cnt[i];
+          for (uint32_t k = 0; k < c; ++k) v = v > 0.0f ? __fdiv_rn(v, rep) : __fmul_rn(v, rep);
+        }
+        nan |= v != v;
+        setf(j, v);
+      }
+    });
   }
   if (nan) atomicOr(&s_nan, 1u);
   __syncthreads();
@@ -308,67 +467,61 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int b = tid; b < 256; b += SD_THREADS) hcount[b] = 0;
       __syncthreads();
-      for (int i = i0; i < i1; ++i) {
-        const uint32_t key = order_key(plog[i]);
-        if ((key & pmask) == prefix) atomicAdd(&hcount[(key >> shift) & 255u], 1u);
-      }
+      each([&](int j) {
+        const uint32_t key = j < cnt ? order_key(getf(j)) : 0u;
+        hist_add(hcount, j < cnt && (key & pmask) == prefix, (key >> shift) & 255u);
+      });
       __syncthreads();
-      if (tid == 0) {
-        unsigned int cum = 0;
-        for (int b = 255; b >= 0; --b) {
-          if (cum + hcount[b] >= rem) {
-            s_prefix = prefix | (unsigned(b) << shift);
-            s_rem = rem - cum;
-            break;
-          }
-          cum += hcount[b];
-        }
-      }
+      if (tid < 32) pick_bin(hcount, prefix, shift, rem, &s_prefix, &s_rem);
       __syncthreads();
       prefix = s_prefix;
       rem = s_rem;
       pmask |= 255u << shift;
     }
   }
-  // x = l / T over the candidates (-inf elsewhere) into plog, and the maximum
+  // x = l / T over the candidates (-inf elsewhere), and the maximum
   {
     unsigned long long eq = 0;
-    if (topk)
-      for (int i = i0; i < i1; ++i) eq += order_key(plog[i]) == prefix;
+    if (topk) each([&](int j) { eq += (j < cnt && order_key(getf(j)) == prefix) ? 1u : 0u; });
     unsigned long long eq_tot;
     unsigned int eq_rank = unsigned(block_excl_u64(eq, &eq_tot, ws));
     float mx = -INFINITY;
-    for (int i = i0; i < i1; ++i) {
-      bool take = true;
-      if (topk) {
-        const uint32_t key = order_key(plog[i]);
-        take = key > prefix;
-        if (key == prefix) take = eq_rank++ < rem;
+    each([&](int j) {
+      if (j < cnt) {
+        const float v = getf(j);
+        bool take = true;
+        if (topk) {
+          const uint32_t key = order_key(v);
+          take = key > prefix;
+          if (key == prefix) take = eq_rank++ < rem;
+        }
+        const float x = take ? __fdiv_rn(v, temp) : -INFINITY;
+        setf(j, x);
+        mx = fmaxf(mx, x);
       }
-      const float x = take ? __fdiv_rn(plog[i], temp) : -INFINITY;
-      plog[i] = x;
-      mx = fmaxf(mx, x);
-    }
+    });
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) wmax[warp] = mx;
     __syncthreads();
-    if (tid == 0) {
-      float m = -INFINITY;
-      for (int w = 0; w < SD_THREADS / 32; ++w) m = fmaxf(m, wmax[w]);
-      s_max = m;
+    if (tid < 32) {
+      float m = wmax[tid];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (tid == 0) s_max = m;
     }
     __syncthreads();
   }
-  // integer weights (stored over plog) and their total
-  uint32_t* E = reinterpret_cast<uint32_t*>(plog);
+  // integer weights and their total
   const float M = s_max;
   unsigned long long mine = 0;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t w = int_weight(wcb_exp_nonpos(__fadd_rn(plog[i], -M)));
-    E[i] = w;
-    mine += w;
-  }
+  each([&](int j) {
+    if (j < cnt) {
+      const uint32_t w = int_weight(wcb_exp_nonpos(__fadd_rn(getf(j), -M)));
+      setw(j, w);
+      mine += w;
+    }
+  });
   unsigned long long S;
   block_excl_u64(mine, &S, ws);
   // top-p: the last kept weight v* (radix search over E from the top, exact sums)
@@ -384,33 +537,57 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
         hsum[b] = 0;
       }
       __syncthreads();
-      for (int i = i0; i < i1; ++i) {
-        const uint32_t w = E[i];
-        if ((w & pmask) == pfx) {
-          atomicAdd(&hcount[(w >> shift) & 255u], 1u);
-          atomicAdd(&hsum[(w >> shift) & 255u], (unsigned long long)w);
-        }
-      }
+      each([&](int j) {
+        const uint32_t w = j < cnt ? getw(j) : 0u;
+        hist_add_sum(hcount, hsum, j < cnt && (w & pmask) == pfx, (w >> shift) & 255u, w);
+      });
       __syncthreads();
-      if (tid == 0) {
-        int b = 255;
-        for (; b > 0; --b) {  // whole buckets whose last weight still starts below top_p * S
-          if (!hcount[b]) continue;
-          if (!below_top_p(C + hsum[b], tpp, S)) break;
-          C += hsum[b];
+      if (tid < 32) {
+        // from the top, whole non-empty buckets are taken while the sum up to and including
+        // them stays below top_p * S; the first bucket that reaches it (bucket 0 at the
+        // latest) holds v*. Suffix sums over 8 buckets a lane.
+        unsigned long long sb[8], tot = 0;
+        unsigned int cb[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          cb[k] = hcount[255 - (8 * lane + k)];
+          sb[k] = hsum[255 - (8 * lane + k)];
+          tot += sb[k];
         }
-        s_prefix = pfx | (unsigned(b) << shift);
-        s_c = C;
-        if (shift == 0) {  // v* reached: how many of its ties (lowest indices first) are kept
-          const unsigned int cnt = hcount[b];
-          const unsigned long long v = (unsigned long long)((pfx | unsigned(b)) & 0xFFFFFFFFu);
-          unsigned int lo = 0, hi = cnt;  // largest r in [0, cnt] with every r' < r kept
-          while (lo < hi) {
-            const unsigned int mid = (lo + hi + 1) / 2;
-            if (below_top_p(C + (unsigned long long)(mid - 1) * v, tpp, S)) lo = mid;
-            else hi = mid - 1;
+        unsigned long long inc = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned long long t = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += t;
+        }
+        unsigned long long above = C + (inc - tot);
+        int hit = -1;
+        unsigned long long hit_above = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int b = 255 - (8 * lane + k);
+          if (hit < 0 && (b == 0 || (cb[k] && !below_top_p(above + sb[k], tpp, S)))) {
+            hit = k;
+            hit_above = above;
           }
-          s_keq = lo;
+          above += sb[k];
+        }
+        const unsigned int hm = __ballot_sync(0xffffffffu, hit >= 0);
+        if (lane == __ffs(hm) - 1) {
+          const int b = 255 - (8 * lane + hit);
+          s_prefix = pfx | (unsigned(b) << shift);
+          s_c = hit_above;
+          if (shift == 0) {  // v* reached: how many of its ties (lowest indices first) are kept
+            const unsigned int cnt_b = cb[hit];
+            const unsigned long long v = (unsigned long long)((pfx | unsigned(b)) & 0xFFFFFFFFu);
+            unsigned int lo = 0, hi = cnt_b;  // largest r in [0, cnt] with every r' < r kept
+            while (lo < hi) {
+              const unsigned int mid = (lo + hi + 1) / 2;
+              if (below_top_p(hit_above + (unsigned long long)(mid - 1) * v, tpp, S)) lo = mid;
+              else hi = mid - 1;
+            }
+            s_keq = lo;
+          }
         }
       }
       __syncthreads();
@@ -423,18 +600,19 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
   }
   // kept weights and their running sum in index order
   unsigned long long eqn = 0;
-  if (tp_on)
-    for (int i = i0; i < i1; ++i) eqn += E[i] == vstar;
+  if (tp_on) each([&](int j) { eqn += (j < cnt && getw(j) == vstar) ? 1u : 0u; });
   unsigned long long eqt;
   unsigned long long er = block_excl_u64(eqn, &eqt, ws);
   unsigned long long kept = 0;
   {
     unsigned long long r = er;
-    for (int i = i0; i < i1; ++i) {
-      const uint32_t w = E[i];
-      const bool k = !tp_on || w > vstar || (w == vstar && r++ < keq);
-      kept += k ? w : 0u;
-    }
+    each([&](int j) {
+      if (j < cnt) {
+        const uint32_t w = getw(j);
+        const bool k = !tp_on || w > vstar || (w == vstar && r++ < keq);
+        kept += k ? w : 0u;
+      }
+    });
   }
   unsigned long long S_kept;
   const unsigned long long before = block_excl_u64(kept, &S_kept, ws);
@@ -452,14 +630,18 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
   const unsigned long long t = s_t;
   {
     unsigned long long r = er, cum = before;
-    for (int i = i0; i < i1; ++i) {
-      const uint32_t w = E[i];
-      const bool k = !tp_on || w > vstar || (w == vstar && r++ < keq);
-      if (probs) probs[i] = k ? float(double(w) / double(S_kept)) : 0.0f;
-      if (!k) continue;
-      cum += w;
-      if (cum > t && before <= t && s_tok == 0xFFFFFFFFu) s_tok = unsigned(i);  // first token past t
-    }
+    each([&](int j) {
+      if (j < cnt) {
+        const int i = i0 + j;
+        const uint32_t w = getw(j);
+        const bool k = !tp_on || w > vstar || (w == vstar && r++ < keq);
+        if (probs) probs[i] = k ? float(double(w) / double(S_kept)) : 0.0f;
+        if (k) {
+          cum += w;
+          if (cum > t && cum - w <= t) s_tok = unsigned(i);  // the token whose range holds t
+        }
+      }
+    });
   }
   __syncthreads();
   if (tid == 0 && s_tok != 0xFFFFFFFFu) {
@@ -484,8 +666,20 @@ cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState*
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, sample_kernel, logits, scratch, n, st, hist, pen_cnt, rep,
-                                           temperature, top_k, top_p, rng);
+  cudaError_t e = cudaSuccess;
+  constexpr int HW_BYTES = (SD_THREADS / 32) * 256 * 4;  // per-warp radix counts
+  if (n <= SD_THREADS * SD_REG) {  // the logits fit the shared-memory stage
+    e = cudaFuncSetAttribute(sample_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SD_STAGE_BYTES + HW_BYTES);
+    cfg.dynamicSmemBytes = size_t(SD_STAGE_BYTES + HW_BYTES);
+    if (e == cudaSuccess)
+      e = cudaLaunchKernelEx(&cfg, sample_kernel<true>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
+                             top_k, top_p, rng);
+  } else {
+    cfg.dynamicSmemBytes = size_t(HW_BYTES);
+    e = cudaLaunchKernelEx(&cfg, sample_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature, top_k,
+                           top_p, rng);
+  }
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
@@ -506,8 +700,18 @@ cudaError_t launch_sample_full(const float* logits, float* scratch, int n, StepS
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, sample_full_kernel, logits, scratch, n, st, hist, pen_cnt, rep,
-                                           temperature, top_k, top_p, rng, probs);
+  const bool sm = n <= SD_THREADS * SD_REG;  // every thread's logits fit shared memory
+  cudaError_t e = cudaSuccess;
+  if (sm) {
+    e = cudaFuncSetAttribute(sample_full_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SD_STAGE_BYTES);
+    cfg.dynamicSmemBytes = size_t(SD_STAGE_BYTES);
+    if (e == cudaSuccess)
+      e = cudaLaunchKernelEx(&cfg, sample_full_kernel<true>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
+                             top_k, top_p, rng, probs);
+  } else {
+    e = cudaLaunchKernelEx(&cfg, sample_full_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
+                           top_k, top_p, rng, probs);
+  }
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
