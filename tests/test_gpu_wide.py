@@ -101,8 +101,8 @@ def test_wide_greedy_generate(wide, kind, rep):
     assert got == want, f"{kind}: first mismatch at " \
                         f"{next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), len(got))}"
     steps = m.launches_per_step()
-    if kind == "persistent" and m.config.intermediate_size <= 16384:
-        assert steps == 1  # the single-launch decode step ran
+    if kind == "persistent":
+        assert steps == 1  # the single-launch decode step ran (the 70B width: its down projection as a K chain)
     if kind == "per_op":
         assert steps > 1
     m.close()

@@ -43,7 +43,7 @@ namespace {
 constexpr int MK_W = 15;            // consumer warps per CTA
 constexpr int MK_T = MK_W * 32;     // consumer threads per CTA
 constexpr int MK_THREADS = MK_T + 32;  // + the producer warp (16 warps: 128 registers a thread)
-constexpr int MK_MAX_K = 16384;     // longest GEMV input (limb planes in shared memory)
+constexpr int MK_MAX_K = MK_MAX_INPUT;  // longest GEMV input (limb planes in shared memory)
 constexpr int MK_GPT = 32;          // most groups in one tile
 constexpr int MK_ANB = 8;          // attention: cache rows per lane in flight (K and V each)
 constexpr int MK_ASMAX = 4;        // most key splits of one query head
@@ -474,6 +474,12 @@ __device__ void issue_tile(const MkPart* Pp, const MkTile& T, uint8_t* dst, uint
   }
   int r0 = 4 * T.g;
   const int r1 = 4 * (T.g + T.ng);
+  if (Pp->row_stride) {  // a K-chain part: each row's slice of the input is its own copy
+    for (int r = r0; r < r1; ++r)
+      bulk_g2s(dst + size_t(r - r0) * row_bytes, Pp->w[0] + size_t(r) * size_t(Pp->row_stride), uint32_t(row_bytes),
+               bar);
+    return;
+  }
   int base = 0;
   for (int sg = 0; sg < 3 && r0 < r1; ++sg) {
     const int s1 = sg == 0 ? Pp->rows0 : sg == 1 && nseg > 1 ? base + Pp->rows1 : r1;
@@ -714,7 +720,7 @@ __device__ bool build_input(const MkArgs& a, int pi, const MkPart& P, const Ctx&
       break;
     case MK_O: src = a.att; break;
     case MK_GU: src = a.xb; break;
-    case MK_D: src = a.act; break;
+    case MK_D: src = a.act + P.kofs; break;
     default: src = a.xa; break;  // MK_LM
   }
   const bool stash = P.kind == MK_QKV || P.kind == MK_GU;  // residual of the o / down share
@@ -1180,7 +1186,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       // flight. The units are (group, 8-block chunk) pairs dealt round-robin to the warps
       // across tiles; the chunks' partial sums meet in part and are added in chunk order
       // once the part's last tile is done, then the epilogues run.
-      const int CH = (NB + 7) / 8;
+      const int CH = (NB + 7) / 8;                  // this part's 8-block chunks
+      const int CHS = P.kchain ? int(P.kchs) : CH;  // chunks of the whole row (a K chain: all its parts)
+      const int CB = P.kchain ? int(P.kch0) : 0;    // this part's first chunk in the row
       int gb = 0;  // CTA-local index of the tile's first group
       for (int tg = g0; tg < g1; tg += gpt, ++k) {
         const int tng = min(gpt, g1 - tg);
@@ -1210,18 +1218,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
           for (int i = 0; i < ROWS; ++i) acc[i] = warp_sum(acc[i]);
           if (lane == 0)
 #pragma unroll
-            for (int i = 0; i < ROWS; ++i) sm.part[((gb + gl) * CH + (ul - gl * CH)) * ROWS + i] = acc[i];
+            for (int i = 0; i < ROWS; ++i) sm.part[((gb + gl) * CHS + CB + (ul - gl * CH)) * ROWS + i] = acc[i];
         }
         gb += tng;
         __syncwarp();
         if (lane == 0) mbar_arrive(sm.empty + s);  // this warp is done with the slot
       }
       cbar();  // every chunk's partial sums are in part
+      if (P.kchain == 1) continue;  // the chain's next part adds its chunks first
       for (int gl = warp; gl < g1 - g0; gl += MK_W) {
         float v[ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int ch = 0; ch < CH; ++ch)
+        for (int ch = 0; ch < CHS; ++ch)
 #pragma unroll
-          for (int i = 0; i < ROWS; ++i) v[i] += sm.part[(gl * CH + ch) * ROWS + i];
+          for (int i = 0; i < ROWS; ++i) v[i] += sm.part[(gl * CHS + ch) * ROWS + i];
         if (P.norm)
 #pragma unroll
           for (int i = 0; i < ROWS; ++i) v[i] = __fmul_rn(v[i], c.rm);
@@ -1361,6 +1370,8 @@ bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* s
   for (int i = 0; i < nparts; ++i) {
     if (parts[i].kind == MK_ATT) continue;
     if (parts[i].K % QK_K || parts[i].K > MK_MAX_K || parts[i].ngroups < 1) return false;
+    // a K chain takes the split path (more than 8 blocks a part, whole 8-block chunks but the last)
+    if (parts[i].kchain && (parts[i].K <= 8 * QK_K || parts[i].kind != MK_D)) return false;
     kmax = std::max(kmax, parts[i].K);
     gmax = std::max(gmax, 4 * size_t(parts[i].K / QK_K) * dev_block_bytes(parts[i].dtype));
   }
@@ -1386,8 +1397,8 @@ bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* s
       if (parts[i].kind == MK_O || parts[i].kind == MK_D) res_rows = std::max(res_rows, rows);
       if (parts[i].kind == MK_LM) lm_rows = std::max(lm_rows, rows);
       const int NB = parts[i].K / QK_K;
-      if (NB > 8)  // split part: a float per (group, 8-block chunk, row)
-        part_floats = std::max(part_floats, (g1 - g0) * ((NB + 7) / 8) * ROWS);
+      if (NB > 8)  // split part: a float per (group, 8-block chunk of the row, row)
+        part_floats = std::max(part_floats, (g1 - g0) * (parts[i].kchain ? int(parts[i].kchs) : (NB + 7) / 8) * ROWS);
     }
   }
   a.nparts = nparts;

@@ -206,8 +206,18 @@ struct MkPart {
   uint8_t first;        // first part of its phase (builds the input planes)
   uint8_t dtype;        // DT_Q4K / DT_Q6K (MK_ATT: unused)
   uint8_t nseg;
+  // K chain (a down projection whose input is longer than MK_MAX_INPUT): the part
+  // covers input values [kofs, kofs + K) of rows row_stride bytes apart; its 8-block
+  // chunks are chunks kch0.. of the kchs of the whole row. kchain 1: more parts of the
+  // chain follow (their partial sums accumulate, no epilogue); 2: the last part.
+  int kofs;
+  int row_stride;       // bytes between weight rows (0: rows of K values are contiguous)
+  int16_t kch0, kchs;
+  uint8_t kchain;
+  uint8_t pad[3];
 };
-static_assert(sizeof(MkPart) == 64, "MkPart layout");
+static_assert(sizeof(MkPart) == 80, "MkPart layout");
+constexpr int MK_MAX_INPUT = 16384;  // longest input of one part of the persistent decode step
 
 // A tile: ng groups starting at group g of part `part` (whole K rows).
 struct MkTile {

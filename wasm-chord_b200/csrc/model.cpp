@@ -913,18 +913,33 @@ void Model::build_decode_step() {
     }
     const int p_d = phase++;
     {
-      MkPart P{};
-      P.kind = MK_D;
-      P.dtype = uint8_t(L.down.dtype);
-      P.K = F;
-      P.w[0] = L.down.ptr;
-      P.rows0 = int(L.down.rows);
-      P.nseg = 1;
-      P.ngroups = groups(L.down.rows / 4);
-      P.phase = int16_t(p_d);
-      P.dep = int16_t(p_gu);
-      P.first = 1;
-      parts.push_back(P);
+      // an input longer than the step's limb planes (the 70B width's FFN, 28672) is cut
+      // into a K chain of parts over 8-block chunks; their partial sums meet per group
+      const int nb = F / QK_K, np = (F + MK_MAX_INPUT - 1) / MK_MAX_INPUT;
+      const int per = ((nb + np - 1) / np + 7) / 8 * 8;  // blocks of a part, whole 8-block chunks
+      const size_t bb = dev_block_bytes(L.down.dtype);
+      for (int b0 = 0; b0 < nb; b0 += per) {
+        const int b1 = std::min(nb, b0 + per);
+        MkPart P{};
+        P.kind = MK_D;
+        P.dtype = uint8_t(L.down.dtype);
+        P.K = (b1 - b0) * QK_K;
+        P.w[0] = L.down.ptr + size_t(b0) * bb;
+        P.rows0 = int(L.down.rows);
+        P.nseg = 1;
+        P.ngroups = groups(L.down.rows / 4);
+        P.phase = int16_t(p_d);
+        P.dep = int16_t(p_gu);
+        P.first = 1;
+        if (np > 1) {
+          P.kofs = b0 * QK_K;
+          P.row_stride = int(size_t(nb) * bb);
+          P.kch0 = int16_t(b0 / 8);
+          P.kchs = int16_t((nb + 7) / 8);
+          P.kchain = uint8_t(b1 < nb ? 1 : 2);
+        }
+        parts.push_back(P);
+      }
     }
     prev_d = p_d;
   }
