@@ -64,25 +64,10 @@ constexpr int SD_REG = 32;  // logits per thread held on chip (vocabularies up t
 constexpr int SD_STAGE_BYTES = (SD_THREADS * SD_REG + SD_THREADS) * 4;
 __device__ __forceinline__ int stage_at(int i) { return i + (i >> 5); }
 
-// One histogram count per element of the radix pass; the lanes of a warp that hit
-// the same bin add together with one atomic, one round per distinct wanted bin (the
-// largest logits crowd into a few bins; later passes have few wanted lanes). Every
-// lane of the warp calls it.
-__device__ __forceinline__ void hist_add(unsigned int* h, bool want, unsigned int bin) {
-  const int lane = threadIdx.x & 31;
-  unsigned int pending = __ballot_sync(0xffffffffu, want);
-  while (pending) {
-    const int src = __ffs(pending) - 1;
-    const unsigned int b = __shfl_sync(0xffffffffu, bin, src);
-    const unsigned int m = __ballot_sync(0xffffffffu, want && bin == b);
-    if (lane == src) atomicAdd(&h[b], unsigned(__popc(m)));
-    pending &= ~m;
-  }
-}
-
-// The same into this warp's own histogram row: one shared atomic per wanted element
-// (the lanes that hit one bin are combined by the hardware; no other warp adds to
-// the row).
+// One count of a radix pass into this warp's own histogram row: one shared atomic
+// per wanted element (the lanes that hit one bin are combined by the hardware; no
+// other warp adds to the row, so the largest logits, which crowd into a few bins,
+// do not serialise the block).
 __device__ __forceinline__ void hist_add_warp(unsigned int* hw, bool want, unsigned int bin) {
   if (want) atomicAdd(&hw[bin], 1u);
 }
@@ -163,7 +148,7 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
   const int per = (n + SD_THREADS - 1) / SD_THREADS;  // REG: per <= SD_REG
   const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
   const int cnt = i1 - i0;
-  uint32_t kr[REG ? SD_REG : 1];
+  uint32_t kr[REG ? SD_REG : 1] = {};
   auto logit_at = [&](int i) -> float {
     if constexpr (REG) return stage[stage_at(i)];
     else return plog[i];
@@ -357,31 +342,9 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
 // with the weights of sample_int.h: the repetition penalty into plog, the top-k
 // candidates (k = 0: all) by a radix select of the order-preserving logit bits
 // (ties at the threshold to the lowest indices), x = l / T, the maximum, the
-// integer weights E (stored over plog), top-p by a radix search over E with
-// per-bucket counts and exact sums, the draw, generate()'s bookkeeping.
+// integer weights E (stored over plog), top-p by a binary search over the weight
+// value with exact sums, the draw, generate()'s bookkeeping.
 // probs (may be null) receives each token's final probability.
-// count and weight sum per histogram bin; the lanes of a warp that hit the same
-// bin add together (one pass per distinct bin of the warp). Every lane calls it.
-__device__ __forceinline__ void hist_add_sum(unsigned int* hc, unsigned long long* hs, bool want, unsigned int bin,
-                                             unsigned long long w) {
-  const int lane = threadIdx.x & 31;
-  unsigned int pending = __ballot_sync(0xffffffffu, want);
-  while (pending) {
-    const int src = __ffs(pending) - 1;
-    const unsigned int b = __shfl_sync(0xffffffffu, bin, src);
-    const bool mine = want && bin == b;
-    const unsigned int m = __ballot_sync(0xffffffffu, mine);
-    unsigned long long sum = mine ? w : 0ull;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == src) {
-      atomicAdd(&hc[b], unsigned(__popc(m)));
-      atomicAdd(&hs[b], sum);
-    }
-    pending &= ~m;
-  }
-}
-
 // SM: the penalised logits, then their x = l / T, then their integer weights, in
 // dynamic shared memory (stage_at: each thread's contiguous run conflict-free, the
 // logits loaded coalesced); otherwise in plog.
@@ -391,10 +354,9 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
                                                                  float temp, int top_k, float top_p,
                                                                  unsigned long long* rng, float* probs) {
   __shared__ unsigned int hcount[256];
-  __shared__ unsigned long long hsum[256];
   __shared__ unsigned long long ws[SD_THREADS / 32];
   __shared__ unsigned int s_prefix, s_rem, s_nan, s_keq, s_tok;
-  __shared__ unsigned long long s_c, s_t;
+  __shared__ unsigned long long s_t;
   __shared__ float s_max;
   __shared__ float wmax[SD_THREADS / 32];
   pdl_trigger();
@@ -404,7 +366,9 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
   const int per = (n + SD_THREADS - 1) / SD_THREADS;  // REG: per <= SD_REG
   const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
   const int cnt = i1 - i0;
-  extern __shared__ uint32_t sv[];  // SM: value i at stage_at(i)
+  // dynamic: SM: value i at stage_at(i); then [warps][256] per-warp counts of a radix pass
+  extern __shared__ __align__(16) uint32_t sv[];
+  unsigned int* hwarp = sv + (SM ? SD_STAGE_BYTES / 4 : 0);
   uint32_t* E = reinterpret_cast<uint32_t*>(plog);
   auto each = [&](auto&& f) {  // the same trip count on every thread
     if constexpr (SM) {
@@ -465,12 +429,19 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
     unsigned int pmask = 0;
     rem = unsigned(top_k);
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = tid; b < 256; b += SD_THREADS) hcount[b] = 0;
+      for (int b = tid; b < (SD_THREADS / 32) * 256; b += SD_THREADS) hwarp[b] = 0;
       __syncthreads();
       each([&](int j) {
         const uint32_t key = j < cnt ? order_key(getf(j)) : 0u;
-        hist_add(hcount, j < cnt && (key & pmask) == prefix, (key >> shift) & 255u);
+        hist_add_warp(hwarp + (tid >> 5) * 256, j < cnt && (key & pmask) == prefix, (key >> shift) & 255u);
       });
+      __syncthreads();
+      if (tid < 256) {  // the warps' counts of each bin
+        unsigned int c = 0;
+#pragma unroll 8
+        for (int w = 0; w < SD_THREADS / 32; ++w) c += hwarp[w * 256 + tid];
+        hcount[tid] = c;
+      }
       __syncthreads();
       if (tid < 32) pick_bin(hcount, prefix, shift, rem, &s_prefix, &s_rem);
       __syncthreads();
@@ -524,78 +495,47 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
   });
   unsigned long long S;
   block_excl_u64(mine, &S, ws);
-  // top-p: the last kept weight v* (radix search over E from the top, exact sums)
+  // top-p: the last kept weight v* (exact sums)
   const bool tp_on = !(top_p <= 0.0f || top_p >= 1.0f);  // TOPP / TOPK_TOPP (sampling.rs:57-78)
   unsigned int vstar = 0, keq = 0xFFFFFFFFu;
   if (tp_on) {
+    // v* = the largest weight value v whose sum of weights >= v is not below top_p * S:
+    // the weight at which the cumulative sum from the top first reaches the threshold
+    // (what a search from the top finds). The sums of weights >= v fall as v
+    // rises, so a binary search over v finds it; S itself is never below (top_p < 1).
     const TopP tpp = top_p_parts(top_p);
-    unsigned int pfx = 0, pmask = 0;
-    unsigned long long C = 0;  // sum of the weights above the current range
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = tid; b < 256; b += SD_THREADS) {
-        hcount[b] = 0;
-        hsum[b] = 0;
-      }
-      __syncthreads();
+    auto sum_ge = [&](unsigned long long v) {
+      unsigned long long part = 0, tot;
       each([&](int j) {
-        const uint32_t w = j < cnt ? getw(j) : 0u;
-        hist_add_sum(hcount, hsum, j < cnt && (w & pmask) == pfx, (w >> shift) & 255u, w);
+        if (j < cnt) {
+          const uint32_t w = getw(j);
+          part += w >= v ? w : 0u;
+        }
       });
-      __syncthreads();
-      if (tid < 32) {
-        // from the top, whole non-empty buckets are taken while the sum up to and including
-        // them stays below top_p * S; the first bucket that reaches it (bucket 0 at the
-        // latest) holds v*. Suffix sums over 8 buckets a lane.
-        unsigned long long sb[8], tot = 0;
-        unsigned int cb[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          cb[k] = hcount[255 - (8 * lane + k)];
-          sb[k] = hsum[255 - (8 * lane + k)];
-          tot += sb[k];
-        }
-        unsigned long long inc = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const unsigned long long t = __shfl_up_sync(0xffffffffu, inc, o);
-          if (lane >= o) inc += t;
-        }
-        unsigned long long above = C + (inc - tot);
-        int hit = -1;
-        unsigned long long hit_above = 0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int b = 255 - (8 * lane + k);
-          if (hit < 0 && (b == 0 || (cb[k] && !below_top_p(above + sb[k], tpp, S)))) {
-            hit = k;
-            hit_above = above;
-          }
-          above += sb[k];
-        }
-        const unsigned int hm = __ballot_sync(0xffffffffu, hit >= 0);
-        if (lane == __ffs(hm) - 1) {
-          const int b = 255 - (8 * lane + hit);
-          s_prefix = pfx | (unsigned(b) << shift);
-          s_c = hit_above;
-          if (shift == 0) {  // v* reached: how many of its ties (lowest indices first) are kept
-            const unsigned int cnt_b = cb[hit];
-            const unsigned long long v = (unsigned long long)((pfx | unsigned(b)) & 0xFFFFFFFFu);
-            unsigned int lo = 0, hi = cnt_b;  // largest r in [0, cnt] with every r' < r kept
-            while (lo < hi) {
-              const unsigned int mid = (lo + hi + 1) / 2;
-              if (below_top_p(hit_above + (unsigned long long)(mid - 1) * v, tpp, S)) lo = mid;
-              else hi = mid - 1;
-            }
-            s_keq = lo;
-          }
-        }
-      }
-      __syncthreads();
-      pfx = s_prefix;
-      C = s_c;
-      pmask |= 255u << shift;
+      block_excl_u64(part, &tot, ws);
+      return tot;
+    };
+    unsigned long long lo = 0, hi = 0xFFFFFFFFull;
+    while (lo < hi) {  // uniform over the block: every thread sees the same totals
+      const unsigned long long mid = (lo + hi + 1) / 2;
+      if (!below_top_p(sum_ge(mid), tpp, S)) lo = mid;
+      else hi = mid - 1;
     }
-    vstar = pfx;
+    vstar = unsigned(lo);
+    const unsigned long long C = sum_ge(lo + 1);  // the weights above v*
+    unsigned long long ties = 0, tie_tot;
+    each([&](int j) { ties += (j < cnt && getw(j) == vstar) ? 1u : 0u; });
+    block_excl_u64(ties, &tie_tot, ws);
+    if (tid == 0) {  // how many of v*'s ties (lowest indices first) are kept
+      unsigned long long l2 = 0, h2 = tie_tot;  // largest r in [0, ties] with every r' < r kept
+      while (l2 < h2) {
+        const unsigned long long m2 = (l2 + h2 + 1) / 2;
+        if (below_top_p(C + (m2 - 1) * (unsigned long long)vstar, tpp, S)) l2 = m2;
+        else h2 = m2 - 1;
+      }
+      s_keq = unsigned(l2);
+    }
+    __syncthreads();
     keq = s_keq;
   }
   // kept weights and their running sum in index order
@@ -701,14 +641,17 @@ cudaError_t launch_sample_full(const float* logits, float* scratch, int n, StepS
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const bool sm = n <= SD_THREADS * SD_REG;  // every thread's logits fit shared memory
+  constexpr int HW_BYTES = (SD_THREADS / 32) * 256 * 4;  // per-warp radix counts
   cudaError_t e = cudaSuccess;
   if (sm) {
-    e = cudaFuncSetAttribute(sample_full_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SD_STAGE_BYTES);
-    cfg.dynamicSmemBytes = size_t(SD_STAGE_BYTES);
+    e = cudaFuncSetAttribute(sample_full_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SD_STAGE_BYTES + HW_BYTES);
+    cfg.dynamicSmemBytes = size_t(SD_STAGE_BYTES + HW_BYTES);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, sample_full_kernel<true>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
                              top_k, top_p, rng, probs);
   } else {
+    cfg.dynamicSmemBytes = size_t(HW_BYTES);
     e = cudaLaunchKernelEx(&cfg, sample_full_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
                            top_k, top_p, rng, probs);
   }
