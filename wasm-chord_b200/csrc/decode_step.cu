@@ -380,7 +380,7 @@ __device__ __forceinline__ void q6k_unit(const uint32_t (&ra)[ROWS], int b, int 
 // Shared-memory carve-up of one CTA (sizes in MkArgs, set on the host):
 //   [slots]  nslots x slot_bytes weight tiles
 //   [region] limb planes (GEMV phases) or attention staging
-//   [parts]  the part list
+//   [parts]  the part list; [share] this CTA's groups [g0, g1) of each part (g0 | g1 << 16)
 //   [rsd]    residual rows of this CTA's o / down share
 //   [rope]   cos, sin of the step's position (head_dim / 2 each)
 //   [pen]    penalty counts of this CTA's LM-head rows
@@ -390,6 +390,7 @@ struct MkSmem {
   uint8_t* slots;
   uint8_t* region;
   MkPart* parts;
+  uint32_t* share;
   float* rsd;
   float* rcos;
   float* rsin;
@@ -403,7 +404,7 @@ struct MkSmem {
 
 // Byte offsets of the carve-up (host and device agree on them).
 struct MkOffsets {
-  size_t region, parts, rsd, rcos, rsin, pen, red, part, flags, full, empty, total;
+  size_t region, parts, share, rsd, rcos, rsin, pen, red, part, flags, full, empty, total;
 };
 
 __host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
@@ -413,6 +414,9 @@ __host__ __device__ __forceinline__ MkOffsets mk_offsets(const MkArgs& a) {
   x += a.region_bytes;
   o.parts = x;
   x += sizeof(MkPart) * size_t(a.nparts);
+  o.share = x;
+  x += sizeof(uint32_t) * size_t(a.nparts);
+  x = (x + 15) / 16 * 16;  // red is read as 64-bit words: keep what follows 16-byte aligned
   o.rsd = x;
   x += sizeof(float) * size_t(a.res_rows);
   o.rcos = x;
@@ -442,6 +446,7 @@ __device__ __forceinline__ MkSmem mk_carve(const MkArgs& a, uint8_t* b) {
   s.slots = b;
   s.region = b + o.region;
   s.parts = reinterpret_cast<MkPart*>(b + o.parts);
+  s.share = reinterpret_cast<uint32_t*>(b + o.share);
   s.rsd = reinterpret_cast<float*>(b + o.rsd);
   s.rcos = reinterpret_cast<float*>(b + o.rcos);
   s.rsin = reinterpret_cast<float*>(b + o.rsin);
@@ -456,6 +461,11 @@ __device__ __forceinline__ MkSmem mk_carve(const MkArgs& a, uint8_t* b) {
 
 // Groups [g0, g1) of a part owned by CTA c of n.
 __host__ __device__ __forceinline__ void cta_share(int ngroups, int c, int n, int& g0, int& g1) {
+  if (ngroups < 65536 && c < 65536) {  // the products fit 32 bits: no 64-bit division
+    g0 = int(unsigned(c) * unsigned(ngroups) / unsigned(n));
+    g1 = int(unsigned(c + 1) * unsigned(ngroups) / unsigned(n));
+    return;
+  }
   g0 = int((long long)c * ngroups / n);
   g1 = int((long long)(c + 1) * ngroups / n);
 }
@@ -500,14 +510,22 @@ struct TileCursor {
   int pi, g, g1;  // part, next group, end of the CTA's share of the part
 };
 
-__device__ __forceinline__ bool next_tile(const MkPart* parts, int nparts, TileCursor& t, MkTile& T) {
+// share: this CTA's group ranges of the parts (null: computed)
+__device__ __forceinline__ bool next_tile(const MkPart* parts, int nparts, TileCursor& t, MkTile& T,
+                                          const uint32_t* share) {
   while (t.g >= t.g1) {
     if (++t.pi >= nparts) return false;
     if (parts[t.pi].kind == MK_ATT) {
       t.g = t.g1 = 0;
       continue;
     }
-    cta_share(parts[t.pi].ngroups, blockIdx.x, gridDim.x, t.g, t.g1);
+    if (share) {
+      const uint32_t r = share[t.pi];
+      t.g = int(r & 0xFFFFu);
+      t.g1 = int(r >> 16);
+    } else {
+      cta_share(parts[t.pi].ngroups, blockIdx.x, gridDim.x, t.g, t.g1);
+    }
   }
   const int gpt = parts[t.pi].gpt;
   T.g = uint16_t(t.g);
@@ -1089,13 +1107,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
     }
     mbar_fence_init();
     MkTile T;
-    for (; kp < a.nslots && next_tile(a.parts, a.nparts, cur, T); ++kp)
+    for (; kp < a.nslots && next_tile(a.parts, a.nparts, cur, T, nullptr); ++kp)
       issue_tile(a.parts + T.part, T, sm.slots + size_t(kp) * a.slot_bytes, sm.full + kp);
   }
   {
     const int4* src = reinterpret_cast<const int4*>(a.parts);
     int4* dst = reinterpret_cast<int4*>(sm.parts);
     for (int i = tid; i < a.nparts * int(sizeof(MkPart) / 16); i += MK_THREADS) dst[i] = src[i];
+    for (int i = tid; i < a.nparts; i += MK_THREADS) {  // this CTA's groups of every part
+      int g0 = 0, g1 = 0;
+      if (a.parts[i].kind != MK_ATT) cta_share(a.parts[i].ngroups, cta, gridDim.x, g0, g1);
+      sm.share[i] = uint32_t(g0) | (uint32_t(g1) << 16);
+    }
   }
   if (tid < 8) sm.flags[tid] = 0;
   for (int i = tid; i < a.head_dim / 2; i += MK_THREADS) {  // cos / sin of this step's position (attention.rs:230-248)
@@ -1123,7 +1146,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
   if (warp == MK_W) {  // ---- producer: refill each slot once the consumer warps have left it
     if (lane != 0) return;
     MkTile T;
-    for (; next_tile(sm.parts, a.nparts, cur, T); ++kp) {
+    for (; next_tile(sm.parts, a.nparts, cur, T, sm.share); ++kp) {
       const int s = kp % a.nslots, use = kp / a.nslots;
       if (!mbar_wait_n(sm.empty + s, uint32_t((use - 1) & 1), MK_MBAR_POLLS)) {
         atomicOr(&st->err, 4);  // the consumers stopped taking tiles
@@ -1150,8 +1173,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MkArgs
       }
       continue;
     }
-    int g0, g1;
-    cta_share(P.ngroups, cta, gridDim.x, g0, g1);
+    const int g0 = int(sm.share[pi] & 0xFFFFu), g1 = int(sm.share[pi] >> 16);
     c.g0 = g0;
     if (P.first) {
       cbar();  // the previous phase is done with the region and the stashes
@@ -1415,6 +1437,10 @@ bool decode_step_plan(MkPart* parts, int nparts, MkArgs& a, int n_rep, size_t* s
   while (a.nslots > 2 && mk_offsets(a).total > g_mk_smem_max) --a.nslots;
   *smem = mk_offsets(a).total;
   if (*smem > g_mk_smem_max) return false;
+  {  // the 64-bit words of the carve-up (argmax keys in red, the mbarriers) must be 8-byte aligned
+    const MkOffsets o = mk_offsets(a);
+    if (o.red % 8 || o.full % 8 || o.empty % 8 || o.parts % 16) return false;
+  }
   int per_sm = 0;
   a.has_q6 = 0;
   for (int i = 0; i < nparts; ++i)
