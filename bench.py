@@ -271,7 +271,7 @@ def run_reference(args, rank, world):
     oracle.set_threads(cores, 1)  # the reference's threading for the timed decode steps
     oracle.set_faithful(True)  # and its one-row-at-a-time matmul loop
     tok = int(len(logits) - 1 - np.argmax(logits[::-1]))
-    for _ in range(min(args.warmup, 1)):
+    for _ in range(args.warmup):  # about 0.6 s a step on 16 host cores
         logits = o.forward([tok], o.kv_len())
         tok = int(len(logits) - 1 - np.argmax(logits[::-1]))
     n = 0
@@ -284,7 +284,7 @@ def run_reference(args, rank, world):
             break
     dt = time.perf_counter() - t0
     v = n / dt
-    line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": n, "warmup": min(args.warmup, 1),
+    line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": n, "warmup": args.warmup,
             "ms_per_step": dt * 1e3 / n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, Q4_K dequantised to f32 at load)",
             "config": {"workload": "TinyLlama-1.1B Q4_K greedy decode after a 128-token prompt, batch 1",
