@@ -291,7 +291,7 @@ def run_reference(args, rank, world):
                        "prompt_len": PROMPT_LEN, "global_batch": 1, "parallelism": "cpu"},
             "impl": "reference",
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": f"{n} decode tokens at positions {PROMPT_LEN + 1}..; projections on 1 thread "
+                             "sample": f"{n} decode tokens from position {PROMPT_LEN + 1 + args.warmup}; projections on 1 thread "
                                        f"and the LM head on {cores} threads, as in the reference"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
