@@ -45,6 +45,23 @@ def test_gguf_file_reads_back_with_gguf_py(tiny_mix_gguf):
     assert int(f.parts[f.data[0]][0]) == cfg.context_length
 
 
+def test_layer_period_repeats_layer_bytes(tmp_path):
+    """Deep timing models (the 80-layer 70B shape) repeat a period of layers: every
+    tensor of layer i holds the bytes of layer i % period, the rest stay distinct, and
+    the file reads back like any other."""
+    from gguf import GGUFReader
+    path = synth.make_model("tiny", str(tmp_path / "p.gguf"), num_layers=5, layer_period=2)
+    t = {x.name: np.array(x.data).tobytes() for x in GGUFReader(path).tensors}
+    for name in ("attn_q.weight", "attn_norm.weight", "ffn_down.weight"):
+        assert t[f"blk.4.{name}"] == t[f"blk.2.{name}"] == t[f"blk.0.{name}"]
+        assert t[f"blk.3.{name}"] == t[f"blk.1.{name}"]
+        assert t[f"blk.1.{name}"] != t[f"blk.0.{name}"]
+    plain = synth.make_model("tiny", str(tmp_path / "q.gguf"), num_layers=5)
+    t2 = {x.name: np.array(x.data).tobytes() for x in GGUFReader(plain).tensors}
+    assert t2["blk.0.attn_q.weight"] == t["blk.0.attn_q.weight"]  # the period keeps layer 0's stream
+    assert t2["blk.2.attn_q.weight"] != t2["blk.0.attn_q.weight"]
+
+
 def _declared_symbols():
     hdr = open(os.path.join(REPO, "include", "wcb.h")).read()
     return sorted(set(re.findall(r"\b(wcb_[a-z0-9_]+)\s*\(", hdr)))
