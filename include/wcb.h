@@ -246,10 +246,11 @@ uint32_t wcb_tp_id(uint8_t out[128]);
 
 /* Tensor parallelism, decode steps without NCCL: each rank exports the CUDA IPC
  * handle (64 bytes) of its receive buffer, the caller gathers them in rank order
- * and hands all of them to every rank; decode steps then write their attn-out /
- * ffn-down partial sums straight into every rank's buffer over NVLink and sum
- * them in rank order (prefill keeps the NCCL all-reduce). No counterpart in the
- * reference. */
+ * and hands all of them to every rank; decode steps (and one-token forwards) then
+ * run as one kernel launch per rank that writes its attn-out / ffn-down partial
+ * sums and its argmax key straight into every rank's buffer over NVLink and sums
+ * them in rank order, every wait bounded by wcb_load_opts.wait_ms (prefill keeps
+ * the NCCL all-reduce). No counterpart in the reference. */
 uint32_t wcb_model_tp_handle(uint32_t h, uint8_t out[64]);
 uint32_t wcb_model_tp_connect(uint32_t h, const uint8_t* handles, uint32_t n_ranks);
 
