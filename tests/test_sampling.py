@@ -170,3 +170,21 @@ def test_device_full_sampler_on_a_large_vocabulary(model_dir, gpu, top_k, top_p,
     assert dev.launches_per_step() == 2 if persistent else dev.launches_per_step() > 2
     dev.close()
     host.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("top_k,top_p", [(40, 0.9), (0, 0.9), (2000, 1.0)])
+def test_device_samplers_above_the_staged_vocabulary(model_dir, gpu, top_k, top_p):
+    """A 40000-token vocabulary (more logits than the samplers stage in shared memory):
+    both device samplers read the penalised logits from global memory and still draw
+    exactly the host sampler's tokens."""
+    path = synth.cached_model("tiny", model_dir, vocab_size=40000)
+    dev = wcb.Model.load_from_gguf(path)
+    host = wcb.Model.load_from_gguf(path, host_sampling=True)
+    prompt = synth.random_prompt(20, 40000, seed=13).tolist()
+    for seed in (6, 7):
+        g = wcb.GenerationConfig(max_tokens=24, temperature=0.9, top_p=top_p, top_k=top_k,
+                                 repetition_penalty=1.1, seed=seed, eos_id=None)
+        assert dev.generate_tokens(prompt, g) == host.generate_tokens(prompt, g)
+    dev.close()
+    host.close()
