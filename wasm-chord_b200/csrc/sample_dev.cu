@@ -615,10 +615,12 @@ cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState*
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, sample_kernel<true>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
                              top_k, top_p, rng);
-  } else {
+  } else {  // static + per-warp counts exceed the default 48 KB
+    e = cudaFuncSetAttribute(sample_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, HW_BYTES);
     cfg.dynamicSmemBytes = size_t(HW_BYTES);
-    e = cudaLaunchKernelEx(&cfg, sample_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature, top_k,
-                           top_p, rng);
+    if (e == cudaSuccess)
+      e = cudaLaunchKernelEx(&cfg, sample_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
+                             top_k, top_p, rng);
   }
   return e != cudaSuccess ? e : cudaGetLastError();
 }
@@ -651,9 +653,11 @@ cudaError_t launch_sample_full(const float* logits, float* scratch, int n, StepS
       e = cudaLaunchKernelEx(&cfg, sample_full_kernel<true>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
                              top_k, top_p, rng, probs);
   } else {
+    e = cudaFuncSetAttribute(sample_full_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, HW_BYTES);
     cfg.dynamicSmemBytes = size_t(HW_BYTES);
-    e = cudaLaunchKernelEx(&cfg, sample_full_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
-                           top_k, top_p, rng, probs);
+    if (e == cudaSuccess)
+      e = cudaLaunchKernelEx(&cfg, sample_full_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
+                             top_k, top_p, rng, probs);
   }
   return e != cudaSuccess ? e : cudaGetLastError();
 }
