@@ -130,3 +130,47 @@ def test_numpy_restatement_matches_the_oracle(model_dir, preset):
         err = np.abs(got - want).max()
         assert err <= REL * np.abs(want).max(), (preset, pos, err, np.abs(want).max())
     o.close()
+
+
+def _penalised_argmax(logits, history, rep):
+    """sampling.rs:86-103 then :118-125: the penalty once per previous occurrence, then the
+    argmax with the last maximum winning (Iterator::max_by)."""
+    l = logits.copy()
+    if rep != 1.0:
+        for t in history:
+            l[t] = l[t] / rep if l[t] > 0.0 else l[t] * rep
+    m = l.max()
+    return int(len(l) - 1 - np.argmax(l[::-1])), l, m
+
+
+@pytest.mark.parametrize("preset,rep", [("tiny", 1.1), ("tiny_mix", 1.3)])
+def test_oracle_generate_bookkeeping_against_numpy(model_dir, preset, rep):
+    """generate() (model.rs:1322-1415) with the oracle's tokens fed back into the numpy
+    restatement: every token is the numpy model's penalised argmax (or within f32 rounding
+    of it), the history holds the sampled tokens only, and an EOS id ends the sequence
+    before it is pushed, except as the first token."""
+    path = synth.cached_model(preset, model_dir)
+    o = oracle.OracleModel(path)
+    n = NumpyModel(path)
+    vocab = n.cfg["vocab"]
+    prompt = synth.random_prompt(11, vocab, seed=22).tolist()
+    toks = o.generate(prompt, 24, repetition_penalty=rep, eos_id=None)
+    assert len(toks) == 24
+    logits = n.forward(prompt, 0)
+    history = []
+    for i, t in enumerate(toks):
+        if i > 0:
+            logits = n.forward([toks[i - 1]], len(prompt) + i - 1)
+        best, pen, m = _penalised_argmax(logits, history, rep)
+        assert t == best or m - pen[t] <= REL * np.abs(pen).max(), (i, t, best, m - pen[t])
+        history.append(t)
+    # EOS: a token the sequence produces again later ends it at that later occurrence
+    eos = next(t for i, t in enumerate(toks) if i >= 2)
+    o.clear_kv_cache()
+    cut = o.generate(prompt, 24, repetition_penalty=rep, eos_id=eos)
+    first_eos = toks.index(eos, 1)  # the first token is never checked
+    assert cut == toks[:first_eos]
+    o.clear_kv_cache()
+    first = o.generate(prompt, 24, repetition_penalty=rep, eos_id=toks[0])
+    assert first[0] == toks[0] and len(first) >= 1  # an EOS as the first token is kept
+    o.close()
