@@ -160,10 +160,14 @@ uint32_t wcb_generate_tokens(uint32_t handle, const uint32_t* prompt, size_t n, 
  * (each sequence has its own KV cache and sampler), each result equal to that
  * sequence's wcb_generate_tokens result. prompts holds the n_seq prompts back
  * to back with lengths lens[]; out is n_seq x cap; n_out receives n_seq counts.
- * Greedy configs on a model loaded with max_batch > 1 prefill the sequences
- * one by one into their own KV slots, then run their decode steps together,
+ * On a model loaded with max_batch > 1 the sequences are prefilled one by one
+ * into their own KV slots, then their decode steps run together,
  * min(max_batch, 32) sequences per batched step (the weights are read once per
- * step for all of them); otherwise the sequences run one after the other.
+ * step for all of them); otherwise the sequences run one after the other. In a
+ * sampled config every sequence draws from the config's seed, as its own
+ * generate() does; the batched step's logits are rounded differently from the
+ * single-sequence step's, so a sampled sequence can leave its single-sequence
+ * tokens where a draw falls within that rounding of a boundary.
  * Replaces the reference's one-sequence-at-a-time serving loop
  * (Model::generate, crates/wasm-chord-runtime/src/transformer/model.rs:1322). */
 uint32_t wcb_generate_batch(uint32_t handle, const uint32_t* prompts, const size_t* lens, size_t n_seq,

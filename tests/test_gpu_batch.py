@@ -93,3 +93,30 @@ def test_batch_f16_kv(tiny_gguf, gpu):
     for p, g in zip(prompts, got):
         assert g == o.generate(p, 16, repetition_penalty=1.0, eos_id=None)
     m.close()
+
+
+def test_batch_sampled_on_the_device(tiny_batch):
+    """Sampled configs run the batched step too, with one device sampler per slot (its
+    own history, penalty counts and random stream, started from the config's seed as a
+    sequence's own generate() starts). Keeping only the most probable token (top_k 1, or
+    a vanishing top_p through the full-vocabulary sampler) reproduces the greedy batch,
+    which is checked against the oracle above; real sampling is deterministic for a seed,
+    and identical prompts in different slots draw identical tokens."""
+    m, _ = tiny_batch
+    prompts = prompts_of([9, 31, 4, 17, 50, 12], 512, seed=90)
+    greedy = m.generate_batch(prompts, wcb.GenerationConfig(max_tokens=32, temperature=0.0, repetition_penalty=1.1,
+                                                           eos_id=None))
+    for k, p in ((1, 1.0), (0, 1e-6)):
+        c = wcb.GenerationConfig(max_tokens=32, temperature=0.8, top_k=k, top_p=p, repetition_penalty=1.1, seed=3,
+                                 eos_id=None)
+        assert m.generate_batch(prompts, c) == greedy, (k, p)
+        assert m.batch_info()[1] == 1 + 5 * 2 + 1 + 1  # the batched step ran, its sampler in place
+    batch = prompts + [prompts[0], prompts[0]]  # 8 sequences: one batched group
+    for k, p in ((40, 0.9), (0, 0.9)):
+        c = wcb.GenerationConfig(max_tokens=32, temperature=0.8, top_k=k, top_p=p, repetition_penalty=1.1, seed=5,
+                                 eos_id=None)
+        a = m.generate_batch(batch, c)
+        assert a == m.generate_batch(batch, c)
+        assert a[0] == a[-1] == a[-2]
+        assert all(len(x) == 32 and all(0 <= t < 512 for t in x) for x in a)
+        assert any(x != g for x, g in zip(a, greedy))

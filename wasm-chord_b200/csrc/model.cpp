@@ -278,8 +278,10 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     xprep_ = static_cast<uint8_t*>(
         dalloc(stage_x_bytes(t_max_, int(std::max({c.hidden, hq_, ffn_l_})))));
     if (tp_ == 1) {  // device sampling: the penalised logits and the splitmix64 state
-      plog_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
-      rng_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long)));
+      // per decode slot (the batched step samples every slot at once)
+      plog_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab * bslots_));
+      rng_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * bslots_));
+      rng_base_ = rng_;
     }
     pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab * bslots_));
     check(cudaMemset(pen_cnt_, 0, sizeof(uint32_t) * c.vocab * bslots_), "clear penalty counts");
@@ -1256,6 +1258,7 @@ void Model::bind_seq(uint32_t b) {
   st_ = st_base_ + b;
   hist_ = hist_base_ + size_t(b) * hist_cap_;
   pen_cnt_ = pen_base_ + size_t(b) * cfg_.vocab;
+  if (rng_base_) rng_ = rng_base_ + b;
 }
 
 int Model::batch_gemm(const DevWeight* segs, int nseg, int rows, int K, int B, const float* x, int ldx,
@@ -1369,7 +1372,17 @@ void Model::enqueue_batch_step(int B) {
   const int VL = int(vocab_l_);  // this rank's LM-head rows (all of them with one rank)
   batch_gemm(head, 1, VL, H, B, x_, H, out_norm_, sqx_, sq_x, c.eps, BEPI_STORE, logits_b_, VL, nullptr, 0, nullptr,
              -1);
-  if (tp_ == 1) {
+  if (tp_ == 1 && sample_mode_ == 1) {  // 1 <= top_k <= 1024: one sampler CTA per slot
+    check(launch_sample(logits_b_, plog_, V, st_base_, hist_base_, pen_base_, rep_, samp_t_, samp_k_, samp_tp_,
+                        rng_base_, stream_, B, int(hist_cap_)),
+          "sampler");
+    ++batch_launches_;
+  } else if (tp_ == 1 && sample_mode_ == 2) {  // every other sampled configuration
+    check(launch_sample_full(logits_b_, plog_, V, st_base_, hist_base_, pen_base_, rep_, samp_t_, samp_k_, samp_tp_,
+                             rng_base_, nullptr, stream_, B, int(hist_cap_)),
+          "sampler");
+    ++batch_launches_;
+  } else if (tp_ == 1) {
     check(launch_batch_sample(logits_b_, V, st_base_, hist_base_, int(hist_cap_), pen_base_, rep_, B, stream_),
           "sampler");
     ++batch_launches_;
@@ -1391,7 +1404,9 @@ std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts
   check_group();
   std::vector<std::vector<uint32_t>> out(n);
   const Sampler probe(g.seed, g.temperature, g.top_p, g.top_k, g.repetition_penalty);
-  if (!batch_ok_ || !probe.greedy() || n < 2) {
+  // sampled configurations draw on the device (sample_dev.cu), one sampler CTA per slot
+  const bool dev_sample = !probe.greedy() && plog_ && !(opt_.flags & 32);
+  if (!batch_ok_ || (!probe.greedy() && !dev_sample) || n < 2) {
     size_t off = 0;
     for (size_t s = 0; s < n; ++s) {
       out[s] = generate(prompts + off, lens[s], g);
@@ -1400,7 +1415,12 @@ std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts
     return out;
   }
   check(cudaSetDevice(device_), "cudaSetDevice");
-  sample_mode_ = 0;  // greedy here: the per-slot prefill takes the argmax path
+  sample_mode_ = dev_sample ? (probe.fixed_path(cfg_.vocab) ? 1 : 2) : 0;
+  if (dev_sample) {
+    samp_t_ = probe.temperature();
+    samp_k_ = int(probe.top_k());
+    samp_tp_ = probe.top_p();
+  }
   ++session_;  // slot 0 is the single-sequence KV cache: an open session ends here
   sess_active_ = false;
   sess_done_ = true;
@@ -1412,6 +1432,13 @@ std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts
   std::vector<StepState> hs(bslots_);
   for (size_t g0 = 0; g0 < n; g0 += bslots_) {
     const int B = int(std::min<size_t>(bslots_, n - g0));
+    if (dev_sample) {  // each sequence draws from the seed's stream, as its own generate() does
+      const std::vector<unsigned long long> seeds(size_t(B), probe.seed_state());
+      check(cudaMemcpyAsync(rng_base_, seeds.data(), sizeof(unsigned long long) * seeds.size(),
+                            cudaMemcpyHostToDevice, stream_),
+            "seed");
+      check(cudaStreamSynchronize(stream_), "seed");
+    }
     try {
       for (int b = 0; b < B; ++b) {
         bind_seq(uint32_t(b));
@@ -1422,7 +1449,10 @@ std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts
       throw;
     }
     bind_seq(0);
-    if (!batch_exec_ || batch_graph_b_ != B || batch_graph_rep_ != rep_) {
+    const bool same_sampler = batch_graph_mode_ == sample_mode_ &&
+                              (sample_mode_ == 0 || (batch_graph_t_ == samp_t_ && batch_graph_k_ == samp_k_ &&
+                                                     batch_graph_tp_ == samp_tp_));
+    if (!batch_exec_ || batch_graph_b_ != B || batch_graph_rep_ != rep_ || !same_sampler) {
       if (batch_exec_) {
         cudaGraphExecDestroy(batch_exec_);
         cudaGraphDestroy(batch_graph_);
@@ -1449,6 +1479,10 @@ std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts
       batch_exec_ = e;
       batch_graph_b_ = B;
       batch_graph_rep_ = rep_;
+      batch_graph_mode_ = sample_mode_;
+      batch_graph_t_ = samp_t_;
+      batch_graph_k_ = samp_k_;
+      batch_graph_tp_ = samp_tp_;
     }
     // decode steps for the whole group; finished sequences are skipped by the
     // sampler and their KV caches are no longer written

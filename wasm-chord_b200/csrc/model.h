@@ -277,6 +277,9 @@ class Model {
   int batch_launches_ = 0;
   int batch_graph_b_ = 0;
   float batch_graph_rep_ = -1.0f;
+  int batch_graph_mode_ = -1;  // the sampler the captured batched step draws with
+  float batch_graph_t_ = -1.0f, batch_graph_tp_ = -1.0f;
+  int batch_graph_k_ = -1;
   cudaGraphExec_t batch_exec_ = nullptr;
   cudaGraph_t batch_graph_ = nullptr;
 
@@ -291,7 +294,8 @@ class Model {
   float samp_t_ = 0.0f, samp_tp_ = 0.0f;
   int samp_k_ = 0;
   float* plog_ = nullptr;                 // [vocab] penalised logits
-  unsigned long long* rng_ = nullptr;     // splitmix64 state
+  unsigned long long* rng_ = nullptr;     // splitmix64 state of the bound slot
+  unsigned long long* rng_base_ = nullptr;  // [slot] splitmix64 states
   bool sess_host_ = false;                // this session samples on the host
 };
 

@@ -128,7 +128,8 @@ __device__ __forceinline__ void pick_bin(const unsigned int* h, unsigned int pre
 template <bool REG>
 __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits, float* plog, int n, StepState* st,
                                                             uint32_t* hist, uint32_t* pen_cnt, float rep, float temp,
-                                                            int top_k, float top_p, unsigned long long* rng) {
+                                                            int top_k, float top_p, unsigned long long* rng,
+                                                            int hstride) {
   __shared__ unsigned int hcount[256];
   __shared__ unsigned int s_prefix, s_rem, s_nan, s_ncand, s_tok;
   __shared__ int sorted[SD_THREADS];
@@ -143,6 +144,15 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
   unsigned int* hwarp = reinterpret_cast<unsigned int*>(dyn + (REG ? SD_STAGE_BYTES : 0));
   pdl_trigger();
   pdl_wait();
+  {  // CTA b samples sequence b of a batch (its logits, state, history, counts and stream)
+    const size_t b = blockIdx.x;
+    logits += b * size_t(n);
+    plog += b * size_t(n);
+    st += b;
+    hist += b * size_t(hstride);
+    pen_cnt += b * size_t(n);
+    rng += b;
+  }
   if (st->done) return;
   const int tid = threadIdx.x;
   const int per = (n + SD_THREADS - 1) / SD_THREADS;  // REG: per <= SD_REG
@@ -352,7 +362,7 @@ template <bool SM>
 __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* logits, float* plog, int n, StepState* st,
                                                                  uint32_t* hist, uint32_t* pen_cnt, float rep,
                                                                  float temp, int top_k, float top_p,
-                                                                 unsigned long long* rng, float* probs) {
+                                                                 unsigned long long* rng, float* probs, int hstride) {
   __shared__ unsigned int hcount[256];
   __shared__ unsigned long long ws[SD_THREADS / 32];
   __shared__ unsigned int s_prefix, s_rem, s_nan, s_keq, s_tok;
@@ -361,6 +371,15 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
   __shared__ float wmax[SD_THREADS / 32];
   pdl_trigger();
   pdl_wait();
+  {  // CTA b samples sequence b of a batch (its logits, state, history, counts and stream)
+    const size_t b = blockIdx.x;
+    logits += b * size_t(n);
+    plog += b * size_t(n);
+    st += b;
+    hist += b * size_t(hstride);
+    pen_cnt += b * size_t(n);
+    rng += b;
+  }
   if (st->done) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int per = (n + SD_THREADS - 1) / SD_THREADS;  // REG: per <= SD_REG
@@ -595,10 +614,10 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
 
 cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
                           uint32_t* pen_cnt, float rep, float temperature, int top_k, float top_p,
-                          unsigned long long* rng, cudaStream_t s) {
-  if (top_k < 1 || top_k > SD_THREADS || n < 1 || !(temperature > 0.0f)) return cudaErrorInvalidValue;
+                          unsigned long long* rng, cudaStream_t s, int nseq, int hist_stride) {
+  if (top_k < 1 || top_k > SD_THREADS || n < 1 || !(temperature > 0.0f) || nseq < 1) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
+  cfg.gridDim = dim3(unsigned(nseq));
   cfg.blockDim = dim3(SD_THREADS);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -614,13 +633,13 @@ cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState*
     cfg.dynamicSmemBytes = size_t(SD_STAGE_BYTES + HW_BYTES);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, sample_kernel<true>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
-                             top_k, top_p, rng);
+                             top_k, top_p, rng, hist_stride);
   } else {  // static + per-warp counts exceed the default 48 KB
     e = cudaFuncSetAttribute(sample_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, HW_BYTES);
     cfg.dynamicSmemBytes = size_t(HW_BYTES);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, sample_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
-                             top_k, top_p, rng);
+                             top_k, top_p, rng, hist_stride);
   }
   return e != cudaSuccess ? e : cudaGetLastError();
 }
@@ -631,10 +650,11 @@ namespace wcb {
 
 cudaError_t launch_sample_full(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
                                uint32_t* pen_cnt, float rep, float temperature, int top_k, float top_p,
-                               unsigned long long* rng, float* probs, cudaStream_t s) {
-  if (top_k < 0 || n < 1 || !(temperature > 0.0f)) return cudaErrorInvalidValue;
+                               unsigned long long* rng, float* probs, cudaStream_t s, int nseq, int hist_stride) {
+  // probs (a test hook) only for one sequence
+  if (top_k < 0 || n < 1 || !(temperature > 0.0f) || nseq < 1 || (probs && nseq > 1)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
+  cfg.gridDim = dim3(unsigned(nseq));
   cfg.blockDim = dim3(SD_THREADS);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -651,13 +671,13 @@ cudaError_t launch_sample_full(const float* logits, float* scratch, int n, StepS
     cfg.dynamicSmemBytes = size_t(SD_STAGE_BYTES + HW_BYTES);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, sample_full_kernel<true>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
-                             top_k, top_p, rng, probs);
+                             top_k, top_p, rng, probs, hist_stride);
   } else {
     e = cudaFuncSetAttribute(sample_full_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, HW_BYTES);
     cfg.dynamicSmemBytes = size_t(HW_BYTES);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, sample_full_kernel<false>, logits, scratch, n, st, hist, pen_cnt, rep, temperature,
-                             top_k, top_p, rng, probs);
+                             top_k, top_p, rng, probs, hist_stride);
   }
   return e != cudaSuccess ? e : cudaGetLastError();
 }
