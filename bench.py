@@ -10,7 +10,7 @@ L2 flush is needed between steps.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N bench.py --gpus N --tp [--layers L] [--prompt P]
       (the Llama-2-70B shape, tensor-parallel over N GPUs; not the headline line)
-  [torchrun ...] bench.py --serve [--sequences S] [--prompt P]
+  [torchrun ...] bench.py --serve [--sequences S] [--prompt P] [--sampled]
       (batched serving: S sequences of a P-token prompt + --steps decode tokens,
       split evenly over the ranks, fp16 KV; not the headline line)
   python bench.py --microbench REPS
@@ -626,9 +626,12 @@ def run_serve(args, rank, world, dist):
     sp = m.stream()
     s = torch.cuda.ExternalStream(sp)
     prompts = [synth.random_prompt(P, cfg.vocab_size, seed=1000 + rank * B + i).tolist() for i in range(B)]
+    # --sampled: the reference's default GenerationConfig (config.rs:74-78), drawn on the device
+    samp = dict(temperature=0.7, top_p=0.9, top_k=40, repetition_penalty=1.1, seed=1) if args.sampled else \
+        dict(temperature=0.0, repetition_penalty=1.0)
 
     def timed(max_tokens):
-        gc = wcb.GenerationConfig(max_tokens=max_tokens, temperature=0.0, repetition_penalty=1.0, eos_id=None)
+        gc = wcb.GenerationConfig(max_tokens=max_tokens, eos_id=None, **samp)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if world > 1:
             dist.barrier()
@@ -658,12 +661,14 @@ def run_serve(args, rank, world, dist):
     step_gbs = (wbytes + kv_bytes) / (step_ms * 1e-3) / 1e9
     if rank == 0:
         print(json.dumps({
-            "metric": "batched decode tok/s (TinyLlama-1.1B Q4_K, %d sequences x %d-token prompt, fp16 KV)" % (S, P),
+            "metric": "batched decode tok/s (TinyLlama-1.1B Q4_K, %d sequences x %d-token prompt, fp16 KV%s)"
+                      % (S, P, ", sampled: temperature 0.7, top-p 0.9, top-k 40, penalty 1.1" if args.sampled else ""),
             "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": step_ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 activations (fp16 hi+lo tensor-core operands), Q4_K weights, fp16 KV",
             "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K; uniform-random prompt ids)",
-            "config": {"workload": f"{S} sequences x ({P}-token prompt + {K} greedy tokens), split over {world} GPU(s)",
+            "config": {"workload": f"{S} sequences x ({P}-token prompt + {K} {'sampled' if args.sampled else 'greedy'} "
+                                   f"tokens), split over {world} GPU(s)",
                        "model": "tinyllama-1.1b-arch", "sequences_per_gpu": B, "prompt_len": P,
                        "parallelism": f"dp{world} (independent replicas)", "kv_cache": "f16",
                        "l2": "weights 582 MB + KV > 126 MB L2, no flush"},
