@@ -222,7 +222,6 @@ __device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity) {
 template <int NB>
 __global__ void __launch_bounds__(BD_THREADS, 1) bgemm_kernel(const BatchGemmArgs a, const int epi) {
   using L = BdLayout<NB>;
-  constexpr uint32_t LBO_X = (NB / 8) * 128;
   constexpr int CP = L::CP;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* At = sm + L::A_OFF;
