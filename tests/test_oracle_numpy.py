@@ -174,3 +174,26 @@ def test_oracle_generate_bookkeeping_against_numpy(model_dir, preset, rep):
     first = o.generate(prompt, 24, repetition_penalty=rep, eos_id=toks[0])
     assert first[0] == toks[0] and len(first) >= 1  # an EOS as the first token is kept
     o.close()
+
+
+# the 7B and 70B widths accumulate over longer rows (K up to 28672): 5e-6 - 8e-6 measured
+REL_WIDE = 4e-5
+
+
+@pytest.mark.parametrize("preset,layers", [("llama7b", 2), ("llama70b", 1)])
+def test_numpy_restatement_matches_the_oracle_at_head_dim_128(model_dir, preset, layers):
+    """The widths of the 7B (32 heads of 128, FFN 11008, the Q4_K_M mix with Q6_K attn_v /
+    ffn_down in even layers) and 70B configurations (64 query / 8 KV heads of 128, FFN 28672),
+    truncated to one or two layers and a 2048-token vocabulary so the check stays a CPU test:
+    the oracle that checks the GPU paths at these widths against the numpy restatement."""
+    path = synth.cached_model(preset, model_dir, num_layers=layers, vocab_size=2048, context_length=256)
+    o = oracle.OracleModel(path)
+    n = NumpyModel(path)
+    assert n.hd == 128
+    prompt = synth.random_prompt(13, 2048, seed=21).tolist()
+    for ids, pos in [(prompt, 0), ([5], 13), ([2048 + 3], 14)]:
+        got = np.asarray(o.forward(ids, pos), dtype=np.float64)
+        want = n.forward(ids, pos)
+        err = np.abs(got - want).max()
+        assert err <= REL_WIDE * np.abs(want).max(), (preset, pos, err, np.abs(want).max())
+    o.close()
