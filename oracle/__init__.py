@@ -78,6 +78,10 @@ def lib() -> C.CDLL:
     L.oracle_sampler_new.argtypes = [C.c_uint64, C.c_double, C.c_double, sz, f32]
     L.oracle_sampler_new.restype = vp
     L.oracle_sampler_free.argtypes = [vp]
+    L.oracle_chacha_block.restype = None
+    L.oracle_chacha_block.argtypes = [vp, C.c_uint64, C.c_int, vp]
+    L.oracle_std_rng_u32.restype = None
+    L.oracle_std_rng_u32.argtypes = [C.c_uint64, sz, vp]
     L.oracle_sampler_free.restype = None
     L.oracle_sampler_sample.argtypes = [vp, vp, sz, C.POINTER(u32)]
     L.oracle_sampler_sample.restype = u32
@@ -226,6 +230,23 @@ class Sampler:
             lib().oracle_sampler_free(self._h)
         except Exception:
             pass
+
+
+def chacha_block(key: bytes, counter: int, rounds: int) -> list:
+    """The 16 words of keystream block `counter` of ChaCha with `rounds` rounds
+    (64-bit counter, zero stream id)."""
+    assert len(key) == 32
+    out = (C.c_uint32 * 16)()
+    kb = C.create_string_buffer(bytes(key), 32)
+    lib().oracle_chacha_block(C.addressof(kb), counter, rounds, C.addressof(out))
+    return list(out)
+
+
+def std_rng_u32(seed: int, n: int) -> list:
+    """The first n u32 outputs of rand 0.9 StdRng::seed_from_u64(seed)."""
+    out = (C.c_uint32 * n)()
+    lib().oracle_std_rng_u32(seed, n, C.addressof(out))
+    return list(out)
 
 
 class OracleModel:

@@ -14,10 +14,13 @@
 // Summation order of the two third-party candle ops (rms_norm, the LM-head
 // matmul) is not pinned: candle's rms_norm is restated as a sequential f32 sum
 // and the LM head as matmul_transposed's sequential dot product. The
-// stochastic-sampling random stream (rand 0.9 StdRng/ChaCha12) is not restated:
-// a splitmix64 stream is used instead, so sampled (temperature > 0) sequences
-// are unpinned; greedy decoding does not touch the random stream.
+// stochastic-sampling random stream (rand 0.9 StdRng = ChaCha12, seeded by
+// rand_core's seed_from_u64, and the Uniform<f32> draw of WeightedIndex) is
+// restated from those crates' published algorithms (they are not under the
+// reference tree); its ChaCha block function is pinned by the RFC 8439 ChaCha20
+// known-answer vectors (tests/test_oracle.py), the seeding and the draw are not.
 #include <algorithm>
+#include <cfloat>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -516,16 +519,82 @@ struct KVCache {
 // ---------------------------------------------------------------------------
 // sampling.rs — LogitsProcessor
 // ---------------------------------------------------------------------------
-struct Rng {  // stand-in for rand::rngs::StdRng (unpinned)
-  uint64_t s;
-  explicit Rng(uint64_t seed) : s(seed) {}
-  uint64_t next() {
-    uint64_t z = (s += 0x9E3779B97F4A7C15ull);
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    return z ^ (z >> 31);
+// rand 0.9 rngs::StdRng (sampling.rs:40, :75): rand_chacha's ChaCha12Rng, a block
+// RNG over the ChaCha keystream (RFC 8439 section 2.3, here with `rounds` rounds,
+// 12 for StdRng): state = 4 constant words, the 32-byte seed as 8 little-endian
+// key words, a 64-bit block counter (words 12-13, from 0) and a 64-bit stream id
+// (words 14-15, 0). Words are handed out in keystream order, one block at a time.
+struct Rng {
+  uint32_t st[16];
+  uint32_t buf[16];
+  int pos = 16;
+  int rounds;
+  Rng(const uint8_t seed[32], int rounds_) : rounds(rounds_) {
+    static const char sigma[] = "expand 32-byte k";
+    for (int i = 0; i < 4; ++i) st[i] = le32(reinterpret_cast<const uint8_t*>(sigma) + 4 * i);
+    for (int i = 0; i < 8; ++i) st[4 + i] = le32(seed + 4 * i);
+    st[12] = st[13] = st[14] = st[15] = 0;
   }
-  float uniform01() { return float(next() >> 40) * (1.0f / 16777216.0f); }
+  // SeedableRng::seed_from_u64 (rand_core 0.9): 32 seed bytes, 4 at a time, from a
+  // PCG32 whose state is first advanced by an LCG step, output = XSH-RR permutation
+  explicit Rng(uint64_t seed) : Rng(pcg_fill(seed).data(), 12) {}
+  static std::vector<uint8_t> pcg_fill(uint64_t state) {
+    std::vector<uint8_t> out(32);
+    for (size_t off = 0; off < out.size(); off += 4) {
+      state = state * 6364136223846793005ull + 11634580027462260723ull;
+      const uint32_t xs = uint32_t(((state >> 18) ^ state) >> 27);
+      const unsigned rot = unsigned(state >> 59);
+      const uint32_t x = (xs >> rot) | (xs << ((32u - rot) & 31u));
+      for (int b = 0; b < 4; ++b) out[off + b] = uint8_t(x >> (8 * b));
+    }
+    return out;
+  }
+  static uint32_t le32(const uint8_t* p) {
+    return uint32_t(p[0]) | uint32_t(p[1]) << 8 | uint32_t(p[2]) << 16 | uint32_t(p[3]) << 24;
+  }
+  static uint32_t rotl(uint32_t v, unsigned c) { return (v << c) | (v >> (32u - c)); }
+  static void quarter(uint32_t* w, int a, int b, int c, int d) {
+    w[a] += w[b]; w[d] ^= w[a]; w[d] = rotl(w[d], 16);
+    w[c] += w[d]; w[b] ^= w[c]; w[b] = rotl(w[b], 12);
+    w[a] += w[b]; w[d] ^= w[a]; w[d] = rotl(w[d], 8);
+    w[c] += w[d]; w[b] ^= w[c]; w[b] = rotl(w[b], 7);
+  }
+  // one keystream block at the current counter into buf, then counter + 1
+  void refill() {
+    uint32_t w[16];
+    std::memcpy(w, st, sizeof(w));
+    for (int r = 0; r < rounds; r += 2) {
+      quarter(w, 0, 4, 8, 12); quarter(w, 1, 5, 9, 13); quarter(w, 2, 6, 10, 14); quarter(w, 3, 7, 11, 15);
+      quarter(w, 0, 5, 10, 15); quarter(w, 1, 6, 11, 12); quarter(w, 2, 7, 8, 13); quarter(w, 3, 4, 9, 14);
+    }
+    for (int i = 0; i < 16; ++i) buf[i] = w[i] + st[i];
+    if (++st[12] == 0) ++st[13];
+    pos = 0;
+  }
+  uint32_t next_u32() {
+    if (pos >= 16) refill();
+    return buf[pos++];
+  }
+};
+
+// rand 0.9 distr::uniform::UniformFloat<f32>: new(low, high) and sample()
+struct UniformF32 {
+  float low, scale;
+  UniformF32(float lo, float hi) : low(lo), scale(hi - lo) {
+    const float max_rand = 1.0f - FLT_EPSILON;
+    while (scale * max_rand + low >= hi) {  // shrink the scale by one ulp until the top value stays below hi
+      uint32_t b;
+      std::memcpy(&b, &scale, 4);
+      --b;
+      std::memcpy(&scale, &b, 4);
+    }
+  }
+  float sample(Rng& r) const {
+    const uint32_t bits = (r.next_u32() >> 9) | (127u << 23);  // [1, 2)
+    float v;
+    std::memcpy(&v, &bits, 4);
+    return (v - 1.0f) * scale + low;
+  }
 };
 
 enum SamplingKind { ARGMAX, ALL, TOPK, TOPP, TOPK_TOPP };
@@ -581,7 +650,9 @@ struct LogitsProcessor {
     }
     return uint32_t(best);
   }
-  // sample_multinomial — sampling.rs:128-132 (WeightedIndex; random stream unpinned)
+  // sample_multinomial — sampling.rs:128-132: rand 0.9 WeightedIndex::new (running f32
+  // totals, the last one the total) and sample (Uniform(0, total), then the first
+  // index whose running total exceeds the drawn value)
   uint32_t multinomial(const std::vector<float>& pr) {
     std::vector<float> cum(pr.size());
     float tot = 0.0f;
@@ -591,7 +662,7 @@ struct LogitsProcessor {
       cum[i] = tot;
     }
     if (!(tot > 0.0f)) throw Error(GENERIC, "Failed to create weighted index: all weights zero");
-    const float u = rng.uniform01() * tot;
+    const float u = UniformF32(0.0f, tot).sample(rng);
     size_t i = size_t(std::upper_bound(cum.begin(), cum.end(), u) - cum.begin());
     return uint32_t(std::min(i, pr.size() - 1));
   }
@@ -1025,6 +1096,19 @@ void* oracle_sampler_new(uint64_t seed, double temperature, double top_p, size_t
   return new LogitsProcessor(seed, temperature, top_p, top_k, rep);
 }
 void oracle_sampler_free(void* s) { delete static_cast<LogitsProcessor*>(s); }
+// the keystream block `counter` of ChaCha with `rounds` rounds under a 32-byte key
+// (zero stream id): the known-answer check of the random stream's block function
+void oracle_chacha_block(const uint8_t* key, uint64_t counter, int rounds, uint32_t* out16) {
+  Rng r(key, rounds);
+  r.st[12] = uint32_t(counter);
+  r.st[13] = uint32_t(counter >> 32);
+  for (int i = 0; i < 16; ++i) out16[i] = r.next_u32();
+}
+// the first n u32 outputs of StdRng::seed_from_u64(seed)
+void oracle_std_rng_u32(uint64_t seed, size_t n, uint32_t* out) {
+  Rng r(seed);
+  for (size_t i = 0; i < n; ++i) out[i] = r.next_u32();
+}
 uint32_t oracle_sampler_sample(void* s, float* logits, size_t n, uint32_t* tok) {
   ORACLE_TRY({ *tok = static_cast<LogitsProcessor*>(s)->sample(logits, n); });
 }

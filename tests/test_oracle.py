@@ -85,6 +85,71 @@ def test_topp_membership():
         assert s.sample(np.array([10.0, 5.0, 2.0, 1.0] + [0.0] * 6, np.float32)) <= 3
 
 
+# ---- the random stream: rand 0.9 StdRng::seed_from_u64 (sampling.rs:40, :75) ----
+# RFC 8439 appendix A.1, ChaCha20 block function test vectors 1 and 2 (all-zero key
+# and nonce, block counters 0 and 1), as keystream bytes
+RFC8439_A1 = [
+    "76b8e0ada0f13d90405d6ae55386bd28bdd219b8a08ded1aa836efcc8b770dc7"
+    "da41597c5157488d7724e03fb8d84a376a43b8f41518a11cc387b669b2ee6586",
+    "9f07e7be5551387a98ba977c732d080dcb0f29a048e3656912c6533e32ee7aed"
+    "29b721769ce64e43d57133b074d839d531ed1f28510afb45ace10a1f4b794d6f",
+]
+
+
+def test_chacha_block_known_answers():
+    """The block function under the oracle's StdRng (ChaCha12) is ChaCha: with 20
+    rounds it reproduces the RFC's keystream, and a block counter of 1 is the next block."""
+    for counter, hexbytes in enumerate(RFC8439_A1):
+        words = oracle.chacha_block(bytes(32), counter, 20)
+        assert b"".join(w.to_bytes(4, "little") for w in words).hex() == hexbytes
+
+
+def _py_std_rng(seed: int, n: int) -> list:
+    """A second restatement: rand_core 0.9 seed_from_u64 (PCG32 fill) + rand_chacha
+    0.9 ChaCha12Rng, one word at a time."""
+    M = (1 << 64) - 1
+    key = []
+    for _ in range(8):
+        seed = (seed * 6364136223846793005 + 11634580027462260723) & M
+        xs = (((seed >> 18) ^ seed) >> 27) & 0xFFFFFFFF
+        rot = seed >> 59
+        key.append(((xs >> rot) | (xs << (32 - rot))) & 0xFFFFFFFF)
+
+    def rotl(v, c):
+        return ((v << c) | (v >> (32 - c))) & 0xFFFFFFFF
+
+    def block(ctr):
+        s = [0x61707865, 0x3320646E, 0x79622D32, 0x6B206574] + key + [ctr & 0xFFFFFFFF, ctr >> 32, 0, 0]
+        x = list(s)
+        for _ in range(6):
+            for a, b, c, d in ((0, 4, 8, 12), (1, 5, 9, 13), (2, 6, 10, 14), (3, 7, 11, 15),
+                               (0, 5, 10, 15), (1, 6, 11, 12), (2, 7, 8, 13), (3, 4, 9, 14)):
+                x[a] = (x[a] + x[b]) & 0xFFFFFFFF
+                x[d] = rotl(x[d] ^ x[a], 16)
+                x[c] = (x[c] + x[d]) & 0xFFFFFFFF
+                x[b] = rotl(x[b] ^ x[c], 12)
+                x[a] = (x[a] + x[b]) & 0xFFFFFFFF
+                x[d] = rotl(x[d] ^ x[a], 8)
+                x[c] = (x[c] + x[d]) & 0xFFFFFFFF
+                x[b] = rotl(x[b] ^ x[c], 7)
+        return [(x[i] + s[i]) & 0xFFFFFFFF for i in range(16)]
+
+    return [block(w // 16)[w % 16] for w in range(n)]
+
+
+@pytest.mark.parametrize("seed", [0, 1, 42, (1 << 64) - 1])
+def test_std_rng_stream_restatements_agree(seed):
+    assert oracle.std_rng_u32(seed, 40) == _py_std_rng(seed, 40)
+
+
+def test_sampled_draw_reads_the_stream():
+    """WeightedIndex over 1024 equal weights (every probability exactly 2^-10) picks
+    floor(u * 1024) for u = Uniform<f32>(0, 1): the top 10 bits of each u32 of the stream."""
+    words = oracle.std_rng_u32(42, 200)
+    s = oracle.Sampler(42, 0.8, 1.0, 0, 1.0)
+    assert [s.sample(np.zeros(1024, np.float32)) for _ in range(200)] == [w >> 22 for w in words]
+
+
 # ---- tests/test_attention.rs:256-278, test_rope.rs, test_kv_cache_fix.rs ----
 def test_attention_single_token_is_v():
     heads, kv_heads, hd = 4, 2, 8

@@ -1,11 +1,16 @@
-"""Sampled decoding (LogitsProcessor::sample, sampling.rs:106-229). The
-reference's rand StdRng stream is not reproduced, so sampled token sequences
-are checked by distribution: for every sampling kind (top-k, top-k + top-p,
-top-p alone, all tokens, top-k above 1024) the host sampler's probabilities
-must equal the oracle's (compute_probabilities, top-k, top-p, renormalisation
-as the reference computes them), it must draw only kept tokens, and its draw
-frequencies must match the exact probabilities (chi-squared). The device
-sampler must then draw exactly the host sampler's tokens (gpu)."""
+"""Sampled decoding (LogitsProcessor::sample, sampling.rs:106-229). Every draw
+takes one u32 of the reference's random stream (rand 0.9 StdRng::seed_from_u64,
+restated; the oracle's copy is pinned by the ChaCha known answers), checked here
+by reading it back through draws over equal weights, and on the same logits the
+host sampler draws the oracle's tokens. Its probabilities are computed in another
+order than the reference's (softmax over the kept candidates), so they are also
+checked by distribution: for every sampling kind (top-k, top-k + top-p, top-p
+alone, all tokens, top-k above 1024) the host sampler's probabilities must equal
+the oracle's (compute_probabilities, top-k, top-p, renormalisation as the
+reference computes them), it must draw only kept tokens, and its draw frequencies
+must match the exact probabilities (chi-squared). The device sampler must then
+draw exactly the host sampler's tokens, and sampled generate() on the device the
+oracle's tokens (gpu)."""
 import oracle
 import numpy as np
 import pytest
@@ -103,6 +108,34 @@ def test_host_full_path_draws_match_the_oracle_distribution(top_k, top_p):
     assert chi2 < dof + 6 * np.sqrt(2 * dof) + 10, (chi2, dof)
 
 
+@pytest.mark.parametrize("n,top_k,top_p,temp", [(300, 40, 0.9, 0.7), (3000, 40, 0.9, 0.7), (300, 0, 0.9, 0.8),
+                                                (3000, 0, 1.0, 1.0), (3000, 1500, 0.8, 0.9)])
+def test_host_sampler_draws_the_oracles_tokens(n, top_k, top_p, temp):
+    """On the same logits the host sampler draws exactly the oracle's token at every
+    step (the same stream position and penalty history): its probabilities differ
+    from the oracle's only by f32 rounding, far below the stream's 2^-23 resolution."""
+    for seed in (42, 7):
+        rng = np.random.default_rng(seed + n)
+        a = wcb.LogitsProcessor(seed, temp, top_p, top_k, 1.1)
+        b = oracle.Sampler(seed, temp, top_p, top_k, 1.1)
+        for step in range(150):
+            logits = rng.normal(0.0, 2.0, n).astype(np.float32)
+            assert a.sample(logits.copy()) == b.sample(logits.copy()), (seed, step)
+
+
+@pytest.mark.parametrize("seed", [0, 42, 7919])
+def test_host_draws_read_the_reference_stream(seed):
+    """Equal logits make every probability a power of two, so the token drawn is the
+    top bits of the stream's next u32: 10 bits over 1024 tokens on the top-k path
+    (float weights, as the reference's WeightedIndex), 12 bits over 4096 tokens on the
+    integer-weight path (top_k = 0). Both equal the oracle's StdRng words."""
+    words = oracle.std_rng_u32(seed, 300)
+    s = wcb.LogitsProcessor(seed, 0.8, 1.0, 1024, 1.0)
+    assert [s.sample(np.zeros(1024, np.float32)) for _ in range(300)] == [w >> 22 for w in words]
+    s = wcb.LogitsProcessor(seed, 0.8, 1.0, 0, 1.0)
+    assert [s.sample(np.zeros(4096, np.float32)) for _ in range(300)] == [w >> 20 for w in words]
+
+
 def test_host_sampler_is_seeded():
     rng = np.random.default_rng(5)
     logits = rng.normal(0.0, 2.0, 1000).astype(np.float32)
@@ -130,6 +163,26 @@ def test_device_sampler_draws_the_host_samplers_tokens(tiny_gguf, gpu, cfg, pers
     assert (dev.launches_per_step() == 2) == persistent
     dev.close()
     host.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("persistent", [False, True])
+def test_device_sampled_generate_matches_the_oracle(tiny_gguf, gpu, persistent):
+    """Sampled generate() on the device against the oracle's generate() with the same
+    seed: the reference's default configuration (top-k 40 then top-p 0.9, T 0.7, penalty
+    1.1) and top-p alone over the whole vocabulary. The draws take the same StdRng words;
+    the device's logits differ from the oracle's by about 1e-6, so a draw could only
+    differ where it falls that close to a cumulative boundary."""
+    m = wcb.Model.load_from_gguf(tiny_gguf, use_persistent=persistent)
+    o = oracle.OracleModel(tiny_gguf)
+    prompt = synth.random_prompt(24, 512, seed=9).tolist()
+    for top_k, top_p, seed in ((40, 0.9, 42), (40, 0.9, 1234), (0, 0.9, 42)):
+        g = wcb.GenerationConfig(max_tokens=32, temperature=0.7, top_p=top_p, top_k=top_k,
+                                 repetition_penalty=1.1, seed=seed, eos_id=None)
+        want = o.generate(prompt, 32, temperature=0.7, top_p=top_p, top_k=top_k, repetition_penalty=1.1,
+                          seed=seed, eos_id=None)
+        assert m.generate_tokens(prompt, g) == want, (top_k, top_p, seed)
+    m.close()
 
 
 @pytest.mark.gpu

@@ -18,6 +18,8 @@
 
 namespace wcb {
 
+struct StdRng;  // the sampled draws' random stream (sample_int.h)
+
 constexpr int QK_K = 256;
 constexpr int Q4K_BYTES = 144;
 constexpr int Q6K_BYTES = 210;
@@ -358,21 +360,21 @@ cudaError_t launch_batch_sample(const float* logits, int vocab, StepState* st, u
 
 // ------------------------------------------------------------ sampling ----
 // Temperature + top-k (+ top-p) draw on the device for one sequence (1 <= top_k
-// <= 1024): penalty into `scratch` [n], the draw with the splitmix64 state *rng
+// <= 1024): penalty into `scratch` [n], the draw with the random stream *rng
 // (the host Sampler's fixed-order path, operation for operation), then
 // generate()'s bookkeeping on st / hist / pen_cnt
 // nseq > 1: one CTA per sequence b of a batch, over logits / scratch / pen_cnt + b * n,
 // st + b, hist + b * hist_stride and rng + b (the batched decode step).
 cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
                           uint32_t* pen_cnt, float rep, float temperature, int top_k, float top_p,
-                          unsigned long long* rng, cudaStream_t s, int nseq = 1, int hist_stride = 0);
+                          StdRng* rng, cudaStream_t s, int nseq = 1, int hist_stride = 0);
 // The same draw for every other sampled configuration (top_k = 0: all tokens, or
 // top_k > 1024), over integer weights (sample_int.h) so that the host sampler's
 // Sampler::sample_int keeps the same candidates and draws the same token; probs
 // (device, may be null) receives each token's final probability.
 cudaError_t launch_sample_full(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
                                uint32_t* pen_cnt, float rep, float temperature, int top_k, float top_p,
-                               unsigned long long* rng, float* probs, cudaStream_t s, int nseq = 1,
+                               StdRng* rng, float* probs, cudaStream_t s, int nseq = 1,
                                int hist_stride = 0);
 
 // ------------------------------------------------------------ elementwise --

@@ -277,10 +277,10 @@ Model::Model(const std::string& path, const LoadOptions& opt) : opt_(opt), devic
     row_m_ = static_cast<float*>(dalloc(sizeof(float) * size_t(t_max_)));
     xprep_ = static_cast<uint8_t*>(
         dalloc(stage_x_bytes(t_max_, int(std::max({c.hidden, hq_, ffn_l_})))));
-    if (tp_ == 1) {  // device sampling: the penalised logits and the splitmix64 state
+    if (tp_ == 1) {  // device sampling: the penalised logits and the random streams
       // per decode slot (the batched step samples every slot at once)
       plog_ = static_cast<float*>(dalloc(sizeof(float) * c.vocab * bslots_));
-      rng_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * bslots_));
+      rng_ = static_cast<StdRng*>(dalloc(sizeof(StdRng) * bslots_));
       rng_base_ = rng_;
     }
     pen_cnt_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t) * c.vocab * bslots_));
@@ -1103,7 +1103,7 @@ void Model::start(const uint32_t* prompt, size_t n, const GenParams& g) {
     samp_t_ = sess_sampler_->temperature();
     samp_k_ = int(sess_sampler_->top_k());
     samp_tp_ = sess_sampler_->top_p();
-    const unsigned long long seed = sess_sampler_->seed_state();
+    const StdRng seed = sess_sampler_->seed_state();
     check(cudaMemcpyAsync(rng_, &seed, sizeof(seed), cudaMemcpyHostToDevice, stream_), "seed");
     check(cudaStreamSynchronize(stream_), "seed");
   }
@@ -1433,8 +1433,8 @@ std::vector<std::vector<uint32_t>> Model::generate_batch(const uint32_t* prompts
   for (size_t g0 = 0; g0 < n; g0 += bslots_) {
     const int B = int(std::min<size_t>(bslots_, n - g0));
     if (dev_sample) {  // each sequence draws from the seed's stream, as its own generate() does
-      const std::vector<unsigned long long> seeds(size_t(B), probe.seed_state());
-      check(cudaMemcpyAsync(rng_base_, seeds.data(), sizeof(unsigned long long) * seeds.size(),
+      const std::vector<StdRng> seeds(size_t(B), probe.seed_state());
+      check(cudaMemcpyAsync(rng_base_, seeds.data(), sizeof(StdRng) * seeds.size(),
                             cudaMemcpyHostToDevice, stream_),
             "seed");
       check(cudaStreamSynchronize(stream_), "seed");

@@ -294,8 +294,8 @@ class Model {
   float samp_t_ = 0.0f, samp_tp_ = 0.0f;
   int samp_k_ = 0;
   float* plog_ = nullptr;                 // [vocab] penalised logits
-  unsigned long long* rng_ = nullptr;     // splitmix64 state of the bound slot
-  unsigned long long* rng_base_ = nullptr;  // [slot] splitmix64 states
+  StdRng* rng_ = nullptr;       // random stream of the bound slot
+  StdRng* rng_base_ = nullptr;  // [slot] random streams
   bool sess_host_ = false;                // this session samples on the host
 };
 

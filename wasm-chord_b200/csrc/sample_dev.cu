@@ -12,7 +12,8 @@
 // (sampler.cpp, Sampler::sample_fixed): x = l / T, e = exp(x - max) with
 // wcb_exp_nonpos, probabilities over the candidates in index order, top-p
 // over (probability desc, index asc), renormalisation, and the weighted draw
-// with the splitmix64 stream, so a seed gives the same tokens on host and device.
+// with one u32 of the sequence's StdRng stream (sample_int.h), so a seed gives
+// the same tokens on host and device.
 #include <cstdint>
 
 #include "device_common.cuh"
@@ -24,14 +25,6 @@ namespace wcb {
 namespace {
 
 constexpr int SD_THREADS = 1024;
-
-__device__ __forceinline__ float sd_uniform(unsigned long long* state) {
-  unsigned long long z = (*state += 0x9E3779B97F4A7C15ull);
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  z ^= z >> 31;
-  return __fmul_rn(float(z >> 40), 1.0f / 16777216.0f);
-}
 
 // inclusive warp scan / block-wide exclusive scan and total of a u64 per thread
 __device__ __forceinline__ unsigned long long warp_incl_u64(unsigned long long v) {
@@ -128,7 +121,7 @@ __device__ __forceinline__ void pick_bin(const unsigned int* h, unsigned int pre
 template <bool REG>
 __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits, float* plog, int n, StepState* st,
                                                             uint32_t* hist, uint32_t* pen_cnt, float rep, float temp,
-                                                            int top_k, float top_p, unsigned long long* rng,
+                                                            int top_k, float top_p, StdRng* rng,
                                                             int hstride) {
   __shared__ unsigned int hcount[256];
   __shared__ unsigned int s_prefix, s_rem, s_nan, s_ncand, s_tok;
@@ -325,7 +318,7 @@ __global__ void __launch_bounds__(SD_THREADS) sample_kernel(const float* logits,
       st->done = 1;
       s_tok = 0xFFFFFFFFu;
     } else {
-      const float u = __fmul_rn(sd_uniform(rng), tot);
+      const float u = __fmul_rn(unit_f32(std_rng_next_u32(rng)), tot);
       float c = 0.0f;
       for (int j = 0; j < nc; ++j) {
         c = __fadd_rn(c, q[j]);
@@ -362,7 +355,7 @@ template <bool SM>
 __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* logits, float* plog, int n, StepState* st,
                                                                  uint32_t* hist, uint32_t* pen_cnt, float rep,
                                                                  float temp, int top_k, float top_p,
-                                                                 unsigned long long* rng, float* probs, int hstride) {
+                                                                 StdRng* rng, float* probs, int hstride) {
   __shared__ unsigned int hcount[256];
   __shared__ unsigned long long ws[SD_THREADS / 32];
   __shared__ unsigned int s_prefix, s_rem, s_nan, s_keq, s_tok;
@@ -581,7 +574,7 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
       st->err = 1;
       st->done = 1;
     } else {
-      s_t = draw_target(splitmix64_next(reinterpret_cast<uint64_t*>(rng)), S_kept);
+      s_t = draw_target(std_rng_next_u32(rng), S_kept);
     }
   }
   __syncthreads();
@@ -614,7 +607,7 @@ __global__ void __launch_bounds__(SD_THREADS) sample_full_kernel(const float* lo
 
 cudaError_t launch_sample(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
                           uint32_t* pen_cnt, float rep, float temperature, int top_k, float top_p,
-                          unsigned long long* rng, cudaStream_t s, int nseq, int hist_stride) {
+                          StdRng* rng, cudaStream_t s, int nseq, int hist_stride) {
   if (top_k < 1 || top_k > SD_THREADS || n < 1 || !(temperature > 0.0f) || nseq < 1) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(nseq));
@@ -650,7 +643,7 @@ namespace wcb {
 
 cudaError_t launch_sample_full(const float* logits, float* scratch, int n, StepState* st, uint32_t* hist,
                                uint32_t* pen_cnt, float rep, float temperature, int top_k, float top_p,
-                               unsigned long long* rng, float* probs, cudaStream_t s, int nseq, int hist_stride) {
+                               StdRng* rng, float* probs, cudaStream_t s, int nseq, int hist_stride) {
   // probs (a test hook) only for one sequence
   if (top_k < 0 || n < 1 || !(temperature > 0.0f) || nseq < 1 || (probs && nseq > 1)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};

@@ -11,7 +11,7 @@
 namespace wcb {
 
 Sampler::Sampler(uint64_t seed, double temperature, double top_p, uint32_t top_k, float rep)
-    : state_(seed), temperature_(temperature), top_p_(top_p), top_k_(top_k), rep_(rep) {
+    : rng_(std_rng_seed_from_u64(seed)), temperature_(temperature), top_p_(top_p), top_k_(top_k), rep_(rep) {
   if (temperature < 1e-7) kind_ = ARGMAX;
   else if (top_k > 0 && top_p > 0.0 && top_p < 1.0) kind_ = TOPK_TOPP;
   else if (top_k > 0) kind_ = TOPK;
@@ -19,13 +19,7 @@ Sampler::Sampler(uint64_t seed, double temperature, double top_p, uint32_t top_k
   else kind_ = ALL;
 }
 
-float Sampler::uniform() {
-  uint64_t z = (state_ += 0x9E3779B97F4A7C15ull);
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  z ^= z >> 31;
-  return float(z >> 40) * (1.0f / 16777216.0f);
-}
+float Sampler::uniform() { return unit_f32(std_rng_next_u32(&rng_)); }
 
 void Sampler::penalize(float* l, size_t n) const {
   if (rep_ == 1.0f) return;
@@ -142,7 +136,7 @@ uint32_t Sampler::sample_int(const float* l, size_t n) {
   if (S_kept == 0) throw WcbError(E_GENERIC, "Failed to create weighted index: all weights zero");
   last_probs_.assign(n, 0.0f);
   for (size_t i = 0; i < n; ++i) last_probs_[i] = kept[i] ? float(double(E[i]) / double(S_kept)) : 0.0f;
-  const uint64_t target = draw_target(splitmix64_next(&state_), S_kept);
+  const uint64_t target = draw_target(std_rng_next_u32(&rng_), S_kept);
   uint64_t cum = 0;
   for (size_t i = 0; i < n; ++i) {
     if (!kept[i]) continue;

@@ -3,9 +3,9 @@
 // top-k, top-p or all (:57-78); sample() applies the repetition penalty once per
 // previously sampled occurrence (:86-103), then argmax (the LAST maximum wins,
 // :118-125; a NaN logit is an error where the reference panics) or temperature
-// softmax + top-k / top-p + a weighted draw (:106-229). The weighted draw uses a
-// splitmix64 stream seeded with `seed`; the reference's rand 0.9 StdRng stream
-// is not reproduced, so sampled (temperature > 0) sequences differ from it.
+// softmax + top-k / top-p + a weighted draw (:106-229). The weighted draw takes one
+// u32 of the reference's random stream, rand 0.9 StdRng::seed_from_u64(seed)
+// (ChaCha12; restated in sample_int.h), per sampled token.
 // Top-k configurations take a fixed evaluation order (sample_fixed) that the
 // device sampler repeats operation for operation: the top-k candidates by
 // (logit desc, index asc) (the reference's select_nth_unstable leaves ties at
@@ -18,6 +18,8 @@
 #include <algorithm>
 #include <cstdint>
 #include <vector>
+
+#include "sample_int.h"
 
 namespace wcb {
 
@@ -37,7 +39,7 @@ class Sampler {
   float temperature() const { return float(temperature_); }
   float top_p() const { return float(top_p_); }
   uint32_t top_k() const { return uint32_t(top_k_); }
-  uint64_t seed_state() const { return state_; }
+  const StdRng& seed_state() const { return rng_; }
   bool greedy() const { return kind_ == ARGMAX; }
   float repetition_penalty() const { return rep_; }
   std::vector<uint32_t>& history() { return prev_; }
@@ -49,7 +51,7 @@ class Sampler {
   uint32_t sample_fixed(const float* logits, size_t n);
   uint32_t sample_int(const float* logits, size_t n);
 
-  uint64_t state_;
+  StdRng rng_;
   Kind kind_;
   double temperature_, top_p_;
   size_t top_k_;
