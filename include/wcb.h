@@ -203,7 +203,10 @@ uint32_t wcb_model_launches_per_step(uint32_t handle, uint32_t* out);
 
 /* LogitsProcessor (sampling.rs:29-264) over host logits: with_params(seed, T,
  * top_p, top_k, repetition_penalty) -> sampler handle; sample() mutates
- * logits in place (repetition penalty) and records the token. */
+ * logits in place (repetition penalty) and records the token. Each sampled
+ * (temperature > 0) token takes the next u32 of rand 0.9's
+ * StdRng::seed_from_u64(seed) stream, as the reference's sampler does; the
+ * device samplers of wcb_generate_* draw from the same stream. */
 uint32_t wcb_sampler_new(const wcb_gen_config* cfg, uint32_t* out_sampler);
 uint32_t wcb_sampler_sample(uint32_t sampler, float* logits, size_t n, uint32_t* out_token);
 uint32_t wcb_sampler_free(uint32_t sampler);

@@ -471,7 +471,8 @@ class TokenStream:
 
 
 class LogitsProcessor:
-    """sampling.rs:29-264 through the C ABI (host sampler)."""
+    """sampling.rs:29-264 through the C ABI (host sampler); sampled draws take the
+    reference's rand 0.9 StdRng::seed_from_u64(seed) stream."""
 
     def __init__(self, seed: int, temperature: float, top_p: float, top_k: int, repetition_penalty: float):
         c = GenerationConfig(temperature=temperature, top_p=top_p, top_k=top_k,
