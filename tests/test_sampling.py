@@ -123,6 +123,21 @@ def test_host_sampler_draws_the_oracles_tokens(n, top_k, top_p, temp):
             assert a.sample(logits.copy()) == b.sample(logits.copy()), (seed, step)
 
 
+@pytest.mark.parametrize("temp,top_p,top_k", [(1e-7, 0.9, 40), (0.5e-7, 0.9, 40), (0.7, 0.0, 40), (0.7, 1.0, 40),
+                                              (0.7, 0.0, 0), (0.7, 1.0, 0), (0.7, 0.5, 1), (0.7, 0.9, 300),
+                                              (0.7, 0.9, 301), (0.7, 0.9, 5000), (2.0, 0.999, 0), (0.05, 0.9, 40)])
+def test_host_sampler_edges_of_with_params(temp, top_p, top_k):
+    """The boundaries of with_params (sampling.rs:57-78: temperature at 1e-7, top_p at
+    0 and 1, top_k 0, 1, = n, = n + 1 and above n) and of sample_topk /
+    sample_topk_topp (top_k >= n): token for token the oracle's draws over 300 logits."""
+    rng = np.random.default_rng(3)
+    a = wcb.LogitsProcessor(11, temp, top_p, top_k, 1.2)
+    b = oracle.Sampler(11, temp, top_p, top_k, 1.2)
+    for step in range(60):
+        logits = rng.normal(0.0, 2.0, 300).astype(np.float32)
+        assert a.sample(logits.copy()) == b.sample(logits.copy()), (b.kind, step)
+
+
 @pytest.mark.parametrize("seed", [0, 42, 7919])
 def test_host_draws_read_the_reference_stream(seed):
     """Equal logits make every probability a power of two, so the token drawn is the
