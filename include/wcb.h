@@ -130,7 +130,11 @@ void wcb_gen_config_default(wcb_gen_config* cfg);
  * output.weight the LM head is the reference's weight tying,
  * transpose_matrix(token embeddings, hidden, vocab) (model.rs:596-606). Models
  * with F32 / F16 2-D weights run the per-op kernels (no persistent decode step,
- * no batched decode step). */
+ * no batched decode step). Shapes the kernels cover: head_dim 64 or 128, hidden
+ * and intermediate sizes multiples of 256, a vocabulary that is a multiple of 4,
+ * at most 16 query heads per KV head; others are refused from the header with
+ * WCB_ERR_BACKEND_UNSUPPORTED before any GPU call (inconsistent head counts:
+ * WCB_ERR_INVALID_ARGUMENT). */
 uint32_t wcb_model_load(const char* gguf_path, const wcb_load_opts* opts, uint32_t* out_handle);
 
 /* Releases a handle (wasmchord_free_model, abi.rs:95-108). */

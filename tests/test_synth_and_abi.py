@@ -101,6 +101,28 @@ def test_load_errors_without_touching_the_gpu(tmp_path):
     assert e.value.code == 4 and "version" in e.value.message
 
 
+@pytest.mark.parametrize("overrides,code,words", [
+    (dict(hidden_size=768, num_heads=8, num_kv_heads=2), 5, "head_dim must be 64 or 128"),
+    (dict(vocab_size=510), 5, "multiple of 4"),
+    (dict(hidden_size=2048, num_heads=32, num_kv_heads=1), 5, "more than 16 query heads"),
+    (dict(hidden_size=384, num_heads=6, num_kv_heads=4), 3, "inconsistent"),
+    (dict(intermediate_size=300), 5, "multiples of 256"),
+    (dict(hidden_size=320, num_heads=5, num_kv_heads=5), 5, "multiples of 256"),
+])
+def test_unsupported_shapes_are_refused_before_any_device_work(tmp_path, overrides, code, words):
+    """Shapes the kernels do not cover (head_dim other than 64 / 128, hidden or FFN
+    sizes off the 256-value Q4_K block, a vocabulary not a multiple of 4, more than 16
+    query heads per KV head) and inconsistent head counts are refused from the GGUF
+    header alone, with the reference's error codes, before any GPU call."""
+    import dataclasses
+    cfg = dataclasses.replace(synth.PRESETS["tiny"], **overrides)
+    path = synth.write_gguf(str(tmp_path / "m.gguf"), cfg,
+                            plan=[("token_embd.weight", (cfg.hidden_size, cfg.vocab_size), synth.GGML_F32)])
+    with pytest.raises(wcb.WcbError) as e:
+        wcb.Model.load_from_gguf(path)
+    assert e.value.code == code and words in e.value.message
+
+
 def test_last_error_is_taken_once():
     L = wcb.lib()
     h = C.c_uint32(0)
